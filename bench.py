@@ -1,0 +1,380 @@
+#!/usr/bin/env python
+"""IVFFlat search throughput on B200 (queries/sec), with the list-scan kernel's
+HBM roofline and a CPU baseline.
+
+Workload (default): IVFFlat L2, d=128, N=20M rows from a Gaussian mixture of
+16384 clusters (centres ~ N(0, 4 I), sigma = 1), nlist=16384 trained by seeded
+k-means on a 256*nlist subsample, Q=10000 queries from the same mixture,
+nprobe=32, k=10. One step = one search of the Q-query batch. The database
+(10.2 GB) is far larger than L2 (126 MB), so no flush is needed between steps.
+
+N>1 GPUs (one process per GPU, NCCL): the inverted lists are partitioned over
+the ranks by greedy LPT on list size; every rank runs the coarse step for all
+queries, scans its own lists, and the (Q, k) partial results are merged after
+an all-gather. The database is fixed as N grows (strong scaling).
+
+--impl reference times the reference algorithm on the host cores: the coarse
+step restated in numpy and the reference's list-scan kernel
+(python/metalfaiss/faissmlx/kernels/ivf_kernels.py:21-122) run as the oracle's C
+port, over a bounded sample of the same queries and index.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+CONFIGS = {
+    # The headline workload: IVFFlat L2 at d=128, N=20M, nlist=16384, Q=10000, nprobe=32, k=10.
+    "ivf20m": dict(d=128, n=20_000_000, nlist=16384, nq=10_000, nprobe=32, k=10, niter=10),
+    # The small IVF configuration (d=64, N=32768, nlist=128, Q=16), for quick runs.
+    "ivf32k": dict(d=64, n=32768, nlist=128, nq=16, nprobe=8, k=10, niter=10),
+    # Mid-size for development runs.
+    "ivf2m": dict(d=128, n=2_000_000, nlist=2048, nq=10_000, nprobe=32, k=10, niter=5),
+}
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.t.join(timeout=2)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def lpt_partition(sizes: np.ndarray, world: int) -> np.ndarray:
+    """Owner rank of each list: greedy longest-processing-time on list sizes."""
+    from metalfaiss_b200.sharding import lpt_partition as f
+
+    return f(sizes, world)
+
+
+def build_index(cfg, device, seed=1234):
+    from metalfaiss_b200 import IVFFlatIndex, synthetic as syn
+    from metalfaiss_b200.clustering import ClusteringParameters
+
+    t0 = time.time()
+    x, centres = syn.torch_mixture(cfg["n"], cfg["d"], cfg["nlist"], seed, device)
+    params = ClusteringParameters(niter=cfg["niter"], seed=seed, max_points_per_centroid=256)
+    idx = IVFFlatIndex(cfg["d"], cfg["nlist"], device=device, clustering=params)
+    idx.train(x)
+    torch.cuda.synchronize(device)
+    t1 = time.time()
+    idx.add(x)
+    torch.cuda.synchronize(device)
+    t2 = time.time()
+    del x
+    xq, _ = syn.torch_mixture(cfg["nq"], cfg["d"], cfg["nlist"], seed + 1, device, centres=centres)
+    torch.cuda.empty_cache()
+    log(f"[bench] built index: train {t1 - t0:.1f}s add {t2 - t1:.1f}s ntotal={idx.ntotal}")
+    return idx, xq
+
+
+def scan_algorithmic_bytes(idx, probes_np, d, k):
+    """Bytes the list-major scan must move once: every probed list's rows
+    (vector + norm) read once, each (query, probe) pair's k partial results
+    written once, and the query vectors read once."""
+    sizes = idx.list_sizes()
+    probed = np.unique(probes_np[probes_np >= 0])
+    rows = int(sizes[probed].sum())
+    nq, P = probes_np.shape
+    return rows * (4 * d + 4) + nq * d * 4 + nq * P * k * 12, rows
+
+
+def run_ours(args, cfg):
+    import torch.distributed as dist
+
+    from metalfaiss_b200 import _native as nat
+    from metalfaiss_b200.sharding import ShardedIVF
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=device)
+    idx, xq = build_index(cfg, device)
+    idx.nprobe = cfg["nprobe"]
+    k = cfg["k"]
+    nq = cfg["nq"]
+    d = cfg["d"]
+    sharded = ShardedIVF(idx, rank, world) if world > 1 else None
+    search = (lambda q: sharded.search(q, k)) if sharded else (lambda q: idx.search(q, k))
+
+    # probes (for the roofline bytes): the coarse step of this batch
+    probes = idx.quantizer._search_padded(xq, min(cfg["nprobe"], cfg["nlist"]), map_ids=False).labels
+    alg_bytes, probed_rows = scan_algorithmic_bytes(sharded.local if sharded else idx,
+                                                    probes.cpu().numpy(), d, k)
+    sizes = idx.list_sizes()
+    logical_bytes = int(sizes[probes.cpu().numpy()].sum()) * d * 4
+
+    for _ in range(args.warmup):
+        search(xq)
+    torch.cuda.synchronize(device)
+    if world > 1:
+        dist.barrier()
+    sampler = ClockSampler(local)
+    sampler.start()
+    nat.timing_reset()
+    nat.timing_enable(True)
+    launches0 = nat.launch_count()
+    stream = torch.cuda.current_stream(device)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(device)
+    if world > 1:
+        dist.barrier()
+    ev0.record(stream)
+    for _ in range(args.steps):
+        res = search(xq)
+    ev1.record(stream)
+    torch.cuda.synchronize(device)
+    launches = nat.launch_count() - launches0
+    nat.timing_enable(False)
+    ms = ev0.elapsed_time(ev1)
+    scan_ms, scan_n = nat.timing_read("scan_topk_ivf")
+    if world > 1:
+        t = torch.tensor([ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    clocks = sampler.stop()
+
+    # ---- end to end through the public API: pinned host queries in, results out
+    xq_host = xq.cpu().pin_memory()
+    D_host = torch.empty((nq, k), dtype=torch.float32).pin_memory()
+    I_host = torch.empty((nq, k), dtype=torch.int64).pin_memory()
+    e2e_steps = max(3, args.steps // 2)
+    for _ in range(2):
+        r = search(xq_host.to(device, non_blocking=True))
+        D_host.copy_(r.distances, non_blocking=True)
+        I_host.copy_(r.labels, non_blocking=True)
+    torch.cuda.synchronize(device)
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        r = search(xq_host.to(device, non_blocking=True))
+        D_host.copy_(r.distances, non_blocking=True)
+        I_host.copy_(r.labels, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize(device)
+    e2e_ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(idx, xq, cfg, args.cpu_sample)
+
+    if rank == 0:
+        peak, peak_kind = measured_peaks()
+        scan_avg_ms = scan_ms / max(scan_n, 1)
+        achieved = alg_bytes / (scan_avg_ms * 1e-3) / 1e9 if scan_n else None
+        value = nq * args.steps / (ms * 1e-3)
+        line = {
+            "metric": "IVFFlat queries/sec (list-scan HBM GB/s vs peak in roofline)",
+            "value": round(value, 1),
+            "unit": "queries/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms / args.steps, 4),
+            "higher_is_better": True,
+            "scaling": "strong" if world > 1 else "weak",
+            "vs_baseline": None,
+            "dtype": "f32",
+            "data": "synthetic (seeded Gaussian mixture, generated in HBM)",
+            "config": {
+                "workload": f"{args.config}: IVFFlat L2 d={d} N={cfg['n']} nlist={cfg['nlist']} "
+                            f"Q={nq} nprobe={cfg['nprobe']} k={k}",
+                "d": d, "N": cfg["n"], "nlist": cfg["nlist"], "Q": nq, "nprobe": cfg["nprobe"],
+                "k": k, "parallelism": f"list-sharded x{world}" if world > 1 else "single GPU",
+                "l2": "database (>=10 GB) larger than L2; no flush",
+                "logical_scan_bytes_per_step": logical_bytes,
+                "probed_rows_per_step": probed_rows,
+            },
+            "roofline": {
+                "bound": "hbm",
+                "kernel": "scan_kernel (IVF list-major scan + warp top-k)",
+                "achieved": round(achieved, 1) if achieved else None,
+                "peak": peak,
+                "unit": "GB/s",
+                "frac": round(achieved / peak, 4) if achieved else None,
+                "peak_kind": f"{peak_kind} hbm_gbs",
+                "algorithmic_bytes_per_launch": alg_bytes,
+                "avg_launch_ms": round(scan_avg_ms, 4),
+                "traffic": None,
+            },
+            "e2e": {
+                "value": round(nq * e2e_steps / (e2e_ms * 1e-3), 1),
+                "unit": "queries/s",
+                "h2d_bytes_per_step": int(nq * d * 4),
+                "d2h_bytes_per_step": int(nq * k * 12),
+            },
+            "gpu_launches": int(launches),
+            "clocks": clocks,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def cpu_baseline(idx, xq, cfg, sample):
+    """The oracle's C port of the reference's IVF search on the host cores, over
+    `sample` queries of the same batch and the same index."""
+    from oracle import cport
+
+    nprobe, k, d = cfg["nprobe"], cfg["k"], cfg["d"]
+    q = xq[:sample, :d].cpu().numpy()
+    cents = idx.centroids.cpu().numpy()
+    probes = cport.coarse_probes(q, cents, nprobe)
+    # only the probed lists travel to the host
+    lists = np.unique(probes)
+    offsets = idx.list_offsets.cpu().numpy()
+    sub_off = np.zeros(idx.nlist + 1, np.int64)
+    sizes = np.zeros(idx.nlist, np.int64)
+    sizes[lists] = offsets[lists + 1] - offsets[lists]
+    np.cumsum(sizes, out=sub_off[1:])
+    vecs = np.empty((int(sub_off[-1]), d), np.float32)
+    ids = np.empty(int(sub_off[-1]), np.int64)
+    for l in lists:
+        a, b = int(offsets[l]), int(offsets[l + 1])
+        vecs[sub_off[l]:sub_off[l + 1]] = idx._vecs[a:b, :d].cpu().numpy()
+        ids[sub_off[l]:sub_off[l + 1]] = idx._ids[a:b].cpu().numpy()
+    threads = len(os.sched_getaffinity(0))
+    t0 = time.perf_counter()
+    cport.ivf_search(q, cents, sub_off, vecs, ids, nprobe, k, threads=threads)
+    dt = time.perf_counter() - t0
+    return {"value": round(sample / dt, 2), "unit": "queries/s", "cores": threads, "kind": "port",
+            "sample": f"{sample} of the {cfg['nq']} queries (coarse + scan + top-k), same index"}
+
+
+def run_reference(args, cfg):
+    """Reference arm: rank 0 only; times the CPU implementation of the path."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    device = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(device)
+    idx, xq = build_index(cfg, device)
+    idx.nprobe = cfg["nprobe"]
+    for _ in range(args.warmup):
+        cpu_baseline(idx, xq, cfg, max(4, args.cpu_sample // 8))
+    vals = []
+    for _ in range(args.steps):
+        vals.append(cpu_baseline(idx, xq, cfg, args.cpu_sample))
+    v = statistics.median(r["value"] for r in vals)
+    base = vals[0]
+    line = {
+        "impl": "reference",
+        "metric": "IVFFlat queries/sec (list-scan HBM GB/s vs peak in roofline)",
+        "value": v, "unit": "queries/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(1000.0 * args.cpu_sample / v, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded Gaussian mixture)",
+        "config": {"workload": f"{args.config}: IVFFlat L2 d={cfg['d']} N={cfg['n']} nlist={cfg['nlist']} "
+                               f"Q={cfg['nq']} nprobe={cfg['nprobe']} k={cfg['k']}"},
+        "cpu_baseline": {"value": v, "unit": "queries/s", "cores": base["cores"], "kind": base["kind"],
+                         "sample": base["sample"]},
+        "e2e": {"value": v, "unit": "queries/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="ivf20m")
+    ap.add_argument("--cpu-sample", type=int, default=64)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    cfg = CONFIGS[args.config]
+    if args.impl == "reference":
+        run_reference(args, cfg)
+    else:
+        run_ours(args, cfg)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,250 @@
+/*
+ * metalfaiss_b200 — C-ABI of the B200 (sm_100a) vector-search hot path.
+ *
+ * Conventions (every entry point):
+ *   - returns an int status: MF_OK (0) or one of the MF_ERR_* codes below; the
+ *     message of the last failure on the calling thread is mf_last_error().
+ *     Nothing aborts and no C++ exception crosses this boundary.
+ *   - `device` is the CUDA ordinal the call runs on; `stream` is a cudaStream_t
+ *     (NULL = legacy default stream). Work is stream-ordered; the call returns
+ *     once the kernels are enqueued.
+ *   - every array pointer is a caller-owned DEVICE pointer, 16-byte aligned;
+ *     vectors are row-major fp32 with a row length `d` that is a multiple of 4
+ *     (callers pad odd dimensions with zeros, which changes none of the four
+ *     metrics). Scratch memory is a caller-provided workspace whose size comes
+ *     from the matching *_workspace_size query; the library allocates nothing.
+ *   - distances follow the reference: L2 is the SQUARED distance clamped at 0,
+ *     INNER_PRODUCT is returned NEGATED and ranked ascending like the others.
+ *   - empty result slots hold distance +inf and label -1.
+ *
+ * The reference (MetalFaiss, Python on MLX) has no C library: each entry point
+ * below replaces a Python function or a Metal kernel launcher, cited beside it
+ * as file:line within the reference project.
+ */
+#ifndef METALFAISS_B200_H
+#define METALFAISS_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define MF_API __attribute__((visibility("default")))
+#else
+#define MF_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes 0..14 are ErrorCode of python/metalfaiss/errors.py:13-29. */
+enum {
+  MF_OK = 0,
+  MF_ERR_READONLY = 1,
+  MF_ERR_MEMORY = 2,
+  MF_ERR_IO = 3,
+  MF_ERR_RUNTIME = 4,
+  MF_ERR_NOT_IMPLEMENTED = 5,
+  MF_ERR_INVALID_ARGS = 6,
+  MF_ERR_BAD_STATE = 7,
+  MF_ERR_ASSERTION = 8,
+  MF_ERR_METRIC = 9,
+  MF_ERR_INDEX = 10,
+  MF_ERR_THREAD = 11,
+  MF_ERR_FILE_NOT_FOUND = 12,
+  MF_ERR_PERMISSION = 13,
+  MF_ERR_FORMAT = 14,
+  MF_ERR_CUDA = 100,    /* a CUDA runtime call failed */
+  MF_ERR_TIMEOUT = 101  /* a bounded device-side wait gave up */
+};
+
+/* Metric ids: the FAISS integers that python/metalfaiss/unittest/test_metric_type.py:29-40
+ * expects (the reference's own enums disagree with each other, python/metalfaiss/metric_type.py:10-21). */
+enum {
+  MF_METRIC_INNER_PRODUCT = 0,
+  MF_METRIC_L2 = 1,
+  MF_METRIC_L1 = 2,
+  MF_METRIC_LINF = 3
+};
+
+/* Library version (major*10000 + minor*100 + patch). */
+MF_API int mf_version(void);
+
+/* Message of the last failed call on this thread ("" if none). */
+MF_API const char* mf_last_error(void);
+
+/* Largest k (and nprobe) the fused top-k kernels accept. */
+MF_API int mf_max_k(void);
+
+/* Squared L2 norm of each row: norms[i] = sum_j x[i,j]^2.
+ * Replaces the norms_b term of pairwise_L2sqr, python/metalfaiss/distances.py:163-164,
+ * computed once at add time instead of on every search. */
+MF_API int mf_vector_norms(int device, void* stream, const float* x, int64_t n, int d,
+                    float* norms);
+
+/* ---------------------------------------------------------------- flat kNN */
+
+MF_API int mf_flat_search_workspace_size(int64_t nq, int64_t nb, int d, int metric, int k,
+                                  size_t* bytes);
+
+/* Exact kNN of xq (nq,d) against xb (nb,d): distances/labels (nq,k), ascending.
+ * labels[i,j] = ids[pos] when ids != NULL, else the row position pos.
+ * xb_norms (nb) is required for L2 and ignored otherwise.
+ * k is clipped by the caller to nb (python/metalfaiss/utils/sorting.py:66-67); here
+ * slots beyond nb are padded (+inf, -1).
+ * Replaces FlatIndex.search, python/metalfaiss/indexflat.py:70-110 (pairwise_L2sqr
+ * distances.py:140-173, -IP indexflat.py:93, L1/Linf indexflat.py:96-99, mlx_topk
+ * utils/sorting.py:39-87, id map indexflat.py:109) and the tuple-returning quantizer
+ * search python/metalfaiss/index/flat_index.py:70-121. */
+MF_API int mf_flat_search(int device, void* stream, const float* xq, int64_t nq,
+                   const float* xb, const float* xb_norms, int64_t nb, int d,
+                   int metric, int k, const int64_t* ids, float* distances,
+                   int64_t* labels, void* workspace, size_t workspace_bytes);
+
+/* ---------------------------------------------------------------- IVFFlat */
+
+/* Inverted lists are CSR: list l holds rows [list_offsets[l], list_offsets[l+1])
+ * of list_vecs (N,d), with list_norms (N) and list_ids (N).
+ * list_order (nlist, optional) is a permutation of the list ids giving the order
+ * in which the scan takes work (largest lists first balances the SMs). */
+
+MF_API int mf_ivf_search_workspace_size(int64_t nq, int nlist, int nprobe, int d, int metric,
+                                 int k, size_t* bytes);
+
+/* IVFFlat search: coarse top-nprobe over the centroids (L2), then the exact
+ * top-k over the union of the probed lists under `metric`.
+ * Replaces IVFFlatIndex.search, python/metalfaiss/index/ivf_flat_index.py:95-151
+ * (coarse step :113, gather :118-135, fused scan ivf_list_topk_l2
+ * python/metalfaiss/faissmlx/kernels/ivf_kernels.py:21-122,252-294, merge :211-250,364-379). */
+MF_API int mf_ivf_search(int device, void* stream, const float* xq, int64_t nq,
+                  const float* centroids, const float* centroid_norms, int nlist,
+                  int nprobe, const int64_t* list_offsets, const float* list_vecs,
+                  const float* list_norms, const int64_t* list_ids,
+                  const int32_t* list_order, int d, int metric, int k,
+                  float* distances, int64_t* labels, void* workspace,
+                  size_t workspace_bytes);
+
+MF_API int mf_ivf_search_preassigned_workspace_size(int64_t nq, int nlist, int nprobe, int d,
+                                             int metric, int k, size_t* bytes);
+
+/* The list-scan half of mf_ivf_search with caller-supplied probes (nq,nprobe)
+ * (list ids; negative entries are skipped). Replaces the per-query gather + fused
+ * kernel loop of python/metalfaiss/index/ivf_flat_index.py:115-151 and the
+ * search_preassigned call the reference tests expect
+ * (python/metalfaiss/unittest/test_mlx_index.py:64-69). */
+MF_API int mf_ivf_search_preassigned(int device, void* stream, const float* xq, int64_t nq,
+                              const int64_t* probes, int nprobe, int nlist,
+                              const int64_t* list_offsets, const float* list_vecs,
+                              const float* list_norms, const int64_t* list_ids,
+                              const int32_t* list_order, int d, int metric, int k,
+                              float* distances, int64_t* labels, void* workspace,
+                              size_t workspace_bytes);
+
+/* ----------------------------------------------------------- merge, k-means */
+
+/* Merge `parts` partial top-k lists per query: in (nq, parts, k_in) ascending,
+ * out (nq, k). Used for cross-split, cross-list and cross-GPU merges.
+ * Replaces device_topk_merge, python/metalfaiss/faissmlx/kernels/ivf_kernels.py:211-250,364-379. */
+MF_API int mf_topk_merge(int device, void* stream, const float* part_distances,
+                  const int64_t* part_labels, int64_t nq, int parts, int k_in, int k,
+                  float* distances, int64_t* labels);
+
+MF_API int mf_kmeans_assign_workspace_size(int64_t n, int nc, int d, size_t* bytes);
+
+/* k-means assignment: labels[i] = argmin_j ||x_i - c_j||^2 (ties: lowest j),
+ * min_distances[i] = that squared distance (may be NULL).
+ * Replaces python/metalfaiss/clustering/any_clustering.py:105-106 and
+ * python/metalfaiss/index/ivf_pq_index.py:66-67. */
+MF_API int mf_kmeans_assign(int device, void* stream, const float* x, int64_t n,
+                     const float* centroids, const float* centroid_norms, int nc, int d,
+                     int64_t* labels, float* min_distances, void* workspace,
+                     size_t workspace_bytes);
+
+MF_API int mf_kmeans_update_workspace_size(int64_t n, int nc, int d, size_t* bytes);
+
+/* k-means update: centroids[j] = mean of the rows assigned to j; a cluster with
+ * no rows keeps its previous centroid (updated in place). counts (nc) receives
+ * the cluster sizes. Sums are accumulated in fp64 in a fixed order (deterministic).
+ * Replaces python/metalfaiss/clustering/any_clustering.py:109-120 and
+ * python/metalfaiss/index/ivf_pq_index.py:68-78. */
+MF_API int mf_kmeans_update(int device, void* stream, const float* x, int64_t n, int d,
+                     const int64_t* labels, int nc, float* centroids, int64_t* counts,
+                     void* workspace, size_t workspace_bytes);
+
+/* ------------------------------------------------------------- IVF build */
+
+MF_API int mf_ivf_add_workspace_size(int64_t n_old, int64_t n_new, int nlist, size_t* bytes);
+
+/* Append n_new rows to the CSR lists. new_labels (n_new) are the coarse
+ * assignments (mf_kmeans_assign). Output CSR (caller-allocated, n_old + n_new
+ * rows) keeps every old row, in order, followed by the new rows of that list in
+ * input order (a stable counting sort by list id).
+ * Replaces IVFFlatIndex.add, python/metalfaiss/index/ivf_flat_index.py:74-93. */
+MF_API int mf_ivf_add(int device, void* stream, int nlist, int d,
+               const int64_t* old_offsets, const float* old_vecs,
+               const float* old_norms, const int64_t* old_ids, int64_t n_old,
+               const float* new_vecs, const float* new_norms, const int64_t* new_ids,
+               const int64_t* new_labels, int64_t n_new, int64_t* out_offsets,
+               float* out_vecs, float* out_norms, int64_t* out_ids, void* workspace,
+               size_t workspace_bytes);
+
+/* ---------------------------------------------------------- range search */
+
+MF_API int mf_flat_range_workspace_size(int64_t nq, int64_t nb, int d, size_t* bytes);
+
+/* Exact range search, first pass: lims (nq+1) gets the prefix sums of the
+ * per-query counts of rows with distance <= radius (ascending metrics; for
+ * INNER_PRODUCT the distance is -IP like everywhere else). *total receives lims[nq]
+ * (a host pointer; the call synchronizes the stream to read it).
+ * Replaces Index.range_search, python/metalfaiss/index.py:90-130, without its
+ * k=min(100,ntotal) cap (python/metalfaiss/index.py:104). */
+MF_API int mf_flat_range_count(int device, void* stream, const float* xq, int64_t nq,
+                        const float* xb, const float* xb_norms, int64_t nb, int d,
+                        int metric, float radius, int64_t* lims, int64_t* total,
+                        void* workspace, size_t workspace_bytes);
+
+/* Second pass: writes the (distance, label) pairs of each query at
+ * [lims[q], lims[q+1]) in row order. The workspace must be the one the count
+ * pass used, unchanged. */
+MF_API int mf_flat_range_fill(int device, void* stream, const float* xq, int64_t nq,
+                       const float* xb, const float* xb_norms, int64_t nb, int d,
+                       int metric, float radius, const int64_t* ids, const int64_t* lims,
+                       float* distances, int64_t* labels, void* workspace,
+                       size_t workspace_bytes);
+
+MF_API int mf_ivf_range_workspace_size(int64_t nq, int nlist, int nprobe, int d, size_t* bytes);
+
+/* IVF range search over the probed lists (coarse step as mf_ivf_search), count pass. */
+MF_API int mf_ivf_range_count(int device, void* stream, const float* xq, int64_t nq,
+                       const float* centroids, const float* centroid_norms, int nlist,
+                       int nprobe, const int64_t* list_offsets, const float* list_vecs,
+                       const float* list_norms, int d, int metric, float radius,
+                       int64_t* lims, int64_t* total, void* workspace,
+                       size_t workspace_bytes);
+
+/* IVF range search, fill pass (probe order, then row order within each list). */
+MF_API int mf_ivf_range_fill(int device, void* stream, const float* xq, int64_t nq,
+                      const float* centroids, const float* centroid_norms, int nlist,
+                      int nprobe, const int64_t* list_offsets, const float* list_vecs,
+                      const float* list_norms, const int64_t* list_ids, int d,
+                      int metric, float radius, const int64_t* lims, float* distances,
+                      int64_t* labels, void* workspace, size_t workspace_bytes);
+
+/* ------------------------------------------------------------- diagnostics */
+
+/* CUDA-event timing of this library's own launches, per kernel name
+ * ("scan_topk", "scan_range", "merge", "ivf_group", "norms"). Replaces the
+ * wall-clock median_time harness of python/metalfaiss/benchmarks/run_benchmarks.py:27-44
+ * with device-side times. mf_timing_read needs the streams synchronized. */
+MF_API int mf_timing_enable(int enable);
+MF_API int mf_timing_reset(void);
+MF_API int mf_timing_read(const char* kernel, double* total_ms, int64_t* launches);
+
+/* Number of kernels this library has launched in this process (all devices). */
+MF_API int64_t mf_launch_count(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* METALFAISS_B200_H */

@@ -1,0 +1,665 @@
+// extern "C" entry points (include/metalfaiss_b200.h): argument checks,
+// workspace planning and kernel sequencing. No entry point allocates memory.
+#include <cstdarg>
+#include <cstdio>
+#include <mutex>
+#include <string>
+
+#include "mf_ivf.cuh"
+#include "mf_scan.cuh"
+
+namespace mf {
+
+namespace {
+thread_local std::string g_last_error;
+std::mutex g_sm_mu;
+int g_sms[64] = {0};
+}  // namespace
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(MF_ERR_CUDA, "%s failed: %s (%s)", what, cudaGetErrorName(e),
+              cudaGetErrorString(e));
+}
+
+void clear_error() { g_last_error.clear(); }
+
+DeviceGuard::DeviceGuard(int device) {
+  if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess || device < 0 || device >= n) {
+    status = fail(MF_ERR_INVALID_ARGS, "invalid CUDA device %d (%d visible)", device, n);
+    return;
+  }
+  if (prev != device) {
+    cudaError_t e = cudaSetDevice(device);
+    if (e != cudaSuccess) status = cuda_fail(e, "cudaSetDevice");
+  }
+}
+
+DeviceGuard::~DeviceGuard() {
+  int cur = -1;
+  if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+}
+
+int check_device_ptr(const void* p, const char* name, bool allow_null) {
+  if (p == nullptr) {
+    if (allow_null) return MF_OK;
+    return fail(MF_ERR_INVALID_ARGS, "%s is NULL", name);
+  }
+  cudaPointerAttributes attr;
+  cudaError_t e = cudaPointerGetAttributes(&attr, p);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return fail(MF_ERR_INVALID_ARGS, "%s is not a CUDA pointer (%s)", name, cudaGetErrorName(e));
+  }
+  if (attr.type != cudaMemoryTypeDevice && attr.type != cudaMemoryTypeManaged)
+    return fail(MF_ERR_INVALID_ARGS, "%s must be device memory (got memory type %d)", name,
+                (int)attr.type);
+  int cur = -1;
+  cudaGetDevice(&cur);
+  if (attr.type == cudaMemoryTypeDevice && attr.device != cur)
+    return fail(MF_ERR_INVALID_ARGS, "%s lives on device %d, call targets device %d", name,
+                attr.device, cur);
+  if ((reinterpret_cast<uintptr_t>(p) & 15u) != 0)
+    return fail(MF_ERR_INVALID_ARGS, "%s is not 16-byte aligned", name);
+  return MF_OK;
+}
+
+int num_sms(int device) {
+  if (device < 0 || device >= 64) return 148;
+  std::lock_guard<std::mutex> lk(g_sm_mu);
+  if (g_sms[device] == 0) {
+    int v = 0;
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, device) != cudaSuccess || v <= 0)
+      v = 148;
+    g_sms[device] = v;
+  }
+  return g_sms[device];
+}
+
+namespace {
+
+int check_common(int d, int metric, int k, bool need_k) {
+  MF_CHECK(d > 0 && d % 4 == 0, MF_ERR_INVALID_ARGS,
+           "d=%d must be a positive multiple of 4 (pad rows with zeros)", d);
+  MF_CHECK(metric >= 0 && metric <= 3, MF_ERR_METRIC,
+           "metric %d is not one of INNER_PRODUCT(0), L2(1), L1(2), LINF(3)", metric);
+  if (need_k)
+    MF_CHECK(k >= 1 && k <= kMaxK, MF_ERR_INVALID_ARGS, "k=%d outside [1, %d]", k, kMaxK);
+  return MF_OK;
+}
+
+// ---- IVF workspace layout shared by search / range passes
+struct IvfWs {
+  float* qn;
+  float* coarse_d;
+  int64_t* coarse_l;
+  void* flat_ws;
+  size_t flat_bytes;
+  IvfGroups g;
+  float* pd;
+  int64_t* pl;
+  int64_t* pair_counts;
+  int64_t* pair_offsets64;
+};
+
+// mode: 0 = top-k search, 1 = preassigned top-k, 2 = range
+IvfWs carve_ivf(Carver& c, int64_t nq, int nlist, int P, int d, int k, int mode, int device) {
+  IvfWs w{};
+  w.qn = c.take<float>(nq);
+  if (mode != 1) {
+    w.coarse_d = c.take<float>((size_t)nq * P);
+    w.coarse_l = c.take<int64_t>((size_t)nq * P);
+    FlatPlan fp = plan_flat(nq, nlist, d, P, device);
+    w.flat_bytes = fp.bytes;
+    w.flat_ws = c.take<char>(fp.bytes);
+  }
+  w.g = carve_ivf_groups(c, nq, nlist, P);
+  if (mode == 2) {
+    w.pair_counts = c.take<int64_t>((size_t)nq * P);
+    w.pair_offsets64 = c.take<int64_t>((size_t)nq * P + 1);
+  } else {
+    w.pd = c.take<float>((size_t)nq * P * k);
+    w.pl = c.take<int64_t>((size_t)nq * P * k);
+  }
+  return w;
+}
+
+int effective_nprobe(int nprobe, int nlist) { return nprobe < nlist ? nprobe : nlist; }
+
+int coarse_metric(int metric) {
+  return metric == MF_METRIC_INNER_PRODUCT ? MF_METRIC_INNER_PRODUCT : MF_METRIC_L2;
+}
+
+int ivf_scan_topk(int device, cudaStream_t stream, const IvfWs& w, const float* xq, int64_t nq,
+                  const int64_t* probes, int P, int nlist, const int64_t* list_offsets,
+                  const float* list_vecs, const float* list_norms, const int64_t* list_ids,
+                  const int32_t* list_order, int d, int metric, int k, float* D, int64_t* I) {
+  if (metric == MF_METRIC_L2) MF_TRY(launch_norms(xq, nq, d, w.qn, stream));
+  MF_TRY(run_ivf_groups_ex(w.g, probes, nq, P, nlist, list_offsets, list_order, w.pd, w.pl, k,
+                           nullptr, stream));
+  ScanArgs a{};
+  a.xq = xq;
+  a.qnorms = w.qn;
+  a.xb = list_vecs;
+  a.xnorms = list_norms;
+  a.ids = list_ids;
+  a.d = d;
+  a.k = k;
+  a.nq = nq;
+  a.P = P;
+  a.flat = 0;
+  a.items = w.g.items;
+  a.item_total = w.g.item_total;
+  a.list_offsets = list_offsets;
+  a.pair_offsets = w.g.pair_offsets;
+  a.pairs = w.g.pairs;
+  a.counter = w.g.counter;
+  a.out_d = w.pd;
+  a.out_l = w.pl;
+  a.direct = 0;
+  MF_TRY(launch_scan(a, metric, kEpiTopK, nq * P, device, stream));
+  MF_TRY(launch_merge(w.pd, w.pl, nq, P, k, k, D, I, stream));
+  return MF_OK;
+}
+
+int check_ivf_lists(const int64_t* list_offsets, const float* list_vecs, const float* list_norms,
+                    const int64_t* list_ids, const int32_t* list_order, int metric) {
+  MF_TRY(check_device_ptr(list_offsets, "list_offsets"));
+  MF_TRY(check_device_ptr(list_vecs, "list_vecs", true));
+  MF_TRY(check_device_ptr(list_ids, "list_ids", true));
+  MF_TRY(check_device_ptr(list_norms, "list_norms", metric != MF_METRIC_L2));
+  MF_TRY(check_device_ptr(list_order, "list_order", true));
+  return MF_OK;
+}
+
+}  // namespace
+}  // namespace mf
+
+using namespace mf;
+
+#define MF_ENTER(device)                     \
+  clear_error();                             \
+  DeviceGuard _guard(device);                \
+  if (_guard.status != MF_OK) return _guard.status
+
+extern "C" {
+
+int mf_version(void) { return 100; }
+
+const char* mf_last_error(void) { return g_last_error.c_str(); }
+
+int mf_max_k(void) { return kMaxK; }
+
+int mf_vector_norms(int device, void* stream, const float* x, int64_t n, int d, float* norms) {
+  MF_ENTER(device);
+  MF_CHECK(n >= 0 && d > 0 && d % 4 == 0, MF_ERR_INVALID_ARGS, "bad shape n=%lld d=%d",
+           (long long)n, d);
+  if (n == 0) return MF_OK;
+  MF_TRY(check_device_ptr(x, "x"));
+  MF_TRY(check_device_ptr(norms, "norms"));
+  return launch_norms(x, n, d, norms, (cudaStream_t)stream);
+}
+
+int mf_flat_search_workspace_size(int64_t nq, int64_t nb, int d, int metric, int k,
+                                  size_t* bytes) {
+  clear_error();
+  MF_CHECK(bytes != nullptr, MF_ERR_INVALID_ARGS, "bytes is NULL");
+  MF_TRY(check_common(d, metric, k, true));
+  int dev = 0;
+  cudaGetDevice(&dev);
+  *bytes = plan_flat(nq, nb, d, k, dev).bytes;
+  return MF_OK;
+}
+
+int mf_flat_search(int device, void* stream, const float* xq, int64_t nq, const float* xb,
+                   const float* xb_norms, int64_t nb, int d, int metric, int k,
+                   const int64_t* ids, float* distances, int64_t* labels, void* workspace,
+                   size_t workspace_bytes) {
+  MF_ENTER(device);
+  MF_TRY(check_common(d, metric, k, true));
+  MF_CHECK(nq >= 0 && nb >= 0, MF_ERR_INVALID_ARGS, "negative sizes");
+  MF_CHECK(nb < (1ll << 31) - 1, MF_ERR_INVALID_ARGS, "nb=%lld exceeds 2^31-2 rows per call",
+           (long long)nb);
+  MF_CHECK(nq < (1ll << 31) / 2, MF_ERR_INVALID_ARGS, "nq too large");
+  if (nq == 0) return MF_OK;
+  MF_TRY(check_device_ptr(xq, "xq"));
+  MF_TRY(check_device_ptr(distances, "distances"));
+  MF_TRY(check_device_ptr(labels, "labels"));
+  MF_TRY(check_device_ptr(xb, "xb", nb == 0));
+  MF_TRY(check_device_ptr(ids, "ids", true));
+  if (metric == MF_METRIC_L2) MF_TRY(check_device_ptr(xb_norms, "xb_norms", nb == 0));
+  MF_TRY(check_device_ptr(workspace, "workspace", true));
+  return run_flat_topk(device, (cudaStream_t)stream, xq, nq, xb, xb_norms, nb, d, metric, k, ids,
+                       distances, labels, workspace, workspace_bytes);
+}
+
+int mf_ivf_search_workspace_size(int64_t nq, int nlist, int nprobe, int d, int metric, int k,
+                                 size_t* bytes) {
+  clear_error();
+  MF_CHECK(bytes != nullptr, MF_ERR_INVALID_ARGS, "bytes is NULL");
+  MF_TRY(check_common(d, metric, k, true));
+  MF_CHECK(nlist >= 1 && nprobe >= 1, MF_ERR_INVALID_ARGS, "nlist=%d nprobe=%d", nlist, nprobe);
+  int dev = 0;
+  cudaGetDevice(&dev);
+  Carver c(nullptr, 0);
+  carve_ivf(c, nq, nlist, effective_nprobe(nprobe, nlist), d, k, 0, dev);
+  *bytes = c.used;
+  return MF_OK;
+}
+
+int mf_ivf_search(int device, void* stream, const float* xq, int64_t nq,
+                  const float* centroids, const float* centroid_norms, int nlist, int nprobe,
+                  const int64_t* list_offsets, const float* list_vecs, const float* list_norms,
+                  const int64_t* list_ids, const int32_t* list_order, int d, int metric, int k,
+                  float* distances, int64_t* labels, void* workspace, size_t workspace_bytes) {
+  MF_ENTER(device);
+  MF_TRY(check_common(d, metric, k, true));
+  MF_CHECK(nlist >= 1, MF_ERR_INVALID_ARGS, "nlist=%d", nlist);
+  MF_CHECK(nprobe >= 1, MF_ERR_INVALID_ARGS, "nprobe must be positive (got %d)", nprobe);
+  const int P = effective_nprobe(nprobe, nlist);
+  MF_CHECK(P <= kMaxK, MF_ERR_INVALID_ARGS, "nprobe=%d exceeds %d", P, kMaxK);
+  MF_CHECK(nq >= 0 && nq * P < (1ll << 31), MF_ERR_INVALID_ARGS, "nq*nprobe too large");
+  if (nq == 0) return MF_OK;
+  MF_TRY(check_device_ptr(xq, "xq"));
+  MF_TRY(check_device_ptr(centroids, "centroids"));
+  MF_TRY(check_device_ptr(centroid_norms, "centroid_norms", coarse_metric(metric) != MF_METRIC_L2));
+  MF_TRY(check_ivf_lists(list_offsets, list_vecs, list_norms, list_ids, list_order, metric));
+  MF_TRY(check_device_ptr(distances, "distances"));
+  MF_TRY(check_device_ptr(labels, "labels"));
+  MF_TRY(check_device_ptr(workspace, "workspace"));
+  Carver c(workspace, workspace_bytes);
+  IvfWs w = carve_ivf(c, nq, nlist, P, d, k, 0, device);
+  MF_CHECK(c.fits(), MF_ERR_INVALID_ARGS, "IVF search workspace too small: %zu < %zu bytes",
+           workspace_bytes, c.used);
+  cudaStream_t s = (cudaStream_t)stream;
+  MF_TRY(run_flat_topk(device, s, xq, nq, centroids, centroid_norms, nlist, d,
+                       coarse_metric(metric), P, nullptr, w.coarse_d, w.coarse_l, w.flat_ws,
+                       w.flat_bytes));
+  return ivf_scan_topk(device, s, w, xq, nq, w.coarse_l, P, nlist, list_offsets, list_vecs,
+                       list_norms, list_ids, list_order, d, metric, k, distances, labels);
+}
+
+int mf_ivf_search_preassigned_workspace_size(int64_t nq, int nlist, int nprobe, int d,
+                                             int metric, int k, size_t* bytes) {
+  clear_error();
+  MF_CHECK(bytes != nullptr, MF_ERR_INVALID_ARGS, "bytes is NULL");
+  MF_TRY(check_common(d, metric, k, true));
+  MF_CHECK(nlist >= 1 && nprobe >= 1, MF_ERR_INVALID_ARGS, "nlist=%d nprobe=%d", nlist, nprobe);
+  Carver c(nullptr, 0);
+  carve_ivf(c, nq, nlist, nprobe, d, k, 1, 0);
+  *bytes = c.used;
+  return MF_OK;
+}
+
+int mf_ivf_search_preassigned(int device, void* stream, const float* xq, int64_t nq,
+                              const int64_t* probes, int nprobe, int nlist,
+                              const int64_t* list_offsets, const float* list_vecs,
+                              const float* list_norms, const int64_t* list_ids,
+                              const int32_t* list_order, int d, int metric, int k,
+                              float* distances, int64_t* labels, void* workspace,
+                              size_t workspace_bytes) {
+  MF_ENTER(device);
+  MF_TRY(check_common(d, metric, k, true));
+  MF_CHECK(nlist >= 1 && nprobe >= 1, MF_ERR_INVALID_ARGS, "nlist=%d nprobe=%d", nlist, nprobe);
+  MF_CHECK(nq >= 0 && nq * nprobe < (1ll << 31), MF_ERR_INVALID_ARGS, "nq*nprobe too large");
+  if (nq == 0) return MF_OK;
+  MF_TRY(check_device_ptr(xq, "xq"));
+  MF_TRY(check_device_ptr(probes, "probes"));
+  MF_TRY(check_ivf_lists(list_offsets, list_vecs, list_norms, list_ids, list_order, metric));
+  MF_TRY(check_device_ptr(distances, "distances"));
+  MF_TRY(check_device_ptr(labels, "labels"));
+  MF_TRY(check_device_ptr(workspace, "workspace"));
+  Carver c(workspace, workspace_bytes);
+  IvfWs w = carve_ivf(c, nq, nlist, nprobe, d, k, 1, device);
+  MF_CHECK(c.fits(), MF_ERR_INVALID_ARGS, "workspace too small: %zu < %zu bytes",
+           workspace_bytes, c.used);
+  return ivf_scan_topk(device, (cudaStream_t)stream, w, xq, nq, probes, nprobe, nlist,
+                       list_offsets, list_vecs, list_norms, list_ids, list_order, d, metric, k,
+                       distances, labels);
+}
+
+int mf_topk_merge(int device, void* stream, const float* part_distances,
+                  const int64_t* part_labels, int64_t nq, int parts, int k_in, int k,
+                  float* distances, int64_t* labels) {
+  MF_ENTER(device);
+  MF_CHECK(k >= 1 && k <= kMaxK, MF_ERR_INVALID_ARGS, "k=%d outside [1, %d]", k, kMaxK);
+  MF_CHECK(parts >= 1 && k_in >= 0 && nq >= 0, MF_ERR_INVALID_ARGS, "bad merge shape");
+  if (nq == 0) return MF_OK;
+  MF_TRY(check_device_ptr(part_distances, "part_distances", k_in == 0));
+  MF_TRY(check_device_ptr(part_labels, "part_labels", k_in == 0));
+  MF_TRY(check_device_ptr(distances, "distances"));
+  MF_TRY(check_device_ptr(labels, "labels"));
+  return launch_merge(part_distances, part_labels, nq, parts, k_in, k, distances, labels,
+                      (cudaStream_t)stream);
+}
+
+int mf_kmeans_assign_workspace_size(int64_t n, int nc, int d, size_t* bytes) {
+  return mf_flat_search_workspace_size(n, nc, d, MF_METRIC_L2, 1, bytes);
+}
+
+int mf_kmeans_assign(int device, void* stream, const float* x, int64_t n,
+                     const float* centroids, const float* centroid_norms, int nc, int d,
+                     int64_t* labels, float* min_distances, void* workspace,
+                     size_t workspace_bytes) {
+  MF_ENTER(device);
+  MF_TRY(check_common(d, MF_METRIC_L2, 1, true));
+  MF_CHECK(nc >= 1, MF_ERR_INVALID_ARGS, "need at least one centroid");
+  MF_CHECK(n >= 0 && n < (1ll << 30), MF_ERR_INVALID_ARGS, "n=%lld out of range", (long long)n);
+  if (n == 0) return MF_OK;
+  MF_TRY(check_device_ptr(x, "x"));
+  MF_TRY(check_device_ptr(centroids, "centroids"));
+  MF_TRY(check_device_ptr(centroid_norms, "centroid_norms"));
+  MF_TRY(check_device_ptr(labels, "labels"));
+  MF_TRY(check_device_ptr(min_distances, "min_distances"));
+  MF_TRY(check_device_ptr(workspace, "workspace", true));
+  return run_flat_topk(device, (cudaStream_t)stream, x, n, centroids, centroid_norms, nc, d,
+                       MF_METRIC_L2, 1, nullptr, min_distances, labels, workspace,
+                       workspace_bytes);
+}
+
+int mf_kmeans_update_workspace_size(int64_t n, int nc, int d, size_t* bytes) {
+  clear_error();
+  (void)d;
+  MF_CHECK(bytes != nullptr, MF_ERR_INVALID_ARGS, "bytes is NULL");
+  *bytes = kmeans_update_bytes(n, nc);
+  return MF_OK;
+}
+
+int mf_kmeans_update(int device, void* stream, const float* x, int64_t n, int d,
+                     const int64_t* labels, int nc, float* centroids, int64_t* counts,
+                     void* workspace, size_t workspace_bytes) {
+  MF_ENTER(device);
+  MF_CHECK(d > 0 && nc >= 1 && n >= 0 && n < (1ll << 31) - 1, MF_ERR_INVALID_ARGS,
+           "bad k-means update shape n=%lld d=%d nc=%d", (long long)n, d, nc);
+  MF_TRY(check_device_ptr(x, "x", n == 0));
+  MF_TRY(check_device_ptr(labels, "labels", n == 0));
+  MF_TRY(check_device_ptr(centroids, "centroids"));
+  MF_TRY(check_device_ptr(counts, "counts", true));
+  MF_TRY(check_device_ptr(workspace, "workspace"));
+  MF_CHECK(workspace_bytes >= kmeans_update_bytes(n, nc), MF_ERR_INVALID_ARGS,
+           "k-means update workspace too small: %zu < %zu", workspace_bytes,
+           kmeans_update_bytes(n, nc));
+  return run_kmeans_update((cudaStream_t)stream, x, n, d, labels, nc, centroids, counts,
+                           workspace, workspace_bytes);
+}
+
+int mf_ivf_add_workspace_size(int64_t n_old, int64_t n_new, int nlist, size_t* bytes) {
+  clear_error();
+  (void)n_old;
+  MF_CHECK(bytes != nullptr, MF_ERR_INVALID_ARGS, "bytes is NULL");
+  *bytes = ivf_add_bytes(n_new, nlist);
+  return MF_OK;
+}
+
+int mf_ivf_add(int device, void* stream, int nlist, int d, const int64_t* old_offsets,
+               const float* old_vecs, const float* old_norms, const int64_t* old_ids,
+               int64_t n_old, const float* new_vecs, const float* new_norms,
+               const int64_t* new_ids, const int64_t* new_labels, int64_t n_new,
+               int64_t* out_offsets, float* out_vecs, float* out_norms, int64_t* out_ids,
+               void* workspace, size_t workspace_bytes) {
+  MF_ENTER(device);
+  MF_CHECK(nlist >= 1 && d > 0 && d % 4 == 0, MF_ERR_INVALID_ARGS, "nlist=%d d=%d", nlist, d);
+  MF_CHECK(n_old >= 0 && n_new >= 0 && n_new < (1ll << 31) - 1, MF_ERR_INVALID_ARGS,
+           "bad row counts");
+  if (n_old > 0) {
+    MF_TRY(check_device_ptr(old_offsets, "old_offsets"));
+    MF_TRY(check_device_ptr(old_vecs, "old_vecs"));
+    MF_TRY(check_device_ptr(old_norms, "old_norms"));
+    MF_TRY(check_device_ptr(old_ids, "old_ids"));
+  }
+  if (n_new > 0) {
+    MF_TRY(check_device_ptr(new_vecs, "new_vecs"));
+    MF_TRY(check_device_ptr(new_norms, "new_norms"));
+    MF_TRY(check_device_ptr(new_ids, "new_ids"));
+    MF_TRY(check_device_ptr(new_labels, "new_labels"));
+  }
+  MF_TRY(check_device_ptr(out_offsets, "out_offsets"));
+  if (n_old + n_new > 0) {
+    MF_TRY(check_device_ptr(out_vecs, "out_vecs"));
+    MF_TRY(check_device_ptr(out_norms, "out_norms"));
+    MF_TRY(check_device_ptr(out_ids, "out_ids"));
+  }
+  MF_TRY(check_device_ptr(workspace, "workspace"));
+  MF_CHECK(workspace_bytes >= ivf_add_bytes(n_new, nlist), MF_ERR_INVALID_ARGS,
+           "ivf add workspace too small");
+  return run_ivf_add((cudaStream_t)stream, nlist, d, old_offsets, old_vecs, old_norms, old_ids,
+                     n_old, new_vecs, new_norms, new_ids, new_labels, n_new, out_offsets,
+                     out_vecs, out_norms, out_ids, workspace, workspace_bytes);
+}
+
+// ------------------------------------------------------------ range search
+int mf_flat_range_workspace_size(int64_t nq, int64_t nb, int d, size_t* bytes) {
+  clear_error();
+  MF_CHECK(bytes != nullptr, MF_ERR_INVALID_ARGS, "bytes is NULL");
+  int dev = 0;
+  cudaGetDevice(&dev);
+  FlatPlan p = plan_flat(nq, nb, d, 32, dev);
+  Carver c(nullptr, 0);
+  c.take<float>(nq);
+  c.take<int>(1);
+  c.take<int64_t>((size_t)nq * p.splits);
+  c.take<int64_t>((size_t)nq * p.splits + 1);
+  *bytes = c.used;
+  return MF_OK;
+}
+
+namespace {
+struct FlatRangeWs {
+  FlatPlan p;
+  float* qn;
+  int* counter;
+  int64_t* counts;
+  int64_t* offsets;
+};
+int carve_flat_range(FlatRangeWs& w, int64_t nq, int64_t nb, int d, int device, void* ws,
+                     size_t bytes) {
+  w.p = plan_flat(nq, nb, d, 32, device);
+  Carver c(ws, bytes);
+  w.qn = c.take<float>(nq);
+  w.counter = c.take<int>(1);
+  w.counts = c.take<int64_t>((size_t)nq * w.p.splits);
+  w.offsets = c.take<int64_t>((size_t)nq * w.p.splits + 1);
+  MF_CHECK(c.fits(), MF_ERR_INVALID_ARGS, "range workspace too small: %zu < %zu", bytes, c.used);
+  return MF_OK;
+}
+ScanArgs flat_range_args(const FlatRangeWs& w, const float* xq, int64_t nq, const float* xb,
+                         const float* xb_norms, int64_t nb, int d, float radius) {
+  ScanArgs a{};
+  a.xq = xq;
+  a.qnorms = w.qn;
+  a.xb = xb;
+  a.xnorms = xb_norms;
+  a.d = d;
+  a.k = 1;
+  a.nq = nq;
+  a.P = w.p.splits;
+  a.flat = 1;
+  a.nqt = w.p.nqt;
+  a.nb = nb;
+  a.rows_per_split = w.p.rows_per_split;
+  a.counter = w.counter;
+  a.radius = radius;
+  a.counts = w.counts;
+  a.offsets = w.offsets;
+  return a;
+}
+int read_total(const int64_t* dev_total, int64_t* total, cudaStream_t s) {
+  MF_CUDA(cudaMemcpyAsync(total, dev_total, sizeof(int64_t), cudaMemcpyDeviceToHost, s));
+  MF_CUDA(cudaStreamSynchronize(s));
+  return MF_OK;
+}
+}  // namespace
+
+int mf_flat_range_count(int device, void* stream, const float* xq, int64_t nq, const float* xb,
+                        const float* xb_norms, int64_t nb, int d, int metric, float radius,
+                        int64_t* lims, int64_t* total, void* workspace, size_t workspace_bytes) {
+  MF_ENTER(device);
+  MF_TRY(check_common(d, metric, 1, false));
+  MF_CHECK(total != nullptr, MF_ERR_INVALID_ARGS, "total is NULL");
+  MF_CHECK(nb < (1ll << 31) - 1 && nq >= 0, MF_ERR_INVALID_ARGS, "bad sizes");
+  MF_TRY(check_device_ptr(lims, "lims"));
+  *total = 0;
+  cudaStream_t s = (cudaStream_t)stream;
+  if (nq == 0) {
+    MF_CUDA(cudaMemsetAsync(lims, 0, sizeof(int64_t), s));
+    return MF_OK;
+  }
+  MF_TRY(check_device_ptr(xq, "xq"));
+  MF_TRY(check_device_ptr(xb, "xb", nb == 0));
+  if (metric == MF_METRIC_L2) MF_TRY(check_device_ptr(xb_norms, "xb_norms", nb == 0));
+  MF_TRY(check_device_ptr(workspace, "workspace"));
+  FlatRangeWs w;
+  MF_TRY(carve_flat_range(w, nq, nb, d, device, workspace, workspace_bytes));
+  if (metric == MF_METRIC_L2) MF_TRY(launch_norms(xq, nq, d, w.qn, s));
+  MF_CUDA(cudaMemsetAsync(w.counts, 0, sizeof(int64_t) * nq * w.p.splits, s));
+  ScanArgs a = flat_range_args(w, xq, nq, xb, xb_norms, nb, d, radius);
+  if (nb > 0) MF_TRY(launch_scan(a, metric, kEpiCount, (int64_t)w.p.nqt * w.p.splits, device, s));
+  MF_TRY(launch_exclusive_scan_i64(w.counts, nq * w.p.splits, w.offsets, s));
+  MF_TRY(launch_lims(w.offsets, nq, w.p.splits, lims, s));
+  return read_total(w.offsets + nq * w.p.splits, total, s);
+}
+
+int mf_flat_range_fill(int device, void* stream, const float* xq, int64_t nq, const float* xb,
+                       const float* xb_norms, int64_t nb, int d, int metric, float radius,
+                       const int64_t* ids, const int64_t* lims, float* distances,
+                       int64_t* labels, void* workspace, size_t workspace_bytes) {
+  MF_ENTER(device);
+  MF_TRY(check_common(d, metric, 1, false));
+  (void)lims;
+  if (nq == 0 || nb == 0) return MF_OK;
+  MF_TRY(check_device_ptr(xq, "xq"));
+  MF_TRY(check_device_ptr(xb, "xb"));
+  MF_TRY(check_device_ptr(ids, "ids", true));
+  MF_TRY(check_device_ptr(distances, "distances", true));
+  MF_TRY(check_device_ptr(labels, "labels", true));
+  MF_TRY(check_device_ptr(workspace, "workspace"));
+  FlatRangeWs w;
+  MF_TRY(carve_flat_range(w, nq, nb, d, device, workspace, workspace_bytes));
+  ScanArgs a = flat_range_args(w, xq, nq, xb, xb_norms, nb, d, radius);
+  a.ids = ids;
+  a.out_d = distances;
+  a.out_l = labels;
+  return launch_scan(a, metric, kEpiFill, (int64_t)w.p.nqt * w.p.splits, device,
+                     (cudaStream_t)stream);
+}
+
+int mf_ivf_range_workspace_size(int64_t nq, int nlist, int nprobe, int d, size_t* bytes) {
+  clear_error();
+  MF_CHECK(bytes != nullptr, MF_ERR_INVALID_ARGS, "bytes is NULL");
+  MF_CHECK(nlist >= 1 && nprobe >= 1, MF_ERR_INVALID_ARGS, "nlist=%d nprobe=%d", nlist, nprobe);
+  int dev = 0;
+  cudaGetDevice(&dev);
+  Carver c(nullptr, 0);
+  carve_ivf(c, nq, nlist, effective_nprobe(nprobe, nlist), d, 1, 2, dev);
+  *bytes = c.used;
+  return MF_OK;
+}
+
+namespace {
+ScanArgs ivf_range_args(const IvfWs& w, const float* xq, int64_t nq, int P,
+                        const int64_t* list_offsets, const float* list_vecs,
+                        const float* list_norms, int d, float radius) {
+  ScanArgs a{};
+  a.xq = xq;
+  a.qnorms = w.qn;
+  a.xb = list_vecs;
+  a.xnorms = list_norms;
+  a.d = d;
+  a.k = 1;
+  a.nq = nq;
+  a.P = P;
+  a.flat = 0;
+  a.items = w.g.items;
+  a.item_total = w.g.item_total;
+  a.list_offsets = list_offsets;
+  a.pair_offsets = w.g.pair_offsets;
+  a.pairs = w.g.pairs;
+  a.counter = w.g.counter;
+  a.radius = radius;
+  a.counts = w.pair_counts;
+  a.offsets = w.pair_offsets64;
+  return a;
+}
+}  // namespace
+
+int mf_ivf_range_count(int device, void* stream, const float* xq, int64_t nq,
+                       const float* centroids, const float* centroid_norms, int nlist,
+                       int nprobe, const int64_t* list_offsets, const float* list_vecs,
+                       const float* list_norms, int d, int metric, float radius, int64_t* lims,
+                       int64_t* total, void* workspace, size_t workspace_bytes) {
+  MF_ENTER(device);
+  MF_TRY(check_common(d, metric, 1, false));
+  MF_CHECK(total != nullptr, MF_ERR_INVALID_ARGS, "total is NULL");
+  MF_CHECK(nlist >= 1 && nprobe >= 1, MF_ERR_INVALID_ARGS, "nlist=%d nprobe=%d", nlist, nprobe);
+  const int P = effective_nprobe(nprobe, nlist);
+  MF_CHECK(P <= kMaxK, MF_ERR_INVALID_ARGS, "nprobe=%d exceeds %d", P, kMaxK);
+  MF_CHECK(nq >= 0 && nq * P < (1ll << 31), MF_ERR_INVALID_ARGS, "nq*nprobe too large");
+  MF_TRY(check_device_ptr(lims, "lims"));
+  *total = 0;
+  cudaStream_t s = (cudaStream_t)stream;
+  if (nq == 0) {
+    MF_CUDA(cudaMemsetAsync(lims, 0, sizeof(int64_t), s));
+    return MF_OK;
+  }
+  MF_TRY(check_device_ptr(xq, "xq"));
+  MF_TRY(check_device_ptr(centroids, "centroids"));
+  MF_TRY(check_device_ptr(centroid_norms, "centroid_norms", coarse_metric(metric) != MF_METRIC_L2));
+  MF_TRY(check_ivf_lists(list_offsets, list_vecs, list_norms, nullptr, nullptr, metric));
+  MF_TRY(check_device_ptr(workspace, "workspace"));
+  Carver c(workspace, workspace_bytes);
+  IvfWs w = carve_ivf(c, nq, nlist, P, d, 1, 2, device);
+  MF_CHECK(c.fits(), MF_ERR_INVALID_ARGS, "IVF range workspace too small");
+  MF_TRY(run_flat_topk(device, s, xq, nq, centroids, centroid_norms, nlist, d,
+                       coarse_metric(metric), P, nullptr, w.coarse_d, w.coarse_l, w.flat_ws,
+                       w.flat_bytes));
+  if (metric == MF_METRIC_L2) MF_TRY(launch_norms(xq, nq, d, w.qn, s));
+  MF_TRY(run_ivf_groups_ex(w.g, w.coarse_l, nq, P, nlist, list_offsets, nullptr, nullptr,
+                           nullptr, 0, w.pair_counts, s));
+  ScanArgs a = ivf_range_args(w, xq, nq, P, list_offsets, list_vecs, list_norms, d, radius);
+  MF_TRY(launch_scan(a, metric, kEpiCount, nq * P, device, s));
+  MF_TRY(launch_exclusive_scan_i64(w.pair_counts, nq * P, w.pair_offsets64, s));
+  MF_TRY(launch_lims(w.pair_offsets64, nq, P, lims, s));
+  return read_total(w.pair_offsets64 + nq * P, total, s);
+}
+
+int mf_ivf_range_fill(int device, void* stream, const float* xq, int64_t nq,
+                      const float* centroids, const float* centroid_norms, int nlist, int nprobe,
+                      const int64_t* list_offsets, const float* list_vecs,
+                      const float* list_norms, const int64_t* list_ids, int d, int metric,
+                      float radius, const int64_t* lims, float* distances, int64_t* labels,
+                      void* workspace, size_t workspace_bytes) {
+  MF_ENTER(device);
+  MF_TRY(check_common(d, metric, 1, false));
+  (void)centroids;
+  (void)centroid_norms;
+  (void)lims;
+  MF_CHECK(nlist >= 1 && nprobe >= 1, MF_ERR_INVALID_ARGS, "nlist=%d nprobe=%d", nlist, nprobe);
+  const int P = effective_nprobe(nprobe, nlist);
+  if (nq == 0) return MF_OK;
+  MF_TRY(check_device_ptr(xq, "xq"));
+  MF_TRY(check_ivf_lists(list_offsets, list_vecs, list_norms, list_ids, nullptr, metric));
+  MF_TRY(check_device_ptr(distances, "distances", true));
+  MF_TRY(check_device_ptr(labels, "labels", true));
+  MF_TRY(check_device_ptr(workspace, "workspace"));
+  Carver c(workspace, workspace_bytes);
+  IvfWs w = carve_ivf(c, nq, nlist, P, d, 1, 2, device);
+  MF_CHECK(c.fits(), MF_ERR_INVALID_ARGS, "IVF range workspace too small");
+  ScanArgs a = ivf_range_args(w, xq, nq, P, list_offsets, list_vecs, list_norms, d, radius);
+  a.ids = list_ids;
+  a.out_d = distances;
+  a.out_l = labels;
+  return launch_scan(a, metric, kEpiFill, nq * P, device, (cudaStream_t)stream);
+}
+
+}  // extern "C"

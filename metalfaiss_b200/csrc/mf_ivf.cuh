@@ -1,0 +1,33 @@
+// Host-side entry points of mf_ivf.cu used by the C-ABI layer.
+#pragma once
+
+#include "mf_scan.cuh"
+
+namespace mf {
+
+int launch_exclusive_scan_i32(const int* in, int64_t n, int* out, cudaStream_t stream);
+int launch_lims(const int64_t* offsets, int64_t nq, int P, int64_t* lims, cudaStream_t stream);
+int launch_iota_i32(int32_t* out, int64_t n, cudaStream_t stream);
+
+// Grouping that also pre-fills the partial slots (pd/pl, k per slot) or the
+// per-pair range counts of pairs whose list is empty or out of range.
+int run_ivf_groups_ex(const IvfGroups& g, const int64_t* probes, int64_t nq, int P, int nlist,
+                      const int64_t* list_offsets, const int32_t* list_order, float* pd,
+                      int64_t* pl, int k, int64_t* pair_counts, cudaStream_t stream);
+
+size_t radix_sort_bytes(int64_t n);
+
+size_t ivf_add_bytes(int64_t n_new, int nlist);
+int run_ivf_add(cudaStream_t stream, int nlist, int d, const int64_t* old_offsets,
+                const float* old_vecs, const float* old_norms, const int64_t* old_ids,
+                int64_t n_old, const float* new_vecs, const float* new_norms,
+                const int64_t* new_ids, const int64_t* new_labels, int64_t n_new,
+                int64_t* out_offsets, float* out_vecs, float* out_norms, int64_t* out_ids,
+                void* ws, size_t ws_bytes);
+
+size_t kmeans_update_bytes(int64_t n, int nc);
+int run_kmeans_update(cudaStream_t stream, const float* x, int64_t n, int d,
+                      const int64_t* labels, int nc, float* centroids, int64_t* counts, void* ws,
+                      size_t ws_bytes);
+
+}  // namespace mf

@@ -1,0 +1,525 @@
+// Slab-scan kernels (SIMT, sm_100a): fused distance tile + per-query warp
+// top-k, and the range-search count/fill epilogues. See mf_scan.cuh.
+#include "mf_scan.cuh"
+#include "mf_timing.cuh"
+#include "mf_topk.cuh"
+
+#include <mutex>
+
+namespace mf {
+
+namespace {
+
+template <int METRIC>
+__device__ __forceinline__ void accum_tile(float (&acc)[4][4], const float4 (&xv)[4],
+                                           const float4 (&qv)[4]) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float a = acc[i][j];
+      if (METRIC == MF_METRIC_L2 || METRIC == MF_METRIC_INNER_PRODUCT) {
+        a = fmaf(xv[i].x, qv[j].x, a);
+        a = fmaf(xv[i].y, qv[j].y, a);
+        a = fmaf(xv[i].z, qv[j].z, a);
+        a = fmaf(xv[i].w, qv[j].w, a);
+      } else if (METRIC == MF_METRIC_L1) {
+        a += fabsf(xv[i].x - qv[j].x);
+        a += fabsf(xv[i].y - qv[j].y);
+        a += fabsf(xv[i].z - qv[j].z);
+        a += fabsf(xv[i].w - qv[j].w);
+      } else {
+        a = fmaxf(a, fabsf(xv[i].x - qv[j].x));
+        a = fmaxf(a, fabsf(xv[i].y - qv[j].y));
+        a = fmaxf(a, fabsf(xv[i].z - qv[j].z));
+        a = fmaxf(a, fabsf(xv[i].w - qv[j].w));
+      }
+      acc[i][j] = a;
+    }
+  }
+}
+
+struct ScanSmemLayout {
+  static constexpr size_t xs_bytes = size_t(kScanStages) * kScanTR * kScanXS * 4;
+  static constexpr size_t qs_bytes = size_t(kScanStages) * kScanTQ * kScanXS * 4;
+  static constexpr size_t meta_bytes = kScanTQ * (8 + 8 + 4 + 4);
+  static size_t bytes(int epi, int kcap) {
+    size_t b = xs_bytes + qs_bytes + meta_bytes;
+    if (epi == kEpiTopK) b += size_t(kScanTQ) * (kcap + 32) * 8;
+    return b;
+  }
+};
+
+template <int METRIC, int KCAP, int EPI>
+__global__ void __launch_bounds__(kScanThreads) scan_kernel(const ScanArgs a) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  float* xs = reinterpret_cast<float*>(smem_raw);
+  float* qs = xs + kScanStages * kScanTR * kScanXS;
+  long long* s_qout = reinterpret_cast<long long*>(qs + kScanStages * kScanTQ * kScanXS);
+  long long* s_off = s_qout + kScanTQ;
+  int* s_qrow = reinterpret_cast<int*>(s_off + kScanTQ);
+  float* s_qn = reinterpret_cast<float*>(s_qrow + kScanTQ);
+  unsigned long long* lists = reinterpret_cast<unsigned long long*>(s_qn + kScanTQ);
+  unsigned long long* bufs = lists + kScanTQ * KCAP;
+
+  __shared__ int s_item;
+  __shared__ long long s_rb, s_re;
+
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int warp = tid >> 5;
+  const int d = a.d;
+  const int k = a.k;
+  const int nchunks = (d + kScanDC - 1) / kScanDC;
+
+  for (;;) {
+    if (tid == 0) s_item = atomicAdd(a.counter, 1);
+    __syncthreads();
+    const int item = s_item;
+    const int total = a.flat ? a.nqt * a.P : *a.item_total;
+    if (item >= total) break;
+
+    // ---- describe the work item: queries, output slots, row slab
+    if (a.flat) {
+      const int qt = item % a.nqt;
+      const int s = item / a.nqt;
+      if (tid < kScanTQ) {
+        long long q = (long long)qt * kScanTQ + tid;
+        bool v = q < a.nq;
+        s_qrow[tid] = v ? (int)q : -1;
+        s_qout[tid] = v ? (a.direct ? q : q * a.P + s) : -1;
+      }
+      if (tid == 0) {
+        long long rb = (long long)s * a.rows_per_split;
+        long long re = rb + a.rows_per_split;
+        s_rb = rb;
+        s_re = re < a.nb ? re : a.nb;
+      }
+    } else {
+      const int2 it = a.items[item];
+      const int pb = a.pair_offsets[it.x] + it.y * kScanTQ;
+      const int pe0 = a.pair_offsets[it.x + 1];
+      const int pe = pe0 < pb + kScanTQ ? pe0 : pb + kScanTQ;
+      if (tid < kScanTQ) {
+        int p = pb + tid;
+        if (p < pe) {
+          int pr = a.pairs[p];
+          s_qrow[tid] = pr / a.P;
+          s_qout[tid] = pr;
+        } else {
+          s_qrow[tid] = -1;
+          s_qout[tid] = -1;
+        }
+      }
+      if (tid == 0) {
+        s_rb = a.list_offsets[it.x];
+        s_re = a.list_offsets[it.x + 1];
+      }
+    }
+    __syncthreads();
+    if (tid < kScanTQ) {
+      int qr = s_qrow[tid];
+      s_qn[tid] = (METRIC == MF_METRIC_L2 && qr >= 0) ? a.qnorms[qr] : 0.0f;
+      if (EPI == kEpiFill) s_off[tid] = (qr >= 0) ? a.offsets[s_qout[tid]] : 0;
+    }
+    __syncthreads();
+
+    const long long rb = s_rb;
+    const long long re = s_re;
+    const long long nrows = re > rb ? re - rb : 0;
+    const int ntiles = (int)((nrows + kScanTR - 1) / kScanTR);
+    const int total_it = ntiles * nchunks;
+    const bool warp_active = s_qrow[warp * 4] >= 0;
+
+    WarpTopK<KCAP> tk[4];
+    long long run[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      run[j] = (EPI == kEpiFill) ? s_off[warp * 4 + j] : 0;
+      if (EPI == kEpiTopK)
+        tk[j].init(lists + (warp * 4 + j) * KCAP, bufs + (warp * 4 + j) * 32, k, lane);
+    }
+
+    auto load_stage = [&](int it, int stage) {
+      const int t = it / nchunks;
+      const int c = it - t * nchunks;
+      const long long r0 = rb + (long long)t * kScanTR;
+      float* xdst = xs + stage * kScanTR * kScanXS;
+#pragma unroll
+      for (int s = tid; s < kScanTR * 8; s += kScanThreads) {
+        const int row = s >> 3;
+        const int part = s & 7;
+        const long long grow = r0 + row;
+        const int col = c * kScanDC + part * 4;
+        const bool v = grow < re && col < d;
+        const float* src = v ? a.xb + grow * d + col : a.xb;
+        cp_async16(xdst + row * kScanXS + part * 4, src, v);
+      }
+      {
+        const int i = tid >> 3;
+        const int part = tid & 7;
+        const int qr = s_qrow[i];
+        const int col = c * kScanDC + part * 4;
+        const bool v = qr >= 0 && col < d;
+        const float* src = v ? a.xq + (long long)qr * d + col : a.xq;
+        cp_async16(qs + stage * kScanTQ * kScanXS + i * kScanXS + part * 4, src, v);
+      }
+    };
+
+    float acc[4][4];
+#pragma unroll
+    for (int s = 0; s < kScanStages - 1; ++s) {
+      if (s < total_it) load_stage(s, s);
+      cp_async_commit();
+    }
+    for (int it = 0; it < total_it; ++it) {
+      const int stage = it % kScanStages;
+      const int t = it / nchunks;
+      const int c = it - t * nchunks;
+      cp_async_wait<kScanStages - 2>();
+      __syncthreads();
+      {
+        const int nit = it + kScanStages - 1;
+        if (nit < total_it) load_stage(nit, nit % kScanStages);
+        cp_async_commit();
+      }
+      if (c == 0) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
+      }
+      if (warp_active) {
+        const float* X = xs + stage * kScanTR * kScanXS + lane * kScanXS;
+        const float* Qp = qs + stage * kScanTQ * kScanXS + (warp * 4) * kScanXS;
+#pragma unroll
+        for (int kk = 0; kk < kScanDC; kk += 4) {
+          float4 xv[4], qv[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            xv[i] = *reinterpret_cast<const float4*>(X + i * 32 * kScanXS + kk);
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            qv[j] = *reinterpret_cast<const float4*>(Qp + j * kScanXS + kk);
+          accum_tile<METRIC>(acc, xv, qv);
+        }
+      }
+      if (c == nchunks - 1 && warp_active) {
+        // ---- epilogue: distances of this tile, fed to the per-query selection
+        const long long r0 = rb + (long long)t * kScanTR;
+        float xn[4];
+        bool rv[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          long long r = r0 + lane + 32 * i;
+          rv[i] = r < re;
+          xn[i] = (METRIC == MF_METRIC_L2 && rv[i]) ? a.xnorms[r] : 0.0f;
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int qi = warp * 4 + j;
+          if (s_qrow[qi] < 0) continue;
+          const float qnj = s_qn[qi];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const long long r = r0 + lane + 32 * i;
+            float dist;
+            if (METRIC == MF_METRIC_L2) dist = l2_from_dot(qnj, xn[i], acc[i][j]);
+            else if (METRIC == MF_METRIC_INNER_PRODUCT) dist = -acc[i][j];
+            else dist = acc[i][j];
+            if (EPI == kEpiTopK) {
+              tk[j].offer(rv[i] ? make_key(dist, (unsigned int)r) : kEmptyKey, k, lane);
+            } else {
+              const bool pass = rv[i] && dist <= a.radius;
+              const unsigned int m = __ballot_sync(0xffffffffu, pass);
+              if (EPI == kEpiFill && pass) {
+                const long long pos = run[j] + __popc(m & lanemask_lt());
+                a.out_d[pos] = dist;
+                a.out_l[pos] = a.ids ? a.ids[r] : r;
+              }
+              run[j] += __popc(m);
+            }
+          }
+        }
+      }
+    }
+    cp_async_wait<0>();
+
+    // ---- finish the item
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int qi = warp * 4 + j;
+      if (s_qrow[qi] < 0) continue;
+      const long long slot = s_qout[qi];
+      if (EPI == kEpiTopK) {
+        tk[j].flush(k, lane);
+        for (int t = lane; t < k; t += 32) {
+          const unsigned long long key = tk[j].list[t];
+          float dv;
+          long long lv;
+          if (key == kEmptyKey) {
+            dv = __int_as_float(0x7f800000);
+            lv = -1;
+          } else {
+            dv = key_dist(key);
+            const unsigned int pos = key_index(key);
+            lv = a.ids ? a.ids[pos] : (long long)pos;
+          }
+          a.out_d[slot * k + t] = dv;
+          a.out_l[slot * k + t] = lv;
+        }
+      } else if (EPI == kEpiCount) {
+        if (lane == 0) a.counts[slot] = run[j];
+      }
+    }
+    __syncthreads();
+  }
+}
+
+template <int KCAP>
+__global__ void __launch_bounds__(256) merge_kernel(const float* __restrict__ pd,
+                                                    const int64_t* __restrict__ pl, int64_t nq,
+                                                    int parts, int k_in, int k, float* D,
+                                                    int64_t* L) {
+  __shared__ unsigned long long lists[8][KCAP];
+  __shared__ unsigned long long bufs[8][32];
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const long long q = (long long)blockIdx.x * 8 + warp;
+  if (q >= nq) return;
+  WarpTopK<KCAP> tk;
+  tk.init(lists[warp], bufs[warp], k, lane);
+  const long long total = (long long)parts * k_in;
+  const long long base = q * total;
+  for (long long c0 = 0; c0 < total; c0 += 32) {
+    const long long c = c0 + lane;
+    unsigned long long key = kEmptyKey;
+    if (c < total && pl[base + c] >= 0) key = make_key(pd[base + c], (unsigned int)c);
+    tk.offer(key, k, lane);
+  }
+  tk.flush(k, lane);
+  for (int t = lane; t < k; t += 32) {
+    const unsigned long long key = tk.list[t];
+    if (key == kEmptyKey) {
+      D[q * k + t] = __int_as_float(0x7f800000);
+      L[q * k + t] = -1;
+    } else {
+      D[q * k + t] = key_dist(key);
+      L[q * k + t] = pl[base + key_index(key)];
+    }
+  }
+}
+
+__global__ void map_ids_kernel(const int64_t* __restrict__ ids, int64_t* labels, int64_t n) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const int64_t p = labels[i];
+  if (p >= 0) labels[i] = ids[p];
+}
+
+__global__ void norms_kernel(const float* __restrict__ x, int64_t n, int d, float* norms) {
+  const int lane = threadIdx.x & 31;
+  const long long row = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= n) return;
+  const float* xr = x + row * d;
+  float s = 0.0f;
+  for (int j = lane; j < d; j += 32) s = fmaf(xr[j], xr[j], s);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if (lane == 0) norms[row] = s;
+}
+
+// ----------------------------------------------------------- kernel table
+typedef void (*ScanFn)(const ScanArgs);
+
+template <int METRIC>
+ScanFn pick_topk(int kcap) {
+  switch (kcap) {
+    case 32: return scan_kernel<METRIC, 32, kEpiTopK>;
+    case 64: return scan_kernel<METRIC, 64, kEpiTopK>;
+    case 128: return scan_kernel<METRIC, 128, kEpiTopK>;
+    case 256: return scan_kernel<METRIC, 256, kEpiTopK>;
+  }
+  return nullptr;
+}
+
+template <int METRIC>
+ScanFn pick(int epi, int kcap) {
+  if (epi == kEpiTopK) return pick_topk<METRIC>(kcap);
+  if (epi == kEpiCount) return scan_kernel<METRIC, 32, kEpiCount>;
+  return scan_kernel<METRIC, 32, kEpiFill>;
+}
+
+ScanFn pick_scan(int metric, int epi, int kcap) {
+  switch (metric) {
+    case MF_METRIC_L2: return pick<MF_METRIC_L2>(epi, kcap);
+    case MF_METRIC_INNER_PRODUCT: return pick<MF_METRIC_INNER_PRODUCT>(epi, kcap);
+    case MF_METRIC_L1: return pick<MF_METRIC_L1>(epi, kcap);
+    case MF_METRIC_LINF: return pick<MF_METRIC_LINF>(epi, kcap);
+  }
+  return nullptr;
+}
+
+constexpr int kMaxDevices = 64;
+constexpr int kNumMetric = 4, kNumEpi = 3, kNumKcap = 4;
+std::mutex g_attr_mu;
+int g_occ[kMaxDevices][kNumMetric][kNumEpi][kNumKcap];  // 0 = unknown
+
+int kcap_slot(int kcap) { return kcap == 32 ? 0 : kcap == 64 ? 1 : kcap == 128 ? 2 : 3; }
+
+// Blocks per SM for an instantiation; sets its shared-memory limit on first use.
+int scan_occupancy(int device, int metric, int epi, int kcap, ScanFn fn, size_t smem) {
+  if (device < 0 || device >= kMaxDevices) return 1;
+  std::lock_guard<std::mutex> lk(g_attr_mu);
+  int& slot = g_occ[device][metric][epi][kcap_slot(kcap)];
+  if (slot == 0) {
+    if (cudaFuncSetAttribute(reinterpret_cast<const void*>(fn),
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+      return -1;
+    int blocks = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, fn, kScanThreads, smem) !=
+        cudaSuccess)
+      return -1;
+    slot = blocks > 0 ? blocks : 1;
+  }
+  return slot;
+}
+
+}  // namespace
+
+int scan_kcap(int k) {
+  if (k <= 32) return 32;
+  if (k <= 64) return 64;
+  if (k <= 128) return 128;
+  if (k <= 256) return 256;
+  return 0;
+}
+
+int launch_scan(const ScanArgs& a, int metric, int epi, int64_t total_items, int device,
+                cudaStream_t stream) {
+  const int kcap = epi == kEpiTopK ? scan_kcap(a.k) : 32;
+  MF_CHECK(kcap != 0, MF_ERR_INVALID_ARGS, "k=%d exceeds the supported maximum %d", a.k, kMaxK);
+  ScanFn fn = pick_scan(metric, epi, kcap);
+  MF_CHECK(fn != nullptr, MF_ERR_METRIC, "unsupported metric %d", metric);
+  const size_t smem = ScanSmemLayout::bytes(epi, kcap);
+  const int occ = scan_occupancy(device, metric, epi, kcap, fn, smem);
+  MF_CHECK(occ > 0, MF_ERR_CUDA, "could not configure the scan kernel (smem %zu)", smem);
+  if (total_items <= 0) return MF_OK;
+  long long grid = (long long)num_sms(device) * occ;
+  if (grid > total_items) grid = total_items;
+  MF_CUDA(cudaMemsetAsync(a.counter, 0, sizeof(int), stream));
+  ScopedTiming tm(epi == kEpiTopK ? (a.flat ? "scan_topk_flat" : "scan_topk_ivf") : "scan_range",
+                  stream);
+  fn<<<(unsigned int)grid, kScanThreads, smem, stream>>>(a);
+  MF_LAUNCH_CHECK();
+  return MF_OK;
+}
+
+int launch_norms(const float* x, int64_t n, int d, float* norms, cudaStream_t stream) {
+  if (n <= 0) return MF_OK;
+  const int warps = 8;
+  const long long grid = ceil_div(n, warps);
+  norms_kernel<<<(unsigned int)grid, warps * 32, 0, stream>>>(x, n, d, norms);
+  MF_LAUNCH_CHECK();
+  return MF_OK;
+}
+
+int launch_map_ids(const int64_t* ids, int64_t* labels, int64_t n, cudaStream_t stream) {
+  if (n <= 0) return MF_OK;
+  map_ids_kernel<<<(unsigned int)ceil_div(n, 256), 256, 0, stream>>>(ids, labels, n);
+  MF_LAUNCH_CHECK();
+  return MF_OK;
+}
+
+int launch_merge(const float* pd, const int64_t* pl, int64_t nq, int parts, int k_in, int k,
+                 float* d, int64_t* l, cudaStream_t stream) {
+  if (nq <= 0 || k <= 0) return MF_OK;
+  const int kcap = scan_kcap(k);
+  MF_CHECK(kcap != 0, MF_ERR_INVALID_ARGS, "k=%d exceeds the supported maximum %d", k, kMaxK);
+  MF_CHECK((long long)parts * k_in < (1ll << 31), MF_ERR_INVALID_ARGS,
+           "parts*k_in too large for one merge");
+  const long long grid = ceil_div(nq, 8);
+  ScopedTiming tm("merge", stream);
+  switch (kcap) {
+    case 32: merge_kernel<32><<<(unsigned int)grid, 256, 0, stream>>>(pd, pl, nq, parts, k_in, k, d, l); break;
+    case 64: merge_kernel<64><<<(unsigned int)grid, 256, 0, stream>>>(pd, pl, nq, parts, k_in, k, d, l); break;
+    case 128: merge_kernel<128><<<(unsigned int)grid, 256, 0, stream>>>(pd, pl, nq, parts, k_in, k, d, l); break;
+    default: merge_kernel<256><<<(unsigned int)grid, 256, 0, stream>>>(pd, pl, nq, parts, k_in, k, d, l); break;
+  }
+  MF_LAUNCH_CHECK();
+  return MF_OK;
+}
+
+// ------------------------------------------------------------- flat search
+FlatPlan plan_flat(int64_t nq, int64_t nb, int d, int k, int device) {
+  (void)d;
+  FlatPlan p;
+  p.nqt = (int)ceil_div(nq, kScanTQ);
+  const int kcap = scan_kcap(k) ? scan_kcap(k) : 256;
+  // Aim for about two waves of resident CTAs; each split keeps >= 1 tile.
+  const int per_sm = kcap >= 256 ? 1 : (kcap >= 128 ? 2 : 3);
+  const long long target = 2ll * (device >= 0 ? num_sms(device) : 148) * per_sm;
+  long long s = ceil_div(target, p.nqt > 0 ? p.nqt : 1);
+  const long long max_s = nb > 0 ? ceil_div(nb, kScanTR) : 1;
+  if (s > max_s) s = max_s;
+  if (s < 1) s = 1;
+  long long rps = ceil_div(nb > 0 ? nb : 1, s);
+  rps = ceil_div(rps, kScanTR) * kScanTR;
+  s = ceil_div(nb > 0 ? nb : 1, rps);
+  p.splits = (int)s;
+  p.rows_per_split = rps;
+  Carver c(nullptr, 0);
+  c.take<float>(nq);     // query norms
+  c.take<int>(1);        // work counter
+  if (p.splits > 1) {
+    c.take<float>((size_t)nq * p.splits * k);
+    c.take<int64_t>((size_t)nq * p.splits * k);
+  }
+  p.bytes = c.used;
+  return p;
+}
+
+int run_flat_topk(int device, cudaStream_t stream, const float* xq, int64_t nq, const float* xb,
+                  const float* xb_norms, int64_t nb, int d, int metric, int k,
+                  const int64_t* ids, float* D, int64_t* I, void* ws, size_t ws_bytes) {
+  const FlatPlan p = plan_flat(nq, nb, d, k, device);
+  MF_CHECK(ws_bytes >= p.bytes, MF_ERR_INVALID_ARGS,
+           "flat search workspace too small: %zu < %zu bytes", ws_bytes, p.bytes);
+  Carver c(ws, ws_bytes);
+  float* qn = c.take<float>(nq);
+  int* counter = c.take<int>(1);
+  float* pd = nullptr;
+  int64_t* pl = nullptr;
+  if (p.splits > 1) {
+    pd = c.take<float>((size_t)nq * p.splits * k);
+    pl = c.take<int64_t>((size_t)nq * p.splits * k);
+  }
+  if (metric == MF_METRIC_L2) MF_TRY(launch_norms(xq, nq, d, qn, stream));
+  ScanArgs a{};
+  a.xq = xq;
+  a.qnorms = qn;
+  a.xb = xb;
+  a.xnorms = xb_norms;
+  a.ids = p.splits > 1 ? nullptr : ids;
+  a.d = d;
+  a.k = k;
+  a.nq = nq;
+  a.P = p.splits;
+  a.flat = 1;
+  a.nqt = p.nqt;
+  a.nb = nb;
+  a.rows_per_split = p.rows_per_split;
+  a.counter = counter;
+  a.direct = p.splits > 1 ? 0 : 1;
+  a.out_d = p.splits > 1 ? pd : D;
+  a.out_l = p.splits > 1 ? pl : I;
+  MF_TRY(launch_scan(a, metric, kEpiTopK, (int64_t)p.nqt * p.splits, device, stream));
+  if (p.splits > 1) {
+    MF_TRY(launch_merge(pd, pl, nq, p.splits, k, k, D, I, stream));
+    // Row positions are the merge's tie-break, so ids are mapped last.
+    if (ids) MF_TRY(launch_map_ids(ids, I, nq * (int64_t)k, stream));
+  }
+  return MF_OK;
+}
+
+}  // namespace mf

@@ -1,0 +1,108 @@
+// Slab scan: the one SIMT kernel family behind flat kNN, the IVF list scan,
+// the coarse quantizer, k-means assignment and both range-search passes.
+//
+// A work item is (a set of <= 32 queries, a contiguous slab of database rows).
+// Flat search: items are (query tile, row split) over the whole database.
+// IVF search: items are (inverted list, group of <= 32 queries probing it),
+// i.e. the scan is list-major: each list slab is streamed from HBM once per
+// group of queries that probe it instead of once per query.
+#pragma once
+
+#include "mf_common.cuh"
+
+namespace mf {
+
+constexpr int kScanThreads = 256;  // 8 warps
+constexpr int kScanTQ = 32;        // queries per item (4 per warp)
+constexpr int kScanTR = 128;       // rows per tile (4 per lane)
+constexpr int kScanDC = 32;        // d-chunk staged per pipeline stage
+constexpr int kScanXS = kScanDC + 4;  // padded smem row stride (floats): conflict-free LDS.128
+constexpr int kScanStages = 2;
+
+enum ScanEpilogue { kEpiTopK = 0, kEpiCount = 1, kEpiFill = 2 };
+
+struct ScanArgs {
+  const float* xq;        // (nq, d)
+  const float* qnorms;    // (nq), L2 only
+  const float* xb;        // (rows, d)
+  const float* xnorms;    // (rows), L2 only
+  const int64_t* ids;     // (rows) or null: labels are row positions
+  int d;
+  int k;
+  int64_t nq;
+  int P;                  // parts per query: row splits (flat) or nprobe (IVF)
+  // flat items
+  int flat;               // 1: items are (query tile, split); 0: IVF items
+  int nqt;
+  int64_t nb;
+  int64_t rows_per_split;
+  // IVF items
+  const int2* items;      // (list, group)
+  const int* item_total;  // device scalar
+  const int64_t* list_offsets;  // (nlist+1) rows of xb
+  const int* pair_offsets;      // (nlist+1) into pairs
+  const int* pairs;             // q*P + slot, grouped by list
+  // persistent work counter (zeroed before launch)
+  int* counter;
+  // top-k outputs: slot s = q*P + part (or q when direct) → [s*k, s*k+k)
+  float* out_d;
+  int64_t* out_l;
+  int direct;
+  // range search
+  float radius;
+  int64_t* counts;        // count pass: (nq*P)
+  const int64_t* offsets; // fill pass: exclusive scan of counts (nq*P)
+};
+
+// Launches the kernel for (metric, kcap, epilogue) on a persistent grid that
+// covers `total_items` work items (an upper bound for IVF).
+int launch_scan(const ScanArgs& a, int metric, int epilogue, int64_t total_items, int device,
+                cudaStream_t stream);
+
+// Smallest supported list capacity >= k, or 0 when k is too large.
+int scan_kcap(int k);
+constexpr int kMaxK = 256;
+
+// Per-row squared norms.
+int launch_norms(const float* x, int64_t n, int d, float* norms, cudaStream_t stream);
+
+// labels[i] = ids[labels[i]] for labels[i] >= 0.
+int launch_map_ids(const int64_t* ids, int64_t* labels, int64_t n, cudaStream_t stream);
+
+// Partial top-k merge (nq, parts, k_in) -> (nq, k).
+int launch_merge(const float* pd, const int64_t* pl, int64_t nq, int parts, int k_in, int k,
+                 float* d, int64_t* l, cudaStream_t stream);
+
+// Flat search plan: splits and workspace.
+struct FlatPlan {
+  int nqt;
+  int splits;
+  int64_t rows_per_split;
+  size_t bytes;
+};
+FlatPlan plan_flat(int64_t nq, int64_t nb, int d, int k, int device);
+
+// Runs flat top-k into (nq, k) outputs using the given workspace.
+int run_flat_topk(int device, cudaStream_t stream, const float* xq, int64_t nq, const float* xb,
+                  const float* xb_norms, int64_t nb, int d, int metric, int k,
+                  const int64_t* ids, float* D, int64_t* I, void* ws, size_t ws_bytes);
+
+// IVF list grouping: probes (nq, P) -> pairs grouped by list and items.
+struct IvfGroups {
+  int* counts;        // nlist
+  int* cursors;       // nlist
+  int* pair_offsets;  // nlist+1
+  int* pairs;         // nq*P
+  int2* items;        // nq*P (upper bound)
+  int* item_total;    // 1
+  int* counter;       // 1
+};
+size_t ivf_groups_bytes(int64_t nq, int nlist, int P);
+IvfGroups carve_ivf_groups(Carver& c, int64_t nq, int nlist, int P);
+int run_ivf_groups(const IvfGroups& g, const int64_t* probes, int64_t nq, int P, int nlist,
+                   const int64_t* list_offsets, const int32_t* list_order, cudaStream_t stream);
+
+// Exclusive scan of n int64 counts into out (n+1 entries; out[n] = total).
+int launch_exclusive_scan_i64(const int64_t* in, int64_t n, int64_t* out, cudaStream_t stream);
+
+}  // namespace mf

@@ -1,0 +1,123 @@
+// Warp-cooperative top-k selection over 64-bit keys (see mf_common.cuh).
+//
+// One warp owns one query's state: a sorted list of the k best keys in shared
+// memory and a 32-entry candidate buffer. A batch of 32 candidates (one per
+// lane) is filtered against the k-th best key; survivors are appended to the
+// buffer. A full buffer is sorted across the lanes (bitonic network on
+// shuffles) and merged into the list in place: every element's new position is
+// its old position plus its rank in the other sequence, so all positions are
+// computed before any write. The design follows the register/shared-memory
+// k-selection of Johnson, Douze and Jegou, "Billion-scale similarity search with
+// GPUs" (2017), which the reference's top-k kernel stubs cite
+// (python/metalfaiss/faissmlx/kernels/topk_kernels.py:4,16-31).
+#pragma once
+
+#include "mf_common.cuh"
+
+namespace mf {
+
+// Ascending bitonic sort of 32 keys, one per lane.
+__device__ __forceinline__ unsigned long long warp_sort32(unsigned long long c, int lane) {
+#pragma unroll
+  for (int size = 2; size <= 32; size <<= 1) {
+#pragma unroll
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      unsigned long long o = __shfl_xor_sync(0xffffffffu, c, stride);
+      bool up = (lane & size) == 0;
+      bool low = (lane & stride) == 0;
+      c = (low == up) ? (c < o ? c : o) : (c < o ? o : c);
+    }
+  }
+  return c;
+}
+
+// Number of lanes whose (sorted, ascending) key is < e.
+// Binary search over the 32 lane-distributed keys; every lane runs the same
+// shuffles but searches for its own e. The five halving steps resolve 0..31;
+// the last lane's key decides 32.
+__device__ __forceinline__ int warp_rank_below(unsigned long long sorted, unsigned long long e) {
+  unsigned long long last = __shfl_sync(0xffffffffu, sorted, 31);
+  int base = 0;
+#pragma unroll
+  for (int step = 16; step > 0; step >>= 1) {
+    unsigned long long probe = __shfl_sync(0xffffffffu, sorted, base + step - 1);
+    if (probe < e) base += step;
+  }
+  if (base == 31 && last < e) base = 32;
+  return base;
+}
+
+// Per-query state held by the owning warp. The list lives in shared memory
+// (`list`, capacity >= k); nbuf and thr are warp-uniform registers.
+template <int KCAP>
+struct WarpTopK {
+  unsigned long long* list;  // KCAP keys, ascending; first k meaningful
+  unsigned long long* buf;   // 32 keys
+  int nbuf;
+  unsigned long long thr;    // list[k-1]
+
+  __device__ __forceinline__ void init(unsigned long long* l, unsigned long long* b, int k,
+                                       int lane) {
+    list = l;
+    buf = b;
+    for (int i = lane; i < k; i += 32) list[i] = kEmptyKey;
+    nbuf = 0;
+    thr = kEmptyKey;
+    __syncwarp();
+  }
+
+  __device__ __forceinline__ void flush(int k, int lane) {
+    if (nbuf == 0) return;
+    __syncwarp();
+    unsigned long long c = (lane < nbuf) ? buf[lane] : kEmptyKey;
+    c = warp_sort32(c, lane);
+    constexpr int PER = (KCAP + 31) / 32;
+    unsigned long long e[PER];
+    int np[PER];
+#pragma unroll
+    for (int p = 0; p < PER; ++p) {
+      int i = lane + 32 * p;
+      e[p] = (i < k) ? list[i] : kEmptyKey;
+      int r = warp_rank_below(c, e[p]);
+      np[p] = i + r;
+    }
+    int cpos = 1 << 30;
+    if (lane < nbuf) {
+      int lo = 0, hi = k;
+      while (lo < hi) {
+        int mid = (lo + hi) >> 1;
+        if (list[mid] < c) lo = mid + 1; else hi = mid;
+      }
+      cpos = lane + lo;
+    }
+    __syncwarp();
+#pragma unroll
+    for (int p = 0; p < PER; ++p) {
+      int i = lane + 32 * p;
+      if (i < k && np[p] < k) list[np[p]] = e[p];
+    }
+    if (cpos < k) list[cpos] = c;
+    __syncwarp();
+    nbuf = 0;
+    thr = list[k - 1];
+  }
+
+  // Offers one candidate per lane (kEmptyKey = no candidate).
+  __device__ __forceinline__ void offer(unsigned long long key, int k, int lane) {
+    bool pass = key < thr;
+    unsigned int m = __ballot_sync(0xffffffffu, pass);
+    if (m == 0u) return;
+    int n = __popc(m);
+    if (nbuf + n > 32) {
+      flush(k, lane);
+      pass = key < thr;
+      m = __ballot_sync(0xffffffffu, pass);
+      if (m == 0u) return;
+      n = __popc(m);
+    }
+    if (pass) buf[nbuf + __popc(m & lanemask_lt())] = key;
+    nbuf += n;
+  }
+};
+
+}  // namespace mf

@@ -1,0 +1,157 @@
+"""Database sharding over the GPUs of one node (one process per GPU).
+
+The reference has no multi-device code (python/metalfaiss/faissmlx/resources.py:24-26);
+its tests describe the intent: a sharded flat index equal to the single one
+(python/metalfaiss/unittest/test_mlx_multi_gpu.py:49-65) and an IVF index
+sharded with a shared quantizer (:86-119), and its facade stubs IndexShards
+(python/metalfaiss/faiss_compat.py:326-366).
+
+* IVFFlat: inverted lists are partitioned over the ranks by greedy LPT on list
+  size; the coarse quantizer is replicated. Each rank scans only the lists it
+  owns and yields a local (nq, k) top-k.
+* Flat: contiguous row shards; labels are global ids.
+The one exchange step is an all-gather of the (nq, k) partial results over
+NCCL (torch.distributed), followed by the on-device merge kernel.
+"""
+from __future__ import annotations
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+from . import _native as nat
+from .search_result import SearchResult
+
+
+def lpt_partition(sizes, world: int) -> np.ndarray:
+    """Owner rank of each list: lists in decreasing size, each to the currently
+    least-loaded rank (ties to the lower rank)."""
+    sizes = np.asarray(sizes, np.int64)
+    owners = np.zeros(len(sizes), np.int32)
+    if world <= 1:
+        return owners
+    load = np.zeros(world, np.int64)
+    for l in np.argsort(-sizes, kind="stable"):
+        r = int(np.argmin(load))
+        owners[l] = r
+        load[r] += sizes[l]
+    return owners
+
+
+def row_shard(n: int, rank: int, world: int):
+    """Contiguous [begin, end) rows of `rank` (sizes differ by at most one)."""
+    base, rem = divmod(n, world)
+    begin = rank * base + min(rank, rem)
+    return begin, begin + base + (1 if rank < rem else 0)
+
+
+def gather_partials(D: torch.Tensor, I: torch.Tensor, group=None):
+    """All-gather of each rank's (nq, k) results → (nq, world, k) on every rank."""
+    world = dist.get_world_size(group)
+    nq, k = D.shape
+    if dist.get_backend(group) == "nccl":
+        gd = torch.empty((world * nq, k), dtype=D.dtype, device=D.device)
+        gi = torch.empty((world * nq, k), dtype=I.dtype, device=I.device)
+        dist.all_gather_into_tensor(gd, D.contiguous(), group=group)
+        dist.all_gather_into_tensor(gi, I.contiguous(), group=group)
+        gd = gd.view(world, nq, k)
+        gi = gi.view(world, nq, k)
+    else:
+        ld = [torch.empty_like(D) for _ in range(world)]
+        li = [torch.empty_like(I) for _ in range(world)]
+        dist.all_gather(ld, D.contiguous(), group=group)
+        dist.all_gather(li, I.contiguous(), group=group)
+        gd = torch.stack(ld)
+        gi = torch.stack(li)
+    return gd.permute(1, 0, 2).contiguous(), gi.permute(1, 0, 2).contiguous()
+
+
+def merge_partials(pd: torch.Tensor, pi: torch.Tensor, k: int) -> SearchResult:
+    """(nq, parts, k_in) → (nq, k) with the on-device merge kernel."""
+    nq, parts, k_in = pd.shape
+    D = torch.empty((nq, k), dtype=torch.float32, device=pd.device)
+    I = torch.empty((nq, k), dtype=torch.int64, device=pd.device)
+    if nq:
+        nat.call("mf_topk_merge", pd.device.index, nat.stream_of(pd.device), nat.ptr(pd),
+                 nat.ptr(pi), nq, parts, k_in, k, nat.ptr(D), nat.ptr(I))
+    return SearchResult(D, I)
+
+
+def keep_lists(index, keep_mask: np.ndarray):
+    """A copy of an IVFFlatIndex holding only the lists where keep_mask is True
+    (the other lists stay empty); shares the quantizer."""
+    from .index_ivf_flat import IVFFlatIndex
+
+    out = IVFFlatIndex(index.d, index.nlist, quantizer=index.quantizer,
+                       metric_type=index.metric_type, device=index.device)
+    out._is_trained = index.is_trained
+    out.nprobe = index.nprobe
+    sizes = index.list_sizes()
+    keep = np.asarray(keep_mask, bool)
+    new_sizes = np.where(keep, sizes, 0)
+    offsets = np.zeros(index.nlist + 1, np.int64)
+    np.cumsum(new_sizes, out=offsets[1:])
+    dev = index.device
+    if index.ntotal:
+        list_of_row = torch.repeat_interleave(torch.arange(index.nlist, device=dev),
+                                              torch.from_numpy(sizes).to(dev))
+        row_mask = torch.from_numpy(keep).to(dev)[list_of_row]
+        out._vecs = index._vecs[: index.ntotal][row_mask].contiguous()
+        out._norms = index._norms[: index.ntotal][row_mask].contiguous()
+        out._ids = index._ids[: index.ntotal][row_mask].contiguous()
+        out._ntotal = int(out._ids.shape[0])
+    out._offsets = torch.from_numpy(offsets).to(dev)
+    order = np.argsort(-new_sizes, kind="stable").astype(np.int32)
+    out._order = torch.from_numpy(order).to(dev)
+    return out
+
+
+class ShardedIVF:
+    """This rank's share of an IVFFlat index; search() returns the merged global top-k."""
+
+    def __init__(self, index, rank: int, world: int, group=None):
+        self.rank, self.world, self.group = rank, world, group
+        owners = lpt_partition(index.list_sizes(), world)
+        self.owners = owners
+        self.local = keep_lists(index, owners == rank)
+
+    @property
+    def nprobe(self):
+        return self.local.nprobe
+
+    @nprobe.setter
+    def nprobe(self, v):
+        self.local.nprobe = v
+
+    def search(self, xq, k: int) -> SearchResult:
+        local = self.local.search(xq, k)
+        pd, pi = gather_partials(local.distances, local.labels, self.group)
+        return merge_partials(pd, pi, k)
+
+
+class ShardedFlat:
+    """Contiguous row shard of a flat database (global ids); search() merges."""
+
+    def __init__(self, index, rank: int, world: int, group=None):
+        from .index_flat import FlatIndex
+
+        self.rank, self.world, self.group = rank, world, group
+        b, e = row_shard(index.ntotal, rank, world)
+        self.local = FlatIndex(index.d, index.metric_type, index.device)
+        if e > b:
+            self.local.add(index.xb[b:e], index.ids[b:e])
+
+    def search(self, xq, k: int) -> SearchResult:
+        kk = k if self.local.ntotal >= k else self.local.ntotal
+        nq = len(xq)
+        if kk > 0:
+            local = self.local.search(xq, kk)
+            D, I = local.distances, local.labels
+        else:
+            D = torch.empty((nq, 0), device=self.local.device)
+            I = torch.empty((nq, 0), dtype=torch.int64, device=self.local.device)
+        if kk < k:  # pad so every rank contributes (nq, k)
+            D = torch.cat([D, torch.full((nq, k - kk), float("inf"), device=D.device)], 1)
+            I = torch.cat([I, torch.full((nq, k - kk), -1, dtype=torch.int64, device=I.device)], 1)
+        pd, pi = gather_partials(D, I, self.group)
+        return merge_partials(pd, pi, k)
