@@ -180,8 +180,11 @@ def run_ours(args, cfg):
     sizes = idx.list_sizes()
     logical_bytes = int(sizes[probes.cpu().numpy()].sum()) * d * 4
 
+    nvtx = torch.cuda.nvtx
+    nvtx.range_push("warmup")
     for _ in range(args.warmup):
         search(xq)
+    nvtx.range_pop()
     torch.cuda.synchronize(device)
     if world > 1:
         dist.barrier()
@@ -195,10 +198,12 @@ def run_ours(args, cfg):
     torch.cuda.synchronize(device)
     if world > 1:
         dist.barrier()
+    nvtx.range_push("timed")
     ev0.record(stream)
     for _ in range(args.steps):
         res = search(xq)
     ev1.record(stream)
+    nvtx.range_pop()
     torch.cuda.synchronize(device)
     launches = nat.launch_count() - launches0
     nat.timing_enable(False)
