@@ -23,6 +23,7 @@ Run:  python tests/golden/make_golden.py   (needs the reference tree)
 from __future__ import annotations
 
 import importlib
+import importlib.util
 import os
 import sys
 import types
@@ -56,12 +57,19 @@ def load_reference():
                  "metalfaiss.utils.search_result", "metalfaiss.utils.sorting",
                  "metalfaiss.distances", "metalfaiss.indexflat",
                  "metalfaiss.index.base_index", "metalfaiss.index.flat_index",
-                 "metalfaiss.faissmlx.kernels.ivf_kernels", "metalfaiss.index.ivf_flat_index",
-                 "metalfaiss.index"]:
+                 "metalfaiss.faissmlx.kernels.ivf_kernels", "metalfaiss.index.ivf_flat_index"]:
         try:
             mods[name] = importlib.import_module(name)
         except Exception as e:  # pragma: no cover - reported, the case is skipped
             print(f"[golden] cannot import {name}: {type(e).__name__}: {e}")
+    # python/metalfaiss/index.py is shadowed by the python/metalfaiss/index/ package;
+    # load the file itself (it holds the only range_search, :90-130).
+    spec = importlib.util.spec_from_file_location("metalfaiss._index_py", REF / "index.py")
+    mod = importlib.util.module_from_spec(spec)
+    mod.__package__ = "metalfaiss"
+    sys.modules["metalfaiss._index_py"] = mod
+    spec.loader.exec_module(mod)
+    mods["metalfaiss._index_py"] = mod
     return mods
 
 
@@ -90,7 +98,7 @@ def gen_flat(m, out):
     MT = m["metalfaiss.metric_type"].MetricType
     cases = []
     for mi, metric in enumerate([MT.L2, MT.INNER_PRODUCT, MT.L1, MT.LINF]):
-        for (n, d, nq, k, seed) in [(500, 16, 8, 10, 3), (2000, 64, 12, 32, 4), (60, 8, 5, 100, 5)]:
+        for (n, d, nq, k, seed) in [(500, 16, 8, 10, 3), (1024, 32, 12, 32, 4), (60, 8, 5, 100, 5)]:
             xb = rng(seed + 10 * mi).standard_normal((n, d), dtype=np.float32)
             xq = rng(seed + 10 * mi + 1).standard_normal((nq, d), dtype=np.float32)
             idx = flat.FlatIndex(d, metric)
@@ -124,7 +132,7 @@ def gen_ivf(m, out):
     fi = m["metalfaiss.index.flat_index"]
     TMT = m["metalfaiss.types.metric_type"].MetricType
     cases = []
-    for (n, d, nlist, nq, nprobe, k, seed) in [(4096, 32, 32, 10, 4, 10, 6), (3000, 64, 24, 8, 1, 32, 7),
+    for (n, d, nlist, nq, nprobe, k, seed) in [(2500, 32, 32, 10, 4, 10, 6), (2000, 48, 24, 8, 1, 32, 7),
                                                (2500, 16, 40, 12, 8, 5, 8)]:
         x, centres = mixture(n, d, nlist, seed)
         cents = x[rng(seed + 1).permutation(n)[:nlist]].copy()
@@ -167,7 +175,7 @@ def gen_ivf(m, out):
 
 
 def gen_range(m, out):
-    Index = m["metalfaiss.index"].Index
+    Index = m["metalfaiss._index_py"].Index
     flat = m["metalfaiss.indexflat"]
     MT = m["metalfaiss.metric_type"].MetricType
 
@@ -194,7 +202,11 @@ def gen_range(m, out):
         xq = rng(seed + 1).standard_normal((nq, d), dtype=np.float32)
         r = FlatRange(d)
         r.add(xb)
-        radius = float(np.median(np.sort(((xq[:, None] - xb[None]) ** 2).sum(-1), 1)[:, 9]))
+        dsort = np.sort(((xq[:, None] - xb[None]) ** 2).sum(-1), 1)
+        # The reference's SearchRangeResult rejects a query with no hit (its lims
+        # length check, python/metalfaiss/utils/search_result.py:61-62, counts only
+        # non-empty per-query arrays), so every query gets at least one.
+        radius = float(max(np.median(dsort[:, 9]), dsort[:, 0].max() * 1.01))
         if tag == "capped":
             radius *= 6.0  # more than 100 hits per query: the reference's cap shows
         res = r.range_search(xq, radius)

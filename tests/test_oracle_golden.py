@@ -1,0 +1,93 @@
+"""Pins the CPU oracle to the reference's own outputs (tests/golden/)."""
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from oracle import compare, cport, oracle
+
+G = np.load(Path(__file__).parent / "golden" / "reference_golden.npz")
+METRIC = {"L2": oracle.L2, "INNER_PRODUCT": oracle.INNER_PRODUCT, "L1": oracle.L1, "LINF": oracle.LINF}
+
+
+@pytest.mark.parametrize("tag", ["a", "b"])
+def test_pairwise(tag):
+    xq, xb = G[f"pairwise_{tag}_xq"], G[f"pairwise_{tag}_xb"]
+    np.testing.assert_allclose(oracle.pairwise_f32(xq, xb, oracle.L2), G[f"pairwise_{tag}_l2"], rtol=1e-6, atol=1e-5)
+    np.testing.assert_allclose(oracle.pairwise_f32(xq, xb, oracle.L1), G[f"pairwise_{tag}_l1"], rtol=1e-6)
+    np.testing.assert_allclose(oracle.pairwise_f32(xq, xb, oracle.LINF), G[f"pairwise_{tag}_linf"], rtol=1e-6)
+    # the property the reference's own test checks (test_distances.py:19-35)
+    exact = oracle.pairwise_exact(xq, xb, oracle.L2)
+    np.testing.assert_allclose(G[f"pairwise_{tag}_l2"], exact, rtol=1e-5, atol=1e-4)
+
+
+@pytest.mark.parametrize("tag", list(G["flat_cases"]))
+def test_flat_search(tag):
+    xb, xq, ids = G[tag + "_xb"], G[tag + "_xq"], G[tag + "_ids"]
+    metric, k = (int(v) for v in G[tag + "_meta"])
+    D, I = oracle.flat_search(xq, xb, k, metric, ids)
+    assert D.shape == G[tag + "_D"].shape  # k clipped to ntotal like the reference
+    atol = compare.l2_atol(xq, xb) if metric == oracle.L2 else 1e-5
+    errs = compare.check_knn(D, I, G[tag + "_D"], G[tag + "_I"], compare.exact_lookup(xq, xb, metric, ids),
+                             atol=atol)
+    assert not errs, errs[:3]
+
+
+@pytest.mark.parametrize("tag", list(G["ivf_cases"]))
+def test_ivf_search(tag):
+    x, cents, labels, xq = G[tag + "_x"], G[tag + "_cents"], G[tag + "_labels"], G[tag + "_xq"]
+    nlist, nprobe, k = (int(v) for v in G[tag + "_meta"])
+    # the list build: the oracle's assignment equals the reference quantizer's
+    lab = oracle.flat_search(x, cents, 1)[1][:, 0]
+    assert np.array_equal(lab, labels)
+    offsets, vecs, ids = oracle.ivf_build(x, labels, nlist)
+    kk = G[tag + "_D"].shape[1]  # the reference kernel returns min(k, 32) columns
+    D, I = oracle.ivf_search(xq, cents, offsets, vecs, ids, nprobe, k)
+    errs = compare.check_knn(D[:, :kk], I[:, :kk], G[tag + "_D"], G[tag + "_I"],
+                             compare.exact_lookup(xq, x, oracle.L2), atol=compare.l2_atol(xq, x))
+    assert not errs, errs[:3]
+    # the C port follows the same algorithm
+    Dc, Ic = cport.ivf_search(xq, cents, offsets, vecs, ids, nprobe, k, threads=2)
+    errs = compare.check_knn(Dc[:, :kk], Ic[:, :kk], G[tag + "_D"], G[tag + "_I"],
+                             compare.exact_lookup(xq, x, oracle.L2), atol=compare.l2_atol(xq, x))
+    assert not errs, errs[:3]
+
+
+@pytest.mark.parametrize("k", [1, 10, 32])
+def test_list_scan_kernel(k):
+    X, ids, Q = G["kernel_X"], G["kernel_ids"].astype(np.int64), G["kernel_Q"]
+    offsets = np.array([0, len(X)], np.int64)
+    D, I = oracle.ivf_search(Q[None], np.zeros((1, len(Q)), np.float32), offsets, X, ids, 1, k)
+    for pre in ("kernel", "kernel_chunked"):
+        errs = compare.check_knn(D, I, G[f"{pre}_k{k}_D"][None], G[f"{pre}_k{k}_I"][None],
+                                 compare.exact_lookup(Q[None], X, oracle.L2, ids), atol=1e-5)
+        assert not errs, (pre, errs[:3])
+
+
+def test_range_search_matches_reference_below_cap():
+    xb, xq, r = G["range_small_xb"], G["range_small_xq"], float(G["range_small_radius"])
+    lims, D, I = oracle.range_search_capped(xq, xb, r)
+    assert np.array_equal(lims, G["range_small_lims"])
+    assert np.array_equal(I, G["range_small_I"])
+    np.testing.assert_allclose(D, G["range_small_D"], rtol=1e-6, atol=1e-5)
+    # below the cap the exact search returns the same sets
+    le, De, Ie = oracle.range_search(xq, xb, r)
+    assert np.array_equal(le, lims)
+    for q in range(len(xq)):
+        assert set(Ie[le[q]:le[q + 1]].tolist()) == set(I[lims[q]:lims[q + 1]].tolist())
+
+
+def test_range_search_reference_cap():
+    """The reference truncates at 100 results per query (python/metalfaiss/index.py:104)."""
+    xb, xq, r = G["range_capped_xb"], G["range_capped_xq"], float(G["range_capped_radius"])
+    lims, D, I = oracle.range_search_capped(xq, xb, r)
+    assert np.array_equal(lims, G["range_capped_lims"]) and np.array_equal(I, G["range_capped_I"])
+    le, _, _ = oracle.range_search(xq, xb, r)
+    assert np.all(np.diff(le) > 100)  # the exact search finds what the cap drops
+
+
+def test_kmeans():
+    x, perm, iters = G["kmeans_x"], G["kmeans_perm"], int(G["kmeans_iters"])
+    k = len(perm)
+    c = oracle.kmeans_train(x, k, iters, seed=0, init=x[perm])
+    np.testing.assert_allclose(c, G["kmeans_centroids"], rtol=1e-4, atol=1e-4)
