@@ -104,7 +104,8 @@ MF_API int mf_flat_search(int device, void* stream, const float* xq, int64_t nq,
 /* ---------------------------------------------------------------- IVFFlat */
 
 /* Inverted lists are CSR: list l holds rows [list_offsets[l], list_offsets[l+1])
- * of list_vecs (N,d), with list_norms (N) and list_ids (N).
+ * of list_vecs (ntotal,d), with list_norms (ntotal) and list_ids (ntotal);
+ * ntotal = list_offsets[nlist] is passed by value (the host knows it).
  * list_order (nlist, optional) is a permutation of the list ids giving the order
  * in which the scan takes work (largest lists first balances the SMs). */
 
@@ -119,7 +120,7 @@ MF_API int mf_ivf_search_workspace_size(int64_t nq, int nlist, int nprobe, int d
 MF_API int mf_ivf_search(int device, void* stream, const float* xq, int64_t nq,
                   const float* centroids, const float* centroid_norms, int nlist,
                   int nprobe, const int64_t* list_offsets, const float* list_vecs,
-                  const float* list_norms, const int64_t* list_ids,
+                  const float* list_norms, const int64_t* list_ids, int64_t ntotal,
                   const int32_t* list_order, int d, int metric, int k,
                   float* distances, int64_t* labels, void* workspace,
                   size_t workspace_bytes);
@@ -136,7 +137,7 @@ MF_API int mf_ivf_search_preassigned(int device, void* stream, const float* xq, 
                               const int64_t* probes, int nprobe, int nlist,
                               const int64_t* list_offsets, const float* list_vecs,
                               const float* list_norms, const int64_t* list_ids,
-                              const int32_t* list_order, int d, int metric, int k,
+                              int64_t ntotal, const int32_t* list_order, int d, int metric, int k,
                               float* distances, int64_t* labels, void* workspace,
                               size_t workspace_bytes);
 
@@ -242,6 +243,17 @@ MF_API int mf_timing_read(const char* kernel, double* total_ms, int64_t* launche
 
 /* Number of kernels this library has launched in this process (all devices). */
 MF_API int64_t mf_launch_count(void);
+
+/* Scan engine for the L2 / inner-product top-k scans: 0 = automatic (tensor
+ * cores where the shape allows), 1 = SIMT only, 2 = tensor cores where the
+ * shape allows. Mirrors the reference's kernel switches
+ * (python/metalfaiss/faissmlx/flags.py:20-35). Process-wide. */
+MF_API int mf_set_scan_engine(int engine);
+
+/* Reads and clears the device-side error word of `device` (MF_ERR_TIMEOUT if a
+ * bounded wait in a kernel gave up since the last read, else MF_OK).
+ * Synchronizes the device. */
+MF_API int mf_device_error(int device, int* code);
 
 #ifdef __cplusplus
 }

@@ -34,9 +34,9 @@ _SIGNATURES = {
     "mf_flat_search_workspace_size": ([I64, I64, I32, I32, I32, PSZ], I32),
     "mf_flat_search": ([I32, P, P, I64, P, P, I64, I32, I32, I32, P, P, P, P, SZ], I32),
     "mf_ivf_search_workspace_size": ([I64, I32, I32, I32, I32, I32, PSZ], I32),
-    "mf_ivf_search": ([I32, P, P, I64, P, P, I32, I32, P, P, P, P, P, I32, I32, I32, P, P, P, SZ], I32),
+    "mf_ivf_search": ([I32, P, P, I64, P, P, I32, I32, P, P, P, P, I64, P, I32, I32, I32, P, P, P, SZ], I32),
     "mf_ivf_search_preassigned_workspace_size": ([I64, I32, I32, I32, I32, I32, PSZ], I32),
-    "mf_ivf_search_preassigned": ([I32, P, P, I64, P, I32, I32, P, P, P, P, P, I32, I32, I32, P, P, P, SZ], I32),
+    "mf_ivf_search_preassigned": ([I32, P, P, I64, P, I32, I32, P, P, P, P, I64, P, I32, I32, I32, P, P, P, SZ], I32),
     "mf_topk_merge": ([I32, P, P, P, I64, I32, I32, I32, P, P], I32),
     "mf_kmeans_assign_workspace_size": ([I64, I32, I32, PSZ], I32),
     "mf_kmeans_assign": ([I32, P, P, I64, P, P, I32, I32, P, P, P, SZ], I32),
@@ -53,6 +53,8 @@ _SIGNATURES = {
     "mf_timing_enable": ([I32], I32),
     "mf_timing_reset": ([], I32),
     "mf_launch_count": ([], I64),
+    "mf_set_scan_engine": ([I32], I32),
+    "mf_device_error": ([I32, ctypes.POINTER(ctypes.c_int)], I32),
     "mf_timing_read": ([ctypes.c_char_p, ctypes.POINTER(ctypes.c_double), PI64], I32),
 }
 
@@ -144,6 +146,18 @@ def timing_read(kernel: str):
     n = ctypes.c_int64(0)
     call("mf_timing_read", kernel.encode(), ctypes.byref(t), ctypes.byref(n))
     return float(t.value), int(n.value)
+
+
+def set_scan_engine(engine: int) -> None:
+    """0 automatic, 1 SIMT only, 2 tensor cores where eligible (process-wide)."""
+    call("mf_set_scan_engine", int(engine))
+
+
+def device_error(device_index: int) -> int:
+    """Reads and clears the device-side error word (0 = none)."""
+    c = ctypes.c_int(0)
+    call("mf_device_error", int(device_index), ctypes.byref(c))
+    return int(c.value)
 
 
 def launch_count() -> int:

@@ -144,7 +144,8 @@ int coarse_metric(int metric) {
 int ivf_scan_topk(int device, cudaStream_t stream, const IvfWs& w, const float* xq, int64_t nq,
                   const int64_t* probes, int P, int nlist, const int64_t* list_offsets,
                   const float* list_vecs, const float* list_norms, const int64_t* list_ids,
-                  const int32_t* list_order, int d, int metric, int k, float* D, int64_t* I) {
+                  int64_t ntotal, const int32_t* list_order, int d, int metric, int k, float* D,
+                  int64_t* I) {
   if (metric == MF_METRIC_L2) MF_TRY(launch_norms(xq, nq, d, w.qn, stream));
   MF_TRY(run_ivf_groups_ex(w.g, probes, nq, P, nlist, list_offsets, list_order, w.pd, w.pl, k,
                            nullptr, stream));
@@ -168,6 +169,7 @@ int ivf_scan_topk(int device, cudaStream_t stream, const IvfWs& w, const float* 
   a.out_d = w.pd;
   a.out_l = w.pl;
   a.direct = 0;
+  a.xb_rows = ntotal;
   MF_TRY(launch_scan(a, metric, kEpiTopK, nq * P, device, stream));
   MF_TRY(launch_merge(w.pd, w.pl, nq, P, k, k, D, I, stream));
   return MF_OK;
@@ -261,8 +263,9 @@ int mf_ivf_search_workspace_size(int64_t nq, int nlist, int nprobe, int d, int m
 int mf_ivf_search(int device, void* stream, const float* xq, int64_t nq,
                   const float* centroids, const float* centroid_norms, int nlist, int nprobe,
                   const int64_t* list_offsets, const float* list_vecs, const float* list_norms,
-                  const int64_t* list_ids, const int32_t* list_order, int d, int metric, int k,
-                  float* distances, int64_t* labels, void* workspace, size_t workspace_bytes) {
+                  const int64_t* list_ids, int64_t ntotal, const int32_t* list_order, int d,
+                  int metric, int k, float* distances, int64_t* labels, void* workspace,
+                  size_t workspace_bytes) {
   MF_ENTER(device);
   MF_TRY(check_common(d, metric, k, true));
   MF_CHECK(nlist >= 1, MF_ERR_INVALID_ARGS, "nlist=%d", nlist);
@@ -287,7 +290,7 @@ int mf_ivf_search(int device, void* stream, const float* xq, int64_t nq,
                        coarse_metric(metric), P, nullptr, w.coarse_d, w.coarse_l, w.flat_ws,
                        w.flat_bytes));
   return ivf_scan_topk(device, s, w, xq, nq, w.coarse_l, P, nlist, list_offsets, list_vecs,
-                       list_norms, list_ids, list_order, d, metric, k, distances, labels);
+                       list_norms, list_ids, ntotal, list_order, d, metric, k, distances, labels);
 }
 
 int mf_ivf_search_preassigned_workspace_size(int64_t nq, int nlist, int nprobe, int d,
@@ -306,7 +309,7 @@ int mf_ivf_search_preassigned(int device, void* stream, const float* xq, int64_t
                               const int64_t* probes, int nprobe, int nlist,
                               const int64_t* list_offsets, const float* list_vecs,
                               const float* list_norms, const int64_t* list_ids,
-                              const int32_t* list_order, int d, int metric, int k,
+                              int64_t ntotal, const int32_t* list_order, int d, int metric, int k,
                               float* distances, int64_t* labels, void* workspace,
                               size_t workspace_bytes) {
   MF_ENTER(device);
@@ -325,8 +328,8 @@ int mf_ivf_search_preassigned(int device, void* stream, const float* xq, int64_t
   MF_CHECK(c.fits(), MF_ERR_INVALID_ARGS, "workspace too small: %zu < %zu bytes",
            workspace_bytes, c.used);
   return ivf_scan_topk(device, (cudaStream_t)stream, w, xq, nq, probes, nprobe, nlist,
-                       list_offsets, list_vecs, list_norms, list_ids, list_order, d, metric, k,
-                       distances, labels);
+                       list_offsets, list_vecs, list_norms, list_ids, ntotal, list_order, d,
+                       metric, k, distances, labels);
 }
 
 int mf_topk_merge(int device, void* stream, const float* part_distances,
@@ -660,6 +663,23 @@ int mf_ivf_range_fill(int device, void* stream, const float* xq, int64_t nq,
   a.out_d = distances;
   a.out_l = labels;
   return launch_scan(a, metric, kEpiFill, nq * P, device, (cudaStream_t)stream);
+}
+
+int mf_set_scan_engine(int engine) {
+  clear_error();
+  MF_CHECK(engine >= 0 && engine <= 2, MF_ERR_INVALID_ARGS, "engine %d not in {0,1,2}", engine);
+  set_scan_engine(engine);
+  return MF_OK;
+}
+
+int mf_device_error(int device, int* code) {
+  MF_ENTER(device);
+  MF_CHECK(code != nullptr, MF_ERR_INVALID_ARGS, "code is NULL");
+  MF_CUDA(cudaDeviceSynchronize());
+  int v = 0;
+  MF_TRY(read_device_error(&v));
+  *code = v ? MF_ERR_TIMEOUT : MF_OK;
+  return MF_OK;
 }
 
 }  // extern "C"

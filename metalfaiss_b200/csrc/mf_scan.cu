@@ -397,6 +397,8 @@ int scan_kcap(int k) {
 
 int launch_scan(const ScanArgs& a, int metric, int epi, int64_t total_items, int device,
                 cudaStream_t stream) {
+  if (epi == kEpiTopK && a.xb_rows > 0 && tc_eligible(metric, a.d, a.k, a.xb_rows))
+    return launch_tc_scan(a, metric, total_items, a.xb_rows, device, stream);
   const int kcap = epi == kEpiTopK ? scan_kcap(a.k) : 32;
   MF_CHECK(kcap != 0, MF_ERR_INVALID_ARGS, "k=%d exceeds the supported maximum %d", a.k, kMaxK);
   ScanFn fn = pick_scan(metric, epi, kcap);
@@ -509,6 +511,7 @@ int run_flat_topk(int device, cudaStream_t stream, const float* xq, int64_t nq, 
   a.nqt = p.nqt;
   a.nb = nb;
   a.rows_per_split = p.rows_per_split;
+  a.xb_rows = nb;
   a.counter = counter;
   a.direct = p.splits > 1 ? 0 : 1;
   a.out_d = p.splits > 1 ? pd : D;

@@ -52,7 +52,16 @@ struct ScanArgs {
   float radius;
   int64_t* counts;        // count pass: (nq*P)
   const int64_t* offsets; // fill pass: exclusive scan of counts (nq*P)
+  int64_t xb_rows;        // rows addressable in xb (tensor-map extent)
 };
+
+// Tensor-core engine (mf_tc.cu) for the L2 / inner-product top-k scans.
+bool tc_eligible(int metric, int d, int k, int64_t xb_rows);
+int launch_tc_scan(const ScanArgs& a, int metric, int64_t total_items, int64_t xb_rows, int device,
+                   cudaStream_t stream);
+void set_scan_engine(int engine);
+int scan_engine();
+int read_device_error(int* code);
 
 // Launches the kernel for (metric, kcap, epilogue) on a persistent grid that
 // covers `total_items` work items (an upper bound for IVF).

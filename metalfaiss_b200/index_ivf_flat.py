@@ -249,8 +249,8 @@ class IVFFlatIndex:
         nat.call("mf_ivf_search", self.device.index, nat.stream_of(self.device), nat.ptr(xq), nq,
                  nat.ptr(q._xb.buf), nat.ptr(q._norms.buf), self._nlist, self._nprobe,
                  nat.ptr(self._offsets), nat.ptr(self._vecs), nat.ptr(self._norms),
-                 nat.ptr(self._ids), nat.ptr(self._order), self._dp, m, k, nat.ptr(D), nat.ptr(I),
-                 nat.ptr(ws), ws.numel())
+                 nat.ptr(self._ids), self._vecs.shape[0], nat.ptr(self._order), self._dp, m, k,
+                 nat.ptr(D), nat.ptr(I), nat.ptr(ws), ws.numel())
         return SearchResult(D, I)
 
     def _check_k(self, k):
@@ -290,8 +290,8 @@ class IVFFlatIndex:
         nat.call("mf_ivf_search_preassigned", self.device.index, nat.stream_of(self.device),
                  nat.ptr(xq), nq, nat.ptr(probes), P, self._nlist, nat.ptr(self._offsets),
                  nat.ptr(self._vecs), nat.ptr(self._norms), nat.ptr(self._ids),
-                 nat.ptr(self._order), self._dp, m, k, nat.ptr(D), nat.ptr(I), nat.ptr(ws),
-                 ws.numel())
+                 self._vecs.shape[0], nat.ptr(self._order), self._dp, m, k, nat.ptr(D), nat.ptr(I),
+                 nat.ptr(ws), ws.numel())
         return SearchResult(D, I)
 
     def range_search(self, xs, radius: float) -> SearchRangeResult:

@@ -1,0 +1,92 @@
+"""The tensor-core (tcgen05, 3xTF32) and SIMT scan engines against each other
+and against the oracle, on flat and IVF searches."""
+import numpy as np
+import pytest
+
+from metalfaiss_b200 import FlatIndex, IVFFlatIndex, MetricType
+from metalfaiss_b200 import _native as nat
+from metalfaiss_b200 import synthetic as syn
+from oracle import compare, oracle
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture
+def engine():
+    yield nat.set_scan_engine
+    nat.set_scan_engine(0)
+    assert nat.device_error(0) == 0, "a bounded device wait timed out"
+
+
+def _flat(metric, d, n, nq, k, seed, engine_id, data="gauss"):
+    nat.set_scan_engine(engine_id)
+    if data == "gauss":
+        xb, xq = syn.gaussian(n, d, seed), syn.gaussian(nq, d, seed + 1)
+    else:
+        xb, cen, _ = syn.mixture(n, d, 64, seed)
+        xq, _, _ = syn.mixture(nq, d, 64, seed + 1, centres=cen)
+    idx = FlatIndex(d, metric)
+    idx.add(xb)
+    D, I = idx.search(xq, k).numpy()
+    return xb, xq, D, I
+
+
+@pytest.mark.parametrize("metric", [MetricType.L2, MetricType.INNER_PRODUCT])
+@pytest.mark.parametrize("d,k", [(32, 10), (64, 1), (128, 32), (96, 100), (256, 256), (48, 7)])
+def test_tc_flat_matches_oracle(cuda_device, engine, metric, d, k):
+    xb, xq, D, I = _flat(metric, d, 5000, 77, k, seed=d + k, engine_id=2)
+    D_ref, I_ref = oracle.flat_search(xq, xb, k, int(metric))
+    atol = compare.l2_atol(xq, xb) if metric == MetricType.L2 else 1e-5 * (1 + np.abs(D_ref).max())
+    errs = compare.check_knn(D, I, D_ref, I_ref, compare.exact_lookup(xq, xb, int(metric)), atol=atol)
+    assert not errs, errs[:5]
+
+
+def test_tc_precision_on_mixture(cuda_device, engine):
+    """Distances of the 3xTF32 path against fp64 on clustered data (norms ~ 5x the distances)."""
+    xb, xq, D, I = _flat(MetricType.L2, 128, 20000, 200, 10, seed=3, engine_id=2, data="mix")
+    exact = oracle.pairwise_exact(xq, xb, oracle.L2)
+    got = D.astype(np.float64)
+    ref = np.take_along_axis(exact, I, 1)
+    rel = np.abs(got - ref) / np.maximum(ref, 1e-6)
+    print(f"3xTF32 L2 max relative distance error {rel.max():.3e} (median {np.median(rel):.3e})")
+    assert rel.max() < 1e-4
+    D_ref, I_ref = oracle.flat_search(xq, xb, 10, oracle.L2)
+    errs = compare.check_knn(D, I, D_ref, I_ref, compare.exact_lookup(xq, xb, oracle.L2),
+                             atol=compare.l2_atol(xq, xb))
+    assert not errs, errs[:5]
+
+
+@pytest.mark.parametrize("nprobe,k", [(1, 10), (8, 32), (16, 100)])
+def test_tc_ivf_equals_simt(cuda_device, engine, nprobe, k):
+    x, cen, _ = syn.mixture(40000, 64, 96, seed=7)
+    idx = IVFFlatIndex(64, 96)
+    idx.set_centroids(oracle.kmeans_train(x, 96, 2, 7))
+    idx.add(x)
+    idx.nprobe = nprobe
+    xq, _, _ = syn.mixture(300, 64, 96, seed=8, centres=cen)
+    nat.set_scan_engine(1)
+    D1, I1 = idx.search(xq, k).numpy()
+    nat.set_scan_engine(2)
+    D2, I2 = idx.search(xq, k).numpy()
+    errs = compare.check_knn(D2, I2, D1, I1, compare.exact_lookup(xq, x, oracle.L2),
+                             atol=compare.l2_atol(xq, x))
+    assert not errs, errs[:5]
+
+
+def test_tc_many_items_persistent(cuda_device, engine):
+    """More work items than CTAs, lists of every size, groups of 1..32 queries."""
+    x, cen, _ = syn.mixture(60000, 128, 300, seed=9)
+    idx = IVFFlatIndex(128, 300)
+    idx.set_centroids(x[:300])
+    idx.add(x)
+    idx.nprobe = 20
+    xq, _, _ = syn.mixture(2000, 128, 300, seed=10, centres=cen)
+    nat.set_scan_engine(2)
+    D, I = idx.search(xq, 10).numpy()
+    offs = idx.list_offsets.cpu().numpy()
+    vecs = idx._vecs[:, :128].cpu().numpy()
+    ids = idx._ids[: idx.ntotal].cpu().numpy()
+    D_ref, I_ref = oracle.ivf_search(xq, x[:300], offs, vecs, ids, 20, 10)
+    errs = compare.check_knn(D, I, D_ref, I_ref, compare.exact_lookup(xq, x, oracle.L2),
+                             atol=compare.l2_atol(xq, x))
+    assert not errs, errs[:5]
