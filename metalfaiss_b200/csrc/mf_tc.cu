@@ -34,13 +34,29 @@ __device__ int g_device_error = 0;
 namespace {
 using namespace sm100;
 
-constexpr int kTcThreads = 128;
+#ifdef MF_TC_PROFILE
+// Phase cycle counters of the tensor-core scan (instrumented builds only).
+__device__ unsigned long long g_tc_prof[16];
+#define TCP_DECL unsigned long long _tcp[16] = {0}; long long _tc0 = 0;
+#define TCP_BEGIN() _tc0 = clock64()
+#define TCP_END(i) _tcp[i] += (unsigned long long)(clock64() - _tc0)
+#define TCP_FLUSH()                                                                  \
+  if (tid == 0 || tid == 64)                                                         \
+    for (int _i = 0; _i < 16; ++_i) atomicAdd(&g_tc_prof[_i], _tcp[_i]);
+#else
+#define TCP_DECL
+#define TCP_BEGIN()
+#define TCP_END(i)
+#define TCP_FLUSH()
+#endif
+
+constexpr int kTcThreads = 256;
 constexpr int kTcM = 128;                 // rows per tile (TMEM lanes)
 constexpr int kTcN = 32;                  // queries per item (accumulator columns)
 constexpr int kTcStageBytes = kTcM * 128;  // one 128 x 32 fp32 box
 constexpr int kTcBBlockBytes = kTcN * 128;
 constexpr int kTcMaxD = 256;
-constexpr int kTcMaxSmem = 227 * 1024;
+constexpr int kTcMaxSmem = 227 * 1024 - 256;  // dynamic part; static smem takes the rest
 
 struct TcSmem {
   int SA;  // A stages
@@ -107,6 +123,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int tid = threadIdx.x;
   const int lane = tid & 31;
   const int warp = tid >> 5;
+  const int quad = warp & 3;   // TMEM lane quadrant this warp may access
+  const int half = warp >> 2;  // which 16 of the 32 query columns it reads
   const int d = a.d;
   const int k = a.k;
   const int SA = L.SA;
@@ -133,23 +151,39 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const uint32_t tmem = *s_tmem;
   constexpr uint32_t idesc = idesc_tf32(kTcM, kTcN);
 
-  uint32_t g = 0;        // A-stage sequence consumed so far (same in every thread)
-  uint32_t g_issued = 0; // A-stage sequence issued (thread 0)
-  uint32_t tt = 0;       // tiles so far
+  TCP_DECL
+#ifdef MF_TC_PROFILE
+  const long long _t_start = clock64();
+#endif
+  uint32_t g = 0;         // A-stage sequence consumed so far (same in every thread)
+  uint32_t g_issued = 0;  // A-stage sequence issued (thread 0)
+  uint32_t tt = 0;        // tiles so far
+  int next_load = 0;      // next K-block of the current item to load (thread 0)
 
-  // Loads the K-block `li` of the current item (sequence number `seq`).
-  auto issue_load = [&](uint32_t seq, int li, long long rb) {
-    const int s = seq % SA;
-    if (seq >= (uint32_t)SA) mbar_wait(&mdone[s], ((seq / SA) - 1) & 1, s_abort, &g_device_error);
-    const int t = li / KB;
-    const int kb = li - t * KB;
-    mbar_arrive_expect_tx(&full[s], kTcStageBytes);
-    tma_load_2d(A + size_t(s) * (kTcStageBytes / 4), &tmap, kb * 32, (int)(rb + (long long)t * kTcM),
-                &full[s]);
-    g_issued = seq + 1;
+  // Thread 0: issues the loads of the current item below `upto`; when `block`
+  // is false it stops at the first stage whose previous MMAs are still running.
+  auto pump = [&](int upto, bool block, long long rb, int nL) {
+    if (upto > nL) upto = nL;
+    while (next_load < upto) {
+      const uint32_t seq = g + next_load;
+      const int s = seq % SA;
+      if (seq >= (uint32_t)SA) {
+        const uint32_t par = ((seq / SA) - 1) & 1;
+        if (block) mbar_wait(&mdone[s], par, s_abort, &g_device_error);
+        else if (!mbar_test(&mdone[s], par)) break;
+      }
+      const int t = next_load / KB;
+      const int kb = next_load - t * KB;
+      mbar_arrive_expect_tx(&full[s], kTcStageBytes);
+      tma_load_2d(A + size_t(s) * (kTcStageBytes / 4), &tmap, kb * 32,
+                  (int)(rb + (long long)t * kTcM), &full[s]);
+      g_issued = seq + 1;
+      ++next_load;
+    }
   };
 
   for (;;) {
+    TCP_BEGIN();
     if (tid == 0) s_item = atomicAdd(a.counter, 1);
     __syncthreads();
     const int item = s_item;
@@ -194,6 +228,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
     }
     __syncthreads();
+    const long long rb = s_rb;
+    const long long re = s_re;
+    const long long nrows = re > rb ? re - rb : 0;
+    const int nT = (int)((nrows + kTcM - 1) / kTcM);
+    const int nL = nT * KB;
+    if (tid == 0) {
+      next_load = 0;
+      pump(SA, false, rb, nL);  // start streaming rows while the queries are prepared
+    }
     if (tid < kTcN) {
       const int qr = s_qrow[tid];
       s_qn[tid] = (METRIC == MF_METRIC_L2 && qr >= 0) ? a.qnorms[qr] : 0.0f;
@@ -217,61 +260,60 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       *reinterpret_cast<float4*>(Bh + off) = h;
       *reinterpret_cast<float4*>(Bl + off) = l;
     }
-    WarpTopK<KCAP> tk[8];
+    WarpTopK<KCAP> tk[4];
 #pragma unroll
-    for (int jj = 0; jj < 8; ++jj) {
-      const int j = warp * 8 + jj;
+    for (int jj = 0; jj < 4; ++jj) {
+      const int j = warp * 4 + jj;
       tk[jj].init(lists + j * KCAP, bufs + j * 32, k, lane);
     }
     fence_proxy_async_smem();
     __syncthreads();
-
-    const long long rb = s_rb;
-    const long long re = s_re;
-    const long long nrows = re > rb ? re - rb : 0;
-    const int nT = (int)((nrows + kTcM - 1) / kTcM);
-    const int nL = nT * KB;
-
-    if (tid == 0) {
-      const int pre = nL < SA - 1 ? nL : SA - 1;
-      for (int i = 0; i < pre; ++i) issue_load(g + i, i, rb);
-    }
+    TCP_END(0);
 
     // Epilogue of local tile u: accumulator -> distances -> top-k offers.
     auto epilogue = [&](int u) {
       const uint32_t ts = tt + u;
       const int b = ts & 1;
+      TCP_BEGIN();
       mbar_wait(&accf[b], (ts >> 1) & 1, s_abort, &g_device_error);
+      TCP_END(1);
+      TCP_BEGIN();
       tc_fence_after();
-      float v[32];
-      tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + b * kTcN, v);
+      float v[16];
+      tmem_ld16(tmem + ((uint32_t)(quad * 32) << 16) + b * kTcN + half * 16, v);
       tc_fence_before();
       const long long r0 = rb + (long long)u * kTcM;
-      const long long row = r0 + warp * 32 + lane;
+      const long long row = r0 + quad * 32 + lane;
       const bool valid = row < re;
       const float xn = (METRIC == MF_METRIC_L2 && valid) ? a.xnorms[row] : 0.0f;
 #pragma unroll
-      for (int j = 0; j < kTcN; ++j) {
+      for (int i = 0; i < 16; ++i) {
+        const int j = half * 16 + i;
         float dist;
-        if (METRIC == MF_METRIC_L2) dist = l2_from_dot(s_qn[j], xn, v[j]);
-        else dist = -v[j];
-        T[j * kTcM + warp * 32 + lane] = dist;
+        if (METRIC == MF_METRIC_L2) dist = l2_from_dot(s_qn[j], xn, v[i]);
+        else dist = -v[i];
+        T[j * kTcM + quad * 32 + lane] = dist;
       }
       __syncthreads();
+      TCP_END(2);
+      TCP_BEGIN();
 #pragma unroll
-      for (int jj = 0; jj < 8; ++jj) {
-        const int j = warp * 8 + jj;
+      for (int jj = 0; jj < 4; ++jj) {
+        const int j = warp * 4 + jj;
         if (s_qrow[j] < 0) continue;
+        unsigned long long key[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           const int ri = i * 32 + lane;
           const long long r = r0 + ri;
-          const unsigned long long key =
-              r < re ? make_key(T[j * kTcM + ri], (unsigned int)r) : kEmptyKey;
-          tk[jj].offer(key, k, lane);
+          key[i] = r < re ? make_key(T[j * kTcM + ri], (unsigned int)r) : kEmptyKey;
         }
+        tk[jj].offer4(key, k, lane);
       }
+      TCP_END(3);
+      TCP_BEGIN();
       __syncthreads();
+      TCP_END(4);
     };
 
     for (int li = 0; li < nL; ++li) {
@@ -280,12 +322,18 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const int t = li / KB;
       const int kb = li - t * KB;
       const int lb = seq & 1;  // lo buffer
+      TCP_BEGIN();
+      if (tid == 0) pump(li + 1, true, rb, nL);  // this K-block's load must be in flight
       // the lo buffer was last read by the MMAs of sequence seq-2
       if (seq >= 2) mbar_wait(&mdone[(seq - 2) % SA], ((seq - 2) / SA) & 1, s_abort, &g_device_error);
+      TCP_END(5);
+      TCP_BEGIN();
       mbar_wait(&full[s], (seq / SA) & 1, s_abort, &g_device_error);
+      TCP_END(6);
+      TCP_BEGIN();
       float4* As = reinterpret_cast<float4*>(A + size_t(s) * (kTcStageBytes / 4));
       float4* Ls = reinterpret_cast<float4*>(Lo + size_t(lb) * (kTcStageBytes / 4));
-#pragma unroll 4
+#pragma unroll
       for (int e = tid; e < kTcStageBytes / 16; e += kTcThreads) {
         const float4 v = As[e];
         float4 h, l;
@@ -296,10 +344,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         As[e] = h;
         Ls[e] = l;
       }
+      TCP_END(7);
+      TCP_BEGIN();
       fence_proxy_async_smem();
       tc_fence_before();
       __syncthreads();
       tc_fence_after();
+      TCP_END(8);
+      TCP_BEGIN();
       if (tid == 0) {
         const uint32_t dt = tmem + ((tt + t) & 1) * kTcN;
         const uint32_t a_addr = smem_u32(As);
@@ -316,17 +368,20 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
         mma_commit(&mdone[s]);
         if (kb == KB - 1) mma_commit(&accf[(tt + t) & 1]);
-        const int nli = li + SA - 1;
-        if (nli < nL) issue_load(g + nli, nli, rb);
+        TCP_END(9);
+        TCP_BEGIN();
+        pump(li + SA, false, rb, nL);
+        TCP_END(10);
       }
       if (kb == KB - 1 && t >= 1) epilogue(t - 1);
     }
     if (nT >= 1) epilogue(nT - 1);
 
     // ---- results of the item
+    TCP_BEGIN();
 #pragma unroll
-    for (int jj = 0; jj < 8; ++jj) {
-      const int j = warp * 8 + jj;
+    for (int jj = 0; jj < 4; ++jj) {
+      const int j = warp * 4 + jj;
       if (s_qrow[j] < 0) continue;
       tk[jj].flush(k, lane);
       const long long slot = s_qout[j];
@@ -349,8 +404,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     g += nL;
     tt += nT;
     __syncthreads();
+    TCP_END(11);
   }
 
+#ifdef MF_TC_PROFILE
+  _tcp[13] = (unsigned long long)(clock64() - _t_start);
+  _tcp[14] = tt;
+  _tcp[15] = g;
+#endif
+  TCP_FLUSH();
   // ---- teardown: copies and MMAs in flight finish before TMEM is released
   if (tid == 0) {
     int dummy = 0;
@@ -407,11 +469,13 @@ void set_scan_engine(int e) { g_engine = e; }
 int scan_engine() { return g_engine; }
 
 bool tc_eligible(int metric, int d, int k, int64_t xb_rows) {
-  if (g_engine == 1) return false;
+  if (g_engine != 2) return false;  // automatic selection keeps the SIMT scan for now
   if (metric != MF_METRIC_L2 && metric != MF_METRIC_INNER_PRODUCT) return false;
   if (d < 32 || d > kTcMaxD) return false;
   if (xb_rows < kTcM) return false;
-  return scan_kcap(k) != 0;
+  const int kcap = scan_kcap(k);
+  if (kcap == 0) return false;
+  return tc_layout(d, kcap, 2).total <= (size_t)kTcMaxSmem;
 }
 
 int launch_tc_scan(const ScanArgs& a, int metric, int64_t total_items, int64_t xb_rows,
@@ -423,7 +487,7 @@ int launch_tc_scan(const ScanArgs& a, int metric, int64_t total_items, int64_t x
   MF_CHECK(fn != nullptr, MF_ERR_METRIC, "metric %d has no tensor-core scan", metric);
   int SA = 8;
   TcSmem lay = tc_layout(a.d, kcap, SA);
-  while (SA > 3 && lay.total > (size_t)kTcMaxSmem) lay = tc_layout(a.d, kcap, --SA);
+  while (SA > 2 && lay.total > (size_t)kTcMaxSmem) lay = tc_layout(a.d, kcap, --SA);
   MF_CHECK(lay.total <= (size_t)kTcMaxSmem, MF_ERR_INVALID_ARGS,
            "tensor-core scan does not fit shared memory (d=%d k=%d)", a.d, a.k);
   PFN_cuTensorMapEncodeTiled_v12000 enc;
@@ -441,10 +505,10 @@ int launch_tc_scan(const ScanArgs& a, int metric, int64_t total_items, int64_t x
     std::lock_guard<std::mutex> lk(g_tc_mu);
     const int mi = metric == MF_METRIC_L2 ? 0 : 1;
     const int ki = kcap == 32 ? 0 : kcap == 64 ? 1 : kcap == 128 ? 2 : 3;
-    if (device >= 0 && device < 64 && g_tc_attr[device][mi][ki] < (int)lay.total) {
+    if (device < 0 || device >= 64 || g_tc_attr[device][mi][ki] < (int)lay.total) {
       MF_CUDA(cudaFuncSetAttribute(reinterpret_cast<const void*>(fn),
-                                   cudaFuncAttributeMaxDynamicSharedMemorySize, kTcMaxSmem));
-      g_tc_attr[device][mi][ki] = kTcMaxSmem;
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)lay.total));
+      if (device >= 0 && device < 64) g_tc_attr[device][mi][ki] = (int)lay.total;
     }
   }
   if (total_items <= 0) return MF_OK;
@@ -456,6 +520,17 @@ int launch_tc_scan(const ScanArgs& a, int metric, int64_t total_items, int64_t x
   MF_LAUNCH_CHECK();
   return MF_OK;
 }
+
+#ifdef MF_TC_PROFILE
+extern "C" MF_API int mf_tc_profile_read(unsigned long long* out16, int reset) {
+  MF_CUDA(cudaMemcpyFromSymbol(out16, g_tc_prof, 16 * sizeof(unsigned long long)));
+  if (reset) {
+    unsigned long long z[16] = {0};
+    MF_CUDA(cudaMemcpyToSymbol(g_tc_prof, z, sizeof(z)));
+  }
+  return MF_OK;
+}
+#endif
 
 int read_device_error(int* code) {
   int v = 0;

@@ -47,6 +47,46 @@ __device__ __forceinline__ int warp_rank_below(unsigned long long sorted, unsign
   return base;
 }
 
+// Sorts the nbuf (<= 32) buffered keys and merges them into the sorted list
+// of k keys; returns the new k-th key. Out of line: it is rare on the hot path
+// and keeping it out of the callers keeps their code small.
+template <int KCAP>
+__device__ __noinline__ unsigned long long merge_into_list(unsigned long long* list,
+                                                          const unsigned long long* buf, int nbuf,
+                                                          int k, int lane) {
+  __syncwarp();
+  unsigned long long c = (lane < nbuf) ? buf[lane] : kEmptyKey;
+  c = warp_sort32(c, lane);
+  constexpr int PER = (KCAP + 31) / 32;
+  unsigned long long e[PER];
+  int np[PER];
+#pragma unroll
+  for (int p = 0; p < PER; ++p) {
+    int i = lane + 32 * p;
+    e[p] = (i < k) ? list[i] : kEmptyKey;
+    int r = warp_rank_below(c, e[p]);
+    np[p] = i + r;
+  }
+  int cpos = 1 << 30;
+  if (lane < nbuf) {
+    int lo = 0, hi = k;
+    while (lo < hi) {
+      int mid = (lo + hi) >> 1;
+      if (list[mid] < c) lo = mid + 1; else hi = mid;
+    }
+    cpos = lane + lo;
+  }
+  __syncwarp();
+#pragma unroll
+  for (int p = 0; p < PER; ++p) {
+    int i = lane + 32 * p;
+    if (i < k && np[p] < k) list[np[p]] = e[p];
+  }
+  if (cpos < k) list[cpos] = c;
+  __syncwarp();
+  return list[k - 1];
+}
+
 // Per-query state held by the owning warp. The list lives in shared memory
 // (`list`, capacity >= k); nbuf and thr are warp-uniform registers.
 template <int KCAP>
@@ -68,38 +108,8 @@ struct WarpTopK {
 
   __device__ __forceinline__ void flush(int k, int lane) {
     if (nbuf == 0) return;
-    __syncwarp();
-    unsigned long long c = (lane < nbuf) ? buf[lane] : kEmptyKey;
-    c = warp_sort32(c, lane);
-    constexpr int PER = (KCAP + 31) / 32;
-    unsigned long long e[PER];
-    int np[PER];
-#pragma unroll
-    for (int p = 0; p < PER; ++p) {
-      int i = lane + 32 * p;
-      e[p] = (i < k) ? list[i] : kEmptyKey;
-      int r = warp_rank_below(c, e[p]);
-      np[p] = i + r;
-    }
-    int cpos = 1 << 30;
-    if (lane < nbuf) {
-      int lo = 0, hi = k;
-      while (lo < hi) {
-        int mid = (lo + hi) >> 1;
-        if (list[mid] < c) lo = mid + 1; else hi = mid;
-      }
-      cpos = lane + lo;
-    }
-    __syncwarp();
-#pragma unroll
-    for (int p = 0; p < PER; ++p) {
-      int i = lane + 32 * p;
-      if (i < k && np[p] < k) list[np[p]] = e[p];
-    }
-    if (cpos < k) list[cpos] = c;
-    __syncwarp();
+    thr = merge_into_list<KCAP>(list, buf, nbuf, k, lane);
     nbuf = 0;
-    thr = list[k - 1];
   }
 
   // Offers one candidate per lane (kEmptyKey = no candidate).
@@ -117,6 +127,15 @@ struct WarpTopK {
     }
     if (pass) buf[nbuf + __popc(m & lanemask_lt())] = key;
     nbuf += n;
+  }
+
+  // Offers four candidates per lane; one warp vote skips the common case where
+  // none of the 128 beats the current k-th best.
+  __device__ __forceinline__ void offer4(const unsigned long long (&key)[4], int k, int lane) {
+    const bool any = (key[0] < thr) | (key[1] < thr) | (key[2] < thr) | (key[3] < thr);
+    if (!__any_sync(0xffffffffu, any)) return;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) offer(key[i], k, lane);
   }
 };
 
