@@ -76,6 +76,14 @@ MF_API const char* mf_last_error(void);
 /* Largest k (and nprobe) the fused top-k kernels accept. */
 MF_API int mf_max_k(void);
 
+/* tf32 residual of each element: lo = x - x with its 13 low mantissa bits
+ * cleared. The tensor cores read fp32 operands as tf32 by that truncation, so
+ * (x, lo) is the exact two-term split the 3xTF32 scans consume. Computed once
+ * per database at add time (no reference counterpart: the reference computes
+ * distances in MLX fp32, python/metalfaiss/distances.py:140-173). */
+MF_API int mf_tf32_residual(int device, void* stream, const float* x, int64_t n, int d,
+                            float* lo);
+
 /* Squared L2 norm of each row: norms[i] = sum_j x[i,j]^2.
  * Replaces the norms_b term of pairwise_L2sqr, python/metalfaiss/distances.py:163-164,
  * computed once at add time instead of on every search. */
@@ -89,7 +97,9 @@ MF_API int mf_flat_search_workspace_size(int64_t nq, int64_t nb, int d, int metr
 
 /* Exact kNN of xq (nq,d) against xb (nb,d): distances/labels (nq,k), ascending.
  * labels[i,j] = ids[pos] when ids != NULL, else the row position pos.
- * xb_norms (nb) is required for L2 and ignored otherwise.
+ * xb_norms (nb) is required for L2 and ignored otherwise. xb_lo (nb,d), optional,
+ * is mf_tf32_residual(xb): when given, L2 / inner-product searches with 32 <= d and
+ * k <= 64 run on the tensor cores (3xTF32), otherwise on the SIMT scan.
  * k is clipped by the caller to nb (python/metalfaiss/utils/sorting.py:66-67); here
  * slots beyond nb are padded (+inf, -1).
  * Replaces FlatIndex.search, python/metalfaiss/indexflat.py:70-110 (pairwise_L2sqr
@@ -97,8 +107,8 @@ MF_API int mf_flat_search_workspace_size(int64_t nq, int64_t nb, int d, int metr
  * utils/sorting.py:39-87, id map indexflat.py:109) and the tuple-returning quantizer
  * search python/metalfaiss/index/flat_index.py:70-121. */
 MF_API int mf_flat_search(int device, void* stream, const float* xq, int64_t nq,
-                   const float* xb, const float* xb_norms, int64_t nb, int d,
-                   int metric, int k, const int64_t* ids, float* distances,
+                   const float* xb, const float* xb_norms, const float* xb_lo, int64_t nb,
+                   int d, int metric, int k, const int64_t* ids, float* distances,
                    int64_t* labels, void* workspace, size_t workspace_bytes);
 
 /* ---------------------------------------------------------------- IVFFlat */
@@ -106,6 +116,8 @@ MF_API int mf_flat_search(int device, void* stream, const float* xq, int64_t nq,
 /* Inverted lists are CSR: list l holds rows [list_offsets[l], list_offsets[l+1])
  * of list_vecs (ntotal,d), with list_norms (ntotal) and list_ids (ntotal);
  * ntotal = list_offsets[nlist] is passed by value (the host knows it).
+ * list_lo (ntotal,d), optional, is mf_tf32_residual(list_vecs): when given, the
+ * L2 / inner-product scan runs on the tensor cores where the shape allows.
  * list_order (nlist, optional) is a permutation of the list ids giving the order
  * in which the scan takes work (largest lists first balances the SMs). */
 
@@ -120,8 +132,8 @@ MF_API int mf_ivf_search_workspace_size(int64_t nq, int nlist, int nprobe, int d
 MF_API int mf_ivf_search(int device, void* stream, const float* xq, int64_t nq,
                   const float* centroids, const float* centroid_norms, int nlist,
                   int nprobe, const int64_t* list_offsets, const float* list_vecs,
-                  const float* list_norms, const int64_t* list_ids, int64_t ntotal,
-                  const int32_t* list_order, int d, int metric, int k,
+                  const float* list_norms, const float* list_lo, const int64_t* list_ids,
+                  int64_t ntotal, const int32_t* list_order, int d, int metric, int k,
                   float* distances, int64_t* labels, void* workspace,
                   size_t workspace_bytes);
 
@@ -136,8 +148,9 @@ MF_API int mf_ivf_search_preassigned_workspace_size(int64_t nq, int nlist, int n
 MF_API int mf_ivf_search_preassigned(int device, void* stream, const float* xq, int64_t nq,
                               const int64_t* probes, int nprobe, int nlist,
                               const int64_t* list_offsets, const float* list_vecs,
-                              const float* list_norms, const int64_t* list_ids,
-                              int64_t ntotal, const int32_t* list_order, int d, int metric, int k,
+                              const float* list_norms, const float* list_lo,
+                              const int64_t* list_ids, int64_t ntotal,
+                              const int32_t* list_order, int d, int metric, int k,
                               float* distances, int64_t* labels, void* workspace,
                               size_t workspace_bytes);
 

@@ -31,12 +31,13 @@ _SIGNATURES = {
     "mf_last_error": ([], ctypes.c_char_p),
     "mf_max_k": ([], I32),
     "mf_vector_norms": ([I32, P, P, I64, I32, P], I32),
+    "mf_tf32_residual": ([I32, P, P, I64, I32, P], I32),
     "mf_flat_search_workspace_size": ([I64, I64, I32, I32, I32, PSZ], I32),
-    "mf_flat_search": ([I32, P, P, I64, P, P, I64, I32, I32, I32, P, P, P, P, SZ], I32),
+    "mf_flat_search": ([I32, P, P, I64, P, P, P, I64, I32, I32, I32, P, P, P, P, SZ], I32),
     "mf_ivf_search_workspace_size": ([I64, I32, I32, I32, I32, I32, PSZ], I32),
-    "mf_ivf_search": ([I32, P, P, I64, P, P, I32, I32, P, P, P, P, I64, P, I32, I32, I32, P, P, P, SZ], I32),
+    "mf_ivf_search": ([I32, P, P, I64, P, P, I32, I32, P, P, P, P, P, I64, P, I32, I32, I32, P, P, P, SZ], I32),
     "mf_ivf_search_preassigned_workspace_size": ([I64, I32, I32, I32, I32, I32, PSZ], I32),
-    "mf_ivf_search_preassigned": ([I32, P, P, I64, P, I32, I32, P, P, P, P, I64, P, I32, I32, I32, P, P, P, SZ], I32),
+    "mf_ivf_search_preassigned": ([I32, P, P, I64, P, I32, I32, P, P, P, P, P, I64, P, I32, I32, I32, P, P, P, SZ], I32),
     "mf_topk_merge": ([I32, P, P, P, I64, I32, I32, I32, P, P], I32),
     "mf_kmeans_assign_workspace_size": ([I64, I32, I32, PSZ], I32),
     "mf_kmeans_assign": ([I32, P, P, I64, P, P, I32, I32, P, P, P, SZ], I32),

@@ -111,6 +111,9 @@ struct IvfWs {
   int64_t* pl;
   int64_t* pair_counts;
   int64_t* pair_offsets64;
+  float* g_hi;       // gathered query rows per (query, probe) pair (tensor cores)
+  float* g_lo;
+  float* cent_lo;    // tf32 residuals of the centroids (coarse step, tensor cores)
 };
 
 // mode: 0 = top-k search, 1 = preassigned top-k, 2 = range
@@ -123,6 +126,7 @@ IvfWs carve_ivf(Carver& c, int64_t nq, int nlist, int P, int d, int k, int mode,
     FlatPlan fp = plan_flat(nq, nlist, d, P, device);
     w.flat_bytes = fp.bytes;
     w.flat_ws = c.take<char>(fp.bytes);
+    w.cent_lo = c.take<float>((size_t)nlist * d);
   }
   w.g = carve_ivf_groups(c, nq, nlist, P);
   if (mode == 2) {
@@ -131,6 +135,8 @@ IvfWs carve_ivf(Carver& c, int64_t nq, int nlist, int P, int d, int k, int mode,
   } else {
     w.pd = c.take<float>((size_t)nq * P * k);
     w.pl = c.take<int64_t>((size_t)nq * P * k);
+    w.g_hi = c.take<float>((size_t)nq * P * d);
+    w.g_lo = c.take<float>((size_t)nq * P * d);
   }
   return w;
 }
@@ -143,12 +149,12 @@ int coarse_metric(int metric) {
 
 int ivf_scan_topk(int device, cudaStream_t stream, const IvfWs& w, const float* xq, int64_t nq,
                   const int64_t* probes, int P, int nlist, const int64_t* list_offsets,
-                  const float* list_vecs, const float* list_norms, const int64_t* list_ids,
-                  int64_t ntotal, const int32_t* list_order, int d, int metric, int k, float* D,
-                  int64_t* I) {
+                  const float* list_vecs, const float* list_norms, const float* list_lo,
+                  const int64_t* list_ids, int64_t ntotal, const int32_t* list_order, int d,
+                  int metric, int k, float* D, int64_t* I) {
+  const bool tc = list_lo != nullptr && tc_eligible(metric, d, k, ntotal);
+  const int group = tc ? tc_group() : kScanTQ;
   if (metric == MF_METRIC_L2) MF_TRY(launch_norms(xq, nq, d, w.qn, stream));
-  MF_TRY(run_ivf_groups_ex(w.g, probes, nq, P, nlist, list_offsets, list_order, w.pd, w.pl, k,
-                           nullptr, stream));
   ScanArgs a{};
   a.xq = xq;
   a.qnorms = w.qn;
@@ -169,8 +175,26 @@ int ivf_scan_topk(int device, cudaStream_t stream, const IvfWs& w, const float* 
   a.out_d = w.pd;
   a.out_l = w.pl;
   a.direct = 0;
-  a.xb_rows = ntotal;
-  MF_TRY(launch_scan(a, metric, kEpiTopK, nq * P, device, stream));
+  // Two phases: every query's first probe (its nearest list), then the rest
+  // with the first probe's k-th distance as an exact bound on the final k-th.
+  const int phases = P > 1 ? 2 : 1;
+  for (int ph = 0; ph < phases; ++ph) {
+    const int s0 = ph == 0 ? 0 : 1;
+    const int s1 = phases == 1 ? P : (ph == 0 ? 1 : P);
+    MF_TRY(run_ivf_groups_ex(w.g, probes, nq, P, nlist, list_offsets, list_order, w.pd, w.pl, k,
+                             nullptr, group, stream, s0, s1));
+    a.bound_pd = ph == 1 ? w.pd : nullptr;
+    if (tc) {
+      // A operand: the queries of every (query, probe) pair, gathered in list order
+      MF_TRY(launch_gather_queries(xq, d, w.g.pairs, w.g.pair_offsets + nlist, nq * P, P, w.g_hi,
+                                   w.g_lo, stream));
+      a.xq = w.g_hi;
+      MF_TRY(launch_tc_scan(a, metric, w.g_lo, nq * P, list_lo, ntotal, nq * P, device, stream));
+      a.xq = xq;
+    } else {
+      MF_TRY(launch_scan(a, metric, kEpiTopK, nq * P, device, stream));
+    }
+  }
   MF_TRY(launch_merge(w.pd, w.pl, nq, P, k, k, D, I, stream));
   return MF_OK;
 }
@@ -225,7 +249,7 @@ int mf_flat_search_workspace_size(int64_t nq, int64_t nb, int d, int metric, int
 }
 
 int mf_flat_search(int device, void* stream, const float* xq, int64_t nq, const float* xb,
-                   const float* xb_norms, int64_t nb, int d, int metric, int k,
+                   const float* xb_norms, const float* xb_lo, int64_t nb, int d, int metric, int k,
                    const int64_t* ids, float* distances, int64_t* labels, void* workspace,
                    size_t workspace_bytes) {
   MF_ENTER(device);
@@ -242,8 +266,9 @@ int mf_flat_search(int device, void* stream, const float* xq, int64_t nq, const 
   MF_TRY(check_device_ptr(ids, "ids", true));
   if (metric == MF_METRIC_L2) MF_TRY(check_device_ptr(xb_norms, "xb_norms", nb == 0));
   MF_TRY(check_device_ptr(workspace, "workspace", true));
-  return run_flat_topk(device, (cudaStream_t)stream, xq, nq, xb, xb_norms, nb, d, metric, k, ids,
-                       distances, labels, workspace, workspace_bytes);
+  MF_TRY(check_device_ptr(xb_lo, "xb_lo", true));
+  return run_flat_topk(device, (cudaStream_t)stream, xq, nq, xb, xb_norms, xb_lo, nb, d, metric,
+                       k, ids, distances, labels, workspace, workspace_bytes);
 }
 
 int mf_ivf_search_workspace_size(int64_t nq, int nlist, int nprobe, int d, int metric, int k,
@@ -263,9 +288,9 @@ int mf_ivf_search_workspace_size(int64_t nq, int nlist, int nprobe, int d, int m
 int mf_ivf_search(int device, void* stream, const float* xq, int64_t nq,
                   const float* centroids, const float* centroid_norms, int nlist, int nprobe,
                   const int64_t* list_offsets, const float* list_vecs, const float* list_norms,
-                  const int64_t* list_ids, int64_t ntotal, const int32_t* list_order, int d,
-                  int metric, int k, float* distances, int64_t* labels, void* workspace,
-                  size_t workspace_bytes) {
+                  const float* list_lo, const int64_t* list_ids, int64_t ntotal,
+                  const int32_t* list_order, int d, int metric, int k, float* distances,
+                  int64_t* labels, void* workspace, size_t workspace_bytes) {
   MF_ENTER(device);
   MF_TRY(check_common(d, metric, k, true));
   MF_CHECK(nlist >= 1, MF_ERR_INVALID_ARGS, "nlist=%d", nlist);
@@ -286,11 +311,17 @@ int mf_ivf_search(int device, void* stream, const float* xq, int64_t nq,
   MF_CHECK(c.fits(), MF_ERR_INVALID_ARGS, "IVF search workspace too small: %zu < %zu bytes",
            workspace_bytes, c.used);
   cudaStream_t s = (cudaStream_t)stream;
-  MF_TRY(run_flat_topk(device, s, xq, nq, centroids, centroid_norms, nlist, d,
+  const float* cent_lo = nullptr;
+  if (tc_eligible(coarse_metric(metric), d, P, nlist)) {
+    MF_TRY(launch_tf32_residual(centroids, nlist, d, w.cent_lo, s));
+    cent_lo = w.cent_lo;
+  }
+  MF_TRY(run_flat_topk(device, s, xq, nq, centroids, centroid_norms, cent_lo, nlist, d,
                        coarse_metric(metric), P, nullptr, w.coarse_d, w.coarse_l, w.flat_ws,
                        w.flat_bytes));
   return ivf_scan_topk(device, s, w, xq, nq, w.coarse_l, P, nlist, list_offsets, list_vecs,
-                       list_norms, list_ids, ntotal, list_order, d, metric, k, distances, labels);
+                       list_norms, list_lo, list_ids, ntotal, list_order, d, metric, k, distances,
+                       labels);
 }
 
 int mf_ivf_search_preassigned_workspace_size(int64_t nq, int nlist, int nprobe, int d,
@@ -308,10 +339,10 @@ int mf_ivf_search_preassigned_workspace_size(int64_t nq, int nlist, int nprobe, 
 int mf_ivf_search_preassigned(int device, void* stream, const float* xq, int64_t nq,
                               const int64_t* probes, int nprobe, int nlist,
                               const int64_t* list_offsets, const float* list_vecs,
-                              const float* list_norms, const int64_t* list_ids,
-                              int64_t ntotal, const int32_t* list_order, int d, int metric, int k,
-                              float* distances, int64_t* labels, void* workspace,
-                              size_t workspace_bytes) {
+                              const float* list_norms, const float* list_lo,
+                              const int64_t* list_ids, int64_t ntotal, const int32_t* list_order,
+                              int d, int metric, int k, float* distances, int64_t* labels,
+                              void* workspace, size_t workspace_bytes) {
   MF_ENTER(device);
   MF_TRY(check_common(d, metric, k, true));
   MF_CHECK(nlist >= 1 && nprobe >= 1, MF_ERR_INVALID_ARGS, "nlist=%d nprobe=%d", nlist, nprobe);
@@ -328,8 +359,8 @@ int mf_ivf_search_preassigned(int device, void* stream, const float* xq, int64_t
   MF_CHECK(c.fits(), MF_ERR_INVALID_ARGS, "workspace too small: %zu < %zu bytes",
            workspace_bytes, c.used);
   return ivf_scan_topk(device, (cudaStream_t)stream, w, xq, nq, probes, nprobe, nlist,
-                       list_offsets, list_vecs, list_norms, list_ids, ntotal, list_order, d,
-                       metric, k, distances, labels);
+                       list_offsets, list_vecs, list_norms, list_lo, list_ids, ntotal, list_order,
+                       d, metric, k, distances, labels);
 }
 
 int mf_topk_merge(int device, void* stream, const float* part_distances,
@@ -348,7 +379,9 @@ int mf_topk_merge(int device, void* stream, const float* part_distances,
 }
 
 int mf_kmeans_assign_workspace_size(int64_t n, int nc, int d, size_t* bytes) {
-  return mf_flat_search_workspace_size(n, nc, d, MF_METRIC_L2, 1, bytes);
+  MF_TRY(mf_flat_search_workspace_size(n, nc, d, MF_METRIC_L2, 1, bytes));
+  *bytes = ((*bytes + 255) & ~size_t(255)) + (size_t)nc * d * sizeof(float);
+  return MF_OK;
 }
 
 int mf_kmeans_assign(int device, void* stream, const float* x, int64_t n,
@@ -365,10 +398,20 @@ int mf_kmeans_assign(int device, void* stream, const float* x, int64_t n,
   MF_TRY(check_device_ptr(centroid_norms, "centroid_norms"));
   MF_TRY(check_device_ptr(labels, "labels"));
   MF_TRY(check_device_ptr(min_distances, "min_distances"));
-  MF_TRY(check_device_ptr(workspace, "workspace", true));
-  return run_flat_topk(device, (cudaStream_t)stream, x, n, centroids, centroid_norms, nc, d,
-                       MF_METRIC_L2, 1, nullptr, min_distances, labels, workspace,
-                       workspace_bytes);
+  MF_TRY(check_device_ptr(workspace, "workspace"));
+  cudaStream_t s = (cudaStream_t)stream;
+  const size_t flat_bytes = plan_flat(n, nc, d, 1, device).bytes;
+  const size_t lo_off = (flat_bytes + 255) & ~size_t(255);
+  MF_CHECK(workspace_bytes >= lo_off + (size_t)nc * d * sizeof(float), MF_ERR_INVALID_ARGS,
+           "k-means assign workspace too small");
+  float* cent_lo = reinterpret_cast<float*>(static_cast<char*>(workspace) + lo_off);
+  const float* lo = nullptr;
+  if (tc_eligible(MF_METRIC_L2, d, 1, nc)) {
+    MF_TRY(launch_tf32_residual(centroids, nc, d, cent_lo, s));
+    lo = cent_lo;
+  }
+  return run_flat_topk(device, s, x, n, centroids, centroid_norms, lo, nc, d, MF_METRIC_L2, 1,
+                       nullptr, min_distances, labels, workspace, flat_bytes);
 }
 
 int mf_kmeans_update_workspace_size(int64_t n, int nc, int d, size_t* bytes) {
@@ -623,12 +666,12 @@ int mf_ivf_range_count(int device, void* stream, const float* xq, int64_t nq,
   Carver c(workspace, workspace_bytes);
   IvfWs w = carve_ivf(c, nq, nlist, P, d, 1, 2, device);
   MF_CHECK(c.fits(), MF_ERR_INVALID_ARGS, "IVF range workspace too small");
-  MF_TRY(run_flat_topk(device, s, xq, nq, centroids, centroid_norms, nlist, d,
+  MF_TRY(run_flat_topk(device, s, xq, nq, centroids, centroid_norms, nullptr, nlist, d,
                        coarse_metric(metric), P, nullptr, w.coarse_d, w.coarse_l, w.flat_ws,
                        w.flat_bytes));
   if (metric == MF_METRIC_L2) MF_TRY(launch_norms(xq, nq, d, w.qn, s));
   MF_TRY(run_ivf_groups_ex(w.g, w.coarse_l, nq, P, nlist, list_offsets, nullptr, nullptr,
-                           nullptr, 0, w.pair_counts, s));
+                           nullptr, 0, w.pair_counts, kScanTQ, s));
   ScanArgs a = ivf_range_args(w, xq, nq, P, list_offsets, list_vecs, list_norms, d, radius);
   MF_TRY(launch_scan(a, metric, kEpiCount, nq * P, device, s));
   MF_TRY(launch_exclusive_scan_i64(w.pair_counts, nq * P, w.pair_offsets64, s));
@@ -663,6 +706,16 @@ int mf_ivf_range_fill(int device, void* stream, const float* xq, int64_t nq,
   a.out_d = distances;
   a.out_l = labels;
   return launch_scan(a, metric, kEpiFill, nq * P, device, (cudaStream_t)stream);
+}
+
+int mf_tf32_residual(int device, void* stream, const float* x, int64_t n, int d, float* lo) {
+  MF_ENTER(device);
+  MF_CHECK(n >= 0 && d > 0 && d % 4 == 0, MF_ERR_INVALID_ARGS, "bad shape n=%lld d=%d",
+           (long long)n, d);
+  if (n == 0) return MF_OK;
+  MF_TRY(check_device_ptr(x, "x"));
+  MF_TRY(check_device_ptr(lo, "lo"));
+  return launch_tf32_residual(x, n, d, lo, (cudaStream_t)stream);
 }
 
 int mf_set_scan_engine(int engine) {

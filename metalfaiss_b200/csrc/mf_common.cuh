@@ -89,6 +89,11 @@ __device__ __forceinline__ float ordered_to_float(unsigned int o) {
 __device__ __forceinline__ unsigned long long make_key(float dist, unsigned int idx) {
   return (static_cast<unsigned long long>(float_to_ordered(dist)) << 32) | idx;
 }
+// The largest key with distance <= d: every candidate at distance d passes a
+// `key < bound` test except the (impossible) index 0xffffffff.
+__device__ __forceinline__ unsigned long long bound_key(float d) {
+  return (d != d || d == __int_as_float(0x7f800000)) ? kEmptyKey : make_key(d, 0xffffffffu);
+}
 __device__ __forceinline__ float key_dist(unsigned long long key) {
   return ordered_to_float(static_cast<unsigned int>(key >> 32));
 }

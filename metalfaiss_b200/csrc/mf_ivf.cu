@@ -64,9 +64,12 @@ __global__ void __launch_bounds__(kScanBlock) exclusive_scan_kernel(const TI* in
 // --------------------------------------------------------------- grouping
 __global__ void ivf_count_kernel(const int64_t* __restrict__ probes, int64_t n, int nlist,
                                  const int64_t* __restrict__ list_offsets, int* counts,
-                                 float* pd, int64_t* pl, int k, int64_t* pair_counts) {
+                                 float* pd, int64_t* pl, int k, int64_t* pair_counts, int P,
+                                 int s0, int s1) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n) return;
+  const int slot = (int)(i % P);
+  if (slot < s0 || slot >= s1) return;
   const int64_t l = probes[i];
   const bool ok = l >= 0 && l < nlist && list_offsets[l + 1] > list_offsets[l];
   if (ok) {
@@ -86,7 +89,8 @@ __global__ void __launch_bounds__(kScanBlock) ivf_plan_kernel(const int* __restr
                                                              int nlist,
                                                              const int32_t* __restrict__ order,
                                                              int* pair_offsets, int2* items,
-                                                             int* item_total, int* cursors) {
+                                                             int* item_total, int* cursors,
+                                                             int group) {
   __shared__ int sums[32];
   const int chunk = (nlist + kScanBlock - 1) / kScanBlock;
   const int b = threadIdx.x * chunk;
@@ -104,13 +108,13 @@ __global__ void __launch_bounds__(kScanBlock) ivf_plan_kernel(const int* __restr
   s = 0;
   for (int i = b; i < e; ++i) {
     const int l = order ? order[i] : i;
-    s += (counts[l] + kScanTQ - 1) / kScanTQ;
+    s += (counts[l] + group - 1) / group;
   }
   int total_items;
   run = block_exclusive_scan<int>(s, sums, total_items);
   for (int i = b; i < e; ++i) {
     const int l = order ? order[i] : i;
-    const int ng = (counts[l] + kScanTQ - 1) / kScanTQ;
+    const int ng = (counts[l] + group - 1) / group;
     for (int g = 0; g < ng; ++g) items[run++] = make_int2(l, g);
   }
   if (threadIdx.x == 0) *item_total = total_items;
@@ -119,9 +123,11 @@ __global__ void __launch_bounds__(kScanBlock) ivf_plan_kernel(const int* __restr
 __global__ void ivf_scatter_kernel(const int64_t* __restrict__ probes, int64_t n, int nlist,
                                    const int64_t* __restrict__ list_offsets,
                                    const int* __restrict__ pair_offsets, int* cursors,
-                                   int* pairs) {
+                                   int* pairs, int P, int s0, int s1) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n) return;
+  const int slot = (int)(i % P);
+  if (slot < s0 || slot >= s1) return;
   const int64_t l = probes[i];
   if (l >= 0 && l < nlist && list_offsets[l + 1] > list_offsets[l]) {
     const int pos = pair_offsets[l] + atomicAdd(&cursors[l], 1);
@@ -332,30 +338,33 @@ IvfGroups carve_ivf_groups(Carver& c, int64_t nq, int nlist, int P) {
 
 int run_ivf_groups_ex(const IvfGroups& g, const int64_t* probes, int64_t nq, int P, int nlist,
                       const int64_t* list_offsets, const int32_t* list_order, float* pd,
-                      int64_t* pl, int k, int64_t* pair_counts, cudaStream_t stream) {
+                      int64_t* pl, int k, int64_t* pair_counts, int group, cudaStream_t stream,
+                      int s0, int s1) {
+  if (s1 < 0) s1 = P;
   const int64_t n = nq * P;
   ScopedTiming tm("ivf_group", stream);
   MF_CUDA(cudaMemsetAsync(g.counts, 0, sizeof(int) * nlist, stream));
   if (n > 0) {
     ivf_count_kernel<<<(unsigned int)ceil_div(n, 256), 256, 0, stream>>>(
-        probes, n, nlist, list_offsets, g.counts, pd, pl, k, pair_counts);
+        probes, n, nlist, list_offsets, g.counts, pd, pl, k, pair_counts, P, s0, s1);
     MF_LAUNCH_CHECK();
   }
   ivf_plan_kernel<<<1, kScanBlock, 0, stream>>>(g.counts, nlist, list_order, g.pair_offsets,
-                                                g.items, g.item_total, g.cursors);
+                                                g.items, g.item_total, g.cursors, group);
   MF_LAUNCH_CHECK();
   if (n > 0) {
     ivf_scatter_kernel<<<(unsigned int)ceil_div(n, 256), 256, 0, stream>>>(
-        probes, n, nlist, list_offsets, g.pair_offsets, g.cursors, g.pairs);
+        probes, n, nlist, list_offsets, g.pair_offsets, g.cursors, g.pairs, P, s0, s1);
     MF_LAUNCH_CHECK();
   }
   return MF_OK;
 }
 
 int run_ivf_groups(const IvfGroups& g, const int64_t* probes, int64_t nq, int P, int nlist,
-                   const int64_t* list_offsets, const int32_t* list_order, cudaStream_t stream) {
+                   const int64_t* list_offsets, const int32_t* list_order, int group,
+                   cudaStream_t stream) {
   return run_ivf_groups_ex(g, probes, nq, P, nlist, list_offsets, list_order, nullptr, nullptr,
-                           0, nullptr, stream);
+                           0, nullptr, group, stream);
 }
 
 // ---- radix sort of (label, row) pairs by label, stable

@@ -10,10 +10,12 @@ int launch_lims(const int64_t* offsets, int64_t nq, int P, int64_t* lims, cudaSt
 int launch_iota_i32(int32_t* out, int64_t n, cudaStream_t stream);
 
 // Grouping that also pre-fills the partial slots (pd/pl, k per slot) or the
-// per-pair range counts of pairs whose list is empty or out of range.
+// per-pair range counts of pairs whose list is empty or out of range. Only
+// probe slots in [s0, s1) take part (s1 < 0: all).
 int run_ivf_groups_ex(const IvfGroups& g, const int64_t* probes, int64_t nq, int P, int nlist,
                       const int64_t* list_offsets, const int32_t* list_order, float* pd,
-                      int64_t* pl, int k, int64_t* pair_counts, cudaStream_t stream);
+                      int64_t* pl, int k, int64_t* pair_counts, int group, cudaStream_t stream,
+                      int s0 = 0, int s1 = -1);
 
 size_t radix_sort_bytes(int64_t n);
 

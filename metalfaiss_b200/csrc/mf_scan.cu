@@ -136,8 +136,12 @@ __global__ void __launch_bounds__(kScanThreads) scan_kernel(const ScanArgs a) {
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       run[j] = (EPI == kEpiFill) ? s_off[warp * 4 + j] : 0;
-      if (EPI == kEpiTopK)
-        tk[j].init(lists + (warp * 4 + j) * KCAP, bufs + (warp * 4 + j) * 32, k, lane);
+      if (EPI == kEpiTopK) {
+        unsigned long long bnd = kEmptyKey;
+        const int qr = s_qrow[warp * 4 + j];
+        if (a.bound_pd && qr >= 0) bnd = bound_key(a.bound_pd[((long long)qr * a.P) * k + k - 1]);
+        tk[j].init(lists + (warp * 4 + j) * KCAP, bufs + (warp * 4 + j) * 32, k, lane, bnd);
+      }
     }
 
     auto load_stage = [&](int it, int stage) {
@@ -397,8 +401,6 @@ int scan_kcap(int k) {
 
 int launch_scan(const ScanArgs& a, int metric, int epi, int64_t total_items, int device,
                 cudaStream_t stream) {
-  if (epi == kEpiTopK && a.xb_rows > 0 && tc_eligible(metric, a.d, a.k, a.xb_rows))
-    return launch_tc_scan(a, metric, total_items, a.xb_rows, device, stream);
   const int kcap = epi == kEpiTopK ? scan_kcap(a.k) : 32;
   MF_CHECK(kcap != 0, MF_ERR_INVALID_ARGS, "k=%d exceeds the supported maximum %d", a.k, kMaxK);
   ScanFn fn = pick_scan(metric, epi, kcap);
@@ -453,14 +455,14 @@ int launch_merge(const float* pd, const int64_t* pl, int64_t nq, int parts, int 
 }
 
 // ------------------------------------------------------------- flat search
-FlatPlan plan_flat(int64_t nq, int64_t nb, int d, int k, int device) {
-  (void)d;
-  FlatPlan p;
-  p.nqt = (int)ceil_div(nq, kScanTQ);
-  const int kcap = scan_kcap(k) ? scan_kcap(k) : 256;
-  // Aim for about two waves of resident CTAs; each split keeps >= 1 tile.
-  const int per_sm = kcap >= 256 ? 1 : (kcap >= 128 ? 2 : 3);
-  const long long target = 2ll * (device >= 0 ? num_sms(device) : 148) * per_sm;
+namespace {
+void plan_splits(FlatPlan& p, int64_t nq, int64_t nb, int k, int device, int tq, int per_sm) {
+  p.nqt = (int)ceil_div(nq, tq);
+  // SIMT: about two waves of resident CTAs (per_sm CTAs per SM); tensor
+  // cores (per_sm = 0): about one item per SM, since every split restarts the
+  // top-k lists. Each split keeps >= 1 tile.
+  const long long sms = device >= 0 ? num_sms(device) : 148;
+  const long long target = per_sm > 0 ? 2ll * sms * per_sm : sms;
   long long s = ceil_div(target, p.nqt > 0 ? p.nqt : 1);
   const long long max_s = nb > 0 ? ceil_div(nb, kScanTR) : 1;
   if (s > max_s) s = max_s;
@@ -470,32 +472,48 @@ FlatPlan plan_flat(int64_t nq, int64_t nb, int d, int k, int device) {
   s = ceil_div(nb > 0 ? nb : 1, rps);
   p.splits = (int)s;
   p.rows_per_split = rps;
-  Carver c(nullptr, 0);
-  c.take<float>(nq);     // query norms
-  c.take<int>(1);        // work counter
-  if (p.splits > 1) {
-    c.take<float>((size_t)nq * p.splits * k);
-    c.take<int64_t>((size_t)nq * p.splits * k);
+  (void)k;
+}
+}  // namespace
+
+FlatPlan plan_flat(int64_t nq, int64_t nb, int d, int k, int device, int tq) {
+  FlatPlan p;
+  const int kcap = scan_kcap(k) ? scan_kcap(k) : 256;
+  if (tq == 32) {
+    plan_splits(p, nq, nb, k, device, 32, kcap >= 256 ? 1 : (kcap >= 128 ? 2 : 3));
+  } else {
+    plan_splits(p, nq, nb, k, device, tq, 0);
   }
+  // workspace: the larger of the two engines' needs
+  FlatPlan other;
+  plan_splits(other, nq, nb, k, device, tq == 32 ? tc_group() : 32, 1);
+  const int max_splits = p.splits > other.splits ? p.splits : other.splits;
+  Carver c(nullptr, 0);
+  c.take<float>(nq);                        // query norms
+  c.take<int>(1);                           // work counter
+  c.take<float>((size_t)nq * max_splits * k);
+  c.take<int64_t>((size_t)nq * max_splits * k);
+  c.take<float>((size_t)nq * d);            // query tf32 residuals (tensor cores)
   p.bytes = c.used;
   return p;
 }
 
 int run_flat_topk(int device, cudaStream_t stream, const float* xq, int64_t nq, const float* xb,
-                  const float* xb_norms, int64_t nb, int d, int metric, int k,
+                  const float* xb_norms, const float* xb_lo, int64_t nb, int d, int metric, int k,
                   const int64_t* ids, float* D, int64_t* I, void* ws, size_t ws_bytes) {
-  const FlatPlan p = plan_flat(nq, nb, d, k, device);
+  const bool tc = xb_lo != nullptr && tc_eligible(metric, d, k, nb);
+  const FlatPlan p = plan_flat(nq, nb, d, k, device, tc ? tc_group() : 32);
   MF_CHECK(ws_bytes >= p.bytes, MF_ERR_INVALID_ARGS,
            "flat search workspace too small: %zu < %zu bytes", ws_bytes, p.bytes);
+  // carve with the same order as plan_flat (partials sized for either engine)
+  FlatPlan other = plan_flat(nq, nb, d, k, device, tc ? 32 : tc_group());
+  const int max_splits = p.splits > other.splits ? p.splits : other.splits;
   Carver c(ws, ws_bytes);
   float* qn = c.take<float>(nq);
   int* counter = c.take<int>(1);
-  float* pd = nullptr;
-  int64_t* pl = nullptr;
-  if (p.splits > 1) {
-    pd = c.take<float>((size_t)nq * p.splits * k);
-    pl = c.take<int64_t>((size_t)nq * p.splits * k);
-  }
+  float* pd = c.take<float>((size_t)nq * max_splits * k);
+  int64_t* pl = c.take<int64_t>((size_t)nq * max_splits * k);
+  float* q_lo = c.take<float>((size_t)nq * d);
   if (metric == MF_METRIC_L2) MF_TRY(launch_norms(xq, nq, d, qn, stream));
   ScanArgs a{};
   a.xq = xq;
@@ -511,12 +529,17 @@ int run_flat_topk(int device, cudaStream_t stream, const float* xq, int64_t nq, 
   a.nqt = p.nqt;
   a.nb = nb;
   a.rows_per_split = p.rows_per_split;
-  a.xb_rows = nb;
   a.counter = counter;
   a.direct = p.splits > 1 ? 0 : 1;
   a.out_d = p.splits > 1 ? pd : D;
   a.out_l = p.splits > 1 ? pl : I;
-  MF_TRY(launch_scan(a, metric, kEpiTopK, (int64_t)p.nqt * p.splits, device, stream));
+  if (tc) {
+    MF_TRY(launch_tf32_residual(xq, nq, d, q_lo, stream));
+    MF_TRY(launch_tc_scan(a, metric, q_lo, nq, xb_lo, nb, (int64_t)p.nqt * p.splits, device,
+                          stream));
+  } else {
+    MF_TRY(launch_scan(a, metric, kEpiTopK, (int64_t)p.nqt * p.splits, device, stream));
+  }
   if (p.splits > 1) {
     MF_TRY(launch_merge(pd, pl, nq, p.splits, k, k, D, I, stream));
     // Row positions are the merge's tie-break, so ids are mapped last.

@@ -48,17 +48,26 @@ struct ScanArgs {
   float* out_d;
   int64_t* out_l;
   int direct;
+  // IVF second phase: bound_pd[(q*P)*k + k-1] (the k-th distance of query q's
+  // nearest list) bounds every other list's candidates; null = no bound.
+  const float* bound_pd;
   // range search
   float radius;
   int64_t* counts;        // count pass: (nq*P)
   const int64_t* offsets; // fill pass: exclusive scan of counts (nq*P)
-  int64_t xb_rows;        // rows addressable in xb (tensor-map extent)
 };
 
-// Tensor-core engine (mf_tc.cu) for the L2 / inner-product top-k scans.
+// Tensor-core engine (mf_tc.cu) for the L2 / inner-product top-k scans: items
+// of tc_group() queries; a.xq / a.xb are the fp32 (hi) operands, a_lo / b_lo
+// their tf32 residuals, a_rows / b_rows their row counts.
 bool tc_eligible(int metric, int d, int k, int64_t xb_rows);
-int launch_tc_scan(const ScanArgs& a, int metric, int64_t total_items, int64_t xb_rows, int device,
+int tc_group();
+int launch_tc_scan(const ScanArgs& a, int metric, const float* a_lo, int64_t a_rows,
+                   const float* b_lo, int64_t b_rows, int64_t total_items, int device,
                    cudaStream_t stream);
+int launch_tf32_residual(const float* x, int64_t n, int d, float* lo, cudaStream_t stream);
+int launch_gather_queries(const float* xq, int d, const int* pairs, const int* n_pairs,
+                          int64_t max_pairs, int P, float* g_hi, float* g_lo, cudaStream_t stream);
 void set_scan_engine(int engine);
 int scan_engine();
 int read_device_error(int* code);
@@ -89,11 +98,14 @@ struct FlatPlan {
   int64_t rows_per_split;
   size_t bytes;
 };
-FlatPlan plan_flat(int64_t nq, int64_t nb, int d, int k, int device);
+// tq = queries per item (32 for the SIMT scan, tc_group() for tensor cores);
+// bytes covers both engines.
+FlatPlan plan_flat(int64_t nq, int64_t nb, int d, int k, int device, int tq = 32);
 
-// Runs flat top-k into (nq, k) outputs using the given workspace.
+// Runs flat top-k into (nq, k) outputs using the given workspace. With xb_lo
+// (the tf32 residual of xb) the tensor-core engine runs where eligible.
 int run_flat_topk(int device, cudaStream_t stream, const float* xq, int64_t nq, const float* xb,
-                  const float* xb_norms, int64_t nb, int d, int metric, int k,
+                  const float* xb_norms, const float* xb_lo, int64_t nb, int d, int metric, int k,
                   const int64_t* ids, float* D, int64_t* I, void* ws, size_t ws_bytes);
 
 // IVF list grouping: probes (nq, P) -> pairs grouped by list and items.
@@ -109,7 +121,8 @@ struct IvfGroups {
 size_t ivf_groups_bytes(int64_t nq, int nlist, int P);
 IvfGroups carve_ivf_groups(Carver& c, int64_t nq, int nlist, int P);
 int run_ivf_groups(const IvfGroups& g, const int64_t* probes, int64_t nq, int P, int nlist,
-                   const int64_t* list_offsets, const int32_t* list_order, cudaStream_t stream);
+                   const int64_t* list_offsets, const int32_t* list_order, int group,
+                   cudaStream_t stream);
 
 // Exclusive scan of n int64 counts into out (n+1 entries; out[n] = total).
 int launch_exclusive_scan_i64(const int64_t* in, int64_t n, int64_t* out, cudaStream_t stream);

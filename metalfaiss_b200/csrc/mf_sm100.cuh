@@ -11,9 +11,12 @@ namespace mf {
 namespace sm100 {
 
 constexpr int kErrWaitTimeout = 1;
-// try_wait suspends for a hardware time slice per call; this bound turns a
-// lost arrival into an error after seconds instead of a hang.
-constexpr unsigned kWaitLimit = 1u << 22;
+// Each try_wait suspends the thread until the phase completes or the hint
+// (kWaitHintNs) expires, so a waiting thread does not spin on the shared
+// memory pipe; the iteration bound turns a lost arrival into an error after
+// about kWaitLimit * kWaitHintNs (~2.5 s) instead of a hang.
+constexpr unsigned kWaitHintNs = 10000000u;
+constexpr unsigned kWaitLimit = 256;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -35,10 +38,10 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(kWaitHintNs)
       : "memory");
   return ok != 0;
 }

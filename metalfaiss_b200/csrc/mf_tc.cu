@@ -1,20 +1,26 @@
-// Tensor-core slab scan (sm_100a): the L2 / inner-product distance tile of a
-// work item (<= 32 queries x a slab of rows) computed by tcgen05 MMAs in
-// 3xTF32 form with the accumulator in TMEM, fed to the same per-query warp
-// top-k as the SIMT scan. Work items and outputs are exactly those of
-// scan_kernel (mf_scan.cu), so either engine serves flat and IVF search.
+// Tensor-core slab scan (sm_100a): L2 / inner-product top-k of a work item
+// (<= 128 queries x a slab of rows) with the distance tile computed by tcgen05
+// MMAs in 3xTF32 form, accumulators in TMEM, and a per-query top-k in the
+// epilogue. Work items and outputs follow scan_kernel (mf_scan.cu), with
+// query groups of 128.
 //
-// Per CTA (128 threads, one CTA per SM, persistent over work items):
-//  * queries: gathered once per item, split into tf32 hi/lo and written as the
-//    K-major B operand (N = 32 rows of 128-byte swizzled K-blocks);
-//  * rows: 128-row x 32-float boxes stream in by TMA (128B swizzle, no
-//    multicast) through a ring of SA stages, one stage per K-block;
-//  * every stage is split in place (hi) plus a lo copy, then one thread issues
-//    12 MMAs (4 K-steps x {hi.hi, hi.lo, lo.hi}) into one of two TMEM
-//    accumulators (128 lanes x 32 columns each);
-//  * the epilogue of tile t-1 (TMEM -> registers -> distances -> transposed
-//    shared tile -> warp top-k) runs while tile t's MMAs execute.
-// x.q = xh.qh + xh.ql + xl.qh, dropping xl.ql (relative size ~2^-22).
+// Operands (K-major, 128-byte swizzle, loaded by TMA without multicast):
+//   A = the item's 128 queries (M = 128), B = a tile of BN database rows (N).
+// The tensor core reads fp32 operands as tf32 by dropping the 13 low mantissa
+// bits (truncation, checked on B200), so the raw fp32 arrays serve as the hi
+// parts; the lo parts (x - trunc_tf32(x)) are precomputed: once per add for
+// the database, once per search for the queries. Per K-step of 8:
+//   D += A.B  +  A.B_lo  +  A_lo.B      (the dropped A_lo.B_lo term is ~2^-22)
+//
+// Warp roles (192 threads, one CTA per SM, items assigned round-robin):
+//   warps 0-3  epilogue: thread t owns query row t of the tile (TMEM lane t),
+//              reads its BN dot products, forms distances and keeps a sorted
+//              per-thread top-k list in shared memory;
+//   warp 4     TMA producer (one lane);
+//   warp 5     TMEM allocation and MMA issue (one lane).
+// Stages flow full -> MMA -> empty; accumulators flow accf -> epilogue -> acce,
+// two of each so the epilogue of tile t overlaps the MMAs of tile t+1. Every
+// wait is bounded (mf_sm100.cuh).
 #include <cudaTypedefs.h>
 
 #include <mutex>
@@ -29,423 +35,413 @@ namespace {
 // Set by a kernel whose bounded wait gave up; read (and cleared) by
 // mf_device_error(). Never set on the normal path.
 __device__ int g_device_error = 0;
-}  // namespace
-
-namespace {
-using namespace sm100;
 
 #ifdef MF_TC_PROFILE
-// Phase cycle counters of the tensor-core scan (instrumented builds only).
+// Per-role cycle counters (instrumented builds only).
 __device__ unsigned long long g_tc_prof[16];
-#define TCP_DECL unsigned long long _tcp[16] = {0}; long long _tc0 = 0;
-#define TCP_BEGIN() _tc0 = clock64()
-#define TCP_END(i) _tcp[i] += (unsigned long long)(clock64() - _tc0)
-#define TCP_FLUSH()                                                                  \
-  if (tid == 0 || tid == 64)                                                         \
-    for (int _i = 0; _i < 16; ++_i) atomicAdd(&g_tc_prof[_i], _tcp[_i]);
+#define TQP(i, expr)                                       \
+  do {                                                     \
+    const long long _t0 = clock64();                       \
+    expr;                                                  \
+    atomicAdd(&g_tc_prof[i], (unsigned long long)(clock64() - _t0)); \
+  } while (0)
 #else
-#define TCP_DECL
-#define TCP_BEGIN()
-#define TCP_END(i)
-#define TCP_FLUSH()
+#define TQP(i, expr) expr
 #endif
 
-constexpr int kTcThreads = 256;
-constexpr int kTcM = 128;                 // rows per tile (TMEM lanes)
-constexpr int kTcN = 32;                  // queries per item (accumulator columns)
-constexpr int kTcStageBytes = kTcM * 128;  // one 128 x 32 fp32 box
-constexpr int kTcBBlockBytes = kTcN * 128;
-constexpr int kTcMaxD = 256;
-constexpr int kTcMaxSmem = 227 * 1024 - 256;  // dynamic part; static smem takes the rest
+using namespace sm100;
 
-struct TcSmem {
-  int SA;  // A stages
-  int KB;  // K-blocks
-  size_t a, l, bh, bl, t, lists, bufs, qout, qrow, qn, bars, total;
+constexpr int kTqThreads = 192;
+constexpr int kTqM = 128;          // queries per item = TMEM lanes
+constexpr int kTqEpiThreads = 128;
+constexpr int kTqMaxD = 1024;
+constexpr int kTqK = 32;  // list slots per query row (k <= 32)
+constexpr int kTqMaxSmem = 227 * 1024 - 512;
+
+struct TqLayout {
+  int SA, KB, BN;
+  size_t stage, a_hi, a_lo, b_hi, b_lo;  // offsets within a stage
+  size_t lists, scratch, xn, bars, total;
 };
 
-TcSmem tc_layout(int d, int kcap, int SA) {
-  TcSmem s;
+TqLayout tq_layout(int d, int kcap, int BN, int SA) {
+  TqLayout s;
   s.SA = SA;
   s.KB = (d + 31) / 32;
-  size_t o = 0;
-  s.a = o;
-  o += size_t(SA) * kTcStageBytes;
-  s.l = o;
-  o += size_t(2) * kTcStageBytes;
-  s.bh = o;
-  o += size_t(s.KB) * kTcBBlockBytes;
-  s.bl = o;
-  o += size_t(s.KB) * kTcBBlockBytes;
-  s.t = o;
-  o += size_t(kTcN) * kTcM * 4;
+  s.BN = BN;
+  s.a_hi = 0;
+  s.a_lo = kTqM * 128;
+  s.b_hi = 2 * kTqM * 128;
+  s.b_lo = s.b_hi + size_t(BN) * 128;
+  s.stage = s.b_lo + size_t(BN) * 128;
+  size_t o = size_t(SA) * s.stage;
   s.lists = o;
-  o += size_t(kTcN) * kcap * 8;
-  s.bufs = o;
-  o += size_t(kTcN) * 32 * 8;
-  s.qout = o;
-  o += kTcN * 8;
-  s.qrow = o;
-  o += kTcN * 4;
-  s.qn = o;
-  o += kTcN * 4;
+  o += size_t(kTqM) * kcap * 8;
+  s.scratch = o;  // candidate buffers: 128 rows x 33 keys (one row per query row)
+  o += size_t(kTqM) * 33 * 8;
+  s.xn = o;
+  o += size_t(2) * BN * 4;
   s.bars = o;
-  o += size_t(2 * SA + 2) * 8 + 16;
-  s.total = o + 1024;  // slack to align the base to 1024 bytes
+  o += size_t(2 * SA + 4) * 8 + 16;
+  s.total = o + 1024;
   return s;
 }
 
-template <int METRIC, int KCAP>
-__global__ void __launch_bounds__(kTcThreads, 1)
-    tc_scan_kernel(const ScanArgs a, const __grid_constant__ CUtensorMap tmap, const TcSmem L) {
+struct TqMaps {
+  CUtensorMap a_hi, a_lo, b_hi, b_lo;
+};
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void named_sync(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
+// Item geometry; every role reads it for itself.
+struct ItemDesc {
+  long long rb, re;  // row slab
+  int a_row0;        // first A row (queries) in the A tensor map
+  int nq_item;       // valid queries (A rows) of this item
+};
+
+__device__ __forceinline__ ItemDesc item_desc(const ScanArgs& a, int item) {
+  ItemDesc it;
+  if (a.flat) {
+    const int qt = item % a.nqt;
+    const int s = item / a.nqt;
+    it.a_row0 = qt * kTqM;
+    const long long rem = a.nq - (long long)it.a_row0;
+    it.nq_item = (int)(rem < kTqM ? rem : kTqM);
+    it.rb = (long long)s * a.rows_per_split;
+    const long long re = it.rb + a.rows_per_split;
+    it.re = re < a.nb ? re : a.nb;
+  } else {
+    const int2 g = a.items[item];
+    const int pb = a.pair_offsets[g.x] + g.y * kTqM;
+    const int pe0 = a.pair_offsets[g.x + 1];
+    it.a_row0 = pb;
+    it.nq_item = (pe0 - pb) < kTqM ? (pe0 - pb) : kTqM;
+    it.rb = a.list_offsets[g.x];
+    it.re = a.list_offsets[g.x + 1];
+  }
+  return it;
+}
+
+template <int METRIC, int BN>
+__global__ void __launch_bounds__(kTqThreads, 1)
+    tq_scan_kernel(const ScanArgs a, const __grid_constant__ TqMaps maps, const TqLayout L) {
   extern __shared__ unsigned char smem_raw[];
   unsigned char* base = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  float* A = reinterpret_cast<float*>(base + L.a);
-  float* Lo = reinterpret_cast<float*>(base + L.l);
-  float* Bh = reinterpret_cast<float*>(base + L.bh);
-  float* Bl = reinterpret_cast<float*>(base + L.bl);
-  float* T = reinterpret_cast<float*>(base + L.t);
   unsigned long long* lists = reinterpret_cast<unsigned long long*>(base + L.lists);
-  unsigned long long* bufs = reinterpret_cast<unsigned long long*>(base + L.bufs);
-  long long* s_qout = reinterpret_cast<long long*>(base + L.qout);
-  int* s_qrow = reinterpret_cast<int*>(base + L.qrow);
-  float* s_qn = reinterpret_cast<float*>(base + L.qn);
+  float* xn_s = reinterpret_cast<float*>(base + L.xn);
+  unsigned long long* cbuf = reinterpret_cast<unsigned long long*>(base + L.scratch);
   uint64_t* full = reinterpret_cast<uint64_t*>(base + L.bars);
-  uint64_t* mdone = full + L.SA;
-  uint64_t* accf = mdone + L.SA;
-  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(accf + 2);
+  uint64_t* empty = full + L.SA;
+  uint64_t* accf = empty + L.SA;
+  uint64_t* acce = accf + 2;
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(acce + 2);
   int* s_abort = reinterpret_cast<int*>(s_tmem + 1);
-
-  __shared__ int s_item;
-  __shared__ long long s_rb, s_re;
+  uint32_t* s_seq = reinterpret_cast<uint32_t*>(s_abort + 1);  // [0] consumed, [1] issued
 
   const int tid = threadIdx.x;
-  const int lane = tid & 31;
   const int warp = tid >> 5;
-  const int quad = warp & 3;   // TMEM lane quadrant this warp may access
-  const int half = warp >> 2;  // which 16 of the 32 query columns it reads
-  const int d = a.d;
-  const int k = a.k;
+  const int lane = tid & 31;
   const int SA = L.SA;
   const int KB = L.KB;
+  const int k = a.k;
+  const int total = a.flat ? a.nqt * a.P : *a.item_total;
+  constexpr uint32_t kStageTx = 2 * kTqM * 128 + 2 * BN * 128;
 
-  if (warp == 0) {
-    tmem_alloc(s_tmem, 64);
+#ifdef MF_TC_PROFILE
+  const long long _tk = clock64();
+#endif
+  if (warp == 5) {
+    tmem_alloc(s_tmem, 2 * BN);
     tmem_relinquish();
   }
   if (tid == 0) {
     for (int i = 0; i < SA; ++i) {
       mbar_init(&full[i], 1);
-      mbar_init(&mdone[i], 1);
+      mbar_init(&empty[i], 1);
     }
-    mbar_init(&accf[0], 1);
-    mbar_init(&accf[1], 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&accf[i], 1);
+      mbar_init(&acce[i], kTqEpiThreads);
+    }
     *s_abort = 0;
+    s_seq[0] = 0;
+    s_seq[1] = 0;
     fence_mbar_init();
-    prefetch_tensormap(&tmap);
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *s_tmem;
-  constexpr uint32_t idesc = idesc_tf32(kTcM, kTcN);
 
-  TCP_DECL
+  if (warp == 4) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      prefetch_tensormap(&maps.a_hi);
+      prefetch_tensormap(&maps.a_lo);
+      prefetch_tensormap(&maps.b_hi);
+      prefetch_tensormap(&maps.b_lo);
+      uint32_t seq = 0;
+      for (int item = blockIdx.x; item < total && !*s_abort; item += gridDim.x) {
+        const ItemDesc it = item_desc(a, item);
+        const long long nrows = it.re > it.rb ? it.re - it.rb : 0;
+        const int nT = (int)((nrows + BN - 1) / BN);
+        for (int t = 0; t < nT && !*s_abort; ++t) {
+          for (int kb = 0; kb < KB; ++kb) {
+            const int s = seq % SA;
+            bool ok = true;
+            if (seq >= (uint32_t)SA)
+              TQP(0, ok = mbar_wait(&empty[s], ((seq / SA) - 1) & 1, s_abort, &g_device_error));
+            if (!ok) break;
+            unsigned char* st = base + size_t(s) * L.stage;
+            mbar_arrive_expect_tx(&full[s], kStageTx);
+            const int x = kb * 32;
+            const int yb = (int)(it.rb + (long long)t * BN);
+            tma_load_2d(st + L.a_hi, &maps.a_hi, x, it.a_row0, &full[s]);
+            tma_load_2d(st + L.a_lo, &maps.a_lo, x, it.a_row0, &full[s]);
+            tma_load_2d(st + L.b_hi, &maps.b_hi, x, yb, &full[s]);
+            tma_load_2d(st + L.b_lo, &maps.b_lo, x, yb, &full[s]);
+            ++seq;
+          }
+        }
+      }
+      s_seq[1] = seq;
+    }
+  } else if (warp == 5) {
+    // ---------------------------------------------------------------- MMA
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_tf32(kTqM, BN);
+      uint32_t seq = 0, tt = 0;
+      for (int item = blockIdx.x; item < total && !*s_abort; item += gridDim.x) {
+        const ItemDesc it = item_desc(a, item);
+        const long long nrows = it.re > it.rb ? it.re - it.rb : 0;
+        const int nT = (int)((nrows + BN - 1) / BN);
+        for (int t = 0; t < nT; ++t, ++tt) {
+          const int b = tt & 1;
+          if (tt >= 2) TQP(1, mbar_wait(&acce[b], ((tt >> 1) - 1) & 1, s_abort, &g_device_error));
+          tc_fence_after();
+          const uint32_t dt = tmem + b * BN;
+          for (int kb = 0; kb < KB; ++kb, ++seq) {
+            const int s = seq % SA;
+            TQP(2, mbar_wait(&full[s], (seq / SA) & 1, s_abort, &g_device_error));
+            tc_fence_after();
+            const uint32_t st = smem_u32(base + size_t(s) * L.stage);
 #ifdef MF_TC_PROFILE
-  const long long _t_start = clock64();
+            const long long _tm = clock64();
 #endif
-  uint32_t g = 0;         // A-stage sequence consumed so far (same in every thread)
-  uint32_t g_issued = 0;  // A-stage sequence issued (thread 0)
-  uint32_t tt = 0;        // tiles so far
-  int next_load = 0;      // next K-block of the current item to load (thread 0)
-
-  // Thread 0: issues the loads of the current item below `upto`; when `block`
-  // is false it stops at the first stage whose previous MMAs are still running.
-  auto pump = [&](int upto, bool block, long long rb, int nL) {
-    if (upto > nL) upto = nL;
-    while (next_load < upto) {
-      const uint32_t seq = g + next_load;
-      const int s = seq % SA;
-      if (seq >= (uint32_t)SA) {
-        const uint32_t par = ((seq / SA) - 1) & 1;
-        if (block) mbar_wait(&mdone[s], par, s_abort, &g_device_error);
-        else if (!mbar_test(&mdone[s], par)) break;
-      }
-      const int t = next_load / KB;
-      const int kb = next_load - t * KB;
-      mbar_arrive_expect_tx(&full[s], kTcStageBytes);
-      tma_load_2d(A + size_t(s) * (kTcStageBytes / 4), &tmap, kb * 32,
-                  (int)(rb + (long long)t * kTcM), &full[s]);
-      g_issued = seq + 1;
-      ++next_load;
-    }
-  };
-
-  for (;;) {
-    TCP_BEGIN();
-    if (tid == 0) s_item = atomicAdd(a.counter, 1);
-    __syncthreads();
-    const int item = s_item;
-    const int total = a.flat ? a.nqt * a.P : *a.item_total;
-    if (item >= total || *s_abort) break;
-
-    // ---- the work item: queries, output slots, row slab (as scan_kernel)
-    if (a.flat) {
-      const int qt = item % a.nqt;
-      const int s = item / a.nqt;
-      if (tid < kTcN) {
-        long long q = (long long)qt * kTcN + tid;
-        bool v = q < a.nq;
-        s_qrow[tid] = v ? (int)q : -1;
-        s_qout[tid] = v ? (a.direct ? q : q * a.P + s) : -1;
-      }
-      if (tid == 0) {
-        long long rb = (long long)s * a.rows_per_split;
-        long long re = rb + a.rows_per_split;
-        s_rb = rb;
-        s_re = re < a.nb ? re : a.nb;
-      }
-    } else {
-      const int2 it = a.items[item];
-      const int pb = a.pair_offsets[it.x] + it.y * kTcN;
-      const int pe0 = a.pair_offsets[it.x + 1];
-      const int pe = pe0 < pb + kTcN ? pe0 : pb + kTcN;
-      if (tid < kTcN) {
-        int p = pb + tid;
-        if (p < pe) {
-          int pr = a.pairs[p];
-          s_qrow[tid] = pr / a.P;
-          s_qout[tid] = pr;
-        } else {
-          s_qrow[tid] = -1;
-          s_qout[tid] = -1;
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+              const uint32_t off = kk * 32;  // 8 tf32 of K per MMA
+              const uint64_t ah = desc_k_sw128(st + L.a_hi + off);
+              const uint64_t al = desc_k_sw128(st + L.a_lo + off);
+              const uint64_t bh = desc_k_sw128(st + L.b_hi + off);
+              const uint64_t bl = desc_k_sw128(st + L.b_lo + off);
+              mma_tf32(dt, ah, bh, idesc, !(kb == 0 && kk == 0));
+              mma_tf32(dt, ah, bl, idesc, true);
+              mma_tf32(dt, al, bh, idesc, true);
+            }
+            mma_commit(&empty[s]);
+#ifdef MF_TC_PROFILE
+            atomicAdd(&g_tc_prof[8], (unsigned long long)(clock64() - _tm));
+#endif
+          }
+          mma_commit(&accf[b]);
         }
       }
-      if (tid == 0) {
-        s_rb = a.list_offsets[it.x];
-        s_re = a.list_offsets[it.x + 1];
+      s_seq[0] = seq;
+    }
+  } else {
+    // ----------------------------------------------------------- epilogue
+    // Lane l of epilogue warp w owns query row 32w+l: it reads that row of the
+    // accumulator, filters the distances against the row's k-th best key
+    // (thr, a register) and appends survivors to the row's 32-slot candidate
+    // buffer. A full buffer is sorted and merged by the whole warp into the
+    // row's top-k list (sorted, one key per lane, in shared memory).
+    uint32_t tt = 0;
+    unsigned long long* my_lists = lists + (size_t)(warp * 32) * kTqK;
+    unsigned long long* my_bufs = cbuf + (size_t)(warp * 32) * 33;
+    unsigned long long* own_buf = my_bufs + lane * 33;
+    // Warp merge of row src's buffered candidates (count n) into its list.
+    auto merge_row = [&](int src, int n, unsigned long long& thr_reg, unsigned long long bnd) {
+      unsigned long long c = lane < n ? my_bufs[src * 33 + lane] : kEmptyKey;
+      unsigned long long* lq = my_lists + (size_t)src * kTqK;
+      const unsigned long long e = lq[lane];  // ascending; kEmpty past k
+      c = warp_sort32(c, lane);
+      // the 32 smallest of e and c: elementwise min against c reversed is
+      // bitonic; five half-cleaners sort it ascending
+      unsigned long long x = __shfl_sync(0xffffffffu, c, 31 - lane);
+      x = e < x ? e : x;
+#pragma unroll
+      for (int st = 16; st > 0; st >>= 1) {
+        const unsigned long long o = __shfl_xor_sync(0xffffffffu, x, st);
+        x = (lane & st) ? (x > o ? x : o) : (x < o ? x : o);
       }
-    }
-    __syncthreads();
-    const long long rb = s_rb;
-    const long long re = s_re;
-    const long long nrows = re > rb ? re - rb : 0;
-    const int nT = (int)((nrows + kTcM - 1) / kTcM);
-    const int nL = nT * KB;
-    if (tid == 0) {
-      next_load = 0;
-      pump(SA, false, rb, nL);  // start streaming rows while the queries are prepared
-    }
-    if (tid < kTcN) {
-      const int qr = s_qrow[tid];
-      s_qn[tid] = (METRIC == MF_METRIC_L2 && qr >= 0) ? a.qnorms[qr] : 0.0f;
-    }
-    // queries -> B operand (hi / lo), K-major, 128-byte swizzle
-    for (int e = tid; e < kTcN * KB * 8; e += kTcThreads) {
-      const int n = e / (KB * 8);
-      const int rem = e - n * KB * 8;
-      const int kb = rem >> 3;
-      const int c = rem & 7;
-      const int qr = s_qrow[n];
-      const int col = kb * 32 + c * 4;
-      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (qr >= 0 && col < d) v = *reinterpret_cast<const float4*>(a.xq + (long long)qr * d + col);
-      float4 h, l;
-      split_tf32(v.x, h.x, l.x);
-      split_tf32(v.y, h.y, l.y);
-      split_tf32(v.z, h.z, l.z);
-      split_tf32(v.w, h.w, l.w);
-      const int off = kb * (kTcN * 32) + n * 32 + ((c ^ (n & 7)) << 2);
-      *reinterpret_cast<float4*>(Bh + off) = h;
-      *reinterpret_cast<float4*>(Bl + off) = l;
-    }
-    WarpTopK<KCAP> tk[4];
-#pragma unroll
-    for (int jj = 0; jj < 4; ++jj) {
-      const int j = warp * 4 + jj;
-      tk[jj].init(lists + j * KCAP, bufs + j * 32, k, lane);
-    }
-    fence_proxy_async_smem();
-    __syncthreads();
-    TCP_END(0);
-
-    // Epilogue of local tile u: accumulator -> distances -> top-k offers.
-    auto epilogue = [&](int u) {
-      const uint32_t ts = tt + u;
-      const int b = ts & 1;
-      TCP_BEGIN();
-      mbar_wait(&accf[b], (ts >> 1) & 1, s_abort, &g_device_error);
-      TCP_END(1);
-      TCP_BEGIN();
-      tc_fence_after();
-      float v[16];
-      tmem_ld16(tmem + ((uint32_t)(quad * 32) << 16) + b * kTcN + half * 16, v);
-      tc_fence_before();
-      const long long r0 = rb + (long long)u * kTcM;
-      const long long row = r0 + quad * 32 + lane;
-      const bool valid = row < re;
-      const float xn = (METRIC == MF_METRIC_L2 && valid) ? a.xnorms[row] : 0.0f;
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const int j = half * 16 + i;
-        float dist;
-        if (METRIC == MF_METRIC_L2) dist = l2_from_dot(s_qn[j], xn, v[i]);
-        else dist = -v[i];
-        T[j * kTcM + quad * 32 + lane] = dist;
-      }
-      __syncthreads();
-      TCP_END(2);
-      TCP_BEGIN();
-#pragma unroll
-      for (int jj = 0; jj < 4; ++jj) {
-        const int j = warp * 4 + jj;
-        if (s_qrow[j] < 0) continue;
-        unsigned long long key[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int ri = i * 32 + lane;
-          const long long r = r0 + ri;
-          key[i] = r < re ? make_key(T[j * kTcM + ri], (unsigned int)r) : kEmptyKey;
-        }
-        tk[jj].offer4(key, k, lane);
-      }
-      TCP_END(3);
-      TCP_BEGIN();
-      __syncthreads();
-      TCP_END(4);
+      if (lane >= k) x = kEmptyKey;
+      lq[lane] = x;
+      const unsigned long long nk = __shfl_sync(0xffffffffu, x, k - 1);
+      if (lane == src) thr_reg = nk < bnd ? nk : bnd;
+      __syncwarp();
     };
-
-    for (int li = 0; li < nL; ++li) {
-      const uint32_t seq = g + li;
-      const int s = seq % SA;
-      const int t = li / KB;
-      const int kb = li - t * KB;
-      const int lb = seq & 1;  // lo buffer
-      TCP_BEGIN();
-      if (tid == 0) pump(li + 1, true, rb, nL);  // this K-block's load must be in flight
-      // the lo buffer was last read by the MMAs of sequence seq-2
-      if (seq >= 2) mbar_wait(&mdone[(seq - 2) % SA], ((seq - 2) / SA) & 1, s_abort, &g_device_error);
-      TCP_END(5);
-      TCP_BEGIN();
-      mbar_wait(&full[s], (seq / SA) & 1, s_abort, &g_device_error);
-      TCP_END(6);
-      TCP_BEGIN();
-      float4* As = reinterpret_cast<float4*>(A + size_t(s) * (kTcStageBytes / 4));
-      float4* Ls = reinterpret_cast<float4*>(Lo + size_t(lb) * (kTcStageBytes / 4));
-#pragma unroll
-      for (int e = tid; e < kTcStageBytes / 16; e += kTcThreads) {
-        const float4 v = As[e];
-        float4 h, l;
-        split_tf32(v.x, h.x, l.x);
-        split_tf32(v.y, h.y, l.y);
-        split_tf32(v.z, h.z, l.z);
-        split_tf32(v.w, h.w, l.w);
-        As[e] = h;
-        Ls[e] = l;
-      }
-      TCP_END(7);
-      TCP_BEGIN();
-      fence_proxy_async_smem();
-      tc_fence_before();
-      __syncthreads();
-      tc_fence_after();
-      TCP_END(8);
-      TCP_BEGIN();
-      if (tid == 0) {
-        const uint32_t dt = tmem + ((tt + t) & 1) * kTcN;
-        const uint32_t a_addr = smem_u32(As);
-        const uint32_t l_addr = smem_u32(Ls);
-        const uint32_t bh_addr = smem_u32(Bh + kb * (kTcN * 32));
-        const uint32_t bl_addr = smem_u32(Bl + kb * (kTcN * 32));
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-          const uint32_t off = kk * 32;  // 8 tf32 of K per MMA
-          mma_tf32(dt, desc_k_sw128(a_addr + off), desc_k_sw128(bh_addr + off), idesc,
-                   !(kb == 0 && kk == 0));
-          mma_tf32(dt, desc_k_sw128(a_addr + off), desc_k_sw128(bl_addr + off), idesc, true);
-          mma_tf32(dt, desc_k_sw128(l_addr + off), desc_k_sw128(bh_addr + off), idesc, true);
-        }
-        mma_commit(&mdone[s]);
-        if (kb == KB - 1) mma_commit(&accf[(tt + t) & 1]);
-        TCP_END(9);
-        TCP_BEGIN();
-        pump(li + SA, false, rb, nL);
-        TCP_END(10);
-      }
-      if (kb == KB - 1 && t >= 1) epilogue(t - 1);
-    }
-    if (nT >= 1) epilogue(nT - 1);
-
-    // ---- results of the item
-    TCP_BEGIN();
-#pragma unroll
-    for (int jj = 0; jj < 4; ++jj) {
-      const int j = warp * 4 + jj;
-      if (s_qrow[j] < 0) continue;
-      tk[jj].flush(k, lane);
-      const long long slot = s_qout[j];
-      for (int t = lane; t < k; t += 32) {
-        const unsigned long long key = tk[jj].list[t];
-        float dv;
-        long long lv;
-        if (key == kEmptyKey) {
-          dv = __int_as_float(0x7f800000);
-          lv = -1;
+    for (int item = blockIdx.x; item < total && !*s_abort; item += gridDim.x) {
+      const ItemDesc it = item_desc(a, item);
+      const long long nrows = it.re > it.rb ? it.re - it.rb : 0;
+      const int nT = (int)((nrows + BN - 1) / BN);
+      const bool valid = tid < it.nq_item;
+      long long slot = -1;
+      int q = 0;
+      if (valid) {
+        if (a.flat) {
+          q = it.a_row0 + tid;
+          const int s = item / a.nqt;
+          slot = a.direct ? q : (long long)q * a.P + s;
         } else {
-          dv = key_dist(key);
-          const unsigned int pos = key_index(key);
-          lv = a.ids ? a.ids[pos] : (long long)pos;
+          const int pr = a.pairs[it.a_row0 + tid];
+          q = pr / a.P;
+          slot = pr;
         }
-        a.out_d[slot * k + t] = dv;
-        a.out_l[slot * k + t] = lv;
       }
+      const float qn = (METRIC == MF_METRIC_L2 && valid) ? a.qnorms[q] : 0.0f;
+      for (int i = 0; i < 32; ++i) my_lists[i * kTqK + lane] = kEmptyKey;
+      __syncwarp();
+      const unsigned long long bound =
+          (a.bound_pd && valid) ? bound_key(a.bound_pd[((long long)q * a.P) * k + k - 1])
+                                : kEmptyKey;
+      unsigned long long thr = bound;
+      int cnt = 0;
+
+      for (int t = 0; t < nT; ++t, ++tt) {
+        const int b = tt & 1;
+        const long long r0 = it.rb + (long long)t * BN;
+        if (METRIC == MF_METRIC_L2) {
+          // row norms of this tile, shared by the four epilogue warps
+          float* xs = xn_s + b * BN;
+          for (int c = tid; c < BN; c += kTqEpiThreads) {
+            const long long r = r0 + c;
+            xs[c] = r < it.re ? a.xnorms[r] : 0.0f;
+          }
+          named_sync(1, kTqEpiThreads);
+        }
+        mbar_wait(&accf[b], (tt >> 1) & 1, s_abort, &g_device_error);
+        tc_fence_after();
+        const float* xs = xn_s + b * BN;
+#pragma unroll 1
+        for (int c0 = 0; c0 < BN; c0 += 32) {
+          float v[32];
+          tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + b * BN + c0, v);
+          // Branch-free pass: which of the 32 columns may beat this row's k-th key.
+          const long long rc = r0 + c0;
+          const bool open = thr == kEmptyKey;  // fewer than k candidates and no bound
+          const float thr_d = open ? 0.0f : key_dist(thr);
+          unsigned int m = 0;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            float dist;
+            if (METRIC == MF_METRIC_L2) dist = l2_from_dot(qn, xs[c0 + j], v[j]);
+            else dist = -v[j];
+            v[j] = dist;
+            m |= ((open || dist <= thr_d) && rc + j < it.re) ? (1u << j) : 0u;
+          }
+          if (!valid) m = 0;
+          // rows whose buffer cannot take this chunk's survivors merge first
+          unsigned int who = __ballot_sync(0xffffffffu, cnt + __popc(m) > 32);
+          while (who) {
+            const int src = __ffs(who) - 1;
+            who &= who - 1;
+            const int n = __shfl_sync(0xffffffffu, cnt, src);
+            const unsigned long long bs = __shfl_sync(0xffffffffu, bound, src);
+            merge_row(src, n, thr, bs);
+            if (lane == src) cnt = 0;
+          }
+          if (m) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if ((m >> j) & 1u) own_buf[cnt++] = make_key(v[j], (unsigned int)(rc + j));
+          }
+          __syncwarp();
+        }
+        tc_fence_before();
+        mbar_arrive(&acce[b]);
+      }
+      // flush the remaining candidates, then write each row's k keys
+      unsigned int who = __ballot_sync(0xffffffffu, cnt > 0);
+      while (who) {
+        const int src = __ffs(who) - 1;
+        who &= who - 1;
+        const int n = __shfl_sync(0xffffffffu, cnt, src);
+        const unsigned long long bs = __shfl_sync(0xffffffffu, bound, src);
+        merge_row(src, n, thr, bs);
+      }
+      for (int qq = 0; qq < 32; ++qq) {
+        const long long sq = __shfl_sync(0xffffffffu, slot, qq);
+        if (sq < 0) continue;
+        if (lane < k) {
+          const unsigned long long key = my_lists[qq * kTqK + lane];
+          float dv;
+          long long lv;
+          if (key == kEmptyKey) {
+            dv = __int_as_float(0x7f800000);
+            lv = -1;
+          } else {
+            dv = key_dist(key);
+            const unsigned int pos = key_index(key);
+            lv = a.ids ? a.ids[pos] : (long long)pos;
+          }
+          a.out_d[sq * k + lane] = dv;
+          a.out_l[sq * k + lane] = lv;
+        }
+      }
+      __syncwarp();
     }
-    g += nL;
-    tt += nT;
-    __syncthreads();
-    TCP_END(11);
   }
 
-#ifdef MF_TC_PROFILE
-  _tcp[13] = (unsigned long long)(clock64() - _t_start);
-  _tcp[14] = tt;
-  _tcp[15] = g;
-#endif
-  TCP_FLUSH();
-  // ---- teardown: copies and MMAs in flight finish before TMEM is released
-  if (tid == 0) {
-    int dummy = 0;
-    for (uint32_t seq = g; seq < g_issued; ++seq)
-      mbar_wait(&full[seq % SA], (seq / SA) & 1, &dummy, &g_device_error);
-    if (g > 0) {
-      dummy = 0;
-      mbar_wait(&mdone[(g - 1) % SA], ((g - 1) / SA) & 1, &dummy, &g_device_error);
-    }
-  }
+  // ---- teardown: stages in flight land and MMAs finish before TMEM is freed
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 0) tmem_dealloc(tmem, 64);
+  if (tid == 4 * 32) {
+    int dummy = 0;
+    for (uint32_t seq = s_seq[0]; seq < s_seq[1]; ++seq)
+      mbar_wait(&full[seq % SA], (seq / SA) & 1, &dummy, &g_device_error);
+  }
+  __syncthreads();
+  if (warp == 5) tmem_dealloc(tmem, 2 * BN);
+#ifdef MF_TC_PROFILE
+  if (tid == 0) atomicAdd(&g_tc_prof[13], (unsigned long long)(clock64() - _tk));
+#endif
 }
 
 // ------------------------------------------------------------------ host
-typedef void (*TcFn)(const ScanArgs, const CUtensorMap, const TcSmem);
+typedef void (*TqFn)(const ScanArgs, const TqMaps, const TqLayout);
 
 template <int METRIC>
-TcFn pick_tc(int kcap) {
-  switch (kcap) {
-    case 32: return tc_scan_kernel<METRIC, 32>;
-    case 64: return tc_scan_kernel<METRIC, 64>;
-    case 128: return tc_scan_kernel<METRIC, 128>;
-    case 256: return tc_scan_kernel<METRIC, 256>;
+TqFn pick_tq(int BN) {
+  return BN == 256 ? tq_scan_kernel<METRIC, 256> : tq_scan_kernel<METRIC, 128>;
+}
+
+int tq_kcap(int k) { return k <= kTqK ? kTqK : 0; }
+
+// The widest tile (BN rows) and deepest ring that fit shared memory.
+bool tq_choose(int d, int kcap, TqLayout* out) {
+  const int cands[4][2] = {{256, 3}, {256, 2}, {128, 3}, {128, 2}};
+  for (auto& c : cands) {
+    TqLayout l = tq_layout(d, kcap, c[0], c[1]);
+    if (l.total <= (size_t)kTqMaxSmem) {
+      *out = l;
+      return true;
+    }
   }
-  return nullptr;
+  return false;
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 std::mutex g_tc_mu;
-int g_tc_attr[64][2][4];  // smem limit set per (device, metric, kcap)
+int g_tc_attr[64][2][2];  // dynamic smem set per (device, metric, BN)
 
 int encoder(PFN_cuTensorMapEncodeTiled_v12000* out) {
   std::lock_guard<std::mutex> lk(g_tc_mu);
@@ -461,62 +457,125 @@ int encoder(PFN_cuTensorMapEncodeTiled_v12000* out) {
   return MF_OK;
 }
 
+int make_map(PFN_cuTensorMapEncodeTiled_v12000 enc, CUtensorMap* map, const float* p, int d,
+             int64_t rows, int box_rows) {
+  cuuint64_t dims[2] = {(cuuint64_t)d, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)d * 4};
+  cuuint32_t box[2] = {32, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(p), dims, strides,
+                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  MF_CHECK(r == CUDA_SUCCESS, MF_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return MF_OK;
+}
+
 int g_engine = 0;  // 0 auto, 1 SIMT only, 2 tensor cores where eligible
+
+__global__ void tf32_residual_kernel(const float4* __restrict__ x, int64_t n4, float4* lo) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n4) return;
+  const float4 v = x[i];
+  float4 h, l;
+  split_tf32(v.x, h.x, l.x);
+  split_tf32(v.y, h.y, l.y);
+  split_tf32(v.z, h.z, l.z);
+  split_tf32(v.w, h.w, l.w);
+  lo[i] = l;
+}
+
+// Gathered query rows for IVF items: row p of (g_hi, g_lo) = query pairs[p] / P.
+__global__ void gather_queries_kernel(const float* __restrict__ xq, int d,
+                                      const int* __restrict__ pairs,
+                                      const int* __restrict__ n_pairs, int P, float* g_hi,
+                                      float* g_lo) {
+  const int p = blockIdx.x;
+  if (p >= *n_pairs) return;
+  const int q = pairs[p] / P;
+  const float4* src = reinterpret_cast<const float4*>(xq + (int64_t)q * d);
+  float4* dh = reinterpret_cast<float4*>(g_hi + (int64_t)p * d);
+  float4* dl = reinterpret_cast<float4*>(g_lo + (int64_t)p * d);
+  for (int j = threadIdx.x; j < (d >> 2); j += blockDim.x) {
+    const float4 v = src[j];
+    float4 h, l;
+    split_tf32(v.x, h.x, l.x);
+    split_tf32(v.y, h.y, l.y);
+    split_tf32(v.z, h.z, l.z);
+    split_tf32(v.w, h.w, l.w);
+    dh[j] = v;
+    dl[j] = l;
+  }
+}
 
 }  // namespace
 
 void set_scan_engine(int e) { g_engine = e; }
 int scan_engine() { return g_engine; }
 
+int tc_group() { return kTqM; }
+
 bool tc_eligible(int metric, int d, int k, int64_t xb_rows) {
-  if (g_engine != 2) return false;  // automatic selection keeps the SIMT scan for now
+  if (g_engine == 1) return false;
   if (metric != MF_METRIC_L2 && metric != MF_METRIC_INNER_PRODUCT) return false;
-  if (d < 32 || d > kTcMaxD) return false;
-  if (xb_rows < kTcM) return false;
-  const int kcap = scan_kcap(k);
+  if (d < 32 || d > kTqMaxD || d % 4 != 0) return false;
+  if (xb_rows < 256) return false;
+  const int kcap = tq_kcap(k);
   if (kcap == 0) return false;
-  return tc_layout(d, kcap, 2).total <= (size_t)kTcMaxSmem;
+  TqLayout l;
+  return tq_choose(d, kcap, &l);
 }
 
-int launch_tc_scan(const ScanArgs& a, int metric, int64_t total_items, int64_t xb_rows,
-                   int device, cudaStream_t stream) {
-  const int kcap = scan_kcap(a.k);
-  MF_CHECK(kcap != 0, MF_ERR_INVALID_ARGS, "k=%d exceeds %d", a.k, kMaxK);
-  TcFn fn = metric == MF_METRIC_L2 ? pick_tc<MF_METRIC_L2>(kcap)
-                                   : pick_tc<MF_METRIC_INNER_PRODUCT>(kcap);
+int launch_tf32_residual(const float* x, int64_t n, int d, float* lo, cudaStream_t stream) {
+  const int64_t n4 = n * (int64_t)d / 4;
+  if (n4 <= 0) return MF_OK;
+  tf32_residual_kernel<<<(unsigned int)ceil_div(n4, 256), 256, 0, stream>>>(
+      reinterpret_cast<const float4*>(x), n4, reinterpret_cast<float4*>(lo));
+  MF_LAUNCH_CHECK();
+  return MF_OK;
+}
+
+int launch_gather_queries(const float* xq, int d, const int* pairs, const int* n_pairs,
+                          int64_t max_pairs, int P, float* g_hi, float* g_lo,
+                          cudaStream_t stream) {
+  if (max_pairs <= 0) return MF_OK;
+  gather_queries_kernel<<<(unsigned int)max_pairs, 64, 0, stream>>>(xq, d, pairs, n_pairs, P,
+                                                                    g_hi, g_lo);
+  MF_LAUNCH_CHECK();
+  return MF_OK;
+}
+
+int launch_tc_scan(const ScanArgs& a, int metric, const float* a_lo, int64_t a_rows,
+                   const float* b_lo, int64_t b_rows, int64_t total_items, int device,
+                   cudaStream_t stream) {
+  const int kcap = tq_kcap(a.k);
+  TqLayout lay;
+  MF_CHECK(kcap != 0 && tq_choose(a.d, kcap, &lay), MF_ERR_INVALID_ARGS,
+           "tensor-core scan does not fit (d=%d k=%d)", a.d, a.k);
+  TqFn fn = metric == MF_METRIC_L2 ? pick_tq<MF_METRIC_L2>(lay.BN)
+                                   : pick_tq<MF_METRIC_INNER_PRODUCT>(lay.BN);
   MF_CHECK(fn != nullptr, MF_ERR_METRIC, "metric %d has no tensor-core scan", metric);
-  int SA = 8;
-  TcSmem lay = tc_layout(a.d, kcap, SA);
-  while (SA > 2 && lay.total > (size_t)kTcMaxSmem) lay = tc_layout(a.d, kcap, --SA);
-  MF_CHECK(lay.total <= (size_t)kTcMaxSmem, MF_ERR_INVALID_ARGS,
-           "tensor-core scan does not fit shared memory (d=%d k=%d)", a.d, a.k);
   PFN_cuTensorMapEncodeTiled_v12000 enc;
   MF_TRY(encoder(&enc));
-  CUtensorMap map;
-  cuuint64_t dims[2] = {(cuuint64_t)a.d, (cuuint64_t)xb_rows};
-  cuuint64_t strides[1] = {(cuuint64_t)a.d * 4};
-  cuuint32_t box[2] = {32, (cuuint32_t)kTcM};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = enc(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(a.xb), dims, strides,
-                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  MF_CHECK(r == CUDA_SUCCESS, MF_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  TqMaps maps;
+  MF_TRY(make_map(enc, &maps.a_hi, a.xq, a.d, a_rows, kTqM));
+  MF_TRY(make_map(enc, &maps.a_lo, a_lo, a.d, a_rows, kTqM));
+  MF_TRY(make_map(enc, &maps.b_hi, a.xb, a.d, b_rows, lay.BN));
+  MF_TRY(make_map(enc, &maps.b_lo, b_lo, a.d, b_rows, lay.BN));
   {
     std::lock_guard<std::mutex> lk(g_tc_mu);
     const int mi = metric == MF_METRIC_L2 ? 0 : 1;
-    const int ki = kcap == 32 ? 0 : kcap == 64 ? 1 : kcap == 128 ? 2 : 3;
-    if (device < 0 || device >= 64 || g_tc_attr[device][mi][ki] < (int)lay.total) {
+    const int bi = lay.BN == 256 ? 1 : 0;
+    if (device < 0 || device >= 64 || g_tc_attr[device][mi][bi] < (int)lay.total) {
       MF_CUDA(cudaFuncSetAttribute(reinterpret_cast<const void*>(fn),
                                    cudaFuncAttributeMaxDynamicSharedMemorySize, (int)lay.total));
-      if (device >= 0 && device < 64) g_tc_attr[device][mi][ki] = (int)lay.total;
+      if (device >= 0 && device < 64) g_tc_attr[device][mi][bi] = (int)lay.total;
     }
   }
   if (total_items <= 0) return MF_OK;
   long long grid = num_sms(device);
   if (grid > total_items) grid = total_items;
-  MF_CUDA(cudaMemsetAsync(a.counter, 0, sizeof(int), stream));
   ScopedTiming tm(a.flat ? "scan_topk_flat" : "scan_topk_ivf", stream);
-  fn<<<(unsigned int)grid, kTcThreads, lay.total, stream>>>(a, map, lay);
+  fn<<<(unsigned int)grid, kTqThreads, lay.total, stream>>>(a, maps, lay);
   MF_LAUNCH_CHECK();
   return MF_OK;
 }

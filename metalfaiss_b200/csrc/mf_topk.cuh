@@ -31,6 +31,40 @@ __device__ __forceinline__ unsigned long long warp_sort32(unsigned long long c, 
   return c;
 }
 
+// N independent ascending bitonic sorts of 32 keys (one per lane each), with
+// their shuffle stages interleaved so the latencies overlap.
+template <int N>
+__device__ __forceinline__ void warp_sort32_n(unsigned long long (&c)[N], int lane) {
+#pragma unroll
+  for (int size = 2; size <= 32; size <<= 1) {
+#pragma unroll
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      const bool up = (lane & size) == 0;
+      const bool low = (lane & stride) == 0;
+      unsigned long long o[N];
+#pragma unroll
+      for (int i = 0; i < N; ++i) o[i] = __shfl_xor_sync(0xffffffffu, c[i], stride);
+#pragma unroll
+      for (int i = 0; i < N; ++i)
+        c[i] = (low == up) ? (c[i] < o[i] ? c[i] : o[i]) : (c[i] < o[i] ? o[i] : c[i]);
+    }
+  }
+}
+
+// Sorts N bitonic 32-key sequences ascending (half-cleaners, strides 16..1).
+template <int N>
+__device__ __forceinline__ void warp_bitonic_clean32_n(unsigned long long (&x)[N], int lane) {
+#pragma unroll
+  for (int st = 16; st > 0; st >>= 1) {
+    unsigned long long o[N];
+#pragma unroll
+    for (int i = 0; i < N; ++i) o[i] = __shfl_xor_sync(0xffffffffu, x[i], st);
+#pragma unroll
+    for (int i = 0; i < N; ++i)
+      x[i] = (lane & st) ? (x[i] > o[i] ? x[i] : o[i]) : (x[i] < o[i] ? x[i] : o[i]);
+  }
+}
+
 // Number of lanes whose (sorted, ascending) key is < e.
 // Binary search over the 32 lane-distributed keys; every lane runs the same
 // shuffles but searches for its own e. The five halving steps resolve 0..31;
@@ -94,21 +128,24 @@ struct WarpTopK {
   unsigned long long* list;  // KCAP keys, ascending; first k meaningful
   unsigned long long* buf;   // 32 keys
   int nbuf;
-  unsigned long long thr;    // list[k-1]
+  unsigned long long thr;    // min(list[k-1], bound)
+  unsigned long long bound;  // a key known to be no better than the final k-th
 
   __device__ __forceinline__ void init(unsigned long long* l, unsigned long long* b, int k,
-                                       int lane) {
+                                       int lane, unsigned long long bnd = kEmptyKey) {
     list = l;
     buf = b;
     for (int i = lane; i < k; i += 32) list[i] = kEmptyKey;
     nbuf = 0;
-    thr = kEmptyKey;
+    bound = bnd;
+    thr = bnd;
     __syncwarp();
   }
 
   __device__ __forceinline__ void flush(int k, int lane) {
     if (nbuf == 0) return;
-    thr = merge_into_list<KCAP>(list, buf, nbuf, k, lane);
+    const unsigned long long t = merge_into_list<KCAP>(list, buf, nbuf, k, lane);
+    thr = t < bound ? t : bound;
     nbuf = 0;
   }
 

@@ -36,6 +36,7 @@ class FlatIndex:
         self._dp = padded_dim(self.d)
         self._xb = GrowBuffer((self._dp,), torch.float32, self.device)
         self._norms = GrowBuffer((), torch.float32, self.device)
+        self._lo = GrowBuffer((self._dp,), torch.float32, self.device)  # tf32 residuals
         self._ids = GrowBuffer((), torch.int64, self.device)
         self._ws = None
         self.verbose = False
@@ -86,10 +87,13 @@ class FlatIndex:
         else:
             idt = as_ids(ids, n, self.device)
         norms = torch.empty(n, dtype=torch.float32, device=self.device)
-        nat.call("mf_vector_norms", self.device.index, nat.stream_of(self.device), nat.ptr(x), n,
-                 self._dp, nat.ptr(norms))
+        lo = torch.empty_like(x)
+        st = nat.stream_of(self.device)
+        nat.call("mf_vector_norms", self.device.index, st, nat.ptr(x), n, self._dp, nat.ptr(norms))
+        nat.call("mf_tf32_residual", self.device.index, st, nat.ptr(x), n, self._dp, nat.ptr(lo))
         self._xb.append(x)
         self._norms.append(norms)
+        self._lo.append(lo)
         self._ids.append(idt)
 
     def add_with_ids(self, xs, ids) -> None:
@@ -100,6 +104,7 @@ class FlatIndex:
         """python/metalfaiss/indexflat.py:127-133."""
         self._xb.reset()
         self._norms.reset()
+        self._lo.reset()
         self._ids.reset()
 
     def clone(self) -> "FlatIndex":
@@ -108,6 +113,7 @@ class FlatIndex:
         if self.ntotal:
             out._xb.append(self._xb.view())
             out._norms.append(self._norms.view())
+            out._lo.append(self._lo.view())
             out._ids.append(self._ids.view())
         return out
 
@@ -138,7 +144,8 @@ class FlatIndex:
                                       m, k)
         ws = self._workspace().get(ws_bytes)
         nat.call("mf_flat_search", self.device.index, nat.stream_of(self.device), nat.ptr(xq), nq,
-                 nat.ptr(self._xb.buf), nat.ptr(self._norms.buf), self.ntotal, self._dp, m, k,
+                 nat.ptr(self._xb.buf), nat.ptr(self._norms.buf), nat.ptr(self._lo.buf),
+                 self.ntotal, self._dp, m, k,
                  nat.ptr(self._ids.buf) if map_ids else nat.ptr(None), nat.ptr(D), nat.ptr(I),
                  nat.ptr(ws), ws.numel())
         return SearchResult(D, I)

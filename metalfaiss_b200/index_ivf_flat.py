@@ -81,6 +81,7 @@ class IVFFlatIndex:
             if torch.cuda.is_available() else None
         self._vecs = None
         self._norms = None
+        self._lo = None  # tf32 residuals of _vecs (tensor-core scan operand)
         self._ids = None
         self._order = None
         self._ntotal = 0
@@ -194,6 +195,9 @@ class IVFFlatIndex:
                  nat.ptr(labels), n, nat.ptr(out_off), nat.ptr(out_vecs), nat.ptr(out_norms),
                  nat.ptr(out_ids), nat.ptr(ws), ws.numel())
         self._offsets, self._vecs, self._norms, self._ids = out_off, out_vecs, out_norms, out_ids
+        self._lo = torch.empty_like(out_vecs)
+        nat.call("mf_tf32_residual", self.device.index, nat.stream_of(self.device),
+                 nat.ptr(out_vecs), total, self._dp, nat.ptr(self._lo))
         self._ntotal = total
         self._direct_map = None
         sizes = np.diff(out_off.cpu().numpy())
@@ -221,6 +225,7 @@ class IVFFlatIndex:
             # An untouched index: give the kernels a valid empty bank.
             self._vecs = torch.zeros((1, self._dp), dtype=torch.float32, device=self.device)
             self._norms = torch.zeros(1, dtype=torch.float32, device=self.device)
+            self._lo = torch.zeros((1, self._dp), dtype=torch.float32, device=self.device)
             self._ids = torch.full((1,), -1, dtype=torch.int64, device=self.device)
 
     def search(self, xs, k: int) -> SearchResult:
@@ -249,8 +254,8 @@ class IVFFlatIndex:
         nat.call("mf_ivf_search", self.device.index, nat.stream_of(self.device), nat.ptr(xq), nq,
                  nat.ptr(q._xb.buf), nat.ptr(q._norms.buf), self._nlist, self._nprobe,
                  nat.ptr(self._offsets), nat.ptr(self._vecs), nat.ptr(self._norms),
-                 nat.ptr(self._ids), self._vecs.shape[0], nat.ptr(self._order), self._dp, m, k,
-                 nat.ptr(D), nat.ptr(I), nat.ptr(ws), ws.numel())
+                 nat.ptr(self._lo), nat.ptr(self._ids), self._vecs.shape[0], nat.ptr(self._order),
+                 self._dp, m, k, nat.ptr(D), nat.ptr(I), nat.ptr(ws), ws.numel())
         return SearchResult(D, I)
 
     def _check_k(self, k):
@@ -289,7 +294,7 @@ class IVFFlatIndex:
         ws = self._workspace().get(nbytes)
         nat.call("mf_ivf_search_preassigned", self.device.index, nat.stream_of(self.device),
                  nat.ptr(xq), nq, nat.ptr(probes), P, self._nlist, nat.ptr(self._offsets),
-                 nat.ptr(self._vecs), nat.ptr(self._norms), nat.ptr(self._ids),
+                 nat.ptr(self._vecs), nat.ptr(self._norms), nat.ptr(self._lo), nat.ptr(self._ids),
                  self._vecs.shape[0], nat.ptr(self._order), self._dp, m, k, nat.ptr(D), nat.ptr(I),
                  nat.ptr(ws), ws.numel())
         return SearchResult(D, I)

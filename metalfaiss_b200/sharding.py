@@ -98,6 +98,7 @@ def keep_lists(index, keep_mask: np.ndarray):
         row_mask = torch.from_numpy(keep).to(dev)[list_of_row]
         out._vecs = index._vecs[: index.ntotal][row_mask].contiguous()
         out._norms = index._norms[: index.ntotal][row_mask].contiguous()
+        out._lo = index._lo[: index.ntotal][row_mask].contiguous()
         out._ids = index._ids[: index.ntotal][row_mask].contiguous()
         out._ntotal = int(out._ids.shape[0])
     out._offsets = torch.from_numpy(offsets).to(dev)

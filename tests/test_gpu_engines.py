@@ -1,5 +1,7 @@
 """The tensor-core (tcgen05, 3xTF32) and SIMT scan engines against each other
-and against the oracle, on flat and IVF searches."""
+and against the oracle, on flat and IVF searches. Engine 2 (like the default)
+uses the tensor cores where the shape allows (L2 / inner product, d >= 32,
+k <= 64) and the SIMT scan otherwise; engine 1 forces the SIMT scan."""
 import numpy as np
 import pytest
 
