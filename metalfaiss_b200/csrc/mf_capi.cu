@@ -111,6 +111,7 @@ struct IvfWs {
   int64_t* pl;
   int64_t* pair_counts;
   int64_t* pair_offsets64;
+  float* bound;      // per-query bound from the first rows of the nearest list
   float* g_hi;       // gathered query rows per (query, probe) pair (tensor cores)
   float* g_lo;
   float* cent_lo;    // tf32 residuals of the centroids (coarse step, tensor cores)
@@ -135,6 +136,7 @@ IvfWs carve_ivf(Carver& c, int64_t nq, int nlist, int P, int d, int k, int mode,
   } else {
     w.pd = c.take<float>((size_t)nq * P * k);
     w.pl = c.take<int64_t>((size_t)nq * P * k);
+    w.bound = c.take<float>((size_t)nq);
     w.g_hi = c.take<float>((size_t)nq * P * d);
     w.g_lo = c.take<float>((size_t)nq * P * d);
   }
@@ -175,15 +177,19 @@ int ivf_scan_topk(int device, cudaStream_t stream, const IvfWs& w, const float* 
   a.out_d = w.pd;
   a.out_l = w.pl;
   a.direct = 0;
-  // Two phases: every query's first probe (its nearest list), then the rest
-  // with the first probe's k-th distance as an exact bound on the final k-th.
+  // Two phases. Phase 1 scans only the first kBoundRows rows of every query's
+  // nearest list (probe 0); the k-th distance found there is an upper bound
+  // on the query's final k-th distance. Phase 2 scans all probes, keeping
+  // only candidates within the bound, so most rows of the farther lists never
+  // enter the top-k merges.
+  constexpr int64_t kBoundRows = 128;
   const int phases = P > 1 ? 2 : 1;
   for (int ph = 0; ph < phases; ++ph) {
-    const int s0 = ph == 0 ? 0 : 1;
-    const int s1 = phases == 1 ? P : (ph == 0 ? 1 : P);
+    const bool bounding = phases == 2 && ph == 0;
     MF_TRY(run_ivf_groups_ex(w.g, probes, nq, P, nlist, list_offsets, list_order, w.pd, w.pl, k,
-                             nullptr, group, stream, s0, s1));
-    a.bound_pd = ph == 1 ? w.pd : nullptr;
+                             nullptr, group, stream, 0, bounding ? 1 : P));
+    a.max_rows = bounding ? kBoundRows : 0;
+    a.bound = (phases == 2 && ph == 1) ? w.bound : nullptr;
     if (tc) {
       // A operand: the queries of every (query, probe) pair, gathered in list order
       MF_TRY(launch_gather_queries(xq, d, w.g.pairs, w.g.pair_offsets + nlist, nq * P, P, w.g_hi,
@@ -194,6 +200,7 @@ int ivf_scan_topk(int device, cudaStream_t stream, const IvfWs& w, const float* 
     } else {
       MF_TRY(launch_scan(a, metric, kEpiTopK, nq * P, device, stream));
     }
+    if (bounding) MF_TRY(launch_extract_bound(w.pd, nq, P, k, w.bound, stream));
   }
   MF_TRY(launch_merge(w.pd, w.pl, nq, P, k, k, D, I, stream));
   return MF_OK;

@@ -113,7 +113,8 @@ __global__ void __launch_bounds__(kScanThreads) scan_kernel(const ScanArgs a) {
       }
       if (tid == 0) {
         s_rb = a.list_offsets[it.x];
-        s_re = a.list_offsets[it.x + 1];
+        const long long re = a.list_offsets[it.x + 1];
+        s_re = (a.max_rows > 0 && re - s_rb > a.max_rows) ? s_rb + a.max_rows : re;
       }
     }
     __syncthreads();
@@ -139,7 +140,7 @@ __global__ void __launch_bounds__(kScanThreads) scan_kernel(const ScanArgs a) {
       if (EPI == kEpiTopK) {
         unsigned long long bnd = kEmptyKey;
         const int qr = s_qrow[warp * 4 + j];
-        if (a.bound_pd && qr >= 0) bnd = bound_key(a.bound_pd[((long long)qr * a.P) * k + k - 1]);
+        if (a.bound && qr >= 0) bnd = bound_key(a.bound[qr]);
         tk[j].init(lists + (warp * 4 + j) * KCAP, bufs + (warp * 4 + j) * 32, k, lane, bnd);
       }
     }
@@ -321,6 +322,12 @@ __global__ void map_ids_kernel(const int64_t* __restrict__ ids, int64_t* labels,
   if (p >= 0) labels[i] = ids[p];
 }
 
+__global__ void extract_bound_kernel(const float* __restrict__ pd, int64_t nq, int P, int k,
+                                     float* bound) {
+  const long long q = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (q < nq) bound[q] = pd[(q * P) * k + k - 1];
+}
+
 __global__ void norms_kernel(const float* __restrict__ x, int64_t n, int d, float* norms) {
   const int lane = threadIdx.x & 31;
   const long long row = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -412,7 +419,10 @@ int launch_scan(const ScanArgs& a, int metric, int epi, int64_t total_items, int
   long long grid = (long long)num_sms(device) * occ;
   if (grid > total_items) grid = total_items;
   MF_CUDA(cudaMemsetAsync(a.counter, 0, sizeof(int), stream));
-  ScopedTiming tm(epi == kEpiTopK ? (a.flat ? "scan_topk_flat" : "scan_topk_ivf") : "scan_range",
+  ScopedTiming tm(epi == kEpiTopK
+                      ? (a.flat ? "scan_topk_flat"
+                                : (a.max_rows > 0 ? "scan_topk_ivf_bound" : "scan_topk_ivf"))
+                      : "scan_range",
                   stream);
   fn<<<(unsigned int)grid, kScanThreads, smem, stream>>>(a);
   MF_LAUNCH_CHECK();
@@ -424,6 +434,14 @@ int launch_norms(const float* x, int64_t n, int d, float* norms, cudaStream_t st
   const int warps = 8;
   const long long grid = ceil_div(n, warps);
   norms_kernel<<<(unsigned int)grid, warps * 32, 0, stream>>>(x, n, d, norms);
+  MF_LAUNCH_CHECK();
+  return MF_OK;
+}
+
+int launch_extract_bound(const float* pd, int64_t nq, int P, int k, float* bound,
+                         cudaStream_t stream) {
+  if (nq <= 0) return MF_OK;
+  extract_bound_kernel<<<(unsigned int)ceil_div(nq, 256), 256, 0, stream>>>(pd, nq, P, k, bound);
   MF_LAUNCH_CHECK();
   return MF_OK;
 }

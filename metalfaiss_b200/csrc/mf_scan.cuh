@@ -48,9 +48,12 @@ struct ScanArgs {
   float* out_d;
   int64_t* out_l;
   int direct;
-  // IVF second phase: bound_pd[(q*P)*k + k-1] (the k-th distance of query q's
-  // nearest list) bounds every other list's candidates; null = no bound.
-  const float* bound_pd;
+  // IVF second phase: bound[q] (a k-th distance over part of query q's nearest
+  // list, an upper bound on its final k-th distance) filters every candidate;
+  // null = no bound.
+  const float* bound;
+  // IVF items scan at most max_rows rows of their list (0 = the whole list).
+  int64_t max_rows;
   // range search
   float radius;
   int64_t* counts;        // count pass: (nq*P)
@@ -123,6 +126,10 @@ IvfGroups carve_ivf_groups(Carver& c, int64_t nq, int nlist, int P);
 int run_ivf_groups(const IvfGroups& g, const int64_t* probes, int64_t nq, int P, int nlist,
                    const int64_t* list_offsets, const int32_t* list_order, int group,
                    cudaStream_t stream);
+
+// bound[q] = pd[(q*P + 0)*k + k-1] (the k-th distance of slot 0).
+int launch_extract_bound(const float* pd, int64_t nq, int P, int k, float* bound,
+                         cudaStream_t stream);
 
 // Exclusive scan of n int64 counts into out (n+1 entries; out[n] = total).
 int launch_exclusive_scan_i64(const int64_t* in, int64_t n, int64_t* out, cudaStream_t stream);

@@ -123,7 +123,8 @@ __device__ __forceinline__ ItemDesc item_desc(const ScanArgs& a, int item) {
     it.a_row0 = pb;
     it.nq_item = (pe0 - pb) < kTqM ? (pe0 - pb) : kTqM;
     it.rb = a.list_offsets[g.x];
-    it.re = a.list_offsets[g.x + 1];
+    const long long re = a.list_offsets[g.x + 1];
+    it.re = (a.max_rows > 0 && re - it.rb > a.max_rows) ? it.rb + a.max_rows : re;
   }
   return it;
 }
@@ -309,9 +310,7 @@ __global__ void __launch_bounds__(kTqThreads, 1)
       const float qn = (METRIC == MF_METRIC_L2 && valid) ? a.qnorms[q] : 0.0f;
       for (int i = 0; i < 32; ++i) my_lists[i * kTqK + lane] = kEmptyKey;
       __syncwarp();
-      const unsigned long long bound =
-          (a.bound_pd && valid) ? bound_key(a.bound_pd[((long long)q * a.P) * k + k - 1])
-                                : kEmptyKey;
+      const unsigned long long bound = (a.bound && valid) ? bound_key(a.bound[q]) : kEmptyKey;
       unsigned long long thr = bound;
       int cnt = 0;
 
@@ -574,7 +573,7 @@ int launch_tc_scan(const ScanArgs& a, int metric, const float* a_lo, int64_t a_r
   if (total_items <= 0) return MF_OK;
   long long grid = num_sms(device);
   if (grid > total_items) grid = total_items;
-  ScopedTiming tm(a.flat ? "scan_topk_flat" : "scan_topk_ivf", stream);
+  ScopedTiming tm(a.flat ? "scan_topk_flat" : (a.max_rows > 0 ? "scan_topk_ivf_bound" : "scan_topk_ivf"), stream);
   fn<<<(unsigned int)grid, kTqThreads, lay.total, stream>>>(a, maps, lay);
   MF_LAUNCH_CHECK();
   return MF_OK;
