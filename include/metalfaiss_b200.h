@@ -111,6 +111,28 @@ MF_API int mf_flat_search(int device, void* stream, const float* xq, int64_t nq,
                    int d, int metric, int k, const int64_t* ids, float* distances,
                    int64_t* labels, void* workspace, size_t workspace_bytes);
 
+/* Size of the fixed device scratch array behind mf_flat_search_noalloc. */
+#define MF_NOALLOC_SCRATCH_BYTES (16u << 20)
+
+/* mf_flat_search without a workspace, for callers that cannot allocate device
+ * memory: an FFI or plugin host that only passes buffers it already owns, code
+ * where cudaMalloc is not allowed or would stall the device, or a process
+ * whose device footprint must stay fixed after start-up. No counterpart in the
+ * reference (its searches allocate through MLX).
+ * Same arguments and results as mf_flat_search minus the workspace. Scratch is
+ * one file-scope device array of MF_NOALLOC_SCRATCH_BYTES (16 MiB) that every
+ * GPU loading this library holds until exit; a search needing more
+ * (mf_flat_search_workspace_size > 16 MiB) returns MF_ERR_INVALID_ARGS
+ * without launching. The first call on a device looks up the array's address
+ * and should come before any stream capture on that device. Nothing is
+ * allocated or freed. All calls on a device share the array: calls that
+ * overlap on the GPU (other streams, other threads) race and must be
+ * serialized by the caller. */
+MF_API int mf_flat_search_noalloc(int device, void* stream, const float* xq, int64_t nq,
+                                  const float* xb, const float* xb_norms, const float* xb_lo,
+                                  int64_t nb, int d, int metric, int k, const int64_t* ids,
+                                  float* distances, int64_t* labels);
+
 /* ---------------------------------------------------------------- IVFFlat */
 
 /* Inverted lists are CSR: list l holds rows [list_offsets[l], list_offsets[l+1])
