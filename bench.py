@@ -50,12 +50,38 @@ def log(*a):
 
 
 def measured_peaks():
+    """(HBM GB/s, bf16 TFLOP/s burst, kind) from MEASURED_PEAKS.json, else the fallback."""
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
         with open(p) as f:
             d = json.load(f)
-        return float(d["hbm_gbs"]), "measured"
-    return 6650.0, "fallback"
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+def tf32_gemm_peak(device, n=8192, reps=10):
+    """Dense TF32 tensor-core throughput of cuBLAS on this GPU (TFLOP/s, best of
+    `reps` n^3 GEMMs, CUDA events): the denominator for the 3xTF32 scans."""
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = True
+    try:
+        a = torch.randn(n, n, device=device)
+        b = torch.randn(n, n, device=device)
+        c = torch.empty(n, n, device=device)
+        for _ in range(3):
+            torch.matmul(a, b, out=c)
+        best = float("inf")
+        for _ in range(reps):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            torch.matmul(a, b, out=c)
+            e1.record()
+            torch.cuda.synchronize(device)
+            best = min(best, e0.elapsed_time(e1))
+        del a, b, c
+        return 2.0 * n ** 3 / (best * 1e-3) / 1e12
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
 
 
 class ClockSampler:
@@ -112,6 +138,11 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
+# dram__bytes_read.sum + dram__bytes_write.sum of one all-probes scan launch,
+# from the ncu capture summarised in profiles/ (None where not captured).
+TRAFFIC = {}
+
+
 def lpt_partition(sizes: np.ndarray, world: int) -> np.ndarray:
     """Owner rank of each list: greedy longest-processing-time on list sizes."""
     from metalfaiss_b200.sharding import lpt_partition as f
@@ -140,15 +171,21 @@ def build_index(cfg, device, seed=1234):
     return idx, xq
 
 
-def scan_algorithmic_bytes(idx, probes_np, d, k):
-    """Bytes the list-major scan must move once: every probed list's rows
-    (vector + norm) read once, each (query, probe) pair's k partial results
-    written once, and the query vectors read once."""
+def scan_work(idx, probes_np, d, k):
+    """Work of one IVF scan over the probes (nq, P) of this index:
+    * pairs: (query, row) distance evaluations, sum over queries of the rows of
+      their probed lists;
+    * bytes: what the list-major scan must move once: every probed list's rows
+      (vector + norm) read once, the query vectors read once and each
+      (query, probe) pair's k partial results written once;
+    * rows: distinct probed rows."""
     sizes = idx.list_sizes()
-    probed = np.unique(probes_np[probes_np >= 0])
+    valid = probes_np[probes_np >= 0]
+    probed = np.unique(valid)
     rows = int(sizes[probed].sum())
+    pairs = int(sizes[valid].sum())
     nq, P = probes_np.shape
-    return rows * (4 * d + 4) + nq * d * 4 + nq * P * k * 12, rows
+    return pairs, rows * (4 * d + 4) + nq * d * 4 + nq * P * k * 12, rows
 
 
 def run_ours(args, cfg):
@@ -175,10 +212,10 @@ def run_ours(args, cfg):
 
     # probes (for the roofline bytes): the coarse step of this batch
     probes = idx.quantizer._search_padded(xq, min(cfg["nprobe"], cfg["nlist"]), map_ids=False).labels
-    alg_bytes, probed_rows = scan_algorithmic_bytes(sharded.local if sharded else idx,
-                                                    probes.cpu().numpy(), d, k)
-    sizes = idx.list_sizes()
-    logical_bytes = int(sizes[probes.cpu().numpy()].sum()) * d * 4
+    pairs, alg_bytes, probed_rows = scan_work(sharded.local if sharded else idx,
+                                              probes.cpu().numpy(), d, k)
+    logical_bytes = pairs * d * 4
+    tf32_peak = tf32_gemm_peak(device) if rank == 0 else None
 
     nvtx = torch.cuda.nvtx
     nvtx.range_push("warmup")
@@ -246,9 +283,12 @@ def run_ours(args, cfg):
         cpu = cpu_baseline(idx, xq, cfg, args.cpu_sample)
 
     if rank == 0:
-        peak, peak_kind = measured_peaks()
+        hbm_peak, bf16_peak, peak_kind = measured_peaks()
         scan_avg_ms = scan_ms / max(scan_n, 1)
-        achieved = alg_bytes / (scan_avg_ms * 1e-3) / 1e9 if scan_n else None
+        scan_s = scan_avg_ms * 1e-3
+        # 3xTF32: three tensor-core products (hi*hi, hi*lo, lo*hi) of 2d flops per pair
+        tflops = 6.0 * d * pairs / scan_s / 1e12 if scan_n else None
+        gbs = alg_bytes / scan_s / 1e9 if scan_n else None
         value = nq * args.steps / (ms * 1e-3)
         line = {
             "metric": "IVFFlat queries/sec (list-scan HBM GB/s vs peak in roofline)",
@@ -273,16 +313,28 @@ def run_ours(args, cfg):
                 "probed_rows_per_step": probed_rows,
             },
             "roofline": {
-                "bound": "hbm",
-                "kernel": "scan_kernel (IVF list-major scan + warp top-k)",
-                "achieved": round(achieved, 1) if achieved else None,
-                "peak": peak,
-                "unit": "GB/s",
-                "frac": round(achieved / peak, 4) if achieved else None,
-                "peak_kind": f"{peak_kind} hbm_gbs",
-                "algorithmic_bytes_per_launch": alg_bytes,
+                "bound": "tensor",
+                "kernel": "tq_scan_kernel (IVF list-major 3xTF32 tcgen05 scan + fused top-k), "
+                          "all-probes pass",
+                "achieved": round(tflops, 2) if tflops else None,
+                "peak": round(tf32_peak, 1),
+                "unit": "TFLOP/s",
+                "frac": round(tflops / tf32_peak, 4) if tflops else None,
+                "peak_kind": "cuBLAS TF32 GEMM 8192^3 measured in this run (best of 10); "
+                             f"{peak_kind} bf16 {bf16_peak} TFLOP/s for context",
+                "algorithmic_flops_per_launch": 6 * d * pairs,
+                "pairs_per_launch": pairs,
                 "avg_launch_ms": round(scan_avg_ms, 4),
-                "traffic": None,
+                "traffic": TRAFFIC.get(args.config) if world == 1 else None,
+                "hbm": {
+                    "algorithmic_bytes_per_launch": alg_bytes,
+                    "achieved": round(gbs, 1) if gbs else None,
+                    "peak": hbm_peak,
+                    "unit": "GB/s",
+                    "frac": round(gbs / hbm_peak, 4) if gbs else None,
+                    "peak_kind": f"{peak_kind} hbm_gbs",
+                    "logical_scan_GBps": round(logical_bytes / scan_s / 1e9, 1) if scan_n else None,
+                },
             },
             "e2e": {
                 "value": round(nq * e2e_steps / (e2e_ms * 1e-3), 1),

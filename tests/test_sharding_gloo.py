@@ -1,0 +1,185 @@
+"""Host logic of the multi-GPU search on CPU ranks (torch.distributed gloo,
+world size 2): list and row partitioning, the all-gather layout of the partial
+results, sharded == single search (the intent of the reference's multi-GPU
+tests, python/metalfaiss/unittest/test_mlx_multi_gpu.py:49-65,86-119), and a
+rank that leaves before the exchange step.
+
+Each rank's local search is the oracle on its shard (the GPU kernels are not
+available on CPU); what is under test is the partitioning, the exchange and
+the merge order."""
+import multiprocessing as mp
+import os
+import socket
+import tempfile
+from datetime import timedelta
+
+import numpy as np
+import pytest
+import torch
+
+from metalfaiss_b200.sharding import gather_partials, lpt_partition, row_shard
+from oracle import oracle
+
+WORLD = 2
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _init(rank, port, timeout_s=20):
+    import torch.distributed as dist
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                            world_size=WORLD, timeout=timedelta(seconds=timeout_s))
+    return dist
+
+
+def _merge(pd, pi, k):
+    """(nq, parts, k) -> (nq, k) ascending by (distance, label); empty slots last."""
+    nq = pd.shape[0]
+    d = pd.reshape(nq, -1)
+    l = pi.reshape(nq, -1)
+    D = np.empty((nq, k), np.float32)
+    I = np.empty((nq, k), np.int64)
+    for q in range(nq):
+        lab = np.where(l[q] < 0, np.iinfo(np.int64).max, l[q])
+        o = np.lexsort((lab, d[q]))[:k]
+        D[q], I[q] = d[q][o], l[q][o]
+    return D, I
+
+
+def _flat_data():
+    rng = np.random.Generator(np.random.PCG64(7))
+    xb = rng.standard_normal((3001, 16)).astype(np.float32)
+    xq = rng.standard_normal((23, 16)).astype(np.float32)
+    return xb, xq
+
+
+def _flat_worker(rank, port, out_dir):
+    dist = _init(rank, port)
+    try:
+        xb, xq = _flat_data()
+        k = 9
+        b, e = row_shard(len(xb), rank, WORLD)
+        D, pos = oracle.flat_search(xq, xb[b:e], k)
+        I = pos + b  # global ids of a contiguous row shard
+        pd, pi = gather_partials(torch.from_numpy(D), torch.from_numpy(I))
+        assert tuple(pd.shape) == (len(xq), WORLD, k)
+        # slot r of the gathered layout is rank r's own contribution
+        assert np.array_equal(pi[:, rank].numpy(), I)
+        Dm, Im = _merge(pd.numpy(), pi.numpy(), k)
+        np.savez(os.path.join(out_dir, f"flat{rank}.npz"), D=Dm, I=Im)
+    finally:
+        dist.destroy_process_group()
+
+
+def _ivf_data():
+    rng = np.random.Generator(np.random.PCG64(11))
+    nlist, d = 24, 8
+    cents = (2.0 * rng.standard_normal((nlist, d))).astype(np.float32)
+    lab = rng.integers(0, nlist, 4000) ** 2 % nlist  # skewed list sizes
+    x = (cents[lab] + rng.standard_normal((4000, d))).astype(np.float32)
+    xq = (cents[rng.integers(0, nlist, 31)] + rng.standard_normal((31, d))).astype(np.float32)
+    offsets, vecs, ids = oracle.ivf_build(x, lab, nlist)
+    return cents, offsets, vecs, ids, xq
+
+
+def _ivf_worker(rank, port, out_dir):
+    dist = _init(rank, port)
+    try:
+        cents, offsets, vecs, ids, xq = _ivf_data()
+        nprobe, k = 5, 7
+        owners = lpt_partition(np.diff(offsets), WORLD)
+        probes = oracle.coarse_probes(xq, cents, nprobe)  # replicated quantizer
+        local = np.where(owners[probes] == rank, probes, -1)  # scan only owned lists
+        D, I = oracle.ivf_search(xq, cents, offsets, vecs, ids, nprobe, k, probes=local)
+        pd, pi = gather_partials(torch.from_numpy(D), torch.from_numpy(I))
+        Dm, Im = _merge(pd.numpy(), pi.numpy(), k)
+        np.savez(os.path.join(out_dir, f"ivf{rank}.npz"), D=Dm, I=Im)
+    finally:
+        dist.destroy_process_group()
+
+
+def _leaving_worker(rank, port, out_dir):
+    """Rank 1 leaves between steps (after set-up, before the exchange); rank 0
+    must get an error from its next collective instead of waiting forever."""
+    dist = _init(rank, port, timeout_s=5)
+    if rank == 1:
+        os._exit(3)
+    msg = "no error"
+    try:
+        gather_partials(torch.zeros(4, 3), torch.zeros(4, 3, dtype=torch.int64))
+    except Exception as e:  # the failure surfaces on the host as an exception
+        msg = f"raised {type(e).__name__}"
+    with open(os.path.join(out_dir, "leave0.txt"), "w") as f:
+        f.write(msg)
+    os._exit(0)
+
+
+def _run(target, out_dir, limit_s=120):
+    ctx = mp.get_context("spawn")
+    port = _free_port()
+    procs = [ctx.Process(target=target, args=(r, port, out_dir)) for r in range(WORLD)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(limit_s)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+            p.join()
+    return [p.exitcode for p in procs]
+
+
+def test_lpt_partition_covers_and_balances():
+    rng = np.random.Generator(np.random.PCG64(3))
+    sizes = (rng.pareto(1.2, 5000) * 100).astype(np.int64)
+    for world in (1, 2, 4, 8):
+        owners = lpt_partition(sizes, world)
+        assert owners.shape == sizes.shape and owners.min() >= 0 and owners.max() < world
+        load = np.bincount(owners, weights=sizes, minlength=world)
+        # greedy LPT: the heaviest rank exceeds the lightest by at most one list
+        assert load.max() - load.min() <= sizes.max()
+
+
+def test_row_shard_is_a_partition():
+    for n in (0, 1, 7, 1000, 1001):
+        for world in (1, 2, 3, 8):
+            spans = [row_shard(n, r, world) for r in range(world)]
+            assert spans[0][0] == 0 and spans[-1][1] == n
+            assert all(spans[r][1] == spans[r + 1][0] for r in range(world - 1))
+            sizes = [e - b for b, e in spans]
+            assert max(sizes) - min(sizes) <= 1
+
+
+def test_sharded_flat_equals_single_gloo():
+    with tempfile.TemporaryDirectory() as tmp:
+        assert _run(_flat_worker, tmp) == [0, 0]
+        xb, xq = _flat_data()
+        D_ref, I_ref = oracle.flat_search(xq, xb, 9)
+        for r in range(WORLD):
+            z = np.load(os.path.join(tmp, f"flat{r}.npz"))
+            assert np.array_equal(z["I"], I_ref)
+            assert np.array_equal(z["D"], D_ref)
+
+
+def test_sharded_ivf_equals_single_gloo():
+    with tempfile.TemporaryDirectory() as tmp:
+        assert _run(_ivf_worker, tmp) == [0, 0]
+        cents, offsets, vecs, ids, xq = _ivf_data()
+        D_ref, I_ref = oracle.ivf_search(xq, cents, offsets, vecs, ids, 5, 7)
+        for r in range(WORLD):
+            z = np.load(os.path.join(tmp, f"ivf{r}.npz"))
+            assert np.array_equal(z["I"], I_ref)
+            assert np.allclose(z["D"], D_ref, rtol=0, atol=0)
+
+
+def test_rank_leaving_before_exchange_is_reported_gloo():
+    with tempfile.TemporaryDirectory() as tmp:
+        codes = _run(_leaving_worker, tmp, limit_s=90)
+        assert codes == [0, 3]
+        with open(os.path.join(tmp, "leave0.txt")) as f:
+            assert f.read().startswith("raised"), "rank 0 did not see the failure"
