@@ -495,17 +495,13 @@ void plan_splits(FlatPlan& p, int64_t nq, int64_t nb, int k, int device, int tq,
 }  // namespace
 
 FlatPlan plan_flat(int64_t nq, int64_t nb, int d, int k, int device, int tq) {
-  FlatPlan p;
   const int kcap = scan_kcap(k) ? scan_kcap(k) : 256;
-  if (tq == 32) {
-    plan_splits(p, nq, nb, k, device, 32, kcap >= 256 ? 1 : (kcap >= 128 ? 2 : 3));
-  } else {
-    plan_splits(p, nq, nb, k, device, tq, 0);
-  }
+  FlatPlan simt, tc;
+  plan_splits(simt, nq, nb, k, device, 32, kcap >= 256 ? 1 : (kcap >= 128 ? 2 : 3));
+  plan_splits(tc, nq, nb, k, device, tc_group(), 0);
+  FlatPlan p = tq == 32 ? simt : tc;
   // workspace: the larger of the two engines' needs
-  FlatPlan other;
-  plan_splits(other, nq, nb, k, device, tq == 32 ? tc_group() : 32, 1);
-  const int max_splits = p.splits > other.splits ? p.splits : other.splits;
+  const int max_splits = simt.splits > tc.splits ? simt.splits : tc.splits;
   Carver c(nullptr, 0);
   c.take<float>(nq);                        // query norms
   c.take<int>(1);                           // work counter
@@ -526,6 +522,7 @@ int run_flat_topk(int device, cudaStream_t stream, const float* xq, int64_t nq, 
   // carve with the same order as plan_flat (partials sized for either engine)
   FlatPlan other = plan_flat(nq, nb, d, k, device, tc ? 32 : tc_group());
   const int max_splits = p.splits > other.splits ? p.splits : other.splits;
+  MF_CHECK(other.bytes == p.bytes, MF_ERR_ASSERTION, "flat plan sizes disagree");
   Carver c(ws, ws_bytes);
   float* qn = c.take<float>(nq);
   int* counter = c.take<int>(1);

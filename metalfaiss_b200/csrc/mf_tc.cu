@@ -18,9 +18,9 @@
 //              per-thread top-k list in shared memory;
 //   warp 4     TMA producer (one lane);
 //   warp 5     TMEM allocation and MMA issue (one lane).
-// Stages flow full -> MMA -> empty; accumulators flow accf -> epilogue -> acce,
-// two of each so the epilogue of tile t overlaps the MMAs of tile t+1. Every
-// wait is bounded (mf_sm100.cuh).
+// Stages flow full -> MMA -> empty; accumulators flow accf -> epilogue -> acce
+// through 512 / BN TMEM buffers, so the MMAs run up to that many tiles ahead of
+// the epilogue. Every wait is bounded (mf_sm100.cuh).
 #include <cudaTypedefs.h>
 
 #include <mutex>
@@ -45,8 +45,16 @@ __device__ unsigned long long g_tc_prof[16];
     expr;                                                  \
     atomicAdd(&g_tc_prof[i], (unsigned long long)(clock64() - _t0)); \
   } while (0)
+// Epilogue thread 0 accumulates into locals (TQL) and adds them once at exit.
+#define TQL(var, expr)                 \
+  do {                                 \
+    const long long _t0 = clock64();   \
+    expr;                              \
+    var += clock64() - _t0;            \
+  } while (0)
 #else
 #define TQP(i, expr) expr
+#define TQL(var, expr) expr
 #endif
 
 using namespace sm100;
@@ -57,6 +65,9 @@ constexpr int kTqEpiThreads = 128;
 constexpr int kTqMaxD = 1024;
 constexpr int kTqK = 32;  // list slots per query row (k <= 32)
 constexpr int kTqMaxSmem = 227 * 1024 - 512;
+// All 512 TMEM columns hold accumulators: 512 / BN tiles in flight between
+// the MMA warp and the epilogue (4 at BN = 128).
+constexpr int kTqTmemCols = 512;
 
 struct TqLayout {
   int SA, KB, BN;
@@ -82,7 +93,7 @@ TqLayout tq_layout(int d, int kcap, int BN, int SA) {
   s.xn = o;
   o += size_t(2) * BN * 4;
   s.bars = o;
-  o += size_t(2 * SA + 4) * 8 + 16;
+  o += size_t(2 * SA + 2 * (kTqTmemCols / BN)) * 8 + 16;
   s.total = o + 1024;
   return s;
 }
@@ -129,10 +140,34 @@ __device__ __forceinline__ ItemDesc item_desc(const ScanArgs& a, int item) {
   return it;
 }
 
+// Accept mask of a 32-column chunk: bit j is set iff column j's distance is
+// <= thr_d (the row's current k-th distance, its bound, or +inf while open)
+// and j < nvalid. For L2, t = (qn + xn) - 2 dot is formed as l2_from_dot forms
+// it before its clamp at 0 (doubling is exact, so the FMA rounds once, like the
+// subtraction); thr_d >= 0, so t <= thr_d iff the clamped distance is. The
+// sign bit of thr_d - t (+0 when equal) is shifted into the reject mask, one
+// funnel shift per column.
+template <int METRIC>
+__device__ __forceinline__ unsigned int tq_accept(const uint32_t (&r)[32], const float* xs,
+                                                  float qn, float thr_d, int nvalid) {
+  unsigned int rej = 0;
+#pragma unroll
+  for (int j = 31; j >= 0; --j) {
+    const float dot = __uint_as_float(r[j]);
+    float diff;
+    if (METRIC == MF_METRIC_L2) diff = __fsub_rn(thr_d, fmaf(-2.0f, dot, __fadd_rn(qn, xs[j])));
+    else diff = __fadd_rn(thr_d, dot);
+    rej = __funnelshift_l(__float_as_uint(diff), rej, 1);
+  }
+  const unsigned int in_range = nvalid >= 32 ? 0xffffffffu : ((1u << nvalid) - 1u);
+  return ~rej & in_range;
+}
+
 template <int METRIC, int BN>
 __global__ void __launch_bounds__(kTqThreads, 1)
     tq_scan_kernel(const ScanArgs a, const __grid_constant__ TqMaps maps, const TqLayout L) {
   extern __shared__ unsigned char smem_raw[];
+  constexpr int NACC = kTqTmemCols / BN;
   unsigned char* base = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   unsigned long long* lists = reinterpret_cast<unsigned long long*>(base + L.lists);
@@ -141,8 +176,8 @@ __global__ void __launch_bounds__(kTqThreads, 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(base + L.bars);
   uint64_t* empty = full + L.SA;
   uint64_t* accf = empty + L.SA;
-  uint64_t* acce = accf + 2;
-  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(acce + 2);
+  uint64_t* acce = accf + NACC;
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(acce + NACC);
   int* s_abort = reinterpret_cast<int*>(s_tmem + 1);
   uint32_t* s_seq = reinterpret_cast<uint32_t*>(s_abort + 1);  // [0] consumed, [1] issued
 
@@ -159,7 +194,7 @@ __global__ void __launch_bounds__(kTqThreads, 1)
   const long long _tk = clock64();
 #endif
   if (warp == 5) {
-    tmem_alloc(s_tmem, 2 * BN);
+    tmem_alloc(s_tmem, kTqTmemCols);
     tmem_relinquish();
   }
   if (tid == 0) {
@@ -167,7 +202,7 @@ __global__ void __launch_bounds__(kTqThreads, 1)
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], 1);
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < NACC; ++i) {
       mbar_init(&accf[i], 1);
       mbar_init(&acce[i], kTqEpiThreads);
     }
@@ -224,8 +259,9 @@ __global__ void __launch_bounds__(kTqThreads, 1)
         const long long nrows = it.re > it.rb ? it.re - it.rb : 0;
         const int nT = (int)((nrows + BN - 1) / BN);
         for (int t = 0; t < nT; ++t, ++tt) {
-          const int b = tt & 1;
-          if (tt >= 2) TQP(1, mbar_wait(&acce[b], ((tt >> 1) - 1) & 1, s_abort, &g_device_error));
+          const int b = tt % NACC;
+          if (tt >= (uint32_t)NACC)
+            TQP(1, mbar_wait(&acce[b], ((tt / NACC) - 1) & 1, s_abort, &g_device_error));
           tc_fence_after();
           const uint32_t dt = tmem + b * BN;
           for (int kb = 0; kb < KB; ++kb, ++seq) {
@@ -265,35 +301,81 @@ __global__ void __launch_bounds__(kTqThreads, 1)
     // buffer. A full buffer is sorted and merged by the whole warp into the
     // row's top-k list (sorted, one key per lane, in shared memory).
     uint32_t tt = 0;
+#ifdef MF_TC_PROFILE
+    long long p_wait = 0, p_loop = 0, p_merge = 0, p_tiles = 0, p_nmerge = 0, p_out = 0;
+    const long long p_start = clock64();
+#endif
     unsigned long long* my_lists = lists + (size_t)(warp * 32) * kTqK;
     unsigned long long* my_bufs = cbuf + (size_t)(warp * 32) * 33;
     unsigned long long* own_buf = my_bufs + lane * 33;
-    // Warp merge of row src's buffered candidates (count n) into its list.
-    auto merge_row = [&](int src, int n, unsigned long long& thr_reg, unsigned long long bnd) {
-      unsigned long long c = lane < n ? my_bufs[src * 33 + lane] : kEmptyKey;
-      unsigned long long* lq = my_lists + (size_t)src * kTqK;
-      const unsigned long long e = lq[lane];  // ascending; kEmpty past k
-      c = warp_sort32(c, lane);
-      // the 32 smallest of e and c: elementwise min against c reversed is
-      // bitonic; five half-cleaners sort it ascending
-      unsigned long long x = __shfl_sync(0xffffffffu, c, 31 - lane);
-      x = e < x ? e : x;
-#pragma unroll
-      for (int st = 16; st > 0; st >>= 1) {
-        const unsigned long long o = __shfl_xor_sync(0xffffffffu, x, st);
-        x = (lane & st) ? (x > o ? x : o) : (x < o ? x : o);
+    // Merges the buffered candidates of the rows in `who` (a warp-uniform
+    // lane mask) into their sorted lists, two rows at a time so the shuffles
+    // of the two sorting networks overlap. Each merged row's lane clears its
+    // count and lowers its threshold to min(new k-th key, bound).
+    auto merge_rows = [&](unsigned int who, int& cnt_reg, unsigned long long& thr_reg,
+                          unsigned long long bnd) {
+      while (who) {
+        const int s0 = __ffs(who) - 1;
+        who &= who - 1;
+        int s1 = -1;
+        if (who) {
+          s1 = __ffs(who) - 1;
+          who &= who - 1;
+        }
+        const int s1r = s1 < 0 ? s0 : s1;
+        const int n0 = __shfl_sync(0xffffffffu, cnt_reg, s0);
+        const int n1 = s1 < 0 ? 0 : __shfl_sync(0xffffffffu, cnt_reg, s1r);
+        unsigned long long c[2], x[2];
+        c[0] = lane < n0 ? my_bufs[s0 * 33 + lane] : kEmptyKey;
+        c[1] = lane < n1 ? my_bufs[s1r * 33 + lane] : kEmptyKey;
+        unsigned long long* l0 = my_lists + (size_t)s0 * kTqK;
+        unsigned long long* l1 = my_lists + (size_t)s1r * kTqK;
+        const unsigned long long e0 = l0[lane];  // ascending; kEmpty past k
+        const unsigned long long e1 = l1[lane];
+        warp_sort32_n<2>(c, lane);
+        // the 32 smallest of a list and a sorted batch: elementwise min against
+        // the batch reversed is bitonic; five half-cleaners sort it ascending
+        x[0] = __shfl_sync(0xffffffffu, c[0], 31 - lane);
+        x[1] = __shfl_sync(0xffffffffu, c[1], 31 - lane);
+        x[0] = e0 < x[0] ? e0 : x[0];
+        x[1] = e1 < x[1] ? e1 : x[1];
+        warp_bitonic_clean32_n<2>(x, lane);
+        if (lane >= k) x[0] = x[1] = kEmptyKey;
+        l0[lane] = x[0];
+        if (s1 >= 0) l1[lane] = x[1];
+        const unsigned long long nk0 = __shfl_sync(0xffffffffu, x[0], k - 1);
+        const unsigned long long nk1 = __shfl_sync(0xffffffffu, x[1], k - 1);
+        if (lane == s0) {
+          thr_reg = nk0 < bnd ? nk0 : bnd;
+          cnt_reg = 0;
+        }
+        if (lane == s1) {
+          thr_reg = nk1 < bnd ? nk1 : bnd;
+          cnt_reg = 0;
+        }
+        __syncwarp();
       }
-      if (lane >= k) x = kEmptyKey;
-      lq[lane] = x;
-      const unsigned long long nk = __shfl_sync(0xffffffffu, x, k - 1);
-      if (lane == src) thr_reg = nk < bnd ? nk : bnd;
-      __syncwarp();
+    };
+    // Row norms (L2) are loaded one tile ahead into registers, so their global
+    // load latency overlaps the previous tile's epilogue. pf_r0 tags the tile
+    // the registers hold; a mismatch (first tile, an empty item) reloads.
+    constexpr int kPf = BN / kTqEpiThreads;
+    float xn_pf[kPf];
+    long long pf_r0 = -1;
+    auto load_norms = [&](long long r0, long long re) {
+#pragma unroll
+      for (int i = 0; i < kPf; ++i) {
+        const long long r = r0 + tid + i * kTqEpiThreads;
+        xn_pf[i] = r < re ? a.xnorms[r] : 0.0f;
+      }
+      pf_r0 = r0;
     };
     for (int item = blockIdx.x; item < total && !*s_abort; item += gridDim.x) {
       const ItemDesc it = item_desc(a, item);
       const long long nrows = it.re > it.rb ? it.re - it.rb : 0;
       const int nT = (int)((nrows + BN - 1) / BN);
       const bool valid = tid < it.nq_item;
+      const int nitem = item + gridDim.x;
       long long slot = -1;
       int q = 0;
       if (valid) {
@@ -315,67 +397,79 @@ __global__ void __launch_bounds__(kTqThreads, 1)
       int cnt = 0;
 
       for (int t = 0; t < nT; ++t, ++tt) {
-        const int b = tt & 1;
+        const int b = tt % NACC;
         const long long r0 = it.rb + (long long)t * BN;
         if (METRIC == MF_METRIC_L2) {
           // row norms of this tile, shared by the four epilogue warps
-          float* xs = xn_s + b * BN;
-          for (int c = tid; c < BN; c += kTqEpiThreads) {
-            const long long r = r0 + c;
-            xs[c] = r < it.re ? a.xnorms[r] : 0.0f;
-          }
+          if (pf_r0 != r0) load_norms(r0, it.re);
+          float* xs = xn_s + (tt & 1) * BN;
+#pragma unroll
+          for (int i = 0; i < kPf; ++i) xs[tid + i * kTqEpiThreads] = xn_pf[i];
           named_sync(1, kTqEpiThreads);
+          // issue the next tile's loads now; they land while this tile runs
+          if (t + 1 < nT) {
+            load_norms(r0 + BN, it.re);
+          } else if (nitem < total) {
+            const ItemDesc nx = item_desc(a, nitem);
+            if (nx.re > nx.rb) load_norms(nx.rb, nx.re);
+          }
         }
-        mbar_wait(&accf[b], (tt >> 1) & 1, s_abort, &g_device_error);
+        TQL(p_wait, mbar_wait(&accf[b], (tt / NACC) & 1, s_abort, &g_device_error));
+#ifdef MF_TC_PROFILE
+        ++p_tiles;
+#endif
         tc_fence_after();
-        const float* xs = xn_s + b * BN;
-#pragma unroll 1
-        for (int c0 = 0; c0 < BN; c0 += 32) {
-          float v[32];
-          tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + b * BN + c0, v);
-          // Branch-free pass: which of the 32 columns may beat this row's k-th key.
+        const float* xs = xn_s + (tt & 1) * BN;
+        // One 32-column chunk: filter, merge rows that would overflow, append.
+        auto chunk = [&](uint32_t (&r)[32], int c0) {
           const long long rc = r0 + c0;
-          const bool open = thr == kEmptyKey;  // fewer than k candidates and no bound
-          const float thr_d = open ? 0.0f : key_dist(thr);
-          unsigned int m = 0;
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            float dist;
-            if (METRIC == MF_METRIC_L2) dist = l2_from_dot(qn, xs[c0 + j], v[j]);
-            else dist = -v[j];
-            v[j] = dist;
-            m |= ((open || dist <= thr_d) && rc + j < it.re) ? (1u << j) : 0u;
+          const long long left = it.re - rc;
+          const int nvalid = left >= 32 ? 32 : (left > 0 ? (int)left : 0);
+          const float thr_d = thr == kEmptyKey ? __int_as_float(0x7f800000) : key_dist(thr);
+          unsigned int acc = tq_accept<METRIC>(r, xs + c0, qn, thr_d, nvalid);
+          if (!valid) acc = 0;
+          const unsigned int over = __ballot_sync(0xffffffffu, cnt + __popc(acc) > 32);
+          if (over) {
+            TQL(p_merge, merge_rows(over, cnt, thr, bound));
+#ifdef MF_TC_PROFILE
+            p_nmerge += __popc(over);
+#endif
           }
-          if (!valid) m = 0;
-          // rows whose buffer cannot take this chunk's survivors merge first
-          unsigned int who = __ballot_sync(0xffffffffu, cnt + __popc(m) > 32);
-          while (who) {
-            const int src = __ffs(who) - 1;
-            who &= who - 1;
-            const int n = __shfl_sync(0xffffffffu, cnt, src);
-            const unsigned long long bs = __shfl_sync(0xffffffffu, bound, src);
-            merge_row(src, n, thr, bs);
-            if (lane == src) cnt = 0;
-          }
-          if (m) {
+          if (acc) {
 #pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if ((m >> j) & 1u) own_buf[cnt++] = make_key(v[j], (unsigned int)(rc + j));
+            for (int j = 0; j < 32; ++j) {
+              if ((acc >> j) & 1u) {
+                const float dot = __uint_as_float(r[j]);
+                const float dist =
+                    METRIC == MF_METRIC_L2 ? l2_from_dot(qn, xs[c0 + j], dot) : -dot;
+                own_buf[cnt++] = make_key(dist, (unsigned int)(rc + j));
+              }
+            }
           }
           __syncwarp();
+        };
+        // TMEM loads are double-buffered: chunk c+1 loads while c is filtered.
+        const uint32_t tb = tmem + ((uint32_t)(warp * 32) << 16) + b * BN;
+        uint32_t ra[32], rb[32];
+        tmem_ld32_async(tb, ra);
+#pragma unroll 1
+        for (int c0 = 0; c0 < BN; c0 += 64) {
+          tmem_wait_ld(ra);
+          tmem_ld32_async(tb + c0 + 32, rb);
+          chunk(ra, c0);
+          tmem_wait_ld(rb);
+          if (c0 + 64 < BN) tmem_ld32_async(tb + c0 + 64, ra);
+          chunk(rb, c0 + 32);
         }
         tc_fence_before();
         mbar_arrive(&acce[b]);
       }
       // flush the remaining candidates, then write each row's k keys
-      unsigned int who = __ballot_sync(0xffffffffu, cnt > 0);
-      while (who) {
-        const int src = __ffs(who) - 1;
-        who &= who - 1;
-        const int n = __shfl_sync(0xffffffffu, cnt, src);
-        const unsigned long long bs = __shfl_sync(0xffffffffu, bound, src);
-        merge_row(src, n, thr, bs);
-      }
+#ifdef MF_TC_PROFILE
+      const long long p_o0 = clock64();
+#endif
+      const unsigned int pending = __ballot_sync(0xffffffffu, cnt > 0);
+      if (pending) merge_rows(pending, cnt, thr, bound);
       for (int qq = 0; qq < 32; ++qq) {
         const long long sq = __shfl_sync(0xffffffffu, slot, qq);
         if (sq < 0) continue;
@@ -396,7 +490,21 @@ __global__ void __launch_bounds__(kTqThreads, 1)
         }
       }
       __syncwarp();
+#ifdef MF_TC_PROFILE
+      p_out += clock64() - p_o0;
+#endif
     }
+#ifdef MF_TC_PROFILE
+    p_loop = clock64() - p_start;
+    if (tid == 0) {
+      atomicAdd(&g_tc_prof[3], (unsigned long long)p_wait);
+      atomicAdd(&g_tc_prof[4], (unsigned long long)p_loop);
+      atomicAdd(&g_tc_prof[5], (unsigned long long)p_tiles);
+      atomicAdd(&g_tc_prof[7], (unsigned long long)p_merge);
+      atomicAdd(&g_tc_prof[11], (unsigned long long)p_nmerge);
+      atomicAdd(&g_tc_prof[12], (unsigned long long)p_out);
+    }
+#endif
   }
 
   // ---- teardown: stages in flight land and MMAs finish before TMEM is freed
@@ -409,7 +517,7 @@ __global__ void __launch_bounds__(kTqThreads, 1)
       mbar_wait(&full[seq % SA], (seq / SA) & 1, &dummy, &g_device_error);
   }
   __syncthreads();
-  if (warp == 5) tmem_dealloc(tmem, 2 * BN);
+  if (warp == 5) tmem_dealloc(tmem, kTqTmemCols);
 #ifdef MF_TC_PROFILE
   if (tid == 0) atomicAdd(&g_tc_prof[13], (unsigned long long)(clock64() - _tk));
 #endif
