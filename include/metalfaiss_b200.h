@@ -98,8 +98,9 @@ MF_API int mf_flat_search_workspace_size(int64_t nq, int64_t nb, int d, int metr
 /* Exact kNN of xq (nq,d) against xb (nb,d): distances/labels (nq,k), ascending.
  * labels[i,j] = ids[pos] when ids != NULL, else the row position pos.
  * xb_norms (nb) is required for L2 and ignored otherwise. xb_lo (nb,d), optional,
- * is mf_tf32_residual(xb): when given, L2 / inner-product searches with 32 <= d and
- * k <= 64 run on the tensor cores (3xTF32), otherwise on the SIMT scan.
+ * is mf_tf32_residual(xb): when given, L2 / inner-product searches with
+ * 32 <= d <= 1024, k <= 32 and nb >= 256 run on the tensor cores (3xTF32),
+ * otherwise on the SIMT scan.
  * k is clipped by the caller to nb (python/metalfaiss/utils/sorting.py:66-67); here
  * slots beyond nb are padded (+inf, -1).
  * Replaces FlatIndex.search, python/metalfaiss/indexflat.py:70-110 (pairwise_L2sqr
@@ -281,8 +282,10 @@ MF_API int64_t mf_launch_count(void);
 
 /* Scan engine for the L2 / inner-product top-k scans: 0 = automatic (tensor
  * cores where the shape allows), 1 = SIMT only, 2 = tensor cores where the
- * shape allows. Mirrors the reference's kernel switches
- * (python/metalfaiss/faissmlx/flags.py:20-35). Process-wide. */
+ * shape allows, 3 = as 2 but with the query tile streamed through shared
+ * memory even where it fits in tensor memory (d <= 128). Mirrors the
+ * reference's kernel switches (python/metalfaiss/faissmlx/flags.py:20-35).
+ * Process-wide. */
 MF_API int mf_set_scan_engine(int engine);
 
 /* Reads and clears the device-side error word of `device` (MF_ERR_TIMEOUT if a

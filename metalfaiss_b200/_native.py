@@ -151,7 +151,8 @@ def timing_read(kernel: str):
 
 
 def set_scan_engine(engine: int) -> None:
-    """0 automatic, 1 SIMT only, 2 tensor cores where eligible (process-wide)."""
+    """0 automatic, 1 SIMT only, 2 tensor cores where eligible, 3 = 2 with the
+    query tile streamed through shared memory (process-wide)."""
     call("mf_set_scan_engine", int(engine))
 
 

@@ -190,7 +190,10 @@ int ivf_scan_topk(int device, cudaStream_t stream, const IvfWs& w, const float* 
                              nullptr, group, stream, 0, bounding ? 1 : P));
     a.max_rows = bounding ? kBoundRows : 0;
     a.bound = (phases == 2 && ph == 1) ? w.bound : nullptr;
-    if (tc) {
+    if (tc && tc_raw_queries(d, k)) {
+      // the scan loads each item's queries itself (through a.pairs)
+      MF_TRY(launch_tc_scan(a, metric, nullptr, nq, list_lo, ntotal, nq * P, device, stream));
+    } else if (tc) {
       // A operand: the queries of every (query, probe) pair, gathered in list order
       MF_TRY(launch_gather_queries(xq, d, w.g.pairs, w.g.pair_offsets + nlist, nq * P, P, w.g_hi,
                                    w.g_lo, stream));
@@ -727,7 +730,7 @@ int mf_tf32_residual(int device, void* stream, const float* x, int64_t n, int d,
 
 int mf_set_scan_engine(int engine) {
   clear_error();
-  MF_CHECK(engine >= 0 && engine <= 2, MF_ERR_INVALID_ARGS, "engine %d not in {0,1,2}", engine);
+  MF_CHECK(engine >= 0 && engine <= 3, MF_ERR_INVALID_ARGS, "engine %d not in {0,1,2,3}", engine);
   set_scan_engine(engine);
   return MF_OK;
 }

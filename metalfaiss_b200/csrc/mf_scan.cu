@@ -549,9 +549,10 @@ int run_flat_topk(int device, cudaStream_t stream, const float* xq, int64_t nq, 
   a.out_d = p.splits > 1 ? pd : D;
   a.out_l = p.splits > 1 ? pl : I;
   if (tc) {
-    MF_TRY(launch_tf32_residual(xq, nq, d, q_lo, stream));
-    MF_TRY(launch_tc_scan(a, metric, q_lo, nq, xb_lo, nb, (int64_t)p.nqt * p.splits, device,
-                          stream));
+    const bool raw = tc_raw_queries(d, k);  // else the scan streams (xq, q_lo) tiles
+    if (!raw) MF_TRY(launch_tf32_residual(xq, nq, d, q_lo, stream));
+    MF_TRY(launch_tc_scan(a, metric, raw ? nullptr : q_lo, nq, xb_lo, nb,
+                          (int64_t)p.nqt * p.splits, device, stream));
   } else {
     MF_TRY(launch_scan(a, metric, kEpiTopK, (int64_t)p.nqt * p.splits, device, stream));
   }

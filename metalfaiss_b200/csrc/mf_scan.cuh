@@ -64,6 +64,10 @@ struct ScanArgs {
 // of tc_group() queries; a.xq / a.xb are the fp32 (hi) operands, a_lo / b_lo
 // their tf32 residuals, a_rows / b_rows their row counts.
 bool tc_eligible(int metric, int d, int k, int64_t xb_rows);
+// True when the tensor-core scan keeps the query tile in tensor memory
+// (d <= 128): it then reads raw fp32 queries (a.xq, rows of a.d floats; for
+// IVF through a.pairs) and needs neither a_lo nor gathered query rows.
+bool tc_raw_queries(int d, int k);
 int tc_group();
 int launch_tc_scan(const ScanArgs& a, int metric, const float* a_lo, int64_t a_rows,
                    const float* b_lo, int64_t b_rows, int64_t total_items, int device,

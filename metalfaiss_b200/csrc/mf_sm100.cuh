@@ -11,12 +11,16 @@ namespace mf {
 namespace sm100 {
 
 constexpr int kErrWaitTimeout = 1;
-// Each try_wait suspends the thread until the phase completes or the hint
-// (kWaitHintNs) expires, so a waiting thread does not spin on the shared
-// memory pipe; the iteration bound turns a lost arrival into an error after
-// about kWaitLimit * kWaitHintNs (~2.5 s) instead of a hang.
-constexpr unsigned kWaitHintNs = 10000000u;
-constexpr unsigned kWaitLimit = 256;
+// Each try_wait may suspend the thread until the phase completes or a time
+// limit passes (kWaitHintNs is only a hint: the hardware may return much
+// sooner), so a waiting thread does not spin on the shared memory pipe. A wait
+// gives up after kWaitLimitNs of %globaltimer time, or after kWaitMaxIters
+// polls whatever the timer says, and turns a lost arrival into an error
+// instead of a hang. Legitimate waits (a role idling through a long item) are
+// well under a millisecond.
+constexpr unsigned kWaitHintNs = 1000000u;
+constexpr unsigned long long kWaitLimitNs = 2000000000ull;
+constexpr unsigned kWaitMaxIters = 1u << 26;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -45,15 +49,27 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+__device__ __forceinline__ unsigned long long globaltimer_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
 // Bounded wait: returns false (and records kErrWaitTimeout in *err) if the
-// phase never completes; `abort` lets the caller skip further waits once one
-// has failed.
+// phase does not complete within the limits above; `abort` (shared by the
+// CTA's roles) is raised then, and a wait that sees it raised by another role
+// returns false at once, so every role leaves its loop.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* abort, int* err) {
-  if (*abort) return false;
-  for (unsigned i = 0; i < kWaitLimit; ++i)
+  if (*(volatile int*)abort) return false;
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = globaltimer_ns();
+  for (unsigned i = 0; i < kWaitMaxIters; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
+    if (*(volatile int*)abort) return false;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) break;
+  }
   if (err) atomicExch(err, kErrWaitTimeout);
-  *abort = 1;
+  *(volatile int*)abort = 1;
   return false;
 }
 
@@ -107,6 +123,35 @@ __device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t a_desc, uint6
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate ? 1u : 0u)
       : "memory");
 }
+// D[tmem] (+)= A[tmem] * B[smem]^T, kind::tf32, A read from tensor memory
+// (row i of A in lane i, one 32-bit element per column), issued by one thread.
+__device__ __forceinline__ void mma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                            uint32_t idesc, bool accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate ? 1u : 0u)
+      : "memory");
+}
+
+// Stores 32 consecutive 32-bit TMEM columns of this thread's lane (32x32b shape).
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),
+      "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
+      "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
 // Arrives once on `bar` when every MMA this thread issued so far has completed.
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(

@@ -12,7 +12,7 @@
 // the database, once per search for the queries. Per K-step of 8:
 //   D += A.B  +  A.B_lo  +  A_lo.B      (the dropped A_lo.B_lo term is ~2^-22)
 //
-// Warp roles (192 threads, one CTA per SM, items assigned round-robin):
+// Warp roles (192 threads, one persistent CTA per SM, items taken dynamically):
 //   warps 0-3  epilogue: thread t owns query row t of the tile (TMEM lane t),
 //              reads its BN dot products, forms distances and keeps a sorted
 //              per-thread top-k list in shared memory;
@@ -23,6 +23,7 @@
 // the epilogue. Every wait is bounded (mf_sm100.cuh).
 #include <cudaTypedefs.h>
 
+#include <cstring>
 #include <mutex>
 
 #include "mf_scan.cuh"
@@ -68,21 +69,45 @@ constexpr int kTqMaxSmem = 227 * 1024 - 512;
 // All 512 TMEM columns hold accumulators: 512 / BN tiles in flight between
 // the MMA warp and the epilogue (4 at BN = 128).
 constexpr int kTqTmemCols = 512;
+// Work items are taken from a global counter by the producer (largest items
+// first, as the item arrays are ordered) and handed to the MMA warp and the
+// epilogue warps through a ring of kTqQueue shared-memory slots. The ring is
+// deeper than the tiles the producer can run ahead (stages + accumulators),
+// so a run of one-tile items never stalls it.
+constexpr int kTqQueue = 16;
+constexpr int kTqMaxAcc = 4;
+// With the query tile resident in tensor memory (d <= 128), warps 6-9 load
+// it: 320 threads. Otherwise the query tile streams with the rows: 192.
+constexpr int kTqThreadsAtm = 320;
+constexpr int kTqMaxDAtm = 128;
 
 struct TqLayout {
   int SA, KB, BN;
+  int atm;   // query tile in tensor memory (columns [0, 2*KB*32): hi then lo)
+  int nacc;  // accumulator buffers in tensor memory
+  int acc0;  // first accumulator column
   size_t stage, a_hi, a_lo, b_hi, b_lo;  // offsets within a stage
   size_t lists, scratch, xn, bars, total;
 };
 
-TqLayout tq_layout(int d, int kcap, int BN, int SA) {
+TqLayout tq_layout(int d, int kcap, int BN, int SA, bool atm) {
   TqLayout s;
   s.SA = SA;
   s.KB = (d + 31) / 32;
   s.BN = BN;
-  s.a_hi = 0;
-  s.a_lo = kTqM * 128;
-  s.b_hi = 2 * kTqM * 128;
+  s.atm = atm ? 1 : 0;
+  if (atm) {
+    s.a_hi = s.a_lo = 0;  // unused: the query tile lives in tensor memory
+    s.b_hi = 0;
+    s.acc0 = 2 * s.KB * 32;
+  } else {
+    s.a_hi = 0;
+    s.a_lo = kTqM * 128;
+    s.b_hi = 2 * kTqM * 128;
+    s.acc0 = 0;
+  }
+  s.nacc = (kTqTmemCols - s.acc0) / BN;
+  if (s.nacc > kTqMaxAcc) s.nacc = kTqMaxAcc;
   s.b_lo = s.b_hi + size_t(BN) * 128;
   s.stage = s.b_lo + size_t(BN) * 128;
   size_t o = size_t(SA) * s.stage;
@@ -90,10 +115,10 @@ TqLayout tq_layout(int d, int kcap, int BN, int SA) {
   o += size_t(kTqM) * kcap * 8;
   s.scratch = o;  // candidate buffers: 128 rows x 33 keys (one row per query row)
   o += size_t(kTqM) * 33 * 8;
-  s.xn = o;
-  o += size_t(2) * BN * 4;
+  s.xn = o;  // row norms of the tile: a double buffer per epilogue warp
+  o += size_t(kTqEpiThreads / 32) * 2 * BN * 4;
   s.bars = o;
-  o += size_t(2 * SA + 2 * (kTqTmemCols / BN)) * 8 + 16;
+  o += size_t(2 * SA + 2 * kTqMaxAcc + 2 * kTqQueue + 3) * 8 + 16 + kTqQueue * 4;
   s.total = o + 1024;
   return s;
 }
@@ -140,6 +165,21 @@ __device__ __forceinline__ ItemDesc item_desc(const ScanArgs& a, int item) {
   return it;
 }
 
+// r[j] for a run-time j without indexing the register array (which would put
+// it in local memory): five levels of selects on the bits of j.
+__device__ __forceinline__ uint32_t select32(const uint32_t (&r)[32], int j) {
+  uint32_t a[16], b[8], c[4], d[2];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) a[i] = (j & 1) ? r[2 * i + 1] : r[2 * i];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) b[i] = (j & 2) ? a[2 * i + 1] : a[2 * i];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) c[i] = (j & 4) ? b[2 * i + 1] : b[2 * i];
+#pragma unroll
+  for (int i = 0; i < 2; ++i) d[i] = (j & 8) ? c[2 * i + 1] : c[2 * i];
+  return (j & 16) ? d[1] : d[0];
+}
+
 // Accept mask of a 32-column chunk: bit j is set iff column j's distance is
 // <= thr_d (the row's current k-th distance, its bound, or +inf while open)
 // and j < nvalid. For L2, t = (qn + xn) - 2 dot is formed as l2_from_dot forms
@@ -150,24 +190,43 @@ __device__ __forceinline__ ItemDesc item_desc(const ScanArgs& a, int item) {
 template <int METRIC>
 __device__ __forceinline__ unsigned int tq_accept(const uint32_t (&r)[32], const float* xs,
                                                   float qn, float thr_d, int nvalid) {
-  unsigned int rej = 0;
+  // four independent shift chains of 8 columns each, joined at the end
+  unsigned int rej[4] = {0u, 0u, 0u, 0u};
+  float x[32];
+  if (METRIC == MF_METRIC_L2) {
+    // xs is 16-byte aligned (chunk offsets are multiples of 32 floats)
+    const float4* x4 = reinterpret_cast<const float4*>(xs);
 #pragma unroll
-  for (int j = 31; j >= 0; --j) {
-    const float dot = __uint_as_float(r[j]);
-    float diff;
-    if (METRIC == MF_METRIC_L2) diff = __fsub_rn(thr_d, fmaf(-2.0f, dot, __fadd_rn(qn, xs[j])));
-    else diff = __fadd_rn(thr_d, dot);
-    rej = __funnelshift_l(__float_as_uint(diff), rej, 1);
+    for (int i = 0; i < 8; ++i) {
+      const float4 t = x4[i];
+      x[4 * i] = t.x;
+      x[4 * i + 1] = t.y;
+      x[4 * i + 2] = t.z;
+      x[4 * i + 3] = t.w;
+    }
   }
+#pragma unroll
+  for (int i = 7; i >= 0; --i) {
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      const int j = 8 * g + i;
+      const float dot = __uint_as_float(r[j]);
+      float diff;
+      if (METRIC == MF_METRIC_L2) diff = __fsub_rn(thr_d, fmaf(-2.0f, dot, __fadd_rn(qn, x[j])));
+      else diff = __fadd_rn(thr_d, dot);
+      rej[g] = __funnelshift_l(__float_as_uint(diff), rej[g], 1);
+    }
+  }
+  const unsigned int all = rej[0] | (rej[1] << 8) | (rej[2] << 16) | (rej[3] << 24);
   const unsigned int in_range = nvalid >= 32 ? 0xffffffffu : ((1u << nvalid) - 1u);
-  return ~rej & in_range;
+  return ~all & in_range;
 }
 
-template <int METRIC, int BN>
-__global__ void __launch_bounds__(kTqThreads, 1)
+template <int METRIC, int BN, bool ATM>
+__global__ void __launch_bounds__(ATM ? kTqThreadsAtm : kTqThreads, 1)
     tq_scan_kernel(const ScanArgs a, const __grid_constant__ TqMaps maps, const TqLayout L) {
   extern __shared__ unsigned char smem_raw[];
-  constexpr int NACC = kTqTmemCols / BN;
+  const int NACC = L.nacc;
   unsigned char* base = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   unsigned long long* lists = reinterpret_cast<unsigned long long*>(base + L.lists);
@@ -176,8 +235,14 @@ __global__ void __launch_bounds__(kTqThreads, 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(base + L.bars);
   uint64_t* empty = full + L.SA;
   uint64_t* accf = empty + L.SA;
-  uint64_t* acce = accf + NACC;
-  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(acce + NACC);
+  uint64_t* acce = accf + kTqMaxAcc;
+  uint64_t* qfull = acce + kTqMaxAcc;
+  uint64_t* qempty = qfull + kTqQueue;
+  uint64_t* afull = qempty + kTqQueue;  // query tile written to tensor memory
+  uint64_t* afree = afull + 1;          // MMAs of the previous item done with it
+  uint64_t* mdone = afree + 1;          // every MMA of this CTA has completed
+  int* s_items = reinterpret_cast<int*>(mdone + 1);
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(s_items + kTqQueue);
   int* s_abort = reinterpret_cast<int*>(s_tmem + 1);
   uint32_t* s_seq = reinterpret_cast<uint32_t*>(s_abort + 1);  // [0] consumed, [1] issued
 
@@ -188,7 +253,7 @@ __global__ void __launch_bounds__(kTqThreads, 1)
   const int KB = L.KB;
   const int k = a.k;
   const int total = a.flat ? a.nqt * a.P : *a.item_total;
-  constexpr uint32_t kStageTx = 2 * kTqM * 128 + 2 * BN * 128;
+  constexpr uint32_t kStageTx = ATM ? 2 * BN * 128 : 2 * kTqM * 128 + 2 * BN * 128;
 
 #ifdef MF_TC_PROFILE
   const long long _tk = clock64();
@@ -206,6 +271,15 @@ __global__ void __launch_bounds__(kTqThreads, 1)
       mbar_init(&accf[i], 1);
       mbar_init(&acce[i], kTqEpiThreads);
     }
+    // readers of each queue slot: the MMA lane and one lane per epilogue
+    // (and loader) warp
+    for (int i = 0; i < kTqQueue; ++i) {
+      mbar_init(&qfull[i], 1);
+      mbar_init(&qempty[i], ATM ? 9 : 5);
+    }
+    mbar_init(afull, kTqM);
+    mbar_init(afree, 1);
+    mbar_init(mdone, 1);
     *s_abort = 0;
     s_seq[0] = 0;
     s_seq[1] = 0;
@@ -219,12 +293,23 @@ __global__ void __launch_bounds__(kTqThreads, 1)
   if (warp == 4) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
-      prefetch_tensormap(&maps.a_hi);
-      prefetch_tensormap(&maps.a_lo);
+      if (!ATM) {
+        prefetch_tensormap(&maps.a_hi);
+        prefetch_tensormap(&maps.a_lo);
+      }
       prefetch_tensormap(&maps.b_hi);
       prefetch_tensormap(&maps.b_lo);
       uint32_t seq = 0;
-      for (int item = blockIdx.x; item < total && !*s_abort; item += gridDim.x) {
+      for (uint32_t qi = 0;; ++qi) {
+        // take the next item and publish it (-1 ends every role's loop)
+        const int qs = qi % kTqQueue;
+        if (qi >= (uint32_t)kTqQueue)
+          mbar_wait(&qempty[qs], ((qi / kTqQueue) - 1) & 1, s_abort, &g_device_error);
+        int item = *s_abort ? -1 : atomicAdd(a.counter, 1);
+        if (item >= total) item = -1;
+        s_items[qs] = item;
+        mbar_arrive(&qfull[qs]);
+        if (item < 0) break;
         const ItemDesc it = item_desc(a, item);
         const long long nrows = it.re > it.rb ? it.re - it.rb : 0;
         const int nT = (int)((nrows + BN - 1) / BN);
@@ -239,8 +324,10 @@ __global__ void __launch_bounds__(kTqThreads, 1)
             mbar_arrive_expect_tx(&full[s], kStageTx);
             const int x = kb * 32;
             const int yb = (int)(it.rb + (long long)t * BN);
-            tma_load_2d(st + L.a_hi, &maps.a_hi, x, it.a_row0, &full[s]);
-            tma_load_2d(st + L.a_lo, &maps.a_lo, x, it.a_row0, &full[s]);
+            if (!ATM) {
+              tma_load_2d(st + L.a_hi, &maps.a_hi, x, it.a_row0, &full[s]);
+              tma_load_2d(st + L.a_lo, &maps.a_lo, x, it.a_row0, &full[s]);
+            }
             tma_load_2d(st + L.b_hi, &maps.b_hi, x, yb, &full[s]);
             tma_load_2d(st + L.b_lo, &maps.b_lo, x, yb, &full[s]);
             ++seq;
@@ -254,16 +341,26 @@ __global__ void __launch_bounds__(kTqThreads, 1)
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_tf32(kTqM, BN);
       uint32_t seq = 0, tt = 0;
-      for (int item = blockIdx.x; item < total && !*s_abort; item += gridDim.x) {
+      for (uint32_t qi = 0;; ++qi) {
+        const int qs = qi % kTqQueue;
+        if (!mbar_wait(&qfull[qs], (qi / kTqQueue) & 1, s_abort, &g_device_error)) break;
+        const int item = s_items[qs];
+        mbar_arrive(&qempty[qs]);
+        if (item < 0) break;
         const ItemDesc it = item_desc(a, item);
         const long long nrows = it.re > it.rb ? it.re - it.rb : 0;
         const int nT = (int)((nrows + BN - 1) / BN);
+        if (ATM) {
+          // this item's query tile is in tensor memory
+          if (!mbar_wait(afull, qi & 1, s_abort, &g_device_error)) break;
+          tc_fence_after();
+        }
         for (int t = 0; t < nT; ++t, ++tt) {
           const int b = tt % NACC;
           if (tt >= (uint32_t)NACC)
             TQP(1, mbar_wait(&acce[b], ((tt / NACC) - 1) & 1, s_abort, &g_device_error));
           tc_fence_after();
-          const uint32_t dt = tmem + b * BN;
+          const uint32_t dt = tmem + L.acc0 + b * BN;
           for (int kb = 0; kb < KB; ++kb, ++seq) {
             const int s = seq % SA;
             TQP(2, mbar_wait(&full[s], (seq / SA) & 1, s_abort, &g_device_error));
@@ -275,13 +372,22 @@ __global__ void __launch_bounds__(kTqThreads, 1)
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk) {
               const uint32_t off = kk * 32;  // 8 tf32 of K per MMA
-              const uint64_t ah = desc_k_sw128(st + L.a_hi + off);
-              const uint64_t al = desc_k_sw128(st + L.a_lo + off);
               const uint64_t bh = desc_k_sw128(st + L.b_hi + off);
               const uint64_t bl = desc_k_sw128(st + L.b_lo + off);
-              mma_tf32(dt, ah, bh, idesc, !(kb == 0 && kk == 0));
-              mma_tf32(dt, ah, bl, idesc, true);
-              mma_tf32(dt, al, bh, idesc, true);
+              if (ATM) {
+                // A columns: hi at [0, KB*32), lo at [KB*32, 2*KB*32)
+                const uint32_t ah = tmem + kb * 32 + kk * 8;
+                const uint32_t al = ah + KB * 32;
+                mma_tf32_ts(dt, ah, bh, idesc, !(kb == 0 && kk == 0));
+                mma_tf32_ts(dt, ah, bl, idesc, true);
+                mma_tf32_ts(dt, al, bh, idesc, true);
+              } else {
+                const uint64_t ah = desc_k_sw128(st + L.a_hi + off);
+                const uint64_t al = desc_k_sw128(st + L.a_lo + off);
+                mma_tf32(dt, ah, bh, idesc, !(kb == 0 && kk == 0));
+                mma_tf32(dt, ah, bl, idesc, true);
+                mma_tf32(dt, al, bh, idesc, true);
+              }
             }
             mma_commit(&empty[s]);
 #ifdef MF_TC_PROFILE
@@ -290,8 +396,68 @@ __global__ void __launch_bounds__(kTqThreads, 1)
           }
           mma_commit(&accf[b]);
         }
+        // the query tile may be overwritten once this item's MMAs complete
+        if (ATM) mma_commit(afree);
       }
       s_seq[0] = seq;
+      // lets the teardown free tensor memory only after the last MMA, also when
+      // a role gave up early
+      mma_commit(mdone);
+    }
+  } else if (ATM && warp >= 6) {
+    // ------------------------------------------------ query tile loader
+    // Thread t of warps 6-9 owns TMEM lane 32*(warp%4)+lane = query row of
+    // the item. It reads its query from global memory before waiting for the
+    // previous item's MMAs, splits it into tf32 hi (the raw fp32; the tensor
+    // core drops the low 13 bits) and lo = x - trunc(x), and writes both to its
+    // lane: hi in columns [0, KB*32), lo in [KB*32, 2*KB*32); zero past d.
+    const int row = 32 * (warp & 3) + lane;
+    const uint32_t lane_base = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
+    constexpr int kMaxV = kTqMaxDAtm / 4;
+    for (uint32_t qi = 0;; ++qi) {
+      const int qs = qi % kTqQueue;
+      if (!mbar_wait(&qfull[qs], (qi / kTqQueue) & 1, s_abort, &g_device_error)) break;
+      const int item = s_items[qs];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&qempty[qs]);
+      if (item < 0) break;
+      const ItemDesc it = item_desc(a, item);
+      const float* src = nullptr;
+      if (row < it.nq_item) {
+        const long long q = a.flat ? (long long)it.a_row0 + row : a.pairs[it.a_row0 + row] / a.P;
+        src = a.xq + q * a.d;
+      }
+      float4 v[kMaxV];
+#pragma unroll
+      for (int i = 0; i < kMaxV; ++i) {
+        v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (src != nullptr && 4 * i < a.d) v[i] = *reinterpret_cast<const float4*>(src + 4 * i);
+      }
+      if (qi > 0 && !mbar_wait(afree, (qi - 1) & 1, s_abort, &g_device_error)) break;
+      tc_fence_after();
+#pragma unroll
+      for (int c = 0; c < kTqMaxDAtm / 32; ++c) {
+        if (c < KB) {
+          uint32_t hi[32], lo[32];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const float e[4] = {v[c * 8 + i].x, v[c * 8 + i].y, v[c * 8 + i].z, v[c * 8 + i].w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              float h, l;
+              split_tf32(e[j], h, l);
+              hi[4 * i + j] = __float_as_uint(e[j]);
+              lo[4 * i + j] = __float_as_uint(l);
+              (void)h;
+            }
+          }
+          tmem_st32(lane_base + c * 32, hi);
+          tmem_st32(lane_base + KB * 32 + c * 32, lo);
+        }
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(afull);
     }
   } else {
     // ----------------------------------------------------------- epilogue
@@ -303,6 +469,7 @@ __global__ void __launch_bounds__(kTqThreads, 1)
     uint32_t tt = 0;
 #ifdef MF_TC_PROFILE
     long long p_wait = 0, p_loop = 0, p_merge = 0, p_tiles = 0, p_nmerge = 0, p_out = 0;
+    long long p_stage = 0, p_filter = 0, p_append = 0, p_tld = 0, p_nappend = 0;
     const long long p_start = clock64();
 #endif
     unsigned long long* my_lists = lists + (size_t)(warp * 32) * kTqK;
@@ -357,25 +524,31 @@ __global__ void __launch_bounds__(kTqThreads, 1)
       }
     };
     // Row norms (L2) are loaded one tile ahead into registers, so their global
-    // load latency overlaps the previous tile's epilogue. pf_r0 tags the tile
-    // the registers hold; a mismatch (first tile, an empty item) reloads.
-    constexpr int kPf = BN / kTqEpiThreads;
+    // load latency overlaps the previous tile's epilogue; each warp stages its
+    // own copy, so no barrier spans the four warps. pf_r0 tags the tile the
+    // registers hold; a mismatch (first tile, an empty item) reloads.
+    constexpr int kPf = BN / 32;
     float xn_pf[kPf];
     long long pf_r0 = -1;
     auto load_norms = [&](long long r0, long long re) {
 #pragma unroll
       for (int i = 0; i < kPf; ++i) {
-        const long long r = r0 + tid + i * kTqEpiThreads;
+        const long long r = r0 + lane + 32 * i;
         xn_pf[i] = r < re ? a.xnorms[r] : 0.0f;
       }
       pf_r0 = r0;
     };
-    for (int item = blockIdx.x; item < total && !*s_abort; item += gridDim.x) {
+    for (uint32_t qi = 0;; ++qi) {
+      const int qs = qi % kTqQueue;
+      if (!mbar_wait(&qfull[qs], (qi / kTqQueue) & 1, s_abort, &g_device_error)) break;
+      const int item = s_items[qs];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&qempty[qs]);
+      if (item < 0) break;
       const ItemDesc it = item_desc(a, item);
       const long long nrows = it.re > it.rb ? it.re - it.rb : 0;
       const int nT = (int)((nrows + BN - 1) / BN);
       const bool valid = tid < it.nq_item;
-      const int nitem = item + gridDim.x;
       long long slot = -1;
       int q = 0;
       if (valid) {
@@ -399,65 +572,86 @@ __global__ void __launch_bounds__(kTqThreads, 1)
       for (int t = 0; t < nT; ++t, ++tt) {
         const int b = tt % NACC;
         const long long r0 = it.rb + (long long)t * BN;
+#ifdef MF_TC_PROFILE
+        const long long p_s0 = clock64();
+#endif
         if (METRIC == MF_METRIC_L2) {
           // row norms of this tile, shared by the four epilogue warps
           if (pf_r0 != r0) load_norms(r0, it.re);
-          float* xs = xn_s + (tt & 1) * BN;
+          float* xs = xn_s + (warp * 2 + (tt & 1)) * BN;
 #pragma unroll
-          for (int i = 0; i < kPf; ++i) xs[tid + i * kTqEpiThreads] = xn_pf[i];
-          named_sync(1, kTqEpiThreads);
+          for (int i = 0; i < kPf; ++i) xs[lane + 32 * i] = xn_pf[i];
+          __syncwarp();
           // issue the next tile's loads now; they land while this tile runs
           if (t + 1 < nT) {
             load_norms(r0 + BN, it.re);
-          } else if (nitem < total) {
-            const ItemDesc nx = item_desc(a, nitem);
-            if (nx.re > nx.rb) load_norms(nx.rb, nx.re);
+          } else {
+            // the next item, if the producer has published it already
+            const uint32_t nq = qi + 1;
+            if (mbar_test(&qfull[nq % kTqQueue], (nq / kTqQueue) & 1)) {
+              const int nitem = s_items[nq % kTqQueue];
+              if (nitem >= 0) {
+                const ItemDesc nx = item_desc(a, nitem);
+                if (nx.re > nx.rb) load_norms(nx.rb, nx.re);
+              }
+            }
           }
         }
+#ifdef MF_TC_PROFILE
+        p_stage += clock64() - p_s0;
+#endif
         TQL(p_wait, mbar_wait(&accf[b], (tt / NACC) & 1, s_abort, &g_device_error));
 #ifdef MF_TC_PROFILE
         ++p_tiles;
 #endif
         tc_fence_after();
-        const float* xs = xn_s + (tt & 1) * BN;
+        const float* xs = xn_s + (warp * 2 + (tt & 1)) * BN;
         // One 32-column chunk: filter, merge rows that would overflow, append.
         auto chunk = [&](uint32_t (&r)[32], int c0) {
           const long long rc = r0 + c0;
           const long long left = it.re - rc;
           const int nvalid = left >= 32 ? 32 : (left > 0 ? (int)left : 0);
           const float thr_d = thr == kEmptyKey ? __int_as_float(0x7f800000) : key_dist(thr);
+#ifdef MF_TC_PROFILE
+          const long long p_f0 = clock64();
+#endif
           unsigned int acc = tq_accept<METRIC>(r, xs + c0, qn, thr_d, nvalid);
           if (!valid) acc = 0;
           const unsigned int over = __ballot_sync(0xffffffffu, cnt + __popc(acc) > 32);
+#ifdef MF_TC_PROFILE
+          p_filter += clock64() - p_f0;
+          const long long p_a0 = clock64();
+          if (__any_sync(0xffffffffu, acc != 0)) ++p_nappend;
+#endif
           if (over) {
             TQL(p_merge, merge_rows(over, cnt, thr, bound));
 #ifdef MF_TC_PROFILE
             p_nmerge += __popc(over);
 #endif
           }
-          if (acc) {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              if ((acc >> j) & 1u) {
-                const float dot = __uint_as_float(r[j]);
-                const float dist =
-                    METRIC == MF_METRIC_L2 ? l2_from_dot(qn, xs[c0 + j], dot) : -dot;
-                own_buf[cnt++] = make_key(dist, (unsigned int)(rc + j));
-              }
-            }
+          // survivors are few: a loop over the set bits, with the column's
+          // value selected from the registers by a 5-level mux tree
+          for (unsigned int m = acc; m != 0u; m &= m - 1u) {
+            const int j = __ffs(m) - 1;
+            const float dot = __uint_as_float(select32(r, j));
+            const float dist = METRIC == MF_METRIC_L2 ? l2_from_dot(qn, xs[c0 + j], dot) : -dot;
+            own_buf[cnt++] = make_key(dist, (unsigned int)(rc + j));
           }
           __syncwarp();
+#ifdef MF_TC_PROFILE
+          p_append += clock64() - p_a0;
+#endif
         };
         // TMEM loads are double-buffered: chunk c+1 loads while c is filtered.
-        const uint32_t tb = tmem + ((uint32_t)(warp * 32) << 16) + b * BN;
+        const uint32_t tb = tmem + ((uint32_t)(warp * 32) << 16) + L.acc0 + b * BN;
         uint32_t ra[32], rb[32];
         tmem_ld32_async(tb, ra);
 #pragma unroll 1
         for (int c0 = 0; c0 < BN; c0 += 64) {
-          tmem_wait_ld(ra);
+          TQL(p_tld, tmem_wait_ld(ra));
           tmem_ld32_async(tb + c0 + 32, rb);
           chunk(ra, c0);
-          tmem_wait_ld(rb);
+          TQL(p_tld, tmem_wait_ld(rb));
           if (c0 + 64 < BN) tmem_ld32_async(tb + c0 + 64, ra);
           chunk(rb, c0 + 32);
         }
@@ -503,6 +697,11 @@ __global__ void __launch_bounds__(kTqThreads, 1)
       atomicAdd(&g_tc_prof[7], (unsigned long long)p_merge);
       atomicAdd(&g_tc_prof[11], (unsigned long long)p_nmerge);
       atomicAdd(&g_tc_prof[12], (unsigned long long)p_out);
+      atomicAdd(&g_tc_prof[6], (unsigned long long)p_stage);
+      atomicAdd(&g_tc_prof[9], (unsigned long long)p_filter);
+      atomicAdd(&g_tc_prof[10], (unsigned long long)p_append);
+      atomicAdd(&g_tc_prof[14], (unsigned long long)p_tld);
+      atomicAdd(&g_tc_prof[15], (unsigned long long)p_nappend);
     }
 #endif
   }
@@ -517,7 +716,15 @@ __global__ void __launch_bounds__(kTqThreads, 1)
       mbar_wait(&full[seq % SA], (seq / SA) & 1, &dummy, &g_device_error);
   }
   __syncthreads();
-  if (warp == 5) tmem_dealloc(tmem, kTqTmemCols);
+  if (warp == 5) {
+    if (lane == 0) {
+      int dummy = 0;
+      mbar_wait(mdone, 0, &dummy, &g_device_error);
+    }
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, kTqTmemCols);
+  }
 #ifdef MF_TC_PROFILE
   if (tid == 0) atomicAdd(&g_tc_prof[13], (unsigned long long)(clock64() - _tk));
 #endif
@@ -527,17 +734,33 @@ __global__ void __launch_bounds__(kTqThreads, 1)
 typedef void (*TqFn)(const ScanArgs, const TqMaps, const TqLayout);
 
 template <int METRIC>
-TqFn pick_tq(int BN) {
-  return BN == 256 ? tq_scan_kernel<METRIC, 256> : tq_scan_kernel<METRIC, 128>;
+TqFn pick_tq(const TqLayout& l) {
+  if (l.atm) return tq_scan_kernel<METRIC, 128, true>;
+  return l.BN == 256 ? tq_scan_kernel<METRIC, 256, false> : tq_scan_kernel<METRIC, 128, false>;
 }
 
 int tq_kcap(int k) { return k <= kTqK ? kTqK : 0; }
 
-// The widest tile (BN rows) and deepest ring that fit shared memory.
+int g_engine = 0;  // 0 auto, 1 SIMT only, 2 tensor cores where eligible, 3 = 2 with streamed queries
+
+// With d <= 128 the query tile (hi and lo) lives in tensor memory next to two
+// accumulator buffers, and shared memory holds only row stages: the deepest
+// ring that fits. Otherwise the widest tile (BN rows) and deepest ring with
+// the query tile streamed beside the rows.
 bool tq_choose(int d, int kcap, TqLayout* out) {
+  const int kb32 = (d + 31) / 32 * 32;
+  if (g_engine != 3 && kb32 <= kTqMaxDAtm && kTqTmemCols - 2 * kb32 >= 2 * 128) {
+    for (int sa = 5; sa >= 2; --sa) {
+      TqLayout l = tq_layout(d, kcap, 128, sa, true);
+      if (l.total <= (size_t)kTqMaxSmem) {
+        *out = l;
+        return true;
+      }
+    }
+  }
   const int cands[4][2] = {{256, 3}, {256, 2}, {128, 3}, {128, 2}};
   for (auto& c : cands) {
-    TqLayout l = tq_layout(d, kcap, c[0], c[1]);
+    TqLayout l = tq_layout(d, kcap, c[0], c[1], false);
     if (l.total <= (size_t)kTqMaxSmem) {
       *out = l;
       return true;
@@ -548,7 +771,7 @@ bool tq_choose(int d, int kcap, TqLayout* out) {
 
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 std::mutex g_tc_mu;
-int g_tc_attr[64][2][2];  // dynamic smem set per (device, metric, BN)
+int g_tc_attr[64][2][3];  // dynamic smem set per (device, metric, variant)
 
 int encoder(PFN_cuTensorMapEncodeTiled_v12000* out) {
   std::lock_guard<std::mutex> lk(g_tc_mu);
@@ -576,8 +799,6 @@ int make_map(PFN_cuTensorMapEncodeTiled_v12000 enc, CUtensorMap* map, const floa
   MF_CHECK(r == CUDA_SUCCESS, MF_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
   return MF_OK;
 }
-
-int g_engine = 0;  // 0 auto, 1 SIMT only, 2 tensor cores where eligible
 
 __global__ void tf32_residual_kernel(const float4* __restrict__ x, int64_t n4, float4* lo) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -632,6 +853,12 @@ bool tc_eligible(int metric, int d, int k, int64_t xb_rows) {
   return tq_choose(d, kcap, &l);
 }
 
+bool tc_raw_queries(int d, int k) {
+  TqLayout l;
+  const int kcap = tq_kcap(k);
+  return kcap != 0 && tq_choose(d, kcap, &l) && l.atm;
+}
+
 int launch_tf32_residual(const float* x, int64_t n, int d, float* lo, cudaStream_t stream) {
   const int64_t n4 = n * (int64_t)d / 4;
   if (n4 <= 0) return MF_OK;
@@ -658,20 +885,23 @@ int launch_tc_scan(const ScanArgs& a, int metric, const float* a_lo, int64_t a_r
   TqLayout lay;
   MF_CHECK(kcap != 0 && tq_choose(a.d, kcap, &lay), MF_ERR_INVALID_ARGS,
            "tensor-core scan does not fit (d=%d k=%d)", a.d, a.k);
-  TqFn fn = metric == MF_METRIC_L2 ? pick_tq<MF_METRIC_L2>(lay.BN)
-                                   : pick_tq<MF_METRIC_INNER_PRODUCT>(lay.BN);
+  TqFn fn = metric == MF_METRIC_L2 ? pick_tq<MF_METRIC_L2>(lay)
+                                   : pick_tq<MF_METRIC_INNER_PRODUCT>(lay);
   MF_CHECK(fn != nullptr, MF_ERR_METRIC, "metric %d has no tensor-core scan", metric);
   PFN_cuTensorMapEncodeTiled_v12000 enc;
   MF_TRY(encoder(&enc));
   TqMaps maps;
-  MF_TRY(make_map(enc, &maps.a_hi, a.xq, a.d, a_rows, kTqM));
-  MF_TRY(make_map(enc, &maps.a_lo, a_lo, a.d, a_rows, kTqM));
+  memset(&maps, 0, sizeof(maps));
+  if (!lay.atm) {  // streamed query tile: a.xq / a_lo hold one row per A row
+    MF_TRY(make_map(enc, &maps.a_hi, a.xq, a.d, a_rows, kTqM));
+    MF_TRY(make_map(enc, &maps.a_lo, a_lo, a.d, a_rows, kTqM));
+  }
   MF_TRY(make_map(enc, &maps.b_hi, a.xb, a.d, b_rows, lay.BN));
   MF_TRY(make_map(enc, &maps.b_lo, b_lo, a.d, b_rows, lay.BN));
   {
     std::lock_guard<std::mutex> lk(g_tc_mu);
     const int mi = metric == MF_METRIC_L2 ? 0 : 1;
-    const int bi = lay.BN == 256 ? 1 : 0;
+    const int bi = lay.atm ? 2 : (lay.BN == 256 ? 1 : 0);
     if (device < 0 || device >= 64 || g_tc_attr[device][mi][bi] < (int)lay.total) {
       MF_CUDA(cudaFuncSetAttribute(reinterpret_cast<const void*>(fn),
                                    cudaFuncAttributeMaxDynamicSharedMemorySize, (int)lay.total));
@@ -679,10 +909,12 @@ int launch_tc_scan(const ScanArgs& a, int metric, const float* a_lo, int64_t a_r
     }
   }
   if (total_items <= 0) return MF_OK;
+  MF_CHECK(a.counter != nullptr, MF_ERR_INVALID_ARGS, "tensor-core scan needs a work counter");
+  MF_CUDA(cudaMemsetAsync(a.counter, 0, sizeof(int), stream));
   long long grid = num_sms(device);
   if (grid > total_items) grid = total_items;
   ScopedTiming tm(a.flat ? "scan_topk_flat" : (a.max_rows > 0 ? "scan_topk_ivf_bound" : "scan_topk_ivf"), stream);
-  fn<<<(unsigned int)grid, kTqThreads, lay.total, stream>>>(a, maps, lay);
+  fn<<<(unsigned int)grid, lay.atm ? kTqThreadsAtm : kTqThreads, lay.total, stream>>>(a, maps, lay);
   MF_LAUNCH_CHECK();
   return MF_OK;
 }

@@ -1,7 +1,9 @@
 """The tensor-core (tcgen05, 3xTF32) and SIMT scan engines against each other
 and against the oracle, on flat and IVF searches. Engine 2 (like the default)
 uses the tensor cores where the shape allows (L2 / inner product, d >= 32,
-k <= 64) and the SIMT scan otherwise; engine 1 forces the SIMT scan."""
+k <= 32) and the SIMT scan otherwise, with the query tile in tensor memory
+when d <= 128; engine 3 streams the query tile through shared memory instead;
+engine 1 forces the SIMT scan."""
 import numpy as np
 import pytest
 
@@ -33,10 +35,11 @@ def _flat(metric, d, n, nq, k, seed, engine_id, data="gauss"):
     return xb, xq, D, I
 
 
+@pytest.mark.parametrize("eng", [2, 3])
 @pytest.mark.parametrize("metric", [MetricType.L2, MetricType.INNER_PRODUCT])
 @pytest.mark.parametrize("d,k", [(32, 10), (64, 1), (128, 32), (96, 100), (256, 256), (48, 7)])
-def test_tc_flat_matches_oracle(cuda_device, engine, metric, d, k):
-    xb, xq, D, I = _flat(metric, d, 5000, 77, k, seed=d + k, engine_id=2)
+def test_tc_flat_matches_oracle(cuda_device, engine, eng, metric, d, k):
+    xb, xq, D, I = _flat(metric, d, 5000, 77, k, seed=d + k, engine_id=eng)
     D_ref, I_ref = oracle.flat_search(xq, xb, k, int(metric))
     atol = compare.l2_atol(xq, xb) if metric == MetricType.L2 else 1e-5 * (1 + np.abs(D_ref).max())
     errs = compare.check_knn(D, I, D_ref, I_ref, compare.exact_lookup(xq, xb, int(metric)), atol=atol)
@@ -58,8 +61,9 @@ def test_tc_precision_on_mixture(cuda_device, engine):
     assert not errs, errs[:5]
 
 
+@pytest.mark.parametrize("eng", [2, 3])
 @pytest.mark.parametrize("nprobe,k", [(1, 10), (8, 32), (16, 100)])
-def test_tc_ivf_equals_simt(cuda_device, engine, nprobe, k):
+def test_tc_ivf_equals_simt(cuda_device, engine, eng, nprobe, k):
     x, cen, _ = syn.mixture(40000, 64, 96, seed=7)
     idx = IVFFlatIndex(64, 96)
     idx.set_centroids(oracle.kmeans_train(x, 96, 2, 7))
@@ -68,22 +72,23 @@ def test_tc_ivf_equals_simt(cuda_device, engine, nprobe, k):
     xq, _, _ = syn.mixture(300, 64, 96, seed=8, centres=cen)
     nat.set_scan_engine(1)
     D1, I1 = idx.search(xq, k).numpy()
-    nat.set_scan_engine(2)
+    nat.set_scan_engine(eng)
     D2, I2 = idx.search(xq, k).numpy()
     errs = compare.check_knn(D2, I2, D1, I1, compare.exact_lookup(xq, x, oracle.L2),
                              atol=compare.l2_atol(xq, x))
     assert not errs, errs[:5]
 
 
-def test_tc_many_items_persistent(cuda_device, engine):
-    """More work items than CTAs, lists of every size, groups of 1..32 queries."""
+@pytest.mark.parametrize("eng", [2, 3])
+def test_tc_many_items_persistent(cuda_device, engine, eng):
+    """More work items than CTAs, lists of every size, groups of 1..128 queries."""
     x, cen, _ = syn.mixture(60000, 128, 300, seed=9)
     idx = IVFFlatIndex(128, 300)
     idx.set_centroids(x[:300])
     idx.add(x)
     idx.nprobe = 20
     xq, _, _ = syn.mixture(2000, 128, 300, seed=10, centres=cen)
-    nat.set_scan_engine(2)
+    nat.set_scan_engine(eng)
     D, I = idx.search(xq, 10).numpy()
     offs = idx.list_offsets.cpu().numpy()
     vecs = idx._vecs[:, :128].cpu().numpy()
