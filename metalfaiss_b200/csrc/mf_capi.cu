@@ -155,7 +155,6 @@ int ivf_scan_topk(int device, cudaStream_t stream, const IvfWs& w, const float* 
                   const int64_t* list_ids, int64_t ntotal, const int32_t* list_order, int d,
                   int metric, int k, float* D, int64_t* I) {
   const bool tc = list_lo != nullptr && tc_eligible(metric, d, k, ntotal);
-  const int group = tc ? tc_group() : kScanTQ;
   if (metric == MF_METRIC_L2) MF_TRY(launch_norms(xq, nq, d, w.qn, stream));
   ScanArgs a{};
   a.xq = xq;
@@ -181,19 +180,25 @@ int ivf_scan_topk(int device, cudaStream_t stream, const IvfWs& w, const float* 
   // nearest list (probe 0); the k-th distance found there is an upper bound
   // on the query's final k-th distance. Phase 2 scans all probes, keeping
   // only candidates within the bound, so most rows of the farther lists never
-  // enter the top-k merges.
+  // enter the top-k merges. For L2 phase 1 runs on the SIMT engine (its
+  // one-tile items are cheaper there); the bound then carries a margin for
+  // the engines' rounding difference, so phase 2 still drops no row that
+  // belongs to the top-k.
   constexpr int64_t kBoundRows = 128;
   const int phases = P > 1 ? 2 : 1;
   for (int ph = 0; ph < phases; ++ph) {
     const bool bounding = phases == 2 && ph == 0;
+    const bool simt_bound = bounding && tc && metric == MF_METRIC_L2;
+    const bool use_tc = tc && !simt_bound;
     MF_TRY(run_ivf_groups_ex(w.g, probes, nq, P, nlist, list_offsets, list_order, w.pd, w.pl, k,
-                             nullptr, group, stream, 0, bounding ? 1 : P));
+                             nullptr, use_tc ? tc_group() : kScanTQ, stream, 0,
+                             bounding ? 1 : P));
     a.max_rows = bounding ? kBoundRows : 0;
     a.bound = (phases == 2 && ph == 1) ? w.bound : nullptr;
-    if (tc && tc_raw_queries(d, k)) {
+    if (use_tc && tc_raw_queries(d, k)) {
       // the scan loads each item's queries itself (through a.pairs)
       MF_TRY(launch_tc_scan(a, metric, nullptr, nq, list_lo, ntotal, nq * P, device, stream));
-    } else if (tc) {
+    } else if (use_tc) {
       // A operand: the queries of every (query, probe) pair, gathered in list order
       MF_TRY(launch_gather_queries(xq, d, w.g.pairs, w.g.pair_offsets + nlist, nq * P, P, w.g_hi,
                                    w.g_lo, stream));
@@ -203,7 +208,11 @@ int ivf_scan_topk(int device, cudaStream_t stream, const IvfWs& w, const float* 
     } else {
       MF_TRY(launch_scan(a, metric, kEpiTopK, nq * P, device, stream));
     }
-    if (bounding) MF_TRY(launch_extract_bound(w.pd, nq, P, k, w.bound, stream));
+    if (simt_bound)
+      MF_TRY(launch_extract_bound_slack(w.pd, nq, P, k, probes, list_offsets, list_norms, w.qn,
+                                        kBoundRows, d, w.bound, stream));
+    else if (bounding)
+      MF_TRY(launch_extract_bound(w.pd, nq, P, k, w.bound, stream));
   }
   MF_TRY(launch_merge(w.pd, w.pl, nq, P, k, k, D, I, stream));
   return MF_OK;

@@ -446,6 +446,49 @@ int launch_extract_bound(const float* pd, int64_t nq, int P, int k, float* bound
   return MF_OK;
 }
 
+// One warp per query: the k-th distance of slot 0 plus a margin that covers
+// the difference between two engines' roundings of the same distance. Both
+// the SIMT fp32 dot (error <= (d-1) u sum|q_i x_i|, u = 2^-24) and the 3xTF32
+// tensor-core dot stay within (d + 32) 2^-22 (|q|^2 + |x|^2) / 2 of the exact
+// value, so (d + 32) 2^-21 (qn + max xn) over the rows the bound came from
+// bounds their difference with room to spare.
+__global__ void extract_bound_slack_kernel(const float* __restrict__ pd, int64_t nq, int P, int k,
+                                           const int64_t* __restrict__ probes,
+                                           const int64_t* __restrict__ list_offsets,
+                                           const float* __restrict__ list_norms,
+                                           const float* __restrict__ qnorms, int64_t max_rows,
+                                           int d, float* bound) {
+  const long long q = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (q >= nq) return;
+  const float kth = pd[(q * P) * k + k - 1];
+  const long long l = probes[q * P];
+  float xmax = 0.0f;
+  if (l >= 0) {
+    const long long rb = list_offsets[l];
+    long long re = list_offsets[l + 1];
+    if (re - rb > max_rows) re = rb + max_rows;
+    for (long long r = rb + lane; r < re; r += 32) xmax = fmaxf(xmax, list_norms[r]);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) xmax = fmaxf(xmax, __shfl_xor_sync(0xffffffffu, xmax, o));
+  if (lane == 0) {
+    const float gamma = (float)(d + 32) * 4.76837158203125e-07f;  // (d + 32) * 2^-21
+    bound[q] = kth + gamma * (qnorms[q] + xmax);  // +inf stays +inf
+  }
+}
+
+int launch_extract_bound_slack(const float* pd, int64_t nq, int P, int k, const int64_t* probes,
+                               const int64_t* list_offsets, const float* list_norms,
+                               const float* qnorms, int64_t max_rows, int d, float* bound,
+                               cudaStream_t stream) {
+  if (nq <= 0) return MF_OK;
+  extract_bound_slack_kernel<<<(unsigned int)ceil_div(nq * 32, 256), 256, 0, stream>>>(
+      pd, nq, P, k, probes, list_offsets, list_norms, qnorms, max_rows, d, bound);
+  MF_LAUNCH_CHECK();
+  return MF_OK;
+}
+
 int launch_map_ids(const int64_t* ids, int64_t* labels, int64_t n, cudaStream_t stream) {
   if (n <= 0) return MF_OK;
   map_ids_kernel<<<(unsigned int)ceil_div(n, 256), 256, 0, stream>>>(ids, labels, n);

@@ -134,6 +134,13 @@ int run_ivf_groups(const IvfGroups& g, const int64_t* probes, int64_t nq, int P,
 // bound[q] = pd[(q*P + 0)*k + k-1] (the k-th distance of slot 0).
 int launch_extract_bound(const float* pd, int64_t nq, int P, int k, float* bound,
                          cudaStream_t stream);
+// Same for a bound computed by the SIMT engine and used by the tensor-core
+// engine (L2): adds a margin for their rounding difference, from the query
+// norm and the largest norm among the first max_rows rows of probe 0's list.
+int launch_extract_bound_slack(const float* pd, int64_t nq, int P, int k, const int64_t* probes,
+                               const int64_t* list_offsets, const float* list_norms,
+                               const float* qnorms, int64_t max_rows, int d, float* bound,
+                               cudaStream_t stream);
 
 // Exclusive scan of n int64 counts into out (n+1 entries; out[n] = total).
 int launch_exclusive_scan_i64(const int64_t* in, int64_t n, int64_t* out, cudaStream_t stream);

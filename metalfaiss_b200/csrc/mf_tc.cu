@@ -118,7 +118,7 @@ TqLayout tq_layout(int d, int kcap, int BN, int SA, bool atm) {
   s.xn = o;  // row norms of the tile: a double buffer per epilogue warp
   o += size_t(kTqEpiThreads / 32) * 2 * BN * 4;
   s.bars = o;
-  o += size_t(2 * SA + 2 * kTqMaxAcc + 2 * kTqQueue + 3) * 8 + 16 + kTqQueue * 4;
+  o += size_t(2 * SA + 2 * kTqMaxAcc + 2 * kTqQueue + 3) * 8 + 16 + kTqQueue * 32;
   s.total = o + 1024;
   return s;
 }
@@ -134,11 +134,17 @@ __device__ __forceinline__ void named_sync(int id, int count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
-// Item geometry; every role reads it for itself.
+// Item geometry, computed by the producer and published with the item.
 struct ItemDesc {
   long long rb, re;  // row slab
   int a_row0;        // first A row (queries) in the A tensor map
   int nq_item;       // valid queries (A rows) of this item
+};
+
+// A queue slot: the item index (-1 ends the roles' loops) and its geometry.
+struct QSlot {
+  ItemDesc it;
+  int item;
 };
 
 __device__ __forceinline__ ItemDesc item_desc(const ScanArgs& a, int item) {
@@ -180,18 +186,42 @@ __device__ __forceinline__ uint32_t select32(const uint32_t (&r)[32], int j) {
   return (j & 16) ? d[1] : d[0];
 }
 
+// Packed pairs of fp32 (Blackwell's two-wide fp32 add / sub / fma): each half
+// is rounded like the scalar instruction.
+__device__ __forceinline__ unsigned long long pack2(float lo, float hi) {
+  return static_cast<unsigned long long>(__float_as_uint(lo)) |
+         (static_cast<unsigned long long>(__float_as_uint(hi)) << 32);
+}
+__device__ __forceinline__ unsigned long long add2(unsigned long long a, unsigned long long b) {
+  unsigned long long d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ unsigned long long sub2(unsigned long long a, unsigned long long b) {
+  unsigned long long d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ unsigned long long fma2(unsigned long long a, unsigned long long b,
+                                                   unsigned long long c) {
+  unsigned long long d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+
 // Accept mask of a 32-column chunk: bit j is set iff column j's distance is
 // <= thr_d (the row's current k-th distance, its bound, or +inf while open)
 // and j < nvalid. For L2, t = (qn + xn) - 2 dot is formed as l2_from_dot forms
 // it before its clamp at 0 (doubling is exact, so the FMA rounds once, like the
 // subtraction); thr_d >= 0, so t <= thr_d iff the clamped distance is. The
-// sign bit of thr_d - t (+0 when equal) is shifted into the reject mask, one
-// funnel shift per column.
+// sign bit of thr_d - t (+0 when equal) is shifted into a reject mask. Columns
+// go two at a time through the packed fp32 pipe, in four independent shift
+// chains of 8 columns joined at the end.
 template <int METRIC>
 __device__ __forceinline__ unsigned int tq_accept(const uint32_t (&r)[32], const float* xs,
                                                   float qn, float thr_d, int nvalid) {
-  // four independent shift chains of 8 columns each, joined at the end
   unsigned int rej[4] = {0u, 0u, 0u, 0u};
+  const unsigned long long thr2 = pack2(thr_d, thr_d);
   float x[32];
   if (METRIC == MF_METRIC_L2) {
     // xs is 16-byte aligned (chunk offsets are multiples of 32 floats)
@@ -205,16 +235,22 @@ __device__ __forceinline__ unsigned int tq_accept(const uint32_t (&r)[32], const
       x[4 * i + 3] = t.w;
     }
   }
+  const unsigned long long qn2 = pack2(qn, qn);
+  const unsigned long long m2 = pack2(-2.0f, -2.0f);
 #pragma unroll
-  for (int i = 7; i >= 0; --i) {
+  for (int p = 3; p >= 0; --p) {
 #pragma unroll
     for (int g = 0; g < 4; ++g) {
-      const int j = 8 * g + i;
-      const float dot = __uint_as_float(r[j]);
-      float diff;
-      if (METRIC == MF_METRIC_L2) diff = __fsub_rn(thr_d, fmaf(-2.0f, dot, __fadd_rn(qn, x[j])));
-      else diff = __fadd_rn(thr_d, dot);
-      rej[g] = __funnelshift_l(__float_as_uint(diff), rej[g], 1);
+      const int j = 8 * g + 2 * p;  // columns j (low half) and j + 1 (high half)
+      const unsigned long long dot2 =
+          static_cast<unsigned long long>(r[j]) | (static_cast<unsigned long long>(r[j + 1]) << 32);
+      unsigned long long diff2;
+      if (METRIC == MF_METRIC_L2)
+        diff2 = sub2(thr2, fma2(m2, dot2, add2(qn2, pack2(x[j], x[j + 1]))));
+      else
+        diff2 = add2(thr2, dot2);
+      rej[g] = __funnelshift_l(static_cast<unsigned int>(diff2 >> 32), rej[g], 1);
+      rej[g] = __funnelshift_l(static_cast<unsigned int>(diff2), rej[g], 1);
     }
   }
   const unsigned int all = rej[0] | (rej[1] << 8) | (rej[2] << 16) | (rej[3] << 24);
@@ -241,8 +277,8 @@ __global__ void __launch_bounds__(ATM ? kTqThreadsAtm : kTqThreads, 1)
   uint64_t* afull = qempty + kTqQueue;  // query tile written to tensor memory
   uint64_t* afree = afull + 1;          // MMAs of the previous item done with it
   uint64_t* mdone = afree + 1;          // every MMA of this CTA has completed
-  int* s_items = reinterpret_cast<int*>(mdone + 1);
-  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(s_items + kTqQueue);
+  QSlot* s_q = reinterpret_cast<QSlot*>(mdone + 1);
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(s_q + kTqQueue);
   int* s_abort = reinterpret_cast<int*>(s_tmem + 1);
   uint32_t* s_seq = reinterpret_cast<uint32_t*>(s_abort + 1);  // [0] consumed, [1] issued
 
@@ -307,10 +343,12 @@ __global__ void __launch_bounds__(ATM ? kTqThreadsAtm : kTqThreads, 1)
           mbar_wait(&qempty[qs], ((qi / kTqQueue) - 1) & 1, s_abort, &g_device_error);
         int item = *s_abort ? -1 : atomicAdd(a.counter, 1);
         if (item >= total) item = -1;
-        s_items[qs] = item;
+        ItemDesc it{};
+        if (item >= 0) it = item_desc(a, item);
+        s_q[qs].it = it;
+        s_q[qs].item = item;
         mbar_arrive(&qfull[qs]);
         if (item < 0) break;
-        const ItemDesc it = item_desc(a, item);
         const long long nrows = it.re > it.rb ? it.re - it.rb : 0;
         const int nT = (int)((nrows + BN - 1) / BN);
         for (int t = 0; t < nT && !*s_abort; ++t) {
@@ -344,10 +382,10 @@ __global__ void __launch_bounds__(ATM ? kTqThreadsAtm : kTqThreads, 1)
       for (uint32_t qi = 0;; ++qi) {
         const int qs = qi % kTqQueue;
         if (!mbar_wait(&qfull[qs], (qi / kTqQueue) & 1, s_abort, &g_device_error)) break;
-        const int item = s_items[qs];
+        const int item = s_q[qs].item;
+        const ItemDesc it = s_q[qs].it;
         mbar_arrive(&qempty[qs]);
         if (item < 0) break;
-        const ItemDesc it = item_desc(a, item);
         const long long nrows = it.re > it.rb ? it.re - it.rb : 0;
         const int nT = (int)((nrows + BN - 1) / BN);
         if (ATM) {
@@ -417,11 +455,11 @@ __global__ void __launch_bounds__(ATM ? kTqThreadsAtm : kTqThreads, 1)
     for (uint32_t qi = 0;; ++qi) {
       const int qs = qi % kTqQueue;
       if (!mbar_wait(&qfull[qs], (qi / kTqQueue) & 1, s_abort, &g_device_error)) break;
-      const int item = s_items[qs];
+      const int item = s_q[qs].item;
+      const ItemDesc it = s_q[qs].it;
       __syncwarp();
       if (lane == 0) mbar_arrive(&qempty[qs]);
       if (item < 0) break;
-      const ItemDesc it = item_desc(a, item);
       const float* src = nullptr;
       if (row < it.nq_item) {
         const long long q = a.flat ? (long long)it.a_row0 + row : a.pairs[it.a_row0 + row] / a.P;
@@ -541,11 +579,11 @@ __global__ void __launch_bounds__(ATM ? kTqThreadsAtm : kTqThreads, 1)
     for (uint32_t qi = 0;; ++qi) {
       const int qs = qi % kTqQueue;
       if (!mbar_wait(&qfull[qs], (qi / kTqQueue) & 1, s_abort, &g_device_error)) break;
-      const int item = s_items[qs];
+      const int item = s_q[qs].item;
+      const ItemDesc it = s_q[qs].it;
       __syncwarp();
       if (lane == 0) mbar_arrive(&qempty[qs]);
       if (item < 0) break;
-      const ItemDesc it = item_desc(a, item);
       const long long nrows = it.re > it.rb ? it.re - it.rb : 0;
       const int nT = (int)((nrows + BN - 1) / BN);
       const bool valid = tid < it.nq_item;
@@ -589,11 +627,8 @@ __global__ void __launch_bounds__(ATM ? kTqThreadsAtm : kTqThreads, 1)
             // the next item, if the producer has published it already
             const uint32_t nq = qi + 1;
             if (mbar_test(&qfull[nq % kTqQueue], (nq / kTqQueue) & 1)) {
-              const int nitem = s_items[nq % kTqQueue];
-              if (nitem >= 0) {
-                const ItemDesc nx = item_desc(a, nitem);
-                if (nx.re > nx.rb) load_norms(nx.rb, nx.re);
-              }
+              const QSlot& ns = s_q[nq % kTqQueue];
+              if (ns.item >= 0 && ns.it.re > ns.it.rb) load_norms(ns.it.rb, ns.it.re);
             }
           }
         }
@@ -664,11 +699,14 @@ __global__ void __launch_bounds__(ATM ? kTqThreadsAtm : kTqThreads, 1)
 #endif
       const unsigned int pending = __ballot_sync(0xffffffffu, cnt > 0);
       if (pending) merge_rows(pending, cnt, thr, bound);
-      for (int qq = 0; qq < 32; ++qq) {
+      // the warp's 32 rows x k results, one per lane per step: the k steps are
+      // independent, so their id lookups overlap
+      for (int e = lane; e < 32 * k; e += 32) {
+        const int qq = e / k;
+        const int kk = e - qq * k;
         const long long sq = __shfl_sync(0xffffffffu, slot, qq);
-        if (sq < 0) continue;
-        if (lane < k) {
-          const unsigned long long key = my_lists[qq * kTqK + lane];
+        if (sq >= 0) {
+          const unsigned long long key = my_lists[qq * kTqK + kk];
           float dv;
           long long lv;
           if (key == kEmptyKey) {
@@ -679,8 +717,8 @@ __global__ void __launch_bounds__(ATM ? kTqThreadsAtm : kTqThreads, 1)
             const unsigned int pos = key_index(key);
             lv = a.ids ? a.ids[pos] : (long long)pos;
           }
-          a.out_d[sq * k + lane] = dv;
-          a.out_l[sq * k + lane] = lv;
+          a.out_d[sq * k + kk] = dv;
+          a.out_l[sq * k + kk] = lv;
         }
       }
       __syncwarp();
