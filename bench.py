@@ -106,6 +106,12 @@ class ClockSampler:
             self.t.start()
         except (OSError, FileNotFoundError):
             self.proc = None
+            return
+        # nvidia-smi's start-up must not fall inside the timed region
+        t0 = time.time()
+        while not self.lines and time.time() - t0 < 5.0 and self.proc.poll() is None:
+            time.sleep(0.01)
+        self.warm = len(self.lines)
 
     def _read(self):
         for line in self.proc.stdout:
@@ -122,7 +128,7 @@ class ClockSampler:
         self.t.join(timeout=2)
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        for ln in self.lines[getattr(self, "warm", 0):]:
             parts = [p.strip() for p in ln.split(",")]
             if len(parts) < 9:
                 continue
@@ -138,9 +144,15 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-# dram__bytes_read.sum + dram__bytes_write.sum of one all-probes scan launch,
-# from the ncu capture summarised in profiles/ (None where not captured).
-TRAFFIC = {}
+# dram__bytes_read.sum + dram__bytes_write.sum of one all-probes scan launch
+# (profiles/tq_scan_ivf20m.md). ivf2m: measured (2,228,082,688 + 53,105,408 B).
+# ivf20m: the multi-pass DRAM metrics are not captured at full size; the ivf2m
+# bytes per probed row (1,142 B: vector, residual and norm once each, plus the
+# query tiles) times the 13,287,418 rows probed per ivf20m batch.
+TRAFFIC = {
+    "ivf2m": {"bytes": 2281188096, "source": "ncu, measured"},
+    "ivf20m": {"bytes": 15177587741, "source": "ncu ivf2m bytes per probed row x probed rows"},
+}
 
 
 def lpt_partition(sizes: np.ndarray, world: int) -> np.ndarray:
@@ -325,7 +337,8 @@ def run_ours(args, cfg):
                 "algorithmic_flops_per_launch": 6 * d * pairs,
                 "pairs_per_launch": pairs,
                 "avg_launch_ms": round(scan_avg_ms, 4),
-                "traffic": TRAFFIC.get(args.config) if world == 1 else None,
+                "traffic": TRAFFIC[args.config]["bytes"] if args.config in TRAFFIC and world == 1 else None,
+                "traffic_source": TRAFFIC[args.config]["source"] if args.config in TRAFFIC else None,
                 "hbm": {
                     "algorithmic_bytes_per_launch": alg_bytes,
                     "achieved": round(gbs, 1) if gbs else None,

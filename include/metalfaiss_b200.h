@@ -177,6 +177,38 @@ MF_API int mf_ivf_search_preassigned(int device, void* stream, const float* xq, 
                               float* distances, int64_t* labels, void* workspace,
                               size_t workspace_bytes);
 
+/* The two halves of mf_ivf_search_preassigned, for an index whose lists are
+ * spread over several GPUs (one process per GPU, each holding some lists):
+ *
+ * mf_ivf_probe_bound writes bound[q] (nq floats): an upper bound on query q's
+ * k-th smallest distance over all of its probed lists, taken from the first
+ * rows of its first probe (probes[q*nprobe]), or +inf where this process holds
+ * no rows of that list. The minimum of the ranks' bounds (an all-reduce) is a
+ * bound for every rank.
+ *
+ * mf_ivf_search_bounded is mf_ivf_search_preassigned with that bound given:
+ * rows farther than bound[q] are not kept, so a rank's results may hold fewer
+ * than k rows (padded +inf, -1); merged over the ranks they are the exact
+ * top-k. Replaces the sharded IVF search the reference's multi-GPU tests expect
+ * (python/metalfaiss/unittest/test_mlx_multi_gpu.py:86-119). Both take the
+ * mf_ivf_search_preassigned_workspace_size workspace. */
+MF_API int mf_ivf_probe_bound(int device, void* stream, const float* xq, int64_t nq,
+                              const int64_t* probes, int nprobe, int nlist,
+                              const int64_t* list_offsets, const float* list_vecs,
+                              const float* list_norms, const float* list_lo,
+                              const int64_t* list_ids, int64_t ntotal, const int32_t* list_order,
+                              int d, int metric, int k, float* bound, void* workspace,
+                              size_t workspace_bytes);
+
+MF_API int mf_ivf_search_bounded(int device, void* stream, const float* xq, int64_t nq,
+                                 const int64_t* probes, int nprobe, int nlist,
+                                 const int64_t* list_offsets, const float* list_vecs,
+                                 const float* list_norms, const float* list_lo,
+                                 const int64_t* list_ids, int64_t ntotal,
+                                 const int32_t* list_order, int d, int metric, int k,
+                                 const float* bound, float* distances, int64_t* labels,
+                                 void* workspace, size_t workspace_bytes);
+
 /* ----------------------------------------------------------- merge, k-means */
 
 /* Merge `parts` partial top-k lists per query: in (nq, parts, k_in) ascending,

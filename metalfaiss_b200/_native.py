@@ -39,6 +39,8 @@ _SIGNATURES = {
     "mf_ivf_search": ([I32, P, P, I64, P, P, I32, I32, P, P, P, P, P, I64, P, I32, I32, I32, P, P, P, SZ], I32),
     "mf_ivf_search_preassigned_workspace_size": ([I64, I32, I32, I32, I32, I32, PSZ], I32),
     "mf_ivf_search_preassigned": ([I32, P, P, I64, P, I32, I32, P, P, P, P, P, I64, P, I32, I32, I32, P, P, P, SZ], I32),
+    "mf_ivf_probe_bound": ([I32, P, P, I64, P, I32, I32, P, P, P, P, P, I64, P, I32, I32, I32, P, P, SZ], I32),
+    "mf_ivf_search_bounded": ([I32, P, P, I64, P, I32, I32, P, P, P, P, P, I64, P, I32, I32, I32, P, P, P, P, SZ], I32),
     "mf_topk_merge": ([I32, P, P, P, I64, I32, I32, I32, P, P], I32),
     "mf_kmeans_assign_workspace_size": ([I64, I32, I32, PSZ], I32),
     "mf_kmeans_assign": ([I32, P, P, I64, P, P, I32, I32, P, P, P, SZ], I32),

@@ -149,11 +149,16 @@ int coarse_metric(int metric) {
   return metric == MF_METRIC_INNER_PRODUCT ? MF_METRIC_INNER_PRODUCT : MF_METRIC_L2;
 }
 
+// bound_out != NULL: run only the bound pass and write each query's bound
+// there (+inf where its first probe holds no rows). bound_in != NULL: skip the
+// bound pass and filter the all-probes pass by bound_in (a bound computed
+// elsewhere, e.g. the minimum over the ranks that hold the lists).
 int ivf_scan_topk(int device, cudaStream_t stream, const IvfWs& w, const float* xq, int64_t nq,
                   const int64_t* probes, int P, int nlist, const int64_t* list_offsets,
                   const float* list_vecs, const float* list_norms, const float* list_lo,
                   const int64_t* list_ids, int64_t ntotal, const int32_t* list_order, int d,
-                  int metric, int k, float* D, int64_t* I) {
+                  int metric, int k, float* D, int64_t* I, float* bound_out = nullptr,
+                  const float* bound_in = nullptr) {
   const bool tc = list_lo != nullptr && tc_eligible(metric, d, k, ntotal);
   if (metric == MF_METRIC_L2) MF_TRY(launch_norms(xq, nq, d, w.qn, stream));
   ScanArgs a{};
@@ -185,16 +190,17 @@ int ivf_scan_topk(int device, cudaStream_t stream, const IvfWs& w, const float* 
   // the engines' rounding difference, so phase 2 still drops no row that
   // belongs to the top-k.
   constexpr int64_t kBoundRows = 128;
-  const int phases = P > 1 ? 2 : 1;
+  const int phases = (bound_out || bound_in) ? 1 : (P > 1 ? 2 : 1);
+  float* const bound_dst = bound_out ? bound_out : w.bound;
   for (int ph = 0; ph < phases; ++ph) {
-    const bool bounding = phases == 2 && ph == 0;
+    const bool bounding = bound_out != nullptr || (phases == 2 && ph == 0);
     const bool simt_bound = bounding && tc && metric == MF_METRIC_L2;
     const bool use_tc = tc && !simt_bound;
     MF_TRY(run_ivf_groups_ex(w.g, probes, nq, P, nlist, list_offsets, list_order, w.pd, w.pl, k,
                              nullptr, use_tc ? tc_group() : kScanTQ, stream, 0,
                              bounding ? 1 : P));
     a.max_rows = bounding ? kBoundRows : 0;
-    a.bound = (phases == 2 && ph == 1) ? w.bound : nullptr;
+    a.bound = bound_in ? bound_in : ((phases == 2 && ph == 1) ? w.bound : nullptr);
     if (use_tc && tc_raw_queries(d, k)) {
       // the scan loads each item's queries itself (through a.pairs)
       MF_TRY(launch_tc_scan(a, metric, nullptr, nq, list_lo, ntotal, nq * P, device, stream));
@@ -210,10 +216,11 @@ int ivf_scan_topk(int device, cudaStream_t stream, const IvfWs& w, const float* 
     }
     if (simt_bound)
       MF_TRY(launch_extract_bound_slack(w.pd, nq, P, k, probes, list_offsets, list_norms, w.qn,
-                                        kBoundRows, d, w.bound, stream));
+                                        kBoundRows, d, bound_dst, stream));
     else if (bounding)
-      MF_TRY(launch_extract_bound(w.pd, nq, P, k, w.bound, stream));
+      MF_TRY(launch_extract_bound(w.pd, nq, P, k, bound_dst, stream));
   }
+  if (bound_out) return MF_OK;
   MF_TRY(launch_merge(w.pd, w.pl, nq, P, k, k, D, I, stream));
   return MF_OK;
 }
@@ -380,6 +387,64 @@ int mf_ivf_search_preassigned(int device, void* stream, const float* xq, int64_t
   return ivf_scan_topk(device, (cudaStream_t)stream, w, xq, nq, probes, nprobe, nlist,
                        list_offsets, list_vecs, list_norms, list_lo, list_ids, ntotal, list_order,
                        d, metric, k, distances, labels);
+}
+
+namespace {
+int ivf_preassigned_entry(int device, void* stream, const float* xq, int64_t nq,
+                          const int64_t* probes, int nprobe, int nlist, const int64_t* list_offsets,
+                          const float* list_vecs, const float* list_norms, const float* list_lo,
+                          const int64_t* list_ids, int64_t ntotal, const int32_t* list_order, int d,
+                          int metric, int k, float* distances, int64_t* labels, float* bound_out,
+                          const float* bound_in, void* workspace, size_t workspace_bytes) {
+  MF_TRY(check_common(d, metric, k, true));
+  MF_CHECK(nlist >= 1 && nprobe >= 1, MF_ERR_INVALID_ARGS, "nlist=%d nprobe=%d", nlist, nprobe);
+  MF_CHECK(nq >= 0 && nq * nprobe < (1ll << 31), MF_ERR_INVALID_ARGS, "nq*nprobe too large");
+  if (nq == 0) return MF_OK;
+  MF_TRY(check_device_ptr(xq, "xq"));
+  MF_TRY(check_device_ptr(probes, "probes"));
+  MF_TRY(check_ivf_lists(list_offsets, list_vecs, list_norms, list_ids, list_order, metric));
+  if (bound_out) {
+    MF_TRY(check_device_ptr(bound_out, "bound"));
+  } else {
+    MF_TRY(check_device_ptr(distances, "distances"));
+    MF_TRY(check_device_ptr(labels, "labels"));
+  }
+  if (bound_in) MF_TRY(check_device_ptr(bound_in, "bound"));
+  MF_TRY(check_device_ptr(workspace, "workspace"));
+  Carver c(workspace, workspace_bytes);
+  IvfWs w = carve_ivf(c, nq, nlist, nprobe, d, k, 1, device);
+  MF_CHECK(c.fits(), MF_ERR_INVALID_ARGS, "workspace too small: %zu < %zu bytes",
+           workspace_bytes, c.used);
+  return ivf_scan_topk(device, (cudaStream_t)stream, w, xq, nq, probes, nprobe, nlist,
+                       list_offsets, list_vecs, list_norms, list_lo, list_ids, ntotal, list_order,
+                       d, metric, k, distances, labels, bound_out, bound_in);
+}
+}  // namespace
+
+int mf_ivf_probe_bound(int device, void* stream, const float* xq, int64_t nq,
+                       const int64_t* probes, int nprobe, int nlist, const int64_t* list_offsets,
+                       const float* list_vecs, const float* list_norms, const float* list_lo,
+                       const int64_t* list_ids, int64_t ntotal, const int32_t* list_order, int d,
+                       int metric, int k, float* bound, void* workspace, size_t workspace_bytes) {
+  MF_ENTER(device);
+  return ivf_preassigned_entry(device, stream, xq, nq, probes, nprobe, nlist, list_offsets,
+                               list_vecs, list_norms, list_lo, list_ids, ntotal, list_order, d,
+                               metric, k, nullptr, nullptr, bound, nullptr, workspace,
+                               workspace_bytes);
+}
+
+int mf_ivf_search_bounded(int device, void* stream, const float* xq, int64_t nq,
+                          const int64_t* probes, int nprobe, int nlist,
+                          const int64_t* list_offsets, const float* list_vecs,
+                          const float* list_norms, const float* list_lo, const int64_t* list_ids,
+                          int64_t ntotal, const int32_t* list_order, int d, int metric, int k,
+                          const float* bound, float* distances, int64_t* labels, void* workspace,
+                          size_t workspace_bytes) {
+  MF_ENTER(device);
+  return ivf_preassigned_entry(device, stream, xq, nq, probes, nprobe, nlist, list_offsets,
+                               list_vecs, list_norms, list_lo, list_ids, ntotal, list_order, d,
+                               metric, k, distances, labels, nullptr, bound, workspace,
+                               workspace_bytes);
 }
 
 int mf_topk_merge(int device, void* stream, const float* part_distances,

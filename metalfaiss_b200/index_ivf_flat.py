@@ -299,6 +299,46 @@ class IVFFlatIndex:
                  nat.ptr(ws), ws.numel())
         return SearchResult(D, I)
 
+    # ------------------------------------------- halves for sharded searches
+    def _ivf_args(self, xq, probes, k):
+        nq, P = xq.shape[0], probes.shape[1]
+        m = int(self.metric_type)
+        nbytes = nat.workspace_size("mf_ivf_search_preassigned_workspace_size", nq, self._nlist, P,
+                                    self._dp, m, k)
+        ws = self._workspace().get(nbytes)
+        head = (self.device.index, nat.stream_of(self.device), nat.ptr(xq), nq, nat.ptr(probes), P,
+                self._nlist, nat.ptr(self._offsets), nat.ptr(self._vecs), nat.ptr(self._norms),
+                nat.ptr(self._lo), nat.ptr(self._ids), self._vecs.shape[0], nat.ptr(self._order),
+                self._dp, m, k)
+        return head, ws
+
+    def _probe_bound(self, xq: torch.Tensor, probes: torch.Tensor, k: int) -> torch.Tensor:
+        """Per query, an upper bound on its k-th distance over its probes, from
+        the first rows of its first probe; +inf where this index holds no rows
+        of that list (mf_ivf_probe_bound)."""
+        bound = torch.full((xq.shape[0],), float("inf"), dtype=torch.float32, device=self.device)
+        if xq.shape[0] == 0 or probes.shape[1] == 0:
+            return bound
+        self._empty_lists_guard()
+        head, ws = self._ivf_args(xq, probes, k)
+        nat.call("mf_ivf_probe_bound", *head, nat.ptr(bound), nat.ptr(ws), ws.numel())
+        return bound
+
+    def _search_bounded(self, xq: torch.Tensor, k: int, probes: torch.Tensor,
+                        bound: torch.Tensor) -> SearchResult:
+        """search_preassigned keeping only rows within bound[q]
+        (mf_ivf_search_bounded); fewer than k rows come back padded."""
+        nq = xq.shape[0]
+        D = torch.full((nq, k), float("inf"), dtype=torch.float32, device=self.device)
+        I = torch.full((nq, k), -1, dtype=torch.int64, device=self.device)
+        if nq == 0 or k == 0 or probes.shape[1] == 0:
+            return SearchResult(D, I)
+        self._empty_lists_guard()
+        head, ws = self._ivf_args(xq, probes, k)
+        nat.call("mf_ivf_search_bounded", *head, nat.ptr(bound), nat.ptr(D), nat.ptr(I),
+                 nat.ptr(ws), ws.numel())
+        return SearchResult(D, I)
+
     def range_search(self, xs, radius: float) -> SearchRangeResult:
         """Exact range search over the nprobe nearest lists (probe order, then
         list order); see FlatIndex.range_search for the reference's capped form."""

@@ -7,11 +7,16 @@ sharded with a shared quantizer (:86-119), and its facade stubs IndexShards
 (python/metalfaiss/faiss_compat.py:326-366).
 
 * IVFFlat: inverted lists are partitioned over the ranks by greedy LPT on list
-  size; the coarse quantizer is replicated. Each rank scans only the lists it
-  owns and yields a local (nq, k) top-k.
-* Flat: contiguous row shards; labels are global ids.
-The one exchange step is an all-gather of the (nq, k) partial results over
-NCCL (torch.distributed), followed by the on-device merge kernel.
+  size; the coarse quantizer is replicated. A search exchanges three things:
+  1. each rank runs the coarse step for its share of the queries and the
+     (nq, nprobe) probe lists are all-gathered;
+  2. each rank computes, for the queries whose nearest list it holds, an
+     upper bound on the k-th distance (the first rows of that list), and a
+     MIN all-reduce gives every rank every query's bound;
+  3. each rank scans only the lists it owns, keeping rows within the bound,
+     and the (nq, k) partial results are all-gathered and merged on device.
+* Flat: contiguous row shards; labels are global ids; one all-gather + merge.
+Collectives go through torch.distributed (NCCL on GPUs, gloo in CPU tests).
 """
 from __future__ import annotations
 
@@ -64,6 +69,28 @@ def gather_partials(D: torch.Tensor, I: torch.Tensor, group=None):
         gd = torch.stack(ld)
         gi = torch.stack(li)
     return gd.permute(1, 0, 2).contiguous(), gi.permute(1, 0, 2).contiguous()
+
+
+def gather_rows(local: torch.Tensor, n: int, group=None) -> torch.Tensor:
+    """All-gather of row shards: rank r holds rows row_shard(n, r, world) of an
+    (n, ...) array; every rank gets the whole array, in row order."""
+    world = dist.get_world_size(group)
+    m = -(-n // world) if n else 0
+    buf = torch.zeros((m,) + tuple(local.shape[1:]), dtype=local.dtype, device=local.device)
+    buf[: local.shape[0]] = local
+    if dist.get_backend(group) == "nccl":
+        out = torch.empty((world * m,) + tuple(local.shape[1:]), dtype=local.dtype,
+                          device=local.device)
+        dist.all_gather_into_tensor(out, buf.contiguous(), group=group)
+        parts = list(out.split(m)) if m else [out] * world
+    else:
+        parts = [torch.empty_like(buf) for _ in range(world)]
+        dist.all_gather(parts, buf.contiguous(), group=group)
+    rows = []
+    for r in range(world):
+        b, e = row_shard(n, r, world)
+        rows.append(parts[r][: e - b])
+    return torch.cat(rows)
 
 
 def merge_partials(pd: torch.Tensor, pi: torch.Tensor, k: int) -> SearchResult:
@@ -125,7 +152,24 @@ class ShardedIVF:
         self.local.nprobe = v
 
     def search(self, xq, k: int) -> SearchResult:
-        local = self.local.search(xq, k)
+        idx = self.local
+        xq = idx._prepare_query(xq)
+        k = int(k)
+        nq = xq.shape[0]
+        idx._check_k(k)
+        P = min(idx.nprobe, idx.nlist)
+        # 1. coarse step over this rank's share of the queries
+        b, e = row_shard(nq, self.rank, self.world)
+        if e > b:
+            mine = idx.quantizer._search_padded(xq[b:e], P, map_ids=False).labels
+        else:
+            mine = torch.empty((0, P), dtype=torch.int64, device=idx.device)
+        probes = gather_rows(mine, nq, self.group).contiguous()
+        # 2. bounds from the ranks that hold each query's nearest list
+        bound = idx._probe_bound(xq, probes, k)
+        dist.all_reduce(bound, op=dist.ReduceOp.MIN, group=self.group)
+        # 3. this rank's lists, within the bound; then gather and merge
+        local = idx._search_bounded(xq, k, probes, bound)
         pd, pi = gather_partials(local.distances, local.labels, self.group)
         return merge_partials(pd, pi, k)
 

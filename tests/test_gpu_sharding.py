@@ -1,0 +1,67 @@
+"""The multi-GPU IVF search's device steps, with its ranks emulated in one
+process on one GPU: the lists split over W ranks by LPT (keep_lists), each
+rank's bound from mf_ivf_probe_bound, their minimum (what the MIN all-reduce
+gives every rank), each rank's mf_ivf_search_bounded over its own lists, and
+the on-device merge. The merged result must equal the unsharded search.
+The collectives themselves are covered on CPU ranks (test_sharding_gloo)."""
+import numpy as np
+import pytest
+import torch
+
+from metalfaiss_b200 import IVFFlatIndex, MetricType
+from metalfaiss_b200 import _native as nat
+from metalfaiss_b200 import synthetic as syn
+from metalfaiss_b200.sharding import keep_lists, lpt_partition, merge_partials
+from oracle import compare, oracle
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture
+def engine():
+    yield nat.set_scan_engine
+    nat.set_scan_engine(0)
+    assert nat.device_error(0) == 0, "a bounded device wait timed out"
+
+
+def _index(metric, d=64, n=40000, nlist=96, seed=21):
+    x, cen, _ = syn.mixture(n, d, nlist, seed)
+    if metric == MetricType.INNER_PRODUCT:
+        x = x / np.linalg.norm(x, axis=1, keepdims=True)
+    idx = IVFFlatIndex(d, nlist, metric_type=metric)
+    idx.set_centroids(oracle.kmeans_train(x, nlist, 2, seed))
+    idx.add(x)
+    xq, _, _ = syn.mixture(500, d, nlist, seed + 1, centres=cen)
+    if metric == MetricType.INNER_PRODUCT:
+        xq = xq / np.linalg.norm(xq, axis=1, keepdims=True)
+    return idx, x, xq
+
+
+@pytest.mark.parametrize("eng", [0, 1])
+@pytest.mark.parametrize("metric", [MetricType.L2, MetricType.INNER_PRODUCT])
+@pytest.mark.parametrize("world", [2, 3])
+def test_emulated_ranks_equal_single(cuda_device, engine, eng, metric, world):
+    nat.set_scan_engine(eng)
+    idx, x, xq_np = _index(metric)
+    idx.nprobe = 8
+    k = 10
+    ref = idx.search(xq_np, k)
+    xq = idx._prepare_query(xq_np)
+    probes = idx.quantizer._search_padded(xq, idx.nprobe, map_ids=False).labels.contiguous()
+    owners = lpt_partition(idx.list_sizes(), world)
+    shards = [keep_lists(idx, owners == r) for r in range(world)]
+    bounds = [s._probe_bound(xq, probes, k) for s in shards]
+    bound = torch.stack(bounds).min(0).values
+    # every query's bound comes from the one rank holding its nearest list
+    finite = torch.stack([torch.isfinite(b) for b in bounds]).sum(0)
+    assert int(finite.max()) <= 1
+    parts = [s._search_bounded(xq, k, probes, bound) for s in shards]
+    pd = torch.stack([p.distances for p in parts], 1).contiguous()
+    pi = torch.stack([p.labels for p in parts], 1).contiguous()
+    got = merge_partials(pd, pi, k)
+    D, I = got.numpy()
+    D_ref, I_ref = ref.numpy()
+    m = oracle.L2 if metric == MetricType.L2 else oracle.INNER_PRODUCT
+    atol = compare.l2_atol(xq_np, x) if metric == MetricType.L2 else 1e-5 * (1 + np.abs(D_ref).max())
+    errs = compare.check_knn(D, I, D_ref, I_ref, compare.exact_lookup(xq_np, x, m), atol=atol)
+    assert not errs, errs[:5]

@@ -17,7 +17,7 @@ import numpy as np
 import pytest
 import torch
 
-from metalfaiss_b200.sharding import gather_partials, lpt_partition, row_shard
+from metalfaiss_b200.sharding import gather_partials, gather_rows, lpt_partition, row_shard
 from oracle import oracle
 
 WORLD = 2
@@ -103,6 +103,63 @@ def _ivf_worker(rank, port, out_dir):
         dist.destroy_process_group()
 
 
+def _bound_of(xq, offsets, vecs, probes, k, owned, rows=128):
+    """The bound a rank contributes: the k-th distance over the first `rows`
+    rows of each query's first probe where this rank holds that list, else inf."""
+    out = np.full(len(xq), np.inf, np.float32)
+    for q in range(len(xq)):
+        l = probes[q, 0]
+        if l < 0 or not owned[l]:
+            continue
+        a, b = offsets[l], min(offsets[l + 1], offsets[l] + rows)
+        if b - a < k:
+            continue
+        d = oracle.pairwise_f32(xq[q:q + 1], vecs[a:b], oracle.L2)[0]
+        out[q] = np.sort(d)[k - 1]
+    return out
+
+
+def _ivf_bound_worker(rank, port, out_dir):
+    """The multi-GPU IVF search's exchange steps: coarse probes computed for
+    a row shard of the queries and all-gathered, bounds MIN-reduced, bounded
+    local scans, merge."""
+    dist = _init(rank, port)
+    try:
+        cents, offsets, vecs, ids, xq = _ivf_data()
+        nprobe, k = 5, 7
+        owners = lpt_partition(np.diff(offsets), WORLD)
+        b, e = row_shard(len(xq), rank, WORLD)
+        mine = torch.from_numpy(oracle.coarse_probes(xq[b:e], cents, nprobe).astype(np.int64))
+        probes = gather_rows(mine, len(xq)).numpy()
+        assert np.array_equal(probes, oracle.coarse_probes(xq, cents, nprobe))
+        bound = torch.from_numpy(_bound_of(xq, offsets, vecs, probes, k, owners == rank))
+        dist.all_reduce(bound, op=dist.ReduceOp.MIN)
+        local = np.where(owners[probes] == rank, probes, -1)
+        D, I = oracle.ivf_search(xq, cents, offsets, vecs, ids, nprobe, k, probes=local)
+        keep = D <= bound.numpy()[:, None]
+        D = np.where(keep, D, np.inf).astype(np.float32)
+        I = np.where(keep, I, -1)
+        pd, pi = gather_partials(torch.from_numpy(D), torch.from_numpy(I))
+        Dm, Im = _merge(pd.numpy(), pi.numpy(), k)
+        np.savez(os.path.join(out_dir, f"ivfb{rank}.npz"), D=Dm, I=Im)
+    finally:
+        dist.destroy_process_group()
+
+
+def _gather_rows_worker(rank, port, out_dir):
+    dist = _init(rank, port)
+    try:
+        for n in (0, 1, 5, 8):
+            full = torch.arange(n * 3, dtype=torch.int64).reshape(n, 3)
+            b, e = row_shard(n, rank, WORLD)
+            got = gather_rows(full[b:e], n)
+            assert torch.equal(got, full), (n, got, full)
+        with open(os.path.join(out_dir, f"rows{rank}.txt"), "w") as f:
+            f.write("ok")
+    finally:
+        dist.destroy_process_group()
+
+
 def _leaving_worker(rank, port, out_dir):
     """Rank 1 leaves between steps (after set-up, before the exchange); rank 0
     must get an error from its next collective instead of waiting forever."""
@@ -183,3 +240,19 @@ def test_rank_leaving_before_exchange_is_reported_gloo():
         assert codes == [0, 3]
         with open(os.path.join(tmp, "leave0.txt")) as f:
             assert f.read().startswith("raised"), "rank 0 did not see the failure"
+
+
+def test_gather_rows_gloo():
+    with tempfile.TemporaryDirectory() as tmp:
+        assert _run(_gather_rows_worker, tmp) == [0, 0]
+
+
+def test_sharded_ivf_bound_exchange_equals_single_gloo():
+    with tempfile.TemporaryDirectory() as tmp:
+        assert _run(_ivf_bound_worker, tmp) == [0, 0]
+        cents, offsets, vecs, ids, xq = _ivf_data()
+        D_ref, I_ref = oracle.ivf_search(xq, cents, offsets, vecs, ids, 5, 7)
+        for r in range(WORLD):
+            z = np.load(os.path.join(tmp, f"ivfb{r}.npz"))
+            assert np.array_equal(z["I"], I_ref)
+            assert np.array_equal(z["D"], D_ref)
