@@ -240,6 +240,19 @@ MF_API int mf_kmeans_update(int device, void* stream, const float* x, int64_t n,
                      const int64_t* labels, int nc, float* centroids, int64_t* counts,
                      void* workspace, size_t workspace_bytes);
 
+/* The update split in two for training over several GPUs (each holding a
+ * share of the points, centroids replicated): mf_kmeans_sums writes the
+ * per-cluster fp64 sums (nc x d) and sizes of this share (same workspace as
+ * mf_kmeans_update); after a SUM all-reduce of both, mf_kmeans_apply sets
+ * centroids[j] = sums[j] / counts[j], leaving empty clusters unchanged.
+ * Replaces the same steps of python/metalfaiss/clustering/any_clustering.py:109-120;
+ * the reference trains on one device only. */
+MF_API int mf_kmeans_sums(int device, void* stream, const float* x, int64_t n, int d,
+                          const int64_t* labels, int nc, double* sums, int64_t* counts,
+                          void* workspace, size_t workspace_bytes);
+MF_API int mf_kmeans_apply(int device, void* stream, const double* sums, const int64_t* counts,
+                           int nc, int d, float* centroids);
+
 /* ------------------------------------------------------------- IVF build */
 
 MF_API int mf_ivf_add_workspace_size(int64_t n_old, int64_t n_new, int nlist, size_t* bytes);

@@ -46,6 +46,8 @@ _SIGNATURES = {
     "mf_kmeans_assign": ([I32, P, P, I64, P, P, I32, I32, P, P, P, SZ], I32),
     "mf_kmeans_update_workspace_size": ([I64, I32, I32, PSZ], I32),
     "mf_kmeans_update": ([I32, P, P, I64, I32, P, I32, P, P, P, SZ], I32),
+    "mf_kmeans_sums": ([I32, P, P, I64, I32, P, I32, P, P, P, SZ], I32),
+    "mf_kmeans_apply": ([I32, P, P, P, I32, I32, P], I32),
     "mf_ivf_add_workspace_size": ([I64, I64, I32, PSZ], I32),
     "mf_ivf_add": ([I32, P, I32, I32, P, P, P, P, I64, P, P, P, P, I64, P, P, P, P, P, SZ], I32),
     "mf_flat_range_workspace_size": ([I64, I64, I32, PSZ], I32),

@@ -88,6 +88,29 @@ def update(x: torch.Tensor, labels: torch.Tensor, centroids: torch.Tensor, works
     return counts
 
 
+def cluster_sums(x: torch.Tensor, labels: torch.Tensor, nc: int, workspace=None):
+    """Per-cluster fp64 sums (nc, d) and sizes of this device's points
+    (mf_kmeans_sums): the update's reduction, before any division."""
+    dev = x.device
+    n, dp = x.shape
+    sums = torch.empty((nc, dp), dtype=torch.float64, device=dev)
+    counts = torch.empty(nc, dtype=torch.int64, device=dev)
+    nbytes = nat.workspace_size("mf_kmeans_update_workspace_size", n, nc, dp)
+    ws, _ = _ws(dev, nbytes, workspace)
+    nat.call("mf_kmeans_sums", dev.index, nat.stream_of(dev), nat.ptr(x), n, dp, nat.ptr(labels),
+             nc, nat.ptr(sums), nat.ptr(counts), nat.ptr(ws), ws.numel())
+    return sums, counts
+
+
+def apply_sums(sums: torch.Tensor, counts: torch.Tensor, centroids: torch.Tensor) -> None:
+    """centroids[j] = sums[j] / counts[j] in place; empty clusters keep theirs
+    (mf_kmeans_apply)."""
+    dev = centroids.device
+    nc, dp = centroids.shape
+    nat.call("mf_kmeans_apply", dev.index, nat.stream_of(dev), nat.ptr(sums), nat.ptr(counts), nc,
+             dp, nat.ptr(centroids))
+
+
 def init_centroids(x: torch.Tensor, k: int, seed: int) -> torch.Tensor:
     """k distinct rows chosen by a seeded permutation (python/metalfaiss/index/ivf_pq_index.py:63;
     numpy PCG64 stands in for MLX's PRNG)."""

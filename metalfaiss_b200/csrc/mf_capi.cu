@@ -524,6 +524,34 @@ int mf_kmeans_update(int device, void* stream, const float* x, int64_t n, int d,
                            workspace, workspace_bytes);
 }
 
+int mf_kmeans_sums(int device, void* stream, const float* x, int64_t n, int d,
+                   const int64_t* labels, int nc, double* sums, int64_t* counts, void* workspace,
+                   size_t workspace_bytes) {
+  MF_ENTER(device);
+  MF_CHECK(d > 0 && nc >= 1 && n >= 0 && n < (1ll << 31) - 1, MF_ERR_INVALID_ARGS,
+           "bad k-means sums shape n=%lld d=%d nc=%d", (long long)n, d, nc);
+  MF_TRY(check_device_ptr(x, "x", n == 0));
+  MF_TRY(check_device_ptr(labels, "labels", n == 0));
+  MF_TRY(check_device_ptr(sums, "sums"));
+  MF_TRY(check_device_ptr(counts, "counts"));
+  MF_TRY(check_device_ptr(workspace, "workspace"));
+  MF_CHECK(workspace_bytes >= kmeans_update_bytes(n, nc), MF_ERR_INVALID_ARGS,
+           "k-means sums workspace too small: %zu < %zu", workspace_bytes,
+           kmeans_update_bytes(n, nc));
+  return run_kmeans_update((cudaStream_t)stream, x, n, d, labels, nc, nullptr, counts, workspace,
+                           workspace_bytes, sums);
+}
+
+int mf_kmeans_apply(int device, void* stream, const double* sums, const int64_t* counts, int nc,
+                    int d, float* centroids) {
+  MF_ENTER(device);
+  MF_CHECK(d > 0 && nc >= 1, MF_ERR_INVALID_ARGS, "bad k-means apply shape d=%d nc=%d", d, nc);
+  MF_TRY(check_device_ptr(sums, "sums"));
+  MF_TRY(check_device_ptr(counts, "counts"));
+  MF_TRY(check_device_ptr(centroids, "centroids"));
+  return launch_kmeans_apply(sums, counts, nc, d, centroids, (cudaStream_t)stream);
+}
+
 int mf_ivf_add_workspace_size(int64_t n_old, int64_t n_new, int nlist, size_t* bytes) {
   clear_error();
   (void)n_old;

@@ -271,16 +271,22 @@ __global__ void ivf_copy_new_kernel(const uint32_t* __restrict__ sorted_labels,
 
 // -------------------------------------------------------- k-means update
 // One CTA per cluster sums its rows (in sorted, i.e. input, order) in fp64.
+// One block per cluster: the fp64 sum of its rows in a fixed order, then
+// either the mean into `centroids` (an empty cluster keeps its centroid) or,
+// with `sums` given, the sums themselves (for a reduction over several GPUs).
 __global__ void kmeans_update_kernel(const float* __restrict__ x, int d,
                                      const int32_t* __restrict__ sorted_rows,
                                      const int* __restrict__ starts, int nc, float* centroids,
-                                     int64_t* counts) {
+                                     int64_t* counts, double* sums) {
   const int j = blockIdx.x;
   if (j >= nc) return;
   const int b = starts[j];
   const int e = starts[j + 1];
   const int cnt = e - b;
   if (threadIdx.x == 0 && counts) counts[j] = cnt;
+  if (cnt == 0 && sums) {
+    for (int c = threadIdx.x; c < d; c += blockDim.x) sums[(int64_t)j * d + c] = 0.0;
+  }
   if (cnt == 0) return;  // empty cluster keeps its centroid
   for (int c = threadIdx.x; c < d; c += blockDim.x) {
     double s0 = 0.0, s1 = 0.0, s2 = 0.0, s3 = 0.0;
@@ -293,8 +299,21 @@ __global__ void kmeans_update_kernel(const float* __restrict__ x, int d,
     }
     for (; i < e; ++i) s0 += (double)x[(int64_t)sorted_rows[i] * d + c];
     const double s = (s0 + s1) + (s2 + s3);
-    centroids[(int64_t)j * d + c] = (float)(s / (double)cnt);
+    if (sums)
+      sums[(int64_t)j * d + c] = s;
+    else
+      centroids[(int64_t)j * d + c] = (float)(s / (double)cnt);
   }
+}
+
+// centroids[j] = sums[j] / counts[j] where counts[j] > 0 (else unchanged).
+__global__ void kmeans_apply_kernel(const double* __restrict__ sums,
+                                    const int64_t* __restrict__ counts, int64_t nc, int d,
+                                    float* centroids) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= nc * d) return;
+  const int64_t cnt = counts[i / d];
+  if (cnt > 0) centroids[i] = (float)(sums[i] / (double)cnt);
 }
 
 }  // namespace
@@ -503,7 +522,7 @@ size_t kmeans_update_bytes(int64_t n, int nc) {
 
 int run_kmeans_update(cudaStream_t stream, const float* x, int64_t n, int d,
                       const int64_t* labels, int nc, float* centroids, int64_t* counts, void* ws,
-                      size_t ws_bytes) {
+                      size_t ws_bytes, double* sums) {
   Carver c(ws, ws_bytes);
   int* cnt = c.take<int>(nc);
   int* starts = c.take<int>((size_t)nc + 1);
@@ -527,7 +546,17 @@ int run_kmeans_update(cudaStream_t stream, const float* x, int64_t n, int d,
     }
   }
   const int threads = d >= 256 ? 256 : ((d + 31) / 32) * 32;
-  kmeans_update_kernel<<<nc, threads, 0, stream>>>(x, d, sr, starts, nc, centroids, counts);
+  kmeans_update_kernel<<<nc, threads, 0, stream>>>(x, d, sr, starts, nc, centroids, counts, sums);
+  MF_LAUNCH_CHECK();
+  return MF_OK;
+}
+
+int launch_kmeans_apply(const double* sums, const int64_t* counts, int nc, int d, float* centroids,
+                        cudaStream_t stream) {
+  const int64_t total = (int64_t)nc * d;
+  if (total <= 0) return MF_OK;
+  kmeans_apply_kernel<<<(unsigned int)ceil_div(total, 256), 256, 0, stream>>>(sums, counts, nc, d,
+                                                                              centroids);
   MF_LAUNCH_CHECK();
   return MF_OK;
 }

@@ -28,8 +28,12 @@ int run_ivf_add(cudaStream_t stream, int nlist, int d, const int64_t* old_offset
                 void* ws, size_t ws_bytes);
 
 size_t kmeans_update_bytes(int64_t n, int nc);
+// With sums != NULL, writes the per-cluster fp64 sums (nc x d) instead of
+// updating the centroids.
 int run_kmeans_update(cudaStream_t stream, const float* x, int64_t n, int d,
                       const int64_t* labels, int nc, float* centroids, int64_t* counts, void* ws,
-                      size_t ws_bytes);
+                      size_t ws_bytes, double* sums = nullptr);
+int launch_kmeans_apply(const double* sums, const int64_t* counts, int nc, int d, float* centroids,
+                        cudaStream_t stream);
 
 }  // namespace mf

@@ -134,6 +134,28 @@ def keep_lists(index, keep_mask: np.ndarray):
     return out
 
 
+def train_kmeans_sharded(x: torch.Tensor, k: int, niter: int, init: torch.Tensor,
+                         group=None) -> torch.Tensor:
+    """Lloyd's k-means over the union of every rank's points x (this rank's
+    share, padded rows as from the index): each iteration assigns the local
+    points, all-reduces the per-cluster fp64 sums and sizes, and applies the
+    same update on every rank, so the centroids stay identical everywhere.
+    `init` (k, padded d) must be the same on all ranks (e.g. broadcast from
+    rank 0). The reference trains on one device only
+    (python/metalfaiss/clustering/any_clustering.py:62-124)."""
+    from .clustering import apply_sums, assign, cluster_sums, compute_norms
+
+    c = init.clone().contiguous()
+    cache = nat.Workspace(x.device)
+    for _ in range(int(niter)):
+        labels, _ = assign(x, c, compute_norms(c), cache)
+        sums, counts = cluster_sums(x, labels, k, cache)
+        dist.all_reduce(sums, op=dist.ReduceOp.SUM, group=group)
+        dist.all_reduce(counts, op=dist.ReduceOp.SUM, group=group)
+        apply_sums(sums, counts, c)
+    return c
+
+
 class ShardedIVF:
     """This rank's share of an IVFFlat index; search() returns the merged global top-k."""
 

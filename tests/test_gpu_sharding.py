@@ -65,3 +65,29 @@ def test_emulated_ranks_equal_single(cuda_device, engine, eng, metric, world):
     atol = compare.l2_atol(xq_np, x) if metric == MetricType.L2 else 1e-5 * (1 + np.abs(D_ref).max())
     errs = compare.check_knn(D, I, D_ref, I_ref, compare.exact_lookup(xq_np, x, m), atol=atol)
     assert not errs, errs[:5]
+
+
+def test_kmeans_sums_over_shards_equal_update(cuda_device):
+    """mf_kmeans_sums on shards + a summed (all-reduced) total + mf_kmeans_apply
+    equals mf_kmeans_update on all points; an empty cluster keeps its centroid."""
+    from metalfaiss_b200 import clustering
+    from metalfaiss_b200.sharding import row_shard
+
+    x, _, _ = syn.mixture(30000, 64, 50, seed=31)
+    xt = torch.from_numpy(x).cuda()
+    c = torch.from_numpy(np.concatenate([x[:49], np.full((1, 64), 1e3, np.float32)])).cuda()
+    labels, _ = clustering.assign(xt, c, clustering.compute_norms(c))
+    ref = c.clone()
+    counts_ref = clustering.update(xt, labels, ref)
+    assert int(counts_ref[-1]) == 0
+    tot_s = tot_n = None
+    for r in range(3):
+        b, e = row_shard(len(x), r, 3)
+        s, n = clustering.cluster_sums(xt[b:e].contiguous(), labels[b:e].contiguous(), 50)
+        tot_s = s if tot_s is None else tot_s + s
+        tot_n = n if tot_n is None else tot_n + n
+    got = c.clone()
+    clustering.apply_sums(tot_s, tot_n, got)
+    assert torch.equal(tot_n, counts_ref)
+    assert torch.equal(got[-1], c[-1])
+    torch.testing.assert_close(got, ref, rtol=1e-6, atol=1e-6)

@@ -256,3 +256,43 @@ def test_sharded_ivf_bound_exchange_equals_single_gloo():
             z = np.load(os.path.join(tmp, f"ivfb{r}.npz"))
             assert np.array_equal(z["I"], I_ref)
             assert np.array_equal(z["D"], D_ref)
+
+
+def _kmeans_data():
+    rng = np.random.Generator(np.random.PCG64(5))
+    cen = 3.0 * rng.standard_normal((12, 6))
+    x = (cen[rng.integers(0, 12, 901)] + rng.standard_normal((901, 6))).astype(np.float32)
+    return x, x[rng.permutation(901)[:12]].copy()
+
+
+def _kmeans_worker(rank, port, out_dir):
+    """Sharded Lloyd iterations: local assignment, SUM all-reduce of the fp64
+    per-cluster sums and sizes, the same update on every rank."""
+    dist = _init(rank, port)
+    try:
+        x, c = _kmeans_data()
+        b, e = row_shard(len(x), rank, WORLD)
+        xs = x[b:e]
+        for _ in range(4):
+            lab, _ = oracle.kmeans_assign(xs, c)
+            sums = np.zeros(c.shape, np.float64)
+            np.add.at(sums, lab, xs.astype(np.float64))
+            cnt = np.bincount(lab, minlength=len(c)).astype(np.int64)
+            ts, tc = torch.from_numpy(sums), torch.from_numpy(cnt)
+            dist.all_reduce(ts, op=dist.ReduceOp.SUM)
+            dist.all_reduce(tc, op=dist.ReduceOp.SUM)
+            s, n = ts.numpy(), tc.numpy()
+            c = np.where(n[:, None] > 0, s / np.maximum(n, 1)[:, None], c).astype(np.float32)
+        np.save(os.path.join(out_dir, f"km{rank}.npy"), c)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_sharded_kmeans_equals_single_gloo():
+    with tempfile.TemporaryDirectory() as tmp:
+        assert _run(_kmeans_worker, tmp) == [0, 0]
+        x, c0 = _kmeans_data()
+        ref = oracle.kmeans_train(x, len(c0), 4, 0, init=c0)
+        c_r = [np.load(os.path.join(tmp, f"km{r}.npy")) for r in range(WORLD)]
+        assert np.array_equal(c_r[0], c_r[1])  # identical on every rank
+        np.testing.assert_allclose(c_r[0], ref, rtol=1e-6, atol=1e-6)
