@@ -22,6 +22,17 @@ def padded_dim(d: int) -> int:
     return (d + 3) // 4 * 4
 
 
+# Up to this padded dimension the tensor-core scan can derive the rows' tf32
+# residuals itself; above it they must be stored (mf_tf32_residual at add
+# time). Loading stored residuals is faster, so indexes store them unless
+# asked to save the memory (residuals=False), which halves their footprint.
+RESIDUAL_FREE_MAX_D = 128
+
+
+def stores_residuals(dp: int, wanted: bool = True) -> bool:
+    return wanted or dp > RESIDUAL_FREE_MAX_D
+
+
 def as_matrix(xs, d: int, device: torch.device, name: str = "xs") -> torch.Tensor:
     """(n, d) input of any array-like → contiguous fp32 (n, padded_dim(d)) on `device`."""
     if torch.is_tensor(xs):

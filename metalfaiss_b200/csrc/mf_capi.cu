@@ -159,7 +159,9 @@ int ivf_scan_topk(int device, cudaStream_t stream, const IvfWs& w, const float* 
                   const int64_t* list_ids, int64_t ntotal, const int32_t* list_order, int d,
                   int metric, int k, float* D, int64_t* I, float* bound_out = nullptr,
                   const float* bound_in = nullptr) {
-  const bool tc = list_lo != nullptr && tc_eligible(metric, d, k, ntotal);
+  // tensor cores: where the shape allows, given the rows' tf32 residuals or,
+  // for d <= 128, deriving them in the kernel
+  const bool tc = tc_eligible(metric, d, k, ntotal) && (list_lo != nullptr || tc_raw_queries(d, k));
   if (metric == MF_METRIC_L2) MF_TRY(launch_norms(xq, nq, d, w.qn, stream));
   ScanArgs a{};
   a.xq = xq;
@@ -338,6 +340,7 @@ int mf_ivf_search(int device, void* stream, const float* xq, int64_t nq,
            workspace_bytes, c.used);
   cudaStream_t s = (cudaStream_t)stream;
   const float* cent_lo = nullptr;
+  // the centroids' residuals (8 MB at 16384 x 128): loading them beats deriving them
   if (tc_eligible(coarse_metric(metric), d, P, nlist)) {
     MF_TRY(launch_tf32_residual(centroids, nlist, d, w.cent_lo, s));
     cent_lo = w.cent_lo;

@@ -558,7 +558,7 @@ FlatPlan plan_flat(int64_t nq, int64_t nb, int d, int k, int device, int tq) {
 int run_flat_topk(int device, cudaStream_t stream, const float* xq, int64_t nq, const float* xb,
                   const float* xb_norms, const float* xb_lo, int64_t nb, int d, int metric, int k,
                   const int64_t* ids, float* D, int64_t* I, void* ws, size_t ws_bytes) {
-  const bool tc = xb_lo != nullptr && tc_eligible(metric, d, k, nb);
+  const bool tc = tc_eligible(metric, d, k, nb) && (xb_lo != nullptr || tc_raw_queries(d, k));
   const FlatPlan p = plan_flat(nq, nb, d, k, device, tc ? tc_group() : 32);
   MF_CHECK(ws_bytes >= p.bytes, MF_ERR_INVALID_ARGS,
            "flat search workspace too small: %zu < %zu bytes", ws_bytes, p.bytes);

@@ -118,7 +118,7 @@ TqLayout tq_layout(int d, int kcap, int BN, int SA, bool atm) {
   s.xn = o;  // row norms of the tile: a double buffer per epilogue warp
   o += size_t(kTqEpiThreads / 32) * 2 * BN * 4;
   s.bars = o;
-  o += size_t(2 * SA + 2 * kTqMaxAcc + 2 * kTqQueue + 3) * 8 + 16 + kTqQueue * 32;
+  o += size_t(3 * SA + 2 * kTqMaxAcc + 2 * kTqQueue + 3) * 8 + 16 + kTqQueue * 32;
   s.total = o + 1024;
   return s;
 }
@@ -258,7 +258,9 @@ __device__ __forceinline__ unsigned int tq_accept(const uint32_t (&r)[32], const
   return ~all & in_range;
 }
 
-template <int METRIC, int BN, bool ATM>
+// CONV (with ATM only): the rows' tf32 residuals are derived in shared memory
+// from the loaded fp32 tile instead of being loaded (no residual array).
+template <int METRIC, int BN, bool ATM, bool CONV>
 __global__ void __launch_bounds__(ATM ? kTqThreadsAtm : kTqThreads, 1)
     tq_scan_kernel(const ScanArgs a, const __grid_constant__ TqMaps maps, const TqLayout L) {
   extern __shared__ unsigned char smem_raw[];
@@ -270,7 +272,8 @@ __global__ void __launch_bounds__(ATM ? kTqThreadsAtm : kTqThreads, 1)
   unsigned long long* cbuf = reinterpret_cast<unsigned long long*>(base + L.scratch);
   uint64_t* full = reinterpret_cast<uint64_t*>(base + L.bars);
   uint64_t* empty = full + L.SA;
-  uint64_t* accf = empty + L.SA;
+  uint64_t* conv = empty + L.SA;  // ATM: the stage's residual tile is written
+  uint64_t* accf = conv + L.SA;
   uint64_t* acce = accf + kTqMaxAcc;
   uint64_t* qfull = acce + kTqMaxAcc;
   uint64_t* qempty = qfull + kTqQueue;
@@ -289,7 +292,10 @@ __global__ void __launch_bounds__(ATM ? kTqThreadsAtm : kTqThreads, 1)
   const int KB = L.KB;
   const int k = a.k;
   const int total = a.flat ? a.nqt * a.P : *a.item_total;
-  constexpr uint32_t kStageTx = ATM ? 2 * BN * 128 : 2 * kTqM * 128 + 2 * BN * 128;
+  // ATM: the rows' fp32 tile and residual tile are loaded (CONV: only the fp32
+  // tile; the loader warps derive its tf32 residual in shared memory).
+  constexpr uint32_t kStageTx = ATM ? (CONV ? BN * 128 : 2 * BN * 128)
+                                    : 2 * kTqM * 128 + 2 * BN * 128;
 
 #ifdef MF_TC_PROFILE
   const long long _tk = clock64();
@@ -302,6 +308,7 @@ __global__ void __launch_bounds__(ATM ? kTqThreadsAtm : kTqThreads, 1)
     for (int i = 0; i < SA; ++i) {
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], 1);
+      mbar_init(&conv[i], kTqM);
     }
     for (int i = 0; i < NACC; ++i) {
       mbar_init(&accf[i], 1);
@@ -334,7 +341,7 @@ __global__ void __launch_bounds__(ATM ? kTqThreadsAtm : kTqThreads, 1)
         prefetch_tensormap(&maps.a_lo);
       }
       prefetch_tensormap(&maps.b_hi);
-      prefetch_tensormap(&maps.b_lo);
+      if (!CONV) prefetch_tensormap(&maps.b_lo);
       uint32_t seq = 0;
       for (uint32_t qi = 0;; ++qi) {
         // take the next item and publish it (-1 ends every role's loop)
@@ -367,7 +374,7 @@ __global__ void __launch_bounds__(ATM ? kTqThreadsAtm : kTqThreads, 1)
               tma_load_2d(st + L.a_lo, &maps.a_lo, x, it.a_row0, &full[s]);
             }
             tma_load_2d(st + L.b_hi, &maps.b_hi, x, yb, &full[s]);
-            tma_load_2d(st + L.b_lo, &maps.b_lo, x, yb, &full[s]);
+            if (!CONV) tma_load_2d(st + L.b_lo, &maps.b_lo, x, yb, &full[s]);
             ++seq;
           }
         }
@@ -401,7 +408,7 @@ __global__ void __launch_bounds__(ATM ? kTqThreadsAtm : kTqThreads, 1)
           const uint32_t dt = tmem + L.acc0 + b * BN;
           for (int kb = 0; kb < KB; ++kb, ++seq) {
             const int s = seq % SA;
-            TQP(2, mbar_wait(&full[s], (seq / SA) & 1, s_abort, &g_device_error));
+            TQP(2, mbar_wait(CONV ? &conv[s] : &full[s], (seq / SA) & 1, s_abort, &g_device_error));
             tc_fence_after();
             const uint32_t st = smem_u32(base + size_t(s) * L.stage);
 #ifdef MF_TC_PROFILE
@@ -443,59 +450,124 @@ __global__ void __launch_bounds__(ATM ? kTqThreadsAtm : kTqThreads, 1)
       mma_commit(mdone);
     }
   } else if (ATM && warp >= 6) {
-    // ------------------------------------------------ query tile loader
+    // ------------------------------------------ query tile loader + residuals
     // Thread t of warps 6-9 owns TMEM lane 32*(warp%4)+lane = query row of
-    // the item. It reads its query from global memory before waiting for the
-    // previous item's MMAs, splits it into tf32 hi (the raw fp32; the tensor
-    // core drops the low 13 bits) and lo = x - trunc(x), and writes both to its
-    // lane: hi in columns [0, KB*32), lo in [KB*32, 2*KB*32); zero past d.
+    // the item. Per item it writes the query tile to its lane once the
+    // previous item's MMAs are done (hi = the raw fp32, which the tensor core
+    // truncates to tf32, in columns [0, KB*32); lo = x - trunc(x) in
+    // [KB*32, 2*KB*32); zero past d), then reads the next item's query rows
+    // into registers (their latency overlaps what follows), then derives the
+    // tf32 residual of every row stage of the item as it lands:
+    // lo = x - trunc(x), elementwise at the same swizzled offset, so only the
+    // rows' fp32 tile crosses HBM.
     const int row = 32 * (warp & 3) + lane;
+    const int cid = (warp - 6) * 32 + lane;
     const uint32_t lane_base = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
     constexpr int kMaxV = kTqMaxDAtm / 4;
-    for (uint32_t qi = 0;; ++qi) {
-      const int qs = qi % kTqQueue;
-      if (!mbar_wait(&qfull[qs], (qi / kTqQueue) & 1, s_abort, &g_device_error)) break;
-      const int item = s_q[qs].item;
-      const ItemDesc it = s_q[qs].it;
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&qempty[qs]);
-      if (item < 0) break;
+    float4 v[kMaxV];
+    auto fetch = [&](const ItemDesc& it) {
       const float* src = nullptr;
       if (row < it.nq_item) {
         const long long q = a.flat ? (long long)it.a_row0 + row : a.pairs[it.a_row0 + row] / a.P;
         src = a.xq + q * a.d;
       }
-      float4 v[kMaxV];
 #pragma unroll
       for (int i = 0; i < kMaxV; ++i) {
         v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
         if (src != nullptr && 4 * i < a.d) v[i] = *reinterpret_cast<const float4*>(src + 4 * i);
       }
-      if (qi > 0 && !mbar_wait(afree, (qi - 1) & 1, s_abort, &g_device_error)) break;
-      tc_fence_after();
+    };
+    auto take = [&](uint32_t qi, int& item, ItemDesc& it) -> bool {
+      const int qs = qi % kTqQueue;
+      if (!mbar_wait(&qfull[qs], (qi / kTqQueue) & 1, s_abort, &g_device_error)) return false;
+      item = s_q[qs].item;
+      it = s_q[qs].it;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&qempty[qs]);
+      return true;
+    };
+    uint32_t cseq = 0;
+    int item;
+    ItemDesc it;
+    if (take(0, item, it) && item >= 0) {
+      fetch(it);
+      for (uint32_t qi = 0;; ++qi) {
+        if (qi > 0 && !mbar_wait(afree, (qi - 1) & 1, s_abort, &g_device_error)) break;
+        tc_fence_after();
 #pragma unroll
-      for (int c = 0; c < kTqMaxDAtm / 32; ++c) {
-        if (c < KB) {
-          uint32_t hi[32], lo[32];
+        for (int c = 0; c < kTqMaxDAtm / 32; ++c) {
+          if (c < KB) {
+            uint32_t hi[32], lo[32];
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const float e[4] = {v[c * 8 + i].x, v[c * 8 + i].y, v[c * 8 + i].z, v[c * 8 + i].w};
+            for (int i = 0; i < 8; ++i) {
+              const float e[4] = {v[c * 8 + i].x, v[c * 8 + i].y, v[c * 8 + i].z, v[c * 8 + i].w};
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              float h, l;
-              split_tf32(e[j], h, l);
-              hi[4 * i + j] = __float_as_uint(e[j]);
-              lo[4 * i + j] = __float_as_uint(l);
-              (void)h;
+              for (int j = 0; j < 4; ++j) {
+                float h, l;
+                split_tf32(e[j], h, l);
+                hi[4 * i + j] = __float_as_uint(e[j]);
+                lo[4 * i + j] = __float_as_uint(l);
+                (void)h;
+              }
             }
+            tmem_st32(lane_base + c * 32, hi);
+            tmem_st32(lane_base + KB * 32 + c * 32, lo);
           }
-          tmem_st32(lane_base + c * 32, hi);
-          tmem_st32(lane_base + KB * 32 + c * 32, lo);
         }
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(afull);
+        // This item's row stages. The next item's queries are fetched as soon
+        // as it is published (checked without blocking between stages: the
+        // producer publishes it only after issuing this item's stages, which
+        // need these conversions to free the ring), else after the loop.
+        const ItemDesc cur = it;
+        int nitem = -1;
+        ItemDesc nit{};
+        bool have_next = false, more = true;
+        const uint32_t nq = qi + 1;
+        const long long nrows = cur.re > cur.rb ? cur.re - cur.rb : 0;
+        const int nst = CONV ? (int)((nrows + BN - 1) / BN) * KB : 0;
+        bool ok = true;
+        for (int j = 0; j < nst && ok; ++j, ++cseq) {
+          // warp-uniform: lane 0's view decides, take() syncs the warp
+          if (!have_next &&
+              __shfl_sync(0xffffffffu, (int)mbar_test(&qfull[nq % kTqQueue], (nq / kTqQueue) & 1),
+                          0)) {
+            more = take(nq, nitem, nit);
+            have_next = true;
+            if (more && nitem >= 0) fetch(nit);
+          }
+          const int sidx = cseq % SA;
+          if (!mbar_wait(&full[sidx], (cseq / SA) & 1, s_abort, &g_device_error)) {
+            ok = false;
+            break;
+          }
+          unsigned char* st = base + size_t(sidx) * L.stage;
+          const float4* hi4 = reinterpret_cast<const float4*>(st + L.b_hi);
+          float4* lo4 = reinterpret_cast<float4*>(st + L.b_lo);
+#pragma unroll
+          for (int i = 0; i < BN * 32 / 4 / kTqM; ++i) {
+            const float4 x = hi4[cid + i * kTqM];
+            float4 h, l;
+            split_tf32(x.x, h.x, l.x);
+            split_tf32(x.y, h.y, l.y);
+            split_tf32(x.z, h.z, l.z);
+            split_tf32(x.w, h.w, l.w);
+            lo4[cid + i * kTqM] = l;
+          }
+          fence_proxy_async_smem();
+          mbar_arrive(&conv[sidx]);
+        }
+        if (!ok) break;
+        if (!have_next) {
+          more = take(nq, nitem, nit);
+          if (more && nitem >= 0) fetch(nit);
+        }
+        if (!more || nitem < 0) break;
+        item = nitem;
+        it = nit;
       }
-      tmem_wait_st();
-      tc_fence_before();
-      mbar_arrive(afull);
     }
   } else {
     // ----------------------------------------------------------- epilogue
@@ -772,9 +844,11 @@ __global__ void __launch_bounds__(ATM ? kTqThreadsAtm : kTqThreads, 1)
 typedef void (*TqFn)(const ScanArgs, const TqMaps, const TqLayout);
 
 template <int METRIC>
-TqFn pick_tq(const TqLayout& l) {
-  if (l.atm) return tq_scan_kernel<METRIC, 128, true>;
-  return l.BN == 256 ? tq_scan_kernel<METRIC, 256, false> : tq_scan_kernel<METRIC, 128, false>;
+TqFn pick_tq(const TqLayout& l, bool conv) {
+  if (l.atm)
+    return conv ? tq_scan_kernel<METRIC, 128, true, true> : tq_scan_kernel<METRIC, 128, true, false>;
+  return l.BN == 256 ? tq_scan_kernel<METRIC, 256, false, false>
+                     : tq_scan_kernel<METRIC, 128, false, false>;
 }
 
 int tq_kcap(int k) { return k <= kTqK ? kTqK : 0; }
@@ -809,7 +883,7 @@ bool tq_choose(int d, int kcap, TqLayout* out) {
 
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 std::mutex g_tc_mu;
-int g_tc_attr[64][2][3];  // dynamic smem set per (device, metric, variant)
+int g_tc_attr[64][2][4];  // dynamic smem set per (device, metric, variant)
 
 int encoder(PFN_cuTensorMapEncodeTiled_v12000* out) {
   std::lock_guard<std::mutex> lk(g_tc_mu);
@@ -923,8 +997,9 @@ int launch_tc_scan(const ScanArgs& a, int metric, const float* a_lo, int64_t a_r
   TqLayout lay;
   MF_CHECK(kcap != 0 && tq_choose(a.d, kcap, &lay), MF_ERR_INVALID_ARGS,
            "tensor-core scan does not fit (d=%d k=%d)", a.d, a.k);
-  TqFn fn = metric == MF_METRIC_L2 ? pick_tq<MF_METRIC_L2>(lay)
-                                   : pick_tq<MF_METRIC_INNER_PRODUCT>(lay);
+  const bool conv = lay.atm && b_lo == nullptr;  // derive the rows' residuals in the kernel
+  TqFn fn = metric == MF_METRIC_L2 ? pick_tq<MF_METRIC_L2>(lay, conv)
+                                   : pick_tq<MF_METRIC_INNER_PRODUCT>(lay, conv);
   MF_CHECK(fn != nullptr, MF_ERR_METRIC, "metric %d has no tensor-core scan", metric);
   PFN_cuTensorMapEncodeTiled_v12000 enc;
   MF_TRY(encoder(&enc));
@@ -935,11 +1010,14 @@ int launch_tc_scan(const ScanArgs& a, int metric, const float* a_lo, int64_t a_r
     MF_TRY(make_map(enc, &maps.a_lo, a_lo, a.d, a_rows, kTqM));
   }
   MF_TRY(make_map(enc, &maps.b_hi, a.xb, a.d, b_rows, lay.BN));
-  MF_TRY(make_map(enc, &maps.b_lo, b_lo, a.d, b_rows, lay.BN));
+  if (!conv) {
+    MF_CHECK(b_lo != nullptr, MF_ERR_INVALID_ARGS, "tensor-core scan needs the rows' residuals");
+    MF_TRY(make_map(enc, &maps.b_lo, b_lo, a.d, b_rows, lay.BN));
+  }
   {
     std::lock_guard<std::mutex> lk(g_tc_mu);
     const int mi = metric == MF_METRIC_L2 ? 0 : 1;
-    const int bi = lay.atm ? 2 : (lay.BN == 256 ? 1 : 0);
+    const int bi = lay.atm ? (conv ? 3 : 2) : (lay.BN == 256 ? 1 : 0);
     if (device < 0 || device >= 64 || g_tc_attr[device][mi][bi] < (int)lay.total) {
       MF_CUDA(cudaFuncSetAttribute(reinterpret_cast<const void*>(fn),
                                    cudaFuncAttributeMaxDynamicSharedMemorySize, (int)lay.total));

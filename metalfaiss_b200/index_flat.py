@@ -16,14 +16,17 @@ import numpy as np
 import torch
 
 from . import _native as nat
-from ._tensors import GrowBuffer, as_ids, as_matrix, default_device, padded_dim
+from ._tensors import GrowBuffer, as_ids, as_matrix, default_device, padded_dim, stores_residuals
 from .errors import InvalidArgumentError, NotImplementedFaissError
 from .metric_type import SUPPORTED_METRICS, MetricType
 from .search_result import SearchRangeResult, SearchResult
 
 
 class FlatIndex:
-    def __init__(self, d: int, metric_type=MetricType.L2, device=None) -> None:
+    def __init__(self, d: int, metric_type=MetricType.L2, device=None,
+                 residuals: bool = True) -> None:
+        """residuals=False stores no tf32 residuals (half the memory); for
+        d <= 128 the tensor-core scan then derives them itself, a little slower."""
         if int(d) <= 0:
             raise InvalidArgumentError(f"dimension must be positive, got {d}")
         self.d = int(d)
@@ -36,7 +39,10 @@ class FlatIndex:
         self._dp = padded_dim(self.d)
         self._xb = GrowBuffer((self._dp,), torch.float32, self.device)
         self._norms = GrowBuffer((), torch.float32, self.device)
-        self._lo = GrowBuffer((self._dp,), torch.float32, self.device)  # tf32 residuals
+        # tf32 residuals, stored only where the tensor-core scan cannot derive them
+        self._residuals = bool(residuals)
+        self._lo = (GrowBuffer((self._dp,), torch.float32, self.device)
+                    if stores_residuals(self._dp, self._residuals) else None)
         self._ids = GrowBuffer((), torch.int64, self.device)
         self._ws = None
         self.verbose = False
@@ -87,13 +93,14 @@ class FlatIndex:
         else:
             idt = as_ids(ids, n, self.device)
         norms = torch.empty(n, dtype=torch.float32, device=self.device)
-        lo = torch.empty_like(x)
         st = nat.stream_of(self.device)
         nat.call("mf_vector_norms", self.device.index, st, nat.ptr(x), n, self._dp, nat.ptr(norms))
-        nat.call("mf_tf32_residual", self.device.index, st, nat.ptr(x), n, self._dp, nat.ptr(lo))
+        if self._lo is not None:
+            lo = torch.empty_like(x)
+            nat.call("mf_tf32_residual", self.device.index, st, nat.ptr(x), n, self._dp, nat.ptr(lo))
+            self._lo.append(lo)
         self._xb.append(x)
         self._norms.append(norms)
-        self._lo.append(lo)
         self._ids.append(idt)
 
     def add_with_ids(self, xs, ids) -> None:
@@ -104,16 +111,18 @@ class FlatIndex:
         """python/metalfaiss/indexflat.py:127-133."""
         self._xb.reset()
         self._norms.reset()
-        self._lo.reset()
+        if self._lo is not None:
+            self._lo.reset()
         self._ids.reset()
 
     def clone(self) -> "FlatIndex":
         """Deep copy, python/metalfaiss/indexflat.py:142-151."""
-        out = FlatIndex(self.d, self.metric_type, self.device)
+        out = FlatIndex(self.d, self.metric_type, self.device, self._residuals)
         if self.ntotal:
             out._xb.append(self._xb.view())
             out._norms.append(self._norms.view())
-            out._lo.append(self._lo.view())
+            if self._lo is not None:
+                out._lo.append(self._lo.view())
             out._ids.append(self._ids.view())
         return out
 
@@ -144,7 +153,7 @@ class FlatIndex:
                                       m, k)
         ws = self._workspace().get(ws_bytes)
         nat.call("mf_flat_search", self.device.index, nat.stream_of(self.device), nat.ptr(xq), nq,
-                 nat.ptr(self._xb.buf), nat.ptr(self._norms.buf), nat.ptr(self._lo.buf),
+                 nat.ptr(self._xb.buf), nat.ptr(self._norms.buf), nat.ptr(self._lo.buf if self._lo is not None else None),
                  self.ntotal, self._dp, m, k,
                  nat.ptr(self._ids.buf) if map_ids else nat.ptr(None), nat.ptr(D), nat.ptr(I),
                  nat.ptr(ws), ws.numel())

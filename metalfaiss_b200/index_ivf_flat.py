@@ -20,7 +20,7 @@ import numpy as np
 import torch
 
 from . import _native as nat
-from ._tensors import as_ids, as_matrix, default_device, padded_dim
+from ._tensors import as_ids, as_matrix, default_device, padded_dim, stores_residuals
 from .clustering import ClusteringParameters, assign, compute_norms, subsample, train_kmeans
 from .errors import BadStateError, InvalidArgumentError, NotImplementedFaissError
 from .index_flat import FlatIndex
@@ -36,7 +36,7 @@ class IVFFlatIndex:
 
     def __init__(self, *args, quantizer: Optional[FlatIndex] = None, d: Optional[int] = None,
                  nlist: Optional[int] = None, metric_type=MetricType.L2, device=None,
-                 clustering: Optional[ClusteringParameters] = None):
+                 clustering: Optional[ClusteringParameters] = None, residuals: bool = True):
         if args and isinstance(args[0], FlatIndex):
             quantizer = args[0]
             args = args[1:]
@@ -56,6 +56,9 @@ class IVFFlatIndex:
         if self.d <= 0 or self._nlist <= 0:
             raise InvalidArgumentError(f"bad IVFFlatIndex shape d={d} nlist={nlist}")
         self.metric_type = MetricType.coerce(metric_type)
+        # residuals=False: no stored tf32 residuals (half the memory; the scan
+        # derives them for d <= 128)
+        self._residuals = bool(residuals)
         if self.metric_type not in SUPPORTED_METRICS:
             raise NotImplementedFaissError(f"metric {self.metric_type.name} is not supported")
         self.device = default_device(device if device is not None else
@@ -195,9 +198,12 @@ class IVFFlatIndex:
                  nat.ptr(labels), n, nat.ptr(out_off), nat.ptr(out_vecs), nat.ptr(out_norms),
                  nat.ptr(out_ids), nat.ptr(ws), ws.numel())
         self._offsets, self._vecs, self._norms, self._ids = out_off, out_vecs, out_norms, out_ids
-        self._lo = torch.empty_like(out_vecs)
-        nat.call("mf_tf32_residual", self.device.index, nat.stream_of(self.device),
-                 nat.ptr(out_vecs), total, self._dp, nat.ptr(self._lo))
+        if stores_residuals(self._dp, self._residuals):
+            self._lo = torch.empty_like(out_vecs)
+            nat.call("mf_tf32_residual", self.device.index, nat.stream_of(self.device),
+                     nat.ptr(out_vecs), total, self._dp, nat.ptr(self._lo))
+        else:
+            self._lo = None  # the tensor-core scan derives them
         self._ntotal = total
         self._direct_map = None
         sizes = np.diff(out_off.cpu().numpy())
@@ -225,7 +231,8 @@ class IVFFlatIndex:
             # An untouched index: give the kernels a valid empty bank.
             self._vecs = torch.zeros((1, self._dp), dtype=torch.float32, device=self.device)
             self._norms = torch.zeros(1, dtype=torch.float32, device=self.device)
-            self._lo = torch.zeros((1, self._dp), dtype=torch.float32, device=self.device)
+            self._lo = (torch.zeros((1, self._dp), dtype=torch.float32, device=self.device)
+                        if stores_residuals(self._dp, self._residuals) else None)
             self._ids = torch.full((1,), -1, dtype=torch.int64, device=self.device)
 
     def search(self, xs, k: int) -> SearchResult:

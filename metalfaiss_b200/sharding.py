@@ -110,7 +110,8 @@ def keep_lists(index, keep_mask: np.ndarray):
     from .index_ivf_flat import IVFFlatIndex
 
     out = IVFFlatIndex(index.d, index.nlist, quantizer=index.quantizer,
-                       metric_type=index.metric_type, device=index.device)
+                       metric_type=index.metric_type, device=index.device,
+                       residuals=index._residuals)
     out._is_trained = index.is_trained
     out.nprobe = index.nprobe
     sizes = index.list_sizes()
@@ -125,7 +126,8 @@ def keep_lists(index, keep_mask: np.ndarray):
         row_mask = torch.from_numpy(keep).to(dev)[list_of_row]
         out._vecs = index._vecs[: index.ntotal][row_mask].contiguous()
         out._norms = index._norms[: index.ntotal][row_mask].contiguous()
-        out._lo = index._lo[: index.ntotal][row_mask].contiguous()
+        out._lo = (index._lo[: index.ntotal][row_mask].contiguous()
+                   if index._lo is not None else None)
         out._ids = index._ids[: index.ntotal][row_mask].contiguous()
         out._ntotal = int(out._ids.shape[0])
     out._offsets = torch.from_numpy(offsets).to(dev)
@@ -204,7 +206,7 @@ class ShardedFlat:
 
         self.rank, self.world, self.group = rank, world, group
         b, e = row_shard(index.ntotal, rank, world)
-        self.local = FlatIndex(index.d, index.metric_type, index.device)
+        self.local = FlatIndex(index.d, index.metric_type, index.device, index._residuals)
         if e > b:
             self.local.add(index.xb[b:e], index.ids[b:e])
 

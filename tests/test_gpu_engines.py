@@ -1,9 +1,11 @@
 """The tensor-core (tcgen05, 3xTF32) and SIMT scan engines against each other
 and against the oracle, on flat and IVF searches. Engine 2 (like the default)
 uses the tensor cores where the shape allows (L2 / inner product, d >= 32,
-k <= 32) and the SIMT scan otherwise, with the query tile in tensor memory
-when d <= 128; engine 3 streams the query tile through shared memory instead;
-engine 1 forces the SIMT scan."""
+k <= 32) and the SIMT scan otherwise. For d <= 128 it keeps the query tile in
+tensor memory and derives the rows' tf32 residuals in the kernel; above that
+it streams both operands with stored residuals. Engine 3 takes the streamed
+form at every d (where residuals are stored: d > 128; the SIMT scan
+otherwise); engine 1 forces the SIMT scan."""
 import numpy as np
 import pytest
 
@@ -37,7 +39,8 @@ def _flat(metric, d, n, nq, k, seed, engine_id, data="gauss"):
 
 @pytest.mark.parametrize("eng", [2, 3])
 @pytest.mark.parametrize("metric", [MetricType.L2, MetricType.INNER_PRODUCT])
-@pytest.mark.parametrize("d,k", [(32, 10), (64, 1), (128, 32), (96, 100), (256, 256), (48, 7)])
+@pytest.mark.parametrize("d,k", [(32, 10), (64, 1), (128, 32), (96, 100), (256, 256), (48, 7),
+                                 (160, 10), (192, 32)])
 def test_tc_flat_matches_oracle(cuda_device, engine, eng, metric, d, k):
     xb, xq, D, I = _flat(metric, d, 5000, 77, k, seed=d + k, engine_id=eng)
     D_ref, I_ref = oracle.flat_search(xq, xb, k, int(metric))
@@ -61,15 +64,16 @@ def test_tc_precision_on_mixture(cuda_device, engine):
     assert not errs, errs[:5]
 
 
+@pytest.mark.parametrize("d", [64, 160])
 @pytest.mark.parametrize("eng", [2, 3])
 @pytest.mark.parametrize("nprobe,k", [(1, 10), (8, 32), (16, 100)])
-def test_tc_ivf_equals_simt(cuda_device, engine, eng, nprobe, k):
-    x, cen, _ = syn.mixture(40000, 64, 96, seed=7)
-    idx = IVFFlatIndex(64, 96)
+def test_tc_ivf_equals_simt(cuda_device, engine, d, eng, nprobe, k):
+    x, cen, _ = syn.mixture(40000, d, 96, seed=7)
+    idx = IVFFlatIndex(d, 96)
     idx.set_centroids(oracle.kmeans_train(x, 96, 2, 7))
     idx.add(x)
     idx.nprobe = nprobe
-    xq, _, _ = syn.mixture(300, 64, 96, seed=8, centres=cen)
+    xq, _, _ = syn.mixture(300, d, 96, seed=8, centres=cen)
     nat.set_scan_engine(1)
     D1, I1 = idx.search(xq, k).numpy()
     nat.set_scan_engine(eng)
@@ -96,4 +100,31 @@ def test_tc_many_items_persistent(cuda_device, engine, eng):
     D_ref, I_ref = oracle.ivf_search(xq, x[:300], offs, vecs, ids, 20, 10)
     errs = compare.check_knn(D, I, D_ref, I_ref, compare.exact_lookup(xq, x, oracle.L2),
                              atol=compare.l2_atol(xq, x))
+    assert not errs, errs[:5]
+
+
+@pytest.mark.parametrize("metric", [MetricType.L2, MetricType.INNER_PRODUCT])
+def test_tc_without_stored_residuals(cuda_device, engine, metric):
+    """residuals=False: the tensor-core scan derives the rows' tf32 residuals in
+    shared memory (d <= 128); flat and IVF results match the oracle."""
+    nat.set_scan_engine(2)
+    x, cen, _ = syn.mixture(30000, 96, 64, seed=17)
+    xq, _, _ = syn.mixture(300, 96, 64, seed=18, centres=cen)
+    flat = FlatIndex(96, metric, residuals=False)
+    flat.add(x)
+    assert flat._lo is None
+    D, I = flat.search(xq, 10).numpy()
+    D_ref, I_ref = oracle.flat_search(xq, x, 10, int(metric))
+    atol = compare.l2_atol(xq, x) if metric == MetricType.L2 else 1e-5 * (1 + np.abs(D_ref).max())
+    errs = compare.check_knn(D, I, D_ref, I_ref, compare.exact_lookup(xq, x, int(metric)), atol=atol)
+    assert not errs, errs[:5]
+    ivf = IVFFlatIndex(96, 64, metric_type=metric, residuals=False)
+    ivf.set_centroids(oracle.kmeans_train(x, 64, 2, 17))
+    ivf.add(x)
+    ivf.nprobe = 8
+    assert ivf._lo is None
+    D2, I2 = ivf.search(xq, 10).numpy()
+    nat.set_scan_engine(1)
+    D1, I1 = ivf.search(xq, 10).numpy()
+    errs = compare.check_knn(D2, I2, D1, I1, compare.exact_lookup(xq, x, int(metric)), atol=atol)
     assert not errs, errs[:5]

@@ -74,7 +74,7 @@ def test_noalloc_matches_workspace_search_twice(cuda_device):
     # call 1: L2 with tf32 residuals (tensor-core engine), k = 10
     xb1, n1, lo1, ids1 = _bank(40000, 64, seed=11, dev=dev)
     xq1 = torch.from_numpy(syn.gaussian(300, 64, 12)).to(dev)
-    # call 2: inner product without residuals (SIMT engine), other shapes, k = 17
+    # call 2: inner product without stored residuals, other shapes, k = 17
     xb2, n2, _, ids2 = _bank(23456, 96, seed=13, dev=dev)
     xq2 = torch.from_numpy(syn.gaussian(129, 96, 14)).to(dev)
 
