@@ -42,6 +42,10 @@ CONFIGS = {
     "ivf32k": dict(d=64, n=32768, nlist=128, nq=16, nprobe=8, k=10, niter=10),
     # Mid-size for development runs.
     "ivf2m": dict(d=128, n=2_000_000, nlist=2048, nq=10_000, nprobe=32, k=10, niter=5),
+    # The headline's list count at a fifth of its rows (4 GB on the device with
+    # residuals): lists probed by few queries dominate, as at full size; small
+    # enough for multi-pass profiler captures.
+    "ivf4m": dict(d=128, n=4_000_000, nlist=16384, nq=10_000, nprobe=32, k=10, niter=5),
 }
 
 
@@ -183,10 +187,17 @@ def build_index(cfg, device, seed=1234):
     return idx, xq
 
 
+# A list's last group of at most this many queries is scanned by the SIMT
+# kernel, the other groups (up to 128 queries) by the tensor-core kernel.
+SMALL_GROUP = 16
+
+
 def scan_work(idx, probes_np, d, k):
     """Work of one IVF scan over the probes (nq, P) of this index:
-    * pairs: (query, row) distance evaluations, sum over queries of the rows of
-      their probed lists;
+    * pairs: (query, row) distance evaluations in the tensor-core launch, i.e.
+      over the groups of more than SMALL_GROUP queries (a list probed by q
+      queries is cut into groups of 128; its last group goes to the SIMT
+      scan when it holds SMALL_GROUP queries or fewer);
     * bytes: what the list-major scan must move once: every probed list's rows
       (vector + norm) read once, the query vectors read once and each
       (query, probe) pair's k partial results written once;
@@ -195,9 +206,13 @@ def scan_work(idx, probes_np, d, k):
     valid = probes_np[probes_np >= 0]
     probed = np.unique(valid)
     rows = int(sizes[probed].sum())
-    pairs = int(sizes[valid].sum())
+    qpl = np.bincount(valid, minlength=len(sizes))
+    last = qpl - (np.maximum(qpl, 1) - 1) // 128 * 128
+    small = (qpl > 0) & (last <= SMALL_GROUP)
+    pairs = int((sizes * qpl).sum() - (sizes * np.where(small, last, 0)).sum())
+    small_rows = int(sizes[small].sum())
     nq, P = probes_np.shape
-    return pairs, rows * (4 * d + 4) + nq * d * 4 + nq * P * k * 12, rows
+    return pairs, rows * (4 * d + 4) + nq * d * 4 + nq * P * k * 12, rows, small_rows
 
 
 def run_ours(args, cfg):
@@ -224,8 +239,8 @@ def run_ours(args, cfg):
 
     # probes (for the roofline bytes): the coarse step of this batch
     probes = idx.quantizer._search_padded(xq, min(cfg["nprobe"], cfg["nlist"]), map_ids=False).labels
-    pairs, alg_bytes, probed_rows = scan_work(sharded.local if sharded else idx,
-                                              probes.cpu().numpy(), d, k)
+    pairs, alg_bytes, probed_rows, small_rows = scan_work(sharded.local if sharded else idx,
+                                                          probes.cpu().numpy(), d, k)
     logical_bytes = pairs * d * 4
     tf32_peak = tf32_gemm_peak(device) if rank == 0 else None
 
@@ -258,6 +273,7 @@ def run_ours(args, cfg):
     nat.timing_enable(False)
     ms = ev0.elapsed_time(ev1)
     scan_ms, scan_n = nat.timing_read("scan_topk_ivf")
+    small_ms, small_n = nat.timing_read("scan_topk_ivf_small")
     if world > 1:
         t = torch.tensor([ms], device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -327,7 +343,7 @@ def run_ours(args, cfg):
             "roofline": {
                 "bound": "tensor",
                 "kernel": "tq_scan_kernel (IVF list-major 3xTF32 tcgen05 scan + fused top-k), "
-                          "all-probes pass",
+                          "all-probes pass over groups of more than 16 queries",
                 "achieved": round(tflops, 2) if tflops else None,
                 "peak": round(tf32_peak, 1),
                 "unit": "TFLOP/s",
@@ -347,6 +363,20 @@ def run_ours(args, cfg):
                     "frac": round(gbs / hbm_peak, 4) if gbs else None,
                     "peak_kind": f"{peak_kind} hbm_gbs",
                     "logical_scan_GBps": round(logical_bytes / scan_s / 1e9, 1) if scan_n else None,
+                },
+                # the few-query groups' pass (one 4-warp block per item): bound by
+                # reading those lists' rows (vector + norm) once
+                "small_groups": {
+                    "kernel": "few_scan_kernel (lists' last groups of at most 16 queries)",
+                    "rows_per_launch": small_rows,
+                    "bytes_per_launch": small_rows * (4 * d + 4),
+                    "avg_launch_ms": round(small_ms / small_n, 4) if small_n else None,
+                    "achieved": (round(small_rows * (4 * d + 4) / (small_ms / small_n * 1e-3) / 1e9, 1)
+                                 if small_n else None),
+                    "peak": hbm_peak,
+                    "unit": "GB/s",
+                    "frac": (round(small_rows * (4 * d + 4) / (small_ms / small_n * 1e-3) / 1e9
+                                   / hbm_peak, 4) if small_n else None),
                 },
             },
             "e2e": {

@@ -153,6 +153,18 @@ int coarse_metric(int metric) {
 // there (+inf where its first probe holds no rows). bound_in != NULL: skip the
 // bound pass and filter the all-probes pass by bound_in (a bound computed
 // elsewhere, e.g. the minimum over the ranks that hold the lists).
+// The items split off as few-query groups (w.g.items2): one warp per item
+// where the shape allows, else the SIMT scan.
+int scan_small_items(const ScanArgs& base, const IvfWs& w, int metric, int64_t max_items,
+                     int device, cudaStream_t stream) {
+  ScanArgs sa = base;
+  sa.items = w.g.items2;
+  sa.item_total = w.g.item_total2;
+  sa.group = tc_group();
+  if (few_eligible(metric, sa.d, sa.k)) return launch_few_scan(sa, metric, max_items, device, stream);
+  return launch_scan(sa, metric, kEpiTopK, max_items, device, stream);
+}
+
 int ivf_scan_topk(int device, cudaStream_t stream, const IvfWs& w, const float* xq, int64_t nq,
                   const int64_t* probes, int P, int nlist, const int64_t* list_offsets,
                   const float* list_vecs, const float* list_norms, const float* list_lo,
@@ -192,20 +204,28 @@ int ivf_scan_topk(int device, cudaStream_t stream, const IvfWs& w, const float* 
   // the engines' rounding difference, so phase 2 still drops no row that
   // belongs to the top-k.
   constexpr int64_t kBoundRows = 128;
+  constexpr int kSmallGroup = 16;
   const int phases = (bound_out || bound_in) ? 1 : (P > 1 ? 2 : 1);
   float* const bound_dst = bound_out ? bound_out : w.bound;
   for (int ph = 0; ph < phases; ++ph) {
     const bool bounding = bound_out != nullptr || (phases == 2 && ph == 0);
     const bool simt_bound = bounding && tc && metric == MF_METRIC_L2;
     const bool use_tc = tc && !simt_bound;
+    // Tensor-core pass: groups of up to 128 queries per list, except that a
+    // list's last group of at most kSmallGroup queries goes to the SIMT scan:
+    // a 128-query tile would be mostly padding, and those rows' bytes, not
+    // their arithmetic, bound the work.
+    // (L2 only: the bound then carries the margin that covers both engines)
+    const int small_max = use_tc && !bounding && metric == MF_METRIC_L2 ? kSmallGroup : 0;
     MF_TRY(run_ivf_groups_ex(w.g, probes, nq, P, nlist, list_offsets, list_order, w.pd, w.pl, k,
                              nullptr, use_tc ? tc_group() : kScanTQ, stream, 0,
-                             bounding ? 1 : P));
+                             bounding ? 1 : P, small_max));
     a.max_rows = bounding ? kBoundRows : 0;
     a.bound = bound_in ? bound_in : ((phases == 2 && ph == 1) ? w.bound : nullptr);
     if (use_tc && tc_raw_queries(d, k)) {
       // the scan loads each item's queries itself (through a.pairs)
       MF_TRY(launch_tc_scan(a, metric, nullptr, nq, list_lo, ntotal, nq * P, device, stream));
+      if (small_max > 0) MF_TRY(scan_small_items(a, w, metric, nq * P, device, stream));
     } else if (use_tc) {
       // A operand: the queries of every (query, probe) pair, gathered in list order
       MF_TRY(launch_gather_queries(xq, d, w.g.pairs, w.g.pair_offsets + nlist, nq * P, P, w.g_hi,
@@ -213,6 +233,7 @@ int ivf_scan_topk(int device, cudaStream_t stream, const IvfWs& w, const float* 
       a.xq = w.g_hi;
       MF_TRY(launch_tc_scan(a, metric, w.g_lo, nq * P, list_lo, ntotal, nq * P, device, stream));
       a.xq = xq;
+      if (small_max > 0) MF_TRY(scan_small_items(a, w, metric, nq * P, device, stream));
     } else {
       MF_TRY(launch_scan(a, metric, kEpiTopK, nq * P, device, stream));
     }

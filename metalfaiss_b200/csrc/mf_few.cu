@@ -1,0 +1,240 @@
+// Scan of IVF items that hold few queries (a list's last group of at most
+// kFewMax queries): one block of four warps per item, the warps taking
+// interleaved 16-row steps of the list, each with its own per-query top-k
+// lists, merged at the end of the item. The item's queries sit in shared
+// memory. Rows are read 16 at a time with
+// fully coalesced loads (one load instruction = one whole row across the warp:
+// lane l holds the row's 16-byte column slice l), each lane forms the partial
+// dot products of its slice with every query, and a butterfly transpose-
+// reduction (16 shuffles per query) leaves row i's sum in lanes 2i and 2i+1.
+// These items hold most of a batch's probed rows but few (query, row) pairs,
+// so the pass is bound by reading the rows once from HBM. Distances, keys and
+// the per-query warp top-k are those of scan_kernel (mf_scan.cu), filtered by
+// the per-query bound when one is given.
+#include "mf_scan.cuh"
+#include "mf_timing.cuh"
+#include "mf_topk.cuh"
+
+namespace mf {
+namespace {
+
+constexpr int kFewMax = 16;     // queries per item at most
+constexpr int kFewWarps = 4;    // warps per block, sharing one item
+constexpr int kFewMaxD = 128;   // d at most: one 16-byte column slice per lane
+constexpr int kFewK = 32;       // list slots per query (k <= 32)
+constexpr int kFewRows = 16;    // rows per step
+
+// Dynamic shared memory of a block: the item's queries, then per warp the
+// query lists (kFewK keys) and candidate buffers (32 keys).
+struct FewSmem {
+  __host__ __device__ static size_t queries(int d) { return size_t(kFewMax) * d * 4; }
+  __host__ __device__ static size_t block(int d) {
+    return queries(d) + size_t(kFewWarps) * kFewMax * (kFewK + 32) * 8;
+  }
+};
+
+// p[0..15] per lane -> the sum over the 32 lanes of p[i] in lanes 2i, 2i+1.
+__device__ __forceinline__ float transpose_reduce16(float (&p)[16], int lane) {
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const bool hi = lane & 16;
+    const float send = hi ? p[i] : p[i + 8];
+    const float keep = hi ? p[i + 8] : p[i];
+    p[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const bool hi = lane & 8;
+    const float send = hi ? p[i] : p[i + 4];
+    const float keep = hi ? p[i + 4] : p[i];
+    p[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+  }
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const bool hi = lane & 4;
+    const float send = hi ? p[i] : p[i + 2];
+    const float keep = hi ? p[i + 2] : p[i];
+    p[i] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+  }
+  {
+    const bool hi = lane & 2;
+    const float send = hi ? p[0] : p[1];
+    const float keep = hi ? p[1] : p[0];
+    p[0] = keep + __shfl_xor_sync(0xffffffffu, send, 2);
+  }
+  return p[0] + __shfl_xor_sync(0xffffffffu, p[0], 1);
+}
+
+template <int METRIC>
+__global__ void __launch_bounds__(kFewWarps * 32) few_scan_kernel(const ScanArgs a) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int d = a.d;
+  const int k = a.k;
+  const int d4 = d >> 2;
+  float4* qs = reinterpret_cast<float4*>(smem_raw);  // kFewMax x d
+  unsigned long long* lists_all =
+      reinterpret_cast<unsigned long long*>(smem_raw + FewSmem::queries(d));
+  unsigned long long* lists = lists_all + warp * kFewMax * (kFewK + 32);  // this warp's
+  unsigned long long* bufs = lists + kFewMax * kFewK;
+  __shared__ int s_item;
+  __shared__ long long s_slot[kFewMax];
+  __shared__ float s_qn[kFewMax];
+  __shared__ unsigned long long s_bnd[kFewMax];
+  const int total = *a.item_total;
+  const int group = a.group > 0 ? a.group : kFewMax;
+
+  for (;;) {
+    if (threadIdx.x == 0) s_item = atomicAdd(a.counter, 1);
+    __syncthreads();
+    const int item = s_item;
+    if (item >= total) break;
+    const int2 g = a.items[item];
+    const int pb = a.pair_offsets[g.x] + g.y * group;
+    const int pe0 = a.pair_offsets[g.x + 1];
+    const int nq = (pe0 - pb) < kFewMax ? (pe0 - pb) : kFewMax;
+    const long long rb = a.list_offsets[g.x];
+    const long long re = a.list_offsets[g.x + 1];
+    // the item's queries (shared by the four warps)
+    if (threadIdx.x < nq) {
+      const int pr = a.pairs[pb + threadIdx.x];
+      const int q = pr / a.P;
+      s_slot[threadIdx.x] = pr;
+      s_qn[threadIdx.x] = METRIC == MF_METRIC_L2 ? a.qnorms[q] : 0.0f;
+      s_bnd[threadIdx.x] = a.bound ? bound_key(a.bound[q]) : kEmptyKey;
+    }
+    for (int i = threadIdx.x; i < nq * d4; i += kFewWarps * 32) {
+      const int j = i / d4;
+      const int pr = a.pairs[pb + j];
+      qs[i] = reinterpret_cast<const float4*>(a.xq + (long long)(pr / a.P) * d)[i - j * d4];
+    }
+    for (int i = lane; i < nq * kFewK; i += 32) lists[i] = kEmptyKey;
+    __syncthreads();
+    // lane j < nq: this warp's threshold and buffered count of query j
+    unsigned long long bnd = lane < nq ? s_bnd[lane] : kEmptyKey;
+    unsigned long long thr = bnd;
+    int nbuf = 0;
+
+    const float4* qv = qs + lane;  // this lane's column slice of each query
+    const bool col_ok = lane < d4;
+    for (long long r0 = rb + (long long)warp * kFewRows; r0 < re;
+         r0 += (long long)kFewWarps * kFewRows) {
+      // rows r0 .. r0+15: load i brings row r0+i across the warp (coalesced)
+      float4 xv[kFewRows];
+#pragma unroll
+      for (int i = 0; i < kFewRows; ++i) {
+        const long long r = r0 + i;
+        xv[i] = (r < re && col_ok) ? reinterpret_cast<const float4*>(a.xb + r * d)[lane]
+                                   : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+      const long long my_row = r0 + (lane >> 1);  // the row whose sum this lane ends with
+      const bool rv = my_row < re && (lane & 1) == 0;
+      const float xn = (METRIC == MF_METRIC_L2 && my_row < re) ? a.xnorms[my_row] : 0.0f;
+#pragma unroll 1
+      for (int j = 0; j < nq; ++j) {
+        const float4 q4 = col_ok ? qv[j * d4] : make_float4(0.f, 0.f, 0.f, 0.f);
+        float p[kFewRows];
+#pragma unroll
+        for (int i = 0; i < kFewRows; ++i) {
+          float t = xv[i].x * q4.x;
+          t = fmaf(xv[i].y, q4.y, t);
+          t = fmaf(xv[i].z, q4.z, t);
+          p[i] = fmaf(xv[i].w, q4.w, t);
+        }
+        const float dot = transpose_reduce16(p, lane);
+        const unsigned long long tj = __shfl_sync(0xffffffffu, thr, j);
+        const float dist = METRIC == MF_METRIC_L2 ? l2_from_dot(s_qn[j], xn, dot) : -dot;
+        const unsigned long long key = rv ? make_key(dist, (unsigned int)my_row) : kEmptyKey;
+        unsigned int m = __ballot_sync(0xffffffffu, key < tj);
+        if (m == 0u) continue;
+        int nb = __shfl_sync(0xffffffffu, nbuf, j);
+        unsigned long long* buf = bufs + j * 32;
+        unsigned long long* list = lists + j * kFewK;
+        if (nb + __popc(m) > 32) {
+          const unsigned long long nk = merge_into_list<kFewK>(list, buf, nb, k, lane);
+          const unsigned long long bj = __shfl_sync(0xffffffffu, bnd, j);
+          const unsigned long long t2 = nk < bj ? nk : bj;
+          if (lane == j) thr = t2;
+          nb = 0;
+          m = __ballot_sync(0xffffffffu, key < t2);
+          if (m == 0u) {
+            if (lane == j) nbuf = 0;
+            continue;
+          }
+        }
+        if ((m >> lane) & 1u) buf[nb + __popc(m & lanemask_lt())] = key;
+        if (lane == j) nbuf = nb + __popc(m);
+        __syncwarp();
+      }
+    }
+    // each warp folds its buffers into its lists; then warp (j mod 4) merges
+    // the four warps' lists of query j and writes its k keys
+    for (int j = 0; j < nq; ++j) {
+      const int nb = __shfl_sync(0xffffffffu, nbuf, j);
+      if (nb > 0) merge_into_list<kFewK>(lists + j * kFewK, bufs + j * 32, nb, k, lane);
+    }
+    __syncthreads();
+    for (int j = warp; j < nq; j += kFewWarps) {
+      unsigned long long* list = lists + j * kFewK;
+      for (int v = 0; v < kFewWarps; ++v) {
+        if (v == warp) continue;
+        const unsigned long long* other = lists_all + v * kFewMax * (kFewK + 32) + j * kFewK;
+        merge_into_list<kFewK>(list, other, k, k, lane);
+      }
+      const long long sj = s_slot[j];
+      if (lane < k) {
+        const unsigned long long key = list[lane];
+        float dv;
+        long long lv;
+        if (key == kEmptyKey) {
+          dv = __int_as_float(0x7f800000);
+          lv = -1;
+        } else {
+          dv = key_dist(key);
+          const unsigned int pos = key_index(key);
+          lv = a.ids ? a.ids[pos] : (long long)pos;
+        }
+        a.out_d[sj * k + lane] = dv;
+        a.out_l[sj * k + lane] = lv;
+      }
+      __syncwarp();
+    }
+    __syncthreads();
+  }
+}
+
+}  // namespace
+
+bool few_eligible(int metric, int d, int k) {
+  return (metric == MF_METRIC_L2 || metric == MF_METRIC_INNER_PRODUCT) && d <= kFewMaxD &&
+         d % 4 == 0 && k >= 1 && k <= kFewK;
+}
+
+int few_max_queries() { return kFewMax; }
+
+int launch_few_scan(const ScanArgs& a, int metric, int64_t max_items, int device,
+                    cudaStream_t stream) {
+  MF_CHECK(few_eligible(metric, a.d, a.k), MF_ERR_INVALID_ARGS,
+           "few-query scan does not take metric %d, d=%d, k=%d", metric, a.d, a.k);
+  MF_CHECK(a.counter != nullptr && a.item_total != nullptr, MF_ERR_INVALID_ARGS,
+           "few-query scan needs its items and a work counter");
+  if (max_items <= 0) return MF_OK;
+  const size_t smem = FewSmem::block(a.d);
+  auto fn = metric == MF_METRIC_L2 ? few_scan_kernel<MF_METRIC_L2>
+                                   : few_scan_kernel<MF_METRIC_INNER_PRODUCT>;
+  MF_CUDA(cudaFuncSetAttribute(reinterpret_cast<const void*>(fn),
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  int per_sm = 0;
+  MF_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kFewWarps * 32, smem));
+  if (per_sm < 1) per_sm = 1;
+  long long grid = (long long)num_sms(device) * per_sm;
+  if (grid > max_items) grid = max_items;
+  MF_CUDA(cudaMemsetAsync(a.counter, 0, sizeof(int), stream));
+  ScopedTiming tm("scan_topk_ivf_small", stream);
+  fn<<<(unsigned int)grid, kFewWarps * 32, smem, stream>>>(a);
+  MF_LAUNCH_CHECK();
+  return MF_OK;
+}
+
+}  // namespace mf

@@ -85,12 +85,15 @@ __global__ void ivf_count_kernel(const int64_t* __restrict__ probes, int64_t n, 
   }
 }
 
+// With small_max > 0, groups of at most small_max queries go to items2
+// (item_total2) instead of items; both keep the list order.
 __global__ void __launch_bounds__(kScanBlock) ivf_plan_kernel(const int* __restrict__ counts,
                                                              int nlist,
                                                              const int32_t* __restrict__ order,
                                                              int* pair_offsets, int2* items,
                                                              int* item_total, int* cursors,
-                                                             int group) {
+                                                             int group, int2* items2,
+                                                             int* item_total2, int small_max) {
   __shared__ int sums[32];
   const int chunk = (nlist + kScanBlock - 1) / kScanBlock;
   const int b = threadIdx.x * chunk;
@@ -106,18 +109,35 @@ __global__ void __launch_bounds__(kScanBlock) ivf_plan_kernel(const int* __restr
   }
   if (threadIdx.x == 0) pair_offsets[nlist] = total;
   s = 0;
+  int s2 = 0;
   for (int i = b; i < e; ++i) {
     const int l = order ? order[i] : i;
-    s += (counts[l] + group - 1) / group;
+    const int c = counts[l];
+    const int ng = (c + group - 1) / group;
+    const bool small_last = small_max > 0 && ng > 0 && c - (ng - 1) * group <= small_max;
+    s += ng - (small_last ? 1 : 0);
+    s2 += small_last ? 1 : 0;
   }
-  int total_items;
+  int total_items, total2;
   run = block_exclusive_scan<int>(s, sums, total_items);
+  __syncthreads();
+  int run2 = block_exclusive_scan<int>(s2, sums, total2);
   for (int i = b; i < e; ++i) {
     const int l = order ? order[i] : i;
-    const int ng = (counts[l] + group - 1) / group;
-    for (int g = 0; g < ng; ++g) items[run++] = make_int2(l, g);
+    const int c = counts[l];
+    const int ng = (c + group - 1) / group;
+    const bool small_last = small_max > 0 && ng > 0 && c - (ng - 1) * group <= small_max;
+    for (int g = 0; g < ng; ++g) {
+      if (small_last && g == ng - 1)
+        items2[run2++] = make_int2(l, g);
+      else
+        items[run++] = make_int2(l, g);
+    }
   }
-  if (threadIdx.x == 0) *item_total = total_items;
+  if (threadIdx.x == 0) {
+    *item_total = total_items;
+    if (item_total2) *item_total2 = total2;
+  }
 }
 
 __global__ void ivf_scatter_kernel(const int64_t* __restrict__ probes, int64_t n, int nlist,
@@ -351,6 +371,8 @@ IvfGroups carve_ivf_groups(Carver& c, int64_t nq, int nlist, int P) {
   g.pairs = c.take<int>((size_t)nq * P);
   g.items = c.take<int2>((size_t)nq * P);
   g.item_total = c.take<int>(1);
+  g.items2 = c.take<int2>((size_t)nq * P);
+  g.item_total2 = c.take<int>(1);
   g.counter = c.take<int>(1);
   return g;
 }
@@ -358,7 +380,7 @@ IvfGroups carve_ivf_groups(Carver& c, int64_t nq, int nlist, int P) {
 int run_ivf_groups_ex(const IvfGroups& g, const int64_t* probes, int64_t nq, int P, int nlist,
                       const int64_t* list_offsets, const int32_t* list_order, float* pd,
                       int64_t* pl, int k, int64_t* pair_counts, int group, cudaStream_t stream,
-                      int s0, int s1) {
+                      int s0, int s1, int small_max) {
   if (s1 < 0) s1 = P;
   const int64_t n = nq * P;
   ScopedTiming tm("ivf_group", stream);
@@ -369,7 +391,8 @@ int run_ivf_groups_ex(const IvfGroups& g, const int64_t* probes, int64_t nq, int
     MF_LAUNCH_CHECK();
   }
   ivf_plan_kernel<<<1, kScanBlock, 0, stream>>>(g.counts, nlist, list_order, g.pair_offsets,
-                                                g.items, g.item_total, g.cursors, group);
+                                                g.items, g.item_total, g.cursors, group, g.items2,
+                                                g.item_total2, small_max);
   MF_LAUNCH_CHECK();
   if (n > 0) {
     ivf_scatter_kernel<<<(unsigned int)ceil_div(n, 256), 256, 0, stream>>>(

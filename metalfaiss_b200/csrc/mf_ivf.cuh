@@ -15,7 +15,7 @@ int launch_iota_i32(int32_t* out, int64_t n, cudaStream_t stream);
 int run_ivf_groups_ex(const IvfGroups& g, const int64_t* probes, int64_t nq, int P, int nlist,
                       const int64_t* list_offsets, const int32_t* list_order, float* pd,
                       int64_t* pl, int k, int64_t* pair_counts, int group, cudaStream_t stream,
-                      int s0 = 0, int s1 = -1);
+                      int s0 = 0, int s1 = -1, int small_max = 0);
 
 size_t radix_sort_bytes(int64_t n);
 

@@ -97,7 +97,7 @@ __global__ void __launch_bounds__(kScanThreads) scan_kernel(const ScanArgs a) {
       }
     } else {
       const int2 it = a.items[item];
-      const int pb = a.pair_offsets[it.x] + it.y * kScanTQ;
+      const int pb = a.pair_offsets[it.x] + it.y * (a.group > 0 ? a.group : kScanTQ);
       const int pe0 = a.pair_offsets[it.x + 1];
       const int pe = pe0 < pb + kScanTQ ? pe0 : pb + kScanTQ;
       if (tid < kScanTQ) {
@@ -421,7 +421,9 @@ int launch_scan(const ScanArgs& a, int metric, int epi, int64_t total_items, int
   MF_CUDA(cudaMemsetAsync(a.counter, 0, sizeof(int), stream));
   ScopedTiming tm(epi == kEpiTopK
                       ? (a.flat ? "scan_topk_flat"
-                                : (a.max_rows > 0 ? "scan_topk_ivf_bound" : "scan_topk_ivf"))
+                                : (a.max_rows > 0 ? "scan_topk_ivf_bound"
+                                                  : (a.group > 0 ? "scan_topk_ivf_small"
+                                                                 : "scan_topk_ivf")))
                       : "scan_range",
                   stream);
   fn<<<(unsigned int)grid, kScanThreads, smem, stream>>>(a);

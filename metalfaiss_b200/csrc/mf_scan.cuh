@@ -17,7 +17,7 @@ constexpr int kScanTQ = 32;        // queries per item (4 per warp)
 constexpr int kScanTR = 128;       // rows per tile (4 per lane)
 constexpr int kScanDC = 32;        // d-chunk staged per pipeline stage
 constexpr int kScanXS = kScanDC + 4;  // padded smem row stride (floats): conflict-free LDS.128
-constexpr int kScanStages = 2;
+constexpr int kScanStages = 4;  // cp.async ring depth: enough bytes in flight per SM to cover HBM latency
 
 enum ScanEpilogue { kEpiTopK = 0, kEpiCount = 1, kEpiFill = 2 };
 
@@ -39,6 +39,7 @@ struct ScanArgs {
   // IVF items
   const int2* items;      // (list, group)
   const int* item_total;  // device scalar
+  int group;              // queries per group the items were cut into (0: the kernel's own)
   const int64_t* list_offsets;  // (nlist+1) rows of xb
   const int* pair_offsets;      // (nlist+1) into pairs
   const int* pairs;             // q*P + slot, grouped by list
@@ -64,6 +65,14 @@ struct ScanArgs {
 // of tc_group() queries; a.xq / a.xb are the fp32 (hi) operands, a_lo / b_lo
 // their tf32 residuals, a_rows / b_rows their row counts.
 bool tc_eligible(int metric, int d, int k, int64_t xb_rows);
+// One warp per IVF item of at most few_max_queries() queries (mf_few.cu):
+// items from a.items / a.item_total cut into groups of a.group, L2 or inner
+// product, d <= 256, k <= 32.
+bool few_eligible(int metric, int d, int k);
+int few_max_queries();
+int launch_few_scan(const ScanArgs& a, int metric, int64_t max_items, int device,
+                    cudaStream_t stream);
+
 // True when the tensor-core scan keeps the query tile in tensor memory
 // (d <= 128): it then reads raw fp32 queries (a.xq, rows of a.d floats; for
 // IVF through a.pairs) and needs neither a_lo nor gathered query rows.
@@ -123,6 +132,8 @@ struct IvfGroups {
   int* pairs;         // nq*P
   int2* items;        // nq*P (upper bound)
   int* item_total;    // 1
+  int2* items2;       // groups of few queries, when split off (nq*P upper bound)
+  int* item_total2;   // 1
   int* counter;       // 1
 };
 size_t ivf_groups_bytes(int64_t nq, int nlist, int P);
