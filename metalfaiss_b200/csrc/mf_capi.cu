@@ -156,11 +156,11 @@ int coarse_metric(int metric) {
 // The items split off as few-query groups (w.g.items2): one warp per item
 // where the shape allows, else the SIMT scan.
 int scan_small_items(const ScanArgs& base, const IvfWs& w, int metric, int64_t max_items,
-                     int device, cudaStream_t stream) {
+                     int device, cudaStream_t stream, int group) {
   ScanArgs sa = base;
   sa.items = w.g.items2;
   sa.item_total = w.g.item_total2;
-  sa.group = tc_group();
+  sa.group = group;
   if (few_eligible(metric, sa.d, sa.k)) return launch_few_scan(sa, metric, max_items, device, stream);
   return launch_scan(sa, metric, kEpiTopK, max_items, device, stream);
 }
@@ -205,6 +205,8 @@ int ivf_scan_topk(int device, cudaStream_t stream, const IvfWs& w, const float* 
   // belongs to the top-k.
   constexpr int64_t kBoundRows = 128;
   constexpr int kSmallGroup = 16;
+  // bound pass groups: the SIMT scan's 32 queries per item
+  const int few_group = kScanTQ;
   const int phases = (bound_out || bound_in) ? 1 : (P > 1 ? 2 : 1);
   float* const bound_dst = bound_out ? bound_out : w.bound;
   for (int ph = 0; ph < phases; ++ph) {
@@ -215,17 +217,21 @@ int ivf_scan_topk(int device, cudaStream_t stream, const IvfWs& w, const float* 
     // list's last group of at most kSmallGroup queries goes to the SIMT scan:
     // a 128-query tile would be mostly padding, and those rows' bytes, not
     // their arithmetic, bound the work.
-    // (L2 only: the bound then carries the margin that covers both engines)
-    const int small_max = use_tc && !bounding && metric == MF_METRIC_L2 ? kSmallGroup : 0;
+    // (L2 only: the bound then carries the margin that covers both engines).
+    // The SIMT bound pass splits off its small groups the same way.
+    const bool few_ok = few_eligible(metric, d, k) && metric == MF_METRIC_L2;
+    const int small_max = (use_tc && !bounding && metric == MF_METRIC_L2) ? kSmallGroup
+                          : (simt_bound && few_ok) ? few_max_queries() : 0;
+    const int grp = use_tc ? tc_group() : (small_max > 0 ? few_group : kScanTQ);
     MF_TRY(run_ivf_groups_ex(w.g, probes, nq, P, nlist, list_offsets, list_order, w.pd, w.pl, k,
-                             nullptr, use_tc ? tc_group() : kScanTQ, stream, 0,
-                             bounding ? 1 : P, small_max));
+                             nullptr, grp, stream, 0, bounding ? 1 : P, small_max));
     a.max_rows = bounding ? kBoundRows : 0;
     a.bound = bound_in ? bound_in : ((phases == 2 && ph == 1) ? w.bound : nullptr);
     if (use_tc && tc_raw_queries(d, k)) {
       // the scan loads each item's queries itself (through a.pairs)
       MF_TRY(launch_tc_scan(a, metric, nullptr, nq, list_lo, ntotal, nq * P, device, stream));
-      if (small_max > 0) MF_TRY(scan_small_items(a, w, metric, nq * P, device, stream));
+      if (small_max > 0)
+        MF_TRY(scan_small_items(a, w, metric, nq * P, device, stream, tc_group()));
     } else if (use_tc) {
       // A operand: the queries of every (query, probe) pair, gathered in list order
       MF_TRY(launch_gather_queries(xq, d, w.g.pairs, w.g.pair_offsets + nlist, nq * P, P, w.g_hi,
@@ -233,7 +239,16 @@ int ivf_scan_topk(int device, cudaStream_t stream, const IvfWs& w, const float* 
       a.xq = w.g_hi;
       MF_TRY(launch_tc_scan(a, metric, w.g_lo, nq * P, list_lo, ntotal, nq * P, device, stream));
       a.xq = xq;
-      if (small_max > 0) MF_TRY(scan_small_items(a, w, metric, nq * P, device, stream));
+      if (small_max > 0)
+        MF_TRY(scan_small_items(a, w, metric, nq * P, device, stream, tc_group()));
+    } else if (small_max > 0) {
+      // bound pass: groups of up to few_group queries; the last group of a
+      // list when it holds at most few_max_queries() goes to the few-query
+      // scan, the other groups to the SIMT scan
+      ScanArgs ga = a;
+      ga.group = few_group;
+      MF_TRY(launch_scan(ga, metric, kEpiTopK, nq * P, device, stream));
+      MF_TRY(scan_small_items(ga, w, metric, nq * P, device, stream, few_group));
     } else {
       MF_TRY(launch_scan(a, metric, kEpiTopK, nq * P, device, stream));
     }

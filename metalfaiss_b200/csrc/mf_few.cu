@@ -95,7 +95,8 @@ __global__ void __launch_bounds__(kFewWarps * 32) few_scan_kernel(const ScanArgs
     const int pe0 = a.pair_offsets[g.x + 1];
     const int nq = (pe0 - pb) < kFewMax ? (pe0 - pb) : kFewMax;
     const long long rb = a.list_offsets[g.x];
-    const long long re = a.list_offsets[g.x + 1];
+    const long long re_all = a.list_offsets[g.x + 1];
+    const long long re = (a.max_rows > 0 && re_all - rb > a.max_rows) ? rb + a.max_rows : re_all;
     // the item's queries (shared by the four warps)
     if (threadIdx.x < nq) {
       const int pr = a.pairs[pb + threadIdx.x];
@@ -231,7 +232,7 @@ int launch_few_scan(const ScanArgs& a, int metric, int64_t max_items, int device
   long long grid = (long long)num_sms(device) * per_sm;
   if (grid > max_items) grid = max_items;
   MF_CUDA(cudaMemsetAsync(a.counter, 0, sizeof(int), stream));
-  ScopedTiming tm("scan_topk_ivf_small", stream);
+  ScopedTiming tm(a.max_rows > 0 ? "scan_topk_ivf_bound_small" : "scan_topk_ivf_small", stream);
   fn<<<(unsigned int)grid, kFewWarps * 32, smem, stream>>>(a);
   MF_LAUNCH_CHECK();
   return MF_OK;
