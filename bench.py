@@ -187,17 +187,16 @@ def build_index(cfg, device, seed=1234):
     return idx, xq
 
 
-# A list's last group of at most this many queries is scanned by the SIMT
-# kernel, the other groups (up to 128 queries) by the tensor-core kernel.
+# A list probed by at most this many queries is scanned by the few-query
+# kernel; the others, in groups of up to 128 queries, by the tensor-core kernel.
 SMALL_GROUP = 16
 
 
 def scan_work(idx, probes_np, d, k):
     """Work of one IVF scan over the probes (nq, P) of this index:
     * pairs: (query, row) distance evaluations in the tensor-core launch, i.e.
-      over the groups of more than SMALL_GROUP queries (a list probed by q
-      queries is cut into groups of 128; its last group goes to the SIMT
-      scan when it holds SMALL_GROUP queries or fewer);
+      over the lists probed by more than SMALL_GROUP queries (a list probed by
+      at most SMALL_GROUP queries is scanned by the few-query kernel);
     * bytes: what the list-major scan must move once: every probed list's rows
       (vector + norm) read once, the query vectors read once and each
       (query, probe) pair's k partial results written once;
@@ -207,9 +206,8 @@ def scan_work(idx, probes_np, d, k):
     probed = np.unique(valid)
     rows = int(sizes[probed].sum())
     qpl = np.bincount(valid, minlength=len(sizes))
-    last = qpl - (np.maximum(qpl, 1) - 1) // 128 * 128
-    small = (qpl > 0) & (last <= SMALL_GROUP)
-    pairs = int((sizes * qpl).sum() - (sizes * np.where(small, last, 0)).sum())
+    small = (qpl > 0) & (qpl <= SMALL_GROUP)
+    pairs = int((sizes * np.where(small, 0, qpl)).sum())
     small_rows = int(sizes[small].sum())
     nq, P = probes_np.shape
     return pairs, rows * (4 * d + 4) + nq * d * 4 + nq * P * k * 12, rows, small_rows
@@ -343,7 +341,7 @@ def run_ours(args, cfg):
             "roofline": {
                 "bound": "tensor",
                 "kernel": "tq_scan_kernel (IVF list-major 3xTF32 tcgen05 scan + fused top-k), "
-                          "all-probes pass over groups of more than 16 queries",
+                          "all-probes pass over lists probed by more than 16 queries",
                 "achieved": round(tflops, 2) if tflops else None,
                 "peak": round(tf32_peak, 1),
                 "unit": "TFLOP/s",
@@ -367,7 +365,7 @@ def run_ours(args, cfg):
                 # the few-query groups' pass (one 4-warp block per item): bound by
                 # reading those lists' rows (vector + norm) once
                 "small_groups": {
-                    "kernel": "few_scan_kernel (lists' last groups of at most 16 queries)",
+                    "kernel": "few_scan_kernel (lists probed by at most 16 queries)",
                     "rows_per_launch": small_rows,
                     "bytes_per_launch": small_rows * (4 * d + 4),
                     "avg_launch_ms": round(small_ms / small_n, 4) if small_n else None,

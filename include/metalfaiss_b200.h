@@ -112,6 +112,19 @@ MF_API int mf_flat_search(int device, void* stream, const float* xq, int64_t nq,
                    int d, int metric, int k, const int64_t* ids, float* distances,
                    int64_t* labels, void* workspace, size_t workspace_bytes);
 
+/* mf_flat_search with bound[q] (nq floats), an upper bound on query q's k-th
+ * distance known in advance (e.g. from a subset of the rows plus a rounding
+ * margin): rows farther than it are not kept, so few candidates reach the
+ * top-k lists from the first tile on. With a valid bound the results equal
+ * mf_flat_search's; where fewer than k rows are within bound[q] the slots are
+ * padded (+inf, -1). Same workspace as mf_flat_search. Used for the coarse
+ * step of an IVF search; no counterpart in the reference. */
+MF_API int mf_flat_search_bounded(int device, void* stream, const float* xq, int64_t nq,
+                                  const float* xb, const float* xb_norms, const float* xb_lo,
+                                  int64_t nb, int d, int metric, int k, const int64_t* ids,
+                                  const float* bound, float* distances, int64_t* labels,
+                                  void* workspace, size_t workspace_bytes);
+
 /* Size of the fixed device scratch array behind mf_flat_search_noalloc. */
 #define MF_NOALLOC_SCRATCH_BYTES (16u << 20)
 

@@ -35,6 +35,7 @@ _SIGNATURES = {
     "mf_flat_search_workspace_size": ([I64, I64, I32, I32, I32, PSZ], I32),
     "mf_flat_search": ([I32, P, P, I64, P, P, P, I64, I32, I32, I32, P, P, P, P, SZ], I32),
     "mf_flat_search_noalloc": ([I32, P, P, I64, P, P, P, I64, I32, I32, I32, P, P, P], I32),
+    "mf_flat_search_bounded": ([I32, P, P, I64, P, P, P, I64, I32, I32, I32, P, P, P, P, P, SZ], I32),
     "mf_ivf_search_workspace_size": ([I64, I32, I32, I32, I32, I32, PSZ], I32),
     "mf_ivf_search": ([I32, P, P, I64, P, P, I32, I32, P, P, P, P, P, I64, P, I32, I32, I32, P, P, P, SZ], I32),
     "mf_ivf_search_preassigned_workspace_size": ([I64, I32, I32, I32, I32, I32, PSZ], I32),

@@ -214,7 +214,7 @@ int ivf_scan_topk(int device, cudaStream_t stream, const IvfWs& w, const float* 
     const bool simt_bound = bounding && tc && metric == MF_METRIC_L2;
     const bool use_tc = tc && !simt_bound;
     // Tensor-core pass: groups of up to 128 queries per list, except that a
-    // list's last group of at most kSmallGroup queries goes to the SIMT scan:
+    // list probed by at most kSmallGroup queries goes to the few-query scan:
     // a 128-query tile would be mostly padding, and those rows' bytes, not
     // their arithmetic, bound the work.
     // (L2 only: the bound then carries the margin that covers both engines).
@@ -242,9 +242,9 @@ int ivf_scan_topk(int device, cudaStream_t stream, const IvfWs& w, const float* 
       if (small_max > 0)
         MF_TRY(scan_small_items(a, w, metric, nq * P, device, stream, tc_group()));
     } else if (small_max > 0) {
-      // bound pass: groups of up to few_group queries; the last group of a
-      // list when it holds at most few_max_queries() goes to the few-query
-      // scan, the other groups to the SIMT scan
+      // bound pass: a list that is the nearest for at most few_max_queries()
+      // queries goes to the few-query scan, the others, in groups of
+      // few_group queries, to the SIMT scan
       ScanArgs ga = a;
       ga.group = few_group;
       MF_TRY(launch_scan(ga, metric, kEpiTopK, nq * P, device, stream));
@@ -333,6 +333,31 @@ int mf_flat_search(int device, void* stream, const float* xq, int64_t nq, const 
   MF_TRY(check_device_ptr(xb_lo, "xb_lo", true));
   return run_flat_topk(device, (cudaStream_t)stream, xq, nq, xb, xb_norms, xb_lo, nb, d, metric,
                        k, ids, distances, labels, workspace, workspace_bytes);
+}
+
+int mf_flat_search_bounded(int device, void* stream, const float* xq, int64_t nq,
+                           const float* xb, const float* xb_norms, const float* xb_lo, int64_t nb,
+                           int d, int metric, int k, const int64_t* ids, const float* bound,
+                           float* distances, int64_t* labels, void* workspace,
+                           size_t workspace_bytes) {
+  MF_ENTER(device);
+  MF_TRY(check_common(d, metric, k, true));
+  MF_CHECK(nq >= 0 && nb >= 0, MF_ERR_INVALID_ARGS, "negative sizes");
+  MF_CHECK(nb < (1ll << 31) - 1, MF_ERR_INVALID_ARGS, "nb=%lld exceeds 2^31-2 rows per call",
+           (long long)nb);
+  MF_CHECK(nq < (1ll << 31) / 2, MF_ERR_INVALID_ARGS, "nq too large");
+  if (nq == 0) return MF_OK;
+  MF_TRY(check_device_ptr(xq, "xq"));
+  MF_TRY(check_device_ptr(bound, "bound"));
+  MF_TRY(check_device_ptr(distances, "distances"));
+  MF_TRY(check_device_ptr(labels, "labels"));
+  MF_TRY(check_device_ptr(xb, "xb", nb == 0));
+  MF_TRY(check_device_ptr(ids, "ids", true));
+  if (metric == MF_METRIC_L2) MF_TRY(check_device_ptr(xb_norms, "xb_norms", nb == 0));
+  MF_TRY(check_device_ptr(workspace, "workspace", true));
+  MF_TRY(check_device_ptr(xb_lo, "xb_lo", true));
+  return run_flat_topk(device, (cudaStream_t)stream, xq, nq, xb, xb_norms, xb_lo, nb, d, metric,
+                       k, ids, distances, labels, workspace, workspace_bytes, bound);
 }
 
 int mf_ivf_search_workspace_size(int64_t nq, int nlist, int nprobe, int d, int metric, int k,

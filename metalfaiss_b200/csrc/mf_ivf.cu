@@ -85,8 +85,10 @@ __global__ void ivf_count_kernel(const int64_t* __restrict__ probes, int64_t n, 
   }
 }
 
-// With small_max > 0, groups of at most small_max queries go to items2
-// (item_total2) instead of items; both keep the list order.
+// With small_max > 0, a list probed by at most small_max queries goes whole to
+// items2 (item_total2) as one item; the other lists' groups go to items. The
+// choice depends only on a list's query count, so it does not vary between
+// runs; both keep the list order.
 __global__ void __launch_bounds__(kScanBlock) ivf_plan_kernel(const int* __restrict__ counts,
                                                              int nlist,
                                                              const int32_t* __restrict__ order,
@@ -114,9 +116,9 @@ __global__ void __launch_bounds__(kScanBlock) ivf_plan_kernel(const int* __restr
     const int l = order ? order[i] : i;
     const int c = counts[l];
     const int ng = (c + group - 1) / group;
-    const bool small_last = small_max > 0 && ng > 0 && c - (ng - 1) * group <= small_max;
-    s += ng - (small_last ? 1 : 0);
-    s2 += small_last ? 1 : 0;
+    const bool small_list = small_max > 0 && c > 0 && c <= small_max;
+    s += small_list ? 0 : ng;
+    s2 += small_list ? 1 : 0;
   }
   int total_items, total2;
   run = block_exclusive_scan<int>(s, sums, total_items);
@@ -126,13 +128,11 @@ __global__ void __launch_bounds__(kScanBlock) ivf_plan_kernel(const int* __restr
     const int l = order ? order[i] : i;
     const int c = counts[l];
     const int ng = (c + group - 1) / group;
-    const bool small_last = small_max > 0 && ng > 0 && c - (ng - 1) * group <= small_max;
-    for (int g = 0; g < ng; ++g) {
-      if (small_last && g == ng - 1)
-        items2[run2++] = make_int2(l, g);
-      else
-        items[run++] = make_int2(l, g);
-    }
+    const bool small_list = small_max > 0 && c > 0 && c <= small_max;
+    if (small_list)
+      items2[run2++] = make_int2(l, 0);
+    else
+      for (int g = 0; g < ng; ++g) items[run++] = make_int2(l, g);
   }
   if (threadIdx.x == 0) {
     *item_total = total_items;

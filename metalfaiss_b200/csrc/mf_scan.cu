@@ -559,7 +559,8 @@ FlatPlan plan_flat(int64_t nq, int64_t nb, int d, int k, int device, int tq) {
 
 int run_flat_topk(int device, cudaStream_t stream, const float* xq, int64_t nq, const float* xb,
                   const float* xb_norms, const float* xb_lo, int64_t nb, int d, int metric, int k,
-                  const int64_t* ids, float* D, int64_t* I, void* ws, size_t ws_bytes) {
+                  const int64_t* ids, float* D, int64_t* I, void* ws, size_t ws_bytes,
+                  const float* bound) {
   const bool tc = tc_eligible(metric, d, k, nb) && (xb_lo != nullptr || tc_raw_queries(d, k));
   const FlatPlan p = plan_flat(nq, nb, d, k, device, tc ? tc_group() : 32);
   MF_CHECK(ws_bytes >= p.bytes, MF_ERR_INVALID_ARGS,
@@ -590,6 +591,7 @@ int run_flat_topk(int device, cudaStream_t stream, const float* xq, int64_t nq, 
   a.nb = nb;
   a.rows_per_split = p.rows_per_split;
   a.counter = counter;
+  a.bound = bound;
   a.direct = p.splits > 1 ? 0 : 1;
   a.out_d = p.splits > 1 ? pd : D;
   a.out_l = p.splits > 1 ? pl : I;

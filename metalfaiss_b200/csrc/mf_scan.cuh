@@ -120,9 +120,12 @@ FlatPlan plan_flat(int64_t nq, int64_t nb, int d, int k, int device, int tq = 32
 
 // Runs flat top-k into (nq, k) outputs using the given workspace. With xb_lo
 // (the tf32 residual of xb) the tensor-core engine runs where eligible.
+// bound (nq floats, optional): an upper bound on each query's k-th distance;
+// rows farther than it are not kept (results may then hold fewer than k).
 int run_flat_topk(int device, cudaStream_t stream, const float* xq, int64_t nq, const float* xb,
                   const float* xb_norms, const float* xb_lo, int64_t nb, int d, int metric, int k,
-                  const int64_t* ids, float* D, int64_t* I, void* ws, size_t ws_bytes);
+                  const int64_t* ids, float* D, int64_t* I, void* ws, size_t ws_bytes,
+                  const float* bound = nullptr);
 
 // IVF list grouping: probes (nq, P) -> pairs grouped by list and items.
 struct IvfGroups {

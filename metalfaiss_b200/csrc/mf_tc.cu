@@ -159,11 +159,16 @@ __device__ __forceinline__ ItemDesc item_desc(const ScanArgs& a, int item) {
     const long long re = it.rb + a.rows_per_split;
     it.re = re < a.nb ? re : a.nb;
   } else {
+    // a list's q queries are cut into ceil(q / 128) groups of nearly equal
+    // size (group g: [p0 + g q / ng, p0 + (g + 1) q / ng))
     const int2 g = a.items[item];
-    const int pb = a.pair_offsets[g.x] + g.y * kTqM;
-    const int pe0 = a.pair_offsets[g.x + 1];
+    const int p0 = a.pair_offsets[g.x];
+    const int q = a.pair_offsets[g.x + 1] - p0;
+    const int ng = (q + kTqM - 1) / kTqM;
+    const int pb = p0 + (int)(((long long)g.y * q) / ng);
+    const int pe = p0 + (int)(((long long)(g.y + 1) * q) / ng);
     it.a_row0 = pb;
-    it.nq_item = (pe0 - pb) < kTqM ? (pe0 - pb) : kTqM;
+    it.nq_item = pe - pb;
     it.rb = a.list_offsets[g.x];
     const long long re = a.list_offsets[g.x + 1];
     it.re = (a.max_rows > 0 && re - it.rb > a.max_rows) ? it.rb + a.max_rows : re;

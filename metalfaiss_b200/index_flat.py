@@ -45,6 +45,7 @@ class FlatIndex:
                     if stores_residuals(self._dp, self._residuals) else None)
         self._ids = GrowBuffer((), torch.int64, self.device)
         self._ws = None
+        self._version = 0  # bumped by every change of the stored rows
         self.verbose = False
 
     # ------------------------------------------------------------- state
@@ -102,6 +103,7 @@ class FlatIndex:
         self._xb.append(x)
         self._norms.append(norms)
         self._ids.append(idt)
+        self._version += 1
 
     def add_with_ids(self, xs, ids) -> None:
         """64-bit ids (python/metalfaiss/unittest/test_mlx_index.py:231-240)."""
@@ -109,6 +111,7 @@ class FlatIndex:
 
     def reset(self) -> None:
         """python/metalfaiss/indexflat.py:127-133."""
+        self._version += 1
         self._xb.reset()
         self._norms.reset()
         if self._lo is not None:
@@ -157,6 +160,26 @@ class FlatIndex:
                  self.ntotal, self._dp, m, k,
                  nat.ptr(self._ids.buf) if map_ids else nat.ptr(None), nat.ptr(D), nat.ptr(I),
                  nat.ptr(ws), ws.numel())
+        return SearchResult(D, I)
+
+    def _search_bounded(self, xq: torch.Tensor, k: int, bound: torch.Tensor,
+                        map_ids: bool = True) -> SearchResult:
+        """_search_padded given bound[q], an upper bound on each query's k-th
+        distance (mf_flat_search_bounded): the same results, fewer candidates."""
+        nq = xq.shape[0]
+        D = torch.empty((nq, k), dtype=torch.float32, device=self.device)
+        I = torch.empty((nq, k), dtype=torch.int64, device=self.device)
+        if nq == 0 or k == 0:
+            return SearchResult(D, I)
+        m = int(self.metric_type)
+        ws_bytes = nat.workspace_size("mf_flat_search_workspace_size", nq, self.ntotal, self._dp,
+                                      m, k)
+        ws = self._workspace().get(ws_bytes)
+        nat.call("mf_flat_search_bounded", self.device.index, nat.stream_of(self.device),
+                 nat.ptr(xq), nq, nat.ptr(self._xb.buf), nat.ptr(self._norms.buf),
+                 nat.ptr(self._lo.buf if self._lo is not None else None), self.ntotal, self._dp,
+                 m, k, nat.ptr(self._ids.buf) if map_ids else nat.ptr(None), nat.ptr(bound),
+                 nat.ptr(D), nat.ptr(I), nat.ptr(ws), ws.numel())
         return SearchResult(D, I)
 
     def assign(self, xs, k: int = 1) -> torch.Tensor:

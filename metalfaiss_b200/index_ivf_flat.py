@@ -59,6 +59,7 @@ class IVFFlatIndex:
         # residuals=False: no stored tf32 residuals (half the memory; the scan
         # derives them for d <= 128)
         self._residuals = bool(residuals)
+        self._cq = None  # (key, IVF over the centroids) for the coarse step's bound
         if self.metric_type not in SUPPORTED_METRICS:
             raise NotImplementedFaissError(f"metric {self.metric_type.name} is not supported")
         self.device = default_device(device if device is not None else
@@ -254,6 +255,9 @@ class IVFFlatIndex:
         if q.metric_type != coarse:
             probes = q._search_padded(xq, min(self._nprobe, self._nlist), map_ids=False).labels
             return self._search_preassigned_padded(xq, k, probes)
+        cq = self._centroid_index()
+        if cq is not None:
+            return self._search_preassigned_padded(xq, k, self._coarse_probes(xq, cq))
         m = int(self.metric_type)
         nbytes = nat.workspace_size("mf_ivf_search_workspace_size", nq, self._nlist, self._nprobe,
                                     self._dp, m, k)
@@ -264,6 +268,43 @@ class IVFFlatIndex:
                  nat.ptr(self._lo), nat.ptr(self._ids), self._vecs.shape[0], nat.ptr(self._order),
                  self._dp, m, k, nat.ptr(D), nat.ptr(I), nat.ptr(ws), ws.numel())
         return SearchResult(D, I)
+
+    # ----------------------------------------------- coarse step with a bound
+    # Lists at least this many: the coarse step's top-nprobe over the centroids
+    # starts from a bound taken from an IVF over the centroids themselves.
+    COARSE_BOUND_MIN_NLIST = 2048
+
+    def _centroid_index(self):
+        """An IVFFlat index over this index's centroids (~128 centroids per
+        list), built on first use and rebuilt when the centroids change; None
+        where it does not pay (IP, few lists, small nprobe) or cannot run."""
+        q = self._quantizer
+        P = min(self._nprobe, self._nlist)
+        if (self.metric_type != MetricType.L2 or q.metric_type != MetricType.L2
+                or self._nlist < self.COARSE_BOUND_MIN_NLIST or P < 8
+                or P > nat.load().mf_max_k() or self._dp > 128 or q.ntotal != self._nlist):
+            return None
+        key = (id(q), q._version)
+        if self._cq is not None and self._cq[0] == key:
+            return self._cq[1]
+        from .clustering import ClusteringParameters as CP
+        n2 = max(16, self._nlist // 128)
+        cents = q._xb.view()[:, : self.d]
+        cq = IVFFlatIndex(self.d, n2, device=self.device,
+                          clustering=CP(niter=10, seed=97, max_points_per_centroid=0))
+        cq.train(cents)
+        cq.add(cents)  # ids = centroid index
+        self._cq = (key, cq)
+        return cq
+
+    def _coarse_probes(self, xq: torch.Tensor, cq) -> torch.Tensor:
+        """Exact top-nprobe centroids: the quantizer's flat search, bounded by
+        the nprobe-th distance among the first 128 centroids of the query's
+        nearest centroid list (plus the engines' rounding margin)."""
+        P = min(self._nprobe, self._nlist)
+        near = cq.quantizer._search_padded(xq, 1, map_ids=False).labels.contiguous()
+        bound = cq._probe_bound(xq, near, P)
+        return self._quantizer._search_bounded(xq, P, bound, map_ids=False).labels.contiguous()
 
     def _check_k(self, k):
         mk = nat.load().mf_max_k()

@@ -213,3 +213,30 @@ def test_topk_merge_capi(cuda_device):
     order = np.argsort(np.where(flatl >= 0, flatd, np.inf), axis=1, kind="stable")[:, :k]
     assert np.array_equal(D.cpu().numpy(), np.take_along_axis(flatd, order, 1))
     assert np.array_equal(I.cpu().numpy(), np.take_along_axis(flatl, order, 1))
+
+
+def test_ivf_coarse_bound_path_equals_plain(cuda_device):
+    """With nlist >= 2048 the coarse step starts from a bound taken from an IVF
+    over the centroids; its probes and the search results must equal those of
+    the unbounded coarse step (mf_ivf_search)."""
+    x, cen, _ = syn.mixture(200_000, 64, 2048, seed=61)
+    idx = IVFFlatIndex(64, 2048)
+    idx.set_centroids(x[:: 200_000 // 2048][:2048])
+    idx.add(x)
+    idx.nprobe = 24
+    xq, _, _ = syn.mixture(3000, 64, 2048, seed=62, centres=cen)
+    xt = idx._prepare_query(xq)
+    cq = idx._centroid_index()
+    assert cq is not None
+    probes_b = idx._coarse_probes(xt, cq).cpu().numpy()
+    probes_p = idx.quantizer._search_padded(xt, 24, map_ids=False).labels.cpu().numpy()
+    assert np.array_equal(probes_b, probes_p)
+    D1, I1 = idx.search(xq, 10).numpy()          # bounded coarse step
+    old = IVFFlatIndex.COARSE_BOUND_MIN_NLIST
+    try:
+        IVFFlatIndex.COARSE_BOUND_MIN_NLIST = 1 << 30
+        D2, I2 = idx.search(xq, 10).numpy()      # mf_ivf_search
+    finally:
+        IVFFlatIndex.COARSE_BOUND_MIN_NLIST = old
+    np.testing.assert_array_equal(I1, I2)
+    np.testing.assert_array_equal(D1, D2)
