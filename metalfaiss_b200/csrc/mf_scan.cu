@@ -521,6 +521,30 @@ int launch_merge(const float* pd, const int64_t* pl, int64_t nq, int parts, int 
 namespace {
 void plan_splits(FlatPlan& p, int64_t nq, int64_t nb, int k, int device, int tq, int per_sm) {
   p.nqt = (int)ceil_div(nq, tq);
+  if (per_sm == 0) {
+    // Tensor cores, one persistent CTA per SM: equal runs of tiles, each CTA
+    // taking the pieces (cut at query-tile boundaries) of its own run, so no
+    // SM waits on another's last item. A query tile's pieces write separate
+    // partial slots: as many as the most runs one query tile meets.
+    const long long sms = device >= 0 ? num_sms(device) : 148;
+    const long long tpq = nb > 0 ? ceil_div(nb, kScanTR) : 1;
+    const long long total = (long long)(p.nqt > 0 ? p.nqt : 1) * tpq;
+    const long long g0 = total < sms ? total : sms;
+    const long long T = ceil_div(total, g0);
+    long long pmax = 1;
+    for (long long q = 0; q < p.nqt; ++q) {
+      const long long c0 = (q * tpq) / T;
+      const long long c1 = ((q + 1) * tpq - 1) / T;
+      if (c1 - c0 + 1 > pmax) pmax = c1 - c0 + 1;
+    }
+    p.splits = (int)pmax;
+    p.rows_per_split = 0;
+    p.chunk_tiles = T;
+    p.tiles_per_qt = tpq;
+    p.chunks = (int)ceil_div(total, T);
+    (void)k;
+    return;
+  }
   // SIMT: about two waves of resident CTAs (per_sm CTAs per SM); tensor
   // cores (per_sm = 0): about one item per SM, since every split restarts the
   // top-k lists. Each split keeps >= 1 tile.
@@ -590,6 +614,8 @@ int run_flat_topk(int device, cudaStream_t stream, const float* xq, int64_t nq, 
   a.nqt = p.nqt;
   a.nb = nb;
   a.rows_per_split = p.rows_per_split;
+  a.chunk_tiles = tc ? p.chunk_tiles : 0;
+  a.tiles_per_qt = tc ? p.tiles_per_qt : 0;
   a.counter = counter;
   a.bound = bound;
   a.direct = p.splits > 1 ? 0 : 1;
@@ -598,8 +624,11 @@ int run_flat_topk(int device, cudaStream_t stream, const float* xq, int64_t nq, 
   if (tc) {
     const bool raw = tc_raw_queries(d, k);  // else the scan streams (xq, q_lo) tiles
     if (!raw) MF_TRY(launch_tf32_residual(xq, nq, d, q_lo, stream));
-    MF_TRY(launch_tc_scan(a, metric, raw ? nullptr : q_lo, nq, xb_lo, nb,
-                          (int64_t)p.nqt * p.splits, device, stream));
+    // a query tile meets fewer runs than the widest: its other slots stay empty
+    if (p.splits > 1)
+      MF_CUDA(cudaMemsetAsync(pl, 0xff, sizeof(int64_t) * (size_t)nq * p.splits * k, stream));
+    MF_TRY(launch_tc_scan(a, metric, raw ? nullptr : q_lo, nq, xb_lo, nb, p.chunks, device,
+                          stream));
   } else {
     MF_TRY(launch_scan(a, metric, kEpiTopK, (int64_t)p.nqt * p.splits, device, stream));
   }

@@ -36,6 +36,11 @@ struct ScanArgs {
   int nqt;
   int64_t nb;
   int64_t rows_per_split;
+  // flat on tensor cores: CTA c scans tiles [c chunk_tiles, (c+1) chunk_tiles)
+  // of the (query tile x 128-row tile) space; the piece of query tile q in
+  // chunk c writes partial slot c - (q tiles_per_qt) / chunk_tiles
+  int64_t chunk_tiles;
+  int64_t tiles_per_qt;
   // IVF items
   const int2* items;      // (list, group)
   const int* item_total;  // device scalar
@@ -113,6 +118,11 @@ struct FlatPlan {
   int splits;
   int64_t rows_per_split;
   size_t bytes;
+  // tensor cores: the (query tile x 128-row tile) space is cut into `chunks`
+  // equal runs of chunk_tiles tiles, one per CTA (0 = items of whole splits)
+  int64_t chunk_tiles = 0;
+  int64_t tiles_per_qt = 0;
+  int chunks = 0;
 };
 // tq = queries per item (32 for the SIMT scan, tc_group() for tensor cores);
 // bytes covers both engines.

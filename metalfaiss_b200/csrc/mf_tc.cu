@@ -139,6 +139,7 @@ struct ItemDesc {
   long long rb, re;  // row slab
   int a_row0;        // first A row (queries) in the A tensor map
   int nq_item;       // valid queries (A rows) of this item
+  int part;          // flat: the partial slot of this item's query tile
 };
 
 // A queue slot: the item index (-1 ends the roles' loops) and its geometry.
@@ -158,7 +159,9 @@ __device__ __forceinline__ ItemDesc item_desc(const ScanArgs& a, int item) {
     it.rb = (long long)s * a.rows_per_split;
     const long long re = it.rb + a.rows_per_split;
     it.re = re < a.nb ? re : a.nb;
+    it.part = s;
   } else {
+    it.part = 0;
     // a list's q queries are cut into ceil(q / 128) groups of nearly equal
     // size (group g: [p0 + g q / ng, p0 + (g + 1) q / ng))
     const int2 g = a.items[item];
@@ -348,15 +351,43 @@ __global__ void __launch_bounds__(ATM ? kTqThreadsAtm : kTqThreads, 1)
       prefetch_tensormap(&maps.b_hi);
       if (!CONV) prefetch_tensormap(&maps.b_lo);
       uint32_t seq = 0;
+      // flat, chunked: this CTA's run of (query tile x 128-row tile) tiles
+      const bool chunked = a.flat && a.chunk_tiles > 0;
+      long long cg = chunked ? (long long)blockIdx.x * a.chunk_tiles : 0;
+      long long cend = 0;
+      if (chunked) {
+        const long long all = (long long)a.nqt * a.tiles_per_qt;
+        cend = cg + a.chunk_tiles < all ? cg + a.chunk_tiles : all;
+      }
       for (uint32_t qi = 0;; ++qi) {
         // take the next item and publish it (-1 ends every role's loop)
         const int qs = qi % kTqQueue;
         if (qi >= (uint32_t)kTqQueue)
           mbar_wait(&qempty[qs], ((qi / kTqQueue) - 1) & 1, s_abort, &g_device_error);
-        int item = *s_abort ? -1 : atomicAdd(a.counter, 1);
-        if (item >= total) item = -1;
+        int item = -1;
         ItemDesc it{};
-        if (item >= 0) it = item_desc(a, item);
+        if (chunked) {
+          // the next piece of the run: up to the end of its query tile
+          if (!*s_abort && cg < cend) {
+            const long long qt = cg / a.tiles_per_qt;
+            const long long t0 = cg - qt * a.tiles_per_qt;
+            long long t1 = t0 + (cend - cg);
+            if (t1 > a.tiles_per_qt) t1 = a.tiles_per_qt;
+            it.a_row0 = (int)(qt * kTqM);
+            const long long rem = a.nq - (long long)it.a_row0;
+            it.nq_item = (int)(rem < kTqM ? rem : kTqM);
+            it.rb = t0 * kScanTR;
+            const long long re = t1 * kScanTR;
+            it.re = re < a.nb ? re : a.nb;
+            it.part = (int)(blockIdx.x - (qt * a.tiles_per_qt) / a.chunk_tiles);
+            item = (int)qi;
+            cg += t1 - t0;
+          }
+        } else {
+          item = *s_abort ? -1 : atomicAdd(a.counter, 1);
+          if (item >= total) item = -1;
+          if (item >= 0) it = item_desc(a, item);
+        }
         s_q[qs].it = it;
         s_q[qs].item = item;
         mbar_arrive(&qfull[qs]);
@@ -669,8 +700,7 @@ __global__ void __launch_bounds__(ATM ? kTqThreadsAtm : kTqThreads, 1)
       if (valid) {
         if (a.flat) {
           q = it.a_row0 + tid;
-          const int s = item / a.nqt;
-          slot = a.direct ? q : (long long)q * a.P + s;
+          slot = a.direct ? q : (long long)q * a.P + it.part;
         } else {
           const int pr = a.pairs[it.a_row0 + tid];
           q = pr / a.P;

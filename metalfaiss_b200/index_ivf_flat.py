@@ -270,8 +270,12 @@ class IVFFlatIndex:
         return SearchResult(D, I)
 
     # ----------------------------------------------- coarse step with a bound
-    # Lists at least this many: the coarse step's top-nprobe over the centroids
-    # starts from a bound taken from an IVF over the centroids themselves.
+    # Opt-in: with coarse_bound set and at least COARSE_BOUND_MIN_NLIST lists,
+    # the coarse step's top-nprobe over the centroids starts from a bound taken
+    # from an IVF over the centroids themselves. It pays where the centroids
+    # cluster well; on centroids of isotropic mixtures the bound stays loose
+    # and the extra passes cost more than they save, so it is off by default.
+    coarse_bound = False
     COARSE_BOUND_MIN_NLIST = 2048
 
     def _centroid_index(self):
@@ -280,7 +284,8 @@ class IVFFlatIndex:
         where it does not pay (IP, few lists, small nprobe) or cannot run."""
         q = self._quantizer
         P = min(self._nprobe, self._nlist)
-        if (self.metric_type != MetricType.L2 or q.metric_type != MetricType.L2
+        if (not self.coarse_bound or self.metric_type != MetricType.L2
+                or q.metric_type != MetricType.L2
                 or self._nlist < self.COARSE_BOUND_MIN_NLIST or P < 8
                 or P > nat.load().mf_max_k() or self._dp > 128 or q.ntotal != self._nlist):
             return None

@@ -216,14 +216,15 @@ def test_topk_merge_capi(cuda_device):
 
 
 def test_ivf_coarse_bound_path_equals_plain(cuda_device):
-    """With nlist >= 2048 the coarse step starts from a bound taken from an IVF
-    over the centroids; its probes and the search results must equal those of
-    the unbounded coarse step (mf_ivf_search)."""
+    """With coarse_bound on and nlist >= 2048 the coarse step starts from a
+    bound taken from an IVF over the centroids; its probes and the search
+    results must equal those of the unbounded coarse step (mf_ivf_search)."""
     x, cen, _ = syn.mixture(200_000, 64, 2048, seed=61)
     idx = IVFFlatIndex(64, 2048)
     idx.set_centroids(x[:: 200_000 // 2048][:2048])
     idx.add(x)
     idx.nprobe = 24
+    idx.coarse_bound = True
     xq, _, _ = syn.mixture(3000, 64, 2048, seed=62, centres=cen)
     xt = idx._prepare_query(xq)
     cq = idx._centroid_index()
