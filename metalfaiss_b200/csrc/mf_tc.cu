@@ -39,7 +39,7 @@ __device__ int g_device_error = 0;
 
 #ifdef MF_TC_PROFILE
 // Per-role cycle counters (instrumented builds only).
-__device__ unsigned long long g_tc_prof[16];
+__device__ unsigned long long g_tc_prof[20];
 #define TQP(i, expr)                                       \
   do {                                                     \
     const long long _t0 = clock64();                       \
@@ -424,7 +424,9 @@ __global__ void __launch_bounds__(ATM ? kTqThreadsAtm : kTqThreads, 1)
       uint32_t seq = 0, tt = 0;
       for (uint32_t qi = 0;; ++qi) {
         const int qs = qi % kTqQueue;
-        if (!mbar_wait(&qfull[qs], (qi / kTqQueue) & 1, s_abort, &g_device_error)) break;
+        bool qok = true;
+        TQP(16, qok = mbar_wait(&qfull[qs], (qi / kTqQueue) & 1, s_abort, &g_device_error));
+        if (!qok) break;
         const int item = s_q[qs].item;
         const ItemDesc it = s_q[qs].it;
         mbar_arrive(&qempty[qs]);
@@ -433,7 +435,9 @@ __global__ void __launch_bounds__(ATM ? kTqThreadsAtm : kTqThreads, 1)
         const int nT = (int)((nrows + BN - 1) / BN);
         if (ATM) {
           // this item's query tile is in tensor memory
-          if (!mbar_wait(afull, qi & 1, s_abort, &g_device_error)) break;
+          bool aok = true;
+          TQP(17, aok = mbar_wait(afull, qi & 1, s_abort, &g_device_error));
+          if (!aok) break;
           tc_fence_after();
         }
         for (int t = 0; t < nT; ++t, ++tt) {
@@ -1072,9 +1076,9 @@ int launch_tc_scan(const ScanArgs& a, int metric, const float* a_lo, int64_t a_r
 
 #ifdef MF_TC_PROFILE
 extern "C" MF_API int mf_tc_profile_read(unsigned long long* out16, int reset) {
-  MF_CUDA(cudaMemcpyFromSymbol(out16, g_tc_prof, 16 * sizeof(unsigned long long)));
+  MF_CUDA(cudaMemcpyFromSymbol(out16, g_tc_prof, 20 * sizeof(unsigned long long)));
   if (reset) {
-    unsigned long long z[16] = {0};
+    unsigned long long z[20] = {0};
     MF_CUDA(cudaMemcpyToSymbol(g_tc_prof, z, sizeof(z)));
   }
   return MF_OK;
