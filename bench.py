@@ -213,6 +213,26 @@ def scan_work(idx, probes_np, d, k):
     return pairs, rows * (4 * d + 4) + nq * d * 4 + nq * P * k * 12, rows, small_rows
 
 
+def filter_work(idx, probes_np, d, slots=20):
+    """Work of the filter search's tensor-core pass over the probes (nq, P),
+    over the lists probed by more than SMALL_GROUP queries (the others go to
+    the exact few-query kernel, as in scan_work):
+    * pairs: (query, row) fp16 distance evaluations (in groups of up to 128
+      queries per list);
+    * bytes: those lists' fp16 residual rows and their squared norms read once,
+      the query rows and their list centroids read once per pair, and each
+      pair's slots (value + row) written at most once;
+    * rows: distinct rows of those lists."""
+    sizes = idx.list_sizes()
+    valid = probes_np[probes_np >= 0]
+    qpl = np.bincount(valid, minlength=len(sizes))
+    big = qpl > SMALL_GROUP
+    rows = int(sizes[big].sum())
+    pairs = int((sizes * np.where(big, qpl, 0)).sum())
+    npairs = int(qpl[big].sum())
+    return pairs, rows * (2 * d + 4) + npairs * d * 8 + npairs * slots * 12, rows
+
+
 def run_ours(args, cfg):
     import torch.distributed as dist
 
@@ -237,8 +257,12 @@ def run_ours(args, cfg):
 
     # probes (for the roofline bytes): the coarse step of this batch
     probes = idx.quantizer._search_padded(xq, min(cfg["nprobe"], cfg["nlist"]), map_ids=False).labels
-    pairs, alg_bytes, probed_rows, small_rows = scan_work(sharded.local if sharded else idx,
-                                                          probes.cpu().numpy(), d, k)
+    local = sharded.local if sharded else idx
+    filtered = local._filter_ok(k)
+    probes_np = probes.cpu().numpy()
+    pairs, alg_bytes, probed_rows, small_rows = scan_work(local, probes_np, d, k)
+    if filtered:
+        pairs, alg_bytes, probed_rows = filter_work(local, probes_np, d)
     logical_bytes = pairs * d * 4
     tf32_peak = tf32_gemm_peak(device) if rank == 0 else None
 
@@ -276,8 +300,10 @@ def run_ours(args, cfg):
         search(xq)
     torch.cuda.synchronize(device)
     nat.timing_enable(False)
-    scan_ms, scan_n = nat.timing_read("scan_topk_ivf")
+    scan_ms, scan_n = nat.timing_read("scan_topk_ivf_filter" if filtered else "scan_topk_ivf")
     small_ms, small_n = nat.timing_read("scan_topk_ivf_small")
+    refine_ms, refine_n = nat.timing_read("ivf_filter_refine")
+    rescans = nat.filter_rescans(local.device.index, reset=True)
     if world > 1:
         t = torch.tensor([ms], device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -317,10 +343,16 @@ def run_ours(args, cfg):
         hbm_peak, bf16_peak, peak_kind = measured_peaks()
         scan_avg_ms = scan_ms / max(scan_n, 1)
         scan_s = scan_avg_ms * 1e-3
-        # 3xTF32: three tensor-core products (hi*hi, hi*lo, lo*hi) of 2d flops per pair
-        tflops = 6.0 * d * pairs / scan_s / 1e12 if scan_n else None
+        # 3xTF32: three tensor-core products (hi*hi, hi*lo, lo*hi) of 2d flops
+        # per pair against the TF32 rate; the filter pass: one fp16 product
+        # against the 16-bit rate (fp16 and bf16 run at the same dense rate;
+        # the measured bf16 GEMM is the denominator)
+        flops_pair = 2.0 * d if filtered else 6.0 * d
+        tc_peak = bf16_peak if filtered else tf32_peak
+        tflops = flops_pair * pairs / scan_s / 1e12 if scan_n else None
         gbs = alg_bytes / scan_s / 1e9 if scan_n else None
         value = nq * args.steps / (ms * 1e-3)
+        tkey = args.config + ("/filter" if filtered else "")
         line = {
             "metric": "IVFFlat queries/sec (list-scan HBM GB/s vs peak in roofline)",
             "value": round(value, 1),
@@ -345,19 +377,26 @@ def run_ours(args, cfg):
             },
             "roofline": {
                 "bound": "tensor",
-                "kernel": "tq_scan_kernel (IVF list-major 3xTF32 tcgen05 scan + fused top-k), "
-                          "all-probes pass over lists probed by more than 16 queries",
+                "kernel": ("tq_scan_kernel<FLT> (IVF list-major fp16 tcgen05 filter over "
+                           "scaled residuals + fused top-2k of upper bounds), lists probed by "
+                           "more than 16 queries"
+                           if filtered else
+                           "tq_scan_kernel (IVF list-major 3xTF32 tcgen05 scan + fused top-k), "
+                           "all-probes pass over lists probed by more than 16 queries"),
                 "achieved": round(tflops, 2) if tflops else None,
-                "peak": round(tf32_peak, 1),
+                "peak": round(tc_peak, 1),
                 "unit": "TFLOP/s",
-                "frac": round(tflops / tf32_peak, 4) if tflops else None,
-                "peak_kind": "cuBLAS TF32 GEMM 8192^3 measured in this run (best of 10); "
-                             f"{peak_kind} bf16 {bf16_peak} TFLOP/s for context",
-                "algorithmic_flops_per_launch": 6 * d * pairs,
+                "frac": round(tflops / tc_peak, 4) if tflops else None,
+                "peak_kind": (f"{peak_kind} bf16 (cuBLAS bf16 GEMM, burst; fp16 runs at the "
+                              f"same dense rate); TF32 measured in "
+                              f"this run {round(tf32_peak, 1)} TFLOP/s" if filtered else
+                              "cuBLAS TF32 GEMM 8192^3 measured in this run (best of 10); "
+                              f"{peak_kind} bf16 {bf16_peak} TFLOP/s for context"),
+                "algorithmic_flops_per_launch": int(flops_pair * pairs),
                 "pairs_per_launch": pairs,
                 "avg_launch_ms": round(scan_avg_ms, 4),
-                "traffic": TRAFFIC[args.config]["bytes"] if args.config in TRAFFIC and world == 1 else None,
-                "traffic_source": TRAFFIC[args.config]["source"] if args.config in TRAFFIC else None,
+                "traffic": (TRAFFIC[tkey]["bytes"] if tkey in TRAFFIC and world == 1 else None),
+                "traffic_source": TRAFFIC[tkey]["source"] if tkey in TRAFFIC else None,
                 "hbm": {
                     "algorithmic_bytes_per_launch": alg_bytes,
                     "achieved": round(gbs, 1) if gbs else None,
@@ -367,6 +406,12 @@ def run_ours(args, cfg):
                     "peak_kind": f"{peak_kind} hbm_gbs",
                     "logical_scan_GBps": round(logical_bytes / scan_s / 1e9, 1) if scan_n else None,
                 },
+                # the filter search's exact refinement (one warp per query)
+                "refine": ({
+                    "kernel": "filter_refine_kernel (exact fp32 distances of the kept rows)",
+                    "avg_launch_ms": round(refine_ms / refine_n, 4) if refine_n else None,
+                    "lists_rescanned": rescans,
+                } if filtered else None),
                 # the few-query groups' pass (one 4-warp block per item): bound by
                 # reading those lists' rows (vector + norm) once
                 "small_groups": {

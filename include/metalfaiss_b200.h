@@ -222,6 +222,70 @@ MF_API int mf_ivf_search_bounded(int device, void* stream, const float* xq, int6
                                  const float* bound, float* distances, int64_t* labels,
                                  void* workspace, size_t workspace_bytes);
 
+/* ------------------------------------------------- IVFFlat filter search (L2)
+ *
+ * The same search as mf_ivf_search for L2, with the list scan split in two:
+ * an fp16 tensor-core pass over residuals against the list centroids keeps,
+ * per (query, probed list), up to 2k (16..32) smallest upper bounds on the
+ * rows' exact distances (bounds from a rigorous per-pair error bound of the
+ * fp16 products), then an exact fp32 refinement computes the distances of
+ * every row those bounds cannot exclude (rescanning a list exactly where its
+ * kept rows cannot prove that) and selects the top-k. The results are the
+ * exact top-k over the probed lists, as mf_ivf_search returns them. Same
+ * reference interface as mf_ivf_search
+ * (python/metalfaiss/index/ivf_flat_index.py:95-151).
+ *
+ * The bank: list_f16 (ntotal, d) fp16 = round-to-nearest(s_l (list_vecs row -
+ * its list's centroid)), list_rnorms (ntotal) = the squared norms of those
+ * fp32 residuals, list_stats (nlist, 4) = per list an upper bound on the
+ * residual norms, the largest list_norms entry, the power-of-two scale s_l
+ * and 0; mf_ivf_filter_bank writes all three (after every add, from the CSR
+ * bank and the centroids). */
+
+/* 1 when the filter search takes this shape (d a multiple of 8 in [64, 128],
+ * 1 <= k <= 16, ntotal >= 256, the tensor-core engine enabled), else 0. */
+MF_API int mf_ivf_filter_eligible(int d, int k, int64_t ntotal);
+
+MF_API int mf_ivf_filter_bank(int device, void* stream, int nlist, int d,
+                              const int64_t* list_offsets, const float* list_vecs,
+                              const float* list_norms, const float* centroids, int64_t ntotal,
+                              void* list_f16, float* list_rnorms, float* list_stats);
+
+MF_API int mf_ivf_search_filtered_workspace_size(int64_t nq, int nlist, int nprobe, int d, int k,
+                                                 size_t* bytes);
+
+MF_API int mf_ivf_search_filtered(int device, void* stream, const float* xq, int64_t nq,
+                                  const float* centroids, const float* centroid_norms, int nlist,
+                                  int nprobe, const int64_t* list_offsets, const float* list_vecs,
+                                  const float* list_norms, const float* list_lo,
+                                  const int64_t* list_ids, int64_t ntotal,
+                                  const int32_t* list_order, const void* list_f16,
+                                  const float* list_rnorms, const float* list_stats, int d, int k,
+                                  float* distances, int64_t* labels, void* workspace,
+                                  size_t workspace_bytes);
+
+/* mf_ivf_search_bounded for L2 through the filter search (the lists of one
+ * rank of a sharded index, caller-supplied probes and the bound from the
+ * ranks' mf_ivf_probe_bound minimum): this rank's exact top-k among rows
+ * within bound[q], padded (+inf, -1). */
+MF_API int mf_ivf_search_bounded_filtered_workspace_size(int64_t nq, int nlist, int nprobe, int d,
+                                                         int k, size_t* bytes);
+
+MF_API int mf_ivf_search_bounded_filtered(int device, void* stream, const float* xq, int64_t nq,
+                                          const int64_t* probes, int nprobe, int nlist,
+                                          const int64_t* list_offsets, const float* list_vecs,
+                                          const float* list_norms, const int64_t* list_ids,
+                                          int64_t ntotal, const int32_t* list_order,
+                                          const void* list_f16, const float* list_rnorms,
+                                          const float* list_stats, const float* centroids, int d,
+                                          int k, const float* bound, float* distances,
+                                          int64_t* labels, void* workspace,
+                                          size_t workspace_bytes);
+
+/* Lists the filter search's refinement rescanned exactly on `device` since the
+ * last reset (a statistic; reset != 0 clears it after reading). */
+MF_API int mf_ivf_filter_rescans(int device, int64_t* count, int reset);
+
 /* ----------------------------------------------------------- merge, k-means */
 
 /* Merge `parts` partial top-k lists per query: in (nq, parts, k_in) ascending,

@@ -42,6 +42,13 @@ _SIGNATURES = {
     "mf_ivf_search_preassigned": ([I32, P, P, I64, P, I32, I32, P, P, P, P, P, I64, P, I32, I32, I32, P, P, P, SZ], I32),
     "mf_ivf_probe_bound": ([I32, P, P, I64, P, I32, I32, P, P, P, P, P, I64, P, I32, I32, I32, P, P, SZ], I32),
     "mf_ivf_search_bounded": ([I32, P, P, I64, P, I32, I32, P, P, P, P, P, I64, P, I32, I32, I32, P, P, P, P, SZ], I32),
+    "mf_ivf_filter_eligible": ([I32, I32, I64], I32),
+    "mf_ivf_filter_bank": ([I32, P, I32, I32, P, P, P, P, I64, P, P, P], I32),
+    "mf_ivf_search_filtered_workspace_size": ([I64, I32, I32, I32, I32, PSZ], I32),
+    "mf_ivf_search_filtered": ([I32, P, P, I64, P, P, I32, I32, P, P, P, P, P, I64, P, P, P, P, I32, I32, P, P, P, SZ], I32),
+    "mf_ivf_search_bounded_filtered_workspace_size": ([I64, I32, I32, I32, I32, PSZ], I32),
+    "mf_ivf_search_bounded_filtered": ([I32, P, P, I64, P, I32, I32, P, P, P, P, I64, P, P, P, P, P, I32, I32, P, P, P, P, SZ], I32),
+    "mf_ivf_filter_rescans": ([I32, PI64, I32], I32),
     "mf_topk_merge": ([I32, P, P, P, I64, I32, I32, I32, P, P], I32),
     "mf_kmeans_assign_workspace_size": ([I64, I32, I32, PSZ], I32),
     "mf_kmeans_assign": ([I32, P, P, I64, P, P, I32, I32, P, P, P, SZ], I32),
@@ -165,6 +172,14 @@ def device_error(device_index: int) -> int:
     """Reads and clears the device-side error word (0 = none)."""
     c = ctypes.c_int(0)
     call("mf_device_error", int(device_index), ctypes.byref(c))
+    return int(c.value)
+
+
+def filter_rescans(device_index: int, reset: bool = False) -> int:
+    """Lists the IVF filter search rescanned exactly on this device since the
+    last reset (mf_ivf_filter_rescans)."""
+    c = ctypes.c_int64(0)
+    call("mf_ivf_filter_rescans", int(device_index), ctypes.byref(c), 1 if reset else 0)
     return int(c.value)
 
 

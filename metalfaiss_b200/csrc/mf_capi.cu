@@ -5,6 +5,7 @@
 #include <mutex>
 #include <string>
 
+#include "mf_filter.cuh"
 #include "mf_ivf.cuh"
 #include "mf_scan.cuh"
 
@@ -115,13 +116,15 @@ struct IvfWs {
   float* g_hi;       // gathered query rows per (query, probe) pair (tensor cores)
   float* g_lo;
   float* cent_lo;    // tf32 residuals of the centroids (coarse step, tensor cores)
+  FilterPairs fp;    // filter search: per (query, probe) pair
 };
 
-// mode: 0 = top-k search, 1 = preassigned top-k, 2 = range
+// mode: 0 = top-k search, 1 = preassigned top-k, 2 = range, 3 = filter search,
+// 4 = preassigned filter search
 IvfWs carve_ivf(Carver& c, int64_t nq, int nlist, int P, int d, int k, int mode, int device) {
   IvfWs w{};
   w.qn = c.take<float>(nq);
-  if (mode != 1) {
+  if (mode != 1 && mode != 4) {
     w.coarse_d = c.take<float>((size_t)nq * P);
     w.coarse_l = c.take<int64_t>((size_t)nq * P);
     FlatPlan fp = plan_flat(nq, nlist, d, P, device);
@@ -133,6 +136,17 @@ IvfWs carve_ivf(Carver& c, int64_t nq, int nlist, int P, int d, int k, int mode,
   if (mode == 2) {
     w.pair_counts = c.take<int64_t>((size_t)nq * P);
     w.pair_offsets64 = c.take<int64_t>((size_t)nq * P + 1);
+  } else if (mode >= 3) {
+    // the filter pass keeps filter_slots() slots per pair (>= k)
+    w.pd = c.take<float>((size_t)nq * P * filter_slots());
+    w.pl = c.take<int64_t>((size_t)nq * P * filter_slots());
+    w.bound = c.take<float>((size_t)nq);
+    w.fp.qn = c.take<float>((size_t)nq * P);
+    w.fp.thr = c.take<float>((size_t)nq * P);
+    w.fp.e = c.take<float>((size_t)nq * P);
+    w.fp.sq = c.take<float>((size_t)nq * P);
+    w.fp.sc = c.take<float>((size_t)nq * P);
+    w.fp.cnt = c.take<int>((size_t)nq * P);
   } else {
     w.pd = c.take<float>((size_t)nq * P * k);
     w.pl = c.take<int64_t>((size_t)nq * P * k);
@@ -260,6 +274,127 @@ int ivf_scan_topk(int device, cudaStream_t stream, const IvfWs& w, const float* 
   }
   if (bound_out) return MF_OK;
   MF_TRY(launch_merge(w.pd, w.pl, nq, P, k, k, D, I, stream));
+  return MF_OK;
+}
+
+// The filter search (L2): the bound pass (unless bound_in is given), the
+// per-pair scales and error bounds, the fp16 filter pass over every probed list in
+// groups of up to 128 queries, and the exact refinement into (D, I). The
+// bound pass runs on the SIMT engines with the margin that also covers the
+// refinement's rounding (filter_eligible requires the tensor-core shape for it).
+int ivf_filter_topk(int device, cudaStream_t stream, const IvfWs& w, const float* xq, int64_t nq,
+                    const int64_t* probes, int P, int nlist, const int64_t* list_offsets,
+                    const float* list_vecs, const float* list_norms, const float* list_lo,
+                    const int64_t* list_ids, int64_t ntotal, const int32_t* list_order,
+                    const void* list_f16, const float* list_rnorms, const float* list_stats,
+                    const float* centroids, int d, int k, float* D, int64_t* I,
+                    const float* bound_in) {
+  const int S = filter_slots_for(k);
+  if (bound_in) {
+    MF_TRY(launch_norms(xq, nq, d, w.qn, stream));
+  } else {
+    MF_TRY(ivf_scan_topk(device, stream, w, xq, nq, probes, P, nlist, list_offsets, list_vecs,
+                         list_norms, list_lo, list_ids, ntotal, list_order, d, MF_METRIC_L2, k,
+                         nullptr, nullptr, w.bound));
+  }
+  const float* bound = bound_in ? bound_in : w.bound;
+  MF_TRY(launch_filter_pairs(xq, w.qn, nq, P, d, probes, list_offsets, nlist, centroids,
+                             list_stats, bound, w.fp, stream));
+  // (pairs that are not scanned have no kept slots: launch_filter_pairs).
+  // A list probed by at most kSmallGroup queries goes to the exact few-query
+  // scan instead (a 128-query tile would be mostly padding; those rows' bytes
+  // bound the work): it keeps each pair's exact top-k, as slots with e >= 0
+  // to spare, never all S of them.
+  constexpr int kSmallGroup = 16;
+  const int small_max = few_eligible(MF_METRIC_L2, d, k) ? kSmallGroup : 0;
+  MF_TRY(run_ivf_groups_ex(w.g, probes, nq, P, nlist, list_offsets, list_order, nullptr, nullptr,
+                           0, nullptr, tc_group(), stream, 0, P, small_max));
+  ScanArgs a{};
+  a.xq = xq;
+  a.qnorms = w.qn;
+  a.xb = reinterpret_cast<const float*>(list_f16);  // fp16 rows, read only by TMA
+  a.xnorms = list_rnorms;
+  a.ids = nullptr;  // slots carry row positions for the refinement
+  a.d = d;
+  a.k = S;
+  a.nq = nq;
+  a.P = P;
+  a.flat = 0;
+  a.items = w.g.items;
+  a.item_total = w.g.item_total;
+  a.list_offsets = list_offsets;
+  a.pair_offsets = w.g.pair_offsets;
+  a.pairs = w.g.pairs;
+  a.counter = w.g.counter;
+  a.out_d = w.pd;
+  a.out_l = w.pl;
+  a.pair_qn = w.fp.qn;
+  a.pair_thr = w.fp.thr;
+  a.pair_sq = w.fp.sq;
+  a.pair_sc = w.fp.sc;
+  a.pair_cnt = w.fp.cnt;
+  a.centroids = centroids;
+  MF_TRY(launch_tc_filter(a, ntotal, nq * P, device, stream));
+  if (small_max > 0) {
+    ScanArgs fa{};
+    fa.xq = xq;
+    fa.qnorms = w.qn;
+    fa.xb = list_vecs;
+    fa.xnorms = list_norms;
+    fa.ids = nullptr;
+    fa.d = d;
+    fa.k = k;
+    fa.nq = nq;
+    fa.P = P;
+    fa.flat = 0;
+    fa.items = w.g.items2;
+    fa.item_total = w.g.item_total2;
+    fa.group = tc_group();
+    fa.list_offsets = list_offsets;
+    fa.pair_offsets = w.g.pair_offsets;
+    fa.pairs = w.g.pairs;
+    fa.counter = w.g.counter;
+    fa.out_d = w.pd;
+    fa.out_l = w.pl;
+    fa.bound = bound;
+    fa.pair_cnt = w.fp.cnt;
+    fa.out_stride = S;
+    MF_TRY(launch_few_scan(fa, MF_METRIC_L2, nq * P, device, stream));
+  }
+  RefineArgs f{};
+  f.xq = xq;
+  f.qnorms = w.qn;
+  f.nq = nq;
+  f.d = d;
+  f.P = P;
+  f.k = k;
+  f.slots = S;
+  f.pd = w.pd;
+  f.pl = w.pl;
+  f.cnt = w.fp.cnt;
+  f.pair_e = w.fp.e;
+  f.bound = bound;
+  f.probes = probes;
+  f.offsets = list_offsets;
+  f.xb = list_vecs;
+  f.xnorms = list_norms;
+  f.ids = list_ids;
+  f.D = D;
+  f.I = I;
+  return launch_filter_refine(f, stream);
+}
+
+bool filter_eligible(int d, int k, int64_t ntotal) {
+  return tc_filter_eligible(d) && k >= 1 && 2 * k <= filter_slots() &&
+         tc_eligible(MF_METRIC_L2, d, k, ntotal) && tc_raw_queries(d, k);
+}
+
+int check_filter_bank(const void* list_f16, const float* list_rnorms, const float* list_stats,
+                      const float* centroids) {
+  MF_TRY(check_device_ptr(list_f16, "list_f16"));
+  MF_TRY(check_device_ptr(list_rnorms, "list_rnorms"));
+  MF_TRY(check_device_ptr(list_stats, "list_stats"));
+  MF_TRY(check_device_ptr(centroids, "centroids"));
   return MF_OK;
 }
 
@@ -509,6 +644,145 @@ int mf_ivf_search_bounded(int device, void* stream, const float* xq, int64_t nq,
                                list_vecs, list_norms, list_lo, list_ids, ntotal, list_order, d,
                                metric, k, distances, labels, nullptr, bound, workspace,
                                workspace_bytes);
+}
+
+int mf_ivf_filter_eligible(int d, int k, int64_t ntotal) {
+  clear_error();
+  return filter_eligible(d, k, ntotal) ? 1 : 0;
+}
+
+int mf_ivf_filter_bank(int device, void* stream, int nlist, int d, const int64_t* list_offsets,
+                       const float* list_vecs, const float* list_norms, const float* centroids,
+                       int64_t ntotal, void* list_f16, float* list_rnorms, float* list_stats) {
+  MF_ENTER(device);
+  MF_CHECK(nlist >= 1 && d > 0 && d % 8 == 0, MF_ERR_INVALID_ARGS,
+           "filter bank: nlist=%d, d=%d (a multiple of 8)", nlist, d);
+  MF_TRY(check_device_ptr(list_offsets, "list_offsets"));
+  MF_TRY(check_device_ptr(centroids, "centroids"));
+  MF_TRY(check_device_ptr(list_stats, "list_stats"));
+  if (ntotal > 0) {
+    MF_TRY(check_device_ptr(list_vecs, "list_vecs"));
+    MF_TRY(check_device_ptr(list_norms, "list_norms"));
+    MF_TRY(check_device_ptr(list_f16, "list_f16"));
+    MF_TRY(check_device_ptr(list_rnorms, "list_rnorms"));
+  }
+  return launch_filter_bank(nlist, d, list_offsets, list_vecs, list_norms, centroids, list_f16,
+                            list_rnorms, list_stats, (cudaStream_t)stream);
+}
+
+int mf_ivf_search_filtered_workspace_size(int64_t nq, int nlist, int nprobe, int d, int k,
+                                          size_t* bytes) {
+  clear_error();
+  MF_CHECK(bytes != nullptr, MF_ERR_INVALID_ARGS, "bytes is NULL");
+  MF_TRY(check_common(d, MF_METRIC_L2, k, true));
+  MF_CHECK(nlist >= 1 && nprobe >= 1, MF_ERR_INVALID_ARGS, "nlist=%d nprobe=%d", nlist, nprobe);
+  int dev = 0;
+  cudaGetDevice(&dev);
+  Carver c(nullptr, 0);
+  carve_ivf(c, nq, nlist, effective_nprobe(nprobe, nlist), d, k, 3, dev);
+  *bytes = c.used;
+  return MF_OK;
+}
+
+int mf_ivf_search_filtered(int device, void* stream, const float* xq, int64_t nq,
+                           const float* centroids, const float* centroid_norms, int nlist,
+                           int nprobe, const int64_t* list_offsets, const float* list_vecs,
+                           const float* list_norms, const float* list_lo,
+                           const int64_t* list_ids, int64_t ntotal, const int32_t* list_order,
+                           const void* list_f16, const float* list_rnorms,
+                           const float* list_stats, int d, int k, float* distances,
+                           int64_t* labels, void* workspace, size_t workspace_bytes) {
+  MF_ENTER(device);
+  MF_TRY(check_common(d, MF_METRIC_L2, k, true));
+  MF_CHECK(nlist >= 1, MF_ERR_INVALID_ARGS, "nlist=%d", nlist);
+  MF_CHECK(nprobe >= 1, MF_ERR_INVALID_ARGS, "nprobe must be positive (got %d)", nprobe);
+  const int P = effective_nprobe(nprobe, nlist);
+  MF_CHECK(P <= kMaxK, MF_ERR_INVALID_ARGS, "nprobe=%d exceeds %d", P, kMaxK);
+  MF_CHECK(nq >= 0 && nq * P < (1ll << 31), MF_ERR_INVALID_ARGS, "nq*nprobe too large");
+  MF_CHECK(filter_eligible(d, k, ntotal), MF_ERR_INVALID_ARGS,
+           "the filter search does not take d=%d, k=%d, ntotal=%lld (mf_ivf_filter_eligible)", d,
+           k, (long long)ntotal);
+  if (nq == 0) return MF_OK;
+  MF_TRY(check_device_ptr(xq, "xq"));
+  MF_TRY(check_device_ptr(centroid_norms, "centroid_norms"));
+  MF_TRY(check_ivf_lists(list_offsets, list_vecs, list_norms, list_ids, list_order,
+                         MF_METRIC_L2));
+  MF_TRY(check_filter_bank(list_f16, list_rnorms, list_stats, centroids));
+  MF_TRY(check_device_ptr(distances, "distances"));
+  MF_TRY(check_device_ptr(labels, "labels"));
+  MF_TRY(check_device_ptr(workspace, "workspace"));
+  Carver c(workspace, workspace_bytes);
+  IvfWs w = carve_ivf(c, nq, nlist, P, d, k, 3, device);
+  MF_CHECK(c.fits(), MF_ERR_INVALID_ARGS, "IVF filter search workspace too small: %zu < %zu bytes",
+           workspace_bytes, c.used);
+  cudaStream_t s = (cudaStream_t)stream;
+  const float* cent_lo = nullptr;
+  if (tc_eligible(MF_METRIC_L2, d, P, nlist)) {
+    MF_TRY(launch_tf32_residual(centroids, nlist, d, w.cent_lo, s));
+    cent_lo = w.cent_lo;
+  }
+  MF_TRY(run_flat_topk(device, s, xq, nq, centroids, centroid_norms, cent_lo, nlist, d,
+                       MF_METRIC_L2, P, nullptr, w.coarse_d, w.coarse_l, w.flat_ws, w.flat_bytes));
+  return ivf_filter_topk(device, s, w, xq, nq, w.coarse_l, P, nlist, list_offsets, list_vecs,
+                         list_norms, list_lo, list_ids, ntotal, list_order, list_f16, list_rnorms,
+                         list_stats, centroids, d, k, distances, labels, nullptr);
+}
+
+int mf_ivf_search_bounded_filtered_workspace_size(int64_t nq, int nlist, int nprobe, int d,
+                                                  int k, size_t* bytes) {
+  clear_error();
+  MF_CHECK(bytes != nullptr, MF_ERR_INVALID_ARGS, "bytes is NULL");
+  MF_TRY(check_common(d, MF_METRIC_L2, k, true));
+  MF_CHECK(nlist >= 1 && nprobe >= 1, MF_ERR_INVALID_ARGS, "nlist=%d nprobe=%d", nlist, nprobe);
+  Carver c(nullptr, 0);
+  carve_ivf(c, nq, nlist, nprobe, d, k, 4, 0);
+  *bytes = c.used;
+  return MF_OK;
+}
+
+int mf_ivf_search_bounded_filtered(int device, void* stream, const float* xq, int64_t nq,
+                                   const int64_t* probes, int nprobe, int nlist,
+                                   const int64_t* list_offsets, const float* list_vecs,
+                                   const float* list_norms, const int64_t* list_ids,
+                                   int64_t ntotal, const int32_t* list_order, const void* list_f16,
+                                   const float* list_rnorms, const float* list_stats,
+                                   const float* centroids, int d, int k, const float* bound,
+                                   float* distances, int64_t* labels, void* workspace,
+                                   size_t workspace_bytes) {
+  MF_ENTER(device);
+  MF_TRY(check_common(d, MF_METRIC_L2, k, true));
+  MF_CHECK(nlist >= 1 && nprobe >= 1, MF_ERR_INVALID_ARGS, "nlist=%d nprobe=%d", nlist, nprobe);
+  MF_CHECK(nq >= 0 && nq * nprobe < (1ll << 31), MF_ERR_INVALID_ARGS, "nq*nprobe too large");
+  MF_CHECK(filter_eligible(d, k, ntotal), MF_ERR_INVALID_ARGS,
+           "the filter search does not take d=%d, k=%d, ntotal=%lld (mf_ivf_filter_eligible)", d,
+           k, (long long)ntotal);
+  if (nq == 0) return MF_OK;
+  MF_TRY(check_device_ptr(xq, "xq"));
+  MF_TRY(check_device_ptr(probes, "probes"));
+  MF_TRY(check_device_ptr(bound, "bound"));
+  MF_TRY(check_ivf_lists(list_offsets, list_vecs, list_norms, list_ids, list_order,
+                         MF_METRIC_L2));
+  MF_TRY(check_filter_bank(list_f16, list_rnorms, list_stats, centroids));
+  MF_TRY(check_device_ptr(distances, "distances"));
+  MF_TRY(check_device_ptr(labels, "labels"));
+  MF_TRY(check_device_ptr(workspace, "workspace"));
+  Carver c(workspace, workspace_bytes);
+  IvfWs w = carve_ivf(c, nq, nlist, nprobe, d, k, 4, device);
+  MF_CHECK(c.fits(), MF_ERR_INVALID_ARGS, "workspace too small: %zu < %zu bytes", workspace_bytes,
+           c.used);
+  return ivf_filter_topk(device, (cudaStream_t)stream, w, xq, nq, probes, nprobe, nlist,
+                         list_offsets, list_vecs, list_norms, nullptr, list_ids, ntotal,
+                         list_order, list_f16, list_rnorms, list_stats, centroids, d, k, distances,
+                         labels, bound);
+}
+
+int mf_ivf_filter_rescans(int device, int64_t* count, int reset) {
+  MF_ENTER(device);
+  MF_CHECK(count != nullptr, MF_ERR_INVALID_ARGS, "count is NULL");
+  unsigned long long v = 0;
+  MF_TRY(read_filter_rescans(&v, reset != 0));
+  *count = (int64_t)v;
+  return MF_OK;
 }
 
 int mf_topk_merge(int device, void* stream, const float* part_distances,

@@ -33,38 +33,6 @@ struct FewSmem {
   }
 };
 
-// p[0..15] per lane -> the sum over the 32 lanes of p[i] in lanes 2i, 2i+1.
-__device__ __forceinline__ float transpose_reduce16(float (&p)[16], int lane) {
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const bool hi = lane & 16;
-    const float send = hi ? p[i] : p[i + 8];
-    const float keep = hi ? p[i + 8] : p[i];
-    p[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
-  }
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const bool hi = lane & 8;
-    const float send = hi ? p[i] : p[i + 4];
-    const float keep = hi ? p[i + 4] : p[i];
-    p[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
-  }
-#pragma unroll
-  for (int i = 0; i < 2; ++i) {
-    const bool hi = lane & 4;
-    const float send = hi ? p[i] : p[i + 2];
-    const float keep = hi ? p[i + 2] : p[i];
-    p[i] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
-  }
-  {
-    const bool hi = lane & 2;
-    const float send = hi ? p[0] : p[1];
-    const float keep = hi ? p[1] : p[0];
-    p[0] = keep + __shfl_xor_sync(0xffffffffu, send, 2);
-  }
-  return p[0] + __shfl_xor_sync(0xffffffffu, p[0], 1);
-}
-
 template <int METRIC>
 __global__ void __launch_bounds__(kFewWarps * 32) few_scan_kernel(const ScanArgs a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -143,7 +111,7 @@ __global__ void __launch_bounds__(kFewWarps * 32) few_scan_kernel(const ScanArgs
           t = fmaf(xv[i].z, q4.z, t);
           p[i] = fmaf(xv[i].w, q4.w, t);
         }
-        const float dot = transpose_reduce16(p, lane);
+        const float dot = warp_transpose_reduce16(p, lane);
         const unsigned long long tj = __shfl_sync(0xffffffffu, thr, j);
         const float dist = METRIC == MF_METRIC_L2 ? l2_from_dot(s_qn[j], xn, dot) : -dot;
         const unsigned long long key = rv ? make_key(dist, (unsigned int)my_row) : kEmptyKey;
@@ -184,7 +152,16 @@ __global__ void __launch_bounds__(kFewWarps * 32) few_scan_kernel(const ScanArgs
         merge_into_list<kFewK>(list, other, k, k, lane);
       }
       const long long sj = s_slot[j];
-      if (lane < k) {
+      if (a.pair_cnt) {
+        // compact: the kept keys (a sorted prefix), row positions, and their count
+        const unsigned long long key = lane < k ? list[lane] : kEmptyKey;
+        const unsigned int m = __ballot_sync(0xffffffffu, key != kEmptyKey);
+        if (lane == 0) a.pair_cnt[sj] = __popc(m);
+        if (key != kEmptyKey) {
+          a.out_d[sj * a.out_stride + lane] = key_dist(key);
+          a.out_l[sj * a.out_stride + lane] = (long long)key_index(key);
+        }
+      } else if (lane < k) {
         const unsigned long long key = list[lane];
         float dv;
         long long lv;

@@ -60,6 +60,23 @@ struct ScanArgs {
   const float* bound;
   // IVF items scan at most max_rows rows of their list (0 = the whole list).
   int64_t max_rows;
+  // IVF filter scan (fp16 tensor cores, mf_filter.cu), per (query, probe)
+  // pair s = q*P + p: pair_qn[s] stands in for the query norm (the query's
+  // squared distance to the list's centroid plus the pair's error bound) and
+  // pair_thr[s] for the bound; the A operand is the query minus its list's
+  // centroid (centroids, rows of d floats) and xb holds the rows' fp16
+  // residuals against that centroid.
+  const float* pair_qn;
+  const float* pair_thr;
+  const float* centroids;
+  // the filter scan's operands are scaled by powers of two: the query by
+  // pair_sq[s], the rows by their list's scale; pair_sc[s] = 1 / (both).
+  // Each pair's kept slots are a sorted prefix of its k; pair_cnt[s] = their count.
+  const float* pair_sq;
+  const float* pair_sc;
+  int* pair_cnt;
+  // few-query scan with pair_cnt set: compact outputs at this slot stride
+  int out_stride;
   // range search
   float radius;
   int64_t* counts;        // count pass: (nq*P)
@@ -86,6 +103,15 @@ int tc_group();
 int launch_tc_scan(const ScanArgs& a, int metric, const float* a_lo, int64_t a_rows,
                    const float* b_lo, int64_t b_rows, int64_t total_items, int device,
                    cudaStream_t stream);
+// The fp16 filter scan: IVF items of tc_group() queries, L2, a.k partial slots
+// per pair (the smallest upper-bound distances of the list, with row
+// positions as labels; a.k <= filter_slots()), A = fp16(scaled query -
+// centroid) in tensor memory, B = a.xb as fp16 rows (b_rows of them),
+// a.xnorms the rows' squared residual norms.
+bool tc_filter_eligible(int d);
+int filter_slots();
+int launch_tc_filter(const ScanArgs& a, int64_t b_rows, int64_t total_items, int device,
+                     cudaStream_t stream);
 int launch_tf32_residual(const float* x, int64_t n, int d, float* lo, cudaStream_t stream);
 int launch_gather_queries(const float* xq, int d, const int* pairs, const int* n_pairs,
                           int64_t max_pairs, int P, float* g_hi, float* g_lo, cudaStream_t stream);

@@ -22,6 +22,7 @@
 // through 512 / BN TMEM buffers, so the MMAs run up to that many tiles ahead of
 // the epilogue. Every wait is bounded (mf_sm100.cuh).
 #include <cudaTypedefs.h>
+#include <cuda_fp16.h>
 
 #include <cstring>
 #include <mutex>
@@ -82,24 +83,26 @@ constexpr int kTqThreadsAtm = 320;
 constexpr int kTqMaxDAtm = 128;
 
 struct TqLayout {
-  int SA, KB, BN;
+  int SA, KB, BN;  // KB: K-blocks of 128 bytes (32 fp32 or, with bf, 64 fp16)
   int atm;   // query tile in tensor memory (columns [0, 2*KB*32): hi then lo)
+  int bf;    // 16-bit operands (filter scan): A in columns [0, KB*32), no residuals
   int nacc;  // accumulator buffers in tensor memory
   int acc0;  // first accumulator column
   size_t stage, a_hi, a_lo, b_hi, b_lo;  // offsets within a stage
   size_t lists, scratch, xn, bars, total;
 };
 
-TqLayout tq_layout(int d, int kcap, int BN, int SA, bool atm) {
+TqLayout tq_layout(int d, int kcap, int BN, int SA, bool atm, bool bf = false) {
   TqLayout s;
   s.SA = SA;
-  s.KB = (d + 31) / 32;
+  s.KB = bf ? (d + 63) / 64 : (d + 31) / 32;
   s.BN = BN;
   s.atm = atm ? 1 : 0;
+  s.bf = bf ? 1 : 0;
   if (atm) {
     s.a_hi = s.a_lo = 0;  // unused: the query tile lives in tensor memory
     s.b_hi = 0;
-    s.acc0 = 2 * s.KB * 32;
+    s.acc0 = (bf ? 1 : 2) * s.KB * 32;
   } else {
     s.a_hi = 0;
     s.a_lo = kTqM * 128;
@@ -109,7 +112,7 @@ TqLayout tq_layout(int d, int kcap, int BN, int SA, bool atm) {
   s.nacc = (kTqTmemCols - s.acc0) / BN;
   if (s.nacc > kTqMaxAcc) s.nacc = kTqMaxAcc;
   s.b_lo = s.b_hi + size_t(BN) * 128;
-  s.stage = s.b_lo + size_t(BN) * 128;
+  s.stage = bf ? s.b_lo : s.b_lo + size_t(BN) * 128;
   size_t o = size_t(SA) * s.stage;
   s.lists = o;
   o += size_t(kTqM) * kcap * 8;
@@ -140,6 +143,7 @@ struct ItemDesc {
   int a_row0;        // first A row (queries) in the A tensor map
   int nq_item;       // valid queries (A rows) of this item
   int part;          // flat: the partial slot of this item's query tile
+  int list;          // IVF: the item's list (-1 for flat)
 };
 
 // A queue slot: the item index (-1 ends the roles' loops) and its geometry.
@@ -160,6 +164,7 @@ __device__ __forceinline__ ItemDesc item_desc(const ScanArgs& a, int item) {
     const long long re = it.rb + a.rows_per_split;
     it.re = re < a.nb ? re : a.nb;
     it.part = s;
+    it.list = -1;
   } else {
     it.part = 0;
     // a list's q queries are cut into ceil(q / 128) groups of nearly equal
@@ -172,11 +177,19 @@ __device__ __forceinline__ ItemDesc item_desc(const ScanArgs& a, int item) {
     const int pe = p0 + (int)(((long long)(g.y + 1) * q) / ng);
     it.a_row0 = pb;
     it.nq_item = pe - pb;
+    it.list = g.x;
     it.rb = a.list_offsets[g.x];
     const long long re = a.list_offsets[g.x + 1];
     it.re = (a.max_rows > 0 && re - it.rb > a.max_rows) ? it.rb + a.max_rows : re;
   }
   return it;
+}
+
+// Two fp32 rounded to fp16 (to nearest, ties to even), packed as one 32-bit
+// tensor-memory column: the first in the low half.
+__device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
+  const __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&h);
 }
 
 // r[j] for a run-time j without indexing the register array (which would put
@@ -221,13 +234,15 @@ __device__ __forceinline__ unsigned long long fma2(unsigned long long a, unsigne
 // <= thr_d (the row's current k-th distance, its bound, or +inf while open)
 // and j < nvalid. For L2, t = (qn + xn) - 2 dot is formed as l2_from_dot forms
 // it before its clamp at 0 (doubling is exact, so the FMA rounds once, like the
-// subtraction); thr_d >= 0, so t <= thr_d iff the clamped distance is. The
+// subtraction; m2 is -2, or -2 times the power-of-two scale of the filter
+// scan's accumulators, so m2 * acc is still exactly -2 dot); thr_d >= 0, so
+// t <= thr_d iff the clamped distance is. The
 // sign bit of thr_d - t (+0 when equal) is shifted into a reject mask. Columns
 // go two at a time through the packed fp32 pipe, in four independent shift
 // chains of 8 columns joined at the end.
 template <int METRIC>
 __device__ __forceinline__ unsigned int tq_accept(const uint32_t (&r)[32], const float* xs,
-                                                  float qn, float thr_d, int nvalid) {
+                                                  float qn, float m2s, float thr_d, int nvalid) {
   unsigned int rej[4] = {0u, 0u, 0u, 0u};
   const unsigned long long thr2 = pack2(thr_d, thr_d);
   float x[32];
@@ -244,7 +259,7 @@ __device__ __forceinline__ unsigned int tq_accept(const uint32_t (&r)[32], const
     }
   }
   const unsigned long long qn2 = pack2(qn, qn);
-  const unsigned long long m2 = pack2(-2.0f, -2.0f);
+  const unsigned long long m2 = pack2(m2s, m2s);
 #pragma unroll
   for (int p = 3; p >= 0; --p) {
 #pragma unroll
@@ -268,7 +283,13 @@ __device__ __forceinline__ unsigned int tq_accept(const uint32_t (&r)[32], const
 
 // CONV (with ATM only): the rows' tf32 residuals are derived in shared memory
 // from the loaded fp32 tile instead of being loaded (no residual array).
-template <int METRIC, int BN, bool ATM, bool CONV>
+// FLT (with ATM, L2, IVF only): the filter scan. One fp16 MMA per K-step of 16
+// replaces the three tf32 ones; A = fp16(s_q (query - list centroid)) in
+// tensor memory, B = the rows' fp16 residuals against that centroid (scaled
+// by the list's power of two s_l); per pair, the query norm, the bound, s_q
+// and 1 / (s_q s_l) come from a.pair_qn / pair_thr / pair_sq / pair_sc, and
+// each pair's kept slots are written with their count (a.pair_cnt).
+template <int METRIC, int BN, bool ATM, bool CONV, bool FLT = false>
 __global__ void __launch_bounds__(ATM ? kTqThreadsAtm : kTqThreads, 1)
     tq_scan_kernel(const ScanArgs a, const __grid_constant__ TqMaps maps, const TqLayout L) {
   extern __shared__ unsigned char smem_raw[];
@@ -302,8 +323,9 @@ __global__ void __launch_bounds__(ATM ? kTqThreadsAtm : kTqThreads, 1)
   const int total = a.flat ? a.nqt * a.P : *a.item_total;
   // ATM: the rows' fp32 tile and residual tile are loaded (CONV: only the fp32
   // tile; the loader warps derive its tf32 residual in shared memory).
-  constexpr uint32_t kStageTx = ATM ? (CONV ? BN * 128 : 2 * BN * 128)
-                                    : 2 * kTqM * 128 + 2 * BN * 128;
+  constexpr uint32_t kStageTx = FLT ? BN * 128
+                                : ATM ? (CONV ? BN * 128 : 2 * BN * 128)
+                                      : 2 * kTqM * 128 + 2 * BN * 128;
 
 #ifdef MF_TC_PROFILE
   const long long _tk = clock64();
@@ -349,7 +371,7 @@ __global__ void __launch_bounds__(ATM ? kTqThreadsAtm : kTqThreads, 1)
         prefetch_tensormap(&maps.a_lo);
       }
       prefetch_tensormap(&maps.b_hi);
-      if (!CONV) prefetch_tensormap(&maps.b_lo);
+      if (!CONV && !FLT) prefetch_tensormap(&maps.b_lo);
       uint32_t seq = 0;
       // flat, chunked: this CTA's run of (query tile x 128-row tile) tiles
       const bool chunked = a.flat && a.chunk_tiles > 0;
@@ -380,6 +402,7 @@ __global__ void __launch_bounds__(ATM ? kTqThreadsAtm : kTqThreads, 1)
             const long long re = t1 * kScanTR;
             it.re = re < a.nb ? re : a.nb;
             it.part = (int)(blockIdx.x - (qt * a.tiles_per_qt) / a.chunk_tiles);
+            it.list = -1;
             item = (int)qi;
             cg += t1 - t0;
           }
@@ -403,14 +426,14 @@ __global__ void __launch_bounds__(ATM ? kTqThreadsAtm : kTqThreads, 1)
             if (!ok) break;
             unsigned char* st = base + size_t(s) * L.stage;
             mbar_arrive_expect_tx(&full[s], kStageTx);
-            const int x = kb * 32;
+            const int x = kb * (FLT ? 64 : 32);
             const int yb = (int)(it.rb + (long long)t * BN);
             if (!ATM) {
               tma_load_2d(st + L.a_hi, &maps.a_hi, x, it.a_row0, &full[s]);
               tma_load_2d(st + L.a_lo, &maps.a_lo, x, it.a_row0, &full[s]);
             }
             tma_load_2d(st + L.b_hi, &maps.b_hi, x, yb, &full[s]);
-            if (!CONV) tma_load_2d(st + L.b_lo, &maps.b_lo, x, yb, &full[s]);
+            if (!CONV && !FLT) tma_load_2d(st + L.b_lo, &maps.b_lo, x, yb, &full[s]);
             ++seq;
           }
         }
@@ -420,7 +443,7 @@ __global__ void __launch_bounds__(ATM ? kTqThreadsAtm : kTqThreads, 1)
   } else if (warp == 5) {
     // ---------------------------------------------------------------- MMA
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_tf32(kTqM, BN);
+      constexpr uint32_t idesc = FLT ? idesc_f16(kTqM, BN) : idesc_tf32(kTqM, BN);
       uint32_t seq = 0, tt = 0;
       for (uint32_t qi = 0;; ++qi) {
         const int qs = qi % kTqQueue;
@@ -456,10 +479,13 @@ __global__ void __launch_bounds__(ATM ? kTqThreadsAtm : kTqThreads, 1)
 #endif
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk) {
-              const uint32_t off = kk * 32;  // 8 tf32 of K per MMA
+              const uint32_t off = kk * 32;  // 8 tf32 (or 16 fp16) of K per MMA
               const uint64_t bh = desc_k_sw128(st + L.b_hi + off);
               const uint64_t bl = desc_k_sw128(st + L.b_lo + off);
-              if (ATM) {
+              if (FLT) {
+                // 16 fp16 of K = 8 columns of the query tile
+                mma_f16_ts(dt, tmem + kb * 32 + kk * 8, bh, idesc, !(kb == 0 && kk == 0));
+              } else if (ATM) {
                 // A columns: hi at [0, KB*32), lo at [KB*32, 2*KB*32)
                 const uint32_t ah = tmem + kb * 32 + kk * 8;
                 const uint32_t al = ah + KB * 32;
@@ -505,16 +531,33 @@ __global__ void __launch_bounds__(ATM ? kTqThreadsAtm : kTqThreads, 1)
     const uint32_t lane_base = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
     constexpr int kMaxV = kTqMaxDAtm / 4;
     float4 v[kMaxV];
+    // FLT: s_q (the query row minus the item's list centroid)
     auto fetch = [&](const ItemDesc& it) {
       const float* src = nullptr;
+      const float* cen = nullptr;
+      float sq = 1.0f;
       if (row < it.nq_item) {
-        const long long q = a.flat ? (long long)it.a_row0 + row : a.pairs[it.a_row0 + row] / a.P;
+        const int pr = a.flat ? 0 : a.pairs[it.a_row0 + row];
+        const long long q = a.flat ? (long long)it.a_row0 + row : pr / a.P;
         src = a.xq + q * a.d;
+        if (FLT) {
+          cen = a.centroids + (long long)it.list * a.d;
+          sq = a.pair_sq[pr];
+        }
       }
 #pragma unroll
       for (int i = 0; i < kMaxV; ++i) {
         v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (src != nullptr && 4 * i < a.d) v[i] = *reinterpret_cast<const float4*>(src + 4 * i);
+        if (src != nullptr && 4 * i < a.d) {
+          v[i] = *reinterpret_cast<const float4*>(src + 4 * i);
+          if (FLT) {
+            const float4 c = *reinterpret_cast<const float4*>(cen + 4 * i);
+            v[i].x = (v[i].x - c.x) * sq;
+            v[i].y = (v[i].y - c.y) * sq;
+            v[i].z = (v[i].z - c.z) * sq;
+            v[i].w = (v[i].w - c.w) * sq;
+          }
+        }
       }
     };
     auto take = [&](uint32_t qi, int& item, ItemDesc& it) -> bool {
@@ -534,9 +577,25 @@ __global__ void __launch_bounds__(ATM ? kTqThreadsAtm : kTqThreads, 1)
       for (uint32_t qi = 0;; ++qi) {
         if (qi > 0 && !mbar_wait(afree, (qi - 1) & 1, s_abort, &g_device_error)) break;
         tc_fence_after();
+        if (FLT) {
+          // 64 fp16 of K per 32 columns
+#pragma unroll
+          for (int c = 0; c < kTqMaxDAtm / 64; ++c) {
+            if (c < KB) {
+              uint32_t pk[32];
+#pragma unroll
+              for (int i = 0; i < 16; ++i) {
+                const float4 e = v[c * 16 + i];
+                pk[2 * i] = pack_f16x2(e.x, e.y);
+                pk[2 * i + 1] = pack_f16x2(e.z, e.w);
+              }
+              tmem_st32(lane_base + c * 32, pk);
+            }
+          }
+        }
 #pragma unroll
         for (int c = 0; c < kTqMaxDAtm / 32; ++c) {
-          if (c < KB) {
+          if (!FLT && c < KB) {
             uint32_t hi[32], lo[32];
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
@@ -711,10 +770,16 @@ __global__ void __launch_bounds__(ATM ? kTqThreadsAtm : kTqThreads, 1)
           slot = pr;
         }
       }
-      const float qn = (METRIC == MF_METRIC_L2 && valid) ? a.qnorms[q] : 0.0f;
+      float qn = 0.0f;
+      if (METRIC == MF_METRIC_L2 && valid) qn = a.pair_qn ? a.pair_qn[slot] : a.qnorms[q];
+      // FLT: the accumulators are s_q s_l times the dot products
+      const float sc = (FLT && valid) ? a.pair_sc[slot] : 1.0f;
+      const float m2s = -2.0f * sc;
       for (int i = 0; i < 32; ++i) my_lists[i * kTqK + lane] = kEmptyKey;
       __syncwarp();
-      const unsigned long long bound = (a.bound && valid) ? bound_key(a.bound[q]) : kEmptyKey;
+      unsigned long long bound = kEmptyKey;
+      if (valid && a.pair_thr) bound = bound_key(a.pair_thr[slot]);
+      else if (valid && a.bound) bound = bound_key(a.bound[q]);
       unsigned long long thr = bound;
       int cnt = 0;
 
@@ -761,7 +826,7 @@ __global__ void __launch_bounds__(ATM ? kTqThreadsAtm : kTqThreads, 1)
 #ifdef MF_TC_PROFILE
           const long long p_f0 = clock64();
 #endif
-          unsigned int acc = tq_accept<METRIC>(r, xs + c0, qn, thr_d, nvalid);
+          unsigned int acc = tq_accept<METRIC>(r, xs + c0, qn, m2s, thr_d, nvalid);
           if (!valid) acc = 0;
           const unsigned int over = __ballot_sync(0xffffffffu, cnt + __popc(acc) > 32);
 #ifdef MF_TC_PROFILE
@@ -779,7 +844,8 @@ __global__ void __launch_bounds__(ATM ? kTqThreadsAtm : kTqThreads, 1)
           // value selected from the registers by a 5-level mux tree
           for (unsigned int m = acc; m != 0u; m &= m - 1u) {
             const int j = __ffs(m) - 1;
-            const float dot = __uint_as_float(select32(r, j));
+            const float dot = FLT ? __uint_as_float(select32(r, j)) * sc
+                                  : __uint_as_float(select32(r, j));
             const float dist = METRIC == MF_METRIC_L2 ? l2_from_dot(qn, xs[c0 + j], dot) : -dot;
             own_buf[cnt++] = make_key(dist, (unsigned int)(rc + j));
           }
@@ -810,9 +876,26 @@ __global__ void __launch_bounds__(ATM ? kTqThreadsAtm : kTqThreads, 1)
 #endif
       const unsigned int pending = __ballot_sync(0xffffffffu, cnt > 0);
       if (pending) merge_rows(pending, cnt, thr, bound);
+      if (FLT) {
+        // the kept slots of each row (a sorted prefix) and their count; rows
+        // that kept none write nothing (their counts start at 0)
+        const unsigned int some =
+            __ballot_sync(0xffffffffu, slot >= 0 && my_lists[lane * kTqK] != kEmptyKey);
+        for (unsigned int mq = some; mq != 0u; mq &= mq - 1u) {
+          const int qq = __ffs(mq) - 1;
+          const long long sq = __shfl_sync(0xffffffffu, slot, qq);
+          const unsigned long long key = lane < k ? my_lists[qq * kTqK + lane] : kEmptyKey;
+          const unsigned int m = __ballot_sync(0xffffffffu, key != kEmptyKey);
+          if (lane == 0) a.pair_cnt[sq] = __popc(m);
+          if (key != kEmptyKey) {
+            a.out_d[sq * k + lane] = key_dist(key);
+            a.out_l[sq * k + lane] = (long long)key_index(key);
+          }
+        }
+      }
       // the warp's 32 rows x k results, one per lane per step: the k steps are
       // independent, so their id lookups overlap
-      for (int e = lane; e < 32 * k; e += 32) {
+      for (int e = lane; e < (FLT ? 0 : 32 * k); e += 32) {
         const int qq = e / k;
         const int kk = e - qq * k;
         const long long sq = __shfl_sync(0xffffffffu, slot, qq);
@@ -920,9 +1003,24 @@ bool tq_choose(int d, int kcap, TqLayout* out) {
   return false;
 }
 
+// The filter scan (fp16, 64 <= d <= 128 with rows of a multiple of 16 bytes):
+// the query tile in tensor memory and the deepest ring of 16 KB row stages
+// that fits. (d >= 64: no tile box wider than the rows.)
+bool tq_choose_bf(int d, TqLayout* out) {
+  if (d < 64 || d > kTqMaxDAtm || d % 8 != 0) return false;
+  for (int sa = 8; sa >= 2; --sa) {
+    TqLayout l = tq_layout(d, kTqK, 128, sa, true, true);
+    if (l.total <= (size_t)kTqMaxSmem) {
+      *out = l;
+      return true;
+    }
+  }
+  return false;
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 std::mutex g_tc_mu;
-int g_tc_attr[64][2][4];  // dynamic smem set per (device, metric, variant)
+int g_tc_attr[64][2][5];  // dynamic smem set per (device, metric, variant)
 
 int encoder(PFN_cuTensorMapEncodeTiled_v12000* out) {
   std::lock_guard<std::mutex> lk(g_tc_mu);
@@ -948,6 +1046,21 @@ int make_map(PFN_cuTensorMapEncodeTiled_v12000 enc, CUtensorMap* map, const floa
                    box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   MF_CHECK(r == CUDA_SUCCESS, MF_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return MF_OK;
+}
+
+// fp16 rows of d elements (d a multiple of 8: 16-byte row pitch), tiles of
+// 64 x box_rows (128-byte inner box, 128-byte swizzle).
+int make_map_f16(PFN_cuTensorMapEncodeTiled_v12000 enc, CUtensorMap* map, const void* p, int d,
+                  int64_t rows, int box_rows) {
+  cuuint64_t dims[2] = {(cuuint64_t)d, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)d * 2};
+  cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(p), dims, strides,
+                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  MF_CHECK(r == CUDA_SUCCESS, MF_ERR_CUDA, "cuTensorMapEncodeTiled (fp16) failed (%d)", (int)r);
   return MF_OK;
 }
 
@@ -1070,6 +1183,47 @@ int launch_tc_scan(const ScanArgs& a, int metric, const float* a_lo, int64_t a_r
   if (grid > total_items) grid = total_items;
   ScopedTiming tm(a.flat ? "scan_topk_flat" : (a.max_rows > 0 ? "scan_topk_ivf_bound" : "scan_topk_ivf"), stream);
   fn<<<(unsigned int)grid, lay.atm ? kTqThreadsAtm : kTqThreads, lay.total, stream>>>(a, maps, lay);
+  MF_LAUNCH_CHECK();
+  return MF_OK;
+}
+
+bool tc_filter_eligible(int d) {
+  if (g_engine == 1) return false;
+  TqLayout l;
+  return tq_choose_bf(d, &l);
+}
+
+int filter_slots() { return kTqK; }
+
+int launch_tc_filter(const ScanArgs& a, int64_t b_rows, int64_t total_items, int device,
+                     cudaStream_t stream) {
+  TqLayout lay;
+  MF_CHECK(a.k >= 1 && a.k <= kTqK && tq_choose_bf(a.d, &lay), MF_ERR_INVALID_ARGS,
+           "filter scan does not fit (d=%d k=%d)", a.d, a.k);
+  MF_CHECK(!a.flat && a.pair_qn && a.pair_thr && a.pair_sq && a.pair_sc && a.pair_cnt &&
+               a.centroids && a.items && a.item_total,
+           MF_ERR_INVALID_ARGS, "filter scan needs IVF items and its per-pair arrays");
+  TqFn fn = tq_scan_kernel<MF_METRIC_L2, 128, true, false, true>;
+  PFN_cuTensorMapEncodeTiled_v12000 enc;
+  MF_TRY(encoder(&enc));
+  TqMaps maps;
+  memset(&maps, 0, sizeof(maps));
+  MF_TRY(make_map_f16(enc, &maps.b_hi, a.xb, a.d, b_rows, lay.BN));
+  {
+    std::lock_guard<std::mutex> lk(g_tc_mu);
+    if (device < 0 || device >= 64 || g_tc_attr[device][0][4] < (int)lay.total) {
+      MF_CUDA(cudaFuncSetAttribute(reinterpret_cast<const void*>(fn),
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)lay.total));
+      if (device >= 0 && device < 64) g_tc_attr[device][0][4] = (int)lay.total;
+    }
+  }
+  if (total_items <= 0) return MF_OK;
+  MF_CHECK(a.counter != nullptr, MF_ERR_INVALID_ARGS, "filter scan needs a work counter");
+  MF_CUDA(cudaMemsetAsync(a.counter, 0, sizeof(int), stream));
+  long long grid = num_sms(device);
+  if (grid > total_items) grid = total_items;
+  ScopedTiming tm("scan_topk_ivf_filter", stream);
+  fn<<<(unsigned int)grid, kTqThreadsAtm, lay.total, stream>>>(a, maps, lay);
   MF_LAUNCH_CHECK();
   return MF_OK;
 }

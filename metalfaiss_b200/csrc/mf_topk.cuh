@@ -121,6 +121,39 @@ __device__ __noinline__ unsigned long long merge_into_list(unsigned long long* l
   return list[k - 1];
 }
 
+// p[0..15] per lane -> the sum over the 32 lanes of p[i] in lanes 2i, 2i+1:
+// a butterfly that halves the live values at each of its five steps.
+__device__ __forceinline__ float warp_transpose_reduce16(float (&p)[16], int lane) {
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const bool hi = lane & 16;
+    const float send = hi ? p[i] : p[i + 8];
+    const float keep = hi ? p[i + 8] : p[i];
+    p[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const bool hi = lane & 8;
+    const float send = hi ? p[i] : p[i + 4];
+    const float keep = hi ? p[i + 4] : p[i];
+    p[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+  }
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const bool hi = lane & 4;
+    const float send = hi ? p[i] : p[i + 2];
+    const float keep = hi ? p[i + 2] : p[i];
+    p[i] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+  }
+  {
+    const bool hi = lane & 2;
+    const float send = hi ? p[0] : p[1];
+    const float keep = hi ? p[1] : p[0];
+    p[0] = keep + __shfl_xor_sync(0xffffffffu, send, 2);
+  }
+  return p[0] + __shfl_xor_sync(0xffffffffu, p[0], 1);
+}
+
 // Per-query state held by the owning warp. The list lives in shared memory
 // (`list`, capacity >= k); nbuf and thr are warp-uniform registers.
 template <int KCAP>

@@ -90,6 +90,7 @@ class IVFFlatIndex:
         self._order = None
         self._ntotal = 0
         self._direct_map = None
+        self._fbank = None  # filter search bank (fp16 residuals, norms, list stats)
 
     @property
     def nlist(self) -> int:
@@ -162,6 +163,7 @@ class IVFFlatIndex:
         self._quantizer.reset()
         self._quantizer.add(c[:, : self.d])
         self._is_trained = True
+        self._fbank = None
 
     # ------------------------------------------------------------------ add
     def _coarse_assign(self, x: torch.Tensor) -> torch.Tensor:
@@ -207,6 +209,7 @@ class IVFFlatIndex:
             self._lo = None  # the tensor-core scan derives them
         self._ntotal = total
         self._direct_map = None
+        self._fbank = None
         sizes = np.diff(out_off.cpu().numpy())
         # Largest lists first: the scan hands out work in this order.
         order = np.argsort(-sizes, kind="stable").astype(np.int32)
@@ -258,6 +261,8 @@ class IVFFlatIndex:
         cq = self._centroid_index()
         if cq is not None:
             return self._search_preassigned_padded(xq, k, self._coarse_probes(xq, cq))
+        if self._filter_ok(k):
+            return self._search_filtered(xq, k, D, I)
         m = int(self.metric_type)
         nbytes = nat.workspace_size("mf_ivf_search_workspace_size", nq, self._nlist, self._nprobe,
                                     self._dp, m, k)
@@ -267,6 +272,51 @@ class IVFFlatIndex:
                  nat.ptr(self._offsets), nat.ptr(self._vecs), nat.ptr(self._norms),
                  nat.ptr(self._lo), nat.ptr(self._ids), self._vecs.shape[0], nat.ptr(self._order),
                  self._dp, m, k, nat.ptr(D), nat.ptr(I), nat.ptr(ws), ws.numel())
+        return SearchResult(D, I)
+
+    # ------------------------------------------------------- filter search
+    # L2 searches run as an fp16 tensor-core filter over residuals against the
+    # list centroids plus an exact fp32 refinement (mf_ivf_search_filtered):
+    # the same exact top-k, with a sixth of the tensor-core work of the 3xTF32
+    # scan. The bank (scaled fp16 residuals, their squared norms, per-list
+    # bounds and scales) is built on the first such search after an add and
+    # kept with the lists.
+    filter_search = True
+
+    def _filter_ok(self, k: int) -> bool:
+        q = self._quantizer
+        return (self.filter_search and self.metric_type == MetricType.L2
+                and q.metric_type == MetricType.L2 and self._ntotal > 0
+                and q.ntotal == self._nlist
+                and nat.load().mf_ivf_filter_eligible(self._dp, int(k), self._ntotal) == 1)
+
+    def _filter_bank(self):
+        if self._fbank is None:
+            dev = self.device
+            n = self._vecs.shape[0]
+            h = torch.empty((n, self._dp), dtype=torch.float16, device=dev)
+            rn = torch.empty(n, dtype=torch.float32, device=dev)
+            stats = torch.empty((self._nlist, 4), dtype=torch.float32, device=dev)
+            q = self._quantizer
+            nat.call("mf_ivf_filter_bank", dev.index, nat.stream_of(dev), self._nlist, self._dp,
+                     nat.ptr(self._offsets), nat.ptr(self._vecs), nat.ptr(self._norms),
+                     nat.ptr(q._xb.buf), n, nat.ptr(h), nat.ptr(rn), nat.ptr(stats))
+            self._fbank = (h, rn, stats)
+        return self._fbank
+
+    def _search_filtered(self, xq, k, D, I) -> SearchResult:
+        bf, rn, stats = self._filter_bank()
+        q = self._quantizer
+        nq = xq.shape[0]
+        nbytes = nat.workspace_size("mf_ivf_search_filtered_workspace_size", nq, self._nlist,
+                                    self._nprobe, self._dp, k)
+        ws = self._workspace().get(nbytes)
+        nat.call("mf_ivf_search_filtered", self.device.index, nat.stream_of(self.device),
+                 nat.ptr(xq), nq, nat.ptr(q._xb.buf), nat.ptr(q._norms.buf), self._nlist,
+                 self._nprobe, nat.ptr(self._offsets), nat.ptr(self._vecs), nat.ptr(self._norms),
+                 nat.ptr(self._lo), nat.ptr(self._ids), self._vecs.shape[0], nat.ptr(self._order),
+                 nat.ptr(bf), nat.ptr(rn), nat.ptr(stats), self._dp, k, nat.ptr(D), nat.ptr(I),
+                 nat.ptr(ws), ws.numel())
         return SearchResult(D, I)
 
     # ----------------------------------------------- coarse step with a bound
@@ -387,6 +437,19 @@ class IVFFlatIndex:
         if nq == 0 or k == 0 or probes.shape[1] == 0:
             return SearchResult(D, I)
         self._empty_lists_guard()
+        if self._filter_ok(k):
+            bf, rn, stats = self._filter_bank()
+            P = probes.shape[1]
+            nbytes = nat.workspace_size("mf_ivf_search_bounded_filtered_workspace_size", nq,
+                                        self._nlist, P, self._dp, k)
+            ws = self._workspace().get(nbytes)
+            nat.call("mf_ivf_search_bounded_filtered", self.device.index,
+                     nat.stream_of(self.device), nat.ptr(xq), nq, nat.ptr(probes), P, self._nlist,
+                     nat.ptr(self._offsets), nat.ptr(self._vecs), nat.ptr(self._norms),
+                     nat.ptr(self._ids), self._vecs.shape[0], nat.ptr(self._order), nat.ptr(bf),
+                     nat.ptr(rn), nat.ptr(stats), nat.ptr(self._quantizer._xb.buf), self._dp, k,
+                     nat.ptr(bound), nat.ptr(D), nat.ptr(I), nat.ptr(ws), ws.numel())
+            return SearchResult(D, I)
         head, ws = self._ivf_args(xq, probes, k)
         nat.call("mf_ivf_search_bounded", *head, nat.ptr(bound), nat.ptr(D), nat.ptr(I),
                  nat.ptr(ws), ws.numel())

@@ -1,0 +1,124 @@
+"""The IVF filter search (an fp16 tensor-core pass over scaled residuals
+against the list centroids, then an exact fp32 refinement;
+mf_ivf_search_filtered) against
+the CPU oracle and against the exact 3xTF32 scan of the same index:
+
+* mixtures at d = 64, 96, 128 with k from 1 to 16 and nprobe from 1 to 32;
+* duplicated rows, so that more rows tie inside a pair's error window than its
+  slots hold: the refinement must rescan those lists and stay exact;
+* lists holding fewer than k rows (padded results), data scaled by 1e3 and
+  1e-3, an add after a search (the bank is rebuilt), and queries far from
+  every centroid."""
+import numpy as np
+import pytest
+import torch
+
+from metalfaiss_b200 import IVFFlatIndex
+from metalfaiss_b200 import _native as nat
+from metalfaiss_b200 import synthetic as syn
+from oracle import compare, oracle
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(autouse=True)
+def _no_device_error():
+    yield
+    assert nat.device_error(0) == 0, "a bounded device wait timed out"
+
+
+def _build(x, nlist, seed):
+    idx = IVFFlatIndex(x.shape[1], nlist)
+    idx.set_centroids(oracle.kmeans_train(x, nlist, 2, seed))
+    idx.add(x)
+    return idx
+
+
+def _check(idx, x, xq, nprobe, k):
+    """Filter search == oracle over the index's own lists, and == the exact scan."""
+    assert nat.load().mf_ivf_filter_eligible(idx._dp, k, idx.ntotal) == 1
+    idx.nprobe = nprobe
+    D, I = idx.search(xq, k).numpy()
+    offsets = idx._offsets.cpu().numpy()
+    vecs = idx._vecs[:, : idx.d].cpu().numpy()
+    ids = idx._ids[: idx.ntotal].cpu().numpy()
+    cents = idx.centroids[: idx.nlist, : idx.d].cpu().numpy()
+    D_ref, I_ref = oracle.ivf_search(xq, cents, offsets, vecs, ids, nprobe, k, oracle.L2)
+    look = compare.exact_lookup(xq, x, oracle.L2)
+    atol = compare.l2_atol(xq, x)
+    errs = compare.check_knn(D, I, D_ref, I_ref, look, atol=atol)
+    assert not errs, errs[:5]
+    idx.filter_search = False
+    try:
+        De, Ie = idx.search(xq, k).numpy()
+    finally:
+        idx.filter_search = True
+    errs = compare.check_knn(D, I, De, Ie, look, atol=atol)
+    assert not errs, errs[:5]
+    return D, I
+
+
+@pytest.mark.parametrize("d,k,nprobe", [(64, 10, 8), (128, 1, 4), (128, 16, 16), (96, 5, 32),
+                                        (128, 10, 32)])
+def test_filter_equals_oracle_and_exact(cuda_device, d, k, nprobe):
+    x, cen, _ = syn.mixture(40000, d, 128, seed=d + k)
+    idx = _build(x, 128, seed=d)
+    xq, _, _ = syn.mixture(700, d, 128, seed=d + k + 1, centres=cen)
+    nat.filter_rescans(0, reset=True)
+    _check(idx, x, xq, nprobe, k)
+
+
+def test_filter_rescans_tied_rows(cuda_device):
+    """Each of 40 points is stored 64 times: a query at one of them sees 64
+    rows at the same distance, more than a pair's slots (at most 32) hold, so
+    the refinement rescans those lists."""
+    d = 64
+    x, cen, _ = syn.mixture(20000, d, 64, seed=71)
+    base = x[:40].copy()
+    x[: 40 * 64] = np.repeat(base, 64, axis=0)
+    idx = _build(x, 64, seed=71)
+    rng = np.random.Generator(np.random.PCG64(72))
+    xq = (base + 1e-3 * rng.standard_normal(base.shape)).astype(np.float32)
+    nat.filter_rescans(0, reset=True)
+    _check(idx, x, xq, 4, 10)
+    assert nat.filter_rescans(0) > 0
+
+
+def test_filter_short_lists_pad(cuda_device):
+    """nlist = 256 over 600 rows: many lists hold fewer than k rows."""
+    d = 64
+    x, cen, _ = syn.mixture(600, d, 256, seed=81)
+    idx = _build(x, 256, seed=81)
+    xq, _, _ = syn.mixture(300, d, 256, seed=82, centres=cen)
+    D, I = _check(idx, x, xq, 1, 16)
+    assert (I == -1).any() and np.isinf(D[I == -1]).all()
+
+
+@pytest.mark.parametrize("scale", [1e3, 1e-3])
+def test_filter_scaled_data(cuda_device, scale):
+    d = 128
+    x, cen, _ = syn.mixture(30000, d, 100, seed=91)
+    x = (x * scale).astype(np.float32)
+    idx = _build(x, 100, seed=91)
+    xq, _, _ = syn.mixture(400, d, 100, seed=92, centres=cen)
+    _check(idx, x, (xq * scale).astype(np.float32), 8, 10)
+
+
+def test_filter_bank_rebuilt_after_add(cuda_device):
+    d = 64
+    x, cen, _ = syn.mixture(30000, d, 80, seed=101)
+    idx = _build(x[:20000], 80, seed=101)
+    xq, _, _ = syn.mixture(300, d, 80, seed=102, centres=cen)
+    _check(idx, x[:20000], xq, 6, 10)
+    idx.add(x[20000:])
+    _check(idx, x, xq, 6, 10)
+
+
+def test_filter_far_queries(cuda_device):
+    """Queries far outside the data: every list is far, the error bounds are
+    large against the distances' spread."""
+    d = 128
+    x, cen, _ = syn.mixture(30000, d, 64, seed=111)
+    idx = _build(x, 64, seed=111)
+    xq = (syn.gaussian(200, d, seed=112) * 40.0).astype(np.float32)
+    _check(idx, x, xq, 8, 10)

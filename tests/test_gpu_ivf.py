@@ -225,6 +225,7 @@ def test_ivf_coarse_bound_path_equals_plain(cuda_device):
     idx.add(x)
     idx.nprobe = 24
     idx.coarse_bound = True
+    idx.filter_search = False  # both sides on the exact 3xTF32 scan
     xq, _, _ = syn.mixture(3000, 64, 2048, seed=62, centres=cen)
     xt = idx._prepare_query(xq)
     cq = idx._centroid_index()
