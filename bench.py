@@ -89,73 +89,88 @@ def tf32_gemm_peak(device, n=8192, reps=10):
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+    """SM clocks and clock-event (throttle) reasons sampled through NVML every
+    few milliseconds during the timed region (reads only)."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = (("hw_slowdown", 0x8), ("hw_thermal_slowdown", 0x40),
+               ("sw_thermal_slowdown", 0x20), ("sw_power_cap", 0x4))
 
-    def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
-        self.proc = None
-        self.lines = []
+    def __init__(self, cuda_index: int, period_s: float = 0.005):
+        self.cuda_index = cuda_index
+        self.period = period_s
+        self.samples = []
+        self.err = None
+        self.handle = None
+        self.stop_flag = threading.Event()
+
+    def _handle(self, nv):
+        # the NVML device with this CUDA device's PCI address (indices may differ)
+        try:
+            pr = torch.cuda.get_device_properties(self.cuda_index)
+            bus = f"{pr.pci_domain_id:08x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
+            return nv.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:
+            return nv.nvmlDeviceGetHandleByIndex(self.cuda_index)
 
     def start(self):
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "100"],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
-            self.t.start()
-        except (OSError, FileNotFoundError):
-            self.proc = None
+            import pynvml as nv
+            nv.nvmlInit()
+            self.nv = nv
+            self.handle = self._handle(nv)
+            self.max_mhz = nv.nvmlDeviceGetMaxClockInfo(self.handle, nv.NVML_CLOCK_SM)
+            self._sample()
+        except Exception as e:  # no NVML: report it, do not fail the run
+            self.err = f"NVML unavailable ({type(e).__name__})"
             return
-        # nvidia-smi's start-up must not fall inside the timed region
-        t0 = time.time()
-        while not self.lines and time.time() - t0 < 5.0 and self.proc.poll() is None:
-            time.sleep(0.01)
-        self.warm = len(self.lines)
+        self.samples = []
+        self.t = threading.Thread(target=self._loop, daemon=True)
+        self.t.start()
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
+    def _sample(self):
+        nv = self.nv
+        mhz = nv.nvmlDeviceGetClockInfo(self.handle, nv.NVML_CLOCK_SM)
+        try:
+            mask = nv.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
+        except AttributeError:
+            mask = nv.nvmlDeviceGetCurrentClocksThrottleReasons(self.handle)
+        self.samples.append((mhz, mask))
+
+    def _loop(self):
+        while not self.stop_flag.is_set():
+            try:
+                self._sample()
+            except Exception:
+                pass
+            time.sleep(self.period)
 
     def stop(self):
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.proc.kill()
+        if self.err is not None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [self.err], "samples": 0}
+        self.stop_flag.set()
         self.t.join(timeout=2)
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines[getattr(self, "warm", 0):]:
-            parts = [p.strip() for p in ln.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                mx = float(parts[2])
-            except ValueError:
-                continue
-            for nm, v in zip(names, parts[5:9]):
-                if v.lower() == "active":
-                    reasons.add(nm)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
-                "reasons": sorted(reasons), "samples": len(sm)}
+        if not self.samples:  # a region shorter than one period: the clocks right after it
+            self._sample()
+        sm = [m for m, _ in self.samples]
+        reasons = sorted({nm for _, mask in self.samples for nm, bit in self.REASONS if mask & bit})
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": self.max_mhz, "reasons": reasons,
+                "samples": len(sm), "source": "NVML every 5 ms"}
 
 
-# dram__bytes_read.sum + dram__bytes_write.sum of one all-probes scan launch
-# (profiles/tq_scan_ivf20m.md). ivf2m: measured (2,228,082,688 + 53,105,408 B).
-# ivf20m: the multi-pass DRAM metrics are not captured at full size; the ivf2m
-# bytes per probed row (1,142 B: vector, residual and norm once each, plus the
-# query tiles) times the 13,287,418 rows probed per ivf20m batch.
+# dram__bytes_read.sum + dram__bytes_write.sum of one launch of the dominant
+# kernel (profiles/). Exact search, the all-probes 3xTF32 launch: ivf2m
+# measured (2,228,082,688 + 53,105,408 B); ivf20m not captured at full size:
+# the ivf2m bytes per probed row (1,142 B: vector, residual and norm once
+# each, plus the query tiles) times the 13,287,418 rows probed per batch.
+# Filter search, the fp16 tensor-core launch: ivf4m measured (272,680,960 +
+# 4,955,904 B over its 918,849 rows); ivf20m: those 302.2 B per row times its
+# 4,620,425 rows.
 TRAFFIC = {
     "ivf2m": {"bytes": 2281188096, "source": "ncu, measured"},
     "ivf20m": {"bytes": 15177587741, "source": "ncu ivf2m bytes per probed row x probed rows"},
+    "ivf4m/filter": {"bytes": 277636864, "source": "ncu, measured"},
+    "ivf20m/filter": {"bytes": 1396094796,
+                      "source": "ncu ivf4m bytes per row of the filter pass x its rows"},
 }
 
 
@@ -310,6 +325,8 @@ def run_ours(args, cfg):
         ms = float(t.item())
 
     # ---- end to end through the public API: pinned host queries in, results out
+    # (every step copies its queries host -> device and its results device ->
+    # host, in stream order, inside the timed region)
     xq_host = xq.cpu().pin_memory()
     D_host = torch.empty((nq, k), dtype=torch.float32).pin_memory()
     I_host = torch.empty((nq, k), dtype=torch.int64).pin_memory()

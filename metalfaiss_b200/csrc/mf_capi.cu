@@ -301,10 +301,10 @@ int ivf_filter_topk(int device, cudaStream_t stream, const IvfWs& w, const float
   MF_TRY(launch_filter_pairs(xq, w.qn, nq, P, d, probes, list_offsets, nlist, centroids,
                              list_stats, bound, w.fp, stream));
   // (pairs that are not scanned have no kept slots: launch_filter_pairs).
-  // A list probed by at most kSmallGroup queries goes to the exact few-query
-  // scan instead (a 128-query tile would be mostly padding; those rows' bytes
-  // bound the work): it keeps each pair's exact top-k, as slots with e >= 0
-  // to spare, never all S of them.
+  // A list probed by at most kSmallGroup queries goes to the few-query scan
+  // instead (a 128-query tile would be mostly padding; those rows' bytes
+  // bound the work), in its filter form: the same fp16 rows, upper bounds and
+  // slots.
   constexpr int kSmallGroup = 16;
   const int small_max = few_eligible(MF_METRIC_L2, d, k) ? kSmallGroup : 0;
   MF_TRY(run_ivf_groups_ex(w.g, probes, nq, P, nlist, list_offsets, list_order, nullptr, nullptr,
@@ -339,11 +339,11 @@ int ivf_filter_topk(int device, cudaStream_t stream, const IvfWs& w, const float
     ScanArgs fa{};
     fa.xq = xq;
     fa.qnorms = w.qn;
-    fa.xb = list_vecs;
-    fa.xnorms = list_norms;
+    fa.xb = reinterpret_cast<const float*>(list_f16);
+    fa.xnorms = list_rnorms;
     fa.ids = nullptr;
     fa.d = d;
-    fa.k = k;
+    fa.k = S;
     fa.nq = nq;
     fa.P = P;
     fa.flat = 0;
@@ -356,8 +356,12 @@ int ivf_filter_topk(int device, cudaStream_t stream, const IvfWs& w, const float
     fa.counter = w.g.counter;
     fa.out_d = w.pd;
     fa.out_l = w.pl;
-    fa.bound = bound;
+    fa.pair_qn = w.fp.qn;
+    fa.pair_thr = w.fp.thr;
+    fa.pair_sq = w.fp.sq;
+    fa.pair_sc = w.fp.sc;
     fa.pair_cnt = w.fp.cnt;
+    fa.centroids = centroids;
     fa.out_stride = S;
     MF_TRY(launch_few_scan(fa, MF_METRIC_L2, nq * P, device, stream));
   }

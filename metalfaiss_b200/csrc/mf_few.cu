@@ -11,6 +11,15 @@
 // so the pass is bound by reading the rows once from HBM. Distances, keys and
 // the per-query warp top-k are those of scan_kernel (mf_scan.cu), filtered by
 // the per-query bound when one is given.
+//
+// FLT (L2, the filter search): the rows are the filter bank's fp16 residuals
+// against the item's list centroid (scaled by the list's power of two; a row
+// is one 8-byte slice per lane), the queries s_q (q - c) in fp32, and each
+// pair's keys are the filter's upper bounds u = (Dc + e) + rn_x - 2 dot, with
+// the pair's query norm, bound and scales from a.pair_qn / pair_thr / pair_sc.
+// Only the rows are rounded (to fp16), so the filter's error bound covers them.
+#include <cuda_fp16.h>
+
 #include "mf_scan.cuh"
 #include "mf_timing.cuh"
 #include "mf_topk.cuh"
@@ -33,7 +42,7 @@ struct FewSmem {
   }
 };
 
-template <int METRIC>
+template <int METRIC, bool FLT>
 __global__ void __launch_bounds__(kFewWarps * 32) few_scan_kernel(const ScanArgs a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const int warp = threadIdx.x >> 5;
@@ -49,6 +58,7 @@ __global__ void __launch_bounds__(kFewWarps * 32) few_scan_kernel(const ScanArgs
   __shared__ int s_item;
   __shared__ long long s_slot[kFewMax];
   __shared__ float s_qn[kFewMax];
+  __shared__ float s_sc[kFewMax];
   __shared__ unsigned long long s_bnd[kFewMax];
   const int total = *a.item_total;
   const int group = a.group > 0 ? a.group : kFewMax;
@@ -70,13 +80,26 @@ __global__ void __launch_bounds__(kFewWarps * 32) few_scan_kernel(const ScanArgs
       const int pr = a.pairs[pb + threadIdx.x];
       const int q = pr / a.P;
       s_slot[threadIdx.x] = pr;
-      s_qn[threadIdx.x] = METRIC == MF_METRIC_L2 ? a.qnorms[q] : 0.0f;
-      s_bnd[threadIdx.x] = a.bound ? bound_key(a.bound[q]) : kEmptyKey;
+      if (FLT) {
+        s_qn[threadIdx.x] = a.pair_qn[pr];
+        s_sc[threadIdx.x] = a.pair_sc[pr];
+        s_bnd[threadIdx.x] = bound_key(a.pair_thr[pr]);
+      } else {
+        s_qn[threadIdx.x] = METRIC == MF_METRIC_L2 ? a.qnorms[q] : 0.0f;
+        s_bnd[threadIdx.x] = a.bound ? bound_key(a.bound[q]) : kEmptyKey;
+      }
     }
     for (int i = threadIdx.x; i < nq * d4; i += kFewWarps * 32) {
       const int j = i / d4;
       const int pr = a.pairs[pb + j];
-      qs[i] = reinterpret_cast<const float4*>(a.xq + (long long)(pr / a.P) * d)[i - j * d4];
+      float4 v = reinterpret_cast<const float4*>(a.xq + (long long)(pr / a.P) * d)[i - j * d4];
+      if (FLT) {
+        // s_q (q - c), exact scaling by a power of two
+        const float4 c = reinterpret_cast<const float4*>(a.centroids + (long long)g.x * d)[i - j * d4];
+        const float sq = a.pair_sq[pr];
+        v = make_float4((v.x - c.x) * sq, (v.y - c.y) * sq, (v.z - c.z) * sq, (v.w - c.w) * sq);
+      }
+      qs[i] = v;
     }
     for (int i = lane; i < nq * kFewK; i += 32) lists[i] = kEmptyKey;
     __syncthreads();
@@ -87,16 +110,8 @@ __global__ void __launch_bounds__(kFewWarps * 32) few_scan_kernel(const ScanArgs
 
     const float4* qv = qs + lane;  // this lane's column slice of each query
     const bool col_ok = lane < d4;
-    for (long long r0 = rb + (long long)warp * kFewRows; r0 < re;
-         r0 += (long long)kFewWarps * kFewRows) {
-      // rows r0 .. r0+15: load i brings row r0+i across the warp (coalesced)
-      float4 xv[kFewRows];
-#pragma unroll
-      for (int i = 0; i < kFewRows; ++i) {
-        const long long r = r0 + i;
-        xv[i] = (r < re && col_ok) ? reinterpret_cast<const float4*>(a.xb + r * d)[lane]
-                                   : make_float4(0.f, 0.f, 0.f, 0.f);
-      }
+    // rows r0 .. r0+15 (row i's column slice `lane` in xv[i]) against every query
+    auto process = [&](const float4 (&xv)[kFewRows], long long r0) {
       const long long my_row = r0 + (lane >> 1);  // the row whose sum this lane ends with
       const bool rv = my_row < re && (lane & 1) == 0;
       const float xn = (METRIC == MF_METRIC_L2 && my_row < re) ? a.xnorms[my_row] : 0.0f;
@@ -113,7 +128,9 @@ __global__ void __launch_bounds__(kFewWarps * 32) few_scan_kernel(const ScanArgs
         }
         const float dot = warp_transpose_reduce16(p, lane);
         const unsigned long long tj = __shfl_sync(0xffffffffu, thr, j);
-        const float dist = METRIC == MF_METRIC_L2 ? l2_from_dot(s_qn[j], xn, dot) : -dot;
+        const float dist = METRIC == MF_METRIC_L2
+                               ? l2_from_dot(s_qn[j], xn, FLT ? dot * s_sc[j] : dot)
+                               : -dot;
         const unsigned long long key = rv ? make_key(dist, (unsigned int)my_row) : kEmptyKey;
         unsigned int m = __ballot_sync(0xffffffffu, key < tj);
         if (m == 0u) continue;
@@ -135,6 +152,41 @@ __global__ void __launch_bounds__(kFewWarps * 32) few_scan_kernel(const ScanArgs
         if ((m >> lane) & 1u) buf[nb + __popc(m & lanemask_lt())] = key;
         if (lane == j) nbuf = nb + __popc(m);
         __syncwarp();
+      }
+    };
+    if (FLT) {
+      // fp16 rows, 8 bytes (4 elements) per lane
+      for (long long r0 = rb + (long long)warp * kFewRows; r0 < re;
+           r0 += (long long)kFewWarps * kFewRows) {
+        uint2 hv[kFewRows];
+#pragma unroll
+        for (int i = 0; i < kFewRows; ++i) {
+          const long long r = r0 + i;
+          hv[i] = (r < re && col_ok)
+                      ? reinterpret_cast<const uint2*>(a.xb)[(r * d >> 2) + lane]
+                      : make_uint2(0u, 0u);
+        }
+        float4 xv[kFewRows];
+#pragma unroll
+        for (int i = 0; i < kFewRows; ++i) {
+          const float2 lo = __half22float2(*reinterpret_cast<const __half2*>(&hv[i].x));
+          const float2 hi = __half22float2(*reinterpret_cast<const __half2*>(&hv[i].y));
+          xv[i] = make_float4(lo.x, lo.y, hi.x, hi.y);
+        }
+        process(xv, r0);
+      }
+    } else {
+      for (long long r0 = rb + (long long)warp * kFewRows; r0 < re;
+           r0 += (long long)kFewWarps * kFewRows) {
+        // rows r0 .. r0+15: load i brings row r0+i across the warp (coalesced)
+        float4 xv[kFewRows];
+#pragma unroll
+        for (int i = 0; i < kFewRows; ++i) {
+          const long long r = r0 + i;
+          xv[i] = (r < re && col_ok) ? reinterpret_cast<const float4*>(a.xb + r * d)[lane]
+                                     : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        process(xv, r0);
       }
     }
     // each warp folds its buffers into its lists; then warp (j mod 4) merges
@@ -199,8 +251,13 @@ int launch_few_scan(const ScanArgs& a, int metric, int64_t max_items, int device
            "few-query scan needs its items and a work counter");
   if (max_items <= 0) return MF_OK;
   const size_t smem = FewSmem::block(a.d);
-  auto fn = metric == MF_METRIC_L2 ? few_scan_kernel<MF_METRIC_L2>
-                                   : few_scan_kernel<MF_METRIC_INNER_PRODUCT>;
+  const bool flt = a.pair_sq != nullptr;
+  MF_CHECK(!flt || (metric == MF_METRIC_L2 && a.d <= kFewMaxD && a.d % 8 == 0 && a.pair_qn &&
+                    a.pair_thr && a.pair_sc && a.pair_cnt && a.centroids),
+           MF_ERR_INVALID_ARGS, "few-query filter scan: L2, d <= %d, per-pair arrays", kFewMaxD);
+  auto fn = flt ? few_scan_kernel<MF_METRIC_L2, true>
+                : (metric == MF_METRIC_L2 ? few_scan_kernel<MF_METRIC_L2, false>
+                                          : few_scan_kernel<MF_METRIC_INNER_PRODUCT, false>);
   MF_CUDA(cudaFuncSetAttribute(reinterpret_cast<const void*>(fn),
                                cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   int per_sm = 0;
