@@ -95,7 +95,7 @@ class ClockSampler:
     REASONS = (("hw_slowdown", 0x8), ("hw_thermal_slowdown", 0x40),
                ("sw_thermal_slowdown", 0x20), ("sw_power_cap", 0x4))
 
-    def __init__(self, cuda_index: int, period_s: float = 0.005):
+    def __init__(self, cuda_index: int, period_s: float = 0.02):
         self.cuda_index = cuda_index
         self.period = period_s
         self.samples = []
@@ -154,7 +154,7 @@ class ClockSampler:
         sm = [m for m, _ in self.samples]
         reasons = sorted({nm for _, mask in self.samples for nm, bit in self.REASONS if mask & bit})
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": self.max_mhz, "reasons": reasons,
-                "samples": len(sm), "source": "NVML every 5 ms"}
+                "samples": len(sm), "source": "NVML every 20 ms"}
 
 
 # dram__bytes_read.sum + dram__bytes_write.sum of one launch of the dominant

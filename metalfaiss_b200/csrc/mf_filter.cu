@@ -143,48 +143,88 @@ __global__ void __launch_bounds__(kBankThreads) filter_bank_kernel(
   }
 }
 
-// One warp per (query, probe) pair.
-__global__ void filter_pairs_kernel(const float* __restrict__ xq, const float* __restrict__ qnorms,
-                                    int64_t n, int P, int d, const int64_t* __restrict__ probes,
-                                    const int64_t* __restrict__ offsets, int nlist,
-                                    const float* __restrict__ cents,
-                                    const float4* __restrict__ stats,
-                                    const float* __restrict__ bound, FilterPairs fp) {
-  const int64_t s = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+// One warp per query: its row stays in registers (lane j: elements 4j + 128 i)
+// while the warp walks its probes; lane p then writes pair p's values.
+constexpr int kPairsWarps = 8;
+
+__global__ void __launch_bounds__(kPairsWarps * 32) filter_pairs_kernel(
+    const float* __restrict__ xq, const float* __restrict__ qnorms, int64_t nq, int P, int d,
+    const int64_t* __restrict__ probes, const int64_t* __restrict__ offsets, int nlist,
+    const float* __restrict__ cents, const float4* __restrict__ stats,
+    const float* __restrict__ bound, FilterPairs fp) {
+  const int64_t q = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
-  if (s >= n) return;
-  const int64_t q = s / P;
-  const int64_t l = probes[s];
-  // no kept slots until the scan writes them (a pair it does not scan keeps none)
-  if (lane == 0) fp.cnt[s] = 0;
-  if (l < 0 || l >= nlist || offsets[l + 1] <= offsets[l]) {
-    if (lane == 0) {
+  if (q >= nq) return;  // warp-uniform
+  constexpr int kMaxSlices = 8;  // d <= 1024
+  float4 xv[kMaxSlices];
+#pragma unroll
+  for (int i = 0; i < kMaxSlices; ++i) {
+    const int j = 4 * lane + 128 * i;
+    xv[i] = j < d ? *reinterpret_cast<const float4*>(xq + q * d + j)
+                  : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  const float qn = qnorms[q];
+  const float bq = bound[q];
+  for (int p0 = 0; p0 < P; p0 += 32) {
+    // lane j ends with pair p0 + j's squared distance to its centroid
+    float my_dc = 0.0f;
+    const int np = P - p0 < 32 ? P - p0 : 32;
+    const int64_t my_l = lane < np ? probes[q * P + p0 + lane] : -1;
+    const bool my_ok = my_l >= 0 && my_l < nlist && offsets[my_l + 1] > offsets[my_l];
+    // four probes at a time, so their centroid loads overlap
+    constexpr int kB = 4;
+    for (unsigned int m = __ballot_sync(0xffffffffu, my_ok); m != 0u;) {
+      int jj[kB];
+#pragma unroll
+      for (int b = 0; b < kB; ++b) {
+        jj[b] = m ? __ffs(m) - 1 : -1;
+        if (m) m &= m - 1u;
+      }
+      float dc[kB];
+#pragma unroll
+      for (int b = 0; b < kB; ++b) {
+        dc[b] = 0.0f;
+        if (jj[b] < 0) continue;
+        const int64_t l = __shfl_sync(0xffffffffu, my_l, jj[b]);
+        const float* c = cents + l * d;
+#pragma unroll
+        for (int i = 0; i < kMaxSlices; ++i) {
+          const int e = 4 * lane + 128 * i;
+          if (e < d) {
+            const float4 cv = *reinterpret_cast<const float4*>(c + e);
+            const float v0 = xv[i].x - cv.x, v1 = xv[i].y - cv.y, v2 = xv[i].z - cv.z,
+                        v3 = xv[i].w - cv.w;
+            dc[b] = fmaf(v0, v0, dc[b]);
+            dc[b] = fmaf(v1, v1, dc[b]);
+            dc[b] = fmaf(v2, v2, dc[b]);
+            dc[b] = fmaf(v3, v3, dc[b]);
+          }
+        }
+      }
+#pragma unroll
+      for (int b = 0; b < kB; ++b) {
+        if (jj[b] < 0) continue;
+        const float t = warp_sum(dc[b]);
+        if (lane == jj[b]) my_dc = t;
+      }
+    }
+    if (lane >= np) continue;
+    const int64_t s = q * P + p0 + lane;
+    // no kept slots until the scan writes them (a pair it does not scan keeps none)
+    fp.cnt[s] = 0;
+    if (!my_ok) {
       fp.qn[s] = 0.0f;
       fp.thr[s] = 0.0f;
       fp.e[s] = 0.0f;
       fp.sq[s] = 1.0f;
       fp.sc[s] = 1.0f;
+      continue;
     }
-    return;
-  }
-  const float* x = xq + q * d;
-  const float* c = cents + l * d;
-  float dc = 0.0f;
-  for (int j = 4 * lane; j < d; j += 128) {
-    const float4 xv = *reinterpret_cast<const float4*>(x + j);
-    const float4 cv = *reinterpret_cast<const float4*>(c + j);
-    const float v0 = xv.x - cv.x, v1 = xv.y - cv.y, v2 = xv.z - cv.z, v3 = xv.w - cv.w;
-    dc = fmaf(v0, v0, dc);
-    dc = fmaf(v1, v1, dc);
-    dc = fmaf(v2, v2, dc);
-    dc = fmaf(v3, v3, dc);
-  }
-  dc = warp_sum(dc);
-  if (lane == 0) {
-    const float4 st = stats[l];
+    const float dc = my_dc;
+    const float4 st = stats[my_l];
     const float R = st.x, XN = st.y, sl = st.z;
-    const float nq = sqrtf(dc) * (1.0f + 0x1p-17f);
-    const int eq = scale_exp(nq);
+    const float nrm = sqrtf(dc) * (1.0f + 0x1p-17f);
+    const int eq = scale_exp(nrm);
     float e, sq = 1.0f, sc = 1.0f, thr;
     if (eq > kScaleExpMax || eq < -kScaleExpMax || !(R * sl < 0x1p13f)) {
       // out of the scales' range: keep nothing, rescan exactly
@@ -194,9 +234,9 @@ __global__ void filter_pairs_kernel(const float* __restrict__ xq, const float* _
       sq = ldexpf(1.0f, eq);
       sc = 1.0f / (sq * sl);  // exact: a power of two within range
       // 0x1.05p-9 >= 2^-9 (1 + 2^-6)(1 + 2^-17)
-      e = 0x1.05p-9f * nq * R + 0x1p-22f * sqrtf((float)d) * (nq / sl + R / sq) +
-          (float)(d + 20) * 0x1p-23f * (qnorms[q] + XN + dc + R * R) + 0x1p-100f;
-      thr = bound[q] + 2.0f * e;  // +inf stays +inf
+      e = 0x1.05p-9f * nrm * R + 0x1p-22f * sqrtf((float)d) * (nrm / sl + R / sq) +
+          (float)(d + 20) * 0x1p-23f * (qn + XN + dc + R * R) + 0x1p-100f;
+      thr = bq + 2.0f * e;  // +inf stays +inf
     }
     fp.qn[s] = dc + e;
     fp.e[s] = e;
@@ -386,10 +426,11 @@ int launch_filter_pairs(const float* xq, const float* qnorms, int64_t nq, int P,
                         const int64_t* probes, const int64_t* offsets, int nlist,
                         const float* cents, const float* stats, const float* bound,
                         const FilterPairs& fp, cudaStream_t stream) {
-  const int64_t n = nq * P;
-  if (n <= 0) return MF_OK;
-  filter_pairs_kernel<<<(unsigned int)ceil_div(n * 32, 256), 256, 0, stream>>>(
-      xq, qnorms, n, P, d, probes, offsets, nlist, cents, reinterpret_cast<const float4*>(stats),
+  if (nq <= 0 || P <= 0) return MF_OK;
+  MF_CHECK(d <= 1024, MF_ERR_INVALID_ARGS, "filter pairs: d=%d", d);
+  ScopedTiming tm("ivf_filter_pairs", stream);
+  filter_pairs_kernel<<<(unsigned int)ceil_div(nq, kPairsWarps), kPairsWarps * 32, 0, stream>>>(
+      xq, qnorms, nq, P, d, probes, offsets, nlist, cents, reinterpret_cast<const float4*>(stats),
       bound, fp);
   MF_LAUNCH_CHECK();
   return MF_OK;

@@ -96,47 +96,65 @@ __global__ void __launch_bounds__(kScanBlock) ivf_plan_kernel(const int* __restr
                                                              int* item_total, int* cursors,
                                                              int group, int2* items2,
                                                              int* item_total2, int small_max) {
+  // Lists in tiles of kScanBlock (thread t: list t0 + t), up to kPlanTiles
+  // tiles per pass with every load issued before the first scan.
+  constexpr int kPlanTiles = 16;
   __shared__ int sums[32];
-  const int chunk = (nlist + kScanBlock - 1) / kScanBlock;
-  const int b = threadIdx.x * chunk;
-  const int e = b + chunk < nlist ? b + chunk : nlist;
-  int s = 0;
-  for (int i = b; i < e; ++i) s += counts[i];
-  int total;
-  int run = block_exclusive_scan<int>(s, sums, total);
-  for (int i = b; i < e; ++i) {
-    pair_offsets[i] = run;
-    run += counts[i];
-    cursors[i] = 0;
+  const int t = threadIdx.x;
+  // pair offsets, in list-id order
+  int base = 0;
+  for (int p0 = 0; p0 < nlist; p0 += kPlanTiles * kScanBlock) {
+    int v[kPlanTiles];
+#pragma unroll
+    for (int j = 0; j < kPlanTiles; ++j) {
+      const int i = p0 + j * kScanBlock + t;
+      v[j] = i < nlist ? counts[i] : 0;
+    }
+#pragma unroll
+    for (int j = 0; j < kPlanTiles; ++j) {
+      if (p0 + j * kScanBlock >= nlist) break;  // block-uniform
+      const int i = p0 + j * kScanBlock + t;
+      int tot;
+      const int ex = block_exclusive_scan<int>(v[j], sums, tot);
+      if (i < nlist) {
+        pair_offsets[i] = base + ex;
+        cursors[i] = 0;
+      }
+      base += tot;
+    }
   }
-  if (threadIdx.x == 0) pair_offsets[nlist] = total;
-  s = 0;
-  int s2 = 0;
-  for (int i = b; i < e; ++i) {
-    const int l = order ? order[i] : i;
-    const int c = counts[l];
-    const int ng = (c + group - 1) / group;
-    const bool small_list = small_max > 0 && c > 0 && c <= small_max;
-    s += small_list ? 0 : ng;
-    s2 += small_list ? 1 : 0;
+  if (t == 0) pair_offsets[nlist] = base;
+  // items, in list order
+  int run = 0, run2 = 0;
+  for (int p0 = 0; p0 < nlist; p0 += kPlanTiles * kScanBlock) {
+    int lv[kPlanTiles], cv[kPlanTiles];
+#pragma unroll
+    for (int j = 0; j < kPlanTiles; ++j) {
+      const int i = p0 + j * kScanBlock + t;
+      lv[j] = i < nlist ? (order ? order[i] : i) : -1;
+    }
+#pragma unroll
+    for (int j = 0; j < kPlanTiles; ++j) cv[j] = lv[j] >= 0 ? counts[lv[j]] : 0;
+#pragma unroll
+    for (int j = 0; j < kPlanTiles; ++j) {
+      if (p0 + j * kScanBlock >= nlist) break;  // block-uniform
+      const int c = cv[j];
+      const int ng = (c + group - 1) / group;
+      const bool small_list = small_max > 0 && c > 0 && c <= small_max;
+      int tot_a, tot_b;
+      const int ea = block_exclusive_scan<int>(small_list ? 0 : ng, sums, tot_a);
+      const int eb = block_exclusive_scan<int>(small_list ? 1 : 0, sums, tot_b);
+      if (small_list)
+        items2[run2 + eb] = make_int2(lv[j], 0);
+      else
+        for (int g = 0; g < ng; ++g) items[run + ea + g] = make_int2(lv[j], g);
+      run += tot_a;
+      run2 += tot_b;
+    }
   }
-  int total_items, total2;
-  run = block_exclusive_scan<int>(s, sums, total_items);
-  __syncthreads();
-  int run2 = block_exclusive_scan<int>(s2, sums, total2);
-  for (int i = b; i < e; ++i) {
-    const int l = order ? order[i] : i;
-    const int c = counts[l];
-    const int ng = (c + group - 1) / group;
-    const bool small_list = small_max > 0 && c > 0 && c <= small_max;
-    if (small_list)
-      items2[run2++] = make_int2(l, 0);
-    else
-      for (int g = 0; g < ng; ++g) items[run++] = make_int2(l, g);
-  }
-  if (threadIdx.x == 0) {
-    *item_total = total_items;
-    if (item_total2) *item_total2 = total2;
+  if (t == 0) {
+    *item_total = run;
+    if (item_total2) *item_total2 = run2;
   }
 }
 

@@ -529,8 +529,11 @@ __global__ void __launch_bounds__(ATM ? kTqThreadsAtm : kTqThreads, 1)
     const int row = 32 * (warp & 3) + lane;
     const int cid = (warp - 6) * 32 + lane;
     const uint32_t lane_base = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
-    constexpr int kMaxV = kTqMaxDAtm / 4;
+    constexpr int kMaxV = FLT ? 1 : kTqMaxDAtm / 4;
     float4 v[kMaxV];
+    // FLT: the row s_q (q - c) is packed to fp16 as it arrives (half the
+    // registers of the fp32 row the tf32 form keeps)
+    uint32_t hq[FLT ? kTqMaxDAtm / 2 : 1];
     // FLT: s_q (the query row minus the item's list centroid)
     auto fetch = [&](const ItemDesc& it) {
       const float* src = nullptr;
@@ -545,18 +548,24 @@ __global__ void __launch_bounds__(ATM ? kTqThreadsAtm : kTqThreads, 1)
           sq = a.pair_sq[pr];
         }
       }
+      if constexpr (FLT) {
 #pragma unroll
-      for (int i = 0; i < kMaxV; ++i) {
-        v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (src != nullptr && 4 * i < a.d) {
-          v[i] = *reinterpret_cast<const float4*>(src + 4 * i);
-          if (FLT) {
+        for (int i = 0; i < kTqMaxDAtm / 4; ++i) {
+          float4 e = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (src != nullptr && 4 * i < a.d) {
+            const float4 x = *reinterpret_cast<const float4*>(src + 4 * i);
             const float4 c = *reinterpret_cast<const float4*>(cen + 4 * i);
-            v[i].x = (v[i].x - c.x) * sq;
-            v[i].y = (v[i].y - c.y) * sq;
-            v[i].z = (v[i].z - c.z) * sq;
-            v[i].w = (v[i].w - c.w) * sq;
+            e = make_float4((x.x - c.x) * sq, (x.y - c.y) * sq, (x.z - c.z) * sq,
+                            (x.w - c.w) * sq);
           }
+          hq[2 * i] = pack_f16x2(e.x, e.y);
+          hq[2 * i + 1] = pack_f16x2(e.z, e.w);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < kMaxV; ++i) {
+          v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (src != nullptr && 4 * i < a.d) v[i] = *reinterpret_cast<const float4*>(src + 4 * i);
         }
       }
     };
@@ -577,25 +586,22 @@ __global__ void __launch_bounds__(ATM ? kTqThreadsAtm : kTqThreads, 1)
       for (uint32_t qi = 0;; ++qi) {
         if (qi > 0 && !mbar_wait(afree, (qi - 1) & 1, s_abort, &g_device_error)) break;
         tc_fence_after();
-        if (FLT) {
+        if constexpr (FLT) {
           // 64 fp16 of K per 32 columns
 #pragma unroll
           for (int c = 0; c < kTqMaxDAtm / 64; ++c) {
             if (c < KB) {
               uint32_t pk[32];
 #pragma unroll
-              for (int i = 0; i < 16; ++i) {
-                const float4 e = v[c * 16 + i];
-                pk[2 * i] = pack_f16x2(e.x, e.y);
-                pk[2 * i + 1] = pack_f16x2(e.z, e.w);
-              }
+              for (int i = 0; i < 32; ++i) pk[i] = hq[c * 32 + i];
               tmem_st32(lane_base + c * 32, pk);
             }
           }
         }
+        if constexpr (!FLT) {
 #pragma unroll
         for (int c = 0; c < kTqMaxDAtm / 32; ++c) {
-          if (!FLT && c < KB) {
+          if (c < KB) {
             uint32_t hi[32], lo[32];
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
@@ -612,6 +618,7 @@ __global__ void __launch_bounds__(ATM ? kTqThreadsAtm : kTqThreads, 1)
             tmem_st32(lane_base + c * 32, hi);
             tmem_st32(lane_base + KB * 32 + c * 32, lo);
           }
+        }
         }
         tmem_wait_st();
         tc_fence_before();
