@@ -112,7 +112,8 @@ TqLayout tq_layout(int d, int kcap, int BN, int SA, bool atm, bool bf = false) {
   s.nacc = (kTqTmemCols - s.acc0) / BN;
   if (s.nacc > kTqMaxAcc) s.nacc = kTqMaxAcc;
   s.b_lo = s.b_hi + size_t(BN) * 128;
-  s.stage = bf ? s.b_lo : s.b_lo + size_t(BN) * 128;
+  // the filter scan's stage holds a whole tile (all K-blocks): one hand-off per tile
+  s.stage = bf ? size_t(s.KB) * BN * 128 : s.b_lo + size_t(BN) * 128;
   size_t o = size_t(SA) * s.stage;
   s.lists = o;
   o += size_t(kTqM) * kcap * 8;
@@ -417,23 +418,26 @@ __global__ void __launch_bounds__(ATM ? kTqThreadsAtm : kTqThreads, 1)
         if (item < 0) break;
         const long long nrows = it.re > it.rb ? it.re - it.rb : 0;
         const int nT = (int)((nrows + BN - 1) / BN);
+        const int kps = FLT ? KB : 1;  // K-blocks per stage
         for (int t = 0; t < nT && !*s_abort; ++t) {
-          for (int kb = 0; kb < KB; ++kb) {
+          for (int kb0 = 0; kb0 < KB; kb0 += kps) {
             const int s = seq % SA;
             bool ok = true;
             if (seq >= (uint32_t)SA)
               TQP(0, ok = mbar_wait(&empty[s], ((seq / SA) - 1) & 1, s_abort, &g_device_error));
             if (!ok) break;
             unsigned char* st = base + size_t(s) * L.stage;
-            mbar_arrive_expect_tx(&full[s], kStageTx);
-            const int x = kb * (FLT ? 64 : 32);
+            mbar_arrive_expect_tx(&full[s], FLT ? (uint32_t)(KB * BN * 128) : kStageTx);
             const int yb = (int)(it.rb + (long long)t * BN);
-            if (!ATM) {
-              tma_load_2d(st + L.a_hi, &maps.a_hi, x, it.a_row0, &full[s]);
-              tma_load_2d(st + L.a_lo, &maps.a_lo, x, it.a_row0, &full[s]);
+            for (int kb = kb0; kb < kb0 + kps; ++kb) {
+              const int x = kb * (FLT ? 64 : 32);
+              if (!ATM) {
+                tma_load_2d(st + L.a_hi, &maps.a_hi, x, it.a_row0, &full[s]);
+                tma_load_2d(st + L.a_lo, &maps.a_lo, x, it.a_row0, &full[s]);
+              }
+              tma_load_2d(st + L.b_hi + size_t(kb - kb0) * BN * 128, &maps.b_hi, x, yb, &full[s]);
+              if (!CONV && !FLT) tma_load_2d(st + L.b_lo, &maps.b_lo, x, yb, &full[s]);
             }
-            tma_load_2d(st + L.b_hi, &maps.b_hi, x, yb, &full[s]);
-            if (!CONV && !FLT) tma_load_2d(st + L.b_lo, &maps.b_lo, x, yb, &full[s]);
             ++seq;
           }
         }
@@ -469,7 +473,8 @@ __global__ void __launch_bounds__(ATM ? kTqThreadsAtm : kTqThreads, 1)
             TQP(1, mbar_wait(&acce[b], ((tt / NACC) - 1) & 1, s_abort, &g_device_error));
           tc_fence_after();
           const uint32_t dt = tmem + L.acc0 + b * BN;
-          for (int kb = 0; kb < KB; ++kb, ++seq) {
+          const int kps = FLT ? KB : 1;  // K-blocks per stage
+          for (int kb0 = 0; kb0 < KB; kb0 += kps, ++seq) {
             const int s = seq % SA;
             TQP(2, mbar_wait(CONV ? &conv[s] : &full[s], (seq / SA) & 1, s_abort, &g_device_error));
             tc_fence_after();
@@ -477,10 +482,12 @@ __global__ void __launch_bounds__(ATM ? kTqThreadsAtm : kTqThreads, 1)
 #ifdef MF_TC_PROFILE
             const long long _tm = clock64();
 #endif
+            for (int kb = kb0; kb < kb0 + kps; ++kb) {
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk) {
               const uint32_t off = kk * 32;  // 8 tf32 (or 16 fp16) of K per MMA
-              const uint64_t bh = desc_k_sw128(st + L.b_hi + off);
+              const uint64_t bh =
+                  desc_k_sw128(st + L.b_hi + (uint32_t)((kb - kb0) * BN * 128) + off);
               const uint64_t bl = desc_k_sw128(st + L.b_lo + off);
               if (FLT) {
                 // 16 fp16 of K = 8 columns of the query tile
@@ -499,6 +506,7 @@ __global__ void __launch_bounds__(ATM ? kTqThreadsAtm : kTqThreads, 1)
                 mma_tf32(dt, ah, bl, idesc, true);
                 mma_tf32(dt, al, bh, idesc, true);
               }
+            }
             }
             mma_commit(&empty[s]);
 #ifdef MF_TC_PROFILE
