@@ -577,6 +577,7 @@ FlatPlan plan_flat(int64_t nq, int64_t nb, int d, int k, int device, int tq) {
   c.take<float>((size_t)nq * max_splits * k);
   c.take<int64_t>((size_t)nq * max_splits * k);
   c.take<float>((size_t)nq * d);            // query tf32 residuals (tensor cores)
+  c.take<unsigned int>(nq);                 // pieces' shared k-th distances (tensor cores)
   p.bytes = c.used;
   return p;
 }
@@ -599,6 +600,7 @@ int run_flat_topk(int device, cudaStream_t stream, const float* xq, int64_t nq, 
   float* pd = c.take<float>((size_t)nq * max_splits * k);
   int64_t* pl = c.take<int64_t>((size_t)nq * max_splits * k);
   float* q_lo = c.take<float>((size_t)nq * d);
+  unsigned int* share = c.take<unsigned int>(nq);
   if (metric == MF_METRIC_L2) MF_TRY(launch_norms(xq, nq, d, qn, stream));
   ScanArgs a{};
   a.xq = xq;
@@ -625,8 +627,12 @@ int run_flat_topk(int device, cudaStream_t stream, const float* xq, int64_t nq, 
     const bool raw = tc_raw_queries(d, k);  // else the scan streams (xq, q_lo) tiles
     if (!raw) MF_TRY(launch_tf32_residual(xq, nq, d, q_lo, stream));
     // a query tile meets fewer runs than the widest: its other slots stay empty
-    if (p.splits > 1)
+    if (p.splits > 1) {
       MF_CUDA(cudaMemsetAsync(pl, 0xff, sizeof(int64_t) * (size_t)nq * p.splits * k, stream));
+      // the pieces of a query tile share their k-th distances (none yet)
+      MF_CUDA(cudaMemsetAsync(share, 0xff, sizeof(unsigned int) * (size_t)nq, stream));
+      a.share = share;
+    }
     MF_TRY(launch_tc_scan(a, metric, raw ? nullptr : q_lo, nq, xb_lo, nb, p.chunks, device,
                           stream));
   } else {

@@ -41,6 +41,12 @@ struct ScanArgs {
   // chunk c writes partial slot c - (q tiles_per_qt) / chunk_tiles
   int64_t chunk_tiles;
   int64_t tiles_per_qt;
+  // flat on tensor cores, a query tile cut into pieces: per query, the
+  // smallest k-th distance any piece has reached so far (order-preserving
+  // bits, all ones: none yet). Each piece publishes its own with atomicMin
+  // and filters by the others': any piece's k-th distance bounds the final
+  // k-th distance from above. Null: no sharing.
+  unsigned int* share;
   // IVF items
   const int2* items;      // (list, group)
   const int* item_total;  // device scalar

@@ -703,8 +703,11 @@ __global__ void __launch_bounds__(ATM ? kTqThreadsAtm : kTqThreads, 1)
     // lane mask) into their sorted lists, two rows at a time so the shuffles
     // of the two sorting networks overlap. Each merged row's lane clears its
     // count and lowers its threshold to min(new k-th key, bound).
+    // The merged rows' threads publish their new k-th distance when the
+    // pieces of a flat query tile share them (a.share; qrow: the calling
+    // thread's own query).
     auto merge_rows = [&](unsigned int who, int& cnt_reg, unsigned long long& thr_reg,
-                          unsigned long long bnd) {
+                          unsigned long long bnd, int qrow) {
       while (who) {
         const int s0 = __ffs(who) - 1;
         who &= who - 1;
@@ -739,10 +742,14 @@ __global__ void __launch_bounds__(ATM ? kTqThreadsAtm : kTqThreads, 1)
         if (lane == s0) {
           thr_reg = nk0 < bnd ? nk0 : bnd;
           cnt_reg = 0;
+          if (!FLT && a.share && nk0 != kEmptyKey)
+            atomicMin(a.share + qrow, (unsigned int)(nk0 >> 32));
         }
         if (lane == s1) {
           thr_reg = nk1 < bnd ? nk1 : bnd;
           cnt_reg = 0;
+          if (!FLT && a.share && nk1 != kEmptyKey)
+            atomicMin(a.share + qrow, (unsigned int)(nk1 >> 32));
         }
         __syncwarp();
       }
@@ -797,10 +804,23 @@ __global__ void __launch_bounds__(ATM ? kTqThreadsAtm : kTqThreads, 1)
       else if (valid && a.bound) bound = bound_key(a.bound[q]);
       unsigned long long thr = bound;
       int cnt = 0;
+      // the other pieces' k-th distance for this row's query, loaded one tile
+      // ahead of its use
+      unsigned int sh_pf = (!FLT && a.share && valid) ? __ldcg(a.share + q) : ~0u;
 
       for (int t = 0; t < nT; ++t, ++tt) {
         const int b = tt % NACC;
         const long long r0 = it.rb + (long long)t * BN;
+        if (!FLT && a.share) {  // flat searches only (never the filter scan)
+          if (sh_pf != ~0u) {
+            // every row with a distance <= that bound passes, as bound_key keeps it
+            const unsigned long long sk =
+                (static_cast<unsigned long long>(sh_pf) << 32) | 0xffffffffull;
+            if (sk < bound) bound = sk;
+            if (sk < thr) thr = sk;
+          }
+          sh_pf = valid ? __ldcg(a.share + q) : ~0u;
+        }
 #ifdef MF_TC_PROFILE
         const long long p_s0 = clock64();
 #endif
@@ -850,7 +870,7 @@ __global__ void __launch_bounds__(ATM ? kTqThreadsAtm : kTqThreads, 1)
           if (__any_sync(0xffffffffu, acc != 0)) ++p_nappend;
 #endif
           if (over) {
-            TQL(p_merge, merge_rows(over, cnt, thr, bound));
+            TQL(p_merge, merge_rows(over, cnt, thr, bound, q));
 #ifdef MF_TC_PROFILE
             p_nmerge += __popc(over);
 #endif
@@ -890,7 +910,7 @@ __global__ void __launch_bounds__(ATM ? kTqThreadsAtm : kTqThreads, 1)
       const long long p_o0 = clock64();
 #endif
       const unsigned int pending = __ballot_sync(0xffffffffu, cnt > 0);
-      if (pending) merge_rows(pending, cnt, thr, bound);
+      if (pending) merge_rows(pending, cnt, thr, bound, q);
       if (FLT) {
         // the kept slots of each row (a sorted prefix) and their count; rows
         // that kept none write nothing (their counts start at 0)
