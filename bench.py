@@ -365,6 +365,9 @@ def run_ours(args, cfg):
         # against the 16-bit rate (fp16 and bf16 run at the same dense rate;
         # the measured bf16 GEMM is the denominator)
         flops_pair = 2.0 * d if filtered else 6.0 * d
+        # the few-query pass reads each row once: its fp16 filter residual and
+        # residual norm (filter search), or its fp32 vector and norm
+        small_row_bytes = (2 * d + 4) if filtered else (4 * d + 4)
         tc_peak = bf16_peak if filtered else tf32_peak
         tflops = flops_pair * pairs / scan_s / 1e12 if scan_n else None
         gbs = alg_bytes / scan_s / 1e9 if scan_n else None
@@ -432,15 +435,18 @@ def run_ours(args, cfg):
                 # the few-query groups' pass (one 4-warp block per item): bound by
                 # reading those lists' rows (vector + norm) once
                 "small_groups": {
-                    "kernel": "few_scan_kernel (lists probed by at most 16 queries)",
+                    "kernel": ("few_scan_kernel<FLT> (fp16 filter rows, lists probed by at most "
+                               "16 queries)" if filtered else
+                               "few_scan_kernel (lists probed by at most 16 queries)"),
                     "rows_per_launch": small_rows,
-                    "bytes_per_launch": small_rows * (4 * d + 4),
+                    "bytes_per_row": small_row_bytes,
+                    "bytes_per_launch": small_rows * small_row_bytes,
                     "avg_launch_ms": round(small_ms / small_n, 4) if small_n else None,
-                    "achieved": (round(small_rows * (4 * d + 4) / (small_ms / small_n * 1e-3) / 1e9, 1)
-                                 if small_n else None),
+                    "achieved": (round(small_rows * small_row_bytes / (small_ms / small_n * 1e-3)
+                                       / 1e9, 1) if small_n else None),
                     "peak": hbm_peak,
                     "unit": "GB/s",
-                    "frac": (round(small_rows * (4 * d + 4) / (small_ms / small_n * 1e-3) / 1e9
+                    "frac": (round(small_rows * small_row_bytes / (small_ms / small_n * 1e-3) / 1e9
                                    / hbm_peak, 4) if small_n else None),
                 },
             },
