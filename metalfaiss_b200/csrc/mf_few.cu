@@ -13,11 +13,15 @@
 // the per-query bound when one is given.
 //
 // FLT (L2, the filter search): the rows are the filter bank's fp16 residuals
-// against the item's list centroid (scaled by the list's power of two; a row
-// is one 8-byte slice per lane), the queries s_q (q - c) in fp32, and each
-// pair's keys are the filter's upper bounds u = (Dc + e) + rn_x - 2 dot, with
-// the pair's query norm, bound and scales from a.pair_qn / pair_thr / pair_sc.
-// Only the rows are rounded (to fp16), so the filter's error bound covers them.
+// against the item's list centroid (scaled by the list's power of two), the
+// queries s_q (q - c) rounded to fp16, and the dot products come from the
+// tensor cores (mma.sync m16n8k16 with fp32 accumulation: 16 queries x 8 rows
+// per instruction), the arithmetic of the tcgen05 filter pass, so the pair's
+// error bound covers them. Each pair's keys are the filter's upper bounds
+// u = (Dc + e) + rn_x - 2 dot, with the pair's query norm, bound and scales
+// from a.pair_qn / pair_thr / pair_sc. A lane tests its 8 (query, row) bounds
+// against the thresholds; only queries with a candidate gather their 16 rows'
+// bounds to one lane each and take the per-query insertion above.
 #include <cuda_fp16.h>
 
 #include "mf_scan.cuh"
@@ -41,6 +45,20 @@ struct FewSmem {
     return queries(d) + size_t(kFewWarps) * kFewMax * (kFewK + 32) * 8;
   }
 };
+
+__device__ __forceinline__ uint32_t few_pack_f16x2(float lo, float hi) {
+  const __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+// c += A B for one m16n8k16 step: A 16 x 16 fp16 (four f16x2 registers per
+// lane), B 16 x 8 fp16 (two), C 16 x 8 fp32
+__device__ __forceinline__ void few_mma_f16(float (&c)[4], const uint32_t (&af)[4], uint2 b) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, "
+      "{%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};\n"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(af[0]), "r"(af[1]), "r"(af[2]), "r"(af[3]), "r"(b.x), "r"(b.y));
+}
 
 template <int METRIC, bool FLT>
 __global__ void __launch_bounds__(kFewWarps * 32) few_scan_kernel(const ScanArgs a) {
@@ -110,6 +128,32 @@ __global__ void __launch_bounds__(kFewWarps * 32) few_scan_kernel(const ScanArgs
 
     const float4* qv = qs + lane;  // this lane's column slice of each query
     const bool col_ok = lane < d4;
+    // offers query j one key per lane (kEmptyKey: none): the keys below the
+    // query's threshold go to its candidate buffer, which is merged into the
+    // query's list first when they would overflow it
+    auto insert = [&](int j, unsigned long long key) {
+      const unsigned long long tj = __shfl_sync(0xffffffffu, thr, j);
+      unsigned int m = __ballot_sync(0xffffffffu, key < tj);
+      if (m == 0u) return;
+      int nb = __shfl_sync(0xffffffffu, nbuf, j);
+      unsigned long long* buf = bufs + j * 32;
+      unsigned long long* list = lists + j * kFewK;
+      if (nb + __popc(m) > 32) {
+        const unsigned long long nk = merge_into_list<kFewK>(list, buf, nb, k, lane);
+        const unsigned long long bj = __shfl_sync(0xffffffffu, bnd, j);
+        const unsigned long long t2 = nk < bj ? nk : bj;
+        if (lane == j) thr = t2;
+        nb = 0;
+        m = __ballot_sync(0xffffffffu, key < t2);
+        if (m == 0u) {
+          if (lane == j) nbuf = 0;
+          return;
+        }
+      }
+      if ((m >> lane) & 1u) buf[nb + __popc(m & lanemask_lt())] = key;
+      if (lane == j) nbuf = nb + __popc(m);
+      __syncwarp();
+    };
     // rows r0 .. r0+15 (row i's column slice `lane` in xv[i]) against every query
     auto process = [&](const float4 (&xv)[kFewRows], long long r0) {
       const long long my_row = r0 + (lane >> 1);  // the row whose sum this lane ends with
@@ -127,53 +171,104 @@ __global__ void __launch_bounds__(kFewWarps * 32) few_scan_kernel(const ScanArgs
           p[i] = fmaf(xv[i].w, q4.w, t);
         }
         const float dot = warp_transpose_reduce16(p, lane);
-        const unsigned long long tj = __shfl_sync(0xffffffffu, thr, j);
-        const float dist = METRIC == MF_METRIC_L2
-                               ? l2_from_dot(s_qn[j], xn, FLT ? dot * s_sc[j] : dot)
-                               : -dot;
-        const unsigned long long key = rv ? make_key(dist, (unsigned int)my_row) : kEmptyKey;
-        unsigned int m = __ballot_sync(0xffffffffu, key < tj);
-        if (m == 0u) continue;
-        int nb = __shfl_sync(0xffffffffu, nbuf, j);
-        unsigned long long* buf = bufs + j * 32;
-        unsigned long long* list = lists + j * kFewK;
-        if (nb + __popc(m) > 32) {
-          const unsigned long long nk = merge_into_list<kFewK>(list, buf, nb, k, lane);
-          const unsigned long long bj = __shfl_sync(0xffffffffu, bnd, j);
-          const unsigned long long t2 = nk < bj ? nk : bj;
-          if (lane == j) thr = t2;
-          nb = 0;
-          m = __ballot_sync(0xffffffffu, key < t2);
-          if (m == 0u) {
-            if (lane == j) nbuf = 0;
-            continue;
-          }
-        }
-        if ((m >> lane) & 1u) buf[nb + __popc(m & lanemask_lt())] = key;
-        if (lane == j) nbuf = nb + __popc(m);
-        __syncwarp();
+        const float dist = METRIC == MF_METRIC_L2 ? l2_from_dot(s_qn[j], xn, dot) : -dot;
+        insert(j, rv ? make_key(dist, (unsigned int)my_row) : kEmptyKey);
       }
     };
-    if (FLT) {
-      // fp16 rows, 8 bytes (4 elements) per lane
+    if constexpr (FLT) {
+      // fp16 tensor-core products (mma.sync m16n8k16, fp32 accumulation). The
+      // item's queries, rounded to fp16 as the tensor-core filter rounds them,
+      // are the A operand (16 queries x 16 elements per K-step), 8 rows the B
+      // operand. In K-step s, lane (g, t) = (lane / 4, lane % 4) holds
+      // elements 16 s + 4 t .. 16 s + 4 t + 3 of queries g, g + 8 and of row
+      // g: both operands' K order is permuted alike, so the products are the
+      // rows' dot products, and a row's B fragment is one 8-byte load.
+      const unsigned int full = 0xffffffffu;
+      const int gq = lane >> 2, tq = lane & 3;
+      const int nks = (d + 15) >> 4;
+      uint32_t af[kFewMaxD / 16][4];
+#pragma unroll
+      for (int s = 0; s < kFewMaxD / 16; ++s) {
+        const int e0 = 16 * s + 4 * tq;
+        float4 lo = make_float4(0.f, 0.f, 0.f, 0.f), hi = lo;
+        if (e0 < d) {
+          if (gq < nq) lo = qs[gq * d4 + (e0 >> 2)];
+          if (gq + 8 < nq) hi = qs[(gq + 8) * d4 + (e0 >> 2)];
+        }
+        af[s][0] = few_pack_f16x2(lo.x, lo.y);
+        af[s][1] = few_pack_f16x2(hi.x, hi.y);
+        af[s][2] = few_pack_f16x2(lo.z, lo.w);
+        af[s][3] = few_pack_f16x2(hi.z, hi.w);
+      }
+      const bool vlo = gq < nq, vhi = gq + 8 < nq;
+      const float qn_lo = vlo ? s_qn[gq] : 0.f, sc_lo = vlo ? s_sc[gq] : 0.f;
+      const float qn_hi = vhi ? s_qn[gq + 8] : 0.f, sc_hi = vhi ? s_sc[gq + 8] : 0.f;
+      const uint2* hrows = reinterpret_cast<const uint2*>(a.xb);
+      // the row this lane gathers in the slow path (lanes 0..15: row r0 + lane)
+      const int src_t = (lane & 7) >> 1, nt_l = (lane >> 3) & 1, e_l = lane & 1;
       for (long long r0 = rb + (long long)warp * kFewRows; r0 < re;
            r0 += (long long)kFewWarps * kFewRows) {
-        uint2 hv[kFewRows];
+        uint2 bv[2][kFewMaxD / 16];
 #pragma unroll
-        for (int i = 0; i < kFewRows; ++i) {
-          const long long r = r0 + i;
-          hv[i] = (r < re && col_ok)
-                      ? reinterpret_cast<const uint2*>(a.xb)[(r * d >> 2) + lane]
-                      : make_uint2(0u, 0u);
-        }
-        float4 xv[kFewRows];
+        for (int nt = 0; nt < 2; ++nt) {
+          const long long r = r0 + 8 * nt + gq;
+          const uint2* rp = hrows + ((r * d) >> 2) + tq;
 #pragma unroll
-        for (int i = 0; i < kFewRows; ++i) {
-          const float2 lo = __half22float2(*reinterpret_cast<const __half2*>(&hv[i].x));
-          const float2 hi = __half22float2(*reinterpret_cast<const __half2*>(&hv[i].y));
-          xv[i] = make_float4(lo.x, lo.y, hi.x, hi.y);
+          for (int s = 0; s < kFewMaxD / 16; ++s)
+            bv[nt][s] = (r < re && 16 * s + 4 * tq < d) ? rp[4 * s] : make_uint2(0u, 0u);
         }
-        process(xv, r0);
+        float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+        for (int s = 0; s < kFewMaxD / 16; ++s) {
+          if (s < nks) {
+            few_mma_f16(acc[0], af[s], bv[0][s]);
+            few_mma_f16(acc[1], af[s], bv[1][s]);
+          }
+        }
+        // acc[nt][2 h + e] (query gq + 8 h, row r0 + 8 nt + 2 tq + e) becomes
+        // its upper bound u; does any of the lane's u pass its query's threshold?
+        const unsigned long long t0 = __shfl_sync(full, thr, gq);
+        const unsigned long long t1 = __shfl_sync(full, thr, gq + 8);
+        const unsigned long long tlo = vlo ? t0 : 0ull, thi = vhi ? t1 : 0ull;
+        bool plo = false, phi = false;
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const long long r = r0 + 8 * nt + 2 * tq + e;
+            const float xn = r < re ? a.xnorms[r] : 0.0f;
+            acc[nt][e] = l2_from_dot(qn_lo, xn, acc[nt][e] * sc_lo);
+            acc[nt][2 + e] = l2_from_dot(qn_hi, xn, acc[nt][2 + e] * sc_hi);
+            if (r < re) {
+              plo |= make_key(acc[nt][e], (unsigned int)r) < tlo;
+              phi |= make_key(acc[nt][2 + e], (unsigned int)r) < thi;
+            }
+          }
+        }
+        const unsigned int mlo = __ballot_sync(full, plo);
+        const unsigned int mhi = __ballot_sync(full, phi);
+        if ((mlo | mhi) == 0u) continue;
+        // the queries with a candidate: gather query j's 16 bounds to lanes
+        // 0..15 (lane i: row r0 + i) and offer them
+        unsigned int qm = 0u;
+#pragma unroll
+        for (int g = 0; g < 8; ++g) {
+          if ((mlo >> (4 * g)) & 0xfu) qm |= 1u << g;
+          if ((mhi >> (4 * g)) & 0xfu) qm |= 1u << (g + 8);
+        }
+        const long long rl = r0 + (lane & 15);
+        while (qm != 0u) {
+          const int j = __ffs(qm) - 1;
+          qm &= qm - 1u;
+          const int src = (j & 7) * 4 + src_t;
+          const bool h = j >= 8;
+          const float v00 = __shfl_sync(full, h ? acc[0][2] : acc[0][0], src);
+          const float v01 = __shfl_sync(full, h ? acc[0][3] : acc[0][1], src);
+          const float v10 = __shfl_sync(full, h ? acc[1][2] : acc[1][0], src);
+          const float v11 = __shfl_sync(full, h ? acc[1][3] : acc[1][1], src);
+          const float u = nt_l ? (e_l ? v11 : v10) : (e_l ? v01 : v00);
+          insert(j, (lane < 16 && rl < re) ? make_key(u, (unsigned int)rl) : kEmptyKey);
+        }
       }
     } else {
       for (long long r0 = rb + (long long)warp * kFewRows; r0 < re;
