@@ -53,15 +53,18 @@ __device__ __forceinline__ uint32_t few_pack_f16x2(float lo, float hi) {
 
 // c += A B for one m16n8k16 step: A 16 x 16 fp16 (four f16x2 registers per
 // lane), B 16 x 8 fp16 (two), C 16 x 8 fp32
-__device__ __forceinline__ void few_mma_f16(float (&c)[4], const uint32_t (&af)[4], uint2 b) {
+__device__ __forceinline__ void few_mma_f16(float (&c)[4], const uint32_t (&af)[4], uint32_t b0,
+                                            uint32_t b1) {
   asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, "
       "{%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};\n"
       : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-      : "r"(af[0]), "r"(af[1]), "r"(af[2]), "r"(af[3]), "r"(b.x), "r"(b.y));
+      : "r"(af[0]), "r"(af[1]), "r"(af[2]), "r"(af[3]), "r"(b0), "r"(b1));
 }
 
+// The fp16 form is held to 128 registers (four blocks per SM, no spills), so
+// that 16 warps per SM each have two 16-row steps of loads in flight.
 template <int METRIC, bool FLT>
-__global__ void __launch_bounds__(kFewWarps * 32) few_scan_kernel(const ScanArgs a) {
+__global__ void __launch_bounds__(kFewWarps * 32, FLT ? 4 : 1) few_scan_kernel(const ScanArgs a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -179,17 +182,19 @@ __global__ void __launch_bounds__(kFewWarps * 32) few_scan_kernel(const ScanArgs
       // fp16 tensor-core products (mma.sync m16n8k16, fp32 accumulation). The
       // item's queries, rounded to fp16 as the tensor-core filter rounds them,
       // are the A operand (16 queries x 16 elements per K-step), 8 rows the B
-      // operand. In K-step s, lane (g, t) = (lane / 4, lane % 4) holds
-      // elements 16 s + 4 t .. 16 s + 4 t + 3 of queries g, g + 8 and of row
-      // g: both operands' K order is permuted alike, so the products are the
-      // rows' dot products, and a row's B fragment is one 8-byte load.
+      // operand. In K-steps 2p and 2p + 1, lane (g, t) = (lane / 4, lane % 4)
+      // holds elements 32 p + 8 t .. + 3 and 32 p + 8 t + 4 .. + 7 of queries
+      // g, g + 8 and of row g: both operands' K order is permuted alike, so the
+      // products are the rows' dot products, and a row's B fragments for two
+      // K-steps are one 16-byte load. The next 16 rows (and their norms) are
+      // loaded before this step's products.
       const unsigned int full = 0xffffffffu;
       const int gq = lane >> 2, tq = lane & 3;
-      const int nks = (d + 15) >> 4;
+      const int nkp = (d + 31) >> 5;  // pairs of K-steps
       uint32_t af[kFewMaxD / 16][4];
 #pragma unroll
       for (int s = 0; s < kFewMaxD / 16; ++s) {
-        const int e0 = 16 * s + 4 * tq;
+        const int e0 = 32 * (s >> 1) + 8 * tq + 4 * (s & 1);
         float4 lo = make_float4(0.f, 0.f, 0.f, 0.f), hi = lo;
         if (e0 < d) {
           if (gq < nq) lo = qs[gq * d4 + (e0 >> 2)];
@@ -203,26 +208,42 @@ __global__ void __launch_bounds__(kFewWarps * 32) few_scan_kernel(const ScanArgs
       const bool vlo = gq < nq, vhi = gq + 8 < nq;
       const float qn_lo = vlo ? s_qn[gq] : 0.f, sc_lo = vlo ? s_sc[gq] : 0.f;
       const float qn_hi = vhi ? s_qn[gq + 8] : 0.f, sc_hi = vhi ? s_sc[gq + 8] : 0.f;
-      const uint2* hrows = reinterpret_cast<const uint2*>(a.xb);
-      // the row this lane gathers in the slow path (lanes 0..15: row r0 + lane)
-      const int src_t = (lane & 7) >> 1, nt_l = (lane >> 3) & 1, e_l = lane & 1;
-      for (long long r0 = rb + (long long)warp * kFewRows; r0 < re;
-           r0 += (long long)kFewWarps * kFewRows) {
-        uint2 bv[2][kFewMaxD / 16];
+      const uint4* hrows = reinterpret_cast<const uint4*>(a.xb);
+      // rows r0 + 8 nt + gq (B fragments) and the norms of rows r0 + 8 nt + 2 tq + e
+      auto load_step = [&](uint4 (&bv)[2][kFewMaxD / 32], float (&xn)[4], long long r0) {
 #pragma unroll
         for (int nt = 0; nt < 2; ++nt) {
           const long long r = r0 + 8 * nt + gq;
-          const uint2* rp = hrows + ((r * d) >> 2) + tq;
+          const uint4* rp = hrows + ((r * d) >> 3) + tq;
 #pragma unroll
-          for (int s = 0; s < kFewMaxD / 16; ++s)
-            bv[nt][s] = (r < re && 16 * s + 4 * tq < d) ? rp[4 * s] : make_uint2(0u, 0u);
+          for (int p = 0; p < kFewMaxD / 32; ++p)
+            bv[nt][p] = (r < re && 32 * p + 8 * tq < d) ? rp[4 * p] : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const long long rx = r0 + 8 * nt + 2 * tq + e;
+            xn[2 * nt + e] = rx < re ? a.xnorms[rx] : 0.0f;
+          }
         }
+      };
+      // the row this lane gathers in the slow path (lanes 0..15: row r0 + lane)
+      const int src_t = (lane & 7) >> 1, nt_l = (lane >> 3) & 1, e_l = lane & 1;
+      const long long rstep = (long long)kFewWarps * kFewRows;
+      uint4 bv[2][kFewMaxD / 32];
+      float xn[4];
+      load_step(bv, xn, rb + (long long)warp * kFewRows);
+      for (long long r0 = rb + (long long)warp * kFewRows; r0 < re; r0 += rstep) {
+        uint4 bn[2][kFewMaxD / 32];
+        float xnn[4];
+        load_step(bn, xnn, r0 + rstep);
         float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll
-        for (int s = 0; s < kFewMaxD / 16; ++s) {
-          if (s < nks) {
-            few_mma_f16(acc[0], af[s], bv[0][s]);
-            few_mma_f16(acc[1], af[s], bv[1][s]);
+        for (int p = 0; p < kFewMaxD / 32; ++p) {
+          if (p < nkp) {
+#pragma unroll
+            for (int nt = 0; nt < 2; ++nt) {
+              few_mma_f16(acc[nt], af[2 * p], bv[nt][p].x, bv[nt][p].y);
+              few_mma_f16(acc[nt], af[2 * p + 1], bv[nt][p].z, bv[nt][p].w);
+            }
           }
         }
         // acc[nt][2 h + e] (query gq + 8 h, row r0 + 8 nt + 2 tq + e) becomes
@@ -236,9 +257,8 @@ __global__ void __launch_bounds__(kFewWarps * 32) few_scan_kernel(const ScanArgs
 #pragma unroll
           for (int e = 0; e < 2; ++e) {
             const long long r = r0 + 8 * nt + 2 * tq + e;
-            const float xn = r < re ? a.xnorms[r] : 0.0f;
-            acc[nt][e] = l2_from_dot(qn_lo, xn, acc[nt][e] * sc_lo);
-            acc[nt][2 + e] = l2_from_dot(qn_hi, xn, acc[nt][2 + e] * sc_hi);
+            acc[nt][e] = l2_from_dot(qn_lo, xn[2 * nt + e], acc[nt][e] * sc_lo);
+            acc[nt][2 + e] = l2_from_dot(qn_hi, xn[2 * nt + e], acc[nt][2 + e] * sc_hi);
             if (r < re) {
               plo |= make_key(acc[nt][e], (unsigned int)r) < tlo;
               phi |= make_key(acc[nt][2 + e], (unsigned int)r) < thi;
@@ -247,28 +267,36 @@ __global__ void __launch_bounds__(kFewWarps * 32) few_scan_kernel(const ScanArgs
         }
         const unsigned int mlo = __ballot_sync(full, plo);
         const unsigned int mhi = __ballot_sync(full, phi);
-        if ((mlo | mhi) == 0u) continue;
-        // the queries with a candidate: gather query j's 16 bounds to lanes
-        // 0..15 (lane i: row r0 + i) and offer them
-        unsigned int qm = 0u;
+        if ((mlo | mhi) != 0u) {
+          // the queries with a candidate: gather query j's 16 bounds to lanes
+          // 0..15 (lane i: row r0 + i) and offer them
+          unsigned int qm = 0u;
 #pragma unroll
-        for (int g = 0; g < 8; ++g) {
-          if ((mlo >> (4 * g)) & 0xfu) qm |= 1u << g;
-          if ((mhi >> (4 * g)) & 0xfu) qm |= 1u << (g + 8);
+          for (int g = 0; g < 8; ++g) {
+            if ((mlo >> (4 * g)) & 0xfu) qm |= 1u << g;
+            if ((mhi >> (4 * g)) & 0xfu) qm |= 1u << (g + 8);
+          }
+          const long long rl = r0 + (lane & 15);
+          while (qm != 0u) {
+            const int j = __ffs(qm) - 1;
+            qm &= qm - 1u;
+            const int src = (j & 7) * 4 + src_t;
+            const bool h = j >= 8;
+            const float v00 = __shfl_sync(full, h ? acc[0][2] : acc[0][0], src);
+            const float v01 = __shfl_sync(full, h ? acc[0][3] : acc[0][1], src);
+            const float v10 = __shfl_sync(full, h ? acc[1][2] : acc[1][0], src);
+            const float v11 = __shfl_sync(full, h ? acc[1][3] : acc[1][1], src);
+            const float u = nt_l ? (e_l ? v11 : v10) : (e_l ? v01 : v00);
+            insert(j, (lane < 16 && rl < re) ? make_key(u, (unsigned int)rl) : kEmptyKey);
+          }
         }
-        const long long rl = r0 + (lane & 15);
-        while (qm != 0u) {
-          const int j = __ffs(qm) - 1;
-          qm &= qm - 1u;
-          const int src = (j & 7) * 4 + src_t;
-          const bool h = j >= 8;
-          const float v00 = __shfl_sync(full, h ? acc[0][2] : acc[0][0], src);
-          const float v01 = __shfl_sync(full, h ? acc[0][3] : acc[0][1], src);
-          const float v10 = __shfl_sync(full, h ? acc[1][2] : acc[1][0], src);
-          const float v11 = __shfl_sync(full, h ? acc[1][3] : acc[1][1], src);
-          const float u = nt_l ? (e_l ? v11 : v10) : (e_l ? v01 : v00);
-          insert(j, (lane < 16 && rl < re) ? make_key(u, (unsigned int)rl) : kEmptyKey);
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+#pragma unroll
+          for (int p = 0; p < kFewMaxD / 32; ++p) bv[nt][p] = bn[nt][p];
         }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) xn[i] = xnn[i];
       }
     } else {
       for (long long r0 = rb + (long long)warp * kFewRows; r0 < re;

@@ -4,6 +4,9 @@ mf_ivf_search_filtered) against
 the CPU oracle and against the exact 3xTF32 scan of the same index:
 
 * mixtures at d = 64, 96, 128 with k from 1 to 16 and nprobe from 1 to 32;
+* batches small enough that every list is probed by at most 16 queries (the
+  fp16 few-query pass alone), at d = 72 and 80 (not multiples of 32: lanes
+  past d carry zeros) and 128;
 * duplicated rows, so that more rows tie inside a pair's error window than its
   slots hold: the refinement must rescan those lists and stay exact;
 * lists holding fewer than k rows (padded results), data scaled by 1e3 and
@@ -65,6 +68,16 @@ def test_filter_equals_oracle_and_exact(cuda_device, d, k, nprobe):
     idx = _build(x, 128, seed=d)
     xq, _, _ = syn.mixture(700, d, 128, seed=d + k + 1, centres=cen)
     nat.filter_rescans(0, reset=True)
+    _check(idx, x, xq, nprobe, k)
+
+
+@pytest.mark.parametrize("d,k,nprobe", [(72, 7, 16), (80, 10, 8), (128, 16, 32)])
+def test_filter_few_query_lists(cuda_device, d, k, nprobe):
+    """16 queries: no list is probed by more than 16, so the few-query pass
+    scans every probed list."""
+    x, cen, _ = syn.mixture(30000, d, 256, seed=d + 5)
+    idx = _build(x, 256, seed=d + 5)
+    xq, _, _ = syn.mixture(16, d, 256, seed=d + 6, centres=cen)
     _check(idx, x, xq, nprobe, k)
 
 
