@@ -32,17 +32,18 @@ namespace mf {
 namespace {
 
 constexpr int kFewMax = 16;     // queries per item at most
-constexpr int kFewWarps = 4;    // warps per block, sharing one item
+constexpr int kFewWarps = 4;    // warps per block, sharing one item (general items)
+constexpr int kFewBoundRows = 256;  // items of at most this many rows: one warp each
 constexpr int kFewMaxD = 128;   // d at most: one 16-byte column slice per lane
 constexpr int kFewK = 32;       // list slots per query (k <= 32)
 constexpr int kFewRows = 16;    // rows per step
 
-// Dynamic shared memory of a block: the item's queries, then per warp the
-// query lists (kFewK keys) and candidate buffers (32 keys).
+// Dynamic shared memory of a block of `warps` warps: the item's queries, then
+// per warp the query lists (kFewK keys) and candidate buffers (32 keys).
 struct FewSmem {
   __host__ __device__ static size_t queries(int d) { return size_t(kFewMax) * d * 4; }
-  __host__ __device__ static size_t block(int d) {
-    return queries(d) + size_t(kFewWarps) * kFewMax * (kFewK + 32) * 8;
+  __host__ __device__ static size_t block(int d, int warps) {
+    return queries(d) + size_t(warps) * kFewMax * (kFewK + 32) * 8;
   }
 };
 
@@ -61,10 +62,13 @@ __device__ __forceinline__ void few_mma_f16(float (&c)[4], const uint32_t (&af)[
       : "r"(af[0]), "r"(af[1]), "r"(af[2]), "r"(af[3]), "r"(b0), "r"(b1));
 }
 
-// The fp16 form is held to 128 registers (four blocks per SM, no spills), so
-// that 16 warps per SM each have two 16-row steps of loads in flight.
-template <int METRIC, bool FLT>
-__global__ void __launch_bounds__(kFewWarps * 32, FLT ? 4 : 1) few_scan_kernel(const ScanArgs a) {
+// W warps per block share an item: 4 for general items; 1 for items of at
+// most kFewBoundRows rows (the bound pass's 128), which would leave four warps
+// two steps each between block barriers and cross-warp merges. The fp16 form
+// is held to 128 registers (four blocks per SM, no spills), so that 16 warps
+// per SM each have two 16-row steps of loads in flight.
+template <int METRIC, bool FLT, int W>
+__global__ void __launch_bounds__(W * 32, FLT ? 4 : 1) few_scan_kernel(const ScanArgs a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -110,7 +114,7 @@ __global__ void __launch_bounds__(kFewWarps * 32, FLT ? 4 : 1) few_scan_kernel(c
         s_bnd[threadIdx.x] = a.bound ? bound_key(a.bound[q]) : kEmptyKey;
       }
     }
-    for (int i = threadIdx.x; i < nq * d4; i += kFewWarps * 32) {
+    for (int i = threadIdx.x; i < nq * d4; i += W * 32) {
       const int j = i / d4;
       const int pr = a.pairs[pb + j];
       float4 v = reinterpret_cast<const float4*>(a.xq + (long long)(pr / a.P) * d)[i - j * d4];
@@ -227,7 +231,7 @@ __global__ void __launch_bounds__(kFewWarps * 32, FLT ? 4 : 1) few_scan_kernel(c
       };
       // the row this lane gathers in the slow path (lanes 0..15: row r0 + lane)
       const int src_t = (lane & 7) >> 1, nt_l = (lane >> 3) & 1, e_l = lane & 1;
-      const long long rstep = (long long)kFewWarps * kFewRows;
+      const long long rstep = (long long)W * kFewRows;
       uint4 bv[2][kFewMaxD / 32];
       float xn[4];
       load_step(bv, xn, rb + (long long)warp * kFewRows);
@@ -300,7 +304,7 @@ __global__ void __launch_bounds__(kFewWarps * 32, FLT ? 4 : 1) few_scan_kernel(c
       }
     } else {
       for (long long r0 = rb + (long long)warp * kFewRows; r0 < re;
-           r0 += (long long)kFewWarps * kFewRows) {
+           r0 += (long long)W * kFewRows) {
         // rows r0 .. r0+15: load i brings row r0+i across the warp (coalesced)
         float4 xv[kFewRows];
 #pragma unroll
@@ -319,9 +323,9 @@ __global__ void __launch_bounds__(kFewWarps * 32, FLT ? 4 : 1) few_scan_kernel(c
       if (nb > 0) merge_into_list<kFewK>(lists + j * kFewK, bufs + j * 32, nb, k, lane);
     }
     __syncthreads();
-    for (int j = warp; j < nq; j += kFewWarps) {
+    for (int j = warp; j < nq; j += W) {
       unsigned long long* list = lists + j * kFewK;
-      for (int v = 0; v < kFewWarps; ++v) {
+      for (int v = 0; v < W; ++v) {
         if (v == warp) continue;
         const unsigned long long* other = lists_all + v * kFewMax * (kFewK + 32) + j * kFewK;
         merge_into_list<kFewK>(list, other, k, k, lane);
@@ -373,24 +377,32 @@ int launch_few_scan(const ScanArgs& a, int metric, int64_t max_items, int device
   MF_CHECK(a.counter != nullptr && a.item_total != nullptr, MF_ERR_INVALID_ARGS,
            "few-query scan needs its items and a work counter");
   if (max_items <= 0) return MF_OK;
-  const size_t smem = FewSmem::block(a.d);
   const bool flt = a.pair_sq != nullptr;
   MF_CHECK(!flt || (metric == MF_METRIC_L2 && a.d <= kFewMaxD && a.d % 8 == 0 && a.pair_qn &&
                     a.pair_thr && a.pair_sc && a.pair_cnt && a.centroids),
            MF_ERR_INVALID_ARGS, "few-query filter scan: L2, d <= %d, per-pair arrays", kFewMaxD);
-  auto fn = flt ? few_scan_kernel<MF_METRIC_L2, true>
-                : (metric == MF_METRIC_L2 ? few_scan_kernel<MF_METRIC_L2, false>
-                                          : few_scan_kernel<MF_METRIC_INNER_PRODUCT, false>);
+  // items capped at a few rows (the bound pass): one warp per item
+  const int warps = (!flt && a.max_rows > 0 && a.max_rows <= kFewBoundRows) ? 1 : kFewWarps;
+  const size_t smem = FewSmem::block(a.d, warps);
+  void (*fn)(const ScanArgs);
+  if (flt)
+    fn = few_scan_kernel<MF_METRIC_L2, true, kFewWarps>;
+  else if (warps == 1)
+    fn = metric == MF_METRIC_L2 ? few_scan_kernel<MF_METRIC_L2, false, 1>
+                                : few_scan_kernel<MF_METRIC_INNER_PRODUCT, false, 1>;
+  else
+    fn = metric == MF_METRIC_L2 ? few_scan_kernel<MF_METRIC_L2, false, kFewWarps>
+                                : few_scan_kernel<MF_METRIC_INNER_PRODUCT, false, kFewWarps>;
   MF_CUDA(cudaFuncSetAttribute(reinterpret_cast<const void*>(fn),
                                cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   int per_sm = 0;
-  MF_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kFewWarps * 32, smem));
+  MF_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, warps * 32, smem));
   if (per_sm < 1) per_sm = 1;
   long long grid = (long long)num_sms(device) * per_sm;
   if (grid > max_items) grid = max_items;
   MF_CUDA(cudaMemsetAsync(a.counter, 0, sizeof(int), stream));
   ScopedTiming tm(a.max_rows > 0 ? "scan_topk_ivf_bound_small" : "scan_topk_ivf_small", stream);
-  fn<<<(unsigned int)grid, kFewWarps * 32, smem, stream>>>(a);
+  fn<<<(unsigned int)grid, warps * 32, smem, stream>>>(a);
   MF_LAUNCH_CHECK();
   return MF_OK;
 }
