@@ -354,7 +354,7 @@ def run_ours(args, cfg):
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_baseline(idx, xq, cfg, args.cpu_sample)
+        cpu = cpu_baseline(idx, xq, cfg, min(args.cpu_baseline_sample, nq))
 
     if rank == 0:
         hbm_peak, bf16_peak, peak_kind = measured_peaks()
@@ -535,7 +535,11 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", choices=sorted(CONFIGS), default="ivf20m")
+    # queries per reference-arm step (each step a bounded sample, so that the
+    # whole --steps K run ends within minutes)
     ap.add_argument("--cpu-sample", type=int, default=64)
+    # queries of this arm's cpu_baseline (about 10 s of host work)
+    ap.add_argument("--cpu-baseline-sample", type=int, default=6144)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
