@@ -1,5 +1,6 @@
 // Scan of IVF items that hold few queries (a list's last group of at most
-// kFewMax queries): one block of four warps per item, the warps taking
+// kFewMax queries): one block of four warps per item (one warp for items of at
+// most kFewBoundRows rows, such as the bound pass's), the warps taking
 // interleaved 16-row steps of the list, each with its own per-query top-k
 // lists, merged at the end of the item. The item's queries sit in shared
 // memory. Rows are read 16 at a time with
