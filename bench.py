@@ -1,30 +1,48 @@
 #!/usr/bin/env python
-"""IVFFlat search throughput on B200 (queries/sec), with the list-scan kernel's
-HBM roofline and a CPU baseline.
+"""Search-path throughput on B200, with the dominant kernel's roofline and a
+CPU baseline. One JSON line per run.
 
-Workload (default): IVFFlat L2, d=128, N=20M rows from a Gaussian mixture of
-16384 clusters (centres ~ N(0, 4 I), sigma = 1), nlist=16384 trained by seeded
-k-means on a 256*nlist subsample, Q=10000 queries from the same mixture,
-nprobe=32, k=10. One step = one search of the Q-query batch. The database
-(10.2 GB) is far larger than L2 (126 MB), so no flush is needed between steps.
+Workloads (--config; the default is the headline):
+* ivf20m (headline): IVFFlat L2, d=128, N=20M rows from a Gaussian mixture of
+  16384 clusters (centres ~ N(0, 4 I), sigma = 1), nlist=16384 trained by
+  seeded k-means on a 256*nlist subsample, Q=10000 queries from the same
+  mixture, nprobe=32, k=10. One step = one search of the Q-query batch. The
+  database (10.2 GB) is far larger than L2 (126 MB), so no flush is needed
+  between steps. ivf32k is the small IVF configuration (d=64, N=32768,
+  nlist=128, Q=16; --nprobe / --k give its nprobe x k sweep); ivf2m and ivf4m
+  are development sizes.
+* flat10m: FlatIndex INNER_PRODUCT, 10M unit rows x d=128, Q=10000 unit
+  queries, k=100. flat32k: FlatIndex L2, N=32768 x d=64 N(0,1), Q=16, k=10.
+  One step = one search of the batch.
+* kmeans5m: k-means on 5M points x d=256 from a 4096-cluster mixture, K=4096;
+  one step = one Lloyd iteration (assignment + centroid update); the
+  configuration runs 20.
 
-N>1 GPUs (one process per GPU, NCCL): the inverted lists are partitioned over
-the ranks by greedy LPT on list size; every rank runs the coarse step for all
-queries, scans its own lists, and the (Q, k) partial results are merged after
-an all-gather. The database is fixed as N grows (strong scaling).
+N>1 GPUs (one process per GPU, NCCL; ivf configurations): the inverted lists
+are partitioned over the ranks by greedy LPT on list size and each rank adds
+only the rows of its own lists; each rank runs the coarse step for its share
+of the queries and the probes are all-gathered, a MIN all-reduce shares each
+query's bound, every rank scans its own lists, and the (Q, k) partial results
+are merged after an all-gather. The database is fixed as N grows (strong
+scaling).
 
---impl reference times the reference algorithm on the host cores: the coarse
-step restated in numpy and the reference's list-scan kernel
-(python/metalfaiss/faissmlx/kernels/ivf_kernels.py:21-122) run as the oracle's C
-port, over a bounded sample of the same queries and index.
+--impl reference times the reference algorithm on the host cores and never
+loads this library: for ivf configurations the index is built with plain
+torch operations (the same data, training sample, initial centroids and Lloyd
+iterations as the library's build) and searched by the oracle's C port of the
+reference's IVF search (python/metalfaiss/index/ivf_flat_index.py:95-151 with
+the list scan of python/metalfaiss/faissmlx/kernels/ivf_kernels.py:21-122)
+over a bounded sample of queries; flat and k-means configurations run the
+numpy restatement of the reference (python/metalfaiss/indexflat.py:70-110,
+python/metalfaiss/clustering/any_clustering.py:62-124) on a sample.
 """
 from __future__ import annotations
 
 import argparse
+import importlib.util
 import json
 import os
 import statistics
-import subprocess
 import sys
 import threading
 import time
@@ -37,16 +55,26 @@ sys.path.insert(0, ROOT)
 
 CONFIGS = {
     # The headline workload: IVFFlat L2 at d=128, N=20M, nlist=16384, Q=10000, nprobe=32, k=10.
-    "ivf20m": dict(d=128, n=20_000_000, nlist=16384, nq=10_000, nprobe=32, k=10, niter=10),
-    # The small IVF configuration (d=64, N=32768, nlist=128, Q=16), for quick runs.
-    "ivf32k": dict(d=64, n=32768, nlist=128, nq=16, nprobe=8, k=10, niter=10),
+    "ivf20m": dict(kind="ivf", d=128, n=20_000_000, nlist=16384, nq=10_000, nprobe=32, k=10,
+                   niter=10),
+    # The small IVF configuration (d=64, N=32768, nlist=128, Q=16).
+    "ivf32k": dict(kind="ivf", d=64, n=32768, nlist=128, nq=16, nprobe=8, k=10, niter=10),
     # Mid-size for development runs.
-    "ivf2m": dict(d=128, n=2_000_000, nlist=2048, nq=10_000, nprobe=32, k=10, niter=5),
+    "ivf2m": dict(kind="ivf", d=128, n=2_000_000, nlist=2048, nq=10_000, nprobe=32, k=10,
+                  niter=5),
     # The headline's list count at a fifth of its rows (4 GB on the device with
     # residuals): lists probed by few queries dominate, as at full size; small
     # enough for multi-pass profiler captures.
-    "ivf4m": dict(d=128, n=4_000_000, nlist=16384, nq=10_000, nprobe=32, k=10, niter=5),
+    "ivf4m": dict(kind="ivf", d=128, n=4_000_000, nlist=16384, nq=10_000, nprobe=32, k=10,
+                  niter=5),
+    # Flat inner product over 10M unit rows, k=100.
+    "flat10m": dict(kind="flat", metric=0, d=128, n=10_000_000, nq=10_000, k=100, data="unit"),
+    # The small flat L2 configuration (N(0,1) rows).
+    "flat32k": dict(kind="flat", metric=1, d=64, n=32768, nq=16, k=10, data="gaussian"),
+    # k-means assignment + update, 5M x d=256, K=4096 (20 iterations).
+    "kmeans5m": dict(kind="kmeans", d=256, n=5_000_000, K=4096, niter=20),
 }
+METRIC_NAMES = {0: "INNER_PRODUCT", 1: "L2"}
 
 
 def log(*a):
@@ -63,11 +91,13 @@ def measured_peaks():
     return 6650.0, 1590.0, "fallback"
 
 
-def tf32_gemm_peak(device, n=8192, reps=10):
-    """Dense TF32 tensor-core throughput of cuBLAS on this GPU (TFLOP/s, best of
-    `reps` n^3 GEMMs, CUDA events): the denominator for the 3xTF32 scans."""
+def gemm_peak(device, tf32: bool, n=8192, reps=10):
+    """Dense fp32 GEMM throughput of cuBLAS on this GPU (TFLOP/s, best of
+    `reps` n^3 GEMMs, CUDA events): with tf32 the tensor-core TF32 rate (the
+    denominator of the 3xTF32 scans), without it the SIMT fp32 rate (the
+    denominator of the fp32 FMA scans)."""
     prev = torch.backends.cuda.matmul.allow_tf32
-    torch.backends.cuda.matmul.allow_tf32 = True
+    torch.backends.cuda.matmul.allow_tf32 = tf32
     try:
         a = torch.randn(n, n, device=device)
         b = torch.randn(n, n, device=device)
@@ -95,8 +125,8 @@ class ClockSampler:
     REASONS = (("hw_slowdown", 0x8), ("hw_thermal_slowdown", 0x40),
                ("sw_thermal_slowdown", 0x20), ("sw_power_cap", 0x4))
 
-    def __init__(self, cuda_index: int, period_s: float = 0.02):
-        self.cuda_index = cuda_index
+    def __init__(self, cuda_index: int, period_s: float = 0.005):
+        self.cuda_index = int(cuda_index)
         self.period = period_s
         self.samples = []
         self.err = None
@@ -154,7 +184,7 @@ class ClockSampler:
         sm = [m for m, _ in self.samples]
         reasons = sorted({nm for _, mask in self.samples for nm, bit in self.REASONS if mask & bit})
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": self.max_mhz, "reasons": reasons,
-                "samples": len(sm), "source": "NVML every 20 ms"}
+                "samples": len(sm), "source": f"NVML every {int(self.period * 1000)} ms"}
 
 
 # dram__bytes_read.sum + dram__bytes_write.sum of one launch of the dominant
@@ -174,14 +204,124 @@ TRAFFIC = {
 }
 
 
-def lpt_partition(sizes: np.ndarray, world: int) -> np.ndarray:
-    """Owner rank of each list: greedy longest-processing-time on list sizes."""
-    from metalfaiss_b200.sharding import lpt_partition as f
+def _synthetic():
+    """metalfaiss_b200/synthetic.py on its own (numpy + torch only): the
+    reference arm draws the same data without importing this library."""
+    spec = importlib.util.spec_from_file_location(
+        "_mf_bench_synthetic", os.path.join(ROOT, "metalfaiss_b200", "synthetic.py"))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
 
-    return f(sizes, world)
+
+def workload_config(name, cfg):
+    """The `config` object of the JSON line: the workload alone, the same in
+    both arms."""
+    if cfg["kind"] == "ivf":
+        big = cfg["n"] * cfg["d"] * 4 > 126e6
+        return {
+            "workload": f"{name}: IVFFlat L2 d={cfg['d']} N={cfg['n']} nlist={cfg['nlist']} "
+                        f"Q={cfg['nq']} nprobe={cfg['nprobe']} k={cfg['k']}",
+            "d": cfg["d"], "N": cfg["n"], "nlist": cfg["nlist"], "Q": cfg["nq"],
+            "nprobe": cfg["nprobe"], "k": cfg["k"],
+            "l2": ("database larger than L2 (126 MB); no flush" if big else
+                   "database fits in L2 (the configuration's own size); no flush"),
+        }
+    if cfg["kind"] == "flat":
+        big = cfg["n"] * cfg["d"] * 4 > 126e6
+        return {
+            "workload": f"{name}: FlatIndex {METRIC_NAMES[cfg['metric']]} d={cfg['d']} "
+                        f"N={cfg['n']} Q={cfg['nq']} k={cfg['k']}",
+            "d": cfg["d"], "N": cfg["n"], "Q": cfg["nq"], "k": cfg["k"],
+            "metric_type": METRIC_NAMES[cfg["metric"]],
+            "l2": ("database larger than L2 (126 MB); no flush" if big else
+                   "database fits in L2 (the configuration's own size); no flush"),
+        }
+    return {
+        "workload": f"{name}: k-means L2 N={cfg['n']} d={cfg['d']} K={cfg['K']} "
+                    f"({cfg['niter']} Lloyd iterations; one per step)",
+        "d": cfg["d"], "N": cfg["n"], "K": cfg["K"], "iterations": cfg["niter"],
+        "l2": "points (5.1 GB) larger than L2; no flush",
+    }
 
 
-def build_index(cfg, device, seed=1234):
+def metric_name(cfg):
+    if cfg["kind"] == "ivf":
+        return "IVFFlat queries/sec (list-scan HBM GB/s vs peak in roofline)"
+    if cfg["kind"] == "flat":
+        return "FlatIndex queries/sec (distance-GEMM tensor fraction in roofline)"
+    return "k-means Lloyd iterations/sec (assignment GEMM tensor fraction in roofline)"
+
+
+def host_threads():
+    return len(os.sched_getaffinity(0))
+
+
+class Timer:
+    """Warm-up, then K steps between CUDA events on the launching stream, with
+    a barrier and a synchronize on both sides and clocks sampled meanwhile;
+    the max over ranks."""
+
+    def __init__(self, device, world):
+        self.device, self.world = device, world
+
+    def run(self, step, steps, warmup):
+        import torch.distributed as dist
+
+        from metalfaiss_b200 import _native as nat
+
+        dev = self.device
+        for _ in range(warmup):
+            step()
+        torch.cuda.synchronize(dev)
+        if self.world > 1:
+            dist.barrier()
+        sampler = ClockSampler(dev.index)
+        sampler.start()
+        launches0 = nat.launch_count()
+        stream = torch.cuda.current_stream(dev)
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize(dev)
+        if self.world > 1:
+            dist.barrier()
+        ev0.record(stream)
+        for _ in range(steps):
+            step()
+        ev1.record(stream)
+        torch.cuda.synchronize(dev)
+        launches = nat.launch_count() - launches0
+        ms = ev0.elapsed_time(ev1)
+        clocks = sampler.stop()
+        return self.max_over_ranks(ms), clocks, launches
+
+    def max_over_ranks(self, ms):
+        if self.world == 1:
+            return ms
+        import torch.distributed as dist
+
+        t = torch.tensor([ms], device=self.device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def kernel_times(self, step, names, steps):
+        """Per-kernel CUDA-event totals over a separate run of a few steps
+        (the per-launch events stay out of the timed steps)."""
+        from metalfaiss_b200 import _native as nat
+
+        nat.timing_reset()
+        nat.timing_enable(True)
+        for _ in range(steps):
+            step()
+        torch.cuda.synchronize(self.device)
+        nat.timing_enable(False)
+        return {n: nat.timing_read(n) for n in names}
+
+
+# ------------------------------------------------------------------- IVF arm
+def build_index(cfg, device, seed=1234, rank=0, world=1):
+    """The benchmark's IVF index. With world > 1 every rank trains on the same
+    subsample (identical centroids) and adds only the rows of the lists it
+    owns (greedy LPT on the list sizes)."""
     from metalfaiss_b200 import IVFFlatIndex, synthetic as syn
     from metalfaiss_b200.clustering import ClusteringParameters
 
@@ -192,14 +332,20 @@ def build_index(cfg, device, seed=1234):
     idx.train(x)
     torch.cuda.synchronize(device)
     t1 = time.time()
-    idx.add(x)
+    owners = None
+    if world > 1:
+        from metalfaiss_b200.sharding import add_owned_rows
+
+        owners = add_owned_rows(idx, x, rank, world)
+    else:
+        idx.add(x)
     torch.cuda.synchronize(device)
     t2 = time.time()
     del x
     xq, _ = syn.torch_mixture(cfg["nq"], cfg["d"], cfg["nlist"], seed + 1, device, centres=centres)
     torch.cuda.empty_cache()
     log(f"[bench] built index: train {t1 - t0:.1f}s add {t2 - t1:.1f}s ntotal={idx.ntotal}")
-    return idx, xq
+    return idx, xq, owners
 
 
 # A list probed by at most this many queries is scanned by the few-query
@@ -207,8 +353,8 @@ def build_index(cfg, device, seed=1234):
 SMALL_GROUP = 16
 
 
-def scan_work(idx, probes_np, d, k):
-    """Work of one IVF scan over the probes (nq, P) of this index:
+def scan_work(sizes, probes_np, d, k):
+    """Work of one IVF scan over the probes (nq, P) of an index with these list sizes:
     * pairs: (query, row) distance evaluations in the tensor-core launch, i.e.
       over the lists probed by more than SMALL_GROUP queries (a list probed by
       at most SMALL_GROUP queries is scanned by the few-query kernel);
@@ -216,7 +362,6 @@ def scan_work(idx, probes_np, d, k):
       (vector + norm) read once, the query vectors read once and each
       (query, probe) pair's k partial results written once;
     * rows: distinct probed rows."""
-    sizes = idx.list_sizes()
     valid = probes_np[probes_np >= 0]
     probed = np.unique(valid)
     rows = int(sizes[probed].sum())
@@ -228,7 +373,7 @@ def scan_work(idx, probes_np, d, k):
     return pairs, rows * (4 * d + 4) + nq * d * 4 + nq * P * k * 12, rows, small_rows
 
 
-def filter_work(idx, probes_np, d, slots=20):
+def filter_work(sizes, probes_np, d, slots=20):
     """Work of the filter search's tensor-core pass over the probes (nq, P),
     over the lists probed by more than SMALL_GROUP queries (the others go to
     the exact few-query kernel, as in scan_work):
@@ -238,7 +383,6 @@ def filter_work(idx, probes_np, d, slots=20):
       the query rows and their list centroids read once per pair, and each
       pair's slots (value + row) written at most once;
     * rows: distinct rows of those lists."""
-    sizes = idx.list_sizes()
     valid = probes_np[probes_np >= 0]
     qpl = np.bincount(valid, minlength=len(sizes))
     big = qpl > SMALL_GROUP
@@ -248,81 +392,38 @@ def filter_work(idx, probes_np, d, slots=20):
     return pairs, rows * (2 * d + 4) + npairs * d * 8 + npairs * slots * 12, rows
 
 
-def run_ours(args, cfg):
-    import torch.distributed as dist
-
+def run_ivf(args, cfg, rank, world, device):
     from metalfaiss_b200 import _native as nat
     from metalfaiss_b200.sharding import ShardedIVF
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    device = torch.device("cuda", local)
-    if world > 1:
-        from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=device)
-    idx, xq = build_index(cfg, device)
+    idx, xq, owners = build_index(cfg, device, rank=rank, world=world)
     idx.nprobe = cfg["nprobe"]
-    k = cfg["k"]
-    nq = cfg["nq"]
-    d = cfg["d"]
-    sharded = ShardedIVF(idx, rank, world) if world > 1 else None
+    k, nq, d = cfg["k"], cfg["nq"], cfg["d"]
+    sharded = ShardedIVF(idx, rank, world, owners=owners) if world > 1 else None
     search = (lambda q: sharded.search(q, k)) if sharded else (lambda q: idx.search(q, k))
 
     # probes (for the roofline bytes): the coarse step of this batch
-    probes = idx.quantizer._search_padded(xq, min(cfg["nprobe"], cfg["nlist"]), map_ids=False).labels
-    local = sharded.local if sharded else idx
-    filtered = local._filter_ok(k)
+    probes = idx.quantizer._search_padded(xq, min(cfg["nprobe"], cfg["nlist"]),
+                                          map_ids=False).labels
+    mine = sharded.local if sharded else idx
+    filtered = mine._filter_ok(k)
     probes_np = probes.cpu().numpy()
-    pairs, alg_bytes, probed_rows, small_rows = scan_work(local, probes_np, d, k)
+    sizes = mine.list_sizes()
+    pairs, alg_bytes, probed_rows, small_rows = scan_work(sizes, probes_np, d, k)
     if filtered:
-        pairs, alg_bytes, probed_rows = filter_work(local, probes_np, d)
+        pairs, alg_bytes, probed_rows = filter_work(sizes, probes_np, d)
     logical_bytes = pairs * d * 4
-    tf32_peak = tf32_gemm_peak(device) if rank == 0 else None
+    tf32_peak = gemm_peak(device, tf32=True) if rank == 0 else None
 
-    nvtx = torch.cuda.nvtx
-    nvtx.range_push("warmup")
-    for _ in range(args.warmup):
-        search(xq)
-    nvtx.range_pop()
-    torch.cuda.synchronize(device)
-    if world > 1:
-        dist.barrier()
-    sampler = ClockSampler(local)
-    sampler.start()
-    launches0 = nat.launch_count()
-    stream = torch.cuda.current_stream(device)
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    torch.cuda.synchronize(device)
-    if world > 1:
-        dist.barrier()
-    nvtx.range_push("timed")
-    ev0.record(stream)
-    for _ in range(args.steps):
-        res = search(xq)
-    ev1.record(stream)
-    nvtx.range_pop()
-    torch.cuda.synchronize(device)
-    launches = nat.launch_count() - launches0
-    ms = ev0.elapsed_time(ev1)
-    clocks = sampler.stop()
-    # per-kernel CUDA-event times for the roofline, from a separate run of a few
-    # steps (the per-launch events stay out of the timed steps above)
-    nat.timing_reset()
-    nat.timing_enable(True)
-    for _ in range(min(args.steps, 20)):
-        search(xq)
-    torch.cuda.synchronize(device)
-    nat.timing_enable(False)
-    scan_ms, scan_n = nat.timing_read("scan_topk_ivf_filter" if filtered else "scan_topk_ivf")
-    small_ms, small_n = nat.timing_read("scan_topk_ivf_small")
-    refine_ms, refine_n = nat.timing_read("ivf_filter_refine")
-    rescans = nat.filter_rescans(local.device.index, reset=True)
-    if world > 1:
-        t = torch.tensor([ms], device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+    timer = Timer(device, world)
+    ms, clocks, launches = timer.run(lambda: search(xq), args.steps, args.warmup)
+    names = ["scan_topk_ivf_filter" if filtered else "scan_topk_ivf", "scan_topk_ivf_small",
+             "ivf_filter_refine"]
+    kt = timer.kernel_times(lambda: search(xq), names, min(args.steps, 20))
+    scan_ms, scan_n = kt[names[0]]
+    small_ms, small_n = kt["scan_topk_ivf_small"]
+    refine_ms, refine_n = kt["ivf_filter_refine"]
+    rescans = nat.filter_rescans(device.index, reset=True)
 
     # ---- end to end through the public API: pinned host queries in, results out
     # (every step copies its queries host -> device and its results device ->
@@ -330,31 +431,20 @@ def run_ours(args, cfg):
     xq_host = xq.cpu().pin_memory()
     D_host = torch.empty((nq, k), dtype=torch.float32).pin_memory()
     I_host = torch.empty((nq, k), dtype=torch.int64).pin_memory()
+
+    def e2e_step():
+        r = search(xq_host.to(device, non_blocking=True))
+        D_host.copy_(r.distances, non_blocking=True)
+        I_host.copy_(r.labels, non_blocking=True)
+
     e2e_steps = max(3, args.steps // 2)
-    for _ in range(2):
-        r = search(xq_host.to(device, non_blocking=True))
-        D_host.copy_(r.distances, non_blocking=True)
-        I_host.copy_(r.labels, non_blocking=True)
-    torch.cuda.synchronize(device)
-    if world > 1:
-        dist.barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(e2e_steps):
-        r = search(xq_host.to(device, non_blocking=True))
-        D_host.copy_(r.distances, non_blocking=True)
-        I_host.copy_(r.labels, non_blocking=True)
-    e1.record(stream)
-    torch.cuda.synchronize(device)
-    e2e_ms = e0.elapsed_time(e1)
-    if world > 1:
-        t = torch.tensor([e2e_ms], device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
+    e2e_ms, _, _ = timer.run(e2e_step, e2e_steps, 2)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_baseline(idx, xq, cfg, min(args.cpu_baseline_sample, nq))
+        cpu = cpu_baseline_ivf(idx.centroids.cpu().numpy(), idx.list_offsets.cpu().numpy(),
+                               idx._vecs, idx._ids, xq, cfg,
+                               min(args.cpu_baseline_sample, nq))
 
     if rank == 0:
         hbm_peak, bf16_peak, peak_kind = measured_peaks()
@@ -373,28 +463,13 @@ def run_ours(args, cfg):
         gbs = alg_bytes / scan_s / 1e9 if scan_n else None
         value = nq * args.steps / (ms * 1e-3)
         tkey = args.config + ("/filter" if filtered else "")
-        line = {
-            "metric": "IVFFlat queries/sec (list-scan HBM GB/s vs peak in roofline)",
-            "value": round(value, 1),
-            "unit": "queries/s",
-            "n_gpus": world,
-            "steps": args.steps,
-            "warmup": args.warmup,
-            "ms_per_step": round(ms / args.steps, 4),
-            "higher_is_better": True,
-            "scaling": "strong" if world > 1 else "weak",
-            "vs_baseline": None,
+        line = line_head(args, cfg, world, value, ms)
+        line.update({
             "dtype": "f32",
             "data": "synthetic (seeded Gaussian mixture, generated in HBM)",
-            "config": {
-                "workload": f"{args.config}: IVFFlat L2 d={d} N={cfg['n']} nlist={cfg['nlist']} "
-                            f"Q={nq} nprobe={cfg['nprobe']} k={k}",
-                "d": d, "N": cfg["n"], "nlist": cfg["nlist"], "Q": nq, "nprobe": cfg["nprobe"],
-                "k": k, "parallelism": f"list-sharded x{world}" if world > 1 else "single GPU",
-                "l2": "database (>=10 GB) larger than L2; no flush",
-                "logical_scan_bytes_per_step": logical_bytes,
-                "probed_rows_per_step": probed_rows,
-            },
+            "parallelism": f"list-sharded x{world}" if world > 1 else "single GPU",
+            "workload_facts": {"logical_scan_bytes_per_step": logical_bytes,
+                               "probed_rows_per_step_tensor_pass": probed_rows},
             "roofline": {
                 "bound": "tensor",
                 "kernel": ("tq_scan_kernel<FLT> (IVF list-major fp16 tcgen05 filter over "
@@ -432,8 +507,7 @@ def run_ours(args, cfg):
                     "avg_launch_ms": round(refine_ms / refine_n, 4) if refine_n else None,
                     "lists_rescanned": rescans,
                 } if filtered else None),
-                # the few-query groups' pass (one 4-warp block per item): bound by
-                # reading those lists' rows (vector + norm) once
+                # the few-query groups' pass: bound by reading those lists' rows once
                 "small_groups": {
                     "kernel": ("few_scan_kernel<FLT> (fp16 filter rows, lists probed by at most "
                                "16 queries)" if filtered else
@@ -459,71 +533,419 @@ def run_ours(args, cfg):
             "gpu_launches": int(launches),
             "clocks": clocks,
             "cpu_baseline": cpu,
-        }
+        })
         print(json.dumps(line), flush=True)
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
 
 
-def cpu_baseline(idx, xq, cfg, sample):
-    """The oracle's C port of the reference's IVF search on the host cores, over
-    `sample` queries of the same batch and the same index."""
+def line_head(args, cfg, world, value, ms):
+    return {
+        "metric": metric_name(cfg),
+        "value": round(value, 3),
+        "unit": "iterations/s" if cfg["kind"] == "kmeans" else "queries/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms / args.steps, 4),
+        "higher_is_better": True,
+        "scaling": "strong" if world > 1 else "weak",
+        "vs_baseline": None,
+        "config": workload_config(args.config, cfg),
+    }
+
+
+def cpu_baseline_ivf(cents, offsets, vecs, ids, xq, cfg, sample, threads=None):
+    """The oracle's C port of the reference's IVF search on the host cores,
+    over `sample` queries of the batch: the coarse step over all centroids,
+    then the exact top-k over the probed lists. Only the probed lists travel
+    to the host (vecs / ids stay on the device until then)."""
     from oracle import cport
 
     nprobe, k, d = cfg["nprobe"], cfg["k"], cfg["d"]
+    threads = threads or host_threads()
     q = xq[:sample, :d].cpu().numpy()
-    cents = idx.centroids.cpu().numpy()
-    probes = cport.coarse_probes(q, cents, nprobe)
-    # only the probed lists travel to the host
+    probes = cport.coarse_probes(q, cents[:, :d], nprobe, threads=threads)
     lists = np.unique(probes)
-    offsets = idx.list_offsets.cpu().numpy()
-    sub_off = np.zeros(idx.nlist + 1, np.int64)
-    sizes = np.zeros(idx.nlist, np.int64)
+    nlist = len(offsets) - 1
+    sizes = np.zeros(nlist, np.int64)
     sizes[lists] = offsets[lists + 1] - offsets[lists]
+    sub_off = np.zeros(nlist + 1, np.int64)
     np.cumsum(sizes, out=sub_off[1:])
-    vecs = np.empty((int(sub_off[-1]), d), np.float32)
-    ids = np.empty(int(sub_off[-1]), np.int64)
+    hv = np.empty((int(sub_off[-1]), d), np.float32)
+    hi = np.empty(int(sub_off[-1]), np.int64)
     for l in lists:
         a, b = int(offsets[l]), int(offsets[l + 1])
-        vecs[sub_off[l]:sub_off[l + 1]] = idx._vecs[a:b, :d].cpu().numpy()
-        ids[sub_off[l]:sub_off[l + 1]] = idx._ids[a:b].cpu().numpy()
-    threads = len(os.sched_getaffinity(0))
+        hv[sub_off[l]:sub_off[l + 1]] = vecs[a:b, :d].cpu().numpy()
+        hi[sub_off[l]:sub_off[l + 1]] = ids[a:b].cpu().numpy()
     t0 = time.perf_counter()
-    cport.ivf_search(q, cents, sub_off, vecs, ids, nprobe, k, threads=threads)
+    cport.ivf_search(q, cents[:, :d], sub_off, hv, hi, nprobe, k, threads=threads)
     dt = time.perf_counter() - t0
     return {"value": round(sample / dt, 2), "unit": "queries/s", "cores": threads, "kind": "port",
             "sample": f"{sample} of the {cfg['nq']} queries (coarse + scan + top-k), same index"}
 
 
+def _torch_assign(x, c, chunk=1 << 17):
+    """argmin_j (|x|^2 + |c_j|^2 - 2 x.c_j) per row, fp32 (TF32 off), in chunks."""
+    cn = (c * c).sum(1)
+    out = torch.empty(x.shape[0], dtype=torch.int64, device=x.device)
+    for s in range(0, x.shape[0], chunk):
+        xs = x[s:s + chunk]
+        dist = (xs * xs).sum(1, keepdim=True) + cn[None, :]
+        dist.addmm_(xs, c.t(), alpha=-2.0)
+        out[s:s + chunk] = dist.argmin(1)
+    return out
+
+
+def _torch_update(x, labels, c, chunk=1 << 20):
+    """Masked mean per cluster in fp64; an empty cluster keeps its centroid."""
+    K = c.shape[0]
+    sums = torch.zeros((K, x.shape[1]), dtype=torch.float64, device=x.device)
+    for s in range(0, x.shape[0], chunk):
+        sums.index_add_(0, labels[s:s + chunk], x[s:s + chunk].double())
+    counts = torch.bincount(labels, minlength=K)
+    nz = counts > 0
+    out = c.clone()
+    out[nz] = (sums[nz] / counts[nz, None].double()).float()
+    return out
+
+
+def reference_ivf_index(cfg, device, seed=1234):
+    """The benchmark's IVF index built with plain torch operations (fp32
+    distances with TF32 off, fp64 sums), never this library: the same
+    mixture, the same 256-per-list training subsample and seeded initial
+    centroids as the library's build, the same number of Lloyd iterations,
+    then every row assigned to its nearest centroid and the rows grouped by
+    list in input order (python/metalfaiss/index/ivf_flat_index.py:74-93)."""
+    syn = _synthetic()
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        n, d, nlist = cfg["n"], cfg["d"], cfg["nlist"]
+        x, centres = syn.torch_mixture(n, d, nlist, seed, device)
+        cap = 256 * nlist
+        xt = x
+        if n > cap:
+            perm = np.random.Generator(np.random.PCG64(seed + 1)).permutation(n)[:cap]
+            xt = x.index_select(0, torch.from_numpy(np.sort(perm)).to(device))
+        init = np.random.Generator(np.random.PCG64(seed)).permutation(xt.shape[0])[:nlist]
+        c = xt.index_select(0, torch.from_numpy(init).to(device)).contiguous()
+        for _ in range(cfg["niter"]):
+            c = _torch_update(xt, _torch_assign(xt, c), c)
+        del xt
+        lab = _torch_assign(x, c)
+        order = torch.argsort(lab, stable=True)
+        counts = torch.bincount(lab, minlength=nlist)
+        offsets = torch.zeros(nlist + 1, dtype=torch.int64, device=device)
+        offsets[1:] = torch.cumsum(counts, 0)
+        vecs = x.index_select(0, order)
+        del x
+        xq, _ = syn.torch_mixture(cfg["nq"], d, nlist, seed + 1, device, centres=centres)
+        return c.cpu().numpy(), offsets.cpu().numpy(), vecs, order, xq
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+
+
+def run_reference_ivf(args, cfg, device):
+    t0 = time.time()
+    cents, offsets, vecs, ids, xq = reference_ivf_index(cfg, device)
+    torch.cuda.synchronize(device)
+    log(f"[bench] reference arm: index built with torch ops in {time.time() - t0:.1f}s")
+    threads = host_threads()
+    sample = min(args.cpu_sample, cfg["nq"])
+    for _ in range(args.warmup):
+        cpu_baseline_ivf(cents, offsets, vecs, ids, xq, cfg, max(4, sample // 8), threads)
+    vals = [cpu_baseline_ivf(cents, offsets, vecs, ids, xq, cfg, sample, threads)
+            for _ in range(args.steps)]
+    v = statistics.median(r["value"] for r in vals)
+    return v, vals[0], sample / v * 1000.0, ("port: the oracle's C port of the reference IVF "
+                                             "search; index built with plain torch operations")
+
+
+# ------------------------------------------------------------------ flat arm
+def flat_data(cfg, device):
+    syn = _synthetic()
+    if cfg["data"] == "unit":
+        return syn.torch_unit_rows(cfg["n"], cfg["d"], 41, device), \
+            syn.torch_unit_rows(cfg["nq"], cfg["d"], 42, device)
+    return syn.torch_gaussian(cfg["n"], cfg["d"], 1, device), \
+        syn.torch_gaussian(cfg["nq"], cfg["d"], 2, device)
+
+
+def run_flat(args, cfg, rank, world, device):
+    from metalfaiss_b200 import FlatIndex, MetricType
+    from metalfaiss_b200 import _native as nat
+    from metalfaiss_b200.sharding import ShardedFlat
+
+    xb, xq = flat_data(cfg, device)
+    n, d, nq, k, metric = cfg["n"], cfg["d"], cfg["nq"], cfg["k"], cfg["metric"]
+    idx = FlatIndex(d, MetricType(metric), device=device)
+    if world > 1:
+        from metalfaiss_b200.sharding import row_shard
+
+        b, e = row_shard(n, rank, world)
+        idx.add(xb[b:e], torch.arange(b, e, dtype=torch.int64, device=device))
+        sharded = ShardedFlat(idx, rank, world, local=True)
+        search = lambda q: sharded.search(q, k)  # noqa: E731
+    else:
+        idx.add(xb)
+        search = lambda q: idx.search(q, k)  # noqa: E731
+    del xb
+    torch.cuda.empty_cache()
+    nloc = idx.ntotal
+    tc = nat.load().mf_flat_engine(metric, d, k, nloc, 1) == 1
+    peak = gemm_peak(device, tf32=tc) if rank == 0 else None
+    timer = Timer(device, world)
+    ms, clocks, launches = timer.run(lambda: search(xq), args.steps, args.warmup)
+    kt = timer.kernel_times(lambda: search(xq), ["scan_topk_flat", "merge"], min(args.steps, 10))
+    scan_ms, scan_n = kt["scan_topk_flat"]
+
+    xq_host = xq.cpu().pin_memory()
+    D_host = torch.empty((nq, k), dtype=torch.float32).pin_memory()
+    I_host = torch.empty((nq, k), dtype=torch.int64).pin_memory()
+
+    def e2e_step():
+        r = search(xq_host.to(device, non_blocking=True))
+        D_host.copy_(r.distances, non_blocking=True)
+        I_host.copy_(r.labels, non_blocking=True)
+
+    e2e_steps = max(3, args.steps // 2)
+    e2e_ms, _, _ = timer.run(e2e_step, e2e_steps, 2)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline_flat(idx.xb, xq, cfg, args.flat_cpu_sample)
+    if rank == 0:
+        hbm_peak, _, peak_kind = measured_peaks()
+        avg = scan_ms / max(scan_n, 1)
+        # useful work of one launch: 2 d flops per (query, row) pair, computed
+        # as three tf32 products on the tensor cores (6 d) or 2 d fp32 FMA flops
+        pairs = nq * nloc
+        flops = (6.0 if tc else 2.0) * d * pairs
+        ach = flops / (avg * 1e-3) / 1e12 if scan_n else None
+        line = line_head(args, cfg, world, nq * args.steps / (ms * 1e-3), ms)
+        line.update({
+            "dtype": "f32",
+            "data": "synthetic (seeded, generated in HBM)",
+            "parallelism": f"row-sharded x{world}" if world > 1 else "single GPU",
+            "roofline": {
+                "bound": "tensor" if tc else "fp32 FMA",
+                "kernel": ("tq_scan_kernel (flat 3xTF32 tcgen05 distance tiles + fused top-k)"
+                           if tc else "scan_kernel (flat SIMT fp32 distance tiles + fused "
+                                      "warp top-k)"),
+                "achieved": round(ach, 2) if ach else None,
+                "peak": round(peak, 1),
+                "unit": "TFLOP/s",
+                "frac": round(ach / peak, 4) if ach else None,
+                "peak_kind": ("cuBLAS TF32 GEMM 8192^3 measured in this run (3xTF32 counts "
+                              "three products per useful one)" if tc else
+                              "cuBLAS fp32 SGEMM (TF32 off) 8192^3 measured in this run"),
+                "algorithmic_flops_per_launch": int(flops),
+                "useful_tflops": round(2.0 * d * pairs / (avg * 1e-3) / 1e12, 2) if scan_n else None,
+                "avg_launch_ms": round(avg, 4),
+                "launches_per_step": round(scan_n / max(1, min(args.steps, 10)), 2),
+                "hbm": {"database_bytes": int(nloc * d * 4 * (2 if tc else 1)),
+                        "peak": hbm_peak, "peak_kind": f"{peak_kind} hbm_gbs"},
+                "traffic": None,
+            },
+            "e2e": {"value": round(nq * e2e_steps / (e2e_ms * 1e-3), 1), "unit": "queries/s",
+                    "h2d_bytes_per_step": int(nq * d * 4), "d2h_bytes_per_step": int(nq * k * 12)},
+            "gpu_launches": int(launches),
+            "clocks": clocks,
+            "cpu_baseline": cpu,
+        })
+        print(json.dumps(line), flush=True)
+
+
+def cpu_baseline_flat(xb, xq, cfg, sample, xb_host=None):
+    """The numpy restatement of FlatIndex.search (BLAS distances, full stable
+    argsort per row, as python/metalfaiss/indexflat.py:88-110 with
+    python/metalfaiss/utils/sorting.py:39-87 does) over `sample` queries."""
+    from oracle import oracle
+
+    d = cfg["d"]
+    xbh = xb_host if xb_host is not None else xb[:, :d].cpu().numpy()
+    q = xq[:sample, :d].cpu().numpy()
+    t0 = time.perf_counter()
+    oracle.flat_search(q, xbh, cfg["k"], cfg["metric"])
+    dt = time.perf_counter() - t0
+    return {"value": round(sample / dt, 4), "unit": "queries/s", "cores": host_threads(),
+            "kind": "port", "sample": f"{sample} of the {cfg['nq']} queries, full database "
+                                      f"(numpy BLAS threads for the distances; the sort is "
+                                      f"single-threaded)"}
+
+
+def run_reference_flat(args, cfg, device):
+    xb, xq = flat_data(cfg, device)
+    xbh = xb[:, :cfg["d"]].cpu().numpy()
+    del xb
+    sample = min(args.flat_cpu_sample, cfg["nq"])
+    for _ in range(min(args.warmup, 1)):
+        cpu_baseline_flat(None, xq, cfg, sample, xbh)
+    vals = [cpu_baseline_flat(None, xq, cfg, sample, xbh) for _ in range(args.steps)]
+    v = statistics.median(r["value"] for r in vals)
+    return v, vals[0], sample / v * 1000.0, "port: numpy restatement of FlatIndex.search"
+
+
+# ---------------------------------------------------------------- k-means arm
+def kmeans_data(cfg, device):
+    syn = _synthetic()
+    x, _ = syn.torch_mixture(cfg["n"], cfg["d"], cfg["K"], 77, device)
+    return x
+
+
+def run_kmeans(args, cfg, rank, world, device):
+    from metalfaiss_b200 import _native as nat
+    from metalfaiss_b200.clustering import (ClusteringParameters, assign, compute_norms,
+                                            init_centroids, kmeans_clustering, update)
+
+    n, d, K = cfg["n"], cfg["d"], cfg["K"]
+    x = kmeans_data(cfg, device)
+    c = init_centroids(x, K, 77)
+    cache = nat.Workspace(device)
+
+    def step():
+        labels, _ = assign(x, c, compute_norms(c), cache)
+        update(x, labels, c, cache)
+
+    tc = nat.load().mf_flat_engine(1, d, 1, K, 1) == 1
+    peak = gemm_peak(device, tf32=tc)
+    timer = Timer(device, 1)
+    ms, clocks, launches = timer.run(step, args.steps, args.warmup)
+    kt = timer.kernel_times(step, ["scan_topk_flat"], min(args.steps, 5))
+    scan_ms, scan_n = kt["scan_topk_flat"]
+    # end to end through the public API: the points from pinned host memory,
+    # kmeans_clustering over `steps` iterations, the centroids back to the host
+    xh = x[:, :d].cpu().pin_memory()
+    del x
+    torch.cuda.empty_cache()
+    params = ClusteringParameters(niter=args.steps, seed=77, max_points_per_centroid=0)
+    torch.cuda.synchronize(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    cents = kmeans_clustering(xh, d, K, params, device=device).cpu()
+    e1.record()
+    torch.cuda.synchronize(device)
+    e2e_ms = e0.elapsed_time(e1)
+    cpu = None if args.no_cpu_baseline else cpu_baseline_kmeans(xh.numpy(), cfg,
+                                                                 args.kmeans_cpu_sample)
+    hbm_peak, _, peak_kind = measured_peaks()
+    avg = scan_ms / max(scan_n, 1)
+    flops = (6.0 if tc else 2.0) * d * n * K
+    ach = flops / (avg * 1e-3) / 1e12 if scan_n else None
+    line = line_head(args, cfg, 1, args.steps / (ms * 1e-3), ms)
+    line.update({
+        "dtype": "f32",
+        "data": "synthetic (seeded Gaussian mixture, generated in HBM)",
+        "parallelism": "single GPU",
+        "roofline": {
+            "bound": "tensor" if tc else "fp32 FMA",
+            "kernel": ("tq_scan_kernel (assignment: 3xTF32 tcgen05 distance tiles + fused "
+                       "argmin, k=1)" if tc else "scan_kernel (assignment, SIMT fp32)"),
+            "achieved": round(ach, 2) if ach else None,
+            "peak": round(peak, 1),
+            "unit": "TFLOP/s",
+            "frac": round(ach / peak, 4) if ach else None,
+            "peak_kind": "cuBLAS TF32 GEMM 8192^3 measured in this run (3xTF32 counts three "
+                         "products per useful one)" if tc else "cuBLAS SGEMM measured",
+            "algorithmic_flops_per_launch": int(flops),
+            "useful_tflops": round(2.0 * d * n * K / (avg * 1e-3) / 1e12, 2) if scan_n else None,
+            "avg_launch_ms": round(avg, 4),
+            "update_ms": round(ms / args.steps - avg, 4),
+            "traffic": None,
+            "hbm": {"points_bytes": n * d * 4, "peak": hbm_peak,
+                    "peak_kind": f"{peak_kind} hbm_gbs"},
+        },
+        "e2e": {"value": round(args.steps / (e2e_ms * 1e-3), 3), "unit": "iterations/s",
+                "h2d_bytes_per_step": int(n * d * 4 / args.steps),
+                "d2h_bytes_per_step": int(K * d * 4 / args.steps),
+                "note": "kmeans_clustering from pinned host points: one copy in, `steps` "
+                        "iterations, the centroids out"},
+        "gpu_launches": int(launches),
+        "clocks": clocks,
+        "cpu_baseline": cpu,
+    })
+    print(json.dumps(line), flush=True)
+
+
+def cpu_baseline_kmeans(xh, cfg, sample, seed=5):
+    """One Lloyd iteration of the numpy restatement (fp32 BLAS distances by
+    norm expansion, argmin, fp64 masked mean; an empty cluster keeps its
+    centroid: python/metalfaiss/clustering/any_clustering.py:105-120) over
+    `sample` points; iterations/s extrapolated to all N points."""
+    from oracle import oracle
+
+    n, K = cfg["n"], cfg["K"]
+    rng = np.random.Generator(np.random.PCG64(seed))
+    pts = np.asarray(xh[np.sort(rng.choice(n, sample, replace=False))], np.float32)
+    c = np.asarray(xh[:K], np.float32)
+    t0 = time.perf_counter()
+    lab = np.argmin(oracle.pairwise_l2sqr_f32(pts, c), axis=1)
+    oracle.kmeans_update(pts, lab, c)
+    dt = time.perf_counter() - t0
+    return {"value": round(sample / (n * dt), 6), "unit": "iterations/s", "cores": host_threads(),
+            "kind": "port", "sample": f"one iteration over {sample} of the {n} points, "
+                                      f"extrapolated to all (numpy BLAS threads)"}
+
+
+def run_reference_kmeans(args, cfg, device):
+    x = kmeans_data(cfg, device)
+    xh = x[:, :cfg["d"]].cpu().numpy()
+    del x
+    vals = [cpu_baseline_kmeans(xh, cfg, args.kmeans_cpu_sample, seed=5 + i)
+            for i in range(args.steps)]
+    v = statistics.median(r["value"] for r in vals)
+    return v, vals[0], 1000.0 / v, "port: numpy restatement of the k-means iteration"
+
+
+# ------------------------------------------------------------------ dispatch
+def run_ours(args, cfg):
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=device)
+    try:
+        if cfg["kind"] == "ivf":
+            run_ivf(args, cfg, rank, world, device)
+        elif cfg["kind"] == "flat":
+            run_flat(args, cfg, rank, world, device)
+        else:
+            if world > 1:
+                raise SystemExit("kmeans5m runs on one GPU")
+            run_kmeans(args, cfg, rank, world, device)
+    finally:
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+
+
 def run_reference(args, cfg):
-    """Reference arm: rank 0 only; times the CPU implementation of the path."""
+    """Reference arm: rank 0 only; times the CPU implementation of the path.
+    This library is never loaded here."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     device = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
     torch.cuda.set_device(device)
-    idx, xq = build_index(cfg, device)
-    idx.nprobe = cfg["nprobe"]
-    for _ in range(args.warmup):
-        cpu_baseline(idx, xq, cfg, max(4, args.cpu_sample // 8))
-    vals = []
-    for _ in range(args.steps):
-        vals.append(cpu_baseline(idx, xq, cfg, args.cpu_sample))
-    v = statistics.median(r["value"] for r in vals)
-    base = vals[0]
+    fn = {"ivf": run_reference_ivf, "flat": run_reference_flat,
+          "kmeans": run_reference_kmeans}[cfg["kind"]]
+    v, base, ms_step, kind = fn(args, cfg, device)
+    unit = "iterations/s" if cfg["kind"] == "kmeans" else "queries/s"
     line = {
         "impl": "reference",
-        "metric": "IVFFlat queries/sec (list-scan HBM GB/s vs peak in roofline)",
-        "value": v, "unit": "queries/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(1000.0 * args.cpu_sample / v, 3), "higher_is_better": True,
+        "metric": metric_name(cfg),
+        "value": v, "unit": unit, "n_gpus": int(os.environ.get("WORLD_SIZE", "1")),
+        "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms_step, 3), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic (seeded Gaussian mixture)",
-        "config": {"workload": f"{args.config}: IVFFlat L2 d={cfg['d']} N={cfg['n']} nlist={cfg['nlist']} "
-                               f"Q={cfg['nq']} nprobe={cfg['nprobe']} k={cfg['k']}"},
-        "cpu_baseline": {"value": v, "unit": "queries/s", "cores": base["cores"], "kind": base["kind"],
-                         "sample": base["sample"]},
-        "e2e": {"value": v, "unit": "queries/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "data": "synthetic (seeded, the same draws as this arm's counterpart)",
+        "config": workload_config(args.config, cfg),
+        "cpu_baseline": {"value": v, "unit": unit, "cores": base["cores"], "kind": base["kind"],
+                         "sample": base["sample"], "what": kind},
+        "e2e": {"value": v, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
@@ -535,16 +957,26 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", choices=sorted(CONFIGS), default="ivf20m")
+    ap.add_argument("--nprobe", type=int, default=None, help="override (ivf configurations)")
+    ap.add_argument("--k", type=int, default=None, help="override")
     # queries per reference-arm step (each step a bounded sample, so that the
     # whole --steps K run ends within minutes)
     ap.add_argument("--cpu-sample", type=int, default=64)
-    # queries of this arm's cpu_baseline (about 10 s of host work)
+    # queries of the ivf arm's cpu_baseline (about 10 s of host work)
     ap.add_argument("--cpu-baseline-sample", type=int, default=6144)
+    # queries of the flat CPU baseline (a full-row argsort each)
+    ap.add_argument("--flat-cpu-sample", type=int, default=2)
+    # points of the k-means CPU baseline's iteration
+    ap.add_argument("--kmeans-cpu-sample", type=int, default=20000)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    cfg = CONFIGS[args.config]
+    cfg = dict(CONFIGS[args.config])
+    if args.nprobe is not None:
+        cfg["nprobe"] = args.nprobe
+    if args.k is not None:
+        cfg["k"] = args.k
     if args.impl == "reference":
         run_reference(args, cfg)
     else:

@@ -13,6 +13,9 @@
  *     (callers pad odd dimensions with zeros, which changes none of the four
  *     metrics). Scratch memory is a caller-provided workspace whose size comes
  *     from the matching *_workspace_size query; the library allocates nothing.
+ *     A size query plans for the CURRENT CUDA device (its SM count sets the
+ *     work split): make the target device current before asking, or the
+ *     search may reject the workspace as too small on a device with more SMs.
  *   - distances follow the reference: L2 is the SQUARED distance clamped at 0,
  *     INNER_PRODUCT is returned NEGATED and ranked ascending like the others.
  *   - empty result slots hold distance +inf and label -1.
@@ -76,6 +79,25 @@ MF_API const char* mf_last_error(void);
 /* Largest k (and nprobe) the fused top-k kernels accept. */
 MF_API int mf_max_k(void);
 
+/* Which engine mf_flat_search runs for this shape: 1 = the tcgen05 tensor-core
+ * scan (3xTF32), 0 = the SIMT fp32 scan. has_residuals says whether xb_lo is
+ * passed. Host-only, no device needed. No reference counterpart (the
+ * reference has one MLX path, python/metalfaiss/indexflat.py:88-110). */
+MF_API int mf_flat_engine(int metric, int d, int k, int64_t nb, int has_residuals);
+
+/* Diagnostic of the fp16 tensor-core arithmetic that the filter search's
+ * error bound rests on (not a search call): out = A . B^T with fp16 operands
+ * and fp32 accumulation, in the exact instruction form of one of the two
+ * filter passes. engine 0 = tcgen05.mma kind::f16 with A in tensor memory and
+ * B loaded by TMA (the tensor-core filter pass): A and B are 128 x d, out is
+ * 128 x 128, 64 <= d <= 128 with d a multiple of 8. engine 1 = mma.sync
+ * m16n8k16 (the few-query filter pass): A is 16 x d, B is 8 x d, out is
+ * 16 x 8, d a multiple of 16 up to 1024. A and B are row-major fp16 device
+ * arrays, out row-major fp32. No reference counterpart (the reference has no
+ * reduced-precision path). */
+MF_API int mf_diag_f16_dot(int device, void* stream, int engine, const void* a, const void* b,
+                           int d, float* out);
+
 /* tf32 residual of each element: lo = x - x with its 13 low mantissa bits
  * cleared. The tensor cores read fp32 operands as tf32 by that truncation, so
  * (x, lo) is the exact two-term split the 3xTF32 scans consume. Computed once
@@ -137,9 +159,11 @@ MF_API int mf_flat_search_bounded(int device, void* stream, const float* xq, int
  * one file-scope device array of MF_NOALLOC_SCRATCH_BYTES (16 MiB) that every
  * GPU loading this library holds until exit; a search needing more
  * (mf_flat_search_workspace_size > 16 MiB) returns MF_ERR_INVALID_ARGS
- * without launching. The first call on a device looks up the array's address
- * and should come before any stream capture on that device. Nothing is
- * allocated or freed. All calls on a device share the array: calls that
+ * without launching. Every call looks up the array's address on `device`
+ * (nothing is cached, so a device reset leaves no stale address behind); the
+ * first call on a device may load the library's device image there and
+ * should come before any stream capture on that device. Nothing is allocated
+ * or freed. All calls on a device share the array: calls that
  * overlap on the GPU (other streams, other threads) race and must be
  * serialized by the caller. */
 MF_API int mf_flat_search_noalloc(int device, void* stream, const float* xq, int64_t nq,

@@ -67,6 +67,8 @@ _SIGNATURES = {
     "mf_timing_enable": ([I32], I32),
     "mf_timing_reset": ([], I32),
     "mf_launch_count": ([], I64),
+    "mf_diag_f16_dot": ([I32, P, I32, P, P, I32, P], I32),
+    "mf_flat_engine": ([I32, I32, I32, I64, I32], I32),
     "mf_set_scan_engine": ([I32], I32),
     "mf_device_error": ([I32, ctypes.POINTER(ctypes.c_int)], I32),
     "mf_timing_read": ([ctypes.c_char_p, ctypes.POINTER(ctypes.c_double), PI64], I32),

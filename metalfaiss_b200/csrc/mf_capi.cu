@@ -430,6 +430,24 @@ const char* mf_last_error(void) { return g_last_error.c_str(); }
 
 int mf_max_k(void) { return kMaxK; }
 
+int mf_diag_f16_dot(int device, void* stream, int engine, const void* a, const void* b, int d,
+                    float* out) {
+  MF_ENTER(device);
+  MF_CHECK(engine == 0 || engine == 1, MF_ERR_INVALID_ARGS,
+           "engine %d: 0 = tcgen05, 1 = mma.sync", engine);
+  MF_TRY(check_device_ptr(a, "a"));
+  MF_TRY(check_device_ptr(b, "b"));
+  MF_TRY(check_device_ptr(out, "out"));
+  return engine == 0 ? launch_f16_probe_tc(a, b, d, out, (cudaStream_t)stream)
+                     : launch_f16_probe_mma(a, b, d, out, (cudaStream_t)stream);
+}
+
+int mf_flat_engine(int metric, int d, int k, int64_t nb, int has_residuals) {
+  clear_error();
+  return (tc_eligible(metric, d, k, nb) && (has_residuals != 0 || tc_raw_queries(d, k))) ? 1
+                                                                                          : 0;
+}
+
 int mf_vector_norms(int device, void* stream, const float* x, int64_t n, int d, float* norms) {
   MF_ENTER(device);
   MF_CHECK(n >= 0 && d > 0 && d % 4 == 0, MF_ERR_INVALID_ARGS, "bad shape n=%lld d=%d",
@@ -559,8 +577,10 @@ int mf_ivf_search_preassigned_workspace_size(int64_t nq, int nlist, int nprobe, 
   MF_CHECK(bytes != nullptr, MF_ERR_INVALID_ARGS, "bytes is NULL");
   MF_TRY(check_common(d, metric, k, true));
   MF_CHECK(nlist >= 1 && nprobe >= 1, MF_ERR_INVALID_ARGS, "nlist=%d nprobe=%d", nlist, nprobe);
+  int dev = 0;
+  cudaGetDevice(&dev);
   Carver c(nullptr, 0);
-  carve_ivf(c, nq, nlist, nprobe, d, k, 1, 0);
+  carve_ivf(c, nq, nlist, nprobe, d, k, 1, dev);
   *bytes = c.used;
   return MF_OK;
 }
@@ -659,8 +679,12 @@ int mf_ivf_filter_bank(int device, void* stream, int nlist, int d, const int64_t
                        const float* list_vecs, const float* list_norms, const float* centroids,
                        int64_t ntotal, void* list_f16, float* list_rnorms, float* list_stats) {
   MF_ENTER(device);
-  MF_CHECK(nlist >= 1 && d > 0 && d % 8 == 0, MF_ERR_INVALID_ARGS,
-           "filter bank: nlist=%d, d=%d (a multiple of 8)", nlist, d);
+  // the filter search's shapes only (mf_ivf_filter_eligible): its scan reads
+  // 128-byte fp16 tiles (d >= 64) and its refinement one float4 per lane
+  // (d <= 128)
+  MF_CHECK(nlist >= 1 && d >= 64 && d <= 128 && d % 8 == 0, MF_ERR_INVALID_ARGS,
+           "filter bank: nlist=%d, d=%d (the filter search takes 64 <= d <= 128, a multiple "
+           "of 8)", nlist, d);
   MF_TRY(check_device_ptr(list_offsets, "list_offsets"));
   MF_TRY(check_device_ptr(centroids, "centroids"));
   MF_TRY(check_device_ptr(list_stats, "list_stats"));
@@ -738,8 +762,10 @@ int mf_ivf_search_bounded_filtered_workspace_size(int64_t nq, int nlist, int npr
   MF_CHECK(bytes != nullptr, MF_ERR_INVALID_ARGS, "bytes is NULL");
   MF_TRY(check_common(d, MF_METRIC_L2, k, true));
   MF_CHECK(nlist >= 1 && nprobe >= 1, MF_ERR_INVALID_ARGS, "nlist=%d nprobe=%d", nlist, nprobe);
+  int dev = 0;
+  cudaGetDevice(&dev);
   Carver c(nullptr, 0);
-  carve_ivf(c, nq, nlist, nprobe, d, k, 4, 0);
+  carve_ivf(c, nq, nlist, nprobe, d, k, 4, dev);
   *bytes = c.used;
   return MF_OK;
 }

@@ -362,6 +362,33 @@ __global__ void __launch_bounds__(W * 32, FLT ? 4 : 1) few_scan_kernel(const Sca
   }
 }
 
+// Accumulation probe (a diagnostic, not on the search path): out (16 x 8) =
+// A (16 x d) . B (8 x d)^T with mma.sync m16n8k16 (fp16 operands, fp32
+// accumulation carried across the d / 16 K-steps in the C registers), the
+// instruction the few-query filter pass uses. One warp; A and B row-major
+// fp16, two elements per 32-bit word. Fragments: lane (g, t) = (lane / 4,
+// lane % 4) holds A rows g and g + 8 at columns 2t, 2t + 1 and 2t + 8,
+// 2t + 9, B row g at the same columns, and C rows g, g + 8 at columns 2t,
+// 2t + 1.
+__global__ void mma_f16_probe_kernel(const uint32_t* __restrict__ a,
+                                     const uint32_t* __restrict__ b, int d,
+                                     float* __restrict__ out) {
+  const int lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int w = d / 2;
+  float c[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  for (int k0 = 0; k0 < d; k0 += 16) {
+    const int kw = k0 / 2 + t;
+    const uint32_t af[4] = {a[g * w + kw], a[(g + 8) * w + kw], a[g * w + kw + 4],
+                            a[(g + 8) * w + kw + 4]};
+    few_mma_f16(c, af, b[g * w + kw], b[g * w + kw + 4]);
+  }
+  out[g * 8 + 2 * t] = c[0];
+  out[g * 8 + 2 * t + 1] = c[1];
+  out[(g + 8) * 8 + 2 * t] = c[2];
+  out[(g + 8) * 8 + 2 * t + 1] = c[3];
+}
+
 }  // namespace
 
 bool few_eligible(int metric, int d, int k) {
@@ -404,6 +431,16 @@ int launch_few_scan(const ScanArgs& a, int metric, int64_t max_items, int device
   MF_CUDA(cudaMemsetAsync(a.counter, 0, sizeof(int), stream));
   ScopedTiming tm(a.max_rows > 0 ? "scan_topk_ivf_bound_small" : "scan_topk_ivf_small", stream);
   fn<<<(unsigned int)grid, warps * 32, smem, stream>>>(a);
+  MF_LAUNCH_CHECK();
+  return MF_OK;
+}
+
+int launch_f16_probe_mma(const void* a, const void* b, int d, float* out,
+                         cudaStream_t stream) {
+  MF_CHECK(d >= 16 && d <= 1024 && d % 16 == 0, MF_ERR_INVALID_ARGS,
+           "mma.sync probe: d=%d (a multiple of 16 in [16, 1024])", d);
+  mma_f16_probe_kernel<<<1, 32, 0, stream>>>(reinterpret_cast<const uint32_t*>(a),
+                                             reinterpret_cast<const uint32_t*>(b), d, out);
   MF_LAUNCH_CHECK();
   return MF_OK;
 }

@@ -17,10 +17,20 @@
 // q' = q - c, x' = x - c, Dc = |q'|^2 and rn_x = |x'|^2 in fp32. Rounding an
 // element to fp16 moves it by at most 2^-11 of itself (or 2^-25 / s in
 // absolute terms where it underflows), so by Cauchy-Schwarz
-//   |<q', x'> - <q', x'>~| <= (2^-10 + 2^-22 + acc) |q'| |x'| + underflow,
-// with acc (the fp32 accumulation) below 2^-17. With |q'| <= sqrt(Dc)(1 + 2^-17)
-// and |x'| <= R_l (rounded up), the pair's bound is
-//   e = 2^-9 (1 + 2^-6) sqrt(Dc) R_l                       (the products)
+//   |<q', x'> - <q', x'>~| <= (2^-10 + 2^-22 + acc (1 + 2^-10)) |q'| |x'| + underflow,
+// where acc bounds the tensor cores' fp32 accumulation of the d exact
+// products relative to the sum of their magnitudes. acc = d 2^-22 (2^-15 at
+// d = 128): every addend truncated by less than one unit in the 24th
+// significant bit of the largest term of its addition, however many terms the
+// hardware adds at once. That covers the multi-term additions that align to
+// the largest exponent and truncate, as published measurements describe NVIDIA
+// tensor cores (Fasi, Higham, Mikaitis, Pranesh, "Numerical behavior of NVIDIA
+// tensor cores", PeerJ Computer Science, 2021); round-to-nearest is tighter.
+// mf_diag_f16_dot runs both instruction forms used here (tcgen05.mma kind::f16
+// and mma.sync m16n8k16) so that tests measure this on the device with
+// adversarial operands. With |q'| <= sqrt(Dc)(1 + 2^-17) and |x'| <= R_l
+// (rounded up), and d <= 128, the pair's bound is
+//   e = 2^-9 (1 + 2^-5 + 2^-9) sqrt(Dc) R_l                (the products)
 //     + 2^-22 sqrt(d) (sqrt(Dc) / s_l + R_l / s_q)         (underflow)
 //     + (d + 20) 2^-23 (|q|^2 + XN_l + Dc + R_l^2)         (fp32 rounding)
 // where the last term covers the rounding of Dc, rn_x, the scan's own
@@ -233,8 +243,9 @@ __global__ void __launch_bounds__(kPairsWarps * 32) filter_pairs_kernel(
     } else {
       sq = ldexpf(1.0f, eq);
       sc = 1.0f / (sq * sl);  // exact: a power of two within range
-      // 0x1.05p-9 >= 2^-9 (1 + 2^-6)(1 + 2^-17)
-      e = 0x1.05p-9f * nrm * R + 0x1p-22f * sqrtf((float)d) * (nrm / sl + R / sq) +
+      // 0x1.09p-9 = 2^-9 (1 + 9 / 256) >= 2 (2^-10 + 2^-22 + 128 2^-22 (1 + 2^-10))
+      // (1 + 2^-17) = 2^-9 (1.0315...): the products term for d <= 128
+      e = 0x1.09p-9f * nrm * R + 0x1p-22f * sqrtf((float)d) * (nrm / sl + R / sq) +
           (float)(d + 20) * 0x1p-23f * (qn + XN + dc + R * R) + 0x1p-100f;
       thr = bq + 2.0f * e;  // +inf stays +inf
     }

@@ -10,9 +10,12 @@
 // that loads the library holds that array until the process exits.
 //
 // Contract:
-//  * The first call on a device looks up the array's device address (with
-//    that device current) and caches it. Make that first call before any
-//    stream capture starts on the device.
+//  * Every call looks up the array's device address on `device` (with that
+//    device current). The address is not cached: a cached one would outlive
+//    a device reset or a released primary context and point at memory this
+//    library no longer owns. The lookup is cheap next to a search, but the
+//    first one on a device may load this library's device image there, so
+//    make the first call on a device before any stream capture starts on it.
 //  * A search whose scratch need exceeds kNoAllocScratchBytes is rejected
 //    with MF_ERR_INVALID_ARGS before anything is launched.
 //  * No call allocates or frees device memory.
@@ -21,8 +24,6 @@
 //    (its work counter) on the stream before the scan reads it. Two calls
 //    whose work overlaps on the GPU (different streams, or different host
 //    threads) race on the array and give wrong results: serialize them.
-#include <mutex>
-
 #include "mf_scan.cuh"
 
 namespace mf {
@@ -34,30 +35,18 @@ namespace {
 // d=512, k=10 about 12.7 MiB; nq=4096, d=128, k=256 needs about 122 MiB and
 // is rejected.
 constexpr size_t kNoAllocScratchBytes = static_cast<size_t>(MF_NOALLOC_SCRATCH_BYTES);
-constexpr int kNoAllocMaxDevices = 64;
-
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
-std::mutex g_noalloc_mu;
-void* g_noalloc_addr[kNoAllocMaxDevices] = {};
-
-// Device address of g_noalloc_scratch on the current device (== `device`),
-// looked up once per device. In host code g_noalloc_scratch names only a host
+// Device address of g_noalloc_scratch in the current context (the caller has
+// made `device` current). In host code g_noalloc_scratch names only a host
 // stand-in for the device symbol, so its address must come from the runtime.
-int noalloc_scratch(int device, void** out) {
-  MF_CHECK(device >= 0 && device < kNoAllocMaxDevices, MF_ERR_INVALID_ARGS,
-           "device %d is beyond the %d devices the static scratch tracks", device,
-           kNoAllocMaxDevices);
-  std::lock_guard<std::mutex> lk(g_noalloc_mu);
-  if (g_noalloc_addr[device] == nullptr) {
-    void* p = nullptr;
-    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(static scratch)");
-    MF_CHECK(p != nullptr && (reinterpret_cast<uintptr_t>(p) & 255) == 0, MF_ERR_CUDA,
-             "static scratch address %p is not 256-byte aligned", p);
-    g_noalloc_addr[device] = p;
-  }
-  *out = g_noalloc_addr[device];
+int noalloc_scratch(void** out) {
+  void* p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(static scratch)");
+  MF_CHECK(p != nullptr && (reinterpret_cast<uintptr_t>(p) & 255) == 0, MF_ERR_CUDA,
+           "static scratch address %p is not 256-byte aligned", p);
+  *out = p;
   return MF_OK;
 }
 
@@ -98,7 +87,7 @@ int mf_flat_search_noalloc(int device, void* stream, const float* xq, int64_t nq
   if (metric == MF_METRIC_L2) MF_TRY(check_device_ptr(xb_norms, "xb_norms", nb == 0));
   MF_TRY(check_device_ptr(xb_lo, "xb_lo", true));
   void* scratch = nullptr;
-  MF_TRY(noalloc_scratch(device, &scratch));
+  MF_TRY(noalloc_scratch(&scratch));
   return run_flat_topk(device, (cudaStream_t)stream, xq, nq, xb, xb_norms, xb_lo, nb, d, metric,
                        k, ids, distances, labels, scratch, kNoAllocScratchBytes);
 }

@@ -201,4 +201,10 @@ int launch_extract_bound_slack(const float* pd, int64_t nq, int P, int k, const 
 // Exclusive scan of n int64 counts into out (n+1 entries; out[n] = total).
 int launch_exclusive_scan_i64(const int64_t* in, int64_t n, int64_t* out, cudaStream_t stream);
 
+// Accumulation probes of the fp16 tensor-core products (diagnostics):
+// tcgen05 (A 128 x d in tensor memory, B 128 x d by TMA; out 128 x 128) and
+// mma.sync m16n8k16 (A 16 x d, B 8 x d; out 16 x 8), fp32 accumulation.
+int launch_f16_probe_tc(const void* a, const void* b, int d, float* out, cudaStream_t stream);
+int launch_f16_probe_mma(const void* a, const void* b, int d, float* out, cudaStream_t stream);
+
 }  // namespace mf

@@ -1134,7 +1134,107 @@ __global__ void gather_queries_kernel(const float* __restrict__ xq, int d,
   }
 }
 
+// Accumulation probe (a diagnostic, not on the search path): out (128 x 128)
+// = A (128 x d) . B (128 x d)^T in the filter pass's instruction form. A
+// (fp16) sits in tensor memory, written by tcgen05.st two elements per
+// column; B (fp16) arrives by TMA in the 128-byte swizzled K-major layout,
+// K-blocks of 64; one tcgen05.mma kind::f16 per 16 of K accumulates in fp32
+// in tensor memory. One CTA of 128 threads; thread t owns row t of A and of
+// the result. Every wait is bounded.
+__global__ void __launch_bounds__(128, 1)
+    tc_f16_probe_kernel(const __grid_constant__ CUtensorMap bmap, const uint32_t* __restrict__ a,
+                        int d, float* __restrict__ out) {
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* base = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int KB = (d + 63) / 64;
+  uint64_t* full = reinterpret_cast<uint64_t*>(base + size_t(KB) * kTqM * 128);
+  uint64_t* done = full + 1;
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(done + 1);
+  int* s_abort = reinterpret_cast<int*>(s_tmem + 1);
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  if (warp == 0) {
+    tmem_alloc(s_tmem, 256);
+    tmem_relinquish();
+  }
+  if (tid == 0) {
+    mbar_init(full, 1);
+    mbar_init(done, 1);
+    *s_abort = 0;
+    fence_mbar_init();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *s_tmem;
+  const uint32_t lane_base = tmem + ((uint32_t)(32 * warp) << 16);
+  const int words = d / 2;  // 32-bit words (fp16 pairs) per row
+  const uint32_t* arow = a + (size_t)tid * words;
+  for (int c = 0; c < KB; ++c) {
+    uint32_t pk[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const int w = c * 32 + i;
+      pk[i] = w < words ? arow[w] : 0u;
+    }
+    tmem_st32(lane_base + c * 32, pk);
+  }
+  tmem_wait_st();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t acc = tmem + 128;  // accumulator columns [128, 256)
+  if (tid == 0) {
+    mbar_arrive_expect_tx(full, (uint32_t)(KB * kTqM * 128));
+    for (int kb = 0; kb < KB; ++kb) tma_load_2d(base + size_t(kb) * kTqM * 128, &bmap, kb * 64, 0, full);
+    if (mbar_wait(full, 0, s_abort, &g_device_error)) {
+      tc_fence_after();
+      const uint32_t st = smem_u32(base);
+      constexpr uint32_t idesc = idesc_f16(kTqM, 128);
+      for (int kb = 0; kb < KB; ++kb)
+        for (int kk = 0; kk < 4; ++kk)
+          mma_f16_ts(acc, tmem + kb * 32 + kk * 8,
+                     desc_k_sw128(st + (uint32_t)(kb * kTqM * 128) + kk * 32), idesc,
+                     !(kb == 0 && kk == 0));
+      mma_commit(done);
+    }
+  }
+  __syncthreads();
+  const bool ok = mbar_wait(done, 0, s_abort, &g_device_error);
+  tc_fence_after();
+  if (ok) {
+    for (int c = 0; c < 4; ++c) {
+      float v[32];
+      tmem_ld32(lane_base + 128 + c * 32, v);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) out[(size_t)tid * 128 + c * 32 + i] = v[i];
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 256);
+  }
+}
+
 }  // namespace
+
+int launch_f16_probe_tc(const void* a, const void* b, int d, float* out, cudaStream_t stream) {
+  MF_CHECK(d >= 64 && d <= kTqMaxDAtm && d % 8 == 0, MF_ERR_INVALID_ARGS,
+           "tensor-core probe: d=%d (64 <= d <= 128, a multiple of 8)", d);
+  PFN_cuTensorMapEncodeTiled_v12000 enc;
+  MF_TRY(encoder(&enc));
+  CUtensorMap map;
+  MF_TRY(make_map_f16(enc, &map, b, d, kTqM, kTqM));
+  const int KB = (d + 63) / 64;
+  const size_t smem = size_t(KB) * kTqM * 128 + 64 + 1024;
+  tc_f16_probe_kernel<<<1, 128, smem, stream>>>(map, reinterpret_cast<const uint32_t*>(a), d,
+                                                out);
+  MF_LAUNCH_CHECK();
+  return MF_OK;
+}
 
 void set_scan_engine(int e) { g_engine = e; }
 int scan_engine() { return g_engine; }

@@ -5,8 +5,11 @@ sorted by list (input order inside a list), list_norms (N), list_ids (N) int64
 and list_offsets (nlist+1) int64 — plus the centroids held by the coarse
 quantizer (a FlatIndex). search() runs entirely on the device: coarse top-nprobe
 (fused distance + warp top-k), grouping of the (query, probe) pairs by list, a
-list-major scan that streams each probed list once per group of up to 32
-queries, and an on-device merge of the nprobe partial top-k lists per query.
+list-major scan that streams each probed list once per group of up to 128
+queries (the tensor-core tile; lists probed by at most 16 queries go to a
+few-query scan), and an on-device merge of the nprobe partial top-k lists per
+query. L2 searches with k <= 16 and 64 <= d <= 128 run as an fp16 filter plus
+an exact refinement (mf_ivf_search_filtered), with the same results.
 
 The reference class cannot run end to end (its train never clusters, its add
 and search raise AttributeError: python/metalfaiss/index/ivf_flat_index.py:71,89-90,138);
@@ -186,7 +189,15 @@ class IVFFlatIndex:
             return
         idt = (torch.arange(self._ntotal, self._ntotal + n, dtype=torch.int64, device=self.device)
                if ids is None else as_ids(ids, n, self.device))
-        labels = self._coarse_assign(x)
+        self._add_assigned(x, idt, self._coarse_assign(x))
+
+    def _add_assigned(self, x: torch.Tensor, idt: torch.Tensor, labels: torch.Tensor) -> None:
+        """Appends padded rows x with ids idt to the lists `labels` (int64,
+        one per row) names: the CSR merge of IVFFlatIndex.add, for callers
+        that have assigned the rows already (a sharded build)."""
+        n = x.shape[0]
+        if n == 0:
+            return
         norms = compute_norms(x)
         total = self._ntotal + n
         out_off = torch.empty(self._nlist + 1, dtype=torch.int64, device=self.device)

@@ -158,14 +158,45 @@ def train_kmeans_sharded(x: torch.Tensor, k: int, niter: int, init: torch.Tensor
     return c
 
 
-class ShardedIVF:
-    """This rank's share of an IVFFlat index; search() returns the merged global top-k."""
+def add_owned_rows(index, xs, rank: int, world: int, ids=None) -> np.ndarray:
+    """Sharded IVF build: `index` (trained; the same centroids on every rank)
+    receives only the rows of xs whose list this rank owns. Every rank
+    assigns all rows once (the same result everywhere), the lists are
+    partitioned by greedy LPT on their sizes, and each rank appends its own
+    lists' rows with their global ids (row positions in xs, or `ids`), in
+    input order. Returns the owner rank of every list. The database held by
+    a rank is about 1/world of the whole."""
+    from ._tensors import as_ids, as_matrix
 
-    def __init__(self, index, rank: int, world: int, group=None):
+    dev = index.device
+    x = as_matrix(xs, index.d, dev)
+    n = x.shape[0]
+    labels = index._coarse_assign(x)
+    sizes = torch.bincount(labels, minlength=index.nlist).cpu().numpy()
+    owners = lpt_partition(sizes, world)
+    mine = torch.from_numpy(owners == rank).to(dev)[labels]
+    gid = (torch.arange(n, dtype=torch.int64, device=dev) if ids is None
+           else as_ids(ids, n, dev))
+    index._add_assigned(x[mine].contiguous(), gid[mine].contiguous(),
+                        labels[mine].contiguous())
+    return owners
+
+
+class ShardedIVF:
+    """This rank's share of an IVFFlat index; search() returns the merged global top-k.
+
+    Built from a whole index (this rank keeps a copy of its own lists) or,
+    with `owners` from add_owned_rows, from an index that holds only this
+    rank's lists already."""
+
+    def __init__(self, index, rank: int, world: int, group=None, owners=None):
         self.rank, self.world, self.group = rank, world, group
-        owners = lpt_partition(index.list_sizes(), world)
-        self.owners = owners
-        self.local = keep_lists(index, owners == rank)
+        if owners is None:
+            owners = lpt_partition(index.list_sizes(), world)
+            self.local = keep_lists(index, owners == rank)
+        else:
+            self.local = index
+        self.owners = np.asarray(owners)
 
     @property
     def nprobe(self):
@@ -199,12 +230,19 @@ class ShardedIVF:
 
 
 class ShardedFlat:
-    """Contiguous row shard of a flat database (global ids); search() merges."""
+    """Contiguous row shard of a flat database (global ids); search() merges.
 
-    def __init__(self, index, rank: int, world: int, group=None):
+    Built from the whole index (this rank copies rows row_shard(...)), or
+    with local=True from an index that already holds only this rank's rows
+    under their global ids."""
+
+    def __init__(self, index, rank: int, world: int, group=None, local: bool = False):
         from .index_flat import FlatIndex
 
         self.rank, self.world, self.group = rank, world, group
+        if local:
+            self.local = index
+            return
         b, e = row_shard(index.ntotal, rank, world)
         self.local = FlatIndex(index.d, index.metric_type, index.device, index._residuals)
         if e > b:

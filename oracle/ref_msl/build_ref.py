@@ -5,13 +5,17 @@ from __future__ import annotations
 
 import ast
 import json
+import os
 import subprocess
 import sys
 from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
 OUT = HERE.parent / "_ref"
-REF_FILE = Path("/root/reference/python/metalfaiss/faissmlx/kernels/ivf_kernels.py")
+# The reference checkout: METALFAISS_REFERENCE, else where this build's
+# container mounts it.
+REF_ROOT = Path(os.environ.get("METALFAISS_REFERENCE", "/root/reference"))
+REF_FILE = REF_ROOT / "python/metalfaiss/faissmlx/kernels/ivf_kernels.py"
 LIB = OUT / "libivf_kernels_ref.so"
 
 # C types of the buffers, by the names the reference's launchers give them

@@ -64,3 +64,21 @@ def test_compute_call_reports_status_not_crash():
         assert b"device" in lib.mf_last_error()
     else:
         assert status == ErrorCode.INVALID_ARGS  # NULL pointers rejected before launch
+
+
+def test_engine_and_filter_eligibility_queries_without_gpu():
+    """The host-side dispatch queries: the tensor-core flat scan takes L2 and
+    inner product at 32 <= d <= 1024; the filter search 64 <= d <= 128 with d
+    a multiple of 8 and k <= 16."""
+    lib = nat.load()
+    L2, IP, L1 = 1, 0, 2
+    assert lib.mf_flat_engine(L2, 128, 10, 1_000_000, 1) == 1
+    assert lib.mf_flat_engine(IP, 128, 10, 1_000_000, 0) == 1
+    assert lib.mf_flat_engine(L1, 128, 10, 1_000_000, 1) == 0
+    assert lib.mf_flat_engine(L2, 16, 10, 1_000_000, 1) == 0      # d < 32
+    assert lib.mf_flat_engine(L2, 128, 10, 100, 1) == 0           # tiny bank
+    for d in (64, 72, 96, 128):
+        assert lib.mf_ivf_filter_eligible(d, 10, 100_000) == 1
+    for d in (32, 56, 60, 132, 136, 256):
+        assert lib.mf_ivf_filter_eligible(d, 10, 100_000) == 0
+    assert lib.mf_ivf_filter_eligible(128, 17, 100_000) == 0

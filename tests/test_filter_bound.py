@@ -6,9 +6,12 @@ x of that list, the filter's approximate distance
     a = |q - c|^2 + |x - c|^2 - 2 <fp16(s_q (q - c)), fp16(s_l (x - c))> / (s_q s_l)
 
 stays within e of the exact distance |q - x|^2, where s_q and s_l are the
-kernel's powers of two and e its bound. The products are summed in fp64 here;
-the bound's margin for the tensor cores' fp32 accumulation is far larger than
-that accumulation's error. Cases: isotropic data, coordinates near fp16
+kernel's powers of two and e its bound. The products are accumulated the worst
+way the bound allows for the tensor cores: one addend at a time into an fp32
+accumulator that truncates toward zero (each step loses less than one unit in
+the 24th bit of the larger term; hardware that adds several terms at once
+or rounds to nearest loses less). tests/test_gpu_mma_accum.py measures the
+device's own accumulation. Cases: isotropic data, coordinates near fp16
 rounding boundaries, one dominant coordinate (where Cauchy-Schwarz is tight),
 tiny and huge magnitudes, and residuals with elements that underflow fp16."""
 import math
@@ -40,10 +43,35 @@ def pair_bound(q, c, R, XN, sl, d):
     nrm = math.sqrt(dc) * (1.0 + 2.0 ** -17)
     sq = 2.0 ** scale_exp(nrm)
     qn = float((q.astype(np.float32) ** 2).sum(dtype=np.float32))
-    e = (float.fromhex("0x1.05p-9") * nrm * R
+    e = (float.fromhex("0x1.09p-9") * nrm * R
          + 2.0 ** -22 * math.sqrt(d) * (nrm / sl + R / sq)
          + (d + 20) * 2.0 ** -23 * (qn + XN + dc + R * R) + 2.0 ** -100)
     return e, sq, dc
+
+
+def to_f32_toward_zero(v: np.ndarray) -> np.ndarray:
+    """fp64 values rounded to fp32 toward zero (as float64)."""
+    f = v.astype(np.float32)
+    over = np.abs(f.astype(np.float64)) > np.abs(v)
+    f[over] = np.nextafter(f[over], np.float32(0))
+    return f.astype(np.float64)
+
+
+def truncating_dot(X: np.ndarray, q: np.ndarray) -> np.ndarray:
+    """Row dot products of fp16 operands (as float64: the products are exact)
+    accumulated one addend at a time in fp32 with truncation toward zero."""
+    acc = np.zeros(X.shape[0], np.float64)
+    for i in range(X.shape[1]):
+        acc = to_f32_toward_zero(acc + X[:, i] * q[i])
+    return acc
+
+
+def test_truncating_accumulation_emulation():
+    x = np.array([[2048.0] + [1.0] * 127])
+    q = np.array([2048.0] + [0.4995] * 127)
+    got = truncating_dot(x, q)[0]
+    assert got == 2.0 ** 22  # every tail below one unit (0.5) is dropped
+    assert abs(got - float(x[0] @ q)) <= 128 * 2.0 ** -22 * float(np.abs(x[0]) @ np.abs(q))
 
 
 def check(q, c, X, rng_name=""):
@@ -56,7 +84,7 @@ def check(q, c, X, rng_name=""):
     qh = ((q - c).astype(np.float32) * np.float32(sq)).astype(np.float16).astype(np.float64)
     xh = (resid * np.float32(sl)).astype(np.float16).astype(np.float64)
     assert np.all(np.isfinite(qh)) and np.all(np.isfinite(xh)), "fp16 overflow"
-    dot = (xh @ qh) / (sq * sl)
+    dot = truncating_dot(xh, qh) / (sq * sl)
     a = dc + rn.astype(np.float64) - 2.0 * dot
     t = ((X.astype(np.float64) - q.astype(np.float64)) ** 2).sum(1)
     err = np.abs(a - t)

@@ -135,3 +135,36 @@ def test_filter_far_queries(cuda_device):
     idx = _build(x, 64, seed=111)
     xq = (syn.gaussian(200, d, seed=112) * 40.0).astype(np.float32)
     _check(idx, x, xq, 8, 10)
+
+
+@pytest.mark.parametrize("d", [56, 136, 256])
+def test_dims_outside_the_filter_take_the_exact_scan(cuda_device, d):
+    """L2 indexes whose d the filter search does not take (below 64, above
+    128) run the exact scan: same results as the oracle, and the filter bank
+    itself refuses those shapes instead of failing inside the refinement."""
+    x, cen, _ = syn.mixture(20000, d, 64, seed=121)
+    idx = _build(x, 64, seed=121)
+    assert nat.load().mf_ivf_filter_eligible(idx._dp, 10, idx.ntotal) == 0
+    assert not idx._filter_ok(10)
+    xq, _, _ = syn.mixture(300, d, 64, seed=122, centres=cen)
+    idx.nprobe = 8
+    D, I = idx.search(xq, 10).numpy()
+    offsets = idx._offsets.cpu().numpy()
+    vecs = idx._vecs[:, : idx.d].cpu().numpy()
+    ids = idx._ids[: idx.ntotal].cpu().numpy()
+    cents = idx.centroids[: idx.nlist, : idx.d].cpu().numpy()
+    D_ref, I_ref = oracle.ivf_search(xq, cents, offsets, vecs, ids, 8, 10, oracle.L2)
+    errs = compare.check_knn(D, I, D_ref, I_ref, compare.exact_lookup(xq, x, oracle.L2),
+                             atol=compare.l2_atol(xq, x))
+    assert not errs, errs[:5]
+    dev = idx.device
+    n = idx._vecs.shape[0]
+    h = torch.empty((n, idx._dp), dtype=torch.float16, device=dev)
+    rn = torch.empty(n, dtype=torch.float32, device=dev)
+    stats = torch.empty((idx.nlist, 4), dtype=torch.float32, device=dev)
+    lib = nat.load()
+    status = lib.mf_ivf_filter_bank(dev.index, nat.stream_of(dev), idx.nlist, idx._dp,
+                                    nat.ptr(idx._offsets), nat.ptr(idx._vecs),
+                                    nat.ptr(idx._norms), nat.ptr(idx.quantizer._xb.buf), n,
+                                    nat.ptr(h), nat.ptr(rn), nat.ptr(stats))
+    assert status == 6, lib.mf_last_error()

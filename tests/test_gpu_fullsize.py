@@ -4,10 +4,13 @@ oracle on a few sampled queries or points:
 
 * flat INNER_PRODUCT, 10M unit rows x d=128, Q=10000, k=100: ascending rows,
   self-queries return themselves first, sampled queries equal the oracle;
-* IVFFlat L2 range search, 20M rows from a 16384-cluster mixture, nlist=16384,
-  nprobe=32, radius = median 10th-NN distance: every reported distance within
-  the radius, every kNN result within the radius reported, sampled queries
-  equal the oracle over their probed lists;
+* IVFFlat L2, 20M rows from a 16384-cluster mixture, nlist=16384, nprobe=32
+  (the benchmarked index, built once for the module): the k=10 search, by the
+  default filter search and by the exact scan, on 64 sampled queries against
+  the oracle (its own coarse step, then the probed lists); range search at
+  radius = median 10th-NN distance: every reported distance within the
+  radius, every kNN result within the radius reported, sampled queries equal
+  the oracle over their probed lists;
 * k-means, 5M points x d=256, K=4096: sampled assignments equal the oracle's
   argmin, sampled cluster means equal the oracle's, sizes sum to N.
 
@@ -20,6 +23,7 @@ import pytest
 import torch
 
 from metalfaiss_b200 import FlatIndex, IVFFlatIndex, MetricType, clustering
+from metalfaiss_b200 import _native as nat
 from metalfaiss_b200 import synthetic as syn
 from metalfaiss_b200.clustering import ClusteringParameters
 from oracle import compare, oracle
@@ -65,18 +69,100 @@ def test_flat_ip_10m_k100(cuda_device):
             assert abs(ip[got_i[j]] - ip[ref_i[j]]) <= 1e-5 * (1 + abs(ip[ref_i[j]]))
 
 
-def test_ivf_20m_range_search(cuda_device):
+IVF20M = dict(n=20_000_000, d=128, nlist=16384, nq=10_000, nprobe=32, k=10, seed=1234)
+
+
+@pytest.fixture(scope="module")
+def ivf20m():
+    """The benchmarked IVFFlat index: 20M rows from the 16384-cluster mixture,
+    nlist=16384 trained by seeded k-means (10 iterations on a 256-per-list
+    subsample), 10000 queries from the same mixture, nprobe=32 (the same seeds
+    and training as the benchmark's index)."""
+    c = IVF20M
     dev = torch.device("cuda", 0)
-    n, d, nlist, nq, nprobe, k = 20_000_000, 128, 16384, 10_000, 32, 10
-    x, cen = syn.torch_mixture(n, d, nlist, 1234, dev)
-    params = ClusteringParameters(niter=10, seed=1234, max_points_per_centroid=256)
-    idx = IVFFlatIndex(d, nlist, device=dev, clustering=params)
+    x, cen = syn.torch_mixture(c["n"], c["d"], c["nlist"], c["seed"], dev)
+    params = ClusteringParameters(niter=10, seed=c["seed"], max_points_per_centroid=256)
+    idx = IVFFlatIndex(c["d"], c["nlist"], device=dev, clustering=params)
     idx.train(x)
     idx.add(x)
     del x
     torch.cuda.empty_cache()
-    xq, _ = syn.torch_mixture(nq, d, nlist, 1235, dev, centres=cen)
-    idx.nprobe = nprobe
+    xq, _ = syn.torch_mixture(c["nq"], c["d"], c["nlist"], c["seed"] + 1, dev, centres=cen)
+    idx.nprobe = c["nprobe"]
+    yield idx, xq
+    del idx, xq
+    gc.collect()
+    torch.cuda.empty_cache()
+
+
+def _probed_rows(idx, lists):
+    """Rows of the given lists, in list order, with a CSR over them."""
+    offs = idx.list_offsets.cpu().numpy()
+    sizes = np.array([offs[l + 1] - offs[l] for l in lists], np.int64)
+    sub = np.zeros(len(lists) + 1, np.int64)
+    np.cumsum(sizes, out=sub[1:])
+    rows = np.concatenate([np.arange(offs[l], offs[l + 1]) for l in lists])
+    return rows, sub
+
+
+@pytest.mark.parametrize("filtered", [True, False], ids=["filter", "exact"])
+def test_ivf_20m_knn_sampled_oracle(cuda_device, ivf20m, filtered):
+    """The benchmarked search (k=10) on 64 sampled queries against the oracle:
+    the oracle's own coarse step over all 16384 centroids, then the exact
+    top-k over the rows of the probed lists. The default L2 path is the fp16
+    filter search with its exact refinement; it must rescan no list here and
+    no bounded device wait may time out."""
+    idx, xq = ivf20m
+    c = IVF20M
+    d, k, P = c["d"], c["k"], c["nprobe"]
+    dev = xq.device
+    nat.filter_rescans(0, reset=True)
+    idx.filter_search = filtered
+    try:
+        assert idx._filter_ok(k) == filtered
+        D, I = idx.search(xq, k)
+    finally:
+        idx.filter_search = True
+    torch.cuda.synchronize()
+    assert nat.device_error(0) == 0, "a bounded device wait timed out"
+    if filtered:
+        assert nat.filter_rescans(0, reset=True) == 0
+    rng = np.random.Generator(np.random.PCG64(20))
+    sample = np.unique(np.concatenate([np.linspace(0, c["nq"] - 1, 32).astype(np.int64),
+                                       rng.choice(c["nq"], 32, replace=False)]))
+    assert len(sample) >= 60
+    cents = idx.centroids[:, :d].cpu().numpy()
+    qs = xq[torch.from_numpy(sample).to(dev)].cpu().numpy()
+    probes_ref = oracle.coarse_probes(qs, cents, P)
+    probes_gpu = idx.quantizer._search_padded(idx._prepare_query(xq), P,
+                                              map_ids=False).labels.cpu().numpy()[sample]
+    Dg, Ig = D.cpu().numpy()[sample], I.cpu().numpy()[sample]
+    for t in range(len(sample)):
+        pr = probes_ref[t]
+        if set(pr.tolist()) != set(probes_gpu[t].tolist()):
+            # only a near-tie at the last probe may differ
+            exact = oracle.pairwise_exact(qs[t:t + 1], cents, oracle.L2)[0]
+            a = np.sort(exact[pr])
+            b = np.sort(exact[probes_gpu[t]])
+            assert np.allclose(a, b, rtol=1e-5, atol=0), (sample[t], a[-3:], b[-3:])
+            pr = probes_gpu[t]
+        rows, sub = _probed_rows(idx, pr)
+        rt = torch.from_numpy(rows).to(dev)
+        vecs = idx._vecs[rt][:, :d].cpu().numpy()
+        ids = idx._ids[rt].cpu().numpy()
+        qv = qs[t:t + 1]
+        D_ref, I_ref = oracle.ivf_search(qv, cents, sub, vecs, ids, P, k,
+                                         probes=np.arange(len(pr))[None, :])
+        errs = compare.check_knn(Dg[t:t + 1], Ig[t:t + 1], D_ref, I_ref,
+                                 compare.exact_lookup(qv, vecs, oracle.L2, ids),
+                                 atol=compare.l2_atol(qv, vecs))
+        assert not errs, (int(sample[t]), errs[:3])
+
+
+def test_ivf_20m_range_search(cuda_device, ivf20m):
+    idx, xq = ivf20m
+    dev = xq.device
+    nq, d, nprobe, k = IVF20M["nq"], IVF20M["d"], IVF20M["nprobe"], IVF20M["k"]
     D, I = idx.search(xq, k)
     radius = float(D[:, k - 1].median())
     res = idx.range_search(xq, radius)
@@ -93,11 +179,11 @@ def test_ivf_20m_range_search(cuda_device):
     # sampled queries against the oracle over their probed lists
     probes = idx.quantizer._search_padded(idx._prepare_query(xq), nprobe,
                                           map_ids=False).labels.cpu().numpy()
-    offs = idx.list_offsets.cpu().numpy()
     for q in (3, 4242, nq - 2):
-        rows = np.concatenate([np.arange(offs[l], offs[l + 1]) for l in probes[q]])
-        vecs = idx._vecs[torch.from_numpy(rows).to(dev)][:, :d].cpu().numpy()
-        ids = idx._ids[torch.from_numpy(rows).to(dev)].cpu().numpy()
+        rows, _ = _probed_rows(idx, probes[q])
+        rt = torch.from_numpy(rows).to(dev)
+        vecs = idx._vecs[rt][:, :d].cpu().numpy()
+        ids = idx._ids[rt].cpu().numpy()
         qv = xq[q:q + 1].cpu().numpy()
         dist = oracle.pairwise_exact(qv, vecs, oracle.L2)[0]
         atol = compare.l2_atol(qv, vecs)

@@ -91,3 +91,56 @@ def test_kmeans_sums_over_shards_equal_update(cuda_device):
     assert torch.equal(tot_n, counts_ref)
     assert torch.equal(got[-1], c[-1])
     torch.testing.assert_close(got, ref, rtol=1e-6, atol=1e-6)
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_sharded_build_holds_each_rank_its_own_lists(cuda_device, world):
+    """add_owned_rows: each emulated rank adds only the rows of the lists it
+    owns (LPT over the sizes every rank computes alike), under global ids and
+    in input order. The ranks' banks partition the whole one exactly, and the
+    bounded filter searches over them merge to the unsharded search."""
+    from metalfaiss_b200.sharding import add_owned_rows
+
+    d, nlist, k = 64, 96, 10
+    x, cen, _ = syn.mixture(40000, d, nlist, seed=41)
+    cents = oracle.kmeans_train(x, nlist, 2, 41)
+    full = IVFFlatIndex(d, nlist)
+    full.set_centroids(cents)
+    full.add(x)
+    shards, owners = [], None
+    for r in range(world):
+        s = IVFFlatIndex(d, nlist)
+        s.set_centroids(cents)
+        o = add_owned_rows(s, x, r, world)
+        assert owners is None or np.array_equal(o, owners)
+        owners = o
+        shards.append(s)
+    assert np.array_equal(owners, lpt_partition(full.list_sizes(), world))
+    assert sum(s.ntotal for s in shards) == full.ntotal
+    offs = full.list_offsets.cpu().numpy()
+    for r, s in enumerate(shards):
+        so = s.list_offsets.cpu().numpy()
+        for l in range(nlist):
+            n_l = so[l + 1] - so[l]
+            if owners[l] != r:
+                assert n_l == 0
+                continue
+            assert n_l == offs[l + 1] - offs[l]
+            torch.testing.assert_close(s._ids[so[l]:so[l + 1]], full._ids[offs[l]:offs[l + 1]],
+                                       rtol=0, atol=0)
+            torch.testing.assert_close(s._vecs[so[l]:so[l + 1]],
+                                       full._vecs[offs[l]:offs[l + 1]], rtol=0, atol=0)
+    xq_np, _, _ = syn.mixture(500, d, nlist, seed=42, centres=cen)
+    full.nprobe = 8
+    ref = full.search(xq_np, k)
+    xq = full._prepare_query(xq_np)
+    probes = full.quantizer._search_padded(xq, 8, map_ids=False).labels.contiguous()
+    bound = torch.stack([s._probe_bound(xq, probes, k) for s in shards]).min(0).values
+    parts = [s._search_bounded(xq, k, probes, bound) for s in shards]
+    pd = torch.stack([p.distances for p in parts], 1).contiguous()
+    pi = torch.stack([p.labels for p in parts], 1).contiguous()
+    D, I = merge_partials(pd, pi, k).numpy()
+    D_ref, I_ref = ref.numpy()
+    errs = compare.check_knn(D, I, D_ref, I_ref, compare.exact_lookup(xq_np, x, oracle.L2),
+                             atol=compare.l2_atol(xq_np, x))
+    assert not errs, errs[:5]

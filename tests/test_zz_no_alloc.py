@@ -3,8 +3,12 @@ array instead of a caller workspace) against mf_flat_search, through the C-ABI.
 
 Two searches of different shapes, metrics and engines run back to back on the
 one shared scratch array; each must match mf_flat_search on the same inputs
-within the tolerances the other parity tests use. Collected last so that it
-also runs after every other test has used the library in this process."""
+within the tolerances the other parity tests use, and the first also the CPU
+oracle directly. Repeating both searches must leave the device's free memory
+unchanged: the entry point is for callers that cannot allocate, so a search
+that allocated (or cached an allocation) would fail them. Collected last so
+that it also runs after every other test has used the library in this
+process."""
 import ctypes
 
 import numpy as np
@@ -14,7 +18,7 @@ import torch
 from metalfaiss_b200 import _native as nat
 from metalfaiss_b200 import synthetic as syn
 from metalfaiss_b200.errors import ErrorCode
-from oracle import compare
+from oracle import compare, oracle
 
 pytestmark = pytest.mark.gpu
 
@@ -85,7 +89,33 @@ def test_noalloc_matches_workspace_search_twice(cuda_device):
     torch.cuda.synchronize()
     _check(xq1, xb1, ids1, L2, got1, ref1)
     _check(xq2, xb2, ids2, IP, got2, ref2)
+    # the first search also against the CPU oracle itself
+    q1, b1 = xq1.cpu().numpy(), xb1.cpu().numpy()
+    D_or, I_or = oracle.flat_search(q1, b1, 10, oracle.L2, ids1.cpu().numpy())
+    errs = compare.check_knn(got1[0].cpu().numpy(), got1[1].cpu().numpy(), D_or, I_or,
+                             compare.exact_lookup(q1, b1, oracle.L2, ids1.cpu().numpy()),
+                             atol=compare.l2_atol(q1, b1))
+    assert not errs, errs[:5]
     assert nat.device_error(0) == 0
+
+    # The same two searches again into buffers allocated up front: the
+    # device's free memory must not move (nothing allocated, nothing cached).
+    outs = [(torch.empty((xq1.shape[0], 10), dtype=torch.float32, device=dev),
+             torch.empty((xq1.shape[0], 10), dtype=torch.int64, device=dev)),
+            (torch.empty((xq2.shape[0], 17), dtype=torch.float32, device=dev),
+             torch.empty((xq2.shape[0], 17), dtype=torch.int64, device=dev))]
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info(dev)
+    for (xq, xb, nrm, lo, ids, metric, k), (D, I) in zip(
+            [(xq1, xb1, n1, lo1, ids1, L2, 10), (xq2, xb2, n2, None, ids2, IP, 17)], outs):
+        nat.call("mf_flat_search_noalloc", dev.index, nat.stream_of(dev), nat.ptr(xq),
+                 xq.shape[0], nat.ptr(xb), nat.ptr(nrm), nat.ptr(lo), xb.shape[0], xq.shape[1],
+                 metric, k, nat.ptr(ids), nat.ptr(D), nat.ptr(I))
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info(dev)
+    assert free1 == free0, f"device free memory moved by {free0 - free1} bytes"
+    assert torch.equal(outs[0][1], got1[1]) and torch.equal(outs[1][1], got2[1])
+    assert torch.equal(outs[0][0], got1[0]) and torch.equal(outs[1][0], got2[0])
 
 
 def test_noalloc_rejects_searches_beyond_the_scratch(cuda_device):
