@@ -66,6 +66,7 @@ constexpr int kTqM = 128;          // queries per item = TMEM lanes
 constexpr int kTqEpiThreads = 128;
 constexpr int kTqMaxD = 1024;
 constexpr int kTqK = 32;  // list slots per query row (k <= 32)
+constexpr int kTqKBig = 128;  // list slots per query row for 32 < k <= 128
 constexpr int kTqMaxSmem = 227 * 1024 - 512;
 // All 512 TMEM columns hold accumulators: 512 / BN tiles in flight between
 // the MMA warp and the epilogue (4 at BN = 128).
@@ -290,7 +291,10 @@ __device__ __forceinline__ unsigned int tq_accept(const uint32_t (&r)[32], const
 // by the list's power of two s_l); per pair, the query norm, the bound, s_q
 // and 1 / (s_q s_l) come from a.pair_qn / pair_thr / pair_sq / pair_sc, and
 // each pair's kept slots are written with their count (a.pair_cnt).
-template <int METRIC, int BN, bool ATM, bool CONV, bool FLT = false>
+//
+// KC: list slots per query row: kTqK (k <= 32) or kTqKBig (k <= 128, with
+// 64-row tiles so the larger lists fit in shared memory beside the stages).
+template <int METRIC, int BN, bool ATM, bool CONV, bool FLT = false, int KC = kTqK>
 __global__ void __launch_bounds__(ATM ? kTqThreadsAtm : kTqThreads, 1)
     tq_scan_kernel(const ScanArgs a, const __grid_constant__ TqMaps maps, const TqLayout L) {
   extern __shared__ unsigned char smem_raw[];
@@ -696,7 +700,7 @@ __global__ void __launch_bounds__(ATM ? kTqThreadsAtm : kTqThreads, 1)
     long long p_stage = 0, p_filter = 0, p_append = 0, p_tld = 0, p_nappend = 0;
     const long long p_start = clock64();
 #endif
-    unsigned long long* my_lists = lists + (size_t)(warp * 32) * kTqK;
+    unsigned long long* my_lists = lists + (size_t)(warp * 32) * KC;
     unsigned long long* my_bufs = cbuf + (size_t)(warp * 32) * 33;
     unsigned long long* own_buf = my_bufs + lane * 33;
     // Merges the buffered candidates of the rows in `who` (a warp-uniform
@@ -708,6 +712,25 @@ __global__ void __launch_bounds__(ATM ? kTqThreadsAtm : kTqThreads, 1)
     // thread's own query).
     auto merge_rows = [&](unsigned int who, int& cnt_reg, unsigned long long& thr_reg,
                           unsigned long long bnd, int qrow) {
+      if constexpr (KC > kTqK) {
+        // longer lists: one row at a time, the rank merge of the SIMT scan
+        // (sorted batch; every element's new place is its old one plus its
+        // rank in the other sequence)
+        while (who) {
+          const int s0 = __ffs(who) - 1;
+          who &= who - 1;
+          const int n0 = __shfl_sync(0xffffffffu, cnt_reg, s0);
+          const unsigned long long nk =
+              merge_into_list<KC>(my_lists + (size_t)s0 * KC, my_bufs + s0 * 33, n0, k, lane);
+          if (lane == s0) {
+            thr_reg = nk < bnd ? nk : bnd;
+            cnt_reg = 0;
+            if (a.share && nk != kEmptyKey) atomicMin(a.share + qrow, (unsigned int)(nk >> 32));
+          }
+          __syncwarp();
+        }
+        return;
+      }
       while (who) {
         const int s0 = __ffs(who) - 1;
         who &= who - 1;
@@ -722,8 +745,8 @@ __global__ void __launch_bounds__(ATM ? kTqThreadsAtm : kTqThreads, 1)
         unsigned long long c[2], x[2];
         c[0] = lane < n0 ? my_bufs[s0 * 33 + lane] : kEmptyKey;
         c[1] = lane < n1 ? my_bufs[s1r * 33 + lane] : kEmptyKey;
-        unsigned long long* l0 = my_lists + (size_t)s0 * kTqK;
-        unsigned long long* l1 = my_lists + (size_t)s1r * kTqK;
+        unsigned long long* l0 = my_lists + (size_t)s0 * KC;
+        unsigned long long* l1 = my_lists + (size_t)s1r * KC;
         const unsigned long long e0 = l0[lane];  // ascending; kEmpty past k
         const unsigned long long e1 = l1[lane];
         warp_sort32_n<2>(c, lane);
@@ -797,7 +820,7 @@ __global__ void __launch_bounds__(ATM ? kTqThreadsAtm : kTqThreads, 1)
       // FLT: the accumulators are s_q s_l times the dot products
       const float sc = (FLT && valid) ? a.pair_sc[slot] : 1.0f;
       const float m2s = -2.0f * sc;
-      for (int i = 0; i < 32; ++i) my_lists[i * kTqK + lane] = kEmptyKey;
+      for (int i = 0; i < 32 * KC; i += 32) my_lists[i + lane] = kEmptyKey;
       __syncwarp();
       unsigned long long bound = kEmptyKey;
       if (valid && a.pair_thr) bound = bound_key(a.pair_thr[slot]);
@@ -915,11 +938,11 @@ __global__ void __launch_bounds__(ATM ? kTqThreadsAtm : kTqThreads, 1)
         // the kept slots of each row (a sorted prefix) and their count; rows
         // that kept none write nothing (their counts start at 0)
         const unsigned int some =
-            __ballot_sync(0xffffffffu, slot >= 0 && my_lists[lane * kTqK] != kEmptyKey);
+            __ballot_sync(0xffffffffu, slot >= 0 && my_lists[lane * KC] != kEmptyKey);
         for (unsigned int mq = some; mq != 0u; mq &= mq - 1u) {
           const int qq = __ffs(mq) - 1;
           const long long sq = __shfl_sync(0xffffffffu, slot, qq);
-          const unsigned long long key = lane < k ? my_lists[qq * kTqK + lane] : kEmptyKey;
+          const unsigned long long key = lane < k ? my_lists[qq * KC + lane] : kEmptyKey;
           const unsigned int m = __ballot_sync(0xffffffffu, key != kEmptyKey);
           if (lane == 0) a.pair_cnt[sq] = __popc(m);
           if (key != kEmptyKey) {
@@ -935,7 +958,7 @@ __global__ void __launch_bounds__(ATM ? kTqThreadsAtm : kTqThreads, 1)
         const int kk = e - qq * k;
         const long long sq = __shfl_sync(0xffffffffu, slot, qq);
         if (sq >= 0) {
-          const unsigned long long key = my_lists[qq * kTqK + kk];
+          const unsigned long long key = my_lists[qq * KC + kk];
           float dv;
           long long lv;
           if (key == kEmptyKey) {
@@ -1001,14 +1024,19 @@ __global__ void __launch_bounds__(ATM ? kTqThreadsAtm : kTqThreads, 1)
 typedef void (*TqFn)(const ScanArgs, const TqMaps, const TqLayout);
 
 template <int METRIC>
-TqFn pick_tq(const TqLayout& l, bool conv) {
+TqFn pick_tq(const TqLayout& l, bool conv, int kcap) {
+  if (kcap > kTqK) {  // 64-row tiles, query tile in tensor memory (d <= 128)
+    if (!l.atm || l.BN != 64) return nullptr;
+    return conv ? tq_scan_kernel<METRIC, 64, true, true, false, kTqKBig>
+                : tq_scan_kernel<METRIC, 64, true, false, false, kTqKBig>;
+  }
   if (l.atm)
     return conv ? tq_scan_kernel<METRIC, 128, true, true> : tq_scan_kernel<METRIC, 128, true, false>;
   return l.BN == 256 ? tq_scan_kernel<METRIC, 256, false, false>
                      : tq_scan_kernel<METRIC, 128, false, false>;
 }
 
-int tq_kcap(int k) { return k <= kTqK ? kTqK : 0; }
+int tq_kcap(int k) { return k <= kTqK ? kTqK : (k <= kTqKBig ? kTqKBig : 0); }
 
 int g_engine = 0;  // 0 auto, 1 SIMT only, 2 tensor cores where eligible, 3 = 2 with streamed queries
 
@@ -1018,6 +1046,19 @@ int g_engine = 0;  // 0 auto, 1 SIMT only, 2 tensor cores where eligible, 3 = 2 
 // the query tile streamed beside the rows.
 bool tq_choose(int d, int kcap, TqLayout* out) {
   const int kb32 = (d + 31) / 32 * 32;
+  if (kcap > kTqK) {
+    // 128-key lists (128 KB for the tile's rows): 64-row tiles, query tile in
+    // tensor memory, the deepest ring that fits
+    if (g_engine == 3 || kb32 > kTqMaxDAtm) return false;
+    for (int sa = 5; sa >= 2; --sa) {
+      TqLayout l = tq_layout(d, kcap, 64, sa, true);
+      if (l.total <= (size_t)kTqMaxSmem) {
+        *out = l;
+        return true;
+      }
+    }
+    return false;
+  }
   if (g_engine != 3 && kb32 <= kTqMaxDAtm && kTqTmemCols - 2 * kb32 >= 2 * 128) {
     for (int sa = 5; sa >= 2; --sa) {
       TqLayout l = tq_layout(d, kcap, 128, sa, true);
@@ -1055,7 +1096,7 @@ bool tq_choose_bf(int d, TqLayout* out) {
 
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 std::mutex g_tc_mu;
-int g_tc_attr[64][2][5];  // dynamic smem set per (device, metric, variant)
+int g_tc_attr[64][2][7];  // dynamic smem set per (device, metric, variant)
 
 int encoder(PFN_cuTensorMapEncodeTiled_v12000* out) {
   std::lock_guard<std::mutex> lk(g_tc_mu);
@@ -1285,8 +1326,8 @@ int launch_tc_scan(const ScanArgs& a, int metric, const float* a_lo, int64_t a_r
   MF_CHECK(kcap != 0 && tq_choose(a.d, kcap, &lay), MF_ERR_INVALID_ARGS,
            "tensor-core scan does not fit (d=%d k=%d)", a.d, a.k);
   const bool conv = lay.atm && b_lo == nullptr;  // derive the rows' residuals in the kernel
-  TqFn fn = metric == MF_METRIC_L2 ? pick_tq<MF_METRIC_L2>(lay, conv)
-                                   : pick_tq<MF_METRIC_INNER_PRODUCT>(lay, conv);
+  TqFn fn = metric == MF_METRIC_L2 ? pick_tq<MF_METRIC_L2>(lay, conv, kcap)
+                                   : pick_tq<MF_METRIC_INNER_PRODUCT>(lay, conv, kcap);
   MF_CHECK(fn != nullptr, MF_ERR_METRIC, "metric %d has no tensor-core scan", metric);
   PFN_cuTensorMapEncodeTiled_v12000 enc;
   MF_TRY(encoder(&enc));
@@ -1304,7 +1345,8 @@ int launch_tc_scan(const ScanArgs& a, int metric, const float* a_lo, int64_t a_r
   {
     std::lock_guard<std::mutex> lk(g_tc_mu);
     const int mi = metric == MF_METRIC_L2 ? 0 : 1;
-    const int bi = lay.atm ? (conv ? 3 : 2) : (lay.BN == 256 ? 1 : 0);
+    const int bi = kcap > kTqK ? (conv ? 6 : 5)
+                               : (lay.atm ? (conv ? 3 : 2) : (lay.BN == 256 ? 1 : 0));
     if (device < 0 || device >= 64 || g_tc_attr[device][mi][bi] < (int)lay.total) {
       MF_CUDA(cudaFuncSetAttribute(reinterpret_cast<const void*>(fn),
                                    cudaFuncAttributeMaxDynamicSharedMemorySize, (int)lay.total));

@@ -86,6 +86,20 @@ class CudaError(MetalFaissError, RuntimeError):
         super().__init__(message, ErrorCode.CUDA)
 
 
+class IOFaissError(MetalFaissError, OSError):
+    """python/metalfaiss/errors.py:64-68 (IOError there)."""
+
+    def __init__(self, message: str):
+        super().__init__(message, ErrorCode.IO)
+
+
+class FormatError(MetalFaissError, ValueError):
+    """python/metalfaiss/errors.py:124-128: a file that is not a valid index."""
+
+    def __init__(self, message: str):
+        super().__init__(message, ErrorCode.FORMAT)
+
+
 class DeviceTimeoutError(MetalFaissError, TimeoutError):
     def __init__(self, message: str):
         super().__init__(message, ErrorCode.TIMEOUT)
@@ -101,6 +115,8 @@ _BY_CODE = {
     ErrorCode.METRIC: MetricError,
     ErrorCode.CUDA: CudaError,
     ErrorCode.TIMEOUT: DeviceTimeoutError,
+    ErrorCode.IO: IOFaissError,
+    ErrorCode.FORMAT: FormatError,
 }
 
 _last_error: Optional[MetalFaissError] = None

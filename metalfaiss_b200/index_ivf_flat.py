@@ -226,6 +226,28 @@ class IVFFlatIndex:
         order = np.argsort(-sizes, kind="stable").astype(np.int32)
         self._order = torch.from_numpy(order).to(self.device)
 
+    def _install_lists(self, offsets: torch.Tensor, vecs: torch.Tensor, ids: torch.Tensor) -> None:
+        """Installs a CSR bank as it stands (offsets (nlist + 1) int64; vecs
+        (N, d) grouped by list; ids (N) int64): what read_index restores,
+        without reassigning any row."""
+        n = int(vecs.shape[0])
+        self._clear_lists()
+        if n == 0:
+            return
+        x = as_matrix(vecs, self.d, self.device)
+        self._offsets = offsets.to(self.device, torch.int64).contiguous()
+        self._vecs = x
+        self._norms = compute_norms(x)
+        self._ids = ids.to(self.device, torch.int64).contiguous()
+        if stores_residuals(self._dp, self._residuals):
+            self._lo = torch.empty_like(x)
+            nat.call("mf_tf32_residual", self.device.index, nat.stream_of(self.device),
+                     nat.ptr(x), n, self._dp, nat.ptr(self._lo))
+        self._ntotal = n
+        sizes = np.diff(self._offsets.cpu().numpy())
+        self._order = torch.from_numpy(np.argsort(-sizes, kind="stable").astype(np.int32)).to(
+            self.device)
+
     def add_with_ids(self, xs, ids) -> None:
         self.add(xs, ids)
 
