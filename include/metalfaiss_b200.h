@@ -171,6 +171,53 @@ MF_API int mf_flat_search_noalloc(int device, void* stream, const float* xq, int
                                   int64_t nb, int d, int metric, int k, const int64_t* ids,
                                   float* distances, int64_t* labels);
 
+/* ------------------------------------------------------- binary (Hamming) */
+
+/* Binary vectors of d bits (d a multiple of 8, at most 1024) are stored packed
+ * as W = ceil(d / 32) uint32 words per row: bit j is bit j % 32 of word j / 32,
+ * padding bits zero. The distance is the Hamming distance, the number of
+ * coordinates where two vectors differ, as BinaryFlatIndex.search counts it
+ * (python/metalfaiss/index/binary_flat_index.py:79-86). */
+
+/* Packs n rows of d coordinates (uint8, nonzero = 1) into codes (n, W).
+ * Replaces the uint8 storage of BinaryFlatIndex.add,
+ * python/metalfaiss/index/binary_flat_index.py:27-48. */
+MF_API int mf_binary_pack(int device, void* stream, const uint8_t* x, int64_t n, int d,
+                          uint32_t* codes);
+
+/* The inverse: codes (n, W) -> x (n, d) of 0/1 bytes
+ * (BinaryFlatIndex.reconstruct, python/metalfaiss/unittest/test_binary_flat_index.py:80-96). */
+MF_API int mf_binary_unpack(int device, void* stream, const uint32_t* codes, int64_t n, int d,
+                            uint8_t* x);
+
+MF_API int mf_binary_flat_search_workspace_size(int64_t nq, int64_t nb, int d, int k,
+                                                size_t* bytes);
+
+/* Hamming kNN of xq (nq, W) against xb (nb, W): distances (nq, k) as exact
+ * fp32 integers, labels (nq, k) (ids[pos] when ids != NULL), ascending by
+ * (distance, row); slots beyond nb are (+inf, -1). k <= 256.
+ * Replaces BinaryFlatIndex.search, python/metalfaiss/index/binary_flat_index.py:50-92
+ * (a (nq, nb) distance matrix and a full argsort there). */
+MF_API int mf_binary_flat_search(int device, void* stream, const uint32_t* xq, int64_t nq,
+                                 const uint32_t* xb, int64_t nb, int d, int k,
+                                 const int64_t* ids, float* distances, int64_t* labels,
+                                 void* workspace, size_t workspace_bytes);
+
+MF_API int mf_binary_range_workspace_size(int64_t nq, int64_t nb, int d, size_t* bytes);
+
+/* Range search in two passes over the same workspace: count writes lims
+ * (nq + 1) and *total (the host waits for it); fill writes the (distance,
+ * label) pairs with distance <= radius, per query in row order.
+ * Replaces BinaryFlatIndex.range_search, python/metalfaiss/index/binary_flat_index.py:94-140. */
+MF_API int mf_binary_range_count(int device, void* stream, const uint32_t* xq, int64_t nq,
+                                 const uint32_t* xb, int64_t nb, int d, int radius,
+                                 int64_t* lims, int64_t* total, void* workspace,
+                                 size_t workspace_bytes);
+MF_API int mf_binary_range_fill(int device, void* stream, const uint32_t* xq, int64_t nq,
+                                const uint32_t* xb, int64_t nb, int d, int radius,
+                                const int64_t* lims, const int64_t* ids, float* distances,
+                                int64_t* labels, void* workspace, size_t workspace_bytes);
+
 /* ---------------------------------------------------------------- IVFFlat */
 
 /* Inverted lists are CSR: list l holds rows [list_offsets[l], list_offsets[l+1])

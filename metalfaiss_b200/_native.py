@@ -68,6 +68,13 @@ _SIGNATURES = {
     "mf_timing_reset": ([], I32),
     "mf_launch_count": ([], I64),
     "mf_diag_f16_dot": ([I32, P, I32, P, P, I32, P], I32),
+    "mf_binary_pack": ([I32, P, P, I64, I32, P], I32),
+    "mf_binary_unpack": ([I32, P, P, I64, I32, P], I32),
+    "mf_binary_flat_search_workspace_size": ([I64, I64, I32, I32, PSZ], I32),
+    "mf_binary_flat_search": ([I32, P, P, I64, P, I64, I32, I32, P, P, P, P, SZ], I32),
+    "mf_binary_range_workspace_size": ([I64, I64, I32, PSZ], I32),
+    "mf_binary_range_count": ([I32, P, P, I64, P, I64, I32, I32, P, PI64, P, SZ], I32),
+    "mf_binary_range_fill": ([I32, P, P, I64, P, I64, I32, I32, P, P, P, P, P, SZ], I32),
     "mf_flat_engine": ([I32, I32, I32, I64, I32], I32),
     "mf_set_scan_engine": ([I32], I32),
     "mf_device_error": ([I32, ctypes.POINTER(ctypes.c_int)], I32),

@@ -233,3 +233,37 @@ def ivf_range_search(xq, centroids, offsets, vecs, ids, nprobe, radius, metric=L
         lims.append(sum(len(a) for a in ds))
     return (np.array(lims, np.int64), np.concatenate(ds).astype(np.float32) if ds else np.zeros(0, np.float32),
             np.concatenate(ls).astype(np.int64) if ls else np.zeros(0, np.int64))
+
+
+# ------------------------------------------------------------ binary (Hamming)
+def hamming_distances(xq01, xb01) -> np.ndarray:
+    """Number of coordinates where a query and a row differ, the distance
+    BinaryFlatIndex.search accumulates (python/metalfaiss/index/binary_flat_index.py:79-86)."""
+    xq01 = np.asarray(xq01, np.uint8)
+    xb01 = np.asarray(xb01, np.uint8)
+    out = np.empty((xq01.shape[0], xb01.shape[0]), np.int32)
+    for s in range(0, xq01.shape[0], 16):
+        out[s:s + 16] = (xq01[s:s + 16, None, :] != xb01[None, :, :]).sum(axis=2)
+    return out
+
+
+def hamming_search(xq01, xb01, k, ids=None):
+    """BinaryFlatIndex.search: ascending distances, k clipped to ntotal (:88-92),
+    ties to the lower row (a stable sort)."""
+    d = hamming_distances(xq01, xb01)
+    kk = min(k, d.shape[1])
+    order = np.argsort(d, axis=1, kind="stable")[:, :kk]
+    labels = order.astype(np.int64) if ids is None else np.asarray(ids, np.int64)[order]
+    return np.take_along_axis(d, order, axis=1), labels
+
+
+def hamming_range(xq01, xb01, radius, ids=None):
+    """Rows within Hamming distance <= radius, in row order, with lims
+    (python/metalfaiss/index/binary_flat_index.py:94-150)."""
+    d = hamming_distances(xq01, xb01)
+    mask = d <= radius
+    lims = np.zeros(len(d) + 1, np.int64)
+    np.cumsum(mask.sum(axis=1), out=lims[1:])
+    qi, ri = np.nonzero(mask)
+    labels = ri.astype(np.int64) if ids is None else np.asarray(ids, np.int64)[ri]
+    return lims, d[qi, ri], labels

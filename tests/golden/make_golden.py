@@ -245,6 +245,39 @@ def gen_kmeans(m, out):
     out["kmeans_centroids"] = np_(cent).astype(np.float32)
 
 
+def gen_binary(m, out):
+    """BinaryFlatIndex search / reconstruct, python/metalfaiss/index/binary_flat_index.py:27-165.
+    The class declares no _add/_train/_search/_reconstruct, which its abstract
+    base requires, and assigns the base's read-only ntotal, so it cannot be
+    instantiated as written; a subclass supplies those members and leaves the
+    class's own add, search and reconstruct in charge. (Its range_search builds
+    a SearchRangeResult its own validation rejects; range search is restated
+    in the oracle.)"""
+    import importlib
+
+    b = importlib.import_module("metalfaiss.index.binary_flat_index")
+    noop = lambda self, *a, **k: None  # noqa: E731
+    Concrete = type("BinaryFlatConcrete", (b.BinaryFlatIndex,), {
+        "_add": noop, "_train": noop, "_search": noop, "_reconstruct": noop,
+        "ntotal": property(lambda s: s._ntotal, lambda s, v: setattr(s, "_ntotal", v))})
+    cases = []
+    for (n, d, nq, k, seed) in [(300, 64, 12, 10, 40), (1000, 256, 9, 32, 41), (50, 8, 5, 60, 42)]:
+        x = rng(seed).integers(0, 2, size=(n, d)).astype(np.uint8)
+        q = rng(seed + 1).integers(0, 2, size=(nq, d)).astype(np.uint8)
+        q[:2] = x[[3, n - 1]]  # two self-queries
+        idx = Concrete(d)
+        idx.add(mxs.array(x))
+        D, I = idx.search(mxs.array(q), k)
+        tag = f"binary_{n}_{d}_{k}"
+        out[tag + "_xb"] = x
+        out[tag + "_xq"] = q
+        out[tag + "_D"] = np_(D).astype(np.int32)
+        out[tag + "_I"] = np_(I).astype(np.int64)
+        out[tag + "_rec"] = np_(idx.reconstruct(5)).astype(np.uint8)
+        cases.append(tag)
+    out["binary_cases"] = np.array(cases)
+
+
 def main():
     mods = load_reference()
     out = {}
@@ -253,6 +286,7 @@ def main():
     gen_ivf(mods, out)
     gen_range(mods, out)
     gen_kmeans(mods, out)
+    gen_binary(mods, out)
     path = HERE / "reference_golden.npz"
     np.savez_compressed(path, **out)
     print(f"[golden] wrote {path} ({path.stat().st_size // 1024} KiB, {len(out)} arrays)")

@@ -79,6 +79,16 @@ take_along_axis = _wrap(lambda x, idx, axis: np.take_along_axis(x, np.asarray(id
 reshape = _wrap(lambda x, shape: np.reshape(x, shape))
 copy = _wrap(np.copy)
 topk = _wrap(lambda x, k, axis=-1: np.sort(x, axis=axis)[..., -k:])
+not_equal = _wrap(np.not_equal)
+less = _wrap(np.less)
+greater_equal = _wrap(np.greater_equal)
+all = _wrap(lambda x, axis=None: np.all(x, axis=axis))  # noqa: A001 - MLX's name
+any = _wrap(lambda x, axis=None: np.any(x, axis=axis))  # noqa: A001 - MLX's name
+bitwise_and = _wrap(lambda a, b: np.bitwise_and(a, np.asarray(b, np.asarray(a).dtype)))
+bitwise_or = _wrap(lambda a, b: np.bitwise_or(a, np.asarray(b, np.asarray(a).dtype)))
+bitwise_xor = _wrap(lambda a, b: np.bitwise_xor(a, np.asarray(b, np.asarray(a).dtype)))
+right_shift = _wrap(lambda a, b: np.right_shift(a, np.asarray(b, np.asarray(a).dtype)))
+left_shift = _wrap(lambda a, b: np.left_shift(a, np.asarray(b, np.asarray(a).dtype)))
 
 
 def eval(*arrays):  # noqa: A001 - MLX's name

@@ -91,3 +91,17 @@ def test_kmeans():
     k = len(perm)
     c = oracle.kmeans_train(x, k, iters, seed=0, init=x[perm])
     np.testing.assert_allclose(c, G["kmeans_centroids"], rtol=1e-4, atol=1e-4)
+
+
+def test_hamming_oracle_matches_reference_binary_flat():
+    """oracle.hamming_search against BinaryFlatIndex.search run from the
+    reference's own module (tests/golden/make_golden.py gen_binary)."""
+    g = G
+    for tag in g["binary_cases"]:
+        tag = str(tag)
+        xb, xq = g[tag + "_xb"], g[tag + "_xq"]
+        k = g[tag + "_D"].shape[1]
+        D, I = oracle.hamming_search(xq, xb, k)
+        np.testing.assert_array_equal(D, g[tag + "_D"])
+        np.testing.assert_array_equal(I, g[tag + "_I"])
+        np.testing.assert_array_equal(xb[5:6], g[tag + "_rec"])
