@@ -473,6 +473,11 @@ MF_API int mf_timing_read(const char* kernel, double* total_ms, int64_t* launche
 /* Number of kernels this library has launched in this process (all devices). */
 MF_API int64_t mf_launch_count(void);
 
+/* Epilogue warpgroups of the filter search's tensor-core pass: 2 (the
+ * default; each takes half of every tile's columns) or 1. Results are the
+ * same; for tests and measurements. No reference counterpart. */
+MF_API int mf_set_filter_groups(int groups);
+
 /* Scan engine for the L2 / inner-product top-k scans: 0 = automatic (tensor
  * cores where the shape allows), 1 = SIMT only, 2 = tensor cores where the
  * shape allows, 3 = as 2 but with the query tile streamed through shared

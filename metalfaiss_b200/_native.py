@@ -77,6 +77,7 @@ _SIGNATURES = {
     "mf_binary_range_fill": ([I32, P, P, I64, P, I64, I32, I32, P, P, P, P, P, SZ], I32),
     "mf_flat_engine": ([I32, I32, I32, I64, I32], I32),
     "mf_set_scan_engine": ([I32], I32),
+    "mf_set_filter_groups": ([I32], I32),
     "mf_device_error": ([I32, ctypes.POINTER(ctypes.c_int)], I32),
     "mf_timing_read": ([ctypes.c_char_p, ctypes.POINTER(ctypes.c_double), PI64], I32),
 }

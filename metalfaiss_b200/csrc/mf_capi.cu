@@ -1198,6 +1198,13 @@ int mf_tf32_residual(int device, void* stream, const float* x, int64_t n, int d,
   return launch_tf32_residual(x, n, d, lo, (cudaStream_t)stream);
 }
 
+int mf_set_filter_groups(int groups) {
+  clear_error();
+  MF_CHECK(groups == 1 || groups == 2, MF_ERR_INVALID_ARGS, "groups=%d (1 or 2)", groups);
+  set_filter_groups(groups);
+  return MF_OK;
+}
+
 int mf_set_scan_engine(int engine) {
   clear_error();
   MF_CHECK(engine >= 0 && engine <= 3, MF_ERR_INVALID_ARGS, "engine %d not in {0,1,2,3}", engine);

@@ -122,6 +122,7 @@ int launch_tf32_residual(const float* x, int64_t n, int d, float* lo, cudaStream
 int launch_gather_queries(const float* xq, int d, const int* pairs, const int* n_pairs,
                           int64_t max_pairs, int P, float* g_hi, float* g_lo, cudaStream_t stream);
 void set_scan_engine(int engine);
+void set_filter_groups(int groups);
 int scan_engine();
 int read_device_error(int* code);
 

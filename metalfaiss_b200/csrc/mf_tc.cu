@@ -85,17 +85,19 @@ constexpr int kTqMaxDAtm = 128;
 
 struct TqLayout {
   int SA, KB, BN;  // KB: K-blocks of 128 bytes (32 fp32 or, with bf, 64 fp16)
+  int ew;    // epilogue warpgroups (2: each takes half of every tile's columns)
   int atm;   // query tile in tensor memory (columns [0, 2*KB*32): hi then lo)
   int bf;    // 16-bit operands (filter scan): A in columns [0, KB*32), no residuals
   int nacc;  // accumulator buffers in tensor memory
   int acc0;  // first accumulator column
   size_t stage, a_hi, a_lo, b_hi, b_lo;  // offsets within a stage
-  size_t lists, scratch, xn, bars, total;
+  size_t lists, scratch, xn, rowthr, bars, total;
 };
 
-TqLayout tq_layout(int d, int kcap, int BN, int SA, bool atm, bool bf = false) {
+TqLayout tq_layout(int d, int kcap, int BN, int SA, bool atm, bool bf = false, int ew = 1) {
   TqLayout s;
   s.SA = SA;
+  s.ew = ew;
   s.KB = bf ? (d + 63) / 64 : (d + 31) / 32;
   s.BN = BN;
   s.atm = atm ? 1 : 0;
@@ -116,14 +118,18 @@ TqLayout tq_layout(int d, int kcap, int BN, int SA, bool atm, bool bf = false) {
   // the filter scan's stage holds a whole tile (all K-blocks): one hand-off per tile
   s.stage = bf ? size_t(s.KB) * BN * 128 : s.b_lo + size_t(BN) * 128;
   size_t o = size_t(SA) * s.stage;
-  s.lists = o;
-  o += size_t(kTqM) * kcap * 8;
-  s.scratch = o;  // candidate buffers: 128 rows x 33 keys (one row per query row)
-  o += size_t(kTqM) * 33 * 8;
+  s.lists = o;  // per epilogue warpgroup: 128 rows x kcap keys
+  o += size_t(ew) * kTqM * kcap * 8;
+  s.scratch = o;  // candidate buffers: 128 rows x 33 keys per warpgroup
+  o += size_t(ew) * kTqM * 33 * 8;
   s.xn = o;  // row norms of the tile: a double buffer per epilogue warp
-  o += size_t(kTqEpiThreads / 32) * 2 * BN * 4;
+  o += size_t(ew) * (kTqEpiThreads / 32) * 2 * BN * 4;
+  s.rowthr = o;  // ew > 1: each row's best k-th key over the warpgroups
+  o += ew > 1 ? size_t(kTqM) * 8 : 0;
   s.bars = o;
-  o += size_t(3 * SA + 2 * kTqMaxAcc + 2 * kTqQueue + 3) * 8 + 16 + kTqQueue * 32;
+  // mbarriers, then the item queue (kTqQueue slots of at most 48 bytes) and
+  // the tensor-memory address, abort flag and sequence counters
+  o += size_t(3 * SA + 2 * kTqMaxAcc + 2 * kTqQueue + 5) * 8 + kTqQueue * 48 + 32;
   s.total = o + 1024;
   return s;
 }
@@ -294,9 +300,19 @@ __device__ __forceinline__ unsigned int tq_accept(const uint32_t (&r)[32], const
 //
 // KC: list slots per query row: kTqK (k <= 32) or kTqKBig (k <= 128, with
 // 64-row tiles so the larger lists fit in shared memory beside the stages).
-template <int METRIC, int BN, bool ATM, bool CONV, bool FLT = false, int KC = kTqK>
-__global__ void __launch_bounds__(ATM ? kTqThreadsAtm : kTqThreads, 1)
+//
+// EW: epilogue warpgroups. With 2 (the filter scan), warps 10-13 form a second
+// epilogue warpgroup: each group takes half of every tile's columns with its
+// own per-row lists and candidate buffers, the rows' thresholds are shared
+// through shared memory (any group's k-th key bounds the union's), and at the
+// end of an item the second group's lists are merged into the first's, which
+// writes the results. Two warps per SM sub-partition then hide each other's
+// latencies in the per-column filter that bounds this scan.
+template <int METRIC, int BN, bool ATM, bool CONV, bool FLT = false, int KC = kTqK, int EW = 1>
+__global__ void __launch_bounds__((ATM ? kTqThreadsAtm : kTqThreads) + (EW - 1) * kTqEpiThreads, 1)
     tq_scan_kernel(const ScanArgs a, const __grid_constant__ TqMaps maps, const TqLayout L) {
+  static_assert(EW == 1 || (EW == 2 && FLT && ATM && KC == kTqK),
+                "two epilogue warpgroups are built for the filter scan only");
   extern __shared__ unsigned char smem_raw[];
   const int NACC = L.nacc;
   unsigned char* base = reinterpret_cast<unsigned char*>(
@@ -314,7 +330,10 @@ __global__ void __launch_bounds__(ATM ? kTqThreadsAtm : kTqThreads, 1)
   uint64_t* afull = qempty + kTqQueue;  // query tile written to tensor memory
   uint64_t* afree = afull + 1;          // MMAs of the previous item done with it
   uint64_t* mdone = afree + 1;          // every MMA of this CTA has completed
-  QSlot* s_q = reinterpret_cast<QSlot*>(mdone + 1);
+  uint64_t* wgdone = mdone + 1;         // EW > 1: the second group's lists are final
+  uint64_t* wgfree = wgdone + 1;        // EW > 1: the first group has read them
+  unsigned long long* rowthr = reinterpret_cast<unsigned long long*>(base + L.rowthr);
+  QSlot* s_q = reinterpret_cast<QSlot*>(wgfree + 1);
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(s_q + kTqQueue);
   int* s_abort = reinterpret_cast<int*>(s_tmem + 1);
   uint32_t* s_seq = reinterpret_cast<uint32_t*>(s_abort + 1);  // [0] consumed, [1] issued
@@ -347,22 +366,25 @@ __global__ void __launch_bounds__(ATM ? kTqThreadsAtm : kTqThreads, 1)
     }
     for (int i = 0; i < NACC; ++i) {
       mbar_init(&accf[i], 1);
-      mbar_init(&acce[i], kTqEpiThreads);
+      mbar_init(&acce[i], kTqEpiThreads * EW);
     }
     // readers of each queue slot: the MMA lane and one lane per epilogue
     // (and loader) warp
     for (int i = 0; i < kTqQueue; ++i) {
       mbar_init(&qfull[i], 1);
-      mbar_init(&qempty[i], ATM ? 9 : 5);
+      mbar_init(&qempty[i], (ATM ? 9 : 5) + 4 * (EW - 1));
     }
     mbar_init(afull, kTqM);
     mbar_init(afree, 1);
     mbar_init(mdone, 1);
+    mbar_init(wgdone, 4);
+    mbar_init(wgfree, 4);
     *s_abort = 0;
     s_seq[0] = 0;
     s_seq[1] = 0;
     fence_mbar_init();
   }
+  if (EW > 1 && tid < kTqM) rowthr[tid] = kEmptyKey;
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -527,7 +549,7 @@ __global__ void __launch_bounds__(ATM ? kTqThreadsAtm : kTqThreads, 1)
       // a role gave up early
       mma_commit(mdone);
     }
-  } else if (ATM && warp >= 6) {
+  } else if (ATM && warp >= 6 && warp < 10) {
     // ------------------------------------------ query tile loader + residuals
     // Thread t of warps 6-9 owns TMEM lane 32*(warp%4)+lane = query row of
     // the item. Per item it writes the query tile to its lane once the
@@ -700,8 +722,18 @@ __global__ void __launch_bounds__(ATM ? kTqThreadsAtm : kTqThreads, 1)
     long long p_stage = 0, p_filter = 0, p_append = 0, p_tld = 0, p_nappend = 0;
     const long long p_start = clock64();
 #endif
-    unsigned long long* my_lists = lists + (size_t)(warp * 32) * KC;
-    unsigned long long* my_bufs = cbuf + (size_t)(warp * 32) * 33;
+    // eg: this warp's epilogue group; eq: its quarter of the tensor-memory
+    // lanes (a warp reads lanes 32 (warp % 4) ...); erow: this thread's row of
+    // the tile. Group eg takes columns [cbeg, cend) of every tile.
+    const int eg = EW > 1 && warp >= 10 ? 1 : 0;
+    const int eq = warp & 3;
+    const int erow = 32 * eq + lane;
+    const int ewarp = eg * 4 + eq;
+    constexpr int kCols = BN / EW;
+    const int cbeg = eg * kCols;
+    const int cend = cbeg + kCols;
+    unsigned long long* my_lists = lists + (size_t)eg * kTqM * KC + (size_t)(eq * 32) * KC;
+    unsigned long long* my_bufs = cbuf + (size_t)eg * kTqM * 33 + (size_t)(eq * 32) * 33;
     unsigned long long* own_buf = my_bufs + lane * 33;
     // Merges the buffered candidates of the rows in `who` (a warp-uniform
     // lane mask) into their sorted lists, two rows at a time so the shuffles
@@ -767,12 +799,14 @@ __global__ void __launch_bounds__(ATM ? kTqThreadsAtm : kTqThreads, 1)
           cnt_reg = 0;
           if (!FLT && a.share && nk0 != kEmptyKey)
             atomicMin(a.share + qrow, (unsigned int)(nk0 >> 32));
+          if (EW > 1 && nk0 != kEmptyKey) atomicMin(rowthr + erow, nk0);
         }
         if (lane == s1) {
           thr_reg = nk1 < bnd ? nk1 : bnd;
           cnt_reg = 0;
           if (!FLT && a.share && nk1 != kEmptyKey)
             atomicMin(a.share + qrow, (unsigned int)(nk1 >> 32));
+          if (EW > 1 && nk1 != kEmptyKey) atomicMin(rowthr + erow, nk1);
         }
         __syncwarp();
       }
@@ -781,13 +815,13 @@ __global__ void __launch_bounds__(ATM ? kTqThreadsAtm : kTqThreads, 1)
     // load latency overlaps the previous tile's epilogue; each warp stages its
     // own copy, so no barrier spans the four warps. pf_r0 tags the tile the
     // registers hold; a mismatch (first tile, an empty item) reloads.
-    constexpr int kPf = BN / 32;
+    constexpr int kPf = kCols / 32;
     float xn_pf[kPf];
     long long pf_r0 = -1;
     auto load_norms = [&](long long r0, long long re) {
 #pragma unroll
       for (int i = 0; i < kPf; ++i) {
-        const long long r = r0 + lane + 32 * i;
+        const long long r = r0 + cbeg + lane + 32 * i;
         xn_pf[i] = r < re ? a.xnorms[r] : 0.0f;
       }
       pf_r0 = r0;
@@ -802,15 +836,15 @@ __global__ void __launch_bounds__(ATM ? kTqThreadsAtm : kTqThreads, 1)
       if (item < 0) break;
       const long long nrows = it.re > it.rb ? it.re - it.rb : 0;
       const int nT = (int)((nrows + BN - 1) / BN);
-      const bool valid = tid < it.nq_item;
+      const bool valid = erow < it.nq_item;
       long long slot = -1;
       int q = 0;
       if (valid) {
         if (a.flat) {
-          q = it.a_row0 + tid;
+          q = it.a_row0 + erow;
           slot = a.direct ? q : (long long)q * a.P + it.part;
         } else {
-          const int pr = a.pairs[it.a_row0 + tid];
+          const int pr = a.pairs[it.a_row0 + erow];
           q = pr / a.P;
           slot = pr;
         }
@@ -850,9 +884,9 @@ __global__ void __launch_bounds__(ATM ? kTqThreadsAtm : kTqThreads, 1)
         if (METRIC == MF_METRIC_L2) {
           // row norms of this tile, shared by the four epilogue warps
           if (pf_r0 != r0) load_norms(r0, it.re);
-          float* xs = xn_s + (warp * 2 + (tt & 1)) * BN;
+          float* xs = xn_s + (ewarp * 2 + (tt & 1)) * BN;
 #pragma unroll
-          for (int i = 0; i < kPf; ++i) xs[lane + 32 * i] = xn_pf[i];
+          for (int i = 0; i < kPf; ++i) xs[cbeg + lane + 32 * i] = xn_pf[i];
           __syncwarp();
           // issue the next tile's loads now; they land while this tile runs
           if (t + 1 < nT) {
@@ -874,7 +908,12 @@ __global__ void __launch_bounds__(ATM ? kTqThreadsAtm : kTqThreads, 1)
         ++p_tiles;
 #endif
         tc_fence_after();
-        const float* xs = xn_s + (warp * 2 + (tt & 1)) * BN;
+        if (EW > 1) {
+          // the other group's best k-th key for this row bounds it too
+          const unsigned long long o = *(volatile unsigned long long*)(rowthr + erow);
+          if (o < thr) thr = o;
+        }
+        const float* xs = xn_s + (ewarp * 2 + (tt & 1)) * BN;
         // One 32-column chunk: filter, merge rows that would overflow, append.
         auto chunk = [&](uint32_t (&r)[32], int c0) {
           const long long rc = r0 + c0;
@@ -913,16 +952,16 @@ __global__ void __launch_bounds__(ATM ? kTqThreadsAtm : kTqThreads, 1)
 #endif
         };
         // TMEM loads are double-buffered: chunk c+1 loads while c is filtered.
-        const uint32_t tb = tmem + ((uint32_t)(warp * 32) << 16) + L.acc0 + b * BN;
+        const uint32_t tb = tmem + ((uint32_t)(eq * 32) << 16) + L.acc0 + b * BN;
         uint32_t ra[32], rb[32];
-        tmem_ld32_async(tb, ra);
+        tmem_ld32_async(tb + cbeg, ra);
 #pragma unroll 1
-        for (int c0 = 0; c0 < BN; c0 += 64) {
+        for (int c0 = cbeg; c0 < cend; c0 += 64) {
           TQL(p_tld, tmem_wait_ld(ra));
           tmem_ld32_async(tb + c0 + 32, rb);
           chunk(ra, c0);
           TQL(p_tld, tmem_wait_ld(rb));
-          if (c0 + 64 < BN) tmem_ld32_async(tb + c0 + 64, ra);
+          if (c0 + 64 < cend) tmem_ld32_async(tb + c0 + 64, ra);
           chunk(rb, c0 + 32);
         }
         tc_fence_before();
@@ -934,6 +973,38 @@ __global__ void __launch_bounds__(ATM ? kTqThreadsAtm : kTqThreads, 1)
 #endif
       const unsigned int pending = __ballot_sync(0xffffffffu, cnt > 0);
       if (pending) merge_rows(pending, cnt, thr, bound, q);
+      if constexpr (EW > 1) {
+        // The second group hands its rows' lists to the first, which merges
+        // them into its own (the k smallest of both: the elementwise minimum
+        // against the other list reversed is bitonic) and writes the results.
+        // Both groups take the same items in the same order, so the item's
+        // queue index gives the handshake's phase. Each row's shared k-th key
+        // is cleared before the second group may start the next item.
+        const uint32_t ph = qi & 1;
+        if (eg == 1) {
+          __syncwarp();
+          if (lane == 0) mbar_arrive(wgdone);
+          if (!mbar_wait(wgfree, ph, s_abort, &g_device_error)) break;
+          continue;
+        }
+        if (!mbar_wait(wgdone, ph, s_abort, &g_device_error)) break;
+        const unsigned long long* other = lists + (size_t)kTqM * KC + (size_t)(eq * 32) * KC;
+        for (int r = 0; r < 32; r += 2) {
+          unsigned long long x[2];
+#pragma unroll
+          for (int i = 0; i < 2; ++i) {
+            const unsigned long long e0 = my_lists[(r + i) * KC + lane];
+            const unsigned long long e1 = other[(r + i) * KC + 31 - lane];
+            x[i] = e0 < e1 ? e0 : e1;
+          }
+          warp_bitonic_clean32_n<2>(x, lane);
+#pragma unroll
+          for (int i = 0; i < 2; ++i) my_lists[(r + i) * KC + lane] = lane < k ? x[i] : kEmptyKey;
+        }
+        rowthr[erow] = kEmptyKey;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(wgfree);
+      }
       if (FLT) {
         // the kept slots of each row (a sorted prefix) and their count; rows
         // that kept none write nothing (their counts start at 0)
@@ -1039,6 +1110,7 @@ TqFn pick_tq(const TqLayout& l, bool conv, int kcap) {
 int tq_kcap(int k) { return k <= kTqK ? kTqK : (k <= kTqKBig ? kTqKBig : 0); }
 
 int g_engine = 0;  // 0 auto, 1 SIMT only, 2 tensor cores where eligible, 3 = 2 with streamed queries
+int g_filter_groups = 2;  // epilogue warpgroups of the filter scan (1 or 2)
 
 // With d <= 128 the query tile (hi and lo) lives in tensor memory next to two
 // accumulator buffers, and shared memory holds only row stages: the deepest
@@ -1084,11 +1156,15 @@ bool tq_choose(int d, int kcap, TqLayout* out) {
 // that fits. (d >= 64: no tile box wider than the rows.)
 bool tq_choose_bf(int d, TqLayout* out) {
   if (d < 64 || d > kTqMaxDAtm || d % 8 != 0) return false;
-  for (int sa = 8; sa >= 2; --sa) {
-    TqLayout l = tq_layout(d, kTqK, 128, sa, true, true);
-    if (l.total <= (size_t)kTqMaxSmem) {
-      *out = l;
-      return true;
+  // two epilogue warpgroups where their lists and buffers leave room for a
+  // ring of at least two stages (g_filter_groups = 1 forces one)
+  for (int ew = g_filter_groups; ew >= 1; --ew) {
+    for (int sa = 8; sa >= 2; --sa) {
+      TqLayout l = tq_layout(d, kTqK, 128, sa, true, true, ew);
+      if (l.total <= (size_t)kTqMaxSmem) {
+        *out = l;
+        return true;
+      }
     }
   }
   return false;
@@ -1096,7 +1172,7 @@ bool tq_choose_bf(int d, TqLayout* out) {
 
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 std::mutex g_tc_mu;
-int g_tc_attr[64][2][7];  // dynamic smem set per (device, metric, variant)
+int g_tc_attr[64][2][8];  // dynamic smem set per (device, metric, variant)
 
 int encoder(PFN_cuTensorMapEncodeTiled_v12000* out) {
   std::lock_guard<std::mutex> lk(g_tc_mu);
@@ -1278,6 +1354,7 @@ int launch_f16_probe_tc(const void* a, const void* b, int d, float* out, cudaStr
 }
 
 void set_scan_engine(int e) { g_engine = e; }
+void set_filter_groups(int g) { g_filter_groups = g == 1 ? 1 : 2; }
 int scan_engine() { return g_engine; }
 
 int tc_group() { return kTqM; }
@@ -1380,7 +1457,9 @@ int launch_tc_filter(const ScanArgs& a, int64_t b_rows, int64_t total_items, int
   MF_CHECK(!a.flat && a.pair_qn && a.pair_thr && a.pair_sq && a.pair_sc && a.pair_cnt &&
                a.centroids && a.items && a.item_total,
            MF_ERR_INVALID_ARGS, "filter scan needs IVF items and its per-pair arrays");
-  TqFn fn = tq_scan_kernel<MF_METRIC_L2, 128, true, false, true>;
+  TqFn fn = lay.ew == 2 ? tq_scan_kernel<MF_METRIC_L2, 128, true, false, true, kTqK, 2>
+                        : tq_scan_kernel<MF_METRIC_L2, 128, true, false, true, kTqK, 1>;
+  const int slot = lay.ew == 2 ? 7 : 4;
   PFN_cuTensorMapEncodeTiled_v12000 enc;
   MF_TRY(encoder(&enc));
   TqMaps maps;
@@ -1388,10 +1467,10 @@ int launch_tc_filter(const ScanArgs& a, int64_t b_rows, int64_t total_items, int
   MF_TRY(make_map_f16(enc, &maps.b_hi, a.xb, a.d, b_rows, lay.BN));
   {
     std::lock_guard<std::mutex> lk(g_tc_mu);
-    if (device < 0 || device >= 64 || g_tc_attr[device][0][4] < (int)lay.total) {
+    if (device < 0 || device >= 64 || g_tc_attr[device][0][slot] < (int)lay.total) {
       MF_CUDA(cudaFuncSetAttribute(reinterpret_cast<const void*>(fn),
                                    cudaFuncAttributeMaxDynamicSharedMemorySize, (int)lay.total));
-      if (device >= 0 && device < 64) g_tc_attr[device][0][4] = (int)lay.total;
+      if (device >= 0 && device < 64) g_tc_attr[device][0][slot] = (int)lay.total;
     }
   }
   if (total_items <= 0) return MF_OK;
@@ -1400,7 +1479,8 @@ int launch_tc_filter(const ScanArgs& a, int64_t b_rows, int64_t total_items, int
   long long grid = num_sms(device);
   if (grid > total_items) grid = total_items;
   ScopedTiming tm("scan_topk_ivf_filter", stream);
-  fn<<<(unsigned int)grid, kTqThreadsAtm, lay.total, stream>>>(a, maps, lay);
+  fn<<<(unsigned int)grid, kTqThreadsAtm + (lay.ew - 1) * kTqEpiThreads, lay.total, stream>>>(
+      a, maps, lay);
   MF_LAUNCH_CHECK();
   return MF_OK;
 }

@@ -168,3 +168,25 @@ def test_dims_outside_the_filter_take_the_exact_scan(cuda_device, d):
                                     nat.ptr(idx._norms), nat.ptr(idx.quantizer._xb.buf), n,
                                     nat.ptr(h), nat.ptr(rn), nat.ptr(stats))
     assert status == 6, lib.mf_last_error()
+
+
+@pytest.mark.parametrize("d,nq", [(128, 3000), (64, 2500), (96, 700)])
+def test_filter_one_and_two_epilogue_groups_agree(cuda_device, d, nq):
+    """The filter pass with one epilogue warpgroup and with two (each taking
+    half of every tile's columns, sharing the rows' thresholds and merging at
+    the end of an item) gives the same results, and both equal the oracle.
+    Batches large enough that most lists are probed by more than 16 queries."""
+    x, cen, _ = syn.mixture(60000, d, 48, seed=131 + d)
+    idx = _build(x, 48, seed=131 + d)
+    xq, _, _ = syn.mixture(nq, d, 48, seed=132 + d, centres=cen)
+    lib = nat.load()
+    try:
+        lib.mf_set_filter_groups(1)
+        idx.nprobe = 6
+        D1, I1 = idx.search(xq, 10).numpy()
+        lib.mf_set_filter_groups(2)
+        D2, I2 = _check(idx, x, xq, 6, 10)
+    finally:
+        lib.mf_set_filter_groups(2)
+    np.testing.assert_array_equal(I1, I2)
+    np.testing.assert_array_equal(D1, D2)
