@@ -218,6 +218,40 @@ MF_API int mf_binary_range_fill(int device, void* stream, const uint32_t* xq, in
                                 const int64_t* lims, const int64_t* ids, float* distances,
                                 int64_t* labels, void* workspace, size_t workspace_bytes);
 
+/* ----------------------------------------------------------------- IVFPQ */
+
+/* Product-quantization codes (IVFPQIndex.add / ProductQuantizer.compute_codes,
+ * python/metalfaiss/index/ivf_pq_index.py:97-113 and
+ * python/metalfaiss/index/product_quantizer.py). x (n, dp) fp32 rows of d
+ * coordinates (dp >= d, a multiple of 4); pq_centroids (M, ksub, d / M)
+ * fp32, ksub <= 256, d / M <= 32, M <= 64. With centroids (nlist, dp) and
+ * labels (n) int64 the residual x - centroids[labels] is encoded (IVFPQ),
+ * else x itself. codes: (n, code_pitch) bytes, code m of row r at
+ * r * code_pitch + m = argmin_j |pq[m][j] - subvector m|^2 (ties to the lowest
+ * j); code_pitch is a multiple of 4 >= M, padding bytes zero. */
+MF_API int mf_pq_encode(int device, void* stream, const float* x, int64_t n, int dp, int d,
+                        int M, int ksub, const float* pq_centroids, const float* centroids,
+                        const int64_t* labels, uint8_t* codes, int code_pitch);
+
+MF_API int mf_ivfpq_search_workspace_size(int64_t nq, int nprobe, int k, size_t* bytes);
+
+/* ADC search of the lists in probes (nq, nprobe) int64 (-1 = none): per
+ * (query q, list l), the distance of a row with codes c is
+ * sum_m |pq[m][c_m] - (q - centroids[l])_m|^2. The lists are CSR: rows
+ * [list_offsets[l], list_offsets[l+1]) of list_codes (rows code_pitch bytes
+ * apart) and list_ids. Results (nq, k) ascending, labels = list_ids[row]
+ * (row positions when list_ids is NULL), empty slots (+inf, -1).
+ * Replaces IVFPQIndex.search, python/metalfaiss/index/ivf_pq_index.py:127-186
+ * (one query at a time on the host there; empty probes give (+inf, 0), :170-174). */
+MF_API int mf_ivfpq_search_preassigned(int device, void* stream, const float* xq, int64_t nq,
+                                       int dp, int d, const int64_t* probes, int nprobe,
+                                       int nlist, const float* centroids,
+                                       const float* pq_centroids, int M, int ksub,
+                                       const int64_t* list_offsets, const uint8_t* list_codes,
+                                       int code_pitch, const int64_t* list_ids, int k,
+                                       float* distances, int64_t* labels, void* workspace,
+                                       size_t workspace_bytes);
+
 /* ---------------------------------------------------------------- IVFFlat */
 
 /* Inverted lists are CSR: list l holds rows [list_offsets[l], list_offsets[l+1])

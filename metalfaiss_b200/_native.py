@@ -75,6 +75,10 @@ _SIGNATURES = {
     "mf_binary_range_workspace_size": ([I64, I64, I32, PSZ], I32),
     "mf_binary_range_count": ([I32, P, P, I64, P, I64, I32, I32, P, PI64, P, SZ], I32),
     "mf_binary_range_fill": ([I32, P, P, I64, P, I64, I32, I32, P, P, P, P, P, SZ], I32),
+    "mf_pq_encode": ([I32, P, P, I64, I32, I32, I32, I32, P, P, P, P, I32], I32),
+    "mf_ivfpq_search_workspace_size": ([I64, I32, I32, PSZ], I32),
+    "mf_ivfpq_search_preassigned": ([I32, P, P, I64, I32, I32, P, I32, I32, P, P, I32, I32, P, P,
+                                     I32, P, I32, P, P, P, SZ], I32),
     "mf_flat_engine": ([I32, I32, I32, I64, I32], I32),
     "mf_set_scan_engine": ([I32], I32),
     "mf_set_filter_groups": ([I32], I32),

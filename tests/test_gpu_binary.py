@@ -43,7 +43,11 @@ def test_binary_knn_equals_oracle(cuda_device, d, k):
     D_ref, I_ref = oracle.hamming_search(xq, xb, k)
     np.testing.assert_array_equal(D, D_ref)
     np.testing.assert_array_equal(I, I_ref)
-    assert (D[:3, 0] == 0).all() and list(I[:3, 0]) == [0, 17, 4999]
+    # self-queries find distance 0 (their own row, or a lower duplicate of it
+    # when d is small enough for duplicates)
+    assert (D[:3, 0] == 0).all()
+    if d >= 64:
+        assert list(I[:3, 0]) == [0, 17, 4999]
 
 
 def test_binary_many_rows_merged_splits_and_ids(cuda_device):
