@@ -16,13 +16,14 @@ from .index_binary_flat import BinaryFlatIndex
 from .index_flat import FlatIndex
 from .index_io import read_index, write_index
 from .index_ivf_flat import IVFFlatIndex
+from .index_ivfpq import IVFPQIndex, ProductQuantizer
 from .metric_type import MetricType
 from .search_result import SearchRangeResult, SearchResult
 
 __version__ = "0.1.0"
 
 __all__ = [
-    "FlatIndex", "IVFFlatIndex", "BinaryFlatIndex", "MetricType", "SearchResult", "SearchRangeResult",
+    "FlatIndex", "IVFFlatIndex", "BinaryFlatIndex", "IVFPQIndex", "ProductQuantizer", "MetricType", "SearchResult", "SearchRangeResult",
     "ClusteringParameters", "KMeans", "kmeans_clustering", "ErrorCode", "MetalFaissError",
     "InvalidArgumentError", "BadStateError", "NotImplementedFaissError", "CudaError",
     "check_error", "get_last_error", "clear_last_error", "IOFaissError", "FormatError",

@@ -267,3 +267,65 @@ def hamming_range(xq01, xb01, radius, ids=None):
     qi, ri = np.nonzero(mask)
     labels = ri.astype(np.int64) if ids is None else np.asarray(ids, np.int64)[ri]
     return lims, d[qi, ri], labels
+
+
+# ------------------------------------------------------------------ IVFPQ
+def pq_encode(x, pq_centroids):
+    """ProductQuantizer.compute_codes (python/metalfaiss/index/product_quantizer.py):
+    per sub-space the nearest centroid (fp64 distances; ties to the lowest code)."""
+    x = np.asarray(x, np.float64)
+    pq = np.asarray(pq_centroids, np.float64)
+    M, ksub, dsub = pq.shape
+    codes = np.empty((len(x), M), np.uint8)
+    for m in range(M):
+        sub = x[:, m * dsub:(m + 1) * dsub]
+        d = ((sub[:, None, :] - pq[m][None, :, :]) ** 2).sum(axis=2)
+        codes[:, m] = np.argmin(d, axis=1)
+    return codes
+
+
+def pq_adc_table(qres, pq_centroids):
+    """IVFPQIndex._adc_lut, python/metalfaiss/index/ivf_pq_index.py:115-125:
+    LUT[m][j] = |pq[m][j] - qres_m|^2, fp32."""
+    pq = np.asarray(pq_centroids, np.float32)
+    M, ksub, dsub = pq.shape
+    q = np.asarray(qres, np.float32).reshape(M, 1, dsub)
+    return np.sum(np.square(pq - q), axis=2, dtype=np.float32)
+
+
+def ivfpq_search(xq, centroids, pq_centroids, offsets, codes, ids, nprobe, k, probes=None):
+    """IVFPQIndex.search, python/metalfaiss/index/ivf_pq_index.py:127-186: coarse
+    top-nprobe, per probed list the ADC scores sum_m LUT[m][code_m] (fp32, in m
+    order), candidates in probe order, stable ascending top-k. Missing slots
+    are (+inf, -1) (the reference pads label 0)."""
+    xq = np.asarray(xq, np.float32)
+    centroids = np.asarray(centroids, np.float32)
+    if probes is None:
+        probes = coarse_probes(xq, centroids, nprobe)
+    codes = np.asarray(codes)
+    M = codes.shape[1]
+    D = np.full((len(xq), k), np.inf, np.float32)
+    I = np.full((len(xq), k), -1, np.int64)
+    for q in range(len(xq)):
+        vals, labs = [], []
+        for l in probes[q]:
+            if l < 0:
+                continue
+            rows = np.arange(offsets[l], offsets[l + 1])
+            if rows.size == 0:
+                continue
+            lut = pq_adc_table(xq[q] - centroids[l], pq_centroids)
+            s = np.zeros(rows.size, np.float32)
+            for m in range(M):
+                s = s + lut[m][codes[rows, m]]
+            vals.append(s)
+            labs.append(np.asarray(ids)[rows])
+        if not vals:
+            continue
+        v = np.concatenate(vals)
+        lb = np.concatenate(labs)
+        kk = min(k, v.size)
+        order = np.argsort(v, kind="stable")[:kk]
+        D[q, :kk] = v[order]
+        I[q, :kk] = lb[order]
+    return D, I
