@@ -218,6 +218,23 @@ MF_API int mf_binary_range_fill(int device, void* stream, const uint32_t* xq, in
                                 const int64_t* lims, const int64_t* ids, float* distances,
                                 int64_t* labels, void* workspace, size_t workspace_bytes);
 
+MF_API int mf_binary_ivf_search_workspace_size(int64_t nq, int nprobe, int k, size_t* bytes);
+
+/* Binary IVF: Hamming kNN of xq (nq, W) over the lists in probes (nq, nprobe)
+ * int64 (-1: none; nprobe <= 64). Lists are CSR: rows [list_offsets[l],
+ * list_offsets[l+1]) of list_codes (rows code_pitch >= W words apart) and
+ * list_ids (NULL: row positions); a list holds fewer than 2^26 rows.
+ * Candidates are ranked by (distance, probe rank, row in list), the order in
+ * which BinaryIVFIndex.search concatenates them
+ * (python/metalfaiss/index/binary_ivf_index.py:150-185); empty slots are
+ * (+inf, -1) (the reference pads label 0). */
+MF_API int mf_binary_ivf_search(int device, void* stream, const uint32_t* xq, int64_t nq,
+                                const int64_t* probes, int nprobe, int nlist,
+                                const int64_t* list_offsets, const uint32_t* list_codes,
+                                int code_pitch, const int64_t* list_ids, int d, int k,
+                                float* distances, int64_t* labels, void* workspace,
+                                size_t workspace_bytes);
+
 /* ----------------------------------------------------------------- IVFPQ */
 
 /* Product-quantization codes (IVFPQIndex.add / ProductQuantizer.compute_codes,
@@ -344,7 +361,10 @@ MF_API int mf_ivf_search_bounded(int device, void* stream, const float* xq, int6
  * its list's centroid)), list_rnorms (ntotal) = the squared norms of those
  * fp32 residuals, list_stats (nlist, 4) = per list an upper bound on the
  * residual norms, the largest list_norms entry, the power-of-two scale s_l
- * and 0; mf_ivf_filter_bank writes all three (after every add, from the CSR
+ * and the power of two beta_l of the norm extension; list_rn16 (ntotal, 16)
+ * fp16 = per row [hi, lo, 0, ...] with hi + lo = beta_l list_rnorms[row] (the
+ * tensor-core pass folds the residual norms into its accumulator through
+ * them). mf_ivf_filter_bank writes all four (after every add, from the CSR
  * bank and the centroids). */
 
 /* 1 when the filter search takes this shape (d a multiple of 8 in [64, 128],
@@ -354,7 +374,8 @@ MF_API int mf_ivf_filter_eligible(int d, int k, int64_t ntotal);
 MF_API int mf_ivf_filter_bank(int device, void* stream, int nlist, int d,
                               const int64_t* list_offsets, const float* list_vecs,
                               const float* list_norms, const float* centroids, int64_t ntotal,
-                              void* list_f16, float* list_rnorms, float* list_stats);
+                              void* list_f16, float* list_rnorms, void* list_rn16,
+                              float* list_stats);
 
 MF_API int mf_ivf_search_filtered_workspace_size(int64_t nq, int nlist, int nprobe, int d, int k,
                                                  size_t* bytes);
@@ -365,9 +386,9 @@ MF_API int mf_ivf_search_filtered(int device, void* stream, const float* xq, int
                                   const float* list_norms, const float* list_lo,
                                   const int64_t* list_ids, int64_t ntotal,
                                   const int32_t* list_order, const void* list_f16,
-                                  const float* list_rnorms, const float* list_stats, int d, int k,
-                                  float* distances, int64_t* labels, void* workspace,
-                                  size_t workspace_bytes);
+                                  const float* list_rnorms, const void* list_rn16,
+                                  const float* list_stats, int d, int k, float* distances,
+                                  int64_t* labels, void* workspace, size_t workspace_bytes);
 
 /* mf_ivf_search_bounded for L2 through the filter search (the lists of one
  * rank of a sharded index, caller-supplied probes and the bound from the
@@ -382,7 +403,8 @@ MF_API int mf_ivf_search_bounded_filtered(int device, void* stream, const float*
                                           const float* list_norms, const int64_t* list_ids,
                                           int64_t ntotal, const int32_t* list_order,
                                           const void* list_f16, const float* list_rnorms,
-                                          const float* list_stats, const float* centroids, int d,
+                                          const void* list_rn16, const float* list_stats,
+                                          const float* centroids, int d,
                                           int k, const float* bound, float* distances,
                                           int64_t* labels, void* workspace,
                                           size_t workspace_bytes);
@@ -511,6 +533,11 @@ MF_API int64_t mf_launch_count(void);
  * default; each takes half of every tile's columns) or 1. Results are the
  * same; for tests and measurements. No reference counterpart. */
 MF_API int mf_set_filter_groups(int groups);
+
+/* The filter search sends lists probed by at most `queries` queries (0 to 16;
+ * default 16) to its few-query pass and the others to the tensor-core pass.
+ * Results are the same; for measurements. No reference counterpart. */
+MF_API int mf_set_filter_small_group(int queries);
 
 /* Scan engine for the L2 / inner-product top-k scans: 0 = automatic (tensor
  * cores where the shape allows), 1 = SIMT only, 2 = tensor cores where the

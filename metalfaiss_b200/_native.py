@@ -43,11 +43,11 @@ _SIGNATURES = {
     "mf_ivf_probe_bound": ([I32, P, P, I64, P, I32, I32, P, P, P, P, P, I64, P, I32, I32, I32, P, P, SZ], I32),
     "mf_ivf_search_bounded": ([I32, P, P, I64, P, I32, I32, P, P, P, P, P, I64, P, I32, I32, I32, P, P, P, P, SZ], I32),
     "mf_ivf_filter_eligible": ([I32, I32, I64], I32),
-    "mf_ivf_filter_bank": ([I32, P, I32, I32, P, P, P, P, I64, P, P, P], I32),
+    "mf_ivf_filter_bank": ([I32, P, I32, I32, P, P, P, P, I64, P, P, P, P], I32),
     "mf_ivf_search_filtered_workspace_size": ([I64, I32, I32, I32, I32, PSZ], I32),
-    "mf_ivf_search_filtered": ([I32, P, P, I64, P, P, I32, I32, P, P, P, P, P, I64, P, P, P, P, I32, I32, P, P, P, SZ], I32),
+    "mf_ivf_search_filtered": ([I32, P, P, I64, P, P, I32, I32, P, P, P, P, P, I64, P, P, P, P, P, I32, I32, P, P, P, SZ], I32),
     "mf_ivf_search_bounded_filtered_workspace_size": ([I64, I32, I32, I32, I32, PSZ], I32),
-    "mf_ivf_search_bounded_filtered": ([I32, P, P, I64, P, I32, I32, P, P, P, P, I64, P, P, P, P, P, I32, I32, P, P, P, P, SZ], I32),
+    "mf_ivf_search_bounded_filtered": ([I32, P, P, I64, P, I32, I32, P, P, P, P, I64, P, P, P, P, P, P, I32, I32, P, P, P, P, SZ], I32),
     "mf_ivf_filter_rescans": ([I32, PI64, I32], I32),
     "mf_topk_merge": ([I32, P, P, P, I64, I32, I32, I32, P, P], I32),
     "mf_kmeans_assign_workspace_size": ([I64, I32, I32, PSZ], I32),
@@ -75,6 +75,9 @@ _SIGNATURES = {
     "mf_binary_range_workspace_size": ([I64, I64, I32, PSZ], I32),
     "mf_binary_range_count": ([I32, P, P, I64, P, I64, I32, I32, P, PI64, P, SZ], I32),
     "mf_binary_range_fill": ([I32, P, P, I64, P, I64, I32, I32, P, P, P, P, P, SZ], I32),
+    "mf_binary_ivf_search_workspace_size": ([I64, I32, I32, PSZ], I32),
+    "mf_binary_ivf_search": ([I32, P, P, I64, P, I32, I32, P, P, I32, P, I32, I32, P, P, P, SZ],
+                             I32),
     "mf_pq_encode": ([I32, P, P, I64, I32, I32, I32, I32, P, P, P, P, I32], I32),
     "mf_ivfpq_search_workspace_size": ([I64, I32, I32, PSZ], I32),
     "mf_ivfpq_search_preassigned": ([I32, P, P, I64, I32, I32, P, I32, I32, P, P, I32, I32, P, P,
@@ -82,6 +85,7 @@ _SIGNATURES = {
     "mf_flat_engine": ([I32, I32, I32, I64, I32], I32),
     "mf_set_scan_engine": ([I32], I32),
     "mf_set_filter_groups": ([I32], I32),
+    "mf_set_filter_small_group": ([I32], I32),
     "mf_device_error": ([I32, ctypes.POINTER(ctypes.c_int)], I32),
     "mf_timing_read": ([ctypes.c_char_p, ctypes.POINTER(ctypes.c_double), PI64], I32),
 }

@@ -254,6 +254,101 @@ __global__ void binary_offsets_kernel(int64_t* counts, int64_t nq, int splits,
   counts[i] += lims[i / splits];
 }
 
+// Binary IVF: one block per (query, probe) pair. The query's words sit in
+// shared memory; the warps take the list's rows 32 at a time (one row per
+// lane, rows `pitch` words apart), feed per-warp top-k lists, and warp 0
+// merges them into the pair's k best. A candidate's index is
+// (probe rank << 26) | (offset in its list), so the merge across probes orders
+// ties by probe, then by row: the order in which the reference concatenates a
+// query's candidates (python/metalfaiss/index/binary_ivf_index.py:150-175).
+constexpr int kBinIvfOffBits = 26;
+
+template <int WMAX, int KCAP>
+__global__ void __launch_bounds__(kBinThreads)
+    binary_ivf_kernel(const uint32_t* __restrict__ xq, int W, const int64_t* __restrict__ probes,
+                      int P, int nlist, const int64_t* __restrict__ offsets,
+                      const uint32_t* __restrict__ codes, int pitch, int k, float* out_d,
+                      int64_t* out_l) {
+  extern __shared__ unsigned long long bin_smem[];
+  unsigned long long* lists = bin_smem;                         // 8 x KCAP
+  unsigned long long* bufs = bin_smem + (kBinThreads / 32) * KCAP;  // 8 x 32
+  __shared__ uint32_t qw[kBinMaxW];
+  const int pair = blockIdx.x;
+  const int64_t q = pair / P;
+  const int pr = pair - (int)(q * P);
+  const int64_t l = probes[pair];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float* od = out_d + (size_t)pair * k;
+  int64_t* ol = out_l + (size_t)pair * k;
+  if (l < 0 || l >= nlist) {
+    for (int i = threadIdx.x; i < k; i += kBinThreads) {
+      od[i] = __int_as_float(0x7f800000);
+      ol[i] = -1;
+    }
+    return;
+  }
+  if (threadIdx.x < kBinMaxW) qw[threadIdx.x] = threadIdx.x < W ? xq[q * W + threadIdx.x] : 0u;
+  WarpTopK<KCAP> tk;
+  tk.init(lists + warp * KCAP, bufs + warp * 32, k, lane);
+  __syncthreads();
+  uint32_t qr[WMAX];
+#pragma unroll
+  for (int w = 0; w < WMAX; ++w) qr[w] = qw[w];
+  const int64_t rb = offsets[l];
+  // rows past 2^26 of one list cannot be tagged; the entry point documents
+  // the limit, and they are left out rather than mislabelled
+  const int64_t re = offsets[l + 1] - rb > (1ll << kBinIvfOffBits) ? rb + (1ll << kBinIvfOffBits)
+                                                                    : offsets[l + 1];
+  const unsigned int tag = (unsigned int)pr << kBinIvfOffBits;
+  for (int64_t r0 = rb + 32 * warp; r0 < re; r0 += kBinThreads) {
+    const int64_t row = r0 + lane;
+    unsigned long long key = kEmptyKey;
+    if (row < re) {
+      const uint32_t* c = codes + row * pitch;
+      int h = 0;
+#pragma unroll
+      for (int w = 0; w < WMAX; ++w)
+        if (w < W) h += __popc(c[w] ^ qr[w]);
+      key = make_key((float)h, tag | (unsigned int)(row - rb));
+    }
+    tk.offer(key, k, lane);
+  }
+  tk.flush(k, lane);
+  __syncthreads();
+  if (warp == 0) {
+    for (int w = 1; w < kBinThreads / 32; ++w)
+      for (int i = 0; i < k; i += 32)
+        tk.offer(i + lane < k ? lists[w * KCAP + i + lane] : kEmptyKey, k, lane);
+    tk.flush(k, lane);
+    for (int i = lane; i < k; i += 32) {
+      const unsigned long long key = tk.list[i];
+      od[i] = key == kEmptyKey ? __int_as_float(0x7f800000) : key_dist(key);
+      ol[i] = key == kEmptyKey ? -1 : (int64_t)key_index(key);
+    }
+  }
+}
+
+// (probe rank << 26 | offset) -> ids[offsets[probes[q][rank]] + offset] (or
+// the row position when ids is NULL); -1 stays.
+__global__ void binary_ivf_labels_kernel(int64_t* labels, int64_t nq, int k, int P,
+                                         const int64_t* __restrict__ probes,
+                                         const int64_t* __restrict__ offsets,
+                                         const int64_t* __restrict__ ids) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= nq * k) return;
+  const int64_t v = labels[i];
+  if (v < 0) return;
+  const int64_t q = i / k;
+  const int pr = (int)(v >> kBinIvfOffBits);
+  if (pr >= P) {
+    labels[i] = -1;
+    return;
+  }
+  const int64_t off = v & ((1ll << kBinIvfOffBits) - 1);
+  const int64_t row = offsets[probes[q * P + pr]] + off;
+  labels[i] = ids ? ids[row] : row;
+}
+
 // About two waves of blocks; every split at least one tile.
 void binary_plan(int64_t nq, int64_t nb, int device, int* nqt, int* splits, int64_t* rps) {
   *nqt = (int)ceil_div(nq, kBinQT);
@@ -301,6 +396,34 @@ int launch_topk(const BinArgs& a, int kcap, int64_t items, cudaStream_t st) {
   if (a.W <= 8) return launch_topk_w<8>(a, kcap, items, st);
   if (a.W <= 16) return launch_topk_w<16>(a, kcap, items, st);
   return launch_topk_w<32>(a, kcap, items, st);
+}
+
+template <int WMAX>
+int launch_ivf_w(const uint32_t* xq, int W, const int64_t* probes, int P, int nlist,
+                 const int64_t* offsets, const uint32_t* codes, int pitch, int k, int kcap,
+                 float* pd, int64_t* pl, int64_t pairs, cudaStream_t st) {
+  const size_t smem = size_t(kBinThreads / 32) * (kcap + 32) * 8;
+  void (*fn)(const uint32_t*, int, const int64_t*, int, int, const int64_t*, const uint32_t*, int,
+             int, float*, int64_t*) = kcap == 32    ? binary_ivf_kernel<WMAX, 32>
+                                      : kcap == 128 ? binary_ivf_kernel<WMAX, 128>
+                                                    : binary_ivf_kernel<WMAX, 256>;
+  MF_CUDA(cudaFuncSetAttribute(reinterpret_cast<const void*>(fn),
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  fn<<<(unsigned)pairs, kBinThreads, smem, st>>>(xq, W, probes, P, nlist, offsets, codes, pitch, k,
+                                                 pd, pl);
+  MF_LAUNCH_CHECK();
+  return MF_OK;
+}
+
+int launch_ivf(const uint32_t* xq, int W, const int64_t* probes, int P, int nlist,
+               const int64_t* offsets, const uint32_t* codes, int pitch, int k, float* pd,
+               int64_t* pl, int64_t pairs, cudaStream_t st) {
+  const int kcap = bin_kcap(k);
+  if (W <= 2) return launch_ivf_w<2>(xq, W, probes, P, nlist, offsets, codes, pitch, k, kcap, pd, pl, pairs, st);
+  if (W <= 4) return launch_ivf_w<4>(xq, W, probes, P, nlist, offsets, codes, pitch, k, kcap, pd, pl, pairs, st);
+  if (W <= 8) return launch_ivf_w<8>(xq, W, probes, P, nlist, offsets, codes, pitch, k, kcap, pd, pl, pairs, st);
+  if (W <= 16) return launch_ivf_w<16>(xq, W, probes, P, nlist, offsets, codes, pitch, k, kcap, pd, pl, pairs, st);
+  return launch_ivf_w<32>(xq, W, probes, P, nlist, offsets, codes, pitch, k, kcap, pd, pl, pairs, st);
 }
 
 int launch_range(const BinArgs& a, bool fill, int64_t items, cudaStream_t st) {
@@ -517,6 +640,58 @@ int mf_binary_range_fill(int device, void* stream, const uint32_t* xq, int64_t n
   MF_CUDA(cudaMemcpyAsync(&total, lims + nq, sizeof(int64_t), cudaMemcpyDeviceToHost, st));
   MF_CUDA(cudaStreamSynchronize(st));
   if (ids && total > 0) MF_TRY(launch_map_ids(ids, labels, total, st));
+  return MF_OK;
+}
+
+int mf_binary_ivf_search_workspace_size(int64_t nq, int nprobe, int k, size_t* bytes) {
+  clear_error();
+  MF_CHECK(bytes != nullptr, MF_ERR_INVALID_ARGS, "bytes is NULL");
+  MF_CHECK(k >= 1 && k <= kMaxK && nprobe >= 1 && nq >= 0, MF_ERR_INVALID_ARGS, "k=%d nprobe=%d",
+           k, nprobe);
+  Carver c(nullptr, 0);
+  c.take<float>((size_t)nq * nprobe * k);
+  c.take<int64_t>((size_t)nq * nprobe * k);
+  *bytes = c.used;
+  return MF_OK;
+}
+
+int mf_binary_ivf_search(int device, void* stream, const uint32_t* xq, int64_t nq,
+                         const int64_t* probes, int nprobe, int nlist,
+                         const int64_t* list_offsets, const uint32_t* list_codes, int code_pitch,
+                         const int64_t* list_ids, int d, int k, float* distances,
+                         int64_t* labels, void* workspace, size_t workspace_bytes) {
+  MF_BIN_ENTER(device);
+  MF_TRY(check_bin_shape(nq, 0, d));
+  const int W = (d + 31) / 32;
+  MF_CHECK(code_pitch >= W, MF_ERR_INVALID_ARGS, "code pitch %d < %d words", code_pitch, W);
+  MF_CHECK(k >= 1 && k <= kMaxK, MF_ERR_INVALID_ARGS, "k=%d must be in [1, %d]", k, kMaxK);
+  MF_CHECK(nprobe >= 1 && nprobe <= 64 && nlist >= 1, MF_ERR_INVALID_ARGS,
+           "nprobe=%d (1 to 64), nlist=%d", nprobe, nlist);
+  MF_CHECK(nq * nprobe < (1ll << 31), MF_ERR_INVALID_ARGS, "nq*nprobe too large");
+  if (nq == 0) return MF_OK;
+  MF_TRY(check_device_ptr(xq, "xq"));
+  MF_TRY(check_device_ptr(probes, "probes"));
+  MF_TRY(check_device_ptr(list_offsets, "list_offsets"));
+  MF_TRY(check_device_ptr(list_codes, "list_codes", true));
+  MF_TRY(check_device_ptr(list_ids, "list_ids", true));
+  MF_TRY(check_device_ptr(distances, "distances"));
+  MF_TRY(check_device_ptr(labels, "labels"));
+  MF_TRY(check_device_ptr(workspace, "workspace"));
+  Carver c(workspace, workspace_bytes);
+  float* pd = c.take<float>((size_t)nq * nprobe * k);
+  int64_t* pl = c.take<int64_t>((size_t)nq * nprobe * k);
+  MF_CHECK(c.fits(), MF_ERR_INVALID_ARGS, "binary IVF workspace too small: %zu < %zu bytes",
+           workspace_bytes, c.used);
+  cudaStream_t st = (cudaStream_t)stream;
+  {
+    ScopedTiming tm("binary_ivf", st);
+    MF_TRY(launch_ivf(xq, W, probes, nprobe, nlist, list_offsets, list_codes, code_pitch, k, pd, pl,
+                      nq * nprobe, st));
+  }
+  MF_TRY(launch_merge(pd, pl, nq, nprobe, k, k, distances, labels, st));
+  binary_ivf_labels_kernel<<<(unsigned)ceil_div(nq * k, 256), 256, 0, st>>>(
+      labels, nq, k, nprobe, probes, list_offsets, list_ids);
+  MF_LAUNCH_CHECK();
   return MF_OK;
 }
 

@@ -146,6 +146,7 @@ IvfWs carve_ivf(Carver& c, int64_t nq, int nlist, int P, int d, int k, int mode,
     w.fp.e = c.take<float>((size_t)nq * P);
     w.fp.sq = c.take<float>((size_t)nq * P);
     w.fp.sc = c.take<float>((size_t)nq * P);
+    w.fp.ae = c.take<float>((size_t)nq * P);
     w.fp.cnt = c.take<int>((size_t)nq * P);
   } else {
     w.pd = c.take<float>((size_t)nq * P * k);
@@ -282,13 +283,17 @@ int ivf_scan_topk(int device, cudaStream_t stream, const IvfWs& w, const float* 
 // groups of up to 128 queries, and the exact refinement into (D, I). The
 // bound pass runs on the SIMT engines with the margin that also covers the
 // refinement's rounding (filter_eligible requires the tensor-core shape for it).
+// Lists probed by at most this many queries go to the few-query pass in the
+// filter search (0: every list to the tensor-core pass).
+int g_filter_small_group = 16;
+
 int ivf_filter_topk(int device, cudaStream_t stream, const IvfWs& w, const float* xq, int64_t nq,
                     const int64_t* probes, int P, int nlist, const int64_t* list_offsets,
                     const float* list_vecs, const float* list_norms, const float* list_lo,
                     const int64_t* list_ids, int64_t ntotal, const int32_t* list_order,
-                    const void* list_f16, const float* list_rnorms, const float* list_stats,
-                    const float* centroids, int d, int k, float* D, int64_t* I,
-                    const float* bound_in) {
+                    const void* list_f16, const float* list_rnorms, const void* list_rn16,
+                    const float* list_stats, const float* centroids, int d, int k, float* D,
+                    int64_t* I, const float* bound_in) {
   const int S = filter_slots_for(k);
   if (bound_in) {
     MF_TRY(launch_norms(xq, nq, d, w.qn, stream));
@@ -305,8 +310,7 @@ int ivf_filter_topk(int device, cudaStream_t stream, const IvfWs& w, const float
   // instead (a 128-query tile would be mostly padding; those rows' bytes
   // bound the work), in its filter form: the same fp16 rows, upper bounds and
   // slots.
-  constexpr int kSmallGroup = 16;
-  const int small_max = few_eligible(MF_METRIC_L2, d, k) ? kSmallGroup : 0;
+  const int small_max = few_eligible(MF_METRIC_L2, d, k) ? g_filter_small_group : 0;
   MF_TRY(run_ivf_groups_ex(w.g, probes, nq, P, nlist, list_offsets, list_order, nullptr, nullptr,
                            0, nullptr, tc_group(), stream, 0, P, small_max));
   ScanArgs a{};
@@ -334,6 +338,8 @@ int ivf_filter_topk(int device, cudaStream_t stream, const IvfWs& w, const float
   a.pair_sc = w.fp.sc;
   a.pair_cnt = w.fp.cnt;
   a.centroids = centroids;
+  a.xrn16 = list_rn16;
+  a.pair_ae = w.fp.ae;
   MF_TRY(launch_tc_filter(a, ntotal, nq * P, device, stream));
   if (small_max > 0) {
     ScanArgs fa{};
@@ -393,10 +399,11 @@ bool filter_eligible(int d, int k, int64_t ntotal) {
          tc_eligible(MF_METRIC_L2, d, k, ntotal) && tc_raw_queries(d, k);
 }
 
-int check_filter_bank(const void* list_f16, const float* list_rnorms, const float* list_stats,
-                      const float* centroids) {
+int check_filter_bank(const void* list_f16, const float* list_rnorms, const void* list_rn16,
+                      const float* list_stats, const float* centroids) {
   MF_TRY(check_device_ptr(list_f16, "list_f16"));
   MF_TRY(check_device_ptr(list_rnorms, "list_rnorms"));
+  MF_TRY(check_device_ptr(list_rn16, "list_rn16"));
   MF_TRY(check_device_ptr(list_stats, "list_stats"));
   MF_TRY(check_device_ptr(centroids, "centroids"));
   return MF_OK;
@@ -677,7 +684,8 @@ int mf_ivf_filter_eligible(int d, int k, int64_t ntotal) {
 
 int mf_ivf_filter_bank(int device, void* stream, int nlist, int d, const int64_t* list_offsets,
                        const float* list_vecs, const float* list_norms, const float* centroids,
-                       int64_t ntotal, void* list_f16, float* list_rnorms, float* list_stats) {
+                       int64_t ntotal, void* list_f16, float* list_rnorms, void* list_rn16,
+                       float* list_stats) {
   MF_ENTER(device);
   // the filter search's shapes only (mf_ivf_filter_eligible): its scan reads
   // 128-byte fp16 tiles (d >= 64) and its refinement one float4 per lane
@@ -693,9 +701,10 @@ int mf_ivf_filter_bank(int device, void* stream, int nlist, int d, const int64_t
     MF_TRY(check_device_ptr(list_norms, "list_norms"));
     MF_TRY(check_device_ptr(list_f16, "list_f16"));
     MF_TRY(check_device_ptr(list_rnorms, "list_rnorms"));
+    MF_TRY(check_device_ptr(list_rn16, "list_rn16"));
   }
   return launch_filter_bank(nlist, d, list_offsets, list_vecs, list_norms, centroids, list_f16,
-                            list_rnorms, list_stats, (cudaStream_t)stream);
+                            list_rnorms, list_stats, list_rn16, (cudaStream_t)stream);
 }
 
 int mf_ivf_search_filtered_workspace_size(int64_t nq, int nlist, int nprobe, int d, int k,
@@ -718,7 +727,8 @@ int mf_ivf_search_filtered(int device, void* stream, const float* xq, int64_t nq
                            const float* list_norms, const float* list_lo,
                            const int64_t* list_ids, int64_t ntotal, const int32_t* list_order,
                            const void* list_f16, const float* list_rnorms,
-                           const float* list_stats, int d, int k, float* distances,
+                           const void* list_rn16, const float* list_stats, int d, int k,
+                           float* distances,
                            int64_t* labels, void* workspace, size_t workspace_bytes) {
   MF_ENTER(device);
   MF_TRY(check_common(d, MF_METRIC_L2, k, true));
@@ -735,7 +745,7 @@ int mf_ivf_search_filtered(int device, void* stream, const float* xq, int64_t nq
   MF_TRY(check_device_ptr(centroid_norms, "centroid_norms"));
   MF_TRY(check_ivf_lists(list_offsets, list_vecs, list_norms, list_ids, list_order,
                          MF_METRIC_L2));
-  MF_TRY(check_filter_bank(list_f16, list_rnorms, list_stats, centroids));
+  MF_TRY(check_filter_bank(list_f16, list_rnorms, list_rn16, list_stats, centroids));
   MF_TRY(check_device_ptr(distances, "distances"));
   MF_TRY(check_device_ptr(labels, "labels"));
   MF_TRY(check_device_ptr(workspace, "workspace"));
@@ -753,7 +763,7 @@ int mf_ivf_search_filtered(int device, void* stream, const float* xq, int64_t nq
                        MF_METRIC_L2, P, nullptr, w.coarse_d, w.coarse_l, w.flat_ws, w.flat_bytes));
   return ivf_filter_topk(device, s, w, xq, nq, w.coarse_l, P, nlist, list_offsets, list_vecs,
                          list_norms, list_lo, list_ids, ntotal, list_order, list_f16, list_rnorms,
-                         list_stats, centroids, d, k, distances, labels, nullptr);
+                         list_rn16, list_stats, centroids, d, k, distances, labels, nullptr);
 }
 
 int mf_ivf_search_bounded_filtered_workspace_size(int64_t nq, int nlist, int nprobe, int d,
@@ -775,7 +785,8 @@ int mf_ivf_search_bounded_filtered(int device, void* stream, const float* xq, in
                                    const int64_t* list_offsets, const float* list_vecs,
                                    const float* list_norms, const int64_t* list_ids,
                                    int64_t ntotal, const int32_t* list_order, const void* list_f16,
-                                   const float* list_rnorms, const float* list_stats,
+                                   const float* list_rnorms, const void* list_rn16,
+                                   const float* list_stats,
                                    const float* centroids, int d, int k, const float* bound,
                                    float* distances, int64_t* labels, void* workspace,
                                    size_t workspace_bytes) {
@@ -792,7 +803,7 @@ int mf_ivf_search_bounded_filtered(int device, void* stream, const float* xq, in
   MF_TRY(check_device_ptr(bound, "bound"));
   MF_TRY(check_ivf_lists(list_offsets, list_vecs, list_norms, list_ids, list_order,
                          MF_METRIC_L2));
-  MF_TRY(check_filter_bank(list_f16, list_rnorms, list_stats, centroids));
+  MF_TRY(check_filter_bank(list_f16, list_rnorms, list_rn16, list_stats, centroids));
   MF_TRY(check_device_ptr(distances, "distances"));
   MF_TRY(check_device_ptr(labels, "labels"));
   MF_TRY(check_device_ptr(workspace, "workspace"));
@@ -802,7 +813,8 @@ int mf_ivf_search_bounded_filtered(int device, void* stream, const float* xq, in
            c.used);
   return ivf_filter_topk(device, (cudaStream_t)stream, w, xq, nq, probes, nprobe, nlist,
                          list_offsets, list_vecs, list_norms, nullptr, list_ids, ntotal,
-                         list_order, list_f16, list_rnorms, list_stats, centroids, d, k, distances,
+                         list_order, list_f16, list_rnorms, list_rn16, list_stats, centroids, d, k,
+                         distances,
                          labels, bound);
 }
 
@@ -1196,6 +1208,14 @@ int mf_tf32_residual(int device, void* stream, const float* x, int64_t n, int d,
   MF_TRY(check_device_ptr(x, "x"));
   MF_TRY(check_device_ptr(lo, "lo"));
   return launch_tf32_residual(x, n, d, lo, (cudaStream_t)stream);
+}
+
+int mf_set_filter_small_group(int queries) {
+  clear_error();
+  MF_CHECK(queries >= 0 && queries <= few_max_queries(), MF_ERR_INVALID_ARGS,
+           "queries=%d (0 to %d)", queries, few_max_queries());
+  g_filter_small_group = queries;
+  return MF_OK;
 }
 
 int mf_set_filter_groups(int groups) {

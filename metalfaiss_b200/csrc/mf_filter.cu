@@ -40,6 +40,19 @@
 // gets e = +inf: the scan keeps none of its rows and the refinement rescans
 // its list exactly.
 //
+// The tensor-core pass folds rn_x into its accumulator: each bank row has a
+// 16-element fp16 extension [hi, lo, 0, ...] with hi + lo = beta_l rn_x (beta_l
+// a power of two per list bringing the list's largest rn_x under 2^15; lo the
+// fp16 rounding of the remainder, so hi + lo is within 2^-22 of it), and each
+// pair's query row the extension [A_e, A_e, 0, ...] with A_e = -s_q s_l /
+// (2 beta_l), a power of two. The accumulator is then s_q s_l (<q', x'>~ - rn_x
+// / 2), and u = (Dc + e) - 2 acc / (s_q s_l): one compare per column against a
+// per-row constant decides the filter. The two extra products enter the
+// accumulation bound, adding (d + 3) 2^-22 R_l^2 to e (the accumulation over
+// d + 2 terms of magnitude up to s_q s_l R_l^2 / 2 each, and the hi/lo
+// representation); a pair whose A_e is not an fp16 power of two gets
+// e = +inf (its list is rescanned exactly).
+//
 // Selection. The scan keeps u = max(a + e, 0) >= t, with t >= u - 2e. Let B be
 // the query's bound from the first rows of its nearest list (an upper bound
 // on its k-th exact distance T_k) and U the k-th smallest u over its probes
@@ -91,10 +104,12 @@ constexpr int kScaleExpMax = 60;  // |exponent| of a list's or a query's scale
 // One block per list; warp w takes rows w, w + 8, ... of the list, lane j the
 // elements [4j, 4j + 4) + 128 i of a row. First pass: the rows' squared
 // residual norms and the list's largest; second pass: the scaled fp16 rows.
+// Per row also the 16-element fp16 norm extension (two uint4 words) for the
+// tensor-core pass: [hi, lo, 0, ...] of beta_l rn_x, and stats.w = beta_l.
 __global__ void __launch_bounds__(kBankThreads) filter_bank_kernel(
     int d, const int64_t* __restrict__ offsets, const float* __restrict__ xb,
     const float* __restrict__ xnorms, const float* __restrict__ cents, uint2* h, float* rn,
-    float4* stats) {
+    float4* stats, uint4* rn16) {
   const int l = blockIdx.x;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -120,7 +135,7 @@ __global__ void __launch_bounds__(kBankThreads) filter_bank_kernel(
     mx = fmaxf(mx, xnorms[r]);
   }
   __shared__ float s_r[kBankThreads / 32], s_x[kBankThreads / 32];
-  __shared__ float s_scale;
+  __shared__ float s_scale, s_beta;
   mr = warp_max(mr);
   mx = warp_max(mx);
   if (lane == 0) {
@@ -138,10 +153,25 @@ __global__ void __launch_bounds__(kBankThreads) filter_bank_kernel(
     int e = scale_exp(R);
     e = e > kScaleExpMax ? kScaleExpMax : (e < -kScaleExpMax ? -kScaleExpMax : e);
     s_scale = ldexpf(1.0f, e);
-    stats[l] = make_float4(R, mx, s_scale, 0.0f);
+    // beta: R^2 beta < 2^15 (R = m 2^er with 0.5 <= m < 1, so R^2 < 2^(2 er))
+    int er = 0;
+    if (R > 0.0f) frexpf(R, &er);
+    int eb = 15 - 2 * er;
+    eb = eb > 2 * kScaleExpMax ? 2 * kScaleExpMax : (eb < -2 * kScaleExpMax ? -2 * kScaleExpMax : eb);
+    s_beta = ldexpf(1.0f, eb);
+    stats[l] = make_float4(R, mx, s_scale, s_beta);
   }
   __syncthreads();
   const float sl = s_scale;
+  const float beta = s_beta;
+  for (int64_t r = rb + threadIdx.x; r < re; r += kBankThreads) {
+    const float v = rn[r] * beta;
+    const __half hi = __float2half_rn(v);
+    const __half lo = __float2half_rn(v - __half2float(hi));
+    const __half2 hl = __halves2half2(hi, lo);
+    rn16[2 * r] = make_uint4(*reinterpret_cast<const uint32_t*>(&hl), 0u, 0u, 0u);
+    rn16[2 * r + 1] = make_uint4(0u, 0u, 0u, 0u);
+  }
   for (int64_t r = rb + warp; r < re; r += kBankThreads / 32) {
     const float* x = xb + r * d;
     for (int j = 4 * lane; j < d; j += 128) {
@@ -228,15 +258,20 @@ __global__ void __launch_bounds__(kPairsWarps * 32) filter_pairs_kernel(
       fp.e[s] = 0.0f;
       fp.sq[s] = 1.0f;
       fp.sc[s] = 1.0f;
+      fp.ae[s] = 0.0f;
       continue;
     }
     const float dc = my_dc;
     const float4 st = stats[my_l];
-    const float R = st.x, XN = st.y, sl = st.z;
+    const float R = st.x, XN = st.y, sl = st.z, beta = st.w;
     const float nrm = sqrtf(dc) * (1.0f + 0x1p-17f);
     const int eq = scale_exp(nrm);
-    float e, sq = 1.0f, sc = 1.0f, thr;
-    if (eq > kScaleExpMax || eq < -kScaleExpMax || !(R * sl < 0x1p13f)) {
+    float e, sq = 1.0f, sc = 1.0f, thr, ae = 0.0f;
+    // the norm fold's multiplier -s_q s_l / (2 beta): an fp16 power of two
+    const float ae_mag = eq > kScaleExpMax || eq < -kScaleExpMax
+                             ? 0.0f : ldexpf(sl * 0.5f / beta, eq);
+    if (eq > kScaleExpMax || eq < -kScaleExpMax || !(R * sl < 0x1p13f) ||
+        !(ae_mag >= 0x1p-24f && ae_mag <= 0x1p15f)) {
       // out of the scales' range: keep nothing, rescan exactly
       e = __int_as_float(0x7f800000);
       thr = -1.0f;
@@ -246,7 +281,9 @@ __global__ void __launch_bounds__(kPairsWarps * 32) filter_pairs_kernel(
       // 0x1.09p-9 = 2^-9 (1 + 9 / 256) >= 2 (2^-10 + 2^-22 + 128 2^-22 (1 + 2^-10))
       // (1 + 2^-17) = 2^-9 (1.0315...): the products term for d <= 128
       e = 0x1.09p-9f * nrm * R + 0x1p-22f * sqrtf((float)d) * (nrm / sl + R / sq) +
-          (float)(d + 20) * 0x1p-23f * (qn + XN + dc + R * R) + 0x1p-100f;
+          (float)(d + 20) * 0x1p-23f * (qn + XN + dc + R * R) +
+          (float)(d + 3) * 0x1p-22f * R * R + 0x1p-100f;
+      ae = -ae_mag;
       thr = bq + 2.0f * e;  // +inf stays +inf
     }
     fp.qn[s] = dc + e;
@@ -254,6 +291,7 @@ __global__ void __launch_bounds__(kPairsWarps * 32) filter_pairs_kernel(
     fp.thr[s] = thr;
     fp.sq[s] = sq;
     fp.sc[s] = sc;
+    fp.ae[s] = ae;
   }
 }
 
@@ -422,13 +460,13 @@ int filter_slots_for(int k) {
 
 int launch_filter_bank(int nlist, int d, const int64_t* offsets, const float* xb,
                        const float* xnorms, const float* cents, void* h, float* rn, float* stats,
-                       cudaStream_t stream) {
+                       void* rn16, cudaStream_t stream) {
   MF_CHECK(d > 0 && d % 8 == 0, MF_ERR_INVALID_ARGS, "filter bank needs d a multiple of 8 (d=%d)",
            d);
   if (nlist <= 0) return MF_OK;
   filter_bank_kernel<<<(unsigned int)nlist, kBankThreads, 0, stream>>>(
       d, offsets, xb, xnorms, cents, reinterpret_cast<uint2*>(h), rn,
-      reinterpret_cast<float4*>(stats));
+      reinterpret_cast<float4*>(stats), reinterpret_cast<uint4*>(rn16));
   MF_LAUNCH_CHECK();
   return MF_OK;
 }

@@ -14,10 +14,12 @@ int filter_slots_for(int k);
 // each, d a multiple of 8): h[r] = fp16(s_l (xb[r] - cents[l])) (to nearest),
 // rn[r] = |xb[r] - cents[l]|^2 in fp32; per list, stats[4l..4l+3] = (R_l, an
 // upper bound on the rows' residual norms; XN_l, the largest xnorms of the
-// list; s_l, the list's power-of-two scale; 0); R_l = XN_l = 0 for an empty list.
+// list; s_l, the list's power-of-two scale; beta_l, the power of two of the
+// norm extension); R_l = XN_l = 0 for an empty list; rn16[r] = the row's
+// 16-element fp16 norm extension [hi, lo, 0, ...] of beta_l rn[r] (32 bytes).
 int launch_filter_bank(int nlist, int d, const int64_t* offsets, const float* xb,
                        const float* xnorms, const float* cents, void* h, float* rn, float* stats,
-                       cudaStream_t stream);
+                       void* rn16, cudaStream_t stream);
 
 // Per (query, probe) pair s = q*P + p of list l = probes[s] (outputs, nq*P each).
 struct FilterPairs {
@@ -26,6 +28,7 @@ struct FilterPairs {
   float* e;
   float* sq;   // the query's power-of-two scale s_q
   float* sc;   // 1 / (s_q s_l)
+  float* ae;   // -s_q s_l / (2 beta_l): the query row's norm-extension element
   int* cnt;    // kept slots: 0 here, then written by the scan
 };
 int launch_filter_pairs(const float* xq, const float* qnorms, int64_t nq, int P, int d,

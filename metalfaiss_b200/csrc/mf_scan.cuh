@@ -81,6 +81,12 @@ struct ScanArgs {
   const float* pair_sq;
   const float* pair_sc;
   int* pair_cnt;
+  // the tensor-core filter pass folds the rows' residual norms into its
+  // accumulator: xrn16 holds each row's 16-element fp16 extension (32 bytes:
+  // [hi, lo, 0, ...] of beta_l rn_x) and pair_ae[s] the query row's
+  // (-s_q s_l / (2 beta_l)), so the accumulator is s_q s_l (dot - rn_x / 2)
+  const void* xrn16;
+  const float* pair_ae;
   // few-query scan with pair_cnt set: compact outputs at this slot stride
   int out_stride;
   // range search

@@ -266,6 +266,20 @@ __device__ __forceinline__ uint64_t desc_k_sw128(uint32_t smem_addr) {
   return d;
 }
 
+// K-major operand in the 32-byte swizzled layout: rows of 32 B (16 fp16 of
+// K, one K-step), 8-row atoms of 256 B stacked along N (SBO = 256 B); the base
+// must be 256-byte aligned. Layout type 6 = SWIZZLE_32B (the sm_100 encoding
+// of bits [61, 64)).
+__device__ __forceinline__ uint64_t desc_k_sw32(uint32_t smem_addr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_addr & 0x3FFFFu) >> 4);  // start address
+  d |= static_cast<uint64_t>(1) << 16;                       // LBO (unused: one atom along K)
+  d |= static_cast<uint64_t>(256 >> 4) << 32;                // SBO
+  d |= static_cast<uint64_t>(1) << 46;                       // descriptor version (sm_100)
+  d |= static_cast<uint64_t>(6) << 61;                       // SWIZZLE_32B
+  return d;
+}
+
 // kind::tf32 instruction descriptor: F32 accumulate, TF32 A and B, both K-major.
 __host__ __device__ constexpr uint32_t idesc_tf32(int M, int N) {
   return (1u << 4) | (2u << 7) | (2u << 10) | (static_cast<uint32_t>(N >> 3) << 17) |

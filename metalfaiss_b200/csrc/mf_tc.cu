@@ -105,7 +105,9 @@ TqLayout tq_layout(int d, int kcap, int BN, int SA, bool atm, bool bf = false, i
   if (atm) {
     s.a_hi = s.a_lo = 0;  // unused: the query tile lives in tensor memory
     s.b_hi = 0;
-    s.acc0 = (bf ? 1 : 2) * s.KB * 32;
+    // bf: A in columns [0, KB*32), its norm-extension K-step in the next 32;
+    // accumulators from the next multiple of 64
+    s.acc0 = bf ? ((s.KB + 1) * 32 + 63) / 64 * 64 : 2 * s.KB * 32;
   } else {
     s.a_hi = 0;
     s.a_lo = kTqM * 128;
@@ -115,8 +117,9 @@ TqLayout tq_layout(int d, int kcap, int BN, int SA, bool atm, bool bf = false, i
   s.nacc = (kTqTmemCols - s.acc0) / BN;
   if (s.nacc > kTqMaxAcc) s.nacc = kTqMaxAcc;
   s.b_lo = s.b_hi + size_t(BN) * 128;
-  // the filter scan's stage holds a whole tile (all K-blocks): one hand-off per tile
-  s.stage = bf ? size_t(s.KB) * BN * 128 : s.b_lo + size_t(BN) * 128;
+  // the filter scan's stage holds a whole tile (all K-blocks, then the rows'
+  // 32-byte norm extensions): one hand-off per tile
+  s.stage = bf ? size_t(s.KB) * BN * 128 + size_t(BN) * 32 : s.b_lo + size_t(BN) * 128;
   size_t o = size_t(SA) * s.stage;
   s.lists = o;  // per epilogue warpgroup: 128 rows x kcap keys
   o += size_t(ew) * kTqM * kcap * 8;
@@ -289,6 +292,33 @@ __device__ __forceinline__ unsigned int tq_accept(const uint32_t (&r)[32], const
   return ~all & in_range;
 }
 
+// Accept mask of a 32-column chunk of the filter scan, whose accumulators
+// already hold s_q s_l (dot - rn_x / 2): bit j is set iff acc_j >= tau (the
+// row's threshold moved to the accumulator's scale, lowered by a margin so
+// that every column the exact form would keep passes) and j < nvalid. One
+// packed subtraction per two columns; the sign bit of acc - tau (+0 when
+// equal) goes into the reject mask, in four independent chains.
+__device__ __forceinline__ unsigned int tq_accept_acc(const uint32_t (&r)[32], float tau,
+                                                      int nvalid) {
+  unsigned int rej[4] = {0u, 0u, 0u, 0u};
+  const unsigned long long tau2 = pack2(tau, tau);
+#pragma unroll
+  for (int p = 3; p >= 0; --p) {
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      const int j = 8 * g + 2 * p;
+      const unsigned long long acc2 =
+          static_cast<unsigned long long>(r[j]) | (static_cast<unsigned long long>(r[j + 1]) << 32);
+      const unsigned long long diff2 = sub2(acc2, tau2);
+      rej[g] = __funnelshift_l(static_cast<unsigned int>(diff2 >> 32), rej[g], 1);
+      rej[g] = __funnelshift_l(static_cast<unsigned int>(diff2), rej[g], 1);
+    }
+  }
+  const unsigned int all = rej[0] | (rej[1] << 8) | (rej[2] << 16) | (rej[3] << 24);
+  const unsigned int in_range = nvalid >= 32 ? 0xffffffffu : ((1u << nvalid) - 1u);
+  return ~all & in_range;
+}
+
 // CONV (with ATM only): the rows' tf32 residuals are derived in shared memory
 // from the loaded fp32 tile instead of being loaded (no residual array).
 // FLT (with ATM, L2, IVF only): the filter scan. One fp16 MMA per K-step of 16
@@ -398,7 +428,7 @@ __global__ void __launch_bounds__((ATM ? kTqThreadsAtm : kTqThreads) + (EW - 1) 
         prefetch_tensormap(&maps.a_lo);
       }
       prefetch_tensormap(&maps.b_hi);
-      if (!CONV && !FLT) prefetch_tensormap(&maps.b_lo);
+      if (!CONV) prefetch_tensormap(&maps.b_lo);  // FLT: the norm extensions
       uint32_t seq = 0;
       // flat, chunked: this CTA's run of (query tile x 128-row tile) tiles
       const bool chunked = a.flat && a.chunk_tiles > 0;
@@ -453,7 +483,7 @@ __global__ void __launch_bounds__((ATM ? kTqThreadsAtm : kTqThreads) + (EW - 1) 
               TQP(0, ok = mbar_wait(&empty[s], ((seq / SA) - 1) & 1, s_abort, &g_device_error));
             if (!ok) break;
             unsigned char* st = base + size_t(s) * L.stage;
-            mbar_arrive_expect_tx(&full[s], FLT ? (uint32_t)(KB * BN * 128) : kStageTx);
+            mbar_arrive_expect_tx(&full[s], FLT ? (uint32_t)(KB * BN * 128 + BN * 32) : kStageTx);
             const int yb = (int)(it.rb + (long long)t * BN);
             for (int kb = kb0; kb < kb0 + kps; ++kb) {
               const int x = kb * (FLT ? 64 : 32);
@@ -464,6 +494,8 @@ __global__ void __launch_bounds__((ATM ? kTqThreadsAtm : kTqThreads) + (EW - 1) 
               tma_load_2d(st + L.b_hi + size_t(kb - kb0) * BN * 128, &maps.b_hi, x, yb, &full[s]);
               if (!CONV && !FLT) tma_load_2d(st + L.b_lo, &maps.b_lo, x, yb, &full[s]);
             }
+            // FLT: the tile's norm extensions (32 bytes a row, x = 0)
+            if (FLT) tma_load_2d(st + size_t(KB) * BN * 128, &maps.b_lo, 0, yb, &full[s]);
             ++seq;
           }
         }
@@ -534,6 +566,9 @@ __global__ void __launch_bounds__((ATM ? kTqThreadsAtm : kTqThreads) + (EW - 1) 
               }
             }
             }
+            if (FLT)  // the norm-extension K-step: acc += A_e (hi + lo) of each row
+              mma_f16_ts(dt, tmem + KB * 32, desc_k_sw32(st + (uint32_t)(KB * BN * 128)), idesc,
+                         true);
             mma_commit(&empty[s]);
 #ifdef MF_TC_PROFILE
             atomicAdd(&g_tc_prof[8], (unsigned long long)(clock64() - _tm));
@@ -568,11 +603,14 @@ __global__ void __launch_bounds__((ATM ? kTqThreadsAtm : kTqThreads) + (EW - 1) 
     // FLT: the row s_q (q - c) is packed to fp16 as it arrives (half the
     // registers of the fp32 row the tf32 form keeps)
     uint32_t hq[FLT ? kTqMaxDAtm / 2 : 1];
+    // FLT: the row's norm-extension element A_e (two copies, as fp16)
+    uint32_t ae2 = 0u;
     // FLT: s_q (the query row minus the item's list centroid)
     auto fetch = [&](const ItemDesc& it) {
       const float* src = nullptr;
       const float* cen = nullptr;
       float sq = 1.0f;
+      ae2 = 0u;
       if (row < it.nq_item) {
         const int pr = a.flat ? 0 : a.pairs[it.a_row0 + row];
         const long long q = a.flat ? (long long)it.a_row0 + row : pr / a.P;
@@ -580,6 +618,8 @@ __global__ void __launch_bounds__((ATM ? kTqThreadsAtm : kTqThreads) + (EW - 1) 
         if (FLT) {
           cen = a.centroids + (long long)it.list * a.d;
           sq = a.pair_sq[pr];
+          const float ae = a.pair_ae[pr];  // a power of two (or 0): exact in fp16
+          ae2 = pack_f16x2(ae, ae);
         }
       }
       if constexpr (FLT) {
@@ -630,6 +670,14 @@ __global__ void __launch_bounds__((ATM ? kTqThreadsAtm : kTqThreads) + (EW - 1) 
               for (int i = 0; i < 32; ++i) pk[i] = hq[c * 32 + i];
               tmem_st32(lane_base + c * 32, pk);
             }
+          }
+          {
+            // the norm-extension K-step: [A_e, A_e, 0, ...] (16 fp16)
+            uint32_t pk[32];
+            pk[0] = ae2;
+#pragma unroll
+            for (int i = 1; i < 32; ++i) pk[i] = 0u;
+            tmem_st32(lane_base + KB * 32, pk);
           }
         }
         if constexpr (!FLT) {
@@ -854,6 +902,8 @@ __global__ void __launch_bounds__((ATM ? kTqThreadsAtm : kTqThreads) + (EW - 1) 
       // FLT: the accumulators are s_q s_l times the dot products
       const float sc = (FLT && valid) ? a.pair_sc[slot] : 1.0f;
       const float m2s = -2.0f * sc;
+      // FLT: u = qn - 2 sc acc, so u <= thr iff acc >= (qn - thr) / (2 sc)
+      const float h2 = 0.5f / sc;  // exact: sc is a power of two
       for (int i = 0; i < 32 * KC; i += 32) my_lists[i + lane] = kEmptyKey;
       __syncwarp();
       unsigned long long bound = kEmptyKey;
@@ -881,7 +931,7 @@ __global__ void __launch_bounds__((ATM ? kTqThreadsAtm : kTqThreads) + (EW - 1) 
 #ifdef MF_TC_PROFILE
         const long long p_s0 = clock64();
 #endif
-        if (METRIC == MF_METRIC_L2) {
+        if (METRIC == MF_METRIC_L2 && !FLT) {
           // row norms of this tile, shared by the four epilogue warps
           if (pf_r0 != r0) load_norms(r0, it.re);
           float* xs = xn_s + (ewarp * 2 + (tt & 1)) * BN;
@@ -923,7 +973,19 @@ __global__ void __launch_bounds__((ATM ? kTqThreadsAtm : kTqThreads) + (EW - 1) 
 #ifdef MF_TC_PROFILE
           const long long p_f0 = clock64();
 #endif
-          unsigned int acc = tq_accept<METRIC>(r, xs + c0, qn, m2s, thr_d, nvalid);
+          unsigned int acc;
+          if (FLT) {
+            // The exact form keeps a column iff RN(qn - 2 sc acc) <= thr, which
+            // implies acc >= (qn - thr - ulp(thr) / 2) h2. tau lowers the
+            // computed (qn - thr) h2 by 2^-22 (|qn| + |thr|) h2, more than that
+            // half ulp plus the roundings of tau itself, so every such column
+            // passes (a few just above thr may pass too: the merge orders them
+            // by their exact key). thr = +inf gives tau = -inf: all pass.
+            const float tau = (qn - thr_d) * h2 - (fabsf(qn) + fabsf(thr_d)) * h2 * 0x1p-22f;
+            acc = tq_accept_acc(r, tau, nvalid);
+          } else {
+            acc = tq_accept<METRIC>(r, xs + c0, qn, m2s, thr_d, nvalid);
+          }
           if (!valid) acc = 0;
           const unsigned int over = __ballot_sync(0xffffffffu, cnt + __popc(acc) > 32);
 #ifdef MF_TC_PROFILE
@@ -941,9 +1003,10 @@ __global__ void __launch_bounds__((ATM ? kTqThreadsAtm : kTqThreads) + (EW - 1) 
           // value selected from the registers by a 5-level mux tree
           for (unsigned int m = acc; m != 0u; m &= m - 1u) {
             const int j = __ffs(m) - 1;
-            const float dot = FLT ? __uint_as_float(select32(r, j)) * sc
-                                  : __uint_as_float(select32(r, j));
-            const float dist = METRIC == MF_METRIC_L2 ? l2_from_dot(qn, xs[c0 + j], dot) : -dot;
+            const float v = __uint_as_float(select32(r, j));
+            // FLT: u = qn - 2 sc acc (the norm is in the accumulator), clamped at 0
+            const float dist = FLT ? fmaxf(fmaf(m2s, v, qn), 0.0f) + 0.0f
+                               : (METRIC == MF_METRIC_L2 ? l2_from_dot(qn, xs[c0 + j], v) : -v);
             own_buf[cnt++] = make_key(dist, (unsigned int)(rc + j));
           }
           __syncwarp();
@@ -1216,6 +1279,22 @@ int make_map_f16(PFN_cuTensorMapEncodeTiled_v12000 enc, CUtensorMap* map, const 
   return MF_OK;
 }
 
+// The filter bank's 16-element fp16 norm extensions: rows of 32 bytes, tiles
+// of 16 x box_rows (32-byte inner box, 32-byte swizzle).
+int make_map_rn16(PFN_cuTensorMapEncodeTiled_v12000 enc, CUtensorMap* map, const void* p,
+                  int64_t rows, int box_rows) {
+  cuuint64_t dims[2] = {16, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {32};
+  cuuint32_t box[2] = {16, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(p), dims, strides,
+                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_32B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  MF_CHECK(r == CUDA_SUCCESS, MF_ERR_CUDA, "cuTensorMapEncodeTiled (norm extensions) failed (%d)",
+           (int)r);
+  return MF_OK;
+}
+
 __global__ void tf32_residual_kernel(const float4* __restrict__ x, int64_t n4, float4* lo) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n4) return;
@@ -1455,7 +1534,7 @@ int launch_tc_filter(const ScanArgs& a, int64_t b_rows, int64_t total_items, int
   MF_CHECK(a.k >= 1 && a.k <= kTqK && tq_choose_bf(a.d, &lay), MF_ERR_INVALID_ARGS,
            "filter scan does not fit (d=%d k=%d)", a.d, a.k);
   MF_CHECK(!a.flat && a.pair_qn && a.pair_thr && a.pair_sq && a.pair_sc && a.pair_cnt &&
-               a.centroids && a.items && a.item_total,
+               a.pair_ae && a.xrn16 && a.centroids && a.items && a.item_total,
            MF_ERR_INVALID_ARGS, "filter scan needs IVF items and its per-pair arrays");
   TqFn fn = lay.ew == 2 ? tq_scan_kernel<MF_METRIC_L2, 128, true, false, true, kTqK, 2>
                         : tq_scan_kernel<MF_METRIC_L2, 128, true, false, true, kTqK, 1>;
@@ -1465,6 +1544,7 @@ int launch_tc_filter(const ScanArgs& a, int64_t b_rows, int64_t total_items, int
   TqMaps maps;
   memset(&maps, 0, sizeof(maps));
   MF_TRY(make_map_f16(enc, &maps.b_hi, a.xb, a.d, b_rows, lay.BN));
+  MF_TRY(make_map_rn16(enc, &maps.b_lo, a.xrn16, b_rows, lay.BN));
   {
     std::lock_guard<std::mutex> lk(g_tc_mu);
     if (device < 0 || device >= 64 || g_tc_attr[device][0][slot] < (int)lay.total) {

@@ -329,16 +329,18 @@ class IVFFlatIndex:
             n = self._vecs.shape[0]
             h = torch.empty((n, self._dp), dtype=torch.float16, device=dev)
             rn = torch.empty(n, dtype=torch.float32, device=dev)
+            rn16 = torch.empty((n, 16), dtype=torch.float16, device=dev)
             stats = torch.empty((self._nlist, 4), dtype=torch.float32, device=dev)
             q = self._quantizer
             nat.call("mf_ivf_filter_bank", dev.index, nat.stream_of(dev), self._nlist, self._dp,
                      nat.ptr(self._offsets), nat.ptr(self._vecs), nat.ptr(self._norms),
-                     nat.ptr(q._xb.buf), n, nat.ptr(h), nat.ptr(rn), nat.ptr(stats))
-            self._fbank = (h, rn, stats)
+                     nat.ptr(q._xb.buf), n, nat.ptr(h), nat.ptr(rn), nat.ptr(rn16),
+                     nat.ptr(stats))
+            self._fbank = (h, rn, rn16, stats)
         return self._fbank
 
     def _search_filtered(self, xq, k, D, I) -> SearchResult:
-        bf, rn, stats = self._filter_bank()
+        bf, rn, rn16, stats = self._filter_bank()
         q = self._quantizer
         nq = xq.shape[0]
         nbytes = nat.workspace_size("mf_ivf_search_filtered_workspace_size", nq, self._nlist,
@@ -348,8 +350,8 @@ class IVFFlatIndex:
                  nat.ptr(xq), nq, nat.ptr(q._xb.buf), nat.ptr(q._norms.buf), self._nlist,
                  self._nprobe, nat.ptr(self._offsets), nat.ptr(self._vecs), nat.ptr(self._norms),
                  nat.ptr(self._lo), nat.ptr(self._ids), self._vecs.shape[0], nat.ptr(self._order),
-                 nat.ptr(bf), nat.ptr(rn), nat.ptr(stats), self._dp, k, nat.ptr(D), nat.ptr(I),
-                 nat.ptr(ws), ws.numel())
+                 nat.ptr(bf), nat.ptr(rn), nat.ptr(rn16), nat.ptr(stats), self._dp, k, nat.ptr(D),
+                 nat.ptr(I), nat.ptr(ws), ws.numel())
         return SearchResult(D, I)
 
     # ----------------------------------------------- coarse step with a bound
@@ -471,7 +473,7 @@ class IVFFlatIndex:
             return SearchResult(D, I)
         self._empty_lists_guard()
         if self._filter_ok(k):
-            bf, rn, stats = self._filter_bank()
+            bf, rn, rn16, stats = self._filter_bank()
             P = probes.shape[1]
             nbytes = nat.workspace_size("mf_ivf_search_bounded_filtered_workspace_size", nq,
                                         self._nlist, P, self._dp, k)
@@ -480,7 +482,8 @@ class IVFFlatIndex:
                      nat.stream_of(self.device), nat.ptr(xq), nq, nat.ptr(probes), P, self._nlist,
                      nat.ptr(self._offsets), nat.ptr(self._vecs), nat.ptr(self._norms),
                      nat.ptr(self._ids), self._vecs.shape[0], nat.ptr(self._order), nat.ptr(bf),
-                     nat.ptr(rn), nat.ptr(stats), nat.ptr(self._quantizer._xb.buf), self._dp, k,
+                     nat.ptr(rn), nat.ptr(rn16), nat.ptr(stats), nat.ptr(self._quantizer._xb.buf),
+                     self._dp, k,
                      nat.ptr(bound), nat.ptr(D), nat.ptr(I), nat.ptr(ws), ws.numel())
             return SearchResult(D, I)
         head, ws = self._ivf_args(xq, probes, k)

@@ -43,7 +43,8 @@ def check_knn(D, I, D_ref, I_ref, exact_of, *, rtol=RTOL, tie_rtol=TIE_RTOL, ato
         # distances, rank by rank
         both_inf = np.isinf(D[q]) & np.isinf(D_ref[q])
         tol = rtol * np.abs(np.where(np.isinf(D_ref[q]), 0, D_ref[q])) + atol
-        bad = ~both_inf & ~(np.abs(D[q] - D_ref[q]) <= tol)
+        with np.errstate(invalid="ignore"):  # inf - inf where both are empty slots
+            bad = ~both_inf & ~(np.abs(D[q] - D_ref[q]) <= tol)
         if bad.any():
             j = int(np.argmax(bad))
             errs.append(f"q{q} rank{j}: distance {D[q, j]!r} vs reference {D_ref[q, j]!r}")

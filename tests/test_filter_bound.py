@@ -29,15 +29,19 @@ def scale_exp(n: float) -> int:
 
 
 def list_scale(resid: np.ndarray):
-    """R_l (rounded up as the bank kernel rounds it) and s_l."""
+    """R_l (rounded up as the bank kernel rounds it), s_l, the rows' rn and
+    beta_l (R^2 beta < 2^15, the norm extension's power of two)."""
     rn = (resid.astype(np.float32) ** 2).sum(1, dtype=np.float32)
     R = float(np.sqrt(np.float32(rn.max()))) * (1.0 + 2.0 ** -10)
     e = max(-60, min(60, scale_exp(R)))
-    return R, 2.0 ** e, rn
+    er = math.frexp(R)[1] if R > 0 else 0
+    eb = max(-120, min(120, 15 - 2 * er))
+    return R, 2.0 ** e, rn, 2.0 ** eb
 
 
 def pair_bound(q, c, R, XN, sl, d):
-    """The kernel's e for this pair, in the same fp32 steps."""
+    """The kernel's e for this pair, in the same fp32 steps (including the
+    term of the norm fold: (d + 3) 2^-22 R^2)."""
     qc = (q - c).astype(np.float32)
     dc = float((qc * qc).sum(dtype=np.float32))
     nrm = math.sqrt(dc) * (1.0 + 2.0 ** -17)
@@ -45,7 +49,8 @@ def pair_bound(q, c, R, XN, sl, d):
     qn = float((q.astype(np.float32) ** 2).sum(dtype=np.float32))
     e = (float.fromhex("0x1.09p-9") * nrm * R
          + 2.0 ** -22 * math.sqrt(d) * (nrm / sl + R / sq)
-         + (d + 20) * 2.0 ** -23 * (qn + XN + dc + R * R) + 2.0 ** -100)
+         + (d + 20) * 2.0 ** -23 * (qn + XN + dc + R * R)
+         + (d + 3) * 2.0 ** -22 * R * R + 2.0 ** -100)
     return e, sq, dc
 
 
@@ -77,15 +82,25 @@ def test_truncating_accumulation_emulation():
 def check(q, c, X, rng_name=""):
     d = q.shape[0]
     resid = (X - c).astype(np.float32)
-    R, sl, rn = list_scale(resid)
+    R, sl, rn, beta = list_scale(resid)
     XN = float((X.astype(np.float32) ** 2).sum(1, dtype=np.float32).max())
     e, sq, dc = pair_bound(q, c, R, XN, sl, d)
     assert math.isfinite(e), "the bound must be finite for these magnitudes"
     qh = ((q - c).astype(np.float32) * np.float32(sq)).astype(np.float16).astype(np.float64)
     xh = (resid * np.float32(sl)).astype(np.float16).astype(np.float64)
     assert np.all(np.isfinite(qh)) and np.all(np.isfinite(xh)), "fp16 overflow"
-    dot = truncating_dot(xh, qh) / (sq * sl)
-    a = dc + rn.astype(np.float64) - 2.0 * dot
+    # the norm fold: each row extended by [hi, lo] of beta rn (fp16), the query
+    # by [A_e, A_e] with A_e = -s_q s_l / (2 beta); the tensor cores then give
+    # s_q s_l (dot - rn / 2), and a = dc - 2 acc / (s_q s_l)
+    ae = -sq * sl / (2.0 * beta)
+    assert 2.0 ** -24 <= abs(ae) <= 2.0 ** 15 and float(np.float16(ae)) == ae
+    v = (rn.astype(np.float32) * np.float32(beta)).astype(np.float32)
+    hi = v.astype(np.float16)
+    lo = (v - hi.astype(np.float32)).astype(np.float16)
+    xa = np.concatenate([xh, hi.astype(np.float64)[:, None], lo.astype(np.float64)[:, None]], 1)
+    qa = np.concatenate([qh, [ae, ae]])
+    acc = truncating_dot(xa, qa)
+    a = dc - 2.0 * acc / (sq * sl)
     t = ((X.astype(np.float64) - q.astype(np.float64)) ** 2).sum(1)
     err = np.abs(a - t)
     assert err.max() <= e, f"{rng_name}: error {err.max():.4g} above the bound {e:.4g}"

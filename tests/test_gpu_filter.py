@@ -162,11 +162,12 @@ def test_dims_outside_the_filter_take_the_exact_scan(cuda_device, d):
     h = torch.empty((n, idx._dp), dtype=torch.float16, device=dev)
     rn = torch.empty(n, dtype=torch.float32, device=dev)
     stats = torch.empty((idx.nlist, 4), dtype=torch.float32, device=dev)
+    rn16 = torch.empty((n, 16), dtype=torch.float16, device=dev)
     lib = nat.load()
     status = lib.mf_ivf_filter_bank(dev.index, nat.stream_of(dev), idx.nlist, idx._dp,
                                     nat.ptr(idx._offsets), nat.ptr(idx._vecs),
                                     nat.ptr(idx._norms), nat.ptr(idx.quantizer._xb.buf), n,
-                                    nat.ptr(h), nat.ptr(rn), nat.ptr(stats))
+                                    nat.ptr(h), nat.ptr(rn), nat.ptr(rn16), nat.ptr(stats))
     assert status == 6, lib.mf_last_error()
 
 
