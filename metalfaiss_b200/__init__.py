@@ -12,7 +12,7 @@ from .clustering import ClusteringParameters, KMeans, kmeans_clustering
 from .errors import (BadStateError, CudaError, ErrorCode, FormatError, InvalidArgumentError,
                      IOFaissError, MetalFaissError, NotImplementedFaissError, check_error,
                      clear_last_error, get_last_error)
-from .index_binary_flat import BinaryFlatIndex
+from .index_binary_flat import BinaryFlatIndex, BinaryIVFIndex
 from .index_flat import FlatIndex
 from .index_io import read_index, write_index
 from .index_ivf_flat import IVFFlatIndex
@@ -23,7 +23,7 @@ from .search_result import SearchRangeResult, SearchResult
 __version__ = "0.1.0"
 
 __all__ = [
-    "FlatIndex", "IVFFlatIndex", "BinaryFlatIndex", "IVFPQIndex", "ProductQuantizer", "MetricType", "SearchResult", "SearchRangeResult",
+    "FlatIndex", "IVFFlatIndex", "BinaryFlatIndex", "BinaryIVFIndex", "IVFPQIndex", "ProductQuantizer", "MetricType", "SearchResult", "SearchRangeResult",
     "ClusteringParameters", "KMeans", "kmeans_clustering", "ErrorCode", "MetalFaissError",
     "InvalidArgumentError", "BadStateError", "NotImplementedFaissError", "CudaError",
     "check_error", "get_last_error", "clear_last_error", "IOFaissError", "FormatError",

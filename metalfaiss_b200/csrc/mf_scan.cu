@@ -519,8 +519,29 @@ int launch_merge(const float* pd, const int64_t* pl, int64_t nq, int parts, int 
 
 // ------------------------------------------------------------- flat search
 namespace {
-void plan_splits(FlatPlan& p, int64_t nq, int64_t nb, int k, int device, int tq, int per_sm) {
+// Tensor-core flat searches whose rows (fp32 + tf32 residual) pass this size
+// are cut into row splits of about this size, taken split-major: the CTAs
+// working at the same time scan the same split for different query tiles, so
+// its rows come from HBM about once and from L2 for the other query tiles
+// (equal runs per CTA would stream the whole database once per query tile).
+constexpr long long kFlatSplitBytes = 64ll << 20;
+
+void plan_splits(FlatPlan& p, int64_t nq, int64_t nb, int d, int k, int device, int tq,
+                 int per_sm) {
   p.nqt = (int)ceil_div(nq, tq);
+  if (per_sm == 0 && p.nqt > 1 && (long long)nb * 8 * d > kFlatSplitBytes) {
+    long long s = ceil_div((long long)nb * 8 * d, kFlatSplitBytes);
+    long long rps = ceil_div(nb, s);
+    rps = ceil_div(rps, kScanTR) * kScanTR;
+    s = ceil_div(nb, rps);
+    p.splits = (int)s;
+    p.rows_per_split = rps;
+    p.chunk_tiles = 0;
+    p.tiles_per_qt = 0;
+    p.chunks = (int)((long long)p.nqt * s);
+    (void)k;
+    return;
+  }
   if (per_sm == 0) {
     // Tensor cores, one persistent CTA per SM: equal runs of tiles, each CTA
     // taking the pieces (cut at query-tile boundaries) of its own run, so no
@@ -566,8 +587,8 @@ void plan_splits(FlatPlan& p, int64_t nq, int64_t nb, int k, int device, int tq,
 FlatPlan plan_flat(int64_t nq, int64_t nb, int d, int k, int device, int tq) {
   const int kcap = scan_kcap(k) ? scan_kcap(k) : 256;
   FlatPlan simt, tc;
-  plan_splits(simt, nq, nb, k, device, 32, kcap >= 256 ? 1 : (kcap >= 128 ? 2 : 3));
-  plan_splits(tc, nq, nb, k, device, tc_group(), 0);
+  plan_splits(simt, nq, nb, d, k, device, 32, kcap >= 256 ? 1 : (kcap >= 128 ? 2 : 3));
+  plan_splits(tc, nq, nb, d, k, device, tc_group(), 0);
   FlatPlan p = tq == 32 ? simt : tc;
   // workspace: the larger of the two engines' needs
   const int max_splits = simt.splits > tc.splits ? simt.splits : tc.splits;

@@ -18,7 +18,10 @@ constexpr int kErrWaitTimeout = 1;
 // polls whatever the timer says, and turns a lost arrival into an error
 // instead of a hang. Legitimate waits (a role idling through a long item) are
 // well under a millisecond.
-constexpr unsigned kWaitHintNs = 1000000u;
+#ifndef MF_WAIT_HINT_NS
+#define MF_WAIT_HINT_NS 1000000u
+#endif
+constexpr unsigned kWaitHintNs = MF_WAIT_HINT_NS;
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;
 constexpr unsigned kWaitMaxIters = 1u << 26;
 
@@ -40,13 +43,23 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
 }
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity), "r"(kWaitHintNs)
-      : "memory");
+  if (kWaitHintNs == 0u) {  // the hardware's own time limit
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+  } else {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(kWaitHintNs)
+        : "memory");
+  }
   return ok != 0;
 }
 __device__ __forceinline__ unsigned long long globaltimer_ns() {

@@ -54,9 +54,23 @@ __device__ unsigned long long g_tc_prof[20];
     expr;                              \
     var += clock64() - _t0;            \
   } while (0)
+// Per-tile and per-item clock stamps of the filter scan in the first kTrCtas
+// CTAs (instrumented builds only): tiles [MMA accumulator free, MMA stage
+// ready, MMA committed, epilogue got it, epilogue released it, -], items
+// [loader wrote A, MMA saw A, epilogue started, epilogue finished].
+constexpr int kTrCtas = 2, kTrTiles = 4096, kTrItems = 1024;
+__device__ long long g_tc_trace[kTrCtas][kTrTiles][6];
+__device__ long long g_tc_trace_item[kTrCtas][kTrItems][4];
+#define TQT(on, arr, idx, f, n)                                               \
+  do {                                                                        \
+    if ((on) && blockIdx.x < kTrCtas && (idx) < (n)) arr[blockIdx.x][idx][f] = clock64(); \
+  } while (0)
 #else
 #define TQP(i, expr) expr
 #define TQL(var, expr) expr
+#define TQT(on, arr, idx, f, n) \
+  do {                          \
+  } while (0)
 #endif
 
 using namespace sm100;
@@ -202,6 +216,10 @@ __device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
   const __half2 h = __floats2half2_rn(lo, hi);
   return *reinterpret_cast<const uint32_t*>(&h);
 }
+
+// Survivors per lane up to which a chunk's keys are built by each lane's own
+// loop over its set bits; past it, by one pass over all 32 columns.
+constexpr unsigned int kTqSerialSurvivors = 6;
 
 // r[j] for a run-time j without indexing the register array (which would put
 // it in local memory): five levels of selects on the bits of j.
@@ -523,18 +541,21 @@ __global__ void __launch_bounds__((ATM ? kTqThreadsAtm : kTqThreads) + (EW - 1) 
           bool aok = true;
           TQP(17, aok = mbar_wait(afull, qi & 1, s_abort, &g_device_error));
           if (!aok) break;
+          TQT(FLT, g_tc_trace_item, qi, 1, kTrItems);
           tc_fence_after();
         }
         for (int t = 0; t < nT; ++t, ++tt) {
           const int b = tt % NACC;
           if (tt >= (uint32_t)NACC)
             TQP(1, mbar_wait(&acce[b], ((tt / NACC) - 1) & 1, s_abort, &g_device_error));
+          TQT(FLT, g_tc_trace, tt, 0, kTrTiles);
           tc_fence_after();
           const uint32_t dt = tmem + L.acc0 + b * BN;
           const int kps = FLT ? KB : 1;  // K-blocks per stage
           for (int kb0 = 0; kb0 < KB; kb0 += kps, ++seq) {
             const int s = seq % SA;
             TQP(2, mbar_wait(CONV ? &conv[s] : &full[s], (seq / SA) & 1, s_abort, &g_device_error));
+            TQT(FLT, g_tc_trace, tt, 1, kTrTiles);
             tc_fence_after();
             const uint32_t st = smem_u32(base + size_t(s) * L.stage);
 #ifdef MF_TC_PROFILE
@@ -575,6 +596,7 @@ __global__ void __launch_bounds__((ATM ? kTqThreadsAtm : kTqThreads) + (EW - 1) 
 #endif
           }
           mma_commit(&accf[b]);
+          TQT(FLT, g_tc_trace, tt, 2, kTrTiles);
         }
         // the query tile may be overwritten once this item's MMAs complete
         if (ATM) mma_commit(afree);
@@ -705,6 +727,7 @@ __global__ void __launch_bounds__((ATM ? kTqThreadsAtm : kTqThreads) + (EW - 1) 
         tmem_wait_st();
         tc_fence_before();
         mbar_arrive(afull);
+        if (cid == 0) TQT(FLT, g_tc_trace_item, qi, 0, kTrItems);
         // This item's row stages. The next item's queries are fetched as soon
         // as it is published (checked without blocking between stages: the
         // producer publishes it only after issuing this item's stages, which
@@ -882,6 +905,7 @@ __global__ void __launch_bounds__((ATM ? kTqThreadsAtm : kTqThreads) + (EW - 1) 
       __syncwarp();
       if (lane == 0) mbar_arrive(&qempty[qs]);
       if (item < 0) break;
+      if (tid == 0) TQT(FLT, g_tc_trace_item, qi, 2, kTrItems);
       const long long nrows = it.re > it.rb ? it.re - it.rb : 0;
       const int nT = (int)((nrows + BN - 1) / BN);
       const bool valid = erow < it.nq_item;
@@ -954,6 +978,7 @@ __global__ void __launch_bounds__((ATM ? kTqThreadsAtm : kTqThreads) + (EW - 1) 
         p_stage += clock64() - p_s0;
 #endif
         TQL(p_wait, mbar_wait(&accf[b], (tt / NACC) & 1, s_abort, &g_device_error));
+        if (tid == 0) TQT(FLT, g_tc_trace, tt, 3, kTrTiles);
 #ifdef MF_TC_PROFILE
         ++p_tiles;
 #endif
@@ -999,15 +1024,30 @@ __global__ void __launch_bounds__((ATM ? kTqThreadsAtm : kTqThreads) + (EW - 1) 
             p_nmerge += __popc(over);
 #endif
           }
-          // survivors are few: a loop over the set bits, with the column's
-          // value selected from the registers by a 5-level mux tree
-          for (unsigned int m = acc; m != 0u; m &= m - 1u) {
-            const int j = __ffs(m) - 1;
-            const float v = __uint_as_float(select32(r, j));
-            // FLT: u = qn - 2 sc acc (the norm is in the accumulator), clamped at 0
+          // The survivors' keys. FLT: u = qn - 2 sc acc (the norm is in the
+          // accumulator), clamped at 0.
+          auto key_of = [&](uint32_t bits, int j) {
+            const float v = __uint_as_float(bits);
             const float dist = FLT ? fmaxf(fmaf(m2s, v, qn), 0.0f) + 0.0f
                                : (METRIC == MF_METRIC_L2 ? l2_from_dot(qn, xs[c0 + j], v) : -v);
-            own_buf[cnt++] = make_key(dist, (unsigned int)(rc + j));
+            return make_key(dist, (unsigned int)(rc + j));
+          };
+          // A lane loops over its own set bits while every lane has few (the
+          // column's value selected by a 5-level mux tree). A warp with a busy
+          // lane (an open list at the start of a flat piece) takes every
+          // column in turn with static register indices instead, so its cost
+          // stops growing with the busiest lane's count. The filter scan keeps
+          // the loop alone: its survivors are rarer, and the extra code slowed it.
+          if (!FLT &&
+              __reduce_max_sync(0xffffffffu, (unsigned int)__popc(acc)) > kTqSerialSurvivors) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (acc & (1u << j)) own_buf[cnt++] = key_of(r[j], j);
+          } else {
+            for (unsigned int m = acc; m != 0u; m &= m - 1u) {
+              const int j = __ffs(m) - 1;
+              own_buf[cnt++] = key_of(select32(r, j), j);
+            }
           }
           __syncwarp();
 #ifdef MF_TC_PROFILE
@@ -1029,6 +1069,7 @@ __global__ void __launch_bounds__((ATM ? kTqThreadsAtm : kTqThreads) + (EW - 1) 
         }
         tc_fence_before();
         mbar_arrive(&acce[b]);
+        if (tid == 0) TQT(FLT, g_tc_trace, tt, 4, kTrTiles);
       }
       // flush the remaining candidates, then write each row's k keys
 #ifdef MF_TC_PROFILE
@@ -1111,6 +1152,7 @@ __global__ void __launch_bounds__((ATM ? kTqThreadsAtm : kTqThreads) + (EW - 1) 
 #ifdef MF_TC_PROFILE
       p_out += clock64() - p_o0;
 #endif
+      if (tid == 0) TQT(FLT, g_tc_trace_item, qi, 3, kTrItems);
     }
 #ifdef MF_TC_PROFILE
     p_loop = clock64() - p_start;
@@ -1566,6 +1608,18 @@ int launch_tc_filter(const ScanArgs& a, int64_t b_rows, int64_t total_items, int
 }
 
 #ifdef MF_TC_PROFILE
+extern "C" MF_API int mf_tc_trace_read(long long* tiles, long long* items, int reset) {
+  MF_CUDA(cudaMemcpyFromSymbol(tiles, g_tc_trace, sizeof(g_tc_trace)));
+  MF_CUDA(cudaMemcpyFromSymbol(items, g_tc_trace_item, sizeof(g_tc_trace_item)));
+  if (reset) {
+    void* p = nullptr;
+    MF_CUDA(cudaGetSymbolAddress(&p, g_tc_trace));
+    MF_CUDA(cudaMemset(p, 0, sizeof(g_tc_trace)));
+    MF_CUDA(cudaGetSymbolAddress(&p, g_tc_trace_item));
+    MF_CUDA(cudaMemset(p, 0, sizeof(g_tc_trace_item)));
+  }
+  return MF_OK;
+}
 extern "C" MF_API int mf_tc_profile_read(unsigned long long* out16, int reset) {
   MF_CUDA(cudaMemcpyFromSymbol(out16, g_tc_prof, 20 * sizeof(unsigned long long)));
   if (reset) {

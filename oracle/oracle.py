@@ -269,6 +269,32 @@ def hamming_range(xq01, xb01, radius, ids=None):
     return lims, d[qi, ri], labels
 
 
+def hamming_ivf_search(xq01, centroids01, list_rows01, list_ids, nprobe, k):
+    """BinaryIVFIndex.search, python/metalfaiss/index/binary_ivf_index.py:113-185:
+    the nprobe Hamming-nearest centroids (hamming_search over them), then the
+    probed lists' rows concatenated in probe order (each list in insertion
+    order) and ranked by Hamming distance, ties to the earlier candidate (a
+    stable sort). Missing slots: distance inf, label -1 (the reference pads
+    with label 0, :163-171). list_rows01[l] is list l's (n_l, d) 0/1 array."""
+    xq01 = np.asarray(xq01, np.uint8)
+    P = min(int(nprobe), len(centroids01))
+    _, probes = hamming_search(xq01, centroids01, P)
+    D = np.full((len(xq01), k), np.inf, np.float32)
+    I = np.full((len(xq01), k), -1, np.int64)
+    for i in range(len(xq01)):
+        rows = [list_rows01[l] for l in probes[i] if len(list_rows01[l])]
+        if not rows:
+            continue
+        cand = np.concatenate(rows)
+        cid = np.concatenate([np.asarray(list_ids[l], np.int64) for l in probes[i]
+                              if len(list_rows01[l])])
+        dist = hamming_distances(xq01[i:i + 1], cand)[0]
+        order = np.argsort(dist, kind="stable")[:k]
+        D[i, :len(order)] = dist[order]
+        I[i, :len(order)] = cid[order]
+    return D, I, probes
+
+
 # ------------------------------------------------------------------ IVFPQ
 def pq_encode(x, pq_centroids):
     """ProductQuantizer.compute_codes (python/metalfaiss/index/product_quantizer.py):

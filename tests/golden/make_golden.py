@@ -278,6 +278,57 @@ def gen_binary(m, out):
     out["binary_cases"] = np.array(cases)
 
 
+def gen_binary_ivf(m, out):
+    """BinaryIVFIndex train / add / search, python/metalfaiss/index/binary_ivf_index.py:84-185,
+    over a quantizer (the BinaryFlatIndex subclass of gen_binary) that holds
+    the centroids: the reference's train() trains the quantizer, which stores
+    nothing, so the centroids are added to it first. Ids are passed as a list
+    (its `ids[i] if ids else i` tests the container's truth), and vectors as
+    nested lists (its _validate_binary tests their truth, binary_index.py:221);
+    the quantizer's search turns those lists into arrays, which the IVF's
+    _add and _search hand it as they are (binary_flat_index.py:67 reads .shape),
+    and wraps its (distances, indices) tuple in the SearchResult whose .labels
+    they read (binary_ivf_index.py:115,138)."""
+    import importlib
+
+    b = importlib.import_module("metalfaiss.index.binary_flat_index")
+    ivf = importlib.import_module("metalfaiss.index.binary_ivf_index")
+    sr = importlib.import_module("metalfaiss.utils.search_result")
+    noop = lambda self, *a, **k: None  # noqa: E731
+    as_arr = lambda xs: mxs.array(np.asarray(xs, np.uint8)) if isinstance(xs, list) else xs  # noqa: E731
+    Concrete = type("BinaryFlatConcrete", (b.BinaryFlatIndex,), {
+        "_add": noop, "_train": noop, "_search": noop, "_reconstruct": noop,
+        "ntotal": property(lambda s: s._ntotal, lambda s, v: setattr(s, "_ntotal", v)),
+        "search": lambda s, xs, k: sr.SearchResult(*b.BinaryFlatIndex.search(s, as_arr(xs), k))})
+    cases = []
+    for (n, d, nlist, nq, k, nprobe, seed) in [(400, 64, 8, 10, 10, 2, 50),
+                                               (600, 128, 12, 8, 40, 3, 51),
+                                               (200, 72, 6, 6, 90, 1, 52)]:
+        x = rng(seed).integers(0, 2, size=(n, d)).astype(np.uint8)
+        q = rng(seed + 1).integers(0, 2, size=(nq, d)).astype(np.uint8)
+        q[:2] = x[[3, n - 1]]
+        cents = x[rng(seed + 2).choice(n, nlist, replace=False)]
+        quant = Concrete(d)
+        quant.add(mxs.array(cents))
+        idx = ivf.BinaryIVFIndex(quant, d, nlist)
+        idx.train(x.tolist())
+        ids = [int(7 * i + 5) for i in range(n)]
+        idx.add(x.tolist(), ids)
+        idx.nprobe = nprobe
+        res = idx.search(q.tolist(), k)
+        D, I = res.distances, res.indices
+        tag = f"binivf_{n}_{d}_{nlist}_{k}"
+        out[tag + "_xb"] = x
+        out[tag + "_xq"] = q
+        out[tag + "_cents"] = cents
+        out[tag + "_ids"] = np.asarray(ids, np.int64)
+        out[tag + "_nprobe"] = np.int64(nprobe)
+        out[tag + "_D"] = np_(D).astype(np.float32)
+        out[tag + "_I"] = np_(I).astype(np.int64)
+        cases.append(tag)
+    out["binivf_cases"] = np.array(cases)
+
+
 def main():
     mods = load_reference()
     out = {}
@@ -287,6 +338,7 @@ def main():
     gen_range(mods, out)
     gen_kmeans(mods, out)
     gen_binary(mods, out)
+    gen_binary_ivf(mods, out)
     path = HERE / "reference_golden.npz"
     np.savez_compressed(path, **out)
     print(f"[golden] wrote {path} ({path.stat().st_size // 1024} KiB, {len(out)} arrays)")

@@ -43,7 +43,8 @@ def _wrap(fn):
     return f
 
 
-sum = _wrap(lambda x, axis=None, keepdims=False: np.sum(x, axis=axis, keepdims=keepdims))
+sum = _wrap(lambda x, axis=None, keepdims=False, dtype=None:
+            np.sum(x, axis=axis, keepdims=keepdims, dtype=dtype))
 max = _wrap(lambda x, axis=None, keepdims=False: np.max(x, axis=axis, keepdims=keepdims))
 min = _wrap(lambda x, axis=None, keepdims=False: np.min(x, axis=axis, keepdims=keepdims))
 mean = _wrap(lambda x, axis=None, keepdims=False: np.mean(x, axis=axis, keepdims=keepdims))
@@ -89,6 +90,19 @@ bitwise_or = _wrap(lambda a, b: np.bitwise_or(a, np.asarray(b, np.asarray(a).dty
 bitwise_xor = _wrap(lambda a, b: np.bitwise_xor(a, np.asarray(b, np.asarray(a).dtype)))
 right_shift = _wrap(lambda a, b: np.right_shift(a, np.asarray(b, np.asarray(a).dtype)))
 left_shift = _wrap(lambda a, b: np.left_shift(a, np.asarray(b, np.asarray(a).dtype)))
+
+
+def _scatter(a, indices, updates, axis=0):
+    out = np.array(a, copy=True)
+    idx = np.asarray(indices).astype(np.int64)
+    sl = [slice(None)] * out.ndim
+    sl[axis] = idx
+    out[tuple(sl)] = np.asarray(updates)
+    return out
+
+
+scatter = _wrap(_scatter)
+broadcast_to = _wrap(lambda x, shape: np.broadcast_to(np.asarray(x), shape).copy())
 
 
 def eval(*arrays):  # noqa: A001 - MLX's name

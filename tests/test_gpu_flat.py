@@ -79,6 +79,21 @@ def test_flat_many_queries_multi_split(cuda_device):
     _check(idx, xq, xb, 16, MetricType.INNER_PRODUCT)
 
 
+@pytest.mark.parametrize("metric,k", [(MetricType.INNER_PRODUCT, 100), (MetricType.L2, 10)])
+def test_flat_split_major_database(cuda_device, metric, k):
+    """A database past 64 MB of fp32 rows and residuals with several query
+    tiles: the tensor-core scan takes (row split, query tile) items split-major
+    and merges one partial list per split; ids mapped after the merge."""
+    xb = syn.unit_rows(80_000, 128, seed=31)
+    xq = syn.unit_rows(300, 128, seed=32)
+    xq[:2] = xb[[7, 79_999]]
+    ids = np.arange(80_000, dtype=np.int64) * 5 + 3
+    idx = FlatIndex(128, metric)
+    idx.add(xb, ids)
+    D, I = _check(idx, xq, xb, k, metric, ids)
+    assert list(I[:2, 0]) == [ids[7], ids[79_999]]
+
+
 def test_flat_ids_64bit_self_query(cuda_device):
     """python/metalfaiss/unittest/test_mlx_index.py:231-240: self-query returns the own 64-bit id."""
     xb = syn.gaussian(1000, 64, seed=11)

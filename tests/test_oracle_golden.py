@@ -105,3 +105,27 @@ def test_hamming_oracle_matches_reference_binary_flat():
         np.testing.assert_array_equal(D, g[tag + "_D"])
         np.testing.assert_array_equal(I, g[tag + "_I"])
         np.testing.assert_array_equal(xb[5:6], g[tag + "_rec"])
+
+
+def _binivf_lists(xb, ids, cents):
+    """Rows into their nearest centroid's list (ties to the lower centroid), in add order."""
+    _, a = oracle.hamming_search(xb, cents, 1)
+    a = a[:, 0]
+    return [xb[a == l] for l in range(len(cents))], [ids[a == l] for l in range(len(cents))]
+
+
+def test_hamming_ivf_oracle_matches_reference_binary_ivf():
+    """oracle.hamming_ivf_search against BinaryIVFIndex.search run from the
+    reference's own module (tests/golden/make_golden.py gen_binary_ivf).
+    Missing slots: the reference pads label 0, the oracle -1; both distance inf."""
+    for tag in G["binivf_cases"]:
+        tag = str(tag)
+        xb, xq, cents, ids = (G[tag + s] for s in ("_xb", "_xq", "_cents", "_ids"))
+        k = G[tag + "_D"].shape[1]
+        rows, lid = _binivf_lists(xb, ids, cents)
+        D, I, _ = oracle.hamming_ivf_search(xq, cents, rows, lid, int(G[tag + "_nprobe"]), k)
+        np.testing.assert_array_equal(D, G[tag + "_D"])
+        pad = np.isinf(D)
+        np.testing.assert_array_equal(I[~pad], G[tag + "_I"][~pad])
+        assert (I[pad] == -1).all() and (G[tag + "_I"][pad] == 0).all()
+    assert any(np.isinf(G[str(t) + "_D"]).any() for t in G["binivf_cases"])  # padding covered
