@@ -41,9 +41,12 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
                "r"(bytes)
                : "memory");
 }
+// SPIN: the form without a suspend-time hint (the hardware's own, shorter
+// limit), for waits on the critical path of a pipeline.
+template <bool SPIN = false>
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
-  if (kWaitHintNs == 0u) {  // the hardware's own time limit
+  if (SPIN || kWaitHintNs == 0u) {
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
         "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
@@ -72,12 +75,13 @@ __device__ __forceinline__ unsigned long long globaltimer_ns() {
 // phase does not complete within the limits above; `abort` (shared by the
 // CTA's roles) is raised then, and a wait that sees it raised by another role
 // returns false at once, so every role leaves its loop.
+template <bool SPIN = false>
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* abort, int* err) {
   if (*(volatile int*)abort) return false;
-  if (mbar_try_wait(bar, parity)) return true;
+  if (mbar_try_wait<SPIN>(bar, parity)) return true;
   const unsigned long long t0 = globaltimer_ns();
   for (unsigned i = 0; i < kWaitMaxIters; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait<SPIN>(bar, parity)) return true;
     if (*(volatile int*)abort) return false;
     if (globaltimer_ns() - t0 > kWaitLimitNs) break;
   }

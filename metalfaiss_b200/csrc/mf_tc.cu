@@ -56,10 +56,12 @@ __device__ unsigned long long g_tc_prof[20];
   } while (0)
 // Per-tile and per-item clock stamps of the filter scan in the first kTrCtas
 // CTAs (instrumented builds only): tiles [MMA accumulator free, MMA stage
-// ready, MMA committed, epilogue got it, epilogue released it, -], items
+// ready, MMA committed, epilogue got it, epilogue released it, its first
+// accumulator chunk arrived, its first two chunks done, all chunks done,
+// producer got the free stage (its loads issued), -], items
 // [loader wrote A, MMA saw A, epilogue started, epilogue finished].
 constexpr int kTrCtas = 2, kTrTiles = 4096, kTrItems = 1024;
-__device__ long long g_tc_trace[kTrCtas][kTrTiles][6];
+__device__ long long g_tc_trace[kTrCtas][kTrTiles][10];
 __device__ long long g_tc_trace_item[kTrCtas][kTrItems][4];
 #define TQT(on, arr, idx, f, n)                                               \
   do {                                                                        \
@@ -217,6 +219,14 @@ __device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
   return *reinterpret_cast<const uint32_t*>(&h);
 }
 
+// The filter scan's pipeline-critical waits (epilogue on an accumulator, MMA
+// on a free accumulator or a landed stage) spin without a suspend hint.
+#ifndef MF_TC_SPIN
+#define MF_TC_SPIN 0
+#endif
+constexpr bool kTcSpin = MF_TC_SPIN != 0;
+constexpr bool kTcSpinProducer = MF_TC_SPIN > 1;  // the producer's waits on free stages too
+
 // Survivors per lane up to which a chunk's keys are built by each lane's own
 // loop over its set bits; past it, by one pass over all 32 columns.
 constexpr unsigned int kTqSerialSurvivors = 6;
@@ -308,6 +318,26 @@ __device__ __forceinline__ unsigned int tq_accept(const uint32_t (&r)[32], const
   const unsigned int all = rej[0] | (rej[1] << 8) | (rej[2] << 16) | (rej[3] << 24);
   const unsigned int in_range = nvalid >= 32 ? 0xffffffffu : ((1u << nvalid) - 1u);
   return ~all & in_range;
+}
+
+// The largest of 32 fp32 values as a tree of three-input maxima (no NaN
+// among them: the accumulators of finite operands).
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+__device__ __forceinline__ float max32(const uint32_t (&r)[32]) {
+  float l1[11];
+#pragma unroll
+  for (int i = 0; i < 10; ++i)
+    l1[i] = max3f(__uint_as_float(r[3 * i]), __uint_as_float(r[3 * i + 1]),
+                  __uint_as_float(r[3 * i + 2]));
+  l1[10] = fmaxf(__uint_as_float(r[30]), __uint_as_float(r[31]));
+  const float a = max3f(l1[0], l1[1], l1[2]);
+  const float b = max3f(l1[3], l1[4], l1[5]);
+  const float c = max3f(l1[6], l1[7], l1[8]);
+  return max3f(max3f(a, b, c), l1[9], l1[10]);
 }
 
 // Accept mask of a 32-column chunk of the filter scan, whose accumulators
@@ -498,8 +528,10 @@ __global__ void __launch_bounds__((ATM ? kTqThreadsAtm : kTqThreads) + (EW - 1) 
             const int s = seq % SA;
             bool ok = true;
             if (seq >= (uint32_t)SA)
-              TQP(0, ok = mbar_wait(&empty[s], ((seq / SA) - 1) & 1, s_abort, &g_device_error));
+              TQP(0, ok = mbar_wait<FLT && kTcSpinProducer>(&empty[s], ((seq / SA) - 1) & 1,
+                                                            s_abort, &g_device_error));
             if (!ok) break;
+            TQT(FLT, g_tc_trace, seq, 8, kTrTiles);
             unsigned char* st = base + size_t(s) * L.stage;
             mbar_arrive_expect_tx(&full[s], FLT ? (uint32_t)(KB * BN * 128 + BN * 32) : kStageTx);
             const int yb = (int)(it.rb + (long long)t * BN);
@@ -547,14 +579,16 @@ __global__ void __launch_bounds__((ATM ? kTqThreadsAtm : kTqThreads) + (EW - 1) 
         for (int t = 0; t < nT; ++t, ++tt) {
           const int b = tt % NACC;
           if (tt >= (uint32_t)NACC)
-            TQP(1, mbar_wait(&acce[b], ((tt / NACC) - 1) & 1, s_abort, &g_device_error));
+            TQP(1, mbar_wait<FLT && kTcSpin>(&acce[b], ((tt / NACC) - 1) & 1, s_abort,
+                                             &g_device_error));
           TQT(FLT, g_tc_trace, tt, 0, kTrTiles);
           tc_fence_after();
           const uint32_t dt = tmem + L.acc0 + b * BN;
           const int kps = FLT ? KB : 1;  // K-blocks per stage
           for (int kb0 = 0; kb0 < KB; kb0 += kps, ++seq) {
             const int s = seq % SA;
-            TQP(2, mbar_wait(CONV ? &conv[s] : &full[s], (seq / SA) & 1, s_abort, &g_device_error));
+            TQP(2, mbar_wait<FLT && kTcSpin>(CONV ? &conv[s] : &full[s], (seq / SA) & 1, s_abort,
+                                             &g_device_error));
             TQT(FLT, g_tc_trace, tt, 1, kTrTiles);
             tc_fence_after();
             const uint32_t st = smem_u32(base + size_t(s) * L.stage);
@@ -977,7 +1011,8 @@ __global__ void __launch_bounds__((ATM ? kTqThreadsAtm : kTqThreads) + (EW - 1) 
 #ifdef MF_TC_PROFILE
         p_stage += clock64() - p_s0;
 #endif
-        TQL(p_wait, mbar_wait(&accf[b], (tt / NACC) & 1, s_abort, &g_device_error));
+        TQL(p_wait,
+            mbar_wait<FLT && kTcSpin>(&accf[b], (tt / NACC) & 1, s_abort, &g_device_error));
         if (tid == 0) TQT(FLT, g_tc_trace, tt, 3, kTrTiles);
 #ifdef MF_TC_PROFILE
         ++p_tiles;
@@ -1007,11 +1042,21 @@ __global__ void __launch_bounds__((ATM ? kTqThreadsAtm : kTqThreads) + (EW - 1) 
             // passes (a few just above thr may pass too: the merge orders them
             // by their exact key). thr = +inf gives tau = -inf: all pass.
             const float tau = (qn - thr_d) * h2 - (fabsf(qn) + fabsf(thr_d)) * h2 * 0x1p-22f;
-            acc = tq_accept_acc(r, tau, nvalid);
+            // Most chunks keep nothing: the chunk's largest accumulator says
+            // whether any column can pass (exactly: acc >= tau for some
+            // column iff their maximum is >= tau); only then is the mask built.
+            const bool hit = valid && (nvalid < 32 ? nvalid > 0 : max32(r) >= tau);
+            if (!__any_sync(0xffffffffu, hit)) {
+#ifdef MF_TC_PROFILE
+              p_filter += clock64() - p_f0;
+#endif
+              return;
+            }
+            acc = hit ? tq_accept_acc(r, tau, nvalid) : 0u;
           } else {
             acc = tq_accept<METRIC>(r, xs + c0, qn, m2s, thr_d, nvalid);
+            if (!valid) acc = 0;
           }
-          if (!valid) acc = 0;
           const unsigned int over = __ballot_sync(0xffffffffu, cnt + __popc(acc) > 32);
 #ifdef MF_TC_PROFILE
           p_filter += clock64() - p_f0;
@@ -1061,12 +1106,15 @@ __global__ void __launch_bounds__((ATM ? kTqThreadsAtm : kTqThreads) + (EW - 1) 
 #pragma unroll 1
         for (int c0 = cbeg; c0 < cend; c0 += 64) {
           TQL(p_tld, tmem_wait_ld(ra));
+          if (tid == 0 && c0 == cbeg) TQT(FLT, g_tc_trace, tt, 5, kTrTiles);
           tmem_ld32_async(tb + c0 + 32, rb);
           chunk(ra, c0);
           TQL(p_tld, tmem_wait_ld(rb));
           if (c0 + 64 < cend) tmem_ld32_async(tb + c0 + 64, ra);
           chunk(rb, c0 + 32);
+          if (tid == 0 && c0 == cbeg) TQT(FLT, g_tc_trace, tt, 6, kTrTiles);
         }
+        if (tid == 0) TQT(FLT, g_tc_trace, tt, 7, kTrTiles);
         tc_fence_before();
         mbar_arrive(&acce[b]);
         if (tid == 0) TQT(FLT, g_tc_trace, tt, 4, kTrTiles);
@@ -1259,13 +1307,23 @@ bool tq_choose(int d, int kcap, TqLayout* out) {
 // The filter scan (fp16, 64 <= d <= 128 with rows of a multiple of 16 bytes):
 // the query tile in tensor memory and the deepest ring of 16 KB row stages
 // that fits. (d >= 64: no tile box wider than the rows.)
+// Build-time caps on the filter scan's ring depth and accumulator buffers
+// (tuning builds; the defaults take what fits).
+#ifndef MF_FLT_MAX_SA
+#define MF_FLT_MAX_SA 8
+#endif
+#ifndef MF_FLT_MAX_NACC
+#define MF_FLT_MAX_NACC kTqMaxAcc
+#endif
+
 bool tq_choose_bf(int d, TqLayout* out) {
   if (d < 64 || d > kTqMaxDAtm || d % 8 != 0) return false;
   // two epilogue warpgroups where their lists and buffers leave room for a
   // ring of at least two stages (g_filter_groups = 1 forces one)
   for (int ew = g_filter_groups; ew >= 1; --ew) {
-    for (int sa = 8; sa >= 2; --sa) {
+    for (int sa = MF_FLT_MAX_SA; sa >= 2; --sa) {
       TqLayout l = tq_layout(d, kTqK, 128, sa, true, true, ew);
+      if (l.nacc > MF_FLT_MAX_NACC) l.nacc = MF_FLT_MAX_NACC;
       if (l.total <= (size_t)kTqMaxSmem) {
         *out = l;
         return true;
