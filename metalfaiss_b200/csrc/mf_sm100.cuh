@@ -74,11 +74,12 @@ __device__ __forceinline__ unsigned long long globaltimer_ns() {
 // Bounded wait: returns false (and records kErrWaitTimeout in *err) if the
 // phase does not complete within the limits above; `abort` (shared by the
 // CTA's roles) is raised then, and a wait that sees it raised by another role
-// returns false at once, so every role leaves its loop.
+// returns false after its first try, so every role leaves its loop.
 template <bool SPIN = false>
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* abort, int* err) {
-  if (*(volatile int*)abort) return false;
+  // the common case first: one try_wait (the abort flag is read only while waiting)
   if (mbar_try_wait<SPIN>(bar, parity)) return true;
+  if (*(volatile int*)abort) return false;
   const unsigned long long t0 = globaltimer_ns();
   for (unsigned i = 0; i < kWaitMaxIters; ++i) {
     if (mbar_try_wait<SPIN>(bar, parity)) return true;

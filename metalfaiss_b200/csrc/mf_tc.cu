@@ -54,6 +54,13 @@ __device__ unsigned long long g_tc_prof[20];
     expr;                              \
     var += clock64() - _t0;            \
   } while (0)
+#else
+#define TQP(i, expr) expr
+#define TQL(var, expr) expr
+#endif
+
+#if defined(MF_TC_PROFILE) || defined(MF_TC_TRACE)
+#define MF_TC_STAMPS 1
 // Per-tile and per-item clock stamps of the filter scan in the first kTrCtas
 // CTAs (instrumented builds only): tiles [MMA accumulator free, MMA stage
 // ready, MMA committed, epilogue got it, epilogue released it, its first
@@ -68,8 +75,6 @@ __device__ long long g_tc_trace_item[kTrCtas][kTrItems][4];
     if ((on) && blockIdx.x < kTrCtas && (idx) < (n)) arr[blockIdx.x][idx][f] = clock64(); \
   } while (0)
 #else
-#define TQP(i, expr) expr
-#define TQL(var, expr) expr
 #define TQT(on, arr, idx, f, n) \
   do {                          \
   } while (0)
@@ -77,6 +82,8 @@ __device__ long long g_tc_trace_item[kTrCtas][kTrItems][4];
 
 using namespace sm100;
 
+// Warps: 0-3 epilogue, 4 producer, 5 MMA, (ATM) 6-9 query tile loader,
+// (EW = 2) the second epilogue warpgroup, (filter scan) the second MMA issuer.
 constexpr int kTqThreads = 192;
 constexpr int kTqM = 128;          // queries per item = TMEM lanes
 constexpr int kTqEpiThreads = 128;
@@ -387,7 +394,8 @@ __device__ __forceinline__ unsigned int tq_accept_acc(const uint32_t (&r)[32], f
 // writes the results. Two warps per SM sub-partition then hide each other's
 // latencies in the per-column filter that bounds this scan.
 template <int METRIC, int BN, bool ATM, bool CONV, bool FLT = false, int KC = kTqK, int EW = 1>
-__global__ void __launch_bounds__((ATM ? kTqThreadsAtm : kTqThreads) + (EW - 1) * kTqEpiThreads, 1)
+__global__ void __launch_bounds__((ATM ? kTqThreadsAtm : kTqThreads) + (EW - 1) * kTqEpiThreads +
+                                      (FLT ? 32 : 0), 1)
     tq_scan_kernel(const ScanArgs a, const __grid_constant__ TqMaps maps, const TqLayout L) {
   static_assert(EW == 1 || (EW == 2 && FLT && ATM && KC == kTqK),
                 "two epilogue warpgroups are built for the filter scan only");
@@ -414,11 +422,16 @@ __global__ void __launch_bounds__((ATM ? kTqThreadsAtm : kTqThreads) + (EW - 1) 
   QSlot* s_q = reinterpret_cast<QSlot*>(wgfree + 1);
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(s_q + kTqQueue);
   int* s_abort = reinterpret_cast<int*>(s_tmem + 1);
-  uint32_t* s_seq = reinterpret_cast<uint32_t*>(s_abort + 1);  // [0] consumed, [1] issued
+  uint32_t* s_seq = reinterpret_cast<uint32_t*>(s_abort + 1);  // [1]: stages issued
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
+  // The filter scan has two MMA issuers (alternate tiles; its one stage per
+  // tile with an even ring keeps every stage's barriers with one issuer, so
+  // each is waited on in phase order); the other variants have one.
+  constexpr bool kTwoIss = FLT;
+  constexpr int kMma2Warp = kTwoIss ? 10 + (EW - 1) * 4 : -1;
   const int SA = L.SA;
   const int KB = L.KB;
   const int k = a.k;
@@ -446,15 +459,15 @@ __global__ void __launch_bounds__((ATM ? kTqThreadsAtm : kTqThreads) + (EW - 1) 
       mbar_init(&accf[i], 1);
       mbar_init(&acce[i], kTqEpiThreads * EW);
     }
-    // readers of each queue slot: the MMA lane and one lane per epilogue
+    // readers of each queue slot: the MMA lane(s) and one lane per epilogue
     // (and loader) warp
     for (int i = 0; i < kTqQueue; ++i) {
       mbar_init(&qfull[i], 1);
-      mbar_init(&qempty[i], (ATM ? 9 : 5) + 4 * (EW - 1));
+      mbar_init(&qempty[i], (ATM ? 9 : 5) + 4 * (EW - 1) + (kTwoIss ? 1 : 0));
     }
     mbar_init(afull, kTqM);
-    mbar_init(afree, 1);
-    mbar_init(mdone, 1);
+    mbar_init(afree, kTwoIss ? 2 : 1);  // one commit from each MMA issuer
+    mbar_init(mdone, kTwoIss ? 2 : 1);
     mbar_init(wgdone, 4);
     mbar_init(wgfree, 4);
     *s_abort = 0;
@@ -552,9 +565,15 @@ __global__ void __launch_bounds__((ATM ? kTqThreadsAtm : kTqThreads) + (EW - 1) 
       }
       s_seq[1] = seq;
     }
-  } else if (warp == 5) {
+  } else if (warp == 5 || warp == kMma2Warp) {
     // ---------------------------------------------------------------- MMA
+    // The filter scan's two issuing threads take alternate tiles. A wait on a
+    // barrier, even one already complete, stalls the issuing thread for about
+    // three MMAs' time while the tensor pipe queues about one, so with one
+    // issuer the pipe sat idle through every tile's two waits; with two, one
+    // issuer's waits overlap the other's MMAs.
     if (lane == 0) {
+      const uint32_t me = warp == 5 ? 0u : 1u;
       constexpr uint32_t idesc = FLT ? idesc_f16(kTqM, BN) : idesc_tf32(kTqM, BN);
       uint32_t seq = 0, tt = 0;
       for (uint32_t qi = 0;; ++qi) {
@@ -577,6 +596,10 @@ __global__ void __launch_bounds__((ATM ? kTqThreadsAtm : kTqThreads) + (EW - 1) 
           tc_fence_after();
         }
         for (int t = 0; t < nT; ++t, ++tt) {
+          if (kTwoIss && (tt & 1u) != me) {  // the other issuer's tile (one stage)
+            ++seq;
+            continue;
+          }
           const int b = tt % NACC;
           if (tt >= (uint32_t)NACC)
             TQP(1, mbar_wait<FLT && kTcSpin>(&acce[b], ((tt / NACC) - 1) & 1, s_abort,
@@ -632,10 +655,10 @@ __global__ void __launch_bounds__((ATM ? kTqThreadsAtm : kTqThreads) + (EW - 1) 
           mma_commit(&accf[b]);
           TQT(FLT, g_tc_trace, tt, 2, kTrTiles);
         }
-        // the query tile may be overwritten once this item's MMAs complete
+        // the query tile may be overwritten once this item's MMAs (both
+        // issuers') complete
         if (ATM) mma_commit(afree);
       }
-      s_seq[0] = seq;
       // lets the teardown free tensor memory only after the last MMA, also when
       // a role gave up early
       mma_commit(mdone);
@@ -1225,8 +1248,11 @@ __global__ void __launch_bounds__((ATM ? kTqThreadsAtm : kTqThreads) + (EW - 1) 
   __syncthreads();
   tc_fence_after();
   if (tid == 4 * 32) {
+    // the last use of each stage: its loads have landed once that phase is
+    // complete (earlier uses were complete before their stage was reissued)
     int dummy = 0;
-    for (uint32_t seq = s_seq[0]; seq < s_seq[1]; ++seq)
+    const uint32_t issued = s_seq[1];
+    for (uint32_t seq = issued > (uint32_t)SA ? issued - SA : 0; seq < issued; ++seq)
       mbar_wait(&full[seq % SA], (seq / SA) & 1, &dummy, &g_device_error);
   }
   __syncthreads();
@@ -1321,7 +1347,8 @@ bool tq_choose_bf(int d, TqLayout* out) {
   // two epilogue warpgroups where their lists and buffers leave room for a
   // ring of at least two stages (g_filter_groups = 1 forces one)
   for (int ew = g_filter_groups; ew >= 1; --ew) {
-    for (int sa = MF_FLT_MAX_SA; sa >= 2; --sa) {
+    // an even ring: stage s then always serves tiles of one MMA issuer
+    for (int sa = MF_FLT_MAX_SA & ~1; sa >= 2; sa -= 2) {
       TqLayout l = tq_layout(d, kTqK, 128, sa, true, true, ew);
       if (l.nacc > MF_FLT_MAX_NACC) l.nacc = MF_FLT_MAX_NACC;
       if (l.total <= (size_t)kTqMaxSmem) {
@@ -1659,13 +1686,14 @@ int launch_tc_filter(const ScanArgs& a, int64_t b_rows, int64_t total_items, int
   long long grid = num_sms(device);
   if (grid > total_items) grid = total_items;
   ScopedTiming tm("scan_topk_ivf_filter", stream);
-  fn<<<(unsigned int)grid, kTqThreadsAtm + (lay.ew - 1) * kTqEpiThreads, lay.total, stream>>>(
+  // + the second MMA issuer's warp
+  fn<<<(unsigned int)grid, kTqThreadsAtm + (lay.ew - 1) * kTqEpiThreads + 32, lay.total, stream>>>(
       a, maps, lay);
   MF_LAUNCH_CHECK();
   return MF_OK;
 }
 
-#ifdef MF_TC_PROFILE
+#ifdef MF_TC_STAMPS
 extern "C" MF_API int mf_tc_trace_read(long long* tiles, long long* items, int reset) {
   MF_CUDA(cudaMemcpyFromSymbol(tiles, g_tc_trace, sizeof(g_tc_trace)));
   MF_CUDA(cudaMemcpyFromSymbol(items, g_tc_trace_item, sizeof(g_tc_trace_item)));
@@ -1678,6 +1706,8 @@ extern "C" MF_API int mf_tc_trace_read(long long* tiles, long long* items, int r
   }
   return MF_OK;
 }
+#endif
+#ifdef MF_TC_PROFILE
 extern "C" MF_API int mf_tc_profile_read(unsigned long long* out16, int reset) {
   MF_CUDA(cudaMemcpyFromSymbol(out16, g_tc_prof, 20 * sizeof(unsigned long long)));
   if (reset) {
