@@ -423,6 +423,27 @@ def run_ivf(args, cfg, rank, world, device):
     names = ["scan_topk_ivf_filter" if filtered else "scan_topk_ivf", "scan_topk_ivf_small",
              "ivf_filter_refine"]
     kt = timer.kernel_times(lambda: search(xq), names, min(args.steps, 20))
+    phases = None
+    if sharded:
+        # per-phase device times of a few more steps (events between the
+        # phases; outside the timed steps), the max over ranks per phase
+        sharded.phase_events = []
+        n_ph = min(args.steps, 10)
+        for _ in range(n_ph):
+            search(xq)
+        torch.cuda.synchronize(device)
+        evs, sharded.phase_events = sharded.phase_events, None
+        per = {}
+        step_len = len(evs) // n_ph
+        for i in range(n_ph):
+            chunk = evs[i * step_len:(i + 1) * step_len]
+            for (_, e0), (name, e1) in zip(chunk[:-1], chunk[1:]):
+                per[name] = per.get(name, 0.0) + e0.elapsed_time(e1) / n_ph
+        import torch.distributed as dist
+        names_ph = list(per)
+        t = torch.tensor([per[n] for n in names_ph], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        phases = {n: round(float(v), 4) for n, v in zip(names_ph, t.tolist())}
     scan_ms, scan_n = kt[names[0]]
     small_ms, small_n = kt["scan_topk_ivf_small"]
     refine_ms, refine_n = kt["ivf_filter_refine"]
@@ -537,6 +558,8 @@ def run_ivf(args, cfg, rank, world, device):
             "clocks": clocks,
             "cpu_baseline": cpu,
         })
+        if phases:
+            line["phases_ms_max_over_ranks"] = phases
         print(json.dumps(line), flush=True)
 
 

@@ -982,7 +982,7 @@ int mf_flat_range_workspace_size(int64_t nq, int64_t nb, int d, size_t* bytes) {
   MF_CHECK(bytes != nullptr, MF_ERR_INVALID_ARGS, "bytes is NULL");
   int dev = 0;
   cudaGetDevice(&dev);
-  FlatPlan p = plan_flat(nq, nb, d, 32, dev);
+  FlatPlan p = plan_flat(nq, nb, d, 32, dev, 32, false);
   Carver c(nullptr, 0);
   c.take<float>(nq);
   c.take<int>(1);
@@ -1002,7 +1002,7 @@ struct FlatRangeWs {
 };
 int carve_flat_range(FlatRangeWs& w, int64_t nq, int64_t nb, int d, int device, void* ws,
                      size_t bytes) {
-  w.p = plan_flat(nq, nb, d, 32, device);
+  w.p = plan_flat(nq, nb, d, 32, device, 32, false);
   Carver c(ws, bytes);
   w.qn = c.take<float>(nq);
   w.counter = c.take<int>(1);

@@ -74,7 +74,9 @@ int mf_flat_search_noalloc(int device, void* stream, const float* xq, int64_t nq
            (long long)nb);
   MF_CHECK(nq < (1ll << 31) / 2, MF_ERR_INVALID_ARGS, "nq too large");
   if (nq == 0) return MF_OK;
-  const size_t need = plan_flat(nq, nb, d, k, device).bytes;
+  // the fused top-k's scratch: the distance-matrix path is taken only when
+  // the scratch also holds the matrix
+  const size_t need = plan_flat(nq, nb, d, k, device).bytes_min;
   MF_CHECK(need <= kNoAllocScratchBytes, MF_ERR_INVALID_ARGS,
            "flat search of nq=%lld nb=%lld d=%d k=%d needs %zu bytes of scratch; the static "
            "scratch holds %zu (split the queries, or call mf_flat_search with a workspace)",

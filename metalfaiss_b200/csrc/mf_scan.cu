@@ -315,6 +315,52 @@ __global__ void __launch_bounds__(256) merge_kernel(const float* __restrict__ pd
   }
 }
 
+// One warp per query over its row of the distance matrix: the k smallest
+// (distance, row) keys, as the fused top-k keeps them.
+template <int KCAP>
+__global__ void __launch_bounds__(256) dmat_select_kernel(const float* __restrict__ dmat, int64_t ld,
+                                                          int64_t nq, int64_t nb, int k,
+                                                          const int64_t* __restrict__ ids,
+                                                          float* D, int64_t* L) {
+  __shared__ unsigned long long lists[8][KCAP];
+  __shared__ unsigned long long bufs[8][32];
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const long long q = (long long)blockIdx.x * 8 + warp;
+  if (q >= nq) return;
+  WarpTopK<KCAP> tk;
+  tk.init(lists[warp], bufs[warp], k, lane);
+  const float* row = dmat + q * ld;
+  // 128 columns per step, four per lane (ld is a multiple of 128, so every
+  // load is in the row); a step offers its keys only when some lane holds a
+  // distance <= the current k-th (a superset of the keys below it)
+  for (long long c0 = 0; c0 < nb; c0 += 128) {
+    const long long c = c0 + 4 * lane;
+    const float4 v = __ldcs(reinterpret_cast<const float4*>(row + c));
+    const float e[4] = {v.x, v.y, v.z, v.w};
+    const float thr_d = tk.thr == kEmptyKey ? __int_as_float(0x7f800000) : key_dist(tk.thr);
+    bool any = false;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) any |= (c + j < nb) && e[j] <= thr_d;
+    if (!__any_sync(0xffffffffu, any)) continue;
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      tk.offer(c + j < nb ? make_key(e[j], (unsigned int)(c + j)) : kEmptyKey, k, lane);
+  }
+  tk.flush(k, lane);
+  for (int t = lane; t < k; t += 32) {
+    const unsigned long long key = tk.list[t];
+    if (key == kEmptyKey) {
+      D[q * k + t] = __int_as_float(0x7f800000);
+      L[q * k + t] = -1;
+    } else {
+      D[q * k + t] = key_dist(key);
+      const unsigned int pos = key_index(key);
+      L[q * k + t] = ids ? ids[pos] : (int64_t)pos;
+    }
+  }
+}
+
 __global__ void map_ids_kernel(const int64_t* __restrict__ ids, int64_t* labels, int64_t n) {
   const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n) return;
@@ -498,6 +544,16 @@ int launch_map_ids(const int64_t* ids, int64_t* labels, int64_t n, cudaStream_t 
   return MF_OK;
 }
 
+int launch_dmat_select(const float* dmat, int64_t ld, int64_t nq, int64_t nb, int k,
+                       const int64_t* ids, float* D, int64_t* I, cudaStream_t stream) {
+  if (nq <= 0) return MF_OK;
+  ScopedTiming tm("dmat_select", stream);
+  dmat_select_kernel<32><<<(unsigned int)ceil_div(nq, 8), 256, 0, stream>>>(dmat, ld, nq, nb, k,
+                                                                            ids, D, I);
+  MF_LAUNCH_CHECK();
+  return MF_OK;
+}
+
 int launch_merge(const float* pd, const int64_t* pl, int64_t nq, int parts, int k_in, int k,
                  float* d, int64_t* l, cudaStream_t stream) {
   if (nq <= 0 || k <= 0) return MF_OK;
@@ -584,7 +640,19 @@ void plan_splits(FlatPlan& p, int64_t nq, int64_t nb, int d, int k, int device, 
 }
 }  // namespace
 
-FlatPlan plan_flat(int64_t nq, int64_t nb, int d, int k, int device, int tq) {
+int64_t flat_dmat_ld(int64_t nq, int64_t nb, int k) {
+  // Few query tiles per SM: the fused top-k's pieces each start their lists
+  // empty, a cost that does not shrink with the queries (at the coarse step
+  // over 16384 centroids, k = 32: 0.24 ms for 1,250 queries and 0.47 ms for
+  // 10,000 fused, against 0.59 ms for 10,000 through the matrix).
+  if (k < 8 || k > 32 || nq < 2 * (int64_t)tc_group() || nq > 64 * (int64_t)tc_group() ||
+      nb <= 0 || nb > (1ll << 24))
+    return 0;
+  const int64_t ld = (nb + 127) / 128 * 128;
+  return nq * ld * 4 <= (2ll << 30) ? ld : 0;
+}
+
+FlatPlan plan_flat(int64_t nq, int64_t nb, int d, int k, int device, int tq, bool dmat) {
   const int kcap = scan_kcap(k) ? scan_kcap(k) : 256;
   FlatPlan simt, tc;
   plan_splits(simt, nq, nb, d, k, device, 32, kcap >= 256 ? 1 : (kcap >= 128 ? 2 : 3));
@@ -599,6 +667,9 @@ FlatPlan plan_flat(int64_t nq, int64_t nb, int d, int k, int device, int tq) {
   c.take<int64_t>((size_t)nq * max_splits * k);
   c.take<float>((size_t)nq * d);            // query tf32 residuals (tensor cores)
   c.take<unsigned int>(nq);                 // pieces' shared k-th distances (tensor cores)
+  p.bytes_min = c.used;
+  p.dmat_ld = dmat ? flat_dmat_ld(nq, nb, k) : 0;
+  if (p.dmat_ld > 0) c.take<float>((size_t)nq * p.dmat_ld);  // the distance matrix
   p.bytes = c.used;
   return p;
 }
@@ -609,12 +680,15 @@ int run_flat_topk(int device, cudaStream_t stream, const float* xq, int64_t nq, 
                   const float* bound) {
   const bool tc = tc_eligible(metric, d, k, nb) && (xb_lo != nullptr || tc_raw_queries(d, k));
   const FlatPlan p = plan_flat(nq, nb, d, k, device, tc ? tc_group() : 32);
-  MF_CHECK(ws_bytes >= p.bytes, MF_ERR_INVALID_ARGS,
-           "flat search workspace too small: %zu < %zu bytes", ws_bytes, p.bytes);
+  MF_CHECK(ws_bytes >= p.bytes_min, MF_ERR_INVALID_ARGS,
+           "flat search workspace too small: %zu < %zu bytes", ws_bytes, p.bytes_min);
   // carve with the same order as plan_flat (partials sized for either engine)
   FlatPlan other = plan_flat(nq, nb, d, k, device, tc ? 32 : tc_group());
   const int max_splits = p.splits > other.splits ? p.splits : other.splits;
   MF_CHECK(other.bytes == p.bytes, MF_ERR_ASSERTION, "flat plan sizes disagree");
+  // the distance-matrix path: tensor cores, no bound, a workspace that holds it
+  const bool dm = tc && bound == nullptr && p.dmat_ld > 0 && ws_bytes >= p.bytes &&
+                  (metric == MF_METRIC_L2 || metric == MF_METRIC_INNER_PRODUCT);
   Carver c(ws, ws_bytes);
   float* qn = c.take<float>(nq);
   int* counter = c.take<int>(1);
@@ -622,6 +696,7 @@ int run_flat_topk(int device, cudaStream_t stream, const float* xq, int64_t nq, 
   int64_t* pl = c.take<int64_t>((size_t)nq * max_splits * k);
   float* q_lo = c.take<float>((size_t)nq * d);
   unsigned int* share = c.take<unsigned int>(nq);
+  float* dmat = dm ? c.take<float>((size_t)nq * p.dmat_ld) : nullptr;
   if (metric == MF_METRIC_L2) MF_TRY(launch_norms(xq, nq, d, qn, stream));
   ScanArgs a{};
   a.xq = xq;
@@ -644,6 +719,21 @@ int run_flat_topk(int device, cudaStream_t stream, const float* xq, int64_t nq, 
   a.direct = p.splits > 1 ? 0 : 1;
   a.out_d = p.splits > 1 ? pd : D;
   a.out_l = p.splits > 1 ? pl : I;
+  if (dm) {
+    // every (query tile x row tile) once, distances to the matrix, then the
+    // per-query selection (ties to the lower row, as the fused top-k)
+    const bool raw = tc_raw_queries(d, k);
+    if (!raw) MF_TRY(launch_tf32_residual(xq, nq, d, q_lo, stream));
+    a.dmat = dmat;
+    a.dmat_ld = p.dmat_ld;
+    a.ids = nullptr;
+    a.direct = 1;
+    a.out_d = nullptr;
+    a.out_l = nullptr;
+    MF_TRY(launch_tc_scan(a, metric, raw ? nullptr : q_lo, nq, xb_lo, nb, p.chunks, device,
+                          stream));
+    return launch_dmat_select(dmat, p.dmat_ld, nq, nb, k, ids, D, I, stream);
+  }
   if (tc) {
     const bool raw = tc_raw_queries(d, k);  // else the scan streams (xq, q_lo) tiles
     if (!raw) MF_TRY(launch_tf32_residual(xq, nq, d, q_lo, stream));

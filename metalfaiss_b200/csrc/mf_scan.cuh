@@ -89,6 +89,11 @@ struct ScanArgs {
   const float* pair_ae;
   // few-query scan with pair_cnt set: compact outputs at this slot stride
   int out_stride;
+  // flat tensor-core scan writing distances instead of a top-k: row q of the
+  // (nq, dmat_ld) matrix gets the distance to every database row (IP: the
+  // negated inner product, the top-k's key order), dmat_ld a multiple of 128
+  float* dmat;
+  int64_t dmat_ld;
   // range search
   float radius;
   int64_t* counts;        // count pass: (nq*P)
@@ -156,7 +161,9 @@ struct FlatPlan {
   int nqt;
   int splits;
   int64_t rows_per_split;
-  size_t bytes;
+  size_t bytes;      // workspace for either path (what the size queries report)
+  size_t bytes_min;  // without the distance matrix (the fused top-k only)
+  int64_t dmat_ld;   // > 0: the distance-matrix path is planned (row stride)
   // tensor cores: the (query tile x 128-row tile) space is cut into `chunks`
   // equal runs of chunk_tiles tiles, one per CTA (0 = items of whole splits)
   int64_t chunk_tiles = 0;
@@ -165,7 +172,20 @@ struct FlatPlan {
 };
 // tq = queries per item (32 for the SIMT scan, tc_group() for tensor cores);
 // bytes covers both engines.
-FlatPlan plan_flat(int64_t nq, int64_t nb, int d, int k, int device, int tq = 32);
+// dmat: plan the distance-matrix path where it applies (flat_dmat_ld).
+FlatPlan plan_flat(int64_t nq, int64_t nb, int d, int k, int device, int tq = 32,
+                   bool dmat = true);
+// Row stride of the flat search's distance-matrix path (the tensor-core scan
+// writes every query's distances, then one warp per query selects its top-k),
+// or 0 where the fused top-k is used: k in [8, 32], 2 to 64 query tiles, and
+// a matrix of at most 2 GB. With few query tiles per SM the fused scan cuts
+// every tile into pieces whose top-k lists each start empty, and those
+// merges (the coarse quantizer of a sharded index: k = nprobe over thousands
+// of centroids for a rank's share of the queries) cost more than writing and
+// reading the matrix.
+int64_t flat_dmat_ld(int64_t nq, int64_t nb, int k);
+int launch_dmat_select(const float* dmat, int64_t ld, int64_t nq, int64_t nb, int k,
+                       const int64_t* ids, float* D, int64_t* I, cudaStream_t stream);
 
 // Runs flat top-k into (nq, k) outputs using the given workspace. With xb_lo
 // (the tf32 residual of xb) the tensor-core engine runs where eligible.

@@ -1050,6 +1050,26 @@ __global__ void __launch_bounds__((ATM ? kTqThreadsAtm : kTqThreads) + (EW - 1) 
         // One 32-column chunk: filter, merge rows that would overflow, append.
         auto chunk = [&](uint32_t (&r)[32], int c0) {
           const long long rc = r0 + c0;
+          if constexpr (!FLT) {
+            if (a.dmat) {
+              // the distance-matrix path: this row's 32 distances, stored as
+              // the top-k would key them (rows past the bank: padding columns)
+              if (valid) {
+                float4* dst = reinterpret_cast<float4*>(a.dmat + (long long)q * a.dmat_ld + rc);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                  float v[4];
+#pragma unroll
+                  for (int j = 0; j < 4; ++j) {
+                    const float x = __uint_as_float(r[4 * i + j]);
+                    v[j] = METRIC == MF_METRIC_L2 ? l2_from_dot(qn, xs[c0 + 4 * i + j], x) : -x;
+                  }
+                  __stcs(dst + i, make_float4(v[0], v[1], v[2], v[3]));
+                }
+              }
+              return;
+            }
+          }
           const long long left = it.re - rc;
           const int nvalid = left >= 32 ? 32 : (left > 0 ? (int)left : 0);
           const float thr_d = thr == kEmptyKey ? __int_as_float(0x7f800000) : key_dist(thr);
@@ -1199,7 +1219,7 @@ __global__ void __launch_bounds__((ATM ? kTqThreadsAtm : kTqThreads) + (EW - 1) 
       }
       // the warp's 32 rows x k results, one per lane per step: the k steps are
       // independent, so their id lookups overlap
-      for (int e = lane; e < (FLT ? 0 : 32 * k); e += 32) {
+      for (int e = lane; e < ((FLT || a.dmat) ? 0 : 32 * k); e += 32) {
         const int qq = e / k;
         const int kk = e - qq * k;
         const long long sq = __shfl_sync(0xffffffffu, slot, qq);

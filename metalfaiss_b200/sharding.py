@@ -197,6 +197,8 @@ class ShardedIVF:
         else:
             self.local = index
         self.owners = np.asarray(owners)
+        # a list here collects (phase, CUDA event) pairs of each search
+        self.phase_events = None
 
     @property
     def nprobe(self):
@@ -206,6 +208,13 @@ class ShardedIVF:
     def nprobe(self, v):
         self.local.nprobe = v
 
+    def _mark(self, name):
+        # phase boundaries on the current stream, when a caller asked for them
+        if self.phase_events is not None:
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record()
+            self.phase_events.append((name, ev))
+
     def search(self, xq, k: int) -> SearchResult:
         idx = self.local
         xq = idx._prepare_query(xq)
@@ -213,20 +222,29 @@ class ShardedIVF:
         nq = xq.shape[0]
         idx._check_k(k)
         P = min(idx.nprobe, idx.nlist)
+        self._mark("start")
         # 1. coarse step over this rank's share of the queries
         b, e = row_shard(nq, self.rank, self.world)
         if e > b:
             mine = idx.quantizer._search_padded(xq[b:e], P, map_ids=False).labels
         else:
             mine = torch.empty((0, P), dtype=torch.int64, device=idx.device)
+        self._mark("coarse")
         probes = gather_rows(mine, nq, self.group).contiguous()
+        self._mark("gather probes")
         # 2. bounds from the ranks that hold each query's nearest list
         bound = idx._probe_bound(xq, probes, k)
+        self._mark("bound pass")
         dist.all_reduce(bound, op=dist.ReduceOp.MIN, group=self.group)
+        self._mark("reduce bounds")
         # 3. this rank's lists, within the bound; then gather and merge
         local = idx._search_bounded(xq, k, probes, bound)
+        self._mark("list scan")
         pd, pi = gather_partials(local.distances, local.labels, self.group)
-        return merge_partials(pd, pi, k)
+        self._mark("gather partials")
+        out = merge_partials(pd, pi, k)
+        self._mark("merge")
+        return out
 
 
 class ShardedFlat:

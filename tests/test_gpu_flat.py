@@ -94,6 +94,37 @@ def test_flat_split_major_database(cuda_device, metric, k):
     assert list(I[:2, 0]) == [ids[7], ids[79_999]]
 
 
+@pytest.mark.parametrize("metric", [MetricType.L2, MetricType.INNER_PRODUCT])
+@pytest.mark.parametrize("k", [8, 32])
+def test_flat_distance_matrix_path_matches_fused(cuda_device, metric, k):
+    """k in [8, 32] over 2 to 64 query tiles takes the distance-matrix path
+    (every distance written, then one warp per query selects) when the
+    workspace holds the matrix; one byte less keeps the fused top-k. The two
+    give identical distances and labels, and both match the oracle."""
+    from metalfaiss_b200 import _native as nat
+    from metalfaiss_b200._tensors import as_matrix
+
+    xb = syn.gaussian(9000, 64, seed=41)
+    xq = syn.gaussian(700, 64, seed=42)
+    ids = np.arange(9000, dtype=np.int64) * 3 + 1
+    idx = FlatIndex(64, metric)
+    idx.add(xb, ids)
+    D, I = _check(idx, xq, xb, k, metric, ids)  # full workspace: the matrix path
+    q = as_matrix(xq, 64, idx.device, "queries")
+    need = nat.workspace_size("mf_flat_search_workspace_size", len(xq), idx.ntotal, idx._dp,
+                              int(metric), k)
+    ws = torch.empty(need, dtype=torch.uint8, device=idx.device)
+    D2 = torch.empty((len(xq), k), dtype=torch.float32, device=idx.device)
+    I2 = torch.empty((len(xq), k), dtype=torch.int64, device=idx.device)
+    nat.call("mf_flat_search", idx.device.index, nat.stream_of(idx.device), nat.ptr(q), len(xq),
+             nat.ptr(idx._xb.buf), nat.ptr(idx._norms.buf),
+             nat.ptr(idx._lo.buf if idx._lo is not None else None), idx.ntotal, idx._dp,
+             int(metric), k, nat.ptr(idx._ids.buf), nat.ptr(D2), nat.ptr(I2), nat.ptr(ws),
+             need - 1)  # one byte short of the matrix: the fused top-k
+    np.testing.assert_array_equal(D2.cpu().numpy(), D)
+    np.testing.assert_array_equal(I2.cpu().numpy(), I)
+
+
 def test_flat_ids_64bit_self_query(cuda_device):
     """python/metalfaiss/unittest/test_mlx_index.py:231-240: self-query returns the own 64-bit id."""
     xb = syn.gaussian(1000, 64, seed=11)
