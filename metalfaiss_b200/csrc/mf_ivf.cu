@@ -10,6 +10,10 @@ namespace mf {
 namespace {
 
 constexpr int kScanBlock = 1024;
+// List tables of up to this many blocks of kScanBlock lists are planned by
+// one block (two scans over the table); longer ones by one block per
+// kScanBlock lists in two launches.
+constexpr int kPlanOneBlock = 2;
 
 // Block-wide exclusive scan (all kScanBlock threads call it). Returns the
 // exclusive prefix of v and writes the block total to `total`.
@@ -155,6 +159,77 @@ __global__ void __launch_bounds__(kScanBlock) ivf_plan_kernel(const int* __restr
   if (t == 0) {
     *item_total = run;
     if (item_total2) *item_total2 = run2;
+  }
+}
+
+// The same plan over many blocks (one list per thread, kScanBlock lists per
+// block), for long list tables: ivf_plan_sums_kernel writes each block's
+// three totals (pairs in list-id order; tensor-core groups and few-query
+// items in list order), then ivf_plan_write_kernel adds the totals of the
+// blocks before its own to its block scans. Same output as ivf_plan_kernel.
+__device__ __forceinline__ void plan_terms(const int* __restrict__ counts, int nlist,
+                                           const int32_t* __restrict__ order, int i, int group,
+                                           int small_max, int& cpair, int& lv, int& c, int& ng,
+                                           bool& small_list) {
+  cpair = i < nlist ? counts[i] : 0;
+  lv = i < nlist ? (order ? order[i] : i) : -1;
+  c = lv >= 0 ? counts[lv] : 0;
+  ng = (c + group - 1) / group;
+  small_list = small_max > 0 && c > 0 && c <= small_max;
+}
+
+__global__ void __launch_bounds__(kScanBlock) ivf_plan_sums_kernel(
+    const int* __restrict__ counts, int nlist, const int32_t* __restrict__ order, int group,
+    int small_max, int3* block_sums) {
+  __shared__ int sums[32];
+  const int i = blockIdx.x * kScanBlock + threadIdx.x;
+  int cpair, lv, c, ng;
+  bool small_list;
+  plan_terms(counts, nlist, order, i, group, small_max, cpair, lv, c, ng, small_list);
+  int t0, t1, t2;
+  block_exclusive_scan<int>(cpair, sums, t0);
+  block_exclusive_scan<int>(small_list ? 0 : ng, sums, t1);
+  block_exclusive_scan<int>(small_list ? 1 : 0, sums, t2);
+  if (threadIdx.x == 0) block_sums[blockIdx.x] = make_int3(t0, t1, t2);
+}
+
+__global__ void __launch_bounds__(kScanBlock) ivf_plan_write_kernel(
+    const int* __restrict__ counts, int nlist, const int32_t* __restrict__ order,
+    const int3* __restrict__ block_sums, int* pair_offsets, int2* items, int* item_total,
+    int* cursors, int group, int2* items2, int* item_total2, int small_max) {
+  __shared__ int sums[32];
+  __shared__ int3 base;
+  if (threadIdx.x == 0) {
+    int3 b = make_int3(0, 0, 0);
+    for (int j = 0; j < (int)blockIdx.x; ++j) {
+      const int3 v = block_sums[j];
+      b.x += v.x;
+      b.y += v.y;
+      b.z += v.z;
+    }
+    base = b;
+  }
+  __syncthreads();
+  const int i = blockIdx.x * kScanBlock + threadIdx.x;
+  int cpair, lv, c, ng;
+  bool small_list;
+  plan_terms(counts, nlist, order, i, group, small_max, cpair, lv, c, ng, small_list);
+  int t0, t1, t2;
+  const int e0 = block_exclusive_scan<int>(cpair, sums, t0);
+  const int ea = block_exclusive_scan<int>(small_list ? 0 : ng, sums, t1);
+  const int eb = block_exclusive_scan<int>(small_list ? 1 : 0, sums, t2);
+  if (i < nlist) {
+    pair_offsets[i] = base.x + e0;
+    cursors[i] = 0;
+    if (small_list)
+      items2[base.z + eb] = make_int2(lv, 0);
+    else
+      for (int g = 0; g < ng; ++g) items[base.y + ea + g] = make_int2(lv, g);
+  }
+  if (blockIdx.x == gridDim.x - 1 && threadIdx.x == 0) {
+    pair_offsets[nlist] = base.x + t0;
+    *item_total = base.y + t1;
+    if (item_total2) *item_total2 = base.z + t2;
   }
 }
 
@@ -392,6 +467,7 @@ IvfGroups carve_ivf_groups(Carver& c, int64_t nq, int nlist, int P) {
   g.items2 = c.take<int2>((size_t)nq * P);
   g.item_total2 = c.take<int>(1);
   g.counter = c.take<int>(1);
+  g.plan_sums = c.take<int3>((size_t)ceil_div(nlist, kScanBlock));
   return g;
 }
 
@@ -408,10 +484,21 @@ int run_ivf_groups_ex(const IvfGroups& g, const int64_t* probes, int64_t nq, int
         probes, n, nlist, list_offsets, g.counts, pd, pl, k, pair_counts, P, s0, s1);
     MF_LAUNCH_CHECK();
   }
-  ivf_plan_kernel<<<1, kScanBlock, 0, stream>>>(g.counts, nlist, list_order, g.pair_offsets,
-                                                g.items, g.item_total, g.cursors, group, g.items2,
-                                                g.item_total2, small_max);
-  MF_LAUNCH_CHECK();
+  const int plan_blocks = (int)ceil_div(nlist, kScanBlock);
+  if (plan_blocks <= kPlanOneBlock) {
+    ivf_plan_kernel<<<1, kScanBlock, 0, stream>>>(g.counts, nlist, list_order, g.pair_offsets,
+                                                  g.items, g.item_total, g.cursors, group,
+                                                  g.items2, g.item_total2, small_max);
+    MF_LAUNCH_CHECK();
+  } else {
+    ivf_plan_sums_kernel<<<plan_blocks, kScanBlock, 0, stream>>>(g.counts, nlist, list_order,
+                                                                 group, small_max, g.plan_sums);
+    MF_LAUNCH_CHECK();
+    ivf_plan_write_kernel<<<plan_blocks, kScanBlock, 0, stream>>>(
+        g.counts, nlist, list_order, g.plan_sums, g.pair_offsets, g.items, g.item_total,
+        g.cursors, group, g.items2, g.item_total2, small_max);
+    MF_LAUNCH_CHECK();
+  }
   if (n > 0) {
     ivf_scatter_kernel<<<(unsigned int)ceil_div(n, 256), 256, 0, stream>>>(
         probes, n, nlist, list_offsets, g.pair_offsets, g.cursors, g.pairs, P, s0, s1);

@@ -207,6 +207,7 @@ struct IvfGroups {
   int2* items2;       // groups of few queries, when split off (nq*P upper bound)
   int* item_total2;   // 1
   int* counter;       // 1
+  int3* plan_sums;    // ceil(nlist / 1024): the multi-block plan's block totals
 };
 size_t ivf_groups_bytes(int64_t nq, int nlist, int P);
 IvfGroups carve_ivf_groups(Carver& c, int64_t nq, int nlist, int P);

@@ -1050,26 +1050,6 @@ __global__ void __launch_bounds__((ATM ? kTqThreadsAtm : kTqThreads) + (EW - 1) 
         // One 32-column chunk: filter, merge rows that would overflow, append.
         auto chunk = [&](uint32_t (&r)[32], int c0) {
           const long long rc = r0 + c0;
-          if constexpr (!FLT) {
-            if (a.dmat) {
-              // the distance-matrix path: this row's 32 distances, stored as
-              // the top-k would key them (rows past the bank: padding columns)
-              if (valid) {
-                float4* dst = reinterpret_cast<float4*>(a.dmat + (long long)q * a.dmat_ld + rc);
-#pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                  float v[4];
-#pragma unroll
-                  for (int j = 0; j < 4; ++j) {
-                    const float x = __uint_as_float(r[4 * i + j]);
-                    v[j] = METRIC == MF_METRIC_L2 ? l2_from_dot(qn, xs[c0 + 4 * i + j], x) : -x;
-                  }
-                  __stcs(dst + i, make_float4(v[0], v[1], v[2], v[3]));
-                }
-              }
-              return;
-            }
-          }
           const long long left = it.re - rc;
           const int nvalid = left >= 32 ? 32 : (left > 0 ? (int)left : 0);
           const float thr_d = thr == kEmptyKey ? __int_as_float(0x7f800000) : key_dist(thr);
@@ -1142,8 +1122,38 @@ __global__ void __launch_bounds__((ATM ? kTqThreadsAtm : kTqThreads) + (EW - 1) 
           p_append += clock64() - p_a0;
 #endif
         };
-        // TMEM loads are double-buffered: chunk c+1 loads while c is filtered.
         const uint32_t tb = tmem + ((uint32_t)(eq * 32) << 16) + L.acc0 + b * BN;
+        if constexpr (!FLT) {
+          if (a.dmat) {
+            // the distance-matrix path: this row's distances of the tile,
+            // stored as the top-k would key them (rows past the bank land in
+            // padding columns), then the accumulator is free
+#pragma unroll 1
+            for (int c0 = cbeg; c0 < cend; c0 += 32) {
+              uint32_t r[32];
+              tmem_ld32_async(tb + c0, r);
+              tmem_wait_ld(r);
+              if (valid) {
+                float4* dst =
+                    reinterpret_cast<float4*>(a.dmat + (long long)q * a.dmat_ld + r0 + c0);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                  float v[4];
+#pragma unroll
+                  for (int j = 0; j < 4; ++j) {
+                    const float x = __uint_as_float(r[4 * i + j]);
+                    v[j] = METRIC == MF_METRIC_L2 ? l2_from_dot(qn, xs[c0 + 4 * i + j], x) : -x;
+                  }
+                  __stcs(dst + i, make_float4(v[0], v[1], v[2], v[3]));
+                }
+              }
+            }
+            tc_fence_before();
+            mbar_arrive(&acce[b]);
+            continue;
+          }
+        }
+        // TMEM loads are double-buffered: chunk c+1 loads while c is filtered.
         uint32_t ra[32], rb[32];
         tmem_ld32_async(tb + cbeg, ra);
 #pragma unroll 1

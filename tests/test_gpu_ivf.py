@@ -67,6 +67,22 @@ def test_ivf_many_queries_and_big_lists(cuda_device):
     _check_ivf(idx, xq, x, cents, lists, 6, 20, MetricType.L2)
 
 
+@pytest.mark.parametrize("filter_search", [True, False])
+def test_ivf_long_list_table(cuda_device, filter_search):
+    """3,000 lists (past two blocks of the grouping plan: its multi-block
+    form), many of them empty, against the oracle on the index's own lists."""
+    x, cen, _ = syn.mixture(60_000, 64, 3000, seed=71)
+    cents = np.concatenate([x[:: 60_000 // 2000][:2000], cen[:1000] + 50.0])  # 1,000 far, empty
+    idx = IVFFlatIndex(64, 3000)
+    idx.set_centroids(cents)
+    idx.add(x)
+    idx.filter_search = filter_search
+    xq, _, _ = syn.mixture(900, 64, 3000, seed=72, centres=cen)
+    sizes = np.diff(idx._offsets.cpu().numpy())
+    assert (sizes == 0).sum() >= 1000
+    _check_ivf(idx, xq, x, cents, gpu_lists(idx), 12, 10, MetricType.L2)
+
+
 def test_ivf_nprobe_all_equals_flat(cuda_device):
     idx, x, cents, lists, cen = _ivf_pair(16, 3000, 12, seed=9)
     xq = syn.gaussian(30, 16, seed=10)
