@@ -73,6 +73,10 @@ CONFIGS = {
     "flat32k": dict(kind="flat", metric=1, d=64, n=32768, nq=16, k=10, data="gaussian"),
     # k-means assignment + update, 5M x d=256, K=4096 (20 iterations).
     "kmeans5m": dict(kind="kmeans", d=256, n=5_000_000, K=4096, niter=20),
+    # Small cases of the two GEMM-shaped configurations, for multi-pass
+    # profiler captures (a few GB on the device, inputs still past L2).
+    "flat1m": dict(kind="flat", metric=0, d=128, n=1_000_000, nq=10_000, k=100, data="unit"),
+    "kmeans500k": dict(kind="kmeans", d=256, n=500_000, K=4096, niter=20),
 }
 METRIC_NAMES = {0: "INNER_PRODUCT", 1: "L2"}
 
