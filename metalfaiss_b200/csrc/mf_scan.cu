@@ -331,21 +331,32 @@ __global__ void __launch_bounds__(256) dmat_select_kernel(const float* __restric
   WarpTopK<KCAP> tk;
   tk.init(lists[warp], bufs[warp], k, lane);
   const float* row = dmat + q * ld;
-  // 128 columns per step, four per lane (ld is a multiple of 128, so every
-  // load is in the row); a step offers its keys only when some lane holds a
+  // 128 columns per step, four per lane (ld is a multiple of 128, so a step
+  // that starts below nb stays in the row), four steps loaded at once so
+  // their reads overlap; a step offers its keys only when some lane holds a
   // distance <= the current k-th (a superset of the keys below it)
-  for (long long c0 = 0; c0 < nb; c0 += 128) {
-    const long long c = c0 + 4 * lane;
-    const float4 v = __ldcs(reinterpret_cast<const float4*>(row + c));
-    const float e[4] = {v.x, v.y, v.z, v.w};
-    const float thr_d = tk.thr == kEmptyKey ? __int_as_float(0x7f800000) : key_dist(tk.thr);
-    bool any = false;
+  constexpr int kSteps = 4;
+  for (long long c0 = 0; c0 < nb; c0 += 128 * kSteps) {
+    float4 v[kSteps];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) any |= (c + j < nb) && e[j] <= thr_d;
-    if (!__any_sync(0xffffffffu, any)) continue;
+    for (int u = 0; u < kSteps; ++u) {
+      const long long cu = c0 + 128 * u;  // warp-uniform
+      v[u] = cu < nb ? __ldcs(reinterpret_cast<const float4*>(row + cu + 4 * lane))
+                     : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
 #pragma unroll
-    for (int j = 0; j < 4; ++j)
-      tk.offer(c + j < nb ? make_key(e[j], (unsigned int)(c + j)) : kEmptyKey, k, lane);
+    for (int u = 0; u < kSteps; ++u) {
+      const long long c = c0 + 128 * u + 4 * lane;
+      const float e[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+      const float thr_d = tk.thr == kEmptyKey ? __int_as_float(0x7f800000) : key_dist(tk.thr);
+      bool any = false;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) any |= (c + j < nb) && e[j] <= thr_d;
+      if (!__any_sync(0xffffffffu, any)) continue;
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        tk.offer(c + j < nb ? make_key(e[j], (unsigned int)(c + j)) : kEmptyKey, k, lane);
+    }
   }
   tk.flush(k, lane);
   for (int t = lane; t < k; t += 32) {
@@ -640,12 +651,18 @@ void plan_splits(FlatPlan& p, int64_t nq, int64_t nb, int d, int k, int device, 
 }
 }  // namespace
 
+#ifndef MF_DMAT_MAX_QT
+#define MF_DMAT_MAX_QT 64
+#endif
+// The most query tiles the distance-matrix path takes (a tuning build may change it).
+constexpr int64_t kDmatMaxQt = MF_DMAT_MAX_QT;
+
 int64_t flat_dmat_ld(int64_t nq, int64_t nb, int k) {
   // Few query tiles per SM: the fused top-k's pieces each start their lists
   // empty, a cost that does not shrink with the queries (at the coarse step
   // over 16384 centroids, k = 32: 0.24 ms for 1,250 queries and 0.47 ms for
   // 10,000 fused, against 0.59 ms for 10,000 through the matrix).
-  if (k < 8 || k > 32 || nq < 2 * (int64_t)tc_group() || nq > 64 * (int64_t)tc_group() ||
+  if (k < 8 || k > 32 || nq < 2 * (int64_t)tc_group() || nq > kDmatMaxQt * (int64_t)tc_group() ||
       nb <= 0 || nb > (1ll << 24))
     return 0;
   const int64_t ld = (nb + 127) / 128 * 128;
