@@ -94,9 +94,9 @@ def test_flat_split_major_database(cuda_device, metric, k):
     assert list(I[:2, 0]) == [ids[7], ids[79_999]]
 
 
-@pytest.mark.parametrize("metric", [MetricType.L2, MetricType.INNER_PRODUCT])
-@pytest.mark.parametrize("k", [8, 32])
-def test_flat_distance_matrix_path_matches_fused(cuda_device, metric, k):
+@pytest.mark.parametrize("metric,k,nq", [(MetricType.L2, 8, 700), (MetricType.INNER_PRODUCT, 32, 700),
+                                         (MetricType.L2, 32, 4500), (MetricType.INNER_PRODUCT, 8, 4500)])
+def test_flat_distance_matrix_path_matches_fused(cuda_device, metric, k, nq):
     """k in [8, 32] over 2 to 64 query tiles takes the distance-matrix path
     (every distance written, then one warp per query selects) when the
     workspace holds the matrix; one byte less keeps the fused top-k. The two
@@ -105,7 +105,7 @@ def test_flat_distance_matrix_path_matches_fused(cuda_device, metric, k):
     from metalfaiss_b200._tensors import as_matrix
 
     xb = syn.gaussian(9000, 64, seed=41)
-    xq = syn.gaussian(700, 64, seed=42)
+    xq = syn.gaussian(nq, 64, seed=42)
     ids = np.arange(9000, dtype=np.int64) * 3 + 1
     idx = FlatIndex(64, metric)
     idx.add(xb, ids)
