@@ -4,7 +4,7 @@ This package restates, in numpy (and plain C under oracle/c/), the reference
 MetalFaiss algorithm for flat kNN, IVFFlat search, k-means and range search,
 each function citing the reference file:line it follows. Only tests/,
 __graft_entry__.smoke() and bench.py's CPU-baseline leg import it, and only as
-the checker or the timed CPU baseline: the product path (metalfaiss_b200) never
+the parity reference of the tests or the timed CPU baseline: the product path (metalfaiss_b200) never
 imports, links or calls anything here.
 
 Pinning: the reference is Python on Apple MLX and cannot run here (no MLX, no

@@ -12,8 +12,7 @@ from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
 OUT = HERE.parent / "_ref"
-# The reference checkout: METALFAISS_REFERENCE, else where this build's
-# container mounts it.
+# The reference checkout: METALFAISS_REFERENCE, else its default location.
 REF_ROOT = Path(os.environ.get("METALFAISS_REFERENCE", "/root/reference"))
 REF_FILE = REF_ROOT / "python/metalfaiss/faissmlx/kernels/ivf_kernels.py"
 LIB = OUT / "libivf_kernels_ref.so"

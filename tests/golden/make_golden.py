@@ -33,8 +33,7 @@ import numpy as np
 
 HERE = Path(__file__).resolve().parent
 ROOT = HERE.parents[1]
-# The reference checkout: METALFAISS_REFERENCE, else where this build's
-# container mounts it.
+# The reference checkout: METALFAISS_REFERENCE, else its default location.
 REF = Path(os.environ.get("METALFAISS_REFERENCE", "/root/reference")) / "python/metalfaiss"
 sys.path.insert(0, str(ROOT))
 sys.path.insert(0, str(HERE))
