@@ -20,10 +20,11 @@ Workloads (--config; the default is the headline):
 
 N>1 GPUs (one process per GPU, NCCL; ivf configurations): the inverted lists
 are partitioned over the ranks by greedy LPT on list size and each rank adds
-only the rows of its own lists; each rank runs the coarse step for its share
-of the queries and the probes are all-gathered, a MIN all-reduce shares each
-query's bound, every rank scans its own lists, and the (Q, k) partial results
-are merged after an all-gather. The database is fixed as N grows (strong
+only the rows of its own lists, plus a copy of every list's first 128 rows
+(the head bank); each rank runs the coarse step and the bound pass (on the
+head bank) for its share of the queries, one all-gather shares the probes and
+bounds, every rank scans its own lists, and the (Q, k) partial results are
+merged after a second all-gather. The database is fixed as N grows (strong
 scaling).
 
 --impl reference times the reference algorithm on the host cores and never
@@ -324,11 +325,64 @@ class Timer:
         return {n: nat.timing_read(n) for n in names}
 
 
+def end_to_end(timer, search, xq, k, device, steps):
+    """The search end to end through the public API, over `steps` batches of
+    the queries from pinned host memory, every batch copied in, searched and
+    its (distances, labels) copied back to pinned host memory inside the
+    timed region. Returns the total ms of
+    * the pipelined run (metalfaiss_b200.pipeline.search_host_batches: batch
+      i + 1's copy in and batch i - 1's copy out overlap batch i's search), and
+    * the serial run (copy in, search, copy out, one stream),
+    each the max over ranks. The pipelined results are checked against the
+    device search."""
+    from metalfaiss_b200.pipeline import search_host_batches
+
+    nq = xq.shape[0]
+    xq_host = xq.cpu().pin_memory()
+    outs = [(torch.empty((nq, k), dtype=torch.float32).pin_memory(),
+             torch.empty((nq, k), dtype=torch.int64).pin_memory()) for _ in range(2)]
+
+    def serial_step():
+        r = search(xq_host.to(device, non_blocking=True))
+        outs[0][0].copy_(r.distances, non_blocking=True)
+        outs[0][1].copy_(r.labels, non_blocking=True)
+
+    serial_ms, _, _ = timer.run(serial_step, steps, 2)
+    for D_h, I_h in outs:
+        D_h.fill_(-1.0)
+        I_h.fill_(-2)
+    batches = [xq_host] * steps
+    batch_outs = [outs[i % 2] for i in range(steps)]
+    pipe_ms, _, _ = timer.run(lambda: search_host_batches(search, batches, batch_outs, device),
+                              1, 1)
+    ref = search(xq)
+    torch.cuda.synchronize(device)
+    for D_h, I_h in outs:
+        if not (torch.equal(I_h, ref.labels.cpu()) and torch.equal(D_h, ref.distances.cpu())):
+            raise RuntimeError("pipelined end-to-end results differ from the device search")
+    return pipe_ms, serial_ms
+
+
+def e2e_entry(nq, d, k, steps, pipe_ms, serial_ms):
+    return {
+        "value": round(nq * steps / (pipe_ms * 1e-3), 1),
+        "unit": "queries/s",
+        "h2d_bytes_per_step": int(nq * d * 4),
+        "d2h_bytes_per_step": int(nq * k * 12),
+        "steps": steps,
+        "mode": "pipelined: search_host_batches, each batch copied in from pinned host "
+                "memory, searched and copied out, the copies overlapping the next and "
+                "previous batches' searches",
+        "serial_value": round(nq * steps / (serial_ms * 1e-3), 1),
+    }
+
+
 # ------------------------------------------------------------------- IVF arm
 def build_index(cfg, device, seed=1234, rank=0, world=1):
     """The benchmark's IVF index. With world > 1 every rank trains on the same
-    subsample (identical centroids) and adds only the rows of the lists it
-    owns (greedy LPT on the list sizes)."""
+    subsample (identical centroids), adds only the rows of the lists it owns
+    (greedy LPT on the list sizes) and keeps the head bank (the first rows of
+    every list, for the bound pass). Returns (index, queries, owners, heads)."""
     from metalfaiss_b200 import IVFFlatIndex, synthetic as syn
     from metalfaiss_b200.clustering import ClusteringParameters
 
@@ -339,11 +393,12 @@ def build_index(cfg, device, seed=1234, rank=0, world=1):
     idx.train(x)
     torch.cuda.synchronize(device)
     t1 = time.time()
-    owners = None
+    owners = heads = None
     if world > 1:
-        from metalfaiss_b200.sharding import add_owned_rows
+        from metalfaiss_b200.sharding import add_owned_rows, empty_heads
 
-        owners = add_owned_rows(idx, x, rank, world)
+        heads = empty_heads(idx)
+        owners = add_owned_rows(idx, x, rank, world, heads=heads)
     else:
         idx.add(x)
     torch.cuda.synchronize(device)
@@ -352,7 +407,7 @@ def build_index(cfg, device, seed=1234, rank=0, world=1):
     xq, _ = syn.torch_mixture(cfg["nq"], cfg["d"], cfg["nlist"], seed + 1, device, centres=centres)
     torch.cuda.empty_cache()
     log(f"[bench] built index: train {t1 - t0:.1f}s add {t2 - t1:.1f}s ntotal={idx.ntotal}")
-    return idx, xq, owners
+    return idx, xq, owners, heads
 
 
 # A list probed by at most this many queries is scanned by the few-query
@@ -403,10 +458,10 @@ def run_ivf(args, cfg, rank, world, device):
     from metalfaiss_b200 import _native as nat
     from metalfaiss_b200.sharding import ShardedIVF
 
-    idx, xq, owners = build_index(cfg, device, rank=rank, world=world)
+    idx, xq, owners, heads = build_index(cfg, device, rank=rank, world=world)
     idx.nprobe = cfg["nprobe"]
     k, nq, d = cfg["k"], cfg["nq"], cfg["d"]
-    sharded = ShardedIVF(idx, rank, world, owners=owners) if world > 1 else None
+    sharded = ShardedIVF(idx, rank, world, owners=owners, heads=heads) if world > 1 else None
     search = (lambda q: sharded.search(q, k)) if sharded else (lambda q: idx.search(q, k))
 
     # probes (for the roofline bytes): the coarse step of this batch
@@ -454,19 +509,8 @@ def run_ivf(args, cfg, rank, world, device):
     rescans = nat.filter_rescans(device.index, reset=True)
 
     # ---- end to end through the public API: pinned host queries in, results out
-    # (every step copies its queries host -> device and its results device ->
-    # host, in stream order, inside the timed region)
-    xq_host = xq.cpu().pin_memory()
-    D_host = torch.empty((nq, k), dtype=torch.float32).pin_memory()
-    I_host = torch.empty((nq, k), dtype=torch.int64).pin_memory()
-
-    def e2e_step():
-        r = search(xq_host.to(device, non_blocking=True))
-        D_host.copy_(r.distances, non_blocking=True)
-        I_host.copy_(r.labels, non_blocking=True)
-
     e2e_steps = max(3, args.steps // 2)
-    e2e_ms, _, _ = timer.run(e2e_step, e2e_steps, 2)
+    e2e_ms, e2e_serial_ms = end_to_end(timer, search, xq, k, device, e2e_steps)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -552,12 +596,7 @@ def run_ivf(args, cfg, rank, world, device):
                                    / hbm_peak, 4) if small_n else None),
                 },
             },
-            "e2e": {
-                "value": round(nq * e2e_steps / (e2e_ms * 1e-3), 1),
-                "unit": "queries/s",
-                "h2d_bytes_per_step": int(nq * d * 4),
-                "d2h_bytes_per_step": int(nq * k * 12),
-            },
+            "e2e": e2e_entry(nq, d, k, e2e_steps, e2e_ms, e2e_serial_ms),
             "gpu_launches": int(launches),
             "clocks": clocks,
             "cpu_baseline": cpu,
@@ -728,17 +767,8 @@ def run_flat(args, cfg, rank, world, device):
     kt = timer.kernel_times(lambda: search(xq), ["scan_topk_flat", "merge"], min(args.steps, 10))
     scan_ms, scan_n = kt["scan_topk_flat"]
 
-    xq_host = xq.cpu().pin_memory()
-    D_host = torch.empty((nq, k), dtype=torch.float32).pin_memory()
-    I_host = torch.empty((nq, k), dtype=torch.int64).pin_memory()
-
-    def e2e_step():
-        r = search(xq_host.to(device, non_blocking=True))
-        D_host.copy_(r.distances, non_blocking=True)
-        I_host.copy_(r.labels, non_blocking=True)
-
     e2e_steps = max(3, args.steps // 2)
-    e2e_ms, _, _ = timer.run(e2e_step, e2e_steps, 2)
+    e2e_ms, e2e_serial_ms = end_to_end(timer, search, xq, k, device, e2e_steps)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline_flat(idx.xb, xq, cfg, args.flat_cpu_sample)
@@ -775,8 +805,7 @@ def run_flat(args, cfg, rank, world, device):
                         "peak": hbm_peak, "peak_kind": f"{peak_kind} hbm_gbs"},
                 "traffic": None,
             },
-            "e2e": {"value": round(nq * e2e_steps / (e2e_ms * 1e-3), 1), "unit": "queries/s",
-                    "h2d_bytes_per_step": int(nq * d * 4), "d2h_bytes_per_step": int(nq * k * 12)},
+            "e2e": e2e_entry(nq, d, k, e2e_steps, e2e_ms, e2e_serial_ms),
             "gpu_launches": int(launches),
             "clocks": clocks,
             "cpu_baseline": cpu,

@@ -327,6 +327,11 @@ MF_API int mf_ivf_search_preassigned(int device, void* stream, const float* xq, 
  * top-k. Replaces the sharded IVF search the reference's multi-GPU tests expect
  * (python/metalfaiss/unittest/test_mlx_multi_gpu.py:86-119). Both take the
  * mf_ivf_search_preassigned_workspace_size workspace. */
+/* Rows of a query's nearest list that mf_ivf_probe_bound scans (its first
+ * rows, at most this many). A process that holds, for every list, a copy of
+ * at least these first rows computes every query's bound by itself. */
+MF_API int mf_ivf_bound_rows(void);
+
 MF_API int mf_ivf_probe_bound(int device, void* stream, const float* xq, int64_t nq,
                               const int64_t* probes, int nprobe, int nlist,
                               const int64_t* list_offsets, const float* list_vecs,
@@ -421,6 +426,21 @@ MF_API int mf_ivf_filter_rescans(int device, int64_t* count, int reset);
 MF_API int mf_topk_merge(int device, void* stream, const float* part_distances,
                   const int64_t* part_labels, int64_t nq, int parts, int k_in, int k,
                   float* distances, int64_t* labels);
+
+/* mf_topk_merge over any layout of the partial lists: slot j of part p of
+ * query q is part_distances[q * dist_query_stride + p * dist_part_stride + j]
+ * and part_labels[q * label_query_stride + p * label_part_stride + j]
+ * (element strides). Equal distances resolve by (p, j) as in mf_topk_merge,
+ * so the result does not depend on the layout. It reads the partials of the
+ * processes of a sharded search where an all-gather left them, part-major
+ * ((parts, nq, k_in), distances and labels in one buffer per part), without
+ * a transposing copy. Replaces the same device_topk_merge
+ * (python/metalfaiss/faissmlx/kernels/ivf_kernels.py:211-250). */
+MF_API int mf_topk_merge_strided(int device, void* stream, const float* part_distances,
+                                 int64_t dist_query_stride, int64_t dist_part_stride,
+                                 const int64_t* part_labels, int64_t label_query_stride,
+                                 int64_t label_part_stride, int64_t nq, int parts, int k_in,
+                                 int k, float* distances, int64_t* labels);
 
 MF_API int mf_kmeans_assign_workspace_size(int64_t n, int nc, int d, size_t* bytes);
 

@@ -50,6 +50,8 @@ _SIGNATURES = {
     "mf_ivf_search_bounded_filtered": ([I32, P, P, I64, P, I32, I32, P, P, P, P, I64, P, P, P, P, P, P, I32, I32, P, P, P, P, SZ], I32),
     "mf_ivf_filter_rescans": ([I32, PI64, I32], I32),
     "mf_topk_merge": ([I32, P, P, P, I64, I32, I32, I32, P, P], I32),
+    "mf_topk_merge_strided": ([I32, P, P, I64, I64, P, I64, I64, I64, I32, I32, I32, P, P], I32),
+    "mf_ivf_bound_rows": ([], I32),
     "mf_kmeans_assign_workspace_size": ([I64, I32, I32, PSZ], I32),
     "mf_kmeans_assign": ([I32, P, P, I64, P, P, I32, I32, P, P, P, SZ], I32),
     "mf_kmeans_update_workspace_size": ([I64, I32, I32, PSZ], I32),

@@ -180,6 +180,9 @@ int scan_small_items(const ScanArgs& base, const IvfWs& w, int metric, int64_t m
   return launch_scan(sa, metric, kEpiTopK, max_items, device, stream);
 }
 
+// Rows of a query's nearest list that the bound pass scans (at most).
+constexpr int64_t kBoundRows = 128;
+
 int ivf_scan_topk(int device, cudaStream_t stream, const IvfWs& w, const float* xq, int64_t nq,
                   const int64_t* probes, int P, int nlist, const int64_t* list_offsets,
                   const float* list_vecs, const float* list_norms, const float* list_lo,
@@ -218,7 +221,6 @@ int ivf_scan_topk(int device, cudaStream_t stream, const IvfWs& w, const float* 
   // one-tile items are cheaper there); the bound then carries a margin for
   // the engines' rounding difference, so phase 2 still drops no row that
   // belongs to the top-k.
-  constexpr int64_t kBoundRows = 128;
   constexpr int kSmallGroup = 16;
   // bound pass groups: the SIMT scan's 32 queries per item
   const int few_group = kScanTQ;
@@ -436,6 +438,8 @@ int mf_version(void) { return 100; }
 const char* mf_last_error(void) { return g_last_error.c_str(); }
 
 int mf_max_k(void) { return kMaxK; }
+
+int mf_ivf_bound_rows(void) { return (int)kBoundRows; }
 
 int mf_diag_f16_dot(int device, void* stream, int engine, const void* a, const void* b, int d,
                     float* out) {
@@ -840,6 +844,27 @@ int mf_topk_merge(int device, void* stream, const float* part_distances,
   MF_TRY(check_device_ptr(labels, "labels"));
   return launch_merge(part_distances, part_labels, nq, parts, k_in, k, distances, labels,
                       (cudaStream_t)stream);
+}
+
+int mf_topk_merge_strided(int device, void* stream, const float* part_distances,
+                          int64_t dist_query_stride, int64_t dist_part_stride,
+                          const int64_t* part_labels, int64_t label_query_stride,
+                          int64_t label_part_stride, int64_t nq, int parts, int k_in, int k,
+                          float* distances, int64_t* labels) {
+  MF_ENTER(device);
+  MF_CHECK(k >= 1 && k <= kMaxK, MF_ERR_INVALID_ARGS, "k=%d outside [1, %d]", k, kMaxK);
+  MF_CHECK(parts >= 1 && k_in >= 0 && nq >= 0, MF_ERR_INVALID_ARGS, "bad merge shape");
+  MF_CHECK(dist_query_stride >= 0 && dist_part_stride >= 0 && label_query_stride >= 0 &&
+               label_part_stride >= 0,
+           MF_ERR_INVALID_ARGS, "merge strides must be non-negative");
+  if (nq == 0) return MF_OK;
+  MF_TRY(check_device_ptr(part_distances, "part_distances", k_in == 0));
+  MF_TRY(check_device_ptr(part_labels, "part_labels", k_in == 0));
+  MF_TRY(check_device_ptr(distances, "distances"));
+  MF_TRY(check_device_ptr(labels, "labels"));
+  return launch_merge_strided(part_distances, dist_query_stride, dist_part_stride, part_labels,
+                              label_query_stride, label_part_stride, nq, parts, k_in, k,
+                              distances, labels, (cudaStream_t)stream);
 }
 
 int mf_kmeans_assign_workspace_size(int64_t n, int nc, int d, size_t* bytes) {

@@ -281,11 +281,18 @@ __global__ void __launch_bounds__(kScanThreads) scan_kernel(const ScanArgs a) {
   }
 }
 
+// Slot j of part p of query q sits at q * qs + p * ps + j (qs, ps in elements,
+// one pair for the distances and one for the labels); its key's index is
+// p * k_in + j whatever the layout, so equal distances resolve alike.
+struct MergeLayout {
+  long long d_qs, d_ps, l_qs, l_ps;
+};
+
 template <int KCAP>
 __global__ void __launch_bounds__(256) merge_kernel(const float* __restrict__ pd,
                                                     const int64_t* __restrict__ pl, int64_t nq,
-                                                    int parts, int k_in, int k, float* D,
-                                                    int64_t* L) {
+                                                    int parts, int k_in, int k, MergeLayout ml,
+                                                    float* D, int64_t* L) {
   __shared__ unsigned long long lists[8][KCAP];
   __shared__ unsigned long long bufs[8][32];
   const int lane = threadIdx.x & 31;
@@ -294,12 +301,16 @@ __global__ void __launch_bounds__(256) merge_kernel(const float* __restrict__ pd
   if (q >= nq) return;
   WarpTopK<KCAP> tk;
   tk.init(lists[warp], bufs[warp], k, lane);
-  const long long total = (long long)parts * k_in;
-  const long long base = q * total;
-  for (long long c0 = 0; c0 < total; c0 += 32) {
-    const long long c = c0 + lane;
+  const int total = parts * k_in;
+  const float* qd = pd + q * ml.d_qs;
+  const int64_t* ql = pl + q * ml.l_qs;
+  for (int c0 = 0; c0 < total; c0 += 32) {
+    const int c = c0 + lane;
     unsigned long long key = kEmptyKey;
-    if (c < total && pl[base + c] >= 0) key = make_key(pd[base + c], (unsigned int)c);
+    if (c < total) {
+      const int p = c / k_in, j = c - p * k_in;
+      if (ql[p * ml.l_ps + j] >= 0) key = make_key(qd[p * ml.d_ps + j], (unsigned int)c);
+    }
     tk.offer(key, k, lane);
   }
   tk.flush(k, lane);
@@ -310,7 +321,9 @@ __global__ void __launch_bounds__(256) merge_kernel(const float* __restrict__ pd
       L[q * k + t] = -1;
     } else {
       D[q * k + t] = key_dist(key);
-      L[q * k + t] = pl[base + key_index(key)];
+      const int c = (int)key_index(key);
+      const int p = c / k_in;
+      L[q * k + t] = ql[p * ml.l_ps + (c - p * k_in)];
     }
   }
 }
@@ -565,23 +578,31 @@ int launch_dmat_select(const float* dmat, int64_t ld, int64_t nq, int64_t nb, in
   return MF_OK;
 }
 
-int launch_merge(const float* pd, const int64_t* pl, int64_t nq, int parts, int k_in, int k,
-                 float* d, int64_t* l, cudaStream_t stream) {
+int launch_merge_strided(const float* pd, int64_t d_qs, int64_t d_ps, const int64_t* pl,
+                         int64_t l_qs, int64_t l_ps, int64_t nq, int parts, int k_in, int k,
+                         float* d, int64_t* l, cudaStream_t stream) {
   if (nq <= 0 || k <= 0) return MF_OK;
   const int kcap = scan_kcap(k);
   MF_CHECK(kcap != 0, MF_ERR_INVALID_ARGS, "k=%d exceeds the supported maximum %d", k, kMaxK);
   MF_CHECK((long long)parts * k_in < (1ll << 31), MF_ERR_INVALID_ARGS,
            "parts*k_in too large for one merge");
+  const MergeLayout ml{d_qs, d_ps, l_qs, l_ps};
   const long long grid = ceil_div(nq, 8);
   ScopedTiming tm("merge", stream);
   switch (kcap) {
-    case 32: merge_kernel<32><<<(unsigned int)grid, 256, 0, stream>>>(pd, pl, nq, parts, k_in, k, d, l); break;
-    case 64: merge_kernel<64><<<(unsigned int)grid, 256, 0, stream>>>(pd, pl, nq, parts, k_in, k, d, l); break;
-    case 128: merge_kernel<128><<<(unsigned int)grid, 256, 0, stream>>>(pd, pl, nq, parts, k_in, k, d, l); break;
-    default: merge_kernel<256><<<(unsigned int)grid, 256, 0, stream>>>(pd, pl, nq, parts, k_in, k, d, l); break;
+    case 32: merge_kernel<32><<<(unsigned int)grid, 256, 0, stream>>>(pd, pl, nq, parts, k_in, k, ml, d, l); break;
+    case 64: merge_kernel<64><<<(unsigned int)grid, 256, 0, stream>>>(pd, pl, nq, parts, k_in, k, ml, d, l); break;
+    case 128: merge_kernel<128><<<(unsigned int)grid, 256, 0, stream>>>(pd, pl, nq, parts, k_in, k, ml, d, l); break;
+    default: merge_kernel<256><<<(unsigned int)grid, 256, 0, stream>>>(pd, pl, nq, parts, k_in, k, ml, d, l); break;
   }
   MF_LAUNCH_CHECK();
   return MF_OK;
+}
+
+int launch_merge(const float* pd, const int64_t* pl, int64_t nq, int parts, int k_in, int k,
+                 float* d, int64_t* l, cudaStream_t stream) {
+  const int64_t qs = (int64_t)parts * k_in;
+  return launch_merge_strided(pd, qs, k_in, pl, qs, k_in, nq, parts, k_in, k, d, l, stream);
 }
 
 // ------------------------------------------------------------- flat search

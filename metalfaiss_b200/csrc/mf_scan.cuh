@@ -155,6 +155,11 @@ int launch_map_ids(const int64_t* ids, int64_t* labels, int64_t n, cudaStream_t 
 // Partial top-k merge (nq, parts, k_in) -> (nq, k).
 int launch_merge(const float* pd, const int64_t* pl, int64_t nq, int parts, int k_in, int k,
                  float* d, int64_t* l, cudaStream_t stream);
+// The same merge over any layout: slot j of part p of query q at
+// q * qs + p * ps + j (element strides, one pair per array).
+int launch_merge_strided(const float* pd, int64_t d_qs, int64_t d_ps, const int64_t* pl,
+                         int64_t l_qs, int64_t l_ps, int64_t nq, int parts, int k_in, int k,
+                         float* d, int64_t* l, cudaStream_t stream);
 
 // Flat search plan: splits and workspace.
 struct FlatPlan {

@@ -142,10 +142,15 @@ class FlatIndex:
         xq = as_matrix(xs, self.d, self.device, "queries")
         return self._search_padded(xq, min(k, self.ntotal))
 
-    def _search_padded(self, xq: torch.Tensor, k: int, map_ids: bool = True) -> SearchResult:
+    def _search_padded(self, xq: torch.Tensor, k: int, map_ids: bool = True,
+                       out=None) -> SearchResult:
+        """out: contiguous (nq, k) float32 and int64 tensors to write into."""
         nq = xq.shape[0]
-        D = torch.empty((nq, k), dtype=torch.float32, device=self.device)
-        I = torch.empty((nq, k), dtype=torch.int64, device=self.device)
+        if out is None:
+            D = torch.empty((nq, k), dtype=torch.float32, device=self.device)
+            I = torch.empty((nq, k), dtype=torch.int64, device=self.device)
+        else:
+            D, I = out
         if nq == 0 or k == 0:
             return SearchResult(D, I)
         if k > nat.load().mf_max_k():

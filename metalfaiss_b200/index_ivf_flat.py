@@ -450,12 +450,16 @@ class IVFFlatIndex:
                 self._dp, m, k)
         return head, ws
 
-    def _probe_bound(self, xq: torch.Tensor, probes: torch.Tensor, k: int) -> torch.Tensor:
+    def _probe_bound(self, xq: torch.Tensor, probes: torch.Tensor, k: int,
+                     out: Optional[torch.Tensor] = None) -> torch.Tensor:
         """Per query, an upper bound on its k-th distance over its probes, from
         the first rows of its first probe; +inf where this index holds no rows
-        of that list (mf_ivf_probe_bound)."""
-        bound = torch.full((xq.shape[0],), float("inf"), dtype=torch.float32, device=self.device)
+        of that list (mf_ivf_probe_bound). out: a contiguous (nq,) float32
+        tensor to write into."""
+        bound = (torch.empty((xq.shape[0],), dtype=torch.float32, device=self.device)
+                 if out is None else out)
         if xq.shape[0] == 0 or probes.shape[1] == 0:
+            bound.fill_(float("inf"))
             return bound
         self._empty_lists_guard()
         head, ws = self._ivf_args(xq, probes, k)
@@ -463,13 +467,19 @@ class IVFFlatIndex:
         return bound
 
     def _search_bounded(self, xq: torch.Tensor, k: int, probes: torch.Tensor,
-                        bound: torch.Tensor) -> SearchResult:
+                        bound: torch.Tensor, out=None) -> SearchResult:
         """search_preassigned keeping only rows within bound[q]
-        (mf_ivf_search_bounded); fewer than k rows come back padded."""
+        (mf_ivf_search_bounded); fewer than k rows come back padded. out:
+        contiguous (nq, k) float32 and int64 tensors to write into."""
         nq = xq.shape[0]
-        D = torch.full((nq, k), float("inf"), dtype=torch.float32, device=self.device)
-        I = torch.full((nq, k), -1, dtype=torch.int64, device=self.device)
+        if out is None:
+            D = torch.empty((nq, k), dtype=torch.float32, device=self.device)
+            I = torch.empty((nq, k), dtype=torch.int64, device=self.device)
+        else:
+            D, I = out
         if nq == 0 or k == 0 or probes.shape[1] == 0:
+            D.fill_(float("inf"))
+            I.fill_(-1)
             return SearchResult(D, I)
         self._empty_lists_guard()
         if self._filter_ok(k):

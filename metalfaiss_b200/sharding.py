@@ -7,14 +7,17 @@ sharded with a shared quantizer (:86-119), and its facade stubs IndexShards
 (python/metalfaiss/faiss_compat.py:326-366).
 
 * IVFFlat: inverted lists are partitioned over the ranks by greedy LPT on list
-  size; the coarse quantizer is replicated. A search exchanges three things:
-  1. each rank runs the coarse step for its share of the queries and the
-     (nq, nprobe) probe lists are all-gathered;
-  2. each rank computes, for the queries whose nearest list it holds, an
-     upper bound on the k-th distance (the first rows of that list), and a
-     MIN all-reduce gives every rank every query's bound;
-  3. each rank scans only the lists it owns, keeping rows within the bound,
-     and the (nq, k) partial results are all-gathered and merged on device.
+  size; the coarse quantizer is replicated, and so are the first rows of every
+  list (the head bank: the rows the bound pass reads, about 2.1 M rows of the
+  20 M-row index). A search has two exchange steps:
+  1. each rank runs the coarse step for its share of the queries and, from the
+     head bank, those queries' upper bounds on the k-th distance; one
+     all-gather gives every rank all (nq, nprobe) probe lists and nq bounds;
+  2. each rank scans only the lists it owns, keeping rows within the bound,
+     and one all-gather of the (nq, k) partial results (distances and labels
+     in one buffer) feeds the on-device merge, which reads them in place.
+  Without a head bank the bounds come from the ranks that hold each query's
+  nearest list and a MIN all-reduce (a third exchange step).
 * Flat: contiguous row shards; labels are global ids; one all-gather + merge.
 Collectives go through torch.distributed (NCCL on GPUs, gloo in CPU tests).
 """
@@ -93,6 +96,106 @@ def gather_rows(local: torch.Tensor, n: int, group=None) -> torch.Tensor:
     return torch.cat(rows)
 
 
+def _half(n: int) -> int:
+    return (n + 1) // 2
+
+
+def probe_buffer(nq: int, nprobe: int, rank: int, world: int, device):
+    """This rank's send buffer of exchange_probes and the views the coarse
+    step and the bound pass write into: int64 words, first the (m, nprobe)
+    probes of its m = row_shard queries, then the m bounds as float32 (the
+    layout of every rank is sized for the largest share)."""
+    b, e = row_shard(nq, rank, world)
+    mmax = -(-nq // world) if nq else 0
+    send = torch.empty(mmax * nprobe + _half(mmax), dtype=torch.int64, device=device)
+    m = e - b
+    probes = send[: m * nprobe].view(m, nprobe)
+    bound = send[mmax * nprobe:].view(torch.float32)[:m]
+    return send, probes, bound
+
+
+def exchange_probes(send: torch.Tensor, nq: int, nprobe: int, group=None):
+    """One all-gather of every rank's probe_buffer → the (nq, nprobe) probes
+    and (nq,) bounds of all queries, in query order, on every rank."""
+    world = dist.get_world_size(group)
+    mmax = -(-nq // world) if nq else 0
+    if dist.get_backend(group) == "nccl":
+        out = torch.empty((world, send.numel()), dtype=send.dtype, device=send.device)
+        dist.all_gather_into_tensor(out, send, group=group)
+    else:
+        parts = [torch.empty_like(send) for _ in range(world)]
+        dist.all_gather(parts, send, group=group)
+        out = torch.stack(parts)
+    bounds = out[:, mmax * nprobe:].view(torch.float32)
+    probes, bound = [], []
+    for r in range(world):
+        b, e = row_shard(nq, r, world)
+        probes.append(out[r, : (e - b) * nprobe].view(e - b, nprobe))
+        bound.append(bounds[r, : e - b])
+    return torch.cat(probes), torch.cat(bound)
+
+
+def partial_buffer(nq: int, k: int, device):
+    """A send buffer for gather_packed and its (nq, k) float32 distance and
+    int64 label views: int64 words, the distances first (padded to a word),
+    then the labels."""
+    hd = _half(nq * k)
+    send = torch.empty(hd + nq * k, dtype=torch.int64, device=device)
+    D = send[:hd].view(torch.float32)[: nq * k].view(nq, k)
+    I = send[hd:].view(nq, k)
+    return send, D, I
+
+
+def gather_packed(send: torch.Tensor, group=None) -> torch.Tensor:
+    """One all-gather of every rank's partial_buffer → (world, words)."""
+    world = dist.get_world_size(group)
+    if dist.get_backend(group) == "nccl":
+        out = torch.empty((world, send.numel()), dtype=send.dtype, device=send.device)
+        dist.all_gather_into_tensor(out, send, group=group)
+        return out
+    parts = [torch.empty_like(send) for _ in range(world)]
+    dist.all_gather(parts, send, group=group)
+    return torch.stack(parts)
+
+
+def unpack_partials(buf: torch.Tensor, nq: int, k: int):
+    """Views of gather_packed's output: (world, nq, k) distances and labels."""
+    world = buf.shape[0]
+    hd = _half(nq * k)
+    D = buf[:, :hd].view(torch.float32)[:, : nq * k].view(world, nq, k)
+    I = buf[:, hd:].view(world, nq, k)
+    return D, I
+
+
+def merge_packed(buf: torch.Tensor, nq: int, k_in: int, k: int) -> SearchResult:
+    """The (nq, k) merge of gather_packed's output, read in place by
+    mf_topk_merge_strided (part p's slot j of query q: distance word
+    p * 2 * words + q * k_in + j of the float32 view, label p * words +
+    hd + q * k_in + j)."""
+    world, words = buf.shape
+    hd = _half(nq * k_in)
+    D = torch.empty((nq, k), dtype=torch.float32, device=buf.device)
+    I = torch.empty((nq, k), dtype=torch.int64, device=buf.device)
+    if nq:
+        nat.call("mf_topk_merge_strided", buf.device.index, nat.stream_of(buf.device),
+                 nat.ptr(buf), k_in, 2 * words, nat.ptr(buf[:, hd:]), k_in, words, nq, world,
+                 k_in, k, nat.ptr(D), nat.ptr(I))
+    return SearchResult(D, I)
+
+
+def head_rows(labels: torch.Tensor, nlist: int, rows: int) -> torch.Tensor:
+    """Positions, ascending, of the first `rows` rows (in input order) of each
+    list, given every row's list: the rows of a head bank."""
+    n = labels.shape[0]
+    if n == 0:
+        return torch.empty(0, dtype=torch.int64, device=labels.device)
+    order = torch.sort(labels, stable=True).indices
+    counts = torch.bincount(labels, minlength=nlist)
+    starts = torch.cumsum(counts, 0) - counts
+    pos = torch.arange(n, device=labels.device) - starts[labels[order]]
+    return torch.sort(order[pos < rows]).values
+
+
 def merge_partials(pd: torch.Tensor, pi: torch.Tensor, k: int) -> SearchResult:
     """(nq, parts, k_in) → (nq, k) with the on-device merge kernel."""
     nq, parts, k_in = pd.shape
@@ -104,9 +207,7 @@ def merge_partials(pd: torch.Tensor, pi: torch.Tensor, k: int) -> SearchResult:
     return SearchResult(D, I)
 
 
-def keep_lists(index, keep_mask: np.ndarray):
-    """A copy of an IVFFlatIndex holding only the lists where keep_mask is True
-    (the other lists stay empty); shares the quantizer."""
+def _empty_like_index(index):
     from .index_ivf_flat import IVFFlatIndex
 
     out = IVFFlatIndex(index.d, index.nlist, quantizer=index.quantizer,
@@ -114,9 +215,19 @@ def keep_lists(index, keep_mask: np.ndarray):
                        residuals=index._residuals)
     out._is_trained = index.is_trained
     out.nprobe = index.nprobe
+    return out
+
+
+def keep_lists(index, keep_mask: np.ndarray, max_rows: int = None):
+    """A copy of an IVFFlatIndex holding only the lists where keep_mask is True
+    (the other lists stay empty), and of those only the first max_rows rows
+    when given; shares the quantizer."""
+    out = _empty_like_index(index)
     sizes = index.list_sizes()
     keep = np.asarray(keep_mask, bool)
     new_sizes = np.where(keep, sizes, 0)
+    if max_rows is not None:
+        new_sizes = np.minimum(new_sizes, max_rows)
     offsets = np.zeros(index.nlist + 1, np.int64)
     np.cumsum(new_sizes, out=offsets[1:])
     dev = index.device
@@ -124,6 +235,10 @@ def keep_lists(index, keep_mask: np.ndarray):
         list_of_row = torch.repeat_interleave(torch.arange(index.nlist, device=dev),
                                               torch.from_numpy(sizes).to(dev))
         row_mask = torch.from_numpy(keep).to(dev)[list_of_row]
+        if max_rows is not None:
+            starts = torch.from_numpy(index.list_offsets.cpu().numpy()[:-1]).to(dev)
+            pos = torch.arange(index.ntotal, device=dev) - starts[list_of_row]
+            row_mask &= pos < max_rows
         out._vecs = index._vecs[: index.ntotal][row_mask].contiguous()
         out._norms = index._norms[: index.ntotal][row_mask].contiguous()
         out._lo = (index._lo[: index.ntotal][row_mask].contiguous()
@@ -158,14 +273,28 @@ def train_kmeans_sharded(x: torch.Tensor, k: int, niter: int, init: torch.Tensor
     return c
 
 
-def add_owned_rows(index, xs, rank: int, world: int, ids=None) -> np.ndarray:
+def empty_heads(index):
+    """An empty index with index's quantizer, to receive a head bank from
+    add_owned_rows."""
+    return _empty_like_index(index)
+
+
+def head_bank(index):
+    """The head bank of a whole IVFFlatIndex: a copy holding the first
+    mf_ivf_bound_rows() rows of every list (what the bound pass reads)."""
+    return keep_lists(index, np.ones(index.nlist, bool), nat.load().mf_ivf_bound_rows())
+
+
+def add_owned_rows(index, xs, rank: int, world: int, ids=None, heads=None) -> np.ndarray:
     """Sharded IVF build: `index` (trained; the same centroids on every rank)
     receives only the rows of xs whose list this rank owns. Every rank
     assigns all rows once (the same result everywhere), the lists are
     partitioned by greedy LPT on their sizes, and each rank appends its own
     lists' rows with their global ids (row positions in xs, or `ids`), in
     input order. Returns the owner rank of every list. The database held by
-    a rank is about 1/world of the whole."""
+    a rank is about 1/world of the whole. `heads` (an empty index with the
+    same centroids), when given, receives the head bank: the first
+    mf_ivf_bound_rows() rows of every list, the same on every rank."""
     from ._tensors import as_ids, as_matrix
 
     dev = index.device
@@ -179,23 +308,29 @@ def add_owned_rows(index, xs, rank: int, world: int, ids=None) -> np.ndarray:
            else as_ids(ids, n, dev))
     index._add_assigned(x[mine].contiguous(), gid[mine].contiguous(),
                         labels[mine].contiguous())
+    if heads is not None:
+        h = head_rows(labels, index.nlist, nat.load().mf_ivf_bound_rows())
+        heads._add_assigned(x[h].contiguous(), gid[h].contiguous(), labels[h].contiguous())
     return owners
 
 
 class ShardedIVF:
     """This rank's share of an IVFFlat index; search() returns the merged global top-k.
 
-    Built from a whole index (this rank keeps a copy of its own lists) or,
-    with `owners` from add_owned_rows, from an index that holds only this
-    rank's lists already."""
+    Built from a whole index (this rank keeps a copy of its own lists and
+    the head bank) or, with `owners` from add_owned_rows, from an index that
+    holds only this rank's lists already (and `heads`, the head bank
+    add_owned_rows filled, if any)."""
 
-    def __init__(self, index, rank: int, world: int, group=None, owners=None):
+    def __init__(self, index, rank: int, world: int, group=None, owners=None, heads=None):
         self.rank, self.world, self.group = rank, world, group
         if owners is None:
             owners = lpt_partition(index.list_sizes(), world)
             self.local = keep_lists(index, owners == rank)
+            heads = head_bank(index) if heads is None else heads
         else:
             self.local = index
+        self.heads = heads
         self.owners = np.asarray(owners)
         # a list here collects (phase, CUDA event) pairs of each search
         self.phase_events = None
@@ -223,6 +358,8 @@ class ShardedIVF:
         idx._check_k(k)
         P = min(idx.nprobe, idx.nlist)
         self._mark("start")
+        if self.heads is not None:
+            return self._search_heads(xq, k, P)
         # 1. coarse step over this rank's share of the queries
         b, e = row_shard(nq, self.rank, self.world)
         if e > b:
@@ -243,6 +380,34 @@ class ShardedIVF:
         pd, pi = gather_partials(local.distances, local.labels, self.group)
         self._mark("gather partials")
         out = merge_partials(pd, pi, k)
+        self._mark("merge")
+        return out
+
+    def _search_heads(self, xq, k: int, P: int) -> SearchResult:
+        idx = self.local
+        nq = xq.shape[0]
+        dev = idx.device
+        # 1. this rank's share of the queries: coarse step and bounds (from
+        #    the head bank), written into the send buffer; one all-gather
+        b, e = row_shard(nq, self.rank, self.world)
+        send, mine, mine_bound = probe_buffer(nq, P, self.rank, self.world, dev)
+        if e > b:
+            scratch = torch.empty((e - b, P), dtype=torch.float32, device=dev)
+            idx.quantizer._search_padded(xq[b:e], P, map_ids=False, out=(scratch, mine))
+        self._mark("coarse")
+        if e > b:
+            self.heads._probe_bound(xq[b:e], mine, k, out=mine_bound)
+        self._mark("bound pass")
+        probes, bound = exchange_probes(send, nq, P, self.group)
+        self._mark("gather probes")
+        # 2. this rank's lists, within the bound, into the partials' send
+        #    buffer; one all-gather; the merge reads the gathered buffer
+        psend, D, I = partial_buffer(nq, k, dev)
+        idx._search_bounded(xq, k, probes, bound, out=(D, I))
+        self._mark("list scan")
+        gathered = gather_packed(psend, self.group)
+        self._mark("gather partials")
+        out = merge_packed(gathered, nq, k, k)
         self._mark("merge")
         return out
 

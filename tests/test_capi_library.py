@@ -38,6 +38,7 @@ def test_version_and_limits():
     lib = nat.load()
     assert lib.mf_version() >= 100
     assert lib.mf_max_k() == 256
+    assert lib.mf_ivf_bound_rows() == 128
 
 
 def test_workspace_queries_without_gpu():

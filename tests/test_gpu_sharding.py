@@ -144,3 +144,92 @@ def test_sharded_build_holds_each_rank_its_own_lists(cuda_device, world):
     errs = compare.check_knn(D, I, D_ref, I_ref, compare.exact_lookup(xq_np, x, oracle.L2),
                              atol=compare.l2_atol(xq_np, x))
     assert not errs, errs[:5]
+
+
+@pytest.mark.parametrize("metric", [MetricType.L2, MetricType.INNER_PRODUCT])
+@pytest.mark.parametrize("world", [2, 3])
+def test_head_bank_search_equals_single(cuda_device, engine, metric, world):
+    """The head-bank form of the multi-GPU search, ranks emulated in one
+    process: each rank's coarse step and bounds (from the head bank, the first
+    mf_ivf_bound_rows() rows of every list) for its share of the queries,
+    written into its probe_buffer; the buffers concatenated as the all-gather
+    leaves them; bounded scans into partial_buffers; merge_packed over the
+    stacked buffers. Equal to merge_partials over the same partials, and to
+    the unsharded search."""
+    from metalfaiss_b200.sharding import (head_bank, merge_packed, partial_buffer,
+                                          probe_buffer, row_shard, unpack_partials)
+
+    idx, x, xq_np = _index(metric)
+    idx.nprobe = P = 8
+    k = 10
+    ref = idx.search(xq_np, k)
+    xq = idx._prepare_query(xq_np)
+    nq = xq.shape[0]
+    heads = head_bank(idx)
+    R = nat.load().mf_ivf_bound_rows()
+    sizes, hsizes = idx.list_sizes(), heads.list_sizes()
+    assert np.array_equal(hsizes, np.minimum(sizes, R))
+    owners = lpt_partition(sizes, world)
+    shards = [keep_lists(idx, owners == r) for r in range(world)]
+    sends = []
+    for r in range(world):
+        b, e = row_shard(nq, r, world)
+        send, mine, mine_bound = probe_buffer(nq, P, r, world, xq.device)
+        scratch = torch.empty((e - b, P), dtype=torch.float32, device=xq.device)
+        idx.quantizer._search_padded(xq[b:e], P, map_ids=False, out=(scratch, mine))
+        heads._probe_bound(xq[b:e], mine, k, out=mine_bound)
+        sends.append(send)
+    # what exchange_probes unpacks from the all-gather's (world, words) output
+    gathered = torch.stack(sends)
+    bounds = gathered[:, -(-nq // world) * P:].view(torch.float32)
+    shares = [row_shard(nq, r, world) for r in range(world)]
+    probes = torch.cat([gathered[r, : (e - b) * P].view(e - b, P)
+                        for r, (b, e) in enumerate(shares)])
+    bound = torch.cat([bounds[r, : e - b] for r, (b, e) in enumerate(shares)])
+    full_probes = idx.quantizer._search_padded(xq, P, map_ids=False).labels
+    assert torch.equal(probes, full_probes)
+    # the head bank's bound is a bound: at least the exact k-th distance
+    D_ref, I_ref = ref.numpy()
+    assert bool((bound.cpu().numpy() >= D_ref[:, k - 1]).all())
+    psends = []
+    for s in shards:
+        psend, Dv, Iv = partial_buffer(nq, k, xq.device)
+        s._search_bounded(xq, k, probes, bound, out=(Dv, Iv))
+        psends.append(psend)
+    buf = torch.stack(psends)
+    D, I = merge_packed(buf, nq, k, k).numpy()
+    pd, pi = unpack_partials(buf, nq, k)
+    D2, I2 = merge_partials(pd.permute(1, 0, 2).contiguous(), pi.permute(1, 0, 2).contiguous(),
+                            k).numpy()
+    assert np.array_equal(I, I2) and np.array_equal(D, D2)
+    m = oracle.L2 if metric == MetricType.L2 else oracle.INNER_PRODUCT
+    atol = compare.l2_atol(xq_np, x) if metric == MetricType.L2 else 1e-5 * (1 + np.abs(D_ref).max())
+    errs = compare.check_knn(D, I, D_ref, I_ref, compare.exact_lookup(xq_np, x, m), atol=atol)
+    assert not errs, errs[:5]
+
+
+def test_strided_merge_matches_contiguous(cuda_device):
+    """mf_topk_merge_strided over a part-major layout with padded rows equals
+    mf_topk_merge over the (nq, parts, k_in) copy, ties and empty slots
+    included."""
+    g = torch.Generator().manual_seed(3)
+    nq, parts, k_in, k = 37, 5, 12, 9
+    d = torch.randint(0, 6, (nq, parts, k_in), generator=g).float()  # many ties
+    d = d.sort(-1).values
+    l = torch.randint(0, 1000, (nq, parts, k_in), generator=g)
+    l[torch.rand((nq, parts, k_in), generator=g) < 0.2] = -1
+    d[l < 0] = float("inf")
+    dev = torch.device("cuda", 0)
+    ref = merge_partials(d.to(dev), l.to(dev), k)
+    # part-major, each part's block padded by 3 elements
+    pad = 3
+    bd = torch.full((parts, nq * k_in + pad), 7.0)
+    bl = torch.full((parts, nq * k_in + pad), 5, dtype=torch.int64)
+    bd[:, : nq * k_in] = d.permute(1, 0, 2).reshape(parts, -1)
+    bl[:, : nq * k_in] = l.permute(1, 0, 2).reshape(parts, -1)
+    bd, bl = bd.to(dev), bl.to(dev)
+    D = torch.empty((nq, k), device=dev)
+    I = torch.empty((nq, k), dtype=torch.int64, device=dev)
+    nat.call("mf_topk_merge_strided", 0, nat.stream_of(dev), nat.ptr(bd), k_in, nq * k_in + pad,
+             nat.ptr(bl), k_in, nq * k_in + pad, nq, parts, k_in, k, nat.ptr(D), nat.ptr(I))
+    assert torch.equal(D, ref.distances) and torch.equal(I, ref.labels)

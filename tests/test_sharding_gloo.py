@@ -17,7 +17,9 @@ import numpy as np
 import pytest
 import torch
 
-from metalfaiss_b200.sharding import gather_partials, gather_rows, lpt_partition, row_shard
+from metalfaiss_b200.sharding import (exchange_probes, gather_packed, gather_partials,
+                                      gather_rows, head_rows, lpt_partition, partial_buffer,
+                                      probe_buffer, row_shard, unpack_partials)
 from oracle import oracle
 
 WORLD = 2
@@ -142,6 +144,42 @@ def _ivf_bound_worker(rank, port, out_dir):
         pd, pi = gather_partials(torch.from_numpy(D), torch.from_numpy(I))
         Dm, Im = _merge(pd.numpy(), pi.numpy(), k)
         np.savez(os.path.join(out_dir, f"ivfb{rank}.npz"), D=Dm, I=Im)
+    finally:
+        dist.destroy_process_group()
+
+
+def _ivf_heads_worker(rank, port, out_dir):
+    """The head-bank form of the multi-GPU IVF search: each rank computes the
+    probes and bounds of its share of the queries (the bounds from a copy of
+    every list's first rows), one all-gather shares both, bounded local scans,
+    one all-gather of the packed partials, merge."""
+    dist = _init(rank, port)
+    try:
+        cents, offsets, vecs, ids, xq = _ivf_data()
+        nprobe, k, nq = 5, 7, len(xq)
+        owners = lpt_partition(np.diff(offsets), WORLD)
+        b, e = row_shard(nq, rank, WORLD)
+        send, mine, mine_bound = probe_buffer(nq, nprobe, rank, WORLD, "cpu")
+        mine.copy_(torch.from_numpy(oracle.coarse_probes(xq[b:e], cents, nprobe).astype(np.int64)))
+        every = np.ones(len(offsets) - 1, bool)  # the head bank holds every list
+        mine_bound.copy_(torch.from_numpy(
+            _bound_of(xq[b:e], offsets, vecs, mine.numpy(), k, every)))
+        probes_t, bound_t = exchange_probes(send, nq, nprobe)
+        probes, bound = probes_t.numpy(), bound_t.numpy()
+        assert np.array_equal(probes, oracle.coarse_probes(xq, cents, nprobe))
+        assert np.array_equal(bound, _bound_of(xq, offsets, vecs, probes, k, every))
+        local = np.where(owners[probes] == rank, probes, -1)
+        D, I = oracle.ivf_search(xq, cents, offsets, vecs, ids, nprobe, k, probes=local)
+        keep = D <= bound[:, None]
+        psend, Dv, Iv = partial_buffer(nq, k, "cpu")
+        Dv.copy_(torch.from_numpy(np.where(keep, D, np.inf).astype(np.float32)))
+        Iv.copy_(torch.from_numpy(np.where(keep, I, -1)))
+        pd, pi = unpack_partials(gather_packed(psend), nq, k)
+        assert tuple(pd.shape) == (WORLD, nq, k)
+        # part r of the gathered buffer is rank r's own contribution
+        assert torch.equal(pi[rank], Iv) and torch.equal(pd[rank], Dv)
+        Dm, Im = _merge(pd.permute(1, 0, 2).numpy(), pi.permute(1, 0, 2).numpy(), k)
+        np.savez(os.path.join(out_dir, f"ivfh{rank}.npz"), D=Dm, I=Im)
     finally:
         dist.destroy_process_group()
 
@@ -296,3 +334,26 @@ def test_sharded_kmeans_equals_single_gloo():
         c_r = [np.load(os.path.join(tmp, f"km{r}.npy")) for r in range(WORLD)]
         assert np.array_equal(c_r[0], c_r[1])  # identical on every rank
         np.testing.assert_allclose(c_r[0], ref, rtol=1e-6, atol=1e-6)
+
+
+def test_sharded_ivf_head_bank_exchange_equals_single_gloo():
+    with tempfile.TemporaryDirectory() as tmp:
+        assert _run(_ivf_heads_worker, tmp) == [0, 0]
+        cents, offsets, vecs, ids, xq = _ivf_data()
+        D_ref, I_ref = oracle.ivf_search(xq, cents, offsets, vecs, ids, 5, 7)
+        for r in range(WORLD):
+            z = np.load(os.path.join(tmp, f"ivfh{r}.npz"))
+            assert np.array_equal(z["I"], I_ref)
+            assert np.array_equal(z["D"], D_ref)
+
+
+def test_head_rows_are_each_lists_first_rows():
+    rng = np.random.Generator(np.random.PCG64(5))
+    nlist = 7
+    labels = rng.integers(0, nlist, 500) ** 2 % nlist  # skewed, some lists empty
+    for rows in (1, 3, 40, 1000):
+        got = head_rows(torch.from_numpy(labels), nlist, rows).numpy()
+        want = np.sort(np.concatenate([np.flatnonzero(labels == l)[:rows]
+                                       for l in range(nlist)]))
+        assert np.array_equal(got, want)
+    assert head_rows(torch.empty(0, dtype=torch.int64), nlist, 4).numel() == 0
