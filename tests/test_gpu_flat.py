@@ -5,6 +5,7 @@ import pytest
 import torch
 
 from metalfaiss_b200 import FlatIndex, MetricType
+from metalfaiss_b200 import _native as nat
 from metalfaiss_b200 import synthetic as syn
 from oracle import compare, oracle
 
@@ -201,3 +202,34 @@ def test_flat_empty_and_errors(cuda_device):
         idx.search(np.zeros((1, 7), np.float32), 1)
     r = idx.search(np.zeros((0, 8), np.float32), 3)
     assert tuple(r.distances.shape) == (0, 3)
+
+
+@pytest.mark.parametrize("k", [1, 10, 32])
+@pytest.mark.parametrize("layout", ["mixture", "near_first", "duplicates"])
+def test_flat_many_queries_l2(cuda_device, k, layout):
+    """L2 tensor-core flat search of many queries against the oracle: rows
+    from a mixture (mixture), the first rows each query's nearest (near_first),
+    and the first 2048 rows repeated at 2048..4095 (duplicates: equal
+    distances, which the lower row must win). Also equal to
+    mf_flat_search_bounded with an infinite bound."""
+    d, nb, nq = 64, 20000, 1500
+    xb, cen, _ = syn.mixture(nb, d, 32, seed=61)
+    xq, _, _ = syn.mixture(nq, d, 32, seed=62, centres=cen)
+    if layout == "near_first":
+        xb[:nq] = xq + 1e-3 * syn.gaussian(nq, d, seed=63)
+    elif layout == "duplicates":
+        xb[2048:4096] = xb[:2048]
+    idx = FlatIndex(d, MetricType.L2)
+    idx.add(xb)
+    assert nat.load().mf_flat_engine(int(MetricType.L2), d, k, nb, 1) == 1
+    D, I = _check(idx, xq, xb, k, MetricType.L2)
+    xqt = torch.from_numpy(xq).cuda()
+    inf = torch.full((nq,), float("inf"), device="cuda")
+    open_ = idx._search_bounded(xqt, k, inf)
+    assert np.array_equal(open_.labels.cpu().numpy(), I)
+    assert np.array_equal(open_.distances.cpu().numpy(), D)
+    if layout == "duplicates":
+        # of two equal rows the lower one comes back first
+        for q in range(nq):
+            got = set(I[q].tolist())
+            assert all(l - 2048 in got for l in I[q] if 2048 <= l < 4096), q
