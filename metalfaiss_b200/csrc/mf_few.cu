@@ -1,6 +1,6 @@
 // Scan of IVF items that hold few queries (a list's last group of at most
-// kFewMax queries): one block of four warps per item (one warp for items of at
-// most kFewBoundRows rows, such as the bound pass's), the warps taking
+// kFewMax queries): one block of four warps per item (two warps for items of
+// at most kFewBoundRows rows, such as the bound pass's), the warps taking
 // interleaved 16-row steps of the list, each with its own per-query top-k
 // lists, merged at the end of the item. The item's queries sit in shared
 // memory. Rows are read 16 at a time with
@@ -33,8 +33,15 @@ namespace mf {
 namespace {
 
 constexpr int kFewMax = 16;     // queries per item at most
-constexpr int kFewWarps = 4;    // warps per block, sharing one item (general items)
-constexpr int kFewBoundRows = 256;  // items of at most this many rows: one warp each
+#ifndef MF_FEW_WARPS
+#define MF_FEW_WARPS 4
+#endif
+#ifndef MF_FEW_BOUND_WARPS
+#define MF_FEW_BOUND_WARPS 2
+#endif
+constexpr int kFewWarps = MF_FEW_WARPS;  // warps per block, sharing one item (general items)
+constexpr int kFewBoundWarps = MF_FEW_BOUND_WARPS;  // the same for the bound pass's items
+constexpr int kFewBoundRows = 256;  // items of at most this many rows: kFewBoundWarps each
 constexpr int kFewMaxD = 128;   // d at most: one 16-byte column slice per lane
 constexpr int kFewK = 32;       // list slots per query (k <= 32)
 constexpr int kFewRows = 16;    // rows per step
@@ -63,13 +70,15 @@ __device__ __forceinline__ void few_mma_f16(float (&c)[4], const uint32_t (&af)[
       : "r"(af[0]), "r"(af[1]), "r"(af[2]), "r"(af[3]), "r"(b0), "r"(b1));
 }
 
-// W warps per block share an item: 4 for general items; 1 for items of at
-// most kFewBoundRows rows (the bound pass's 128), which would leave four warps
-// two steps each between block barriers and cross-warp merges. The fp16 form
-// is held to 128 registers (four blocks per SM, no spills), so that 16 warps
-// per SM each have two 16-row steps of loads in flight.
+// W warps per block share an item: 4 for general items (2 measured the same, 8
+// a third slower: its block barriers wait on more warps); 2 for items of at
+// most kFewBoundRows rows (the bound pass's 128: four steps each, 1-2 % faster
+// than one warp at 10,000 queries and 8 % at 1,250). The fp16 form is held to
+// 128 registers (16 warps per SM, no spills), so that each warp has two
+// 16-row steps of loads in flight.
 template <int METRIC, bool FLT, int W>
-__global__ void __launch_bounds__(W * 32, FLT ? 4 : 1) few_scan_kernel(const ScanArgs a) {
+__global__ void __launch_bounds__(W * 32, FLT ? (W < 16 ? 16 / W : 1) : 1)
+    few_scan_kernel(const ScanArgs a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -409,15 +418,16 @@ int launch_few_scan(const ScanArgs& a, int metric, int64_t max_items, int device
   MF_CHECK(!flt || (metric == MF_METRIC_L2 && a.d <= kFewMaxD && a.d % 8 == 0 && a.pair_qn &&
                     a.pair_thr && a.pair_sc && a.pair_cnt && a.centroids),
            MF_ERR_INVALID_ARGS, "few-query filter scan: L2, d <= %d, per-pair arrays", kFewMaxD);
-  // items capped at a few rows (the bound pass): one warp per item
-  const int warps = (!flt && a.max_rows > 0 && a.max_rows <= kFewBoundRows) ? 1 : kFewWarps;
+  // items capped at a few rows (the bound pass): kFewBoundWarps per item
+  const bool bound_items = !flt && a.max_rows > 0 && a.max_rows <= kFewBoundRows;
+  const int warps = bound_items ? kFewBoundWarps : kFewWarps;
   const size_t smem = FewSmem::block(a.d, warps);
   void (*fn)(const ScanArgs);
   if (flt)
     fn = few_scan_kernel<MF_METRIC_L2, true, kFewWarps>;
-  else if (warps == 1)
-    fn = metric == MF_METRIC_L2 ? few_scan_kernel<MF_METRIC_L2, false, 1>
-                                : few_scan_kernel<MF_METRIC_INNER_PRODUCT, false, 1>;
+  else if (bound_items)
+    fn = metric == MF_METRIC_L2 ? few_scan_kernel<MF_METRIC_L2, false, kFewBoundWarps>
+                                : few_scan_kernel<MF_METRIC_INNER_PRODUCT, false, kFewBoundWarps>;
   else
     fn = metric == MF_METRIC_L2 ? few_scan_kernel<MF_METRIC_L2, false, kFewWarps>
                                 : few_scan_kernel<MF_METRIC_INNER_PRODUCT, false, kFewWarps>;
