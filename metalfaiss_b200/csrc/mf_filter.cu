@@ -187,6 +187,12 @@ __global__ void __launch_bounds__(kBankThreads) filter_bank_kernel(
 // while the warp walks its probes; lane p then writes pair p's values.
 constexpr int kPairsWarps = 8;
 
+#ifndef MF_PAIRS_BATCH
+#define MF_PAIRS_BATCH 4
+#endif
+// Probes of a query whose centroid rows one warp loads at a time.
+constexpr int kPairsBatch = MF_PAIRS_BATCH;
+
 __global__ void __launch_bounds__(kPairsWarps * 32) filter_pairs_kernel(
     const float* __restrict__ xq, const float* __restrict__ qnorms, int64_t nq, int P, int d,
     const int64_t* __restrict__ probes, const int64_t* __restrict__ offsets, int nlist,
@@ -211,8 +217,8 @@ __global__ void __launch_bounds__(kPairsWarps * 32) filter_pairs_kernel(
     const int np = P - p0 < 32 ? P - p0 : 32;
     const int64_t my_l = lane < np ? probes[q * P + p0 + lane] : -1;
     const bool my_ok = my_l >= 0 && my_l < nlist && offsets[my_l + 1] > offsets[my_l];
-    // four probes at a time, so their centroid loads overlap
-    constexpr int kB = 4;
+    // kPairsBatch probes at a time, so their centroid loads overlap
+    constexpr int kB = kPairsBatch;
     for (unsigned int m = __ballot_sync(0xffffffffu, my_ok); m != 0u;) {
       int jj[kB];
 #pragma unroll
