@@ -118,7 +118,10 @@ def exchange_probes(send: torch.Tensor, nq: int, nprobe: int, group=None):
     """One all-gather of every rank's probe_buffer → the (nq, nprobe) probes
     and (nq,) bounds of all queries, in query order, on every rank."""
     world = dist.get_world_size(group)
-    mmax = -(-nq // world) if nq else 0
+    if nq == 0:  # every rank has the same batch, so none of them gathers
+        return (torch.empty((0, nprobe), dtype=torch.int64, device=send.device),
+                torch.empty(0, dtype=torch.float32, device=send.device))
+    mmax = -(-nq // world)
     if dist.get_backend(group) == "nccl":
         out = torch.empty((world, send.numel()), dtype=send.dtype, device=send.device)
         dist.all_gather_into_tensor(out, send, group=group)
@@ -387,6 +390,9 @@ class ShardedIVF:
         idx = self.local
         nq = xq.shape[0]
         dev = idx.device
+        if nq == 0 or k == 0:  # the same on every rank: no exchange
+            return SearchResult(torch.empty((nq, k), dtype=torch.float32, device=dev),
+                                torch.empty((nq, k), dtype=torch.int64, device=dev))
         # 1. this rank's share of the queries: coarse step and bounds (from
         #    the head bank), written into the send buffer; one all-gather
         b, e = row_shard(nq, self.rank, self.world)

@@ -184,6 +184,28 @@ def _ivf_heads_worker(rank, port, out_dir):
         dist.destroy_process_group()
 
 
+def _exchange_shapes_worker(rank, port, out_dir):
+    """exchange_probes for batches with fewer queries than ranks (rank 1's
+    share empty) and an empty batch."""
+    dist = _init(rank, port)
+    try:
+        nprobe = 3
+        for nq in (0, 1, 2, 3, 7):
+            probes = torch.arange(nq * nprobe, dtype=torch.int64).reshape(nq, nprobe)
+            bound = torch.arange(nq, dtype=torch.float32) / 4
+            b, e = row_shard(nq, rank, WORLD)
+            send, mine, mine_bound = probe_buffer(nq, nprobe, rank, WORLD, "cpu")
+            assert tuple(mine.shape) == (e - b, nprobe) and mine_bound.numel() == e - b
+            mine.copy_(probes[b:e])
+            mine_bound.copy_(bound[b:e])
+            got_p, got_b = exchange_probes(send, nq, nprobe)
+            assert torch.equal(got_p, probes) and torch.equal(got_b, bound), nq
+        with open(os.path.join(out_dir, f"shapes{rank}.txt"), "w") as f:
+            f.write("ok")
+    finally:
+        dist.destroy_process_group()
+
+
 def _gather_rows_worker(rank, port, out_dir):
     dist = _init(rank, port)
     try:
@@ -357,3 +379,8 @@ def test_head_rows_are_each_lists_first_rows():
                                        for l in range(nlist)]))
         assert np.array_equal(got, want)
     assert head_rows(torch.empty(0, dtype=torch.int64), nlist, 4).numel() == 0
+
+
+def test_exchange_probes_uneven_and_empty_gloo():
+    with tempfile.TemporaryDirectory() as tmp:
+        assert _run(_exchange_shapes_worker, tmp) == [0, 0]
