@@ -212,7 +212,7 @@ def read_index(fname: str, device=None):
             if cents.shape != (nlist, d):
                 raise FormatError(f"{fname}: centroids are {cents.shape}, not ({nlist}, {d})")
             index.set_centroids(_to_device(cents, index.device))
-            index._install_lists(torch.from_numpy(offs).to(index.device),
+            index._install_lists(_to_device(offs, index.device),
                                  _to_device(vecs, index.device), _to_device(ids, index.device))
         elif ntotal:
             raise FormatError(f"{fname}: an untrained index with {ntotal} rows")
