@@ -716,7 +716,8 @@ def reference_ivf_index(cfg, device, seed=1234):
 def run_reference_ivf(args, cfg, device):
     t0 = time.time()
     cents, offsets, vecs, ids, xq = reference_ivf_index(cfg, device)
-    torch.cuda.synchronize(device)
+    if device.type == "cuda":
+        torch.cuda.synchronize(device)
     log(f"[bench] reference arm: index built with torch ops in {time.time() - t0:.1f}s")
     threads = host_threads()
     sample = min(args.cpu_sample, cfg["nq"])
@@ -987,8 +988,11 @@ def run_reference(args, cfg):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    device = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
-    torch.cuda.set_device(device)
+    if torch.cuda.is_available():
+        device = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+        torch.cuda.set_device(device)
+    else:  # the arm times host code; only its data preparation uses torch
+        device = torch.device("cpu")
     fn = {"ivf": run_reference_ivf, "flat": run_reference_flat,
           "kmeans": run_reference_kmeans}[cfg["kind"]]
     v, base, ms_step, kind = fn(args, cfg, device)
