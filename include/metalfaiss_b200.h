@@ -319,7 +319,9 @@ MF_API int mf_ivf_search_preassigned(int device, void* stream, const float* xq, 
  * k-th smallest distance over all of its probed lists, taken from the first
  * rows of its first probe (probes[q*nprobe]), or +inf where this process holds
  * no rows of that list. The minimum of the ranks' bounds (an all-reduce) is a
- * bound for every rank.
+ * bound for every rank; so is the bound a process computes on a copy of every
+ * list's first mf_ivf_bound_rows() rows (the same rows the owner would scan),
+ * which spares that all-reduce.
  *
  * mf_ivf_search_bounded is mf_ivf_search_preassigned with that bound given:
  * rows farther than bound[q] are not kept, so a rank's results may hold fewer
