@@ -17,6 +17,10 @@ Workloads (--config; the default is the headline):
 * kmeans5m: k-means on 5M points x d=256 from a 4096-cluster mixture, K=4096;
   one step = one Lloyd iteration (assignment + centroid update); the
   configuration runs 20.
+* ivfpq10m: IVFPQ L2, d=128, N=10M mixture rows, nlist=4096, M=16 one-byte
+  codes, Q=10000, nprobe=32, k=10. binary10m: BinaryFlatIndex, 256-bit
+  uniform random rows, N=10M, Q=1000, k=10. ivfpq32k and binary32k are their
+  small cases. One step = one search of the batch.
 
 N>1 GPUs (one process per GPU, NCCL; ivf configurations): the inverted lists
 are partitioned over the ranks by greedy LPT on list size and each rank adds
@@ -78,6 +82,17 @@ CONFIGS = {
     # profiler captures (a few GB on the device, inputs still past L2).
     "flat1m": dict(kind="flat", metric=0, d=128, n=1_000_000, nq=10_000, k=100, data="unit"),
     "kmeans500k": dict(kind="kmeans", d=256, n=500_000, K=4096, niter=20),
+    # IVFPQ L2 (the ADC scan over residual codes): d=128, N=10M rows from a
+    # 4096-cluster mixture, nlist=4096, M=16 one-byte codes (16 B per row),
+    # Q=10000, nprobe=32, k=10; ivfpq32k is its small case (ivf32k's shapes).
+    "ivfpq10m": dict(kind="ivfpq", d=128, n=10_000_000, nlist=4096, M=16, nq=10_000, nprobe=32,
+                     k=10, niter=10),
+    "ivfpq32k": dict(kind="ivfpq", d=64, n=32768, nlist=128, M=8, nq=16, nprobe=8, k=10,
+                     niter=10),
+    # BinaryFlatIndex (Hamming): 256-bit rows, N=10M, Q=1000, k=10;
+    # binary32k is its small case.
+    "binary10m": dict(kind="binary", d=256, n=10_000_000, nq=1000, k=10),
+    "binary32k": dict(kind="binary", d=256, n=32768, nq=16, k=10),
 }
 METRIC_NAMES = {0: "INNER_PRODUCT", 1: "L2"}
 
@@ -242,6 +257,26 @@ def workload_config(name, cfg):
             "l2": ("database larger than L2 (126 MB); no flush" if big else
                    "database fits in L2 (the configuration's own size); no flush"),
         }
+    if cfg["kind"] == "ivfpq":
+        code_bytes = cfg["n"] * ((cfg["M"] + 15) // 16 * 16)
+        return {
+            "workload": f"{name}: IVFPQ L2 d={cfg['d']} N={cfg['n']} nlist={cfg['nlist']} "
+                        f"M={cfg['M']} (8-bit codes) Q={cfg['nq']} nprobe={cfg['nprobe']} "
+                        f"k={cfg['k']}",
+            "d": cfg["d"], "N": cfg["n"], "nlist": cfg["nlist"], "M": cfg["M"], "Q": cfg["nq"],
+            "nprobe": cfg["nprobe"], "k": cfg["k"],
+            "l2": ("codes larger than L2 (126 MB); no flush" if code_bytes > 126e6 else
+                   "codes fit in L2 (the configuration's own size); no flush"),
+        }
+    if cfg["kind"] == "binary":
+        return {
+            "workload": f"{name}: BinaryFlatIndex Hamming d={cfg['d']} bits N={cfg['n']} "
+                        f"Q={cfg['nq']} k={cfg['k']}",
+            "d": cfg["d"], "N": cfg["n"], "Q": cfg["nq"], "k": cfg["k"],
+            "l2": ("packed rows larger than L2 (126 MB); no flush"
+                   if cfg["n"] * cfg["d"] / 8 > 126e6 else
+                   "packed rows fit in L2 (the configuration's own size); no flush"),
+        }
     return {
         "workload": f"{name}: k-means L2 N={cfg['n']} d={cfg['d']} K={cfg['K']} "
                     f"({cfg['niter']} Lloyd iterations; one per step)",
@@ -255,6 +290,10 @@ def metric_name(cfg):
         return "IVFFlat queries/sec (list-scan HBM GB/s vs peak in roofline)"
     if cfg["kind"] == "flat":
         return "FlatIndex queries/sec (distance-GEMM tensor fraction in roofline)"
+    if cfg["kind"] == "ivfpq":
+        return "IVFPQ queries/sec (ADC code-scan bytes in roofline)"
+    if cfg["kind"] == "binary":
+        return "BinaryFlatIndex queries/sec (Hamming word operations in roofline)"
     return "k-means Lloyd iterations/sec (assignment GEMM tensor fraction in roofline)"
 
 
@@ -337,10 +376,12 @@ def end_to_end(timer, search, xq, k, device, steps):
     device search."""
     from metalfaiss_b200.pipeline import search_host_batches
 
-    nq = xq.shape[0]
     xq_host = xq.cpu().pin_memory()
-    outs = [(torch.empty((nq, k), dtype=torch.float32).pin_memory(),
-             torch.empty((nq, k), dtype=torch.int64).pin_memory()) for _ in range(2)]
+    r0 = search(xq)  # the results' shapes and types
+    outs = [(torch.empty(r0.distances.shape, dtype=r0.distances.dtype).pin_memory(),
+             torch.empty(r0.labels.shape, dtype=r0.labels.dtype).pin_memory())
+            for _ in range(2)]
+    del r0
 
     def serial_step():
         r = search(xq_host.to(device, non_blocking=True))
@@ -349,7 +390,7 @@ def end_to_end(timer, search, xq, k, device, steps):
 
     serial_ms, _, _ = timer.run(serial_step, steps, 2)
     for D_h, I_h in outs:
-        D_h.fill_(-1.0)
+        D_h.fill_(-1)
         I_h.fill_(-2)
     batches = [xq_host] * steps
     batch_outs = [outs[i % 2] for i in range(steps)]
@@ -363,11 +404,11 @@ def end_to_end(timer, search, xq, k, device, steps):
     return pipe_ms, serial_ms
 
 
-def e2e_entry(nq, d, k, steps, pipe_ms, serial_ms):
+def e2e_entry(nq, d, k, steps, pipe_ms, serial_ms, query_bytes=None):
     return {
         "value": round(nq * steps / (pipe_ms * 1e-3), 1),
         "unit": "queries/s",
-        "h2d_bytes_per_step": int(nq * d * 4),
+        "h2d_bytes_per_step": int(nq * (d * 4 if query_bytes is None else query_bytes)),
         "d2h_bytes_per_step": int(nq * k * 12),
         "steps": steps,
         "mode": "pipelined: search_host_batches, each batch copied in from pinned host "
@@ -955,6 +996,246 @@ def run_reference_kmeans(args, cfg, device):
     return v, vals[0], 1000.0 / v, "port: numpy restatement of the k-means iteration"
 
 
+# ------------------------------------------------------------ IVFPQ / binary
+def training_sample(x, cap, seed):
+    """The rows a build trains on: all of x up to `cap`, else a seeded sample
+    of `cap` rows in input order."""
+    if x.shape[0] <= cap:
+        return x
+    perm = np.random.Generator(np.random.PCG64(seed + 1)).permutation(x.shape[0])[:cap]
+    return x.index_select(0, torch.from_numpy(np.sort(perm)).to(x.device))
+
+
+def ivfpq_index(cfg, device, seed=1234):
+    """The IVFPQ benchmark index through the library: coarse centroids and the
+    PQ trained on 256 rows per list, then every row added."""
+    from metalfaiss_b200 import IVFPQIndex, synthetic as syn
+
+    x, centres = syn.torch_mixture(cfg["n"], cfg["d"], cfg["nlist"], seed, device)
+    idx = IVFPQIndex(cfg["d"], cfg["nlist"], cfg["M"], device=device, seed=seed)
+    idx.train(training_sample(x, 256 * cfg["nlist"], seed), niter=cfg["niter"])
+    idx.add(x)
+    del x
+    xq, _ = syn.torch_mixture(cfg["nq"], cfg["d"], cfg["nlist"], seed + 1, device, centres=centres)
+    idx.nprobe = cfg["nprobe"]
+    return idx, xq
+
+
+def cpu_baseline_ivfpq(cents, pqc, offsets, codes, ids, xq, cfg, sample):
+    """The oracle's numpy restatement of IVFPQIndex.search (coarse step, then
+    the per-list ADC tables and scores, python/metalfaiss/index/ivf_pq_index.py:127-186)
+    over `sample` queries."""
+    from oracle import oracle
+
+    q = xq[:sample, :cfg["d"]].cpu().numpy()
+    t0 = time.perf_counter()
+    oracle.ivfpq_search(q, cents, pqc, offsets, codes, ids, cfg["nprobe"], cfg["k"])
+    dt = time.perf_counter() - t0
+    return {"value": round(sample / dt, 4), "unit": "queries/s", "cores": 1, "kind": "port",
+            "sample": f"{sample} of the {cfg['nq']} queries, the whole index (numpy, one core "
+                      f"for the per-list loop)"}
+
+
+def run_ivfpq(args, cfg, device):
+    idx, xq = ivfpq_index(cfg, device)
+    k, nq, d = cfg["k"], cfg["nq"], cfg["d"]
+    P = min(cfg["nprobe"], cfg["nlist"])
+    search = lambda q: idx.search(q, k)  # noqa: E731
+    probes = idx.quantizer._search_padded(xq, P, map_ids=False).labels.cpu().numpy()
+    sizes = idx.list_sizes()
+    valid = probes[probes >= 0]
+    pitch = idx.pq.code_pitch
+    pair_rows = int(sizes[valid].sum())  # (query, row) scores of one search
+    distinct_rows = int(sizes[np.unique(valid)].sum())
+    timer = Timer(device, 1)
+    ms, clocks, launches = timer.run(lambda: search(xq), args.steps, args.warmup)
+    kt = timer.kernel_times(lambda: search(xq), ["ivfpq_scan"], min(args.steps, 10))
+    scan_ms, scan_n = kt["ivfpq_scan"]
+    e2e_steps = max(3, args.steps // 2)
+    e2e_ms, e2e_serial_ms = end_to_end(timer, search, xq, k, device, e2e_steps)
+    cpu = None
+    if not args.no_cpu_baseline:
+        M = cfg["M"]
+        cpu = cpu_baseline_ivfpq(idx.centroids[:, :d].cpu().numpy(),
+                                 idx.pq.centroids.cpu().numpy(), idx._offsets.cpu().numpy(),
+                                 idx._codes[:, :M].cpu().numpy(), idx._ids.cpu().numpy(), xq,
+                                 cfg, min(args.pq_cpu_sample, nq))
+    hbm_peak, _, peak_kind = measured_peaks()
+    avg = scan_ms / max(scan_n, 1)
+    logical = pair_rows * pitch
+    line = line_head(args, cfg, 1, nq * args.steps / (ms * 1e-3), ms)
+    line.update({
+        "dtype": "u8 codes, f32 tables",
+        "data": "synthetic (seeded Gaussian mixture, generated in HBM)",
+        "parallelism": "single GPU",
+        "roofline": {
+            "bound": "hbm",
+            "kernel": "ivfpq_adc_kernel (one block per (query, probe): the pair's ADC table in "
+                      "shared memory, the list's codes once per probing query)",
+            "achieved": round(logical / (avg * 1e-3) / 1e9, 1) if scan_n else None,
+            "peak": hbm_peak, "unit": "GB/s",
+            "frac": round(logical / (avg * 1e-3) / 1e9 / hbm_peak, 4) if scan_n else None,
+            "peak_kind": f"{peak_kind} hbm_gbs",
+            "traffic": None,
+            "algorithmic_bytes_per_launch": int(logical),
+            "bytes_note": "code bytes once per (query, probed row); the distinct probed rows' "
+                          f"codes are {distinct_rows * pitch} bytes, the rest comes from L2",
+            "scores_per_launch": pair_rows,
+            "avg_launch_ms": round(avg, 4),
+        },
+        "e2e": e2e_entry(nq, d, k, e2e_steps, e2e_ms, e2e_serial_ms),
+        "gpu_launches": int(launches),
+        "clocks": clocks,
+        "cpu_baseline": cpu,
+    })
+    print(json.dumps(line), flush=True)
+
+
+def reference_ivfpq_index(cfg, device, seed=1234):
+    """The IVFPQ benchmark index built with plain torch operations, never this
+    library: the same mixture and training sample, seeded k-means for the
+    coarse centroids and for each subspace's 256 codewords on the training
+    rows' residuals, then every row's residual encoded and the rows grouped by
+    list in input order (python/metalfaiss/index/ivf_pq_index.py:59-124)."""
+    syn = _synthetic()
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        n, d, nlist, M = cfg["n"], cfg["d"], cfg["nlist"], cfg["M"]
+        dsub = d // M
+        x, centres = syn.torch_mixture(n, d, nlist, seed, device)
+        x = x[:, :d].contiguous()
+        xt = training_sample(x, 256 * nlist, seed)
+
+        def kmeans(v, K, s):
+            init = np.random.Generator(np.random.PCG64(s)).permutation(v.shape[0])[:K]
+            c = v.index_select(0, torch.from_numpy(init).to(v.device)).contiguous()
+            for _ in range(cfg["niter"]):
+                c = _torch_update(v, _torch_assign(v, c), c)
+            return c
+
+        c = kmeans(xt, nlist, seed)
+        rt = xt - c.index_select(0, _torch_assign(xt, c))
+        pqc = torch.stack([kmeans(rt[:, m * dsub:(m + 1) * dsub].contiguous(), 256,
+                                  seed + 1 + m) for m in range(M)])
+        del xt, rt
+        lab = _torch_assign(x, c)
+        res = x - c.index_select(0, lab)
+        codes = torch.stack([_torch_assign(res[:, m * dsub:(m + 1) * dsub].contiguous(), pqc[m])
+                             for m in range(M)], 1).to(torch.uint8)
+        del res, x
+        order = torch.argsort(lab, stable=True)
+        offsets = torch.zeros(nlist + 1, dtype=torch.int64, device=device)
+        offsets[1:] = torch.cumsum(torch.bincount(lab, minlength=nlist), 0)
+        xq, _ = syn.torch_mixture(cfg["nq"], d, nlist, seed + 1, device, centres=centres)
+        return (c.cpu().numpy(), pqc.cpu().numpy(), offsets.cpu().numpy(),
+                codes.index_select(0, order).cpu().numpy(), order.cpu().numpy(), xq)
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+
+
+def run_reference_ivfpq(args, cfg, device):
+    cents, pqc, offsets, codes, ids, xq = reference_ivfpq_index(cfg, device)
+    sample = min(args.pq_cpu_sample, cfg["nq"])
+    cpu_baseline_ivfpq(cents, pqc, offsets, codes, ids, xq, cfg, max(1, sample // 8))
+    vals = [cpu_baseline_ivfpq(cents, pqc, offsets, codes, ids, xq, cfg, sample)
+            for _ in range(args.steps)]
+    v = statistics.median(r["value"] for r in vals)
+    return v, vals[0], sample / v * 1000.0, ("port: the oracle's numpy IVFPQ search; index "
+                                             "built with plain torch operations")
+
+
+def binary_data(cfg, device, seed=91):
+    """Uniform random 0/1 rows (n, d) and queries (nq, d), uint8, seeded."""
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    xb = torch.randint(0, 2, (cfg["n"], cfg["d"]), generator=g, dtype=torch.uint8, device=device)
+    xq = torch.randint(0, 2, (cfg["nq"], cfg["d"]), generator=g, dtype=torch.uint8, device=device)
+    return xb, xq
+
+
+def cpu_baseline_binary(xb_words, xq, cfg, sample):
+    """The oracle's Hamming search (popcount of XOR over packed 64-bit words,
+    then the k smallest with ties to the lower row: BinaryFlatIndex.search,
+    python/metalfaiss/index/binary_flat_index.py:50-92) over `sample` queries."""
+    from oracle import oracle
+
+    q = oracle.pack01_words(xq[:sample].cpu().numpy())
+    t0 = time.perf_counter()
+    oracle.hamming_search_packed(q, xb_words, cfg["k"])
+    dt = time.perf_counter() - t0
+    return {"value": round(sample / dt, 4), "unit": "queries/s", "cores": 1, "kind": "port",
+            "sample": f"{sample} of the {cfg['nq']} queries, all rows (numpy, one core)"}
+
+
+def run_binary(args, cfg, device):
+    from metalfaiss_b200 import BinaryFlatIndex
+
+    xb, xq = binary_data(cfg, device)
+    n, d, nq, k = cfg["n"], cfg["d"], cfg["nq"], cfg["k"]
+    idx = BinaryFlatIndex(d, device=device)
+    idx.add(xb)
+    del xb
+    search = lambda q: idx.search(q, k)  # noqa: E731
+    timer = Timer(device, 1)
+    ms, clocks, launches = timer.run(lambda: search(xq), args.steps, args.warmup)
+    kt = timer.kernel_times(lambda: search(xq), ["binary_topk"], min(args.steps, 10))
+    scan_ms, scan_n = kt["binary_topk"]
+    e2e_steps = max(3, args.steps // 2)
+    e2e_ms, e2e_serial_ms = end_to_end(timer, search, xq, k, device, e2e_steps)
+    cpu = None
+    if not args.no_cpu_baseline:
+        # the library's packed rows: bit j of a row is bit j % 64 of 64-bit word
+        # j / 64, as pack01_words packs the queries
+        words = idx.codes.cpu().numpy().view(np.uint64) if d % 64 == 0 else None
+        if words is not None:
+            cpu = cpu_baseline_binary(words, xq, cfg, min(args.bin_cpu_sample, nq))
+    hbm_peak, _, peak_kind = measured_peaks()
+    avg = scan_ms / max(scan_n, 1)
+    W = (d + 31) // 32
+    word_ops = nq * n * W  # xor + popc per 32-bit word of every (query, row) pair
+    row_bytes = n * W * 4
+    line = line_head(args, cfg, 1, nq * args.steps / (ms * 1e-3), ms)
+    line.update({
+        "dtype": "u32 words",
+        "data": "synthetic (seeded uniform bits, generated in HBM)",
+        "parallelism": "single GPU",
+        "roofline": {
+            "bound": "int",
+            "kernel": "binary_topk_kernel (32-query tiles x 128-row tiles, xor + popc per word, "
+                      "warp top-k)",
+            "achieved": round(word_ops / (avg * 1e-3) / 1e12, 3) if scan_n else None,
+            "peak": None, "unit": "T word-ops/s",
+            "frac": None,
+            "peak_kind": "no measured integer-pipe peak on this pool",
+            "traffic": None,
+            "hbm": {"row_bytes": row_bytes, "reads_per_launch": -(-nq // 32),
+                    "achieved_distinct_GBps": (round(row_bytes / (avg * 1e-3) / 1e9, 1)
+                                               if scan_n else None),
+                    "peak": hbm_peak, "peak_kind": f"{peak_kind} hbm_gbs"},
+            "avg_launch_ms": round(avg, 4),
+        },
+        "e2e": e2e_entry(nq, d, k, e2e_steps, e2e_ms, e2e_serial_ms, query_bytes=d),
+        "gpu_launches": int(launches),
+        "clocks": clocks,
+        "cpu_baseline": cpu,
+    })
+    print(json.dumps(line), flush=True)
+
+
+def run_reference_binary(args, cfg, device):
+    from oracle import oracle
+
+    xb, xq = binary_data(cfg, device)
+    words = oracle.pack01_words(xb.cpu().numpy())
+    del xb
+    sample = min(args.bin_cpu_sample, cfg["nq"])
+    cpu_baseline_binary(words, xq, cfg, 1)
+    vals = [cpu_baseline_binary(words, xq, cfg, sample) for _ in range(args.steps)]
+    v = statistics.median(r["value"] for r in vals)
+    return v, vals[0], sample / v * 1000.0, "port: the oracle's packed Hamming search"
+
+
 # ------------------------------------------------------------------ dispatch
 def run_ours(args, cfg):
     import torch.distributed as dist
@@ -972,6 +1253,10 @@ def run_ours(args, cfg):
             run_ivf(args, cfg, rank, world, device)
         elif cfg["kind"] == "flat":
             run_flat(args, cfg, rank, world, device)
+        elif cfg["kind"] in ("ivfpq", "binary"):
+            if world > 1:
+                raise SystemExit(f"{args.config} runs on one GPU")
+            (run_ivfpq if cfg["kind"] == "ivfpq" else run_binary)(args, cfg, device)
         else:
             if world > 1:
                 raise SystemExit("kmeans5m runs on one GPU")
@@ -994,7 +1279,8 @@ def run_reference(args, cfg):
     else:  # the arm times host code; only its data preparation uses torch
         device = torch.device("cpu")
     fn = {"ivf": run_reference_ivf, "flat": run_reference_flat,
-          "kmeans": run_reference_kmeans}[cfg["kind"]]
+          "kmeans": run_reference_kmeans, "ivfpq": run_reference_ivfpq,
+          "binary": run_reference_binary}[cfg["kind"]]
     v, base, ms_step, kind = fn(args, cfg, device)
     unit = "iterations/s" if cfg["kind"] == "kmeans" else "queries/s"
     line = {
@@ -1003,7 +1289,8 @@ def run_reference(args, cfg):
         "value": v, "unit": unit, "n_gpus": int(os.environ.get("WORLD_SIZE", "1")),
         "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(ms_step, 3), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "scaling": "weak", "vs_baseline": None,
+        "dtype": {"ivfpq": "u8 codes, f32 tables", "binary": "u32 words"}.get(cfg["kind"], "f32"),
         "data": "synthetic (seeded, the same draws as this arm's counterpart)",
         "config": workload_config(args.config, cfg),
         "cpu_baseline": {"value": v, "unit": unit, "cores": base["cores"], "kind": base["kind"],
@@ -1031,6 +1318,9 @@ def main():
     ap.add_argument("--flat-cpu-sample", type=int, default=2)
     # points of the k-means CPU baseline's iteration
     ap.add_argument("--kmeans-cpu-sample", type=int, default=20000)
+    # queries of the IVFPQ and binary CPU baselines (per reference-arm step too)
+    ap.add_argument("--pq-cpu-sample", type=int, default=64)
+    ap.add_argument("--bin-cpu-sample", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:

@@ -257,6 +257,36 @@ def hamming_search(xq01, xb01, k, ids=None):
     return np.take_along_axis(d, order, axis=1), labels
 
 
+def pack01_words(x01) -> np.ndarray:
+    """(n, d) 0/1 rows → (n, ceil(d / 64)) uint64 words, zero padding bits.
+    The bit order within a word is fixed, so Hamming distances between rows
+    packed alike are those of the 0/1 rows."""
+    b = np.packbits(np.asarray(x01, np.uint8), axis=1, bitorder="little")
+    pad = (-b.shape[1]) % 8
+    if pad:
+        b = np.concatenate([b, np.zeros((b.shape[0], pad), np.uint8)], axis=1)
+    return np.ascontiguousarray(b).view(np.uint64)
+
+
+def hamming_search_packed(xq_words, xb_words, k):
+    """hamming_search over pack01_words rows: per query the popcount of
+    q XOR x summed over the words, then the k smallest with ties to the lower
+    row (the stable order of hamming_search), without its (n, d) temporaries."""
+    xq_words = np.asarray(xq_words, np.uint64)
+    xb_words = np.asarray(xb_words, np.uint64)
+    n = len(xb_words)
+    kk = min(k, n)
+    D = np.empty((len(xq_words), kk), np.int32)
+    I = np.empty((len(xq_words), kk), np.int64)
+    for i, q in enumerate(xq_words):
+        d = np.bitwise_count(xb_words ^ q).sum(axis=1, dtype=np.int32)
+        kth = np.partition(d, kk - 1)[kk - 1] if kk < n else d.max()
+        cand = np.flatnonzero(d <= kth)  # ascending rows
+        order = cand[np.argsort(d[cand], kind="stable")[:kk]]
+        D[i], I[i] = d[order], order
+    return D, I
+
+
 def hamming_range(xq01, xb01, radius, ids=None):
     """Rows within Hamming distance <= radius, in row order, with lims
     (python/metalfaiss/index/binary_flat_index.py:94-150)."""

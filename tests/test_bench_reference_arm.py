@@ -1,7 +1,7 @@
 """bench.py's reference arm on the host (no GPU needed: it times the CPU
 implementation of the path and prepares its data with torch on the host when
 no GPU is present): one JSON line with the keys the benchmark contract asks
-for, on the two small configurations."""
+for, on the small IVFFlat, flat, IVFPQ and binary configurations."""
 import json
 import os
 import subprocess
@@ -24,7 +24,9 @@ def _line(*args):
 
 
 @pytest.mark.parametrize("config,extra", [("ivf32k", ["--cpu-sample", "16"]),
-                                          ("flat32k", [])])
+                                          ("flat32k", []),
+                                          ("ivfpq32k", ["--pq-cpu-sample", "16"]),
+                                          ("binary32k", [])])
 def test_reference_arm_line(config, extra):
     d = _line("--config", config, *extra)
     assert d["impl"] == "reference"

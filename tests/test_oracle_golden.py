@@ -129,3 +129,18 @@ def test_hamming_ivf_oracle_matches_reference_binary_ivf():
         np.testing.assert_array_equal(I[~pad], G[tag + "_I"][~pad])
         assert (I[pad] == -1).all() and (G[tag + "_I"][pad] == 0).all()
     assert any(np.isinf(G[str(t) + "_D"]).any() for t in G["binivf_cases"])  # padding covered
+
+
+def test_hamming_search_packed_equals_unpacked():
+    """The packed host form the benchmark's CPU baseline uses gives
+    hamming_search's results, ties (to the lower row) included."""
+    rng = np.random.Generator(np.random.PCG64(17))
+    for d in (8, 64, 100, 256):
+        xb = (rng.random((3000, d)) < 0.5).astype(np.uint8)
+        xb[1500:1600] = xb[:100]  # equal rows: equal distances
+        xq = (rng.random((9, d)) < 0.5).astype(np.uint8)
+        for k in (1, 10, 150):
+            D0, I0 = oracle.hamming_search(xq, xb, k)
+            D1, I1 = oracle.hamming_search_packed(oracle.pack01_words(xq),
+                                                  oracle.pack01_words(xb), k)
+            assert np.array_equal(D0, D1) and np.array_equal(I0, I1), (d, k)
