@@ -23,6 +23,8 @@ Collectives go through torch.distributed (NCCL on GPUs, gloo in CPU tests).
 """
 from __future__ import annotations
 
+from typing import Optional
+
 import numpy as np
 import torch
 import torch.distributed as dist
@@ -221,7 +223,7 @@ def _empty_like_index(index):
     return out
 
 
-def keep_lists(index, keep_mask: np.ndarray, max_rows: int = None):
+def keep_lists(index, keep_mask: np.ndarray, max_rows: Optional[int] = None):
     """A copy of an IVFFlatIndex holding only the lists where keep_mask is True
     (the other lists stay empty), and of those only the first max_rows rows
     when given; shares the quantizer."""
