@@ -328,6 +328,76 @@ def gen_binary_ivf(m, out):
     out["binivf_cases"] = np.array(cases)
 
 
+def gen_ivfpq(m, out):
+    """IVFPQIndex add / search, python/metalfaiss/index/ivf_pq_index.py:101-186,
+    on installed coarse centroids and PQ codebooks. Its train draws MLX random
+    permutations (:62, product_quantizer.py:57), which the shim does not
+    reproduce, so the centroids are seeded rows of the data and each subspace's
+    256 codewords seeded rows of the residuals, installed where train leaves
+    them (_centroids, pq.centroids, is_trained). add then assigns, encodes and
+    files the rows as written, and search probes and scores them through its
+    ADC tables. Every query's probed lists hold at least k rows (its search
+    stacks one row of k per query). Saved beside D and I: each row's list and
+    codes as add filed them, and the probes its search takes (the same shim
+    operations, :149-150)."""
+    import mlx.core as mx  # the shim
+
+    try:
+        ivfpq = importlib.import_module("metalfaiss.index.ivf_pq_index")
+    except Exception as e:  # pragma: no cover
+        print(f"[golden] IVFPQIndex unavailable ({type(e).__name__}: {e})")
+        return
+    cases = []
+    for (n, d, nlist, M, nq, k, nprobe, seed) in [(2000, 32, 8, 4, 9, 10, 2, 60),
+                                                  (3000, 64, 16, 8, 7, 20, 3, 61),
+                                                  (1500, 16, 6, 16, 5, 5, 1, 62)]:
+        x, cen = mixture(n, d, nlist, seed)
+        q, _ = mixture(nq, d, nlist, seed + 1, centres=cen)
+        g = rng(seed + 2)
+        cents = x[g.choice(n, nlist, replace=False)].copy()
+        lab0 = np.argmin(((x[:, None, :] - cents[None, :, :]) ** 2).sum(2), axis=1)
+        res0 = x - cents[lab0]
+        dsub = d // M
+        pick = g.choice(n, 256, replace=False)
+        pqc = np.stack([res0[pick, j * dsub:(j + 1) * dsub] for j in range(M)]).astype(np.float32)
+        idx = ivfpq.IVFPQIndex(d, nlist, M)
+        idx._centroids = mx.array(cents)
+        idx._pq.centroids = mx.array(pqc)
+        idx.is_trained = True
+        ids = [int(3 * i + 1) for i in range(n)]
+        idx.add(x.tolist(), ids)
+        idx.nprobe = nprobe
+        try:
+            r = idx.search(q.tolist(), k)
+        except Exception as e:  # pragma: no cover
+            print(f"[golden] IVFPQ case {n}/{d}: search failed ({type(e).__name__}: {e})")
+            continue
+        codes = np.zeros((n, M), np.uint8)
+        labels = np.zeros(n, np.int64)
+        for lid, lst in enumerate(idx._codes):
+            for vid, c in lst:
+                row = (vid - 1) // 3
+                codes[row] = np_(c).astype(np.uint8)
+                labels[row] = lid
+        cm = mx.array(cents)
+        probes = np.stack([np_(mx.argsort(mx.sum(mx.square(mx.subtract(cm, mx.array(qq)[None, :])),
+                                                 axis=1))[:nprobe]) for qq in q]).astype(np.int64)
+        tag = f"ivfpq_{n}_{d}_{M}_{k}"
+        out[tag + "_xb"] = x
+        out[tag + "_xq"] = q
+        out[tag + "_cents"] = cents
+        out[tag + "_pqc"] = pqc
+        out[tag + "_ids"] = np.asarray(ids, np.int64)
+        out[tag + "_nprobe"] = np.int64(nprobe)
+        out[tag + "_probes"] = probes
+        out[tag + "_codes"] = codes
+        out[tag + "_labels"] = labels
+        out[tag + "_D"] = np_(r.distances).astype(np.float32)
+        out[tag + "_I"] = np_(r.indices).astype(np.int64)
+        cases.append(tag)
+    out["ivfpq_cases"] = np.array(cases)
+
+
 def main():
     mods = load_reference()
     out = {}
@@ -338,6 +408,7 @@ def main():
     gen_kmeans(mods, out)
     gen_binary(mods, out)
     gen_binary_ivf(mods, out)
+    gen_ivfpq(mods, out)
     path = HERE / "reference_golden.npz"
     np.savez_compressed(path, **out)
     print(f"[golden] wrote {path} ({path.stat().st_size // 1024} KiB, {len(out)} arrays)")

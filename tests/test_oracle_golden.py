@@ -144,3 +144,38 @@ def test_hamming_search_packed_equals_unpacked():
             D1, I1 = oracle.hamming_search_packed(oracle.pack01_words(xq),
                                                   oracle.pack01_words(xb), k)
             assert np.array_equal(D0, D1) and np.array_equal(I0, I1), (d, k)
+
+
+def test_ivfpq_oracle_matches_reference_golden():
+    """oracle.pq_encode and oracle.ivfpq_search against the reference
+    IVFPQIndex's own add and search on installed centroids and codebooks
+    (tests/golden/make_golden.py gen_ivfpq): the lists the reference filed
+    the rows into, their codes (equal but for fp32 / fp64 near-ties of two
+    codewords), and the ADC search's distances and labels over the
+    reference's lists and probes."""
+    cases = [str(t) for t in G["ivfpq_cases"]]
+    assert len(cases) == 3
+    for t in cases:
+        xb, xq, cents, pqc = G[t + "_xb"], G[t + "_xq"], G[t + "_cents"], G[t + "_pqc"]
+        ids, codes, labels = G[t + "_ids"], G[t + "_codes"], G[t + "_labels"]
+        nprobe, probes = int(G[t + "_nprobe"]), G[t + "_probes"]
+        D, I = G[t + "_D"], G[t + "_I"]
+        nlist, k = len(cents), D.shape[1]
+        # the reference's assignment: direct-difference fp32 distances, argmin
+        lab = np.argmin(np.sum(np.square(xb[:, None, :] - cents[None, :, :]), axis=2), axis=1)
+        assert np.array_equal(lab, labels), t
+        res = (xb - cents[labels]).astype(np.float64)
+        enc = oracle.pq_encode(res, pqc)
+        dsub = xb.shape[1] // pqc.shape[0]
+        for r, m in np.argwhere(enc != codes):
+            sub = res[r, m * dsub:(m + 1) * dsub]
+            d_ours = np.sum((pqc[m, enc[r, m]].astype(np.float64) - sub) ** 2)
+            d_ref = np.sum((pqc[m, codes[r, m]].astype(np.float64) - sub) ** 2)
+            assert abs(d_ours - d_ref) <= 1e-5 * max(d_ref, 1e-30), (t, r, m)
+        order = np.argsort(labels, kind="stable")
+        offsets = np.zeros(nlist + 1, np.int64)
+        np.cumsum(np.bincount(labels, minlength=nlist), out=offsets[1:])
+        Do, Io = oracle.ivfpq_search(xq, cents, pqc, offsets, codes[order], ids[order], nprobe, k,
+                                     probes=probes)
+        assert np.array_equal(Io, I), t
+        assert np.array_equal(Do, D), t
