@@ -67,6 +67,16 @@ def test_compute_call_reports_status_not_crash():
         assert status == ErrorCode.INVALID_ARGS  # NULL pointers rejected before launch
 
 
+def test_strided_merge_rejects_bad_layout_before_launch():
+    """mf_topk_merge_strided returns a status for a negative stride (or, with
+    no usable device, for the device) and launches nothing."""
+    lib = nat.load()
+    status = lib.mf_topk_merge_strided(0, None, None, 10, -1, None, 10, 10, 4, 2, 10, 10, None,
+                                       None)
+    assert status == ErrorCode.INVALID_ARGS
+    assert lib.mf_last_error()
+
+
 def test_engine_and_filter_eligibility_queries_without_gpu():
     """The host-side dispatch queries: the tensor-core flat scan takes L2 and
     inner product at 32 <= d <= 1024; the filter search 64 <= d <= 128 with d
